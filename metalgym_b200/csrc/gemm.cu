@@ -1,0 +1,113 @@
+// Host launcher for the tcgen05 GEMM engine (gemm_tc.cuh) and its C ABI.
+#include "gemm.h"
+#include "gemm_tc.cuh"
+#include "runtime.h"
+
+namespace mg {
+
+namespace {
+
+template <int BN, bool AMN, bool BMN, int EPI>
+int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits, cudaStream_t st) {
+    using S = GemmShape<BN>;
+    auto kern = gemm_tc_kernel<BN, AMN, BMN, EPI>;
+    static uint64_t attr_done = 0;  // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done & (1ull << (dev & 63)))) {
+        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES));
+        attr_done |= 1ull << (dev & 63);
+    }
+    dim3 grid((p.M + S::BM - 1) / S::BM, (p.N + BN - 1) / BN, splits);
+    kern<<<grid, 128, S::SMEM_BYTES, st>>>(ta, tb, p);
+    return check_launch("gemm_tc_kernel");
+}
+
+template <int BN, bool AMN, bool BMN>
+int by_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits, cudaStream_t st) {
+    switch (epi) {
+        case kEpiBf16: return launch_one<BN, AMN, BMN, kEpiBf16>(ta, tb, p, splits, st);
+        case kEpiBf16Relu: return launch_one<BN, AMN, BMN, kEpiBf16Relu>(ta, tb, p, splits, st);
+        case kEpiBf16Resid: return launch_one<BN, AMN, BMN, kEpiBf16Resid>(ta, tb, p, splits, st);
+        case kEpiBf16Mask: return launch_one<BN, AMN, BMN, kEpiBf16Mask>(ta, tb, p, splits, st);
+        case kEpiF32: return launch_one<BN, AMN, BMN, kEpiF32>(ta, tb, p, splits, st);
+    }
+    return fail(MG_ERR_ARGUMENT, "unknown GEMM epilogue");
+}
+
+template <int BN>
+int by_major(bool amn, bool bmn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+             int splits, cudaStream_t st) {
+    if (!amn && !bmn) return by_epi<BN, false, false>(epi, ta, tb, p, splits, st);
+    if (!amn && bmn) return by_epi<BN, false, true>(epi, ta, tb, p, splits, st);
+    if (amn && !bmn) return by_epi<BN, true, false>(epi, ta, tb, p, splits, st);
+    return by_epi<BN, true, true>(epi, ta, tb, p, splits, st);
+}
+
+}  // namespace
+
+int gemm_bf16(const GemmCall& c, cudaStream_t st) {
+    MG_CHECK_ARG(c.A && c.B && c.out, "gemm: null pointer");
+    MG_CHECK_ARG(c.M > 0 && c.N > 0 && c.K > 0, "gemm: empty shape");
+    MG_CHECK_ARG(c.N % 32 == 0, "gemm: N must be a multiple of 32");
+    MG_CHECK_ARG(c.lda % 8 == 0 && c.ldb % 8 == 0 && c.ldo % 8 == 0, "gemm: leading dimensions must be multiples of 8");
+    MG_CHECK_ARG(c.lda >= (c.a_mn ? c.M : c.K) && c.ldb >= (c.b_mn ? c.N : c.K) && c.ldo >= c.N,
+                 "gemm: leading dimension smaller than the matrix");
+    MG_CHECK_ARG(c.splits >= 1, "gemm: splits must be >= 1");
+    MG_CHECK_ARG(c.splits == 1 || c.epilogue == kEpiF32, "gemm: split-K needs the fp32 epilogue");
+    MG_CHECK_ARG(!(c.epilogue == kEpiBf16Resid || c.epilogue == kEpiBf16Mask) || (c.aux && c.ldaux % 8 == 0),
+                 "gemm: this epilogue needs aux with ldaux a multiple of 8");
+    int bn = c.bn;
+    if (bn == 0) bn = c.N >= 128 ? 128 : 64;
+    MG_CHECK_ARG(bn == 64 || bn == 128 || bn == 256, "gemm: tile N must be 64, 128 or 256");
+
+    int kPerSplit = (c.K + c.splits - 1) / c.splits;
+    kPerSplit = (kPerSplit + 63) / 64 * 64;
+    const int splits = (c.K + kPerSplit - 1) / kPerSplit;
+
+    CUtensorMap ta, tb;
+    int rc = c.a_mn ? make_tmap_bf16(&ta, c.A, c.M, c.K, c.lda, 64) : make_tmap_bf16(&ta, c.A, c.K, c.M, c.lda, 128);
+    if (rc) return rc;
+    rc = c.b_mn ? make_tmap_bf16(&tb, c.B, c.N, c.K, c.ldb, 64) : make_tmap_bf16(&tb, c.B, c.K, c.N, c.ldb, bn);
+    if (rc) return rc;
+
+    GemmParams p;
+    p.M = c.M;
+    p.N = c.N;
+    p.K = c.K;
+    p.kPerSplit = kPerSplit;
+    p.out = c.out;
+    p.ldo = c.ldo;
+    p.aux = static_cast<const __nv_bfloat16*>(c.aux);
+    p.ldaux = c.ldaux;
+    p.status = status_ptr();
+    switch (bn) {
+        case 64: return by_major<64>(c.a_mn, c.b_mn, c.epilogue, ta, tb, p, splits, st);
+        case 128: return by_major<128>(c.a_mn, c.b_mn, c.epilogue, ta, tb, p, splits, st);
+        default: return by_major<256>(c.a_mn, c.b_mn, c.epilogue, ta, tb, p, splits, st);
+    }
+}
+
+}  // namespace mg
+
+extern "C" int mg_gemm_bf16(const void* A_dev, int a_mn_major, int lda, const void* B_dev, int b_mn_major, int ldb,
+                            int M, int N, int K, int epilogue, void* out_dev, int ldo, const void* aux_dev, int ldaux,
+                            int splits, mg_stream_t stream) {
+    mg::GemmCall c;
+    c.A = A_dev;
+    c.a_mn = a_mn_major != 0;
+    c.lda = lda;
+    c.B = B_dev;
+    c.b_mn = b_mn_major != 0;
+    c.ldb = ldb;
+    c.M = M;
+    c.N = N;
+    c.K = K;
+    c.epilogue = epilogue;
+    c.out = out_dev;
+    c.ldo = ldo;
+    c.aux = aux_dev;
+    c.ldaux = ldaux;
+    c.splits = splits;
+    return mg::gemm_bf16(c, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,99 @@
+// Host runtime: error strings, the device status word, TMA descriptors.
+#include "runtime.h"
+
+#include <mutex>
+#include <string>
+
+namespace mg {
+
+namespace {
+thread_local std::string g_last_error;
+
+// One status word per device: kernels record wait timeouts and shape errors
+// here (first error wins); mg_device_status() reads and clears it.
+__device__ int g_status_word;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+}  // namespace
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(MG_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int* status_ptr() {
+    constexpr int kMaxDevices = 64;
+    static int* cache[kMaxDevices] = {};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cache[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+        cache[dev] = static_cast<int*>(p);
+    }
+    return cache[dev];
+}
+
+int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride,
+                   uint32_t box_outer) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(MG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(MG_ERR_ARGUMENT, "TMA base not 16-byte aligned");
+    if ((row_stride * 2) % 16 != 0) return fail(MG_ERR_ARGUMENT, "TMA row stride not a multiple of 16 bytes");
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_stride * 2};
+    cuuint32_t box[2] = {64, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MG_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return MG_OK;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return MG_OK;
+}
+
+}  // namespace mg
+
+extern "C" {
+
+const char* mg_last_error(void) { return mg::g_last_error.c_str(); }
+
+int mg_version(void) { return MG_VERSION; }
+
+int mg_device_status(int clear, int* status) {
+    int* p = mg::status_ptr();
+    if (!p) return mg::fail(MG_ERR_CUDA, "status word lookup failed");
+    int v = 0;
+    MG_CUDA_TRY(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (clear) MG_CUDA_TRY(cudaMemset(p, 0, sizeof(int)));
+    if (status) *status = v;
+    return MG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,101 @@
+"""tcgen05 GEMM engine vs a PyTorch fp32 reference of the same product.
+
+Operands are bf16; the reference multiplies the same bf16 values in fp64 and
+applies the epilogue in fp32. Tolerances: bf16 outputs within one bf16
+rounding of the reference (rtol 1e-2, atol 1e-2 * scale); fp32 outputs within
+accumulation-order noise (rtol 2e-3, atol 1e-3 * scale).
+"""
+import ctypes
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+EPI = {"bf16": 0, "relu": 1, "resid": 2, "mask": 3, "f32": 4}
+
+
+def run_gemm(mg, A, a_mn, B, b_mn, M, N, K, epi, aux=None, splits=1):
+    """A, B are the logical [M,K] and [K,N] bf16 matrices; stores them in the requested major."""
+    Ast = (A.t().contiguous() if a_mn else A.contiguous())
+    Bst = (B.contiguous() if b_mn else B.t().contiguous())
+    lda = M if a_mn else K
+    ldb = N if b_mn else K
+    if EPI[epi] == 4:
+        out = torch.full((splits, M, N), float("nan"), device="cuda", dtype=torch.float32)
+    else:
+        out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    rc = mg.mg_gemm_bf16(Ast.data_ptr(), int(a_mn), lda, Bst.data_ptr(), int(b_mn), ldb, M, N, K, EPI[epi],
+                         out.data_ptr(), N, aux.data_ptr() if aux is not None else None, N, splits, None)
+    assert rc == 0, mg.mg_last_error()
+    torch.cuda.synchronize()
+    st = ctypes.c_int(0)
+    assert mg.mg_device_status(1, ctypes.byref(st)) == 0 and st.value == 0
+    return out
+
+
+def reference(A, B, epi, aux=None):
+    acc = (A.double() @ B.double()).float()
+    if epi == "f32":
+        return acc
+    r = acc.bfloat16().float()
+    if epi == "relu":
+        r = torch.where(r > 0, r, r * 0)
+    elif epi == "resid":
+        r = (aux.float() + r).bfloat16().float()
+    elif epi == "mask":
+        r = r * (aux.float() > 0).float()
+    return r
+
+
+SHAPES = [
+    (256, 128, 128),
+    (4096, 512, 128),   # MLP up-projection at the CartPole config
+    (4096, 128, 512),   # MLP down-projection
+    (4096, 64, 128),    # policy head
+    (200, 96, 96),      # ragged M, N and K tails
+]
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_gemm_bf16_out(mg, a_mn, b_mn, shape):
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 3 + K)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn(K, N, device="cuda", generator=g).bfloat16()
+    out = run_gemm(mg, A, a_mn, B, b_mn, M, N, K, "bf16")
+    ref = reference(A, B, "bf16")
+    scale = ref.abs().max().item()
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2 * scale)
+
+
+@pytest.mark.parametrize("epi", ["relu", "resid", "mask"])
+def test_gemm_epilogues(mg, epi):
+    M, N, K = 512, 256, 128
+    g = torch.Generator(device="cuda").manual_seed(11)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn(K, N, device="cuda", generator=g).bfloat16()
+    aux = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    out = run_gemm(mg, A, 0, B, 1, M, N, K, epi, aux=aux)
+    ref = reference(A, B, epi, aux)
+    scale = ref.abs().max().item()
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2 * scale)
+
+
+@pytest.mark.parametrize("shape,splits", [((128, 512, 4096), 16), ((512, 128, 4096), 8), ((128, 64, 4096), 1),
+                                          ((128, 128, 1000), 4)])
+def test_gemm_weight_grad_splitk(mg, shape, splits):
+    """X^T dZ with K = rows: both operands MN-major, fp32 split-K partials."""
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(5)
+    X = torch.randn(K, M, device="cuda", generator=g).bfloat16()   # rows x features
+    dZ = torch.randn(K, N, device="cuda", generator=g).bfloat16()  # rows x outputs
+    kps = ((K + splits - 1) // splits + 63) // 64 * 64
+    real_splits = (K + kps - 1) // kps
+    out = run_gemm(mg, X.t(), 1, dZ, 1, M, N, K, "f32", splits=real_splits)
+    total = out.sum(0)
+    ref = reference(X.t(), dZ, "f32")
+    scale = ref.abs().max().item()
+    torch.testing.assert_close(total, ref, rtol=2e-3, atol=1e-3 * scale)
