@@ -1,0 +1,247 @@
+// Environment registration: the device-side replacement of the reference's
+// per-environment kernel instantiation
+//     template [[host_name("rollout_cartpole")]] kernel void rollout<CartPole>(...);
+// (rollout.h:31-54, README.md:42-52). Compile a .cu translation unit that
+// includes this header and the environment, then write
+//     MG_REGISTER_ENV(CartPole)
+// at file scope. That instantiates the three environment kernels below for
+// the type and registers them, at load time, under Env::KERNEL with the
+// metalgym_b200 library (mg_env_register), where Gym<Env> and PPOModel<Env>
+// find them by name.
+//
+// Compile such translation units with nvcc --fmad=false so environment
+// arithmetic rounds every multiply and add separately (bit-exact with the
+// same environment compiled as host C++ with -ffp-contract=off).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "../metalgym_b200.h"
+#include "sampling.cuh"
+
+namespace mg {
+
+template <class Env>
+struct EnvTraits {
+    using State = typename Env::State;
+    using Action = typename Env::Action;
+    using Obs = typename Env::Obs;
+    static constexpr bool kContinuous = !std::is_integral<Action>::value;
+    // Large states (e.g. a 1 KB heightmap) are stepped in place in global
+    // memory instead of being copied into registers / local memory.
+    static constexpr bool kInPlace = sizeof(State) > 64;
+    static_assert(sizeof(Obs) == Env::OBS_DIM * sizeof(float), "Env::Obs must be exactly OBS_DIM floats");
+    static_assert(kContinuous || sizeof(Action) == 4, "a discrete Env::Action must be a 4-byte integer");
+    static_assert(!kContinuous || sizeof(Action) == Env::ACT_DIM * sizeof(float),
+                  "a continuous Env::Action must be exactly ACT_DIM floats");
+    static_assert(Env::ACT_DIM + 1 <= (uint32_t)kHeadDim, "ACT_DIM + value must fit the 64-wide head");
+};
+
+// The policy-side draw of one action for env row i (sample.metal / gaussian.metal).
+template <class Env>
+__device__ __forceinline__ typename Env::Action draw_policy_action(const __nv_bfloat16* headRow,
+                                                                   const __nv_bfloat16* logStd, uint32_t& w,
+                                                                   float& lp, float& v) {
+    typename Env::Action a;
+    if constexpr (EnvTraits<Env>::kContinuous) {
+        sample_gaussian_row(headRow, logStd, (int)Env::ACT_DIM, w, reinterpret_cast<float*>(&a), lp, v);
+    } else {
+        a = (typename Env::Action)sample_categorical_row(headRow, (int)Env::ACT_DIM, w, lp, v);
+    }
+    return a;
+}
+
+// The random policy of the raw-step benchmark: the policy draw with an
+// all-zero head (mode 0), or a constant zero action (mode 1, the action the
+// reference benchmark leaves in the buffer).
+template <class Env>
+__device__ __forceinline__ typename Env::Action draw_random_action(uint32_t& w, int mode) {
+    typename Env::Action a;
+    if constexpr (EnvTraits<Env>::kContinuous) {
+        float* f = reinterpret_cast<float*>(&a);
+        if (mode == 1) {
+            for (uint32_t k = 0; k < Env::ACT_DIM; k++) f[k] = 0.0f;
+        } else {
+            __nv_bfloat16 zeros[Env::ACT_DIM + 1];  // head row (means, value) and log-std, all 0
+            for (auto& z : zeros) z = __float2bfloat16_rn(0.0f);
+            float lp, v;
+            sample_gaussian_row(zeros, zeros, (int)Env::ACT_DIM, w, f, lp, v);
+        }
+    } else {
+        a = mode == 1 ? (typename Env::Action)0 : (typename Env::Action)uniform_action(w, (int)Env::ACT_DIM);
+    }
+    return a;
+}
+
+// rollout<Env> (rollout.h:31-54): load, reset if done, step, store.
+// doneCopy (optional) also receives the new done flag (the per-slot copy
+// model/ppo.h:731-732 makes with a blit).
+template <class Env>
+__global__ void env_step_kernel(typename Env::State* states, const typename Env::Action* actions,
+                                typename Env::Obs* obs, float* reward, uint8_t* done, uint8_t* doneCopy, uint32_t* rng,
+                                int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t w = rng[i];
+    uint8_t d = done[i];
+    float r;
+    if constexpr (EnvTraits<Env>::kInPlace) {
+        typename Env::State& s = states[i];
+        if (d) Env::reset(s, w);
+        Env::step(s, actions[i], obs[i], r, d);
+    } else {
+        typename Env::State s = states[i];
+        typename Env::Obs o;
+        if (d) Env::reset(s, w);
+        Env::step(s, actions[i], o, r, d);
+        states[i] = s;
+        obs[i] = o;
+    }
+    reward[i] = r;
+    done[i] = d;
+    if (doneCopy) doneCopy[i] = d;
+    rng[i] = w;
+}
+
+// `steps` env steps per thread with the benchmark's random policy, drawn
+// before the reset / step on the same word (the order collect() uses). Step
+// k's obs / reward / done go to slot k % ring of the ring buffers.
+template <class Env>
+__global__ void env_run_random_kernel(typename Env::State* states, typename Env::Obs* obsRing, float* rewardRing,
+                                      uint8_t* doneRing, uint8_t* done, uint32_t* rng, int n, int steps, int ring,
+                                      int mode) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t w = rng[i];
+    uint8_t d = done[i];
+    typename Env::State local;
+    typename Env::State* sp;
+    if constexpr (EnvTraits<Env>::kInPlace) {
+        sp = &states[i];
+    } else {
+        local = states[i];
+        sp = &local;
+    }
+    for (int k = 0; k < steps; k++) {
+        const typename Env::Action a = draw_random_action<Env>(w, mode);
+        if (d) Env::reset(*sp, w);
+        const size_t slot = (size_t)(k % ring) * n + i;
+        float r;
+        if constexpr (EnvTraits<Env>::kInPlace) {
+            Env::step(*sp, a, obsRing[slot], r, d);
+        } else {
+            typename Env::Obs o;
+            Env::step(*sp, a, o, r, d);
+            obsRing[slot] = o;
+        }
+        rewardRing[slot] = r;
+        doneRing[slot] = d;
+    }
+    if constexpr (!EnvTraits<Env>::kInPlace) states[i] = local;
+    done[i] = d;
+    rng[i] = w;
+}
+
+// One collect() step for env row i, fused: draw the action from this row of
+// the policy head (model/sample.metal or model/gaussian.metal), record
+// action / log-prob / value in slot t, then reset-if-done and step the env
+// with it (rollout.h:31-54) and record obs t+1, reward t and done t
+// (model/ppo.h:727-733: sample, encodeStep, done copy).
+template <class Env>
+__global__ void env_collect_step_kernel(const __nv_bfloat16* head, const __nv_bfloat16* logStd,
+                                        typename Env::State* states, typename Env::Action* actionOut, float* logpOut,
+                                        float* valueOut, typename Env::Obs* obsOut, float* rewardOut, uint8_t* done,
+                                        uint8_t* doneSlot, uint32_t* rng, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint32_t w = rng[i];
+    float lp, v;
+    const typename Env::Action a = draw_policy_action<Env>(head + (size_t)i * kHeadDim, logStd, w, lp, v);
+    actionOut[i] = a;
+    logpOut[i] = lp;
+    valueOut[i] = v;
+    uint8_t d = done[i];
+    float r;
+    if constexpr (EnvTraits<Env>::kInPlace) {
+        typename Env::State& s = states[i];
+        if (d) Env::reset(s, w);
+        Env::step(s, a, obsOut[i], r, d);
+    } else {
+        typename Env::State s = states[i];
+        typename Env::Obs o;
+        if (d) Env::reset(s, w);
+        Env::step(s, a, o, r, d);
+        states[i] = s;
+        obsOut[i] = o;
+    }
+    rewardOut[i] = r;
+    done[i] = d;
+    doneSlot[i] = d;
+    rng[i] = w;
+}
+
+template <class Env>
+struct EnvLaunchers {
+    using T = EnvTraits<Env>;
+    static constexpr int kBlock = T::kInPlace ? 64 : 128;
+    static int grid(int n) { return (n + kBlock - 1) / kBlock; }
+
+    static int step(void* states, const void* actions, void* obs, float* reward, uint8_t* done, uint8_t* doneCopy,
+                    uint32_t* rng, int n, mg_stream_t s) {
+        if (n <= 0) return MG_ERR_ARGUMENT;
+        env_step_kernel<Env><<<grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s)>>>(
+            static_cast<typename T::State*>(states), static_cast<const typename T::Action*>(actions),
+            static_cast<typename T::Obs*>(obs), reward, done, doneCopy, rng, n);
+        return cudaGetLastError() == cudaSuccess ? MG_OK : MG_ERR_CUDA;
+    }
+    static int run_random(void* states, void* obsRing, float* rewardRing, uint8_t* doneRing, uint8_t* done,
+                          uint32_t* rng, int n, int steps, int ring, int mode, mg_stream_t s) {
+        if (n <= 0 || steps < 0 || ring <= 0) return MG_ERR_ARGUMENT;
+        env_run_random_kernel<Env><<<grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s)>>>(
+            static_cast<typename T::State*>(states), static_cast<typename T::Obs*>(obsRing), rewardRing, doneRing,
+            done, rng, n, steps, ring, mode);
+        return cudaGetLastError() == cudaSuccess ? MG_OK : MG_ERR_CUDA;
+    }
+    static int collect_step(const void* head, const void* logStd, void* states, void* actionOut, float* logpOut,
+                            float* valueOut, void* obsOut, float* rewardOut, uint8_t* done, uint8_t* doneSlot,
+                            uint32_t* rng, int n, mg_stream_t s) {
+        if (n <= 0) return MG_ERR_ARGUMENT;
+        env_collect_step_kernel<Env><<<grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s)>>>(
+            static_cast<const __nv_bfloat16*>(head), static_cast<const __nv_bfloat16*>(logStd),
+            static_cast<typename T::State*>(states), static_cast<typename T::Action*>(actionOut), logpOut, valueOut,
+            static_cast<typename T::Obs*>(obsOut), rewardOut, done, doneSlot, rng, n);
+        return cudaGetLastError() == cudaSuccess ? MG_OK : MG_ERR_CUDA;
+    }
+    static mg_env_ops ops() {
+        mg_env_ops o{};
+        o.abi_version = MG_VERSION;
+        o.name = Env::KERNEL;
+        o.state_bytes = (uint32_t)sizeof(typename T::State);
+        o.action_bytes = (uint32_t)sizeof(typename T::Action);
+        o.obs_bytes = (uint32_t)sizeof(typename T::Obs);
+        o.obs_dim = Env::OBS_DIM;
+        o.act_dim = Env::ACT_DIM;
+        o.continuous = T::kContinuous ? 1u : 0u;
+        o.step = &step;
+        o.run_random = &run_random;
+        o.collect_step = &collect_step;
+        return o;
+    }
+};
+
+}  // namespace mg
+
+#define MG_ENV_CONCAT_(a, b) a##b
+#define MG_ENV_CONCAT(a, b) MG_ENV_CONCAT_(a, b)
+#define MG_REGISTER_ENV(EnvType)                                                          \
+    namespace {                                                                           \
+    struct MG_ENV_CONCAT(mg_env_registrar_, __LINE__) {                                   \
+        MG_ENV_CONCAT(mg_env_registrar_, __LINE__)() {                                    \
+            static const mg_env_ops ops = ::mg::EnvLaunchers<EnvType>::ops();              \
+            mg_env_register(&ops);                                                        \
+        }                                                                                 \
+    } MG_ENV_CONCAT(mg_env_registrar_instance_, __LINE__);                                \
+    }

@@ -49,3 +49,24 @@ def check(rc: int, what: str = "") -> None:
 def call(name: str, *args) -> None:
     """Calls C-ABI function `name` and raises on a non-zero status."""
     check(getattr(lib(), name)(*args), name)
+
+
+class EnvOps(ctypes.Structure):
+    """Layout of mg_env_ops (include/metalgym_b200.h)."""
+
+    _fields_ = [("abi_version", ctypes.c_uint32), ("name", ctypes.c_char_p),
+                ("state_bytes", ctypes.c_uint32), ("action_bytes", ctypes.c_uint32),
+                ("obs_bytes", ctypes.c_uint32), ("obs_dim", ctypes.c_uint32),
+                ("act_dim", ctypes.c_uint32), ("continuous", ctypes.c_uint32),
+                ("step", ctypes.c_void_p), ("run_random", ctypes.c_void_p),
+                ("collect_step", ctypes.c_void_p)]
+
+
+def _env_ops_info(name: str) -> dict:
+    """Sizes and dims of a registered environment."""
+    p = lib().mg_env_find(name.encode())
+    if not p:
+        raise MgError(f"no environment registered as {name!r}")
+    o = EnvOps.from_address(p)
+    return dict(state_bytes=o.state_bytes, action_bytes=o.action_bytes, obs_bytes=o.obs_bytes,
+                obs_dim=o.obs_dim, act_dim=o.act_dim, continuous=o.continuous)

@@ -21,4 +21,31 @@ SIGNATURES = {
     "mg_device_status": (I, [I, PI]),
     # GEMM
     "mg_gemm_bf16": (I, [P, I, I, P, I, I, I, I, I, I, P, I, P, I, I, P]),
+    # environments
+    "mg_env_register": (I, [P]),
+    "mg_env_find": (P, [S]),
+    "mg_env_count": (I, []),
+    "mg_env_name": (S, [I]),
+    "mg_env_init": (I, [S, P, P, P, I, U, U, P]),
+    "mg_env_step": (I, [S, P, P, P, P, P, P, P, I, P]),
+    "mg_env_run_random": (I, [S, P, P, P, P, P, P, I, I, I, I, P]),
+    "mg_env_collect_step": (I, [S, P, P, P, P, P, P, P, P, P, P, P, I, P]),
+    # policy kernels
+    "mg_input_forward": (I, [P, P, P, P, I, I, I, P]),
+    "mg_input_backward_partials": (I, [P, P, P, I, I, I, P]),
+    "mg_input_backward_num_partials": (I, [I]),
+    "mg_layernorm_forward": (I, [P, P, P, P, P, P, I, I, P]),
+    "mg_layernorm_backward": (I, [P, P, P, P, P, P, I, I, P]),
+    "mg_layernorm_backward_num_partials": (I, [I]),
+    "mg_sample_categorical": (I, [P, P, P, P, P, I, I, P]),
+    "mg_sample_gaussian": (I, [P, P, P, P, P, P, I, I, P]),
+    "mg_policy_loss": (I, [P, P, P, P, P, P, P, P, I, I, F, F, F, P]),
+    "mg_gaussian_loss": (I, [P, P, P, P, P, P, P, P, P, P, I, I, F, F, F, P]),
+    "mg_gaussian_loss_num_partials": (I, [I]),
+    "mg_gae": (I, [P, P, P, P, P, P, I, I, I, F, F, P]),
+    "mg_advantage_stats": (I, [P, P, I, I, P]),
+    "mg_reduce_partials": (I, [P, C.c_int64, I, C.c_int64, P, I, P, P]),
+    "mg_reduce_partials_num_norm_partials": (I, [C.c_int64]),
+    "mg_adam_step": (I, [P, P, P, P, P, P, I, C.c_int64, F, F, F, F, P, P]),
+    "mg_stats_mean": (I, [P, I, P, P]),
 }

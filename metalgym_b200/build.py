@@ -29,6 +29,9 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relax
 SOURCES: dict[str, list[str]] = {
     "runtime.cu": [],
     "gemm.cu": [],
+    "policy.cu": [],
+    "envs.cu": [],
+    "envs_builtin.cu": ["--fmad=false"],
 }
 
 

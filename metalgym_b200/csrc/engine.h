@@ -1,0 +1,157 @@
+// The runtime behind the drop-in Gym<Env> / PPOModel<Env> API: a gym core
+// (env buffers, stream, RNG) and a PPO engine (parameters, rollout slots,
+// activations, CUDA graphs), both sized at run time from the registered
+// environment's mg_env_ops. Exposed through the mg_gym_* / mg_ppo_* C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <random>
+#include <vector>
+
+#include "../../include/metalgym_b200.h"
+#include "policy.h"
+
+namespace mg {
+
+// gym.h:15-121: device, stream, and the six per-env buffers.
+struct GymCore {
+    const mg_env_ops* ops = nullptr;
+    int n = 0;
+    int device = 0;
+    uint32_t seed = 0;
+    uint32_t firstEnvId = 0;
+    cudaStream_t stream = nullptr;
+    void* states = nullptr;
+    void* actions = nullptr;
+    void* obs = nullptr;
+    float* reward = nullptr;
+    uint8_t* done = nullptr;
+    uint32_t* rng = nullptr;
+    // pinned staging for run(): actions in, rewards out
+    void* hostActions = nullptr;
+    float* hostReward = nullptr;
+    // rings for run_random (allocated on first use)
+    void* obsRing = nullptr;
+    float* rewardRing = nullptr;
+    uint8_t* doneRing = nullptr;
+    int ringSlots = 0;
+    int steps_rng_reserved = 0;
+
+    ~GymCore();
+};
+
+int gym_create(const char* name, int n, uint32_t seed, uint32_t firstEnvId, int device, GymCore** out);
+
+struct PpoHyper {
+    float clip = 0.2f, valueCoef = 0.5f, entropyCoef = 0.01f, maxGradNorm = 0.5f, gamma = 0.99f, lambda = 0.95f;
+    bool operator==(const PpoHyper& o) const {
+        return clip == o.clip && valueCoef == o.valueCoef && entropyCoef == o.entropyCoef &&
+               maxGradNorm == o.maxGradNorm && gamma == o.gamma && lambda == o.lambda;
+    }
+};
+
+// Per-forward activation pointers (collect shares one set across blocks).
+struct ActSet {
+    void* h;                  // residual stream, R x E bf16 (updated in place)
+    std::vector<void*> lnXn;  // per block, R x E
+    std::vector<void*> lnOut;
+    std::vector<float*> lnSd;
+    std::vector<void*> v;     // per block, R x H (post-ReLU)
+    void* fXn;
+    void* fOut;
+    float* fSd;
+    void* head;  // R x 64
+};
+
+struct ParamSpec {
+    uint32_t count;
+    bool gradIsFloat;
+    uint64_t offset;
+};
+
+class PpoEngine {
+   public:
+    PpoEngine(GymCore* gym, int embed, int scale, int layers, float lr, int horizon, uint32_t seed);
+    ~PpoEngine();
+    int init();  // allocation + seeded init; returns MG_OK or an error
+
+    int collect();
+    int train(int epochs);
+    int trainSlot(int t);
+    int forward();  // on the gym's live obs; head in the collect activations
+    int lastStats(float out6[6]);
+    int setLogStd(float v);
+    int logStd(int k, float* out);
+    int setComm(void* comm, int rank, int world);
+
+    GymCore* gym;
+    int R, O, A, E, H, L, T;
+    bool cont;
+    size_t actBytes;
+    float lr;
+    uint32_t seed;
+    PpoHyper hp;
+    bool rolloutStarted = false;
+    float stepCounter = 0.0f;  // model/ppo.h:265 (float, as the reference)
+    std::mt19937 hostRng;      // slot shuffle (model/ppo.h:349, 920)
+    std::vector<uint32_t> slotOrder;
+
+    std::vector<ParamSpec> params;
+    uint32_t pInW, pInB, pLnFg, pLnFb, pHead, pLogStd;
+    std::vector<uint32_t> pLnG, pLnB, pUp, pDown;
+    uint64_t optCount = 0, optFloatCount = 0;
+
+    // parameter state (device)
+    uint16_t* weights = nullptr;
+    float *master = nullptr, *mom = nullptr, *var = nullptr, *grad = nullptr;
+    // rollout slots (device), layouts of model/ppo.h:336-345
+    float* obsSlots = nullptr;
+    void* actionSlots = nullptr;
+    float *logpSlots = nullptr, *valueSlots = nullptr, *rewardSlots = nullptr, *advSlots = nullptr,
+          *retSlots = nullptr;
+    uint8_t* doneSlots = nullptr;
+    float* advStats = nullptr;  // T x {mean, inv}
+    // activations
+    ActSet collectActs, trainActs;
+    void *dLogits = nullptr, *dStream = nullptr, *dBranch = nullptr, *dV = nullptr;
+    float* stats = nullptr;  // R x 5
+    // gradient partials
+    std::vector<float*> upPart, downPart, lnPart;
+    float *headPart = nullptr, *lnFPart = nullptr, *inPart = nullptr, *lsPart = nullptr;
+    int upSplits = 1, downSplits = 1, headSplits = 1;
+    GradSegmentTable gradTable{};
+    int nNorm = 0;  // CTAs of the finalize kernel = norm partials
+    float* normPartial = nullptr;
+    float* normSq = nullptr;
+    float* statsMean = nullptr;  // 5 floats
+    // per-minibatch schedule: slot index and bias-correction powers
+    int maxSchedule = 0;
+    int* schedSlot = nullptr;      // device
+    float* schedBetaPow = nullptr;  // device, 2 per minibatch
+    int* hostSchedSlot = nullptr;   // pinned
+    float* hostSchedBetaPow = nullptr;
+    // host-side LossStats readback
+    float* hostStats = nullptr;  // pinned, 6 floats
+
+    // graphs
+    cudaGraphExec_t collectExec = nullptr;
+    cudaGraphExec_t trainExec = nullptr;
+    int trainExecMinibatches = 0;
+    PpoHyper collectHp, trainHp;
+
+    // multi-GPU
+    void* comm = nullptr;
+    int rank = 0, world = 1;
+
+   private:
+    int forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st);
+    int minibatch(int j, cudaStream_t st);  // reads schedSlot[j], schedBetaPow[j]
+    int captureCollect();
+    int captureTrain(int minibatches);
+    int ensureSchedule(int n);
+    int checkStatus(const char* what);
+};
+
+}  // namespace mg

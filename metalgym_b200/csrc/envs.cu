@@ -1,0 +1,119 @@
+// Environment registry and the by-name C-ABI wrappers around the kernels
+// that MG_REGISTER_ENV instantiates (include/metalgym/register_env.cuh).
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "metalgym/rng.h"
+#include "runtime.h"
+
+namespace mg {
+namespace {
+
+constexpr int kMaxEnvs = 64;
+
+struct Registry {
+    std::mutex mu;
+    const mg_env_ops* ops[kMaxEnvs] = {};
+    int n = 0;
+};
+
+Registry& registry() {
+    static Registry r;
+    return r;
+}
+
+// gym.h:54-61: done = 1 (the first step resets every env), one seeded
+// xorshift word per env.
+__global__ void k_env_init(uint8_t* done, uint32_t* rng, int n, uint32_t seed, uint32_t first) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    done[i] = 1;
+    rng[i] = mgSeedWord(seed, first + (uint32_t)i);
+}
+
+const mg_env_ops* find_or_fail(const char* name) {
+    const mg_env_ops* o = mg_env_find(name);
+    if (!o) fail(MG_ERR_NOT_FOUND, std::string("no environment registered as '") + (name ? name : "(null)") + "'");
+    return o;
+}
+
+}  // namespace
+}  // namespace mg
+
+extern "C" {
+
+int mg_env_register(const mg_env_ops* ops) {
+    if (!ops || !ops->name || ops->abi_version != MG_VERSION) return mg::fail(MG_ERR_ARGUMENT, "mg_env_register: bad ops");
+    auto& r = mg::registry();
+    std::lock_guard<std::mutex> lock(r.mu);
+    for (int i = 0; i < r.n; i++) {
+        if (std::strcmp(r.ops[i]->name, ops->name) == 0) {
+            r.ops[i] = ops;
+            return MG_OK;
+        }
+    }
+    if (r.n >= mg::kMaxEnvs) return mg::fail(MG_ERR_ARGUMENT, "mg_env_register: registry full");
+    r.ops[r.n++] = ops;
+    return MG_OK;
+}
+
+const mg_env_ops* mg_env_find(const char* kernel_name) {
+    if (!kernel_name) return nullptr;
+    auto& r = mg::registry();
+    std::lock_guard<std::mutex> lock(r.mu);
+    for (int i = 0; i < r.n; i++)
+        if (std::strcmp(r.ops[i]->name, kernel_name) == 0) return r.ops[i];
+    return nullptr;
+}
+
+int mg_env_count(void) {
+    auto& r = mg::registry();
+    std::lock_guard<std::mutex> lock(r.mu);
+    return r.n;
+}
+
+const char* mg_env_name(int i) {
+    auto& r = mg::registry();
+    std::lock_guard<std::mutex> lock(r.mu);
+    return (i >= 0 && i < r.n) ? r.ops[i]->name : nullptr;
+}
+
+int mg_env_init(const char* kernel_name, void* states, uint8_t* done, uint32_t* rng, int n, uint32_t seed,
+                uint32_t first_env_id, mg_stream_t stream) {
+    const mg_env_ops* o = mg::find_or_fail(kernel_name);
+    if (!o) return MG_ERR_NOT_FOUND;
+    MG_CHECK_ARG(states && done && rng && n > 0, "mg_env_init: bad arguments");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    MG_CUDA_TRY(cudaMemsetAsync(states, 0, (size_t)n * o->state_bytes, st));
+    mg::k_env_init<<<(n + 255) / 256, 256, 0, st>>>(done, rng, n, seed, first_env_id);
+    return mg::check_launch("k_env_init");
+}
+
+int mg_env_step(const char* kernel_name, void* states, const void* actions, void* obs, float* reward, uint8_t* done,
+                uint8_t* done_copy, uint32_t* rng, int n, mg_stream_t stream) {
+    const mg_env_ops* o = mg::find_or_fail(kernel_name);
+    if (!o) return MG_ERR_NOT_FOUND;
+    int rc = o->step(states, actions, obs, reward, done, done_copy, rng, n, stream);
+    return rc ? mg::fail(rc, "env step launch failed") : MG_OK;
+}
+
+int mg_env_run_random(const char* kernel_name, void* states, void* obs_ring, float* reward_ring, uint8_t* done_ring,
+                      uint8_t* done, uint32_t* rng, int n, int steps, int ring, int mode, mg_stream_t stream) {
+    const mg_env_ops* o = mg::find_or_fail(kernel_name);
+    if (!o) return MG_ERR_NOT_FOUND;
+    int rc = o->run_random(states, obs_ring, reward_ring, done_ring, done, rng, n, steps, ring, mode, stream);
+    return rc ? mg::fail(rc, "env run_random launch failed") : MG_OK;
+}
+
+int mg_env_collect_step(const char* kernel_name, const void* head, const void* log_std, void* states,
+                        void* action_out, float* logp_out, float* value_out, void* obs_out, float* reward_out,
+                        uint8_t* done, uint8_t* done_slot, uint32_t* rng, int n, mg_stream_t stream) {
+    const mg_env_ops* o = mg::find_or_fail(kernel_name);
+    if (!o) return MG_ERR_NOT_FOUND;
+    int rc = o->collect_step(head, log_std, states, action_out, logp_out, value_out, obs_out, reward_out, done,
+                             done_slot, rng, n, stream);
+    return rc ? mg::fail(rc, "env collect_step launch failed") : MG_OK;
+}
+
+}  // extern "C"

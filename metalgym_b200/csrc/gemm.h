@@ -24,4 +24,12 @@ struct GemmCall {
 
 int gemm_bf16(const GemmCall& c, cudaStream_t st);
 
+// Number of K-splits gemm_bf16 actually launches when asked for `splits`
+// (each split covers a multiple of 64 of K).
+inline int gemm_effective_splits(int K, int splits) {
+    int kps = (K + splits - 1) / splits;
+    kps = (kps + 63) / 64 * 64;
+    return (K + kps - 1) / kps;
+}
+
 }  // namespace mg

@@ -1,0 +1,858 @@
+// Row-wise kernels of the PPO hot path and their C-ABI entry points.
+// The dense products live in gemm.cu; everything else lives here.
+#include <algorithm>
+
+#include "policy.h"
+#include "policy_kernels.cuh"
+#include "runtime.h"
+
+namespace mg {
+
+namespace {
+
+constexpr int kLnRowsPerCta = 64;      // LayerNorm backward: rows per CTA (8 warps x 8 rows)
+constexpr int kInputRowsPerCta = 128;  // input backward: rows per CTA
+constexpr int kGaussRowsPerCta = 256;  // Gaussian loss: rows per CTA
+
+// ------------------------------------------------------------------ input
+
+// model/input.metal:11-27: out[r, c] = bf16(b[c] + sum_k obs[r, k] * W[k, c]),
+// summed in k order with separate roundings. One warp per row.
+template <int VPT>
+__global__ void k_input_forward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ w,
+                                const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int rows,
+                                int inDim, int outDim, const int* __restrict__ slotIdx, int64_t slotStride) {
+    extern __shared__ float s_w[];  // inDim x outDim as fp32
+    if (slotIdx) obs += (int64_t)(*slotIdx) * slotStride;
+    for (int i = threadIdx.x; i < inDim * outDim; i += blockDim.x) s_w[i] = bf(w[i]);
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int c0 = lane * VPT;
+    float b[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; j++) b[j] = bf(bias[c0 + j]);
+    for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += gridDim.x * (blockDim.x >> 5)) {
+        float acc[VPT];
+#pragma unroll
+        for (int j = 0; j < VPT; j++) acc[j] = b[j];
+        const float* o = obs + (size_t)r * inDim;
+        for (int k = 0; k < inDim; k++) {
+            const float ok = o[k];
+#pragma unroll
+            for (int j = 0; j < VPT; j++) acc[j] = __fadd_rn(acc[j], __fmul_rn(ok, s_w[k * outDim + c0 + j]));
+        }
+        __nv_bfloat16* dst = out + (size_t)r * outDim + c0;
+#pragma unroll
+        for (int j = 0; j < VPT; j += 2) *reinterpret_cast<__nv_bfloat162*>(dst + j) = __floats2bfloat162_rn(acc[j], acc[j + 1]);
+    }
+}
+
+// model/input.metal:38-60: per-CTA partial sums over a chunk of rows of
+// dW[k, c] = sum_r obs[r, k] dZ[r, c] and db[c] = sum_r dZ[r, c].
+// partial[blockIdx] = [(inDim + 1) x outDim]: rows 0..inDim-1 dW, row inDim db.
+__global__ void k_input_backward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ dZ,
+                                 float* __restrict__ partial, int rows, int inDim, int outDim,
+                                 const int* __restrict__ slotIdx, int64_t slotStride) {
+    extern __shared__ float s_obs[];  // kInputRowsPerCta x inDim
+    if (slotIdx) obs += (int64_t)(*slotIdx) * slotStride;
+    const int r0 = blockIdx.x * kInputRowsPerCta;
+    const int nr = min(kInputRowsPerCta, rows - r0);
+    for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) s_obs[i] = obs[(size_t)r0 * inDim + i];
+    __syncthreads();
+    float* part = partial + (size_t)blockIdx.x * (inDim + 1) * outDim;
+    for (int c = threadIdx.x; c < outDim; c += blockDim.x) {
+        float accB = 0.0f;
+        for (int k0 = 0; k0 < inDim; k0 += 8) {
+            float acc[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) acc[k] = 0.0f;
+            for (int r = 0; r < nr; r++) {
+                const float d = bf(dZ[(size_t)(r0 + r) * outDim + c]);
+                if (k0 == 0) accB = __fadd_rn(accB, d);
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (k0 + k < inDim) acc[k] = __fadd_rn(acc[k], __fmul_rn(s_obs[r * inDim + k0 + k], d));
+            }
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (k0 + k < inDim) part[(size_t)(k0 + k) * outDim + c] = acc[k];
+        }
+        part[(size_t)inDim * outDim + c] = accB;
+    }
+}
+
+// -------------------------------------------------------------- layernorm
+
+// model/layernorm.metal:10-71. One warp per row; lane l owns VPT consecutive
+// columns. Two-pass mean / population variance, sigma = sqrt(var + 1e-5).
+template <int VPT>
+__global__ void k_layernorm_forward(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ xNorm,
+                                    __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gamma,
+                                    const __nv_bfloat16* __restrict__ beta, float* __restrict__ stdev, int rows) {
+    constexpr int E = VPT * 32;
+    const int lane = threadIdx.x & 31;
+    const int c0 = lane * VPT;
+    float g[VPT], b[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+        g[j] = bf(gamma[c0 + j]);
+        b[j] = bf(beta[c0 + j]);
+    }
+    for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += gridDim.x * (blockDim.x >> 5)) {
+        float v[VPT];
+        const __nv_bfloat16* xr = x + (size_t)r * E + c0;
+#pragma unroll
+        for (int j = 0; j < VPT; j += 2) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xr + j));
+            v[j] = f.x;
+            v[j + 1] = f.y;
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < VPT; j++) s = __fadd_rn(s, v[j]);
+        const float mean = __fdiv_rn(warp_sum(s), (float)E);
+        float q = 0.0f;
+#pragma unroll
+        for (int j = 0; j < VPT; j++) {
+            const float d = __fsub_rn(v[j], mean);
+            q = __fadd_rn(q, __fmul_rn(d, d));
+        }
+        const float var = __fdiv_rn(warp_sum(q), (float)E);
+        const float sd = __fsqrt_rn(__fadd_rn(var, 1e-5f));
+        const float rstd = __fdiv_rn(1.0f, sd);
+        if (lane == 0) stdev[r] = sd;
+        __nv_bfloat16* xn_out = xNorm + (size_t)r * E + c0;
+        __nv_bfloat16* y_out = out + (size_t)r * E + c0;
+#pragma unroll
+        for (int j = 0; j < VPT; j += 2) {
+            const float xn0 = __fmul_rn(__fsub_rn(v[j], mean), rstd);
+            const float xn1 = __fmul_rn(__fsub_rn(v[j + 1], mean), rstd);
+            *reinterpret_cast<__nv_bfloat162*>(xn_out + j) = __floats2bfloat162_rn(xn0, xn1);
+            *reinterpret_cast<__nv_bfloat162*>(y_out + j) = __floats2bfloat162_rn(
+                __fadd_rn(__fmul_rn(g[j], xn0), b[j]), __fadd_rn(__fmul_rn(g[j + 1], xn1), b[j + 1]));
+        }
+    }
+}
+
+// model/layernorm.metal:74-127 (+ model/elementwise.metal:4-13 when resid is
+// given). Per row: dxhat = bf16(dz * gamma); dx = bf16((dxhat - mean(dxhat)
+// - xhat * mean(bf16(dxhat * xhat))) / sigma). Without resid dx overwrites dZ;
+// with resid, resid = bf16(dx + resid) and dZ is left as is. dgamma
+// (sum of bf16(xhat * dz)) and dbeta (sum of dz) are summed over this CTA's
+// rows into partial[blockIdx] = [dgamma (E) | dbeta (E)].
+template <int VPT>
+__global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __restrict__ dZ,
+                                                            const __nv_bfloat16* __restrict__ xNorm,
+                                                            const __nv_bfloat16* __restrict__ gamma,
+                                                            const float* __restrict__ stdev,
+                                                            __nv_bfloat16* __restrict__ resid,
+                                                            float* __restrict__ partial, int rows) {
+    constexpr int E = VPT * 32;
+    __shared__ float s_red[8][2 * E];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int c0 = lane * VPT;
+    float g[VPT], dg[VPT], db[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+        g[j] = bf(gamma[c0 + j]);
+        dg[j] = 0.0f;
+        db[j] = 0.0f;
+    }
+    const int r0 = blockIdx.x * kLnRowsPerCta;
+    const int r1 = min(rows, r0 + kLnRowsPerCta);
+    for (int r = r0 + warp; r < r1; r += 8) {
+        float dz[VPT], xn[VPT], dxn[VPT];
+        const size_t base = (size_t)r * E + c0;
+#pragma unroll
+        for (int j = 0; j < VPT; j += 2) {
+            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dZ + base + j));
+            const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xNorm + base + j));
+            dz[j] = a.x;
+            dz[j + 1] = a.y;
+            xn[j] = c.x;
+            xn[j + 1] = c.y;
+        }
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < VPT; j++) {
+            dg[j] = __fadd_rn(dg[j], rbf(__fmul_rn(xn[j], dz[j])));
+            db[j] = __fadd_rn(db[j], dz[j]);
+            dxn[j] = rbf(__fmul_rn(dz[j], g[j]));
+            s1 = __fadd_rn(s1, dxn[j]);
+            s2 = __fadd_rn(s2, rbf(__fmul_rn(dxn[j], xn[j])));
+        }
+        const float m1 = __fdiv_rn(warp_sum(s1), (float)E);
+        const float m2 = __fdiv_rn(warp_sum(s2), (float)E);
+        const float rdev = __fdiv_rn(1.0f, stdev[r]);
+        float dx[VPT];
+#pragma unroll
+        for (int j = 0; j < VPT; j++) dx[j] = __fmul_rn(rdev, __fsub_rn(__fsub_rn(dxn[j], m1), __fmul_rn(xn[j], m2)));
+        if (resid) {
+#pragma unroll
+            for (int j = 0; j < VPT; j += 2) {
+                __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(resid + base + j);
+                const float2 o = __bfloat1622float2(*p);
+                *p = __floats2bfloat162_rn(__fadd_rn(rbf(dx[j]), o.x), __fadd_rn(rbf(dx[j + 1]), o.y));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < VPT; j += 2)
+                *reinterpret_cast<__nv_bfloat162*>(dZ + base + j) = __floats2bfloat162_rn(dx[j], dx[j + 1]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < VPT; j++) {
+        s_red[warp][c0 + j] = dg[j];
+        s_red[warp][E + c0 + j] = db[j];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 2 * E; i += blockDim.x) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int w2 = 0; w2 < 8; w2++) acc = __fadd_rn(acc, s_red[w2][i]);
+        partial[(size_t)blockIdx.x * 2 * E + i] = acc;
+    }
+}
+
+// ------------------------------------------------------- sampling / losses
+
+__global__ void k_sample_categorical(const __nv_bfloat16* __restrict__ head, uint32_t* __restrict__ rng,
+                                     int32_t* __restrict__ action, float* __restrict__ logProb,
+                                     float* __restrict__ value, int rows, int actDim) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    uint32_t s = rng[r];
+    float lp, v;
+    action[r] = sample_categorical_row(head + (size_t)r * kHeadDim, actDim, s, lp, v);
+    rng[r] = s;
+    logProb[r] = lp;
+    value[r] = v;
+}
+
+__global__ void k_sample_gaussian(const __nv_bfloat16* __restrict__ head, const __nv_bfloat16* __restrict__ logStd,
+                                  uint32_t* __restrict__ rng, float* __restrict__ action, float* __restrict__ logProb,
+                                  float* __restrict__ value, int rows, int actDim) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    uint32_t s = rng[r];
+    float lp, v;
+    sample_gaussian_row(head + (size_t)r * kHeadDim, logStd, actDim, s, action + (size_t)r * actDim, lp, v);
+    rng[r] = s;
+    logProb[r] = lp;
+    value[r] = v;
+}
+
+__device__ __forceinline__ float norm_adv(const float* adv, const float* advStats, int r) {
+    // model/gae.metal:76: (a - mean) * inv, inv = 1 / (sigma + 1e-8)
+    return advStats ? __fmul_rn(__fsub_rn(adv[r], advStats[0]), advStats[1]) : adv[r];
+}
+
+// model/policy.metal:14-69. One thread per row.
+__global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int32_t* __restrict__ action,
+                              const float* __restrict__ adv, const float* __restrict__ advStats,
+                              const float* __restrict__ ret, const float* __restrict__ oldLogProb,
+                              __nv_bfloat16* __restrict__ dZ, float* __restrict__ stats, int rows, int actDim,
+                              LossHyper hp, int* status, const int* __restrict__ slotIdx) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    if (slotIdx) {  // slot-major rollout buffers: slot s starts at s * rows
+        const int64_t s = *slotIdx;
+        action += s * rows;
+        adv += s * rows;
+        ret += s * rows;
+        oldLogProb += s * rows;
+        if (advStats) advStats += 2 * s;
+    }
+    const float scale = __fdiv_rn(1.0f, (float)rows);
+    const __nv_bfloat16* h = head + (size_t)r * kHeadDim;
+    float rowMax = -INFINITY;
+    for (int j = 0; j < actDim; j++) rowMax = fmaxf(rowMax, bf(h[j]));
+    float sum = 0.0f;
+    for (int j = 0; j < actDim; j++) sum = __fadd_rn(sum, mg_expf(__fsub_rn(bf(h[j]), rowMax)));
+    const float lse = __fadd_rn(rowMax, mg_logf(sum));
+    float entropy = 0.0f;
+    for (int j = 0; j < actDim; j++) {
+        const float logp = __fsub_rn(bf(h[j]), lse);
+        entropy = __fsub_rn(entropy, __fmul_rn(mg_expf(logp), logp));
+    }
+    const int a = action[r];
+    if (a < 0 || a >= actDim) {  // never index the head with an invalid action
+        record_error(status, kDevBadAction);
+        return;
+    }
+    const float A = norm_adv(adv, advStats, r);
+    const float logpA = __fsub_rn(bf(h[a]), lse);
+    const float ratio = mg_expf(__fsub_rn(logpA, oldLogProb[r]));
+    const float surr1 = __fmul_rn(ratio, A);
+    const float surr2 = __fmul_rn(fminf(fmaxf(ratio, __fsub_rn(1.0f, hp.clip)), __fadd_rn(1.0f, hp.clip)), A);
+    const float policyLoss = -fminf(surr1, surr2);
+    const float gLogp = (surr1 <= surr2) ? __fmul_rn(-A, ratio) : 0.0f;
+    uint32_t packed[kHeadDim / 2];
+#pragma unroll
+    for (int i = 0; i < kHeadDim / 2; i++) packed[i] = 0;
+    __nv_bfloat16* pz = reinterpret_cast<__nv_bfloat16*>(packed);
+    for (int j = 0; j < actDim; j++) {
+        const float logp = __fsub_rn(bf(h[j]), lse);
+        const float prob = mg_expf(logp);
+        const float g = __fadd_rn(__fmul_rn(gLogp, __fsub_rn(j == a ? 1.0f : 0.0f, prob)),
+                                  __fmul_rn(__fmul_rn(hp.entropyCoef, prob), __fadd_rn(logp, entropy)));
+        pz[j] = tobf(__fmul_rn(g, scale));
+    }
+    const float vErr = __fsub_rn(bf(h[actDim]), ret[r]);
+    pz[actDim] = tobf(__fmul_rn(__fmul_rn(hp.valueCoef, vErr), scale));
+    uint4* dst = reinterpret_cast<uint4*>(dZ + (size_t)r * kHeadDim);
+    const uint4* src = reinterpret_cast<const uint4*>(packed);
+#pragma unroll
+    for (int i = 0; i < kHeadDim / 8; i++) dst[i] = src[i];
+    float* st = stats + (size_t)r * 5;
+    st[0] = policyLoss;
+    st[1] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, hp.valueCoef), vErr), vErr);
+    st[2] = entropy;
+    st[3] = __fsub_rn(oldLogProb[r], logpA);
+    st[4] = (fabsf(__fsub_rn(ratio, 1.0f)) > hp.clip) ? 1.0f : 0.0f;
+}
+
+// model/gaussian.metal:76-135. One thread per row; the log-std gradient is a
+// batch sum, summed per CTA into partial[blockIdx][k].
+__global__ void __launch_bounds__(kGaussRowsPerCta) k_gaussian_loss(
+    const __nv_bfloat16* __restrict__ head, const float* __restrict__ action, const float* __restrict__ adv,
+    const float* __restrict__ advStats, const float* __restrict__ ret, const float* __restrict__ oldLogProb,
+    __nv_bfloat16* __restrict__ dZ, float* __restrict__ stats, const __nv_bfloat16* __restrict__ logStd,
+    float* __restrict__ partial, int rows, int actDim, LossHyper hp, const int* __restrict__ slotIdx) {
+    __shared__ float s_gls[kGaussRowsPerCta];
+    if (slotIdx) {
+        const int64_t s = *slotIdx;
+        action += s * rows * actDim;
+        adv += s * rows;
+        ret += s * rows;
+        oldLogProb += s * rows;
+        if (advStats) advStats += 2 * s;
+    }
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = r < rows;
+    const float scale = __fdiv_rn(1.0f, (float)rows);
+    float gLogp = 0.0f;
+    if (live) {
+        const __nv_bfloat16* h = head + (size_t)r * kHeadDim;
+        const float* act = action + (size_t)r * actDim;
+        float logp = 0.0f, entropy = 0.0f;
+        for (int k = 0; k < actDim; k++) {
+            const float ls = bf(logStd[k]);
+            const float d = __fmul_rn(__fsub_rn(act[k], bf(h[k])), mg_expf(-ls));
+            logp = __fadd_rn(logp, __fsub_rn(__fsub_rn(__fmul_rn(__fmul_rn(-0.5f, d), d), ls), kLogSqrt2Pi));
+            entropy = __fadd_rn(entropy, __fadd_rn(__fadd_rn(ls, kLogSqrt2Pi), 0.5f));
+        }
+        const float A = norm_adv(adv, advStats, r);
+        const float ratio = mg_expf(__fsub_rn(logp, oldLogProb[r]));
+        const float surr1 = __fmul_rn(ratio, A);
+        const float surr2 = __fmul_rn(fminf(fmaxf(ratio, __fsub_rn(1.0f, hp.clip)), __fadd_rn(1.0f, hp.clip)), A);
+        const float policyLoss = -fminf(surr1, surr2);
+        gLogp = (surr1 <= surr2) ? __fmul_rn(-A, ratio) : 0.0f;
+        uint32_t packed[kHeadDim / 2];
+#pragma unroll
+        for (int i = 0; i < kHeadDim / 2; i++) packed[i] = 0;
+        __nv_bfloat16* pz = reinterpret_cast<__nv_bfloat16*>(packed);
+        for (int k = 0; k < actDim; k++) {
+            const float ls = bf(logStd[k]);
+            const float invStd = mg_expf(-ls);
+            const float d = __fmul_rn(__fsub_rn(act[k], bf(h[k])), invStd);
+            pz[k] = tobf(__fmul_rn(__fmul_rn(__fmul_rn(gLogp, d), invStd), scale));
+        }
+        const float vErr = __fsub_rn(bf(h[actDim]), ret[r]);
+        pz[actDim] = tobf(__fmul_rn(__fmul_rn(hp.valueCoef, vErr), scale));
+        uint4* dst = reinterpret_cast<uint4*>(dZ + (size_t)r * kHeadDim);
+        const uint4* src = reinterpret_cast<const uint4*>(packed);
+#pragma unroll
+        for (int i = 0; i < kHeadDim / 8; i++) dst[i] = src[i];
+        float* st = stats + (size_t)r * 5;
+        st[0] = policyLoss;
+        st[1] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, hp.valueCoef), vErr), vErr);
+        st[2] = entropy;
+        st[3] = __fsub_rn(oldLogProb[r], logp);
+        st[4] = (fabsf(__fsub_rn(ratio, 1.0f)) > hp.clip) ? 1.0f : 0.0f;
+    }
+    for (int k = 0; k < actDim; k++) {
+        float gls = 0.0f;
+        if (live) {
+            const float ls = bf(logStd[k]);
+            const float invStd = mg_expf(-ls);
+            const float d = __fmul_rn(__fsub_rn(action[(size_t)r * actDim + k], bf(head[(size_t)r * kHeadDim + k])),
+                                      invStd);
+            gls = __fmul_rn(__fsub_rn(__fmul_rn(gLogp, __fsub_rn(__fmul_rn(d, d), 1.0f)), hp.entropyCoef), scale);
+        }
+        s_gls[threadIdx.x] = gls;
+        __syncthreads();
+        for (int w = blockDim.x >> 1; w > 0; w >>= 1) {
+            if (threadIdx.x < w) s_gls[threadIdx.x] = __fadd_rn(s_gls[threadIdx.x], s_gls[threadIdx.x + w]);
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) partial[(size_t)blockIdx.x * actDim + k] = s_gls[0];
+        __syncthreads();
+    }
+}
+
+// --------------------------------------------------------------------- GAE
+
+// model/gae.metal:14-36: one thread per env, reverse scan over the T slots of
+// the slot-major buffers [t * rows + i]; the bootstrap value is column actDim
+// of the last forward's head. Operation order as the reference (no FMA).
+__global__ void k_gae(const float* __restrict__ reward, const uint8_t* __restrict__ done,
+                      const float* __restrict__ value, const __nv_bfloat16* __restrict__ bootHead,
+                      float* __restrict__ advantage, float* __restrict__ ret, int rows, int horizon, int actDim,
+                      float gamma, float lambda) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows) return;
+    float lastAdv = 0.0f;
+    float nextValue = bf(bootHead[(size_t)i * kHeadDim + actDim]);
+    const float gl = __fmul_rn(gamma, lambda);
+    for (int t = horizon - 1; t >= 0; t--) {
+        const size_t k = (size_t)t * rows + i;
+        const float nonTerminal = done[k] ? 0.0f : 1.0f;
+        const float v = value[k];
+        const float delta = __fsub_rn(__fadd_rn(reward[k], __fmul_rn(__fmul_rn(gamma, nextValue), nonTerminal)), v);
+        lastAdv = __fadd_rn(delta, __fmul_rn(__fmul_rn(gl, nonTerminal), lastAdv));
+        advantage[k] = lastAdv;
+        ret[k] = __fadd_rn(lastAdv, v);
+        nextValue = v;
+    }
+}
+
+// model/gae.metal:42-77 statistics: for minibatch (slot) s, mean and
+// inv = 1 / (population std + 1e-8) of adv[s * rows .. s * rows + rows).
+__global__ void __launch_bounds__(1024) k_adv_stats(const float* __restrict__ adv, float* __restrict__ out, int rows) {
+    __shared__ float s_part[32];
+    __shared__ float s_mean;
+    const float* a = adv + (size_t)blockIdx.x * rows;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < rows; i += blockDim.x) s = __fadd_rn(s, a[i]);
+    s = warp_sum(s);
+    if (lane == 0) s_part[warp] = s;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < nw ? s_part[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) s_mean = __fdiv_rn(t, (float)rows);
+    }
+    __syncthreads();
+    const float mean = s_mean;
+    float q = 0.0f;
+    for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+        const float d = __fsub_rn(a[i], mean);
+        q = __fadd_rn(q, __fmul_rn(d, d));
+    }
+    q = warp_sum(q);
+    __syncthreads();
+    if (lane == 0) s_part[warp] = q;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < nw ? s_part[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) {
+            const float var = __fdiv_rn(t, (float)rows);
+            out[2 * blockIdx.x] = mean;
+            out[2 * blockIdx.x + 1] = __fdiv_rn(1.0f, __fadd_rn(__fsqrt_rn(var), 1e-8f));
+        }
+    }
+}
+
+// ------------------------------------------------------ gradients and Adam
+
+// Sums the partials of every gradient segment into the flat fp32 gradient
+// arena (model/elementwise.metal:21-31 for the GEMM weights, whose sum is
+// rounded to bf16 as the reference's bf16 gradient arena stores it; the
+// LayerNorm / input / log-std sums stay fp32) and writes one partial sum of
+// squares per CTA for the global norm (model/optimizer.metal:23-34).
+__global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ GradSegmentTable tab,
+                                                       float* __restrict__ grad, float* __restrict__ normPartial) {
+    __shared__ float s_red[8];
+    int b = blockIdx.x, si = 0;
+    while (si < tab.n - 1 && b >= tab.seg[si].blockEnd) si++;
+    const GradSegment& sg = tab.seg[si];
+    const int blockBase = si == 0 ? 0 : tab.seg[si - 1].blockEnd;
+    const int64_t i0 = (int64_t)(b - blockBase) * 1024;
+    float sq = 0.0f;
+    for (int j = 0; j < 4; j++) {
+        const int64_t i = i0 + j * 256 + threadIdx.x;
+        if (i < sg.count) {
+            float acc = 0.0f;
+            const float* src = sg.src + i;
+            for (int p = 0; p < sg.nparts; p++) acc = __fadd_rn(acc, src[(size_t)p * sg.partStride]);
+            if (sg.roundBf16) acc = rbf(acc);
+            grad[sg.dstOffset + i] = acc;
+            sq = __fadd_rn(sq, __fmul_rn(acc, acc));
+        }
+    }
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < 8; w++) t = __fadd_rn(t, s_red[w]);
+        normPartial[blockIdx.x] = t;
+    }
+}
+
+// Sum of squares of grad[0..count) in fixed-size CTA partials (used after a
+// cross-GPU all-reduce, which also rescales the sum to a mean).
+__global__ void __launch_bounds__(256) k_grad_scale_norm(float* __restrict__ grad, int64_t count, float scale,
+                                                         float* __restrict__ normPartial) {
+    __shared__ float s_red[8];
+    float sq = 0.0f;
+    const int64_t i0 = (int64_t)blockIdx.x * 1024;
+    for (int j = 0; j < 4; j++) {
+        const int64_t i = i0 + j * 256 + threadIdx.x;
+        if (i < count) {
+            const float g = __fmul_rn(grad[i], scale);
+            grad[i] = g;
+            sq = __fadd_rn(sq, __fmul_rn(g, g));
+        }
+    }
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < 8; w++) t = __fadd_rn(t, s_red[w]);
+        normPartial[blockIdx.x] = t;
+    }
+}
+
+// model/optimizer.metal:36-60 with the host bias-correction powers of
+// model/ppo.h:879-880 (from betaPow[0..1] if given, else the scalars).
+// Every CTA first sums the norm partials in the same order, so all agree.
+__global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const float* __restrict__ grad,
+                                              float* __restrict__ mom, float* __restrict__ var,
+                                              __nv_bfloat16* __restrict__ weights,
+                                              const float* __restrict__ normPartial, int nNorm, int64_t count,
+                                              AdamHyper hp, const float* __restrict__ betaPow,
+                                              float* __restrict__ normSqOut) {
+    __shared__ float s_scale;
+    if (threadIdx.x < 32) {
+        float s = 0.0f;
+        for (int i = threadIdx.x; i < nNorm; i += 32) s = __fadd_rn(s, normPartial[i]);
+        s = warp_sum(s);
+        if (threadIdx.x == 0) {
+            const float norm = __fsqrt_rn(s);
+            s_scale = (hp.maxGradNorm > 0.0f && norm > hp.maxGradNorm)
+                          ? __fdiv_rn(hp.maxGradNorm, __fadd_rn(norm, 1e-6f))
+                          : 1.0f;
+            if (blockIdx.x == 0 && normSqOut) *normSqOut = s;
+        }
+    }
+    __syncthreads();
+    const float scale = s_scale;
+    const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+    const float b1p = betaPow ? betaPow[0] : hp.beta1Pow;
+    const float b2p = betaPow ? betaPow[1] : hp.beta2Pow;
+    const float c1 = __fsub_rn(1.0f, b1p), c2 = __fsub_rn(1.0f, b2p);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+        const float g = __fmul_rn(grad[i], scale);
+        const float m = __fadd_rn(__fmul_rn(b1, mom[i]), __fmul_rn(__fsub_rn(1.0f, b1), g));
+        const float v = __fadd_rn(__fmul_rn(b2, var[i]), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
+        mom[i] = m;
+        var[i] = v;
+        const float mHat = __fdiv_rn(m, c1);
+        const float vHat = __fdiv_rn(v, c2);
+        const float x = __fsub_rn(param[i], __fdiv_rn(__fmul_rn(hp.lr, mHat), __fadd_rn(__fsqrt_rn(vHat), eps)));
+        param[i] = x;
+        weights[i] = tobf(x);
+    }
+}
+
+// LossStats (model/ppo.h:925-943): column means of the rows x 5 stats.
+__global__ void __launch_bounds__(256) k_stats_mean(const float* __restrict__ stats, int rows, float* __restrict__ out) {
+    __shared__ float s_red[8][5];
+    float acc[5] = {0, 0, 0, 0, 0};
+    for (int r = threadIdx.x; r < rows; r += blockDim.x)
+        for (int k = 0; k < 5; k++) acc[k] = __fadd_rn(acc[k], stats[(size_t)r * 5 + k]);
+    for (int k = 0; k < 5; k++) {
+        const float s = warp_sum(acc[k]);
+        if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5][k] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x < 5) {
+        float t = 0.0f;
+        for (int w = 0; w < 8; w++) t = __fadd_rn(t, s_red[w][threadIdx.x]);
+        out[threadIdx.x] = __fmul_rn(t, __fdiv_rn(1.0f, (float)rows));
+    }
+}
+
+int grid_rows(int rows, int rowsPerCta) { return (rows + rowsPerCta - 1) / rowsPerCta; }
+
+}  // namespace
+
+// ------------------------------------------------------------ host launchers
+
+int input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int inDim, int outDim,
+                  cudaStream_t st, const int* slotIdx, int64_t slotStride) {
+    MG_CHECK_ARG(rows > 0 && inDim > 0 && outDim % 64 == 0 && outDim <= 1024, "input_forward: bad shape");
+    MG_CHECK_ARG(inDim * outDim * 4 <= 160 * 1024, "input_forward: weight too large for shared memory");
+    const int blocks = std::min(grid_rows(rows, 8), 148 * 8);
+    const size_t sm = (size_t)inDim * outDim * 4;
+    auto W = static_cast<const __nv_bfloat16*>(w);
+    auto B = static_cast<const __nv_bfloat16*>(b);
+    auto O = static_cast<__nv_bfloat16*>(out);
+#define MG_IN_FWD(V)                                                                               \
+    case V:                                                                                        \
+        if (sm > 48 * 1024)                                                                        \
+            MG_CUDA_TRY(cudaFuncSetAttribute(k_input_forward<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
+        k_input_forward<V><<<blocks, 256, sm, st>>>(obs, W, B, O, rows, inDim, outDim, slotIdx, slotStride); \
+        break;
+    switch (outDim / 32) {
+        MG_IN_FWD(2) MG_IN_FWD(4) MG_IN_FWD(8) MG_IN_FWD(16) MG_IN_FWD(32)
+        default: return fail(MG_ERR_ARGUMENT, "input_forward: out_dim must be 64, 128, 256, 512 or 1024");
+    }
+#undef MG_IN_FWD
+    return check_launch("k_input_forward");
+}
+
+int input_backward_parts(int rows) { return grid_rows(rows, kInputRowsPerCta); }
+
+int input_backward(const float* obs, const void* dZ, float* partial, int rows, int inDim, int outDim,
+                   cudaStream_t st, const int* slotIdx, int64_t slotStride) {
+    MG_CHECK_ARG(rows > 0 && inDim > 0 && inDim <= 256 && outDim > 0 && outDim <= 1024, "input_backward: bad shape");
+    const size_t sm = (size_t)kInputRowsPerCta * inDim * 4;
+    if (sm > 48 * 1024)
+        MG_CUDA_TRY(cudaFuncSetAttribute(k_input_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    k_input_backward<<<input_backward_parts(rows), std::min(outDim, 1024), sm, st>>>(
+        obs, static_cast<const __nv_bfloat16*>(dZ), partial, rows, inDim, outDim, slotIdx, slotStride);
+    return check_launch("k_input_backward");
+}
+
+int layernorm_forward(const void* x, void* xNorm, void* out, const void* gamma, const void* beta, float* stdev,
+                      int rows, int cols, cudaStream_t st) {
+    MG_CHECK_ARG(rows > 0, "layernorm_forward: rows must be > 0");
+    const int blocks = std::min(grid_rows(rows, 8), 148 * 16);
+    auto X = static_cast<const __nv_bfloat16*>(x);
+    auto XN = static_cast<__nv_bfloat16*>(xNorm);
+    auto Y = static_cast<__nv_bfloat16*>(out);
+    auto G = static_cast<const __nv_bfloat16*>(gamma);
+    auto Bt = static_cast<const __nv_bfloat16*>(beta);
+    switch (cols) {
+        case 64: k_layernorm_forward<2><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
+        case 128: k_layernorm_forward<4><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
+        case 256: k_layernorm_forward<8><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
+        case 512: k_layernorm_forward<16><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
+        case 1024: k_layernorm_forward<32><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
+        default: return fail(MG_ERR_ARGUMENT, "layernorm: cols must be 64, 128, 256, 512 or 1024");
+    }
+    return check_launch("k_layernorm_forward");
+}
+
+int layernorm_backward_parts(int rows) { return grid_rows(rows, kLnRowsPerCta); }
+
+int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, void* resid,
+                       float* partial, int rows, int cols, cudaStream_t st) {
+    MG_CHECK_ARG(rows > 0, "layernorm_backward: rows must be > 0");
+    const int blocks = layernorm_backward_parts(rows);
+    auto DZ = static_cast<__nv_bfloat16*>(dZ);
+    auto XN = static_cast<const __nv_bfloat16*>(xNorm);
+    auto G = static_cast<const __nv_bfloat16*>(gamma);
+    auto R = static_cast<__nv_bfloat16*>(resid);
+    switch (cols) {
+        case 64: k_layernorm_backward<2><<<blocks, 256, 0, st>>>(DZ, XN, G, stdev, R, partial, rows); break;
+        case 128: k_layernorm_backward<4><<<blocks, 256, 0, st>>>(DZ, XN, G, stdev, R, partial, rows); break;
+        case 256: k_layernorm_backward<8><<<blocks, 256, 0, st>>>(DZ, XN, G, stdev, R, partial, rows); break;
+        case 512: k_layernorm_backward<16><<<blocks, 256, 0, st>>>(DZ, XN, G, stdev, R, partial, rows); break;
+        default: return fail(MG_ERR_ARGUMENT, "layernorm_backward: cols must be 64, 128, 256 or 512");
+    }
+    return check_launch("k_layernorm_backward");
+}
+
+int sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* logProb, float* value, int rows,
+                       int actDim, cudaStream_t st) {
+    MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "sample_categorical: bad shape");
+    k_sample_categorical<<<grid_rows(rows, 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(head), rng, action,
+                                                                logProb, value, rows, actDim);
+    return check_launch("k_sample_categorical");
+}
+
+int sample_gaussian(const void* head, const void* logStd, uint32_t* rng, float* action, float* logProb,
+                    float* value, int rows, int actDim, cudaStream_t st) {
+    MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "sample_gaussian: bad shape");
+    k_sample_gaussian<<<grid_rows(rows, 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(head),
+                                                             static_cast<const __nv_bfloat16*>(logStd), rng, action,
+                                                             logProb, value, rows, actDim);
+    return check_launch("k_sample_gaussian");
+}
+
+int policy_loss(const void* head, const int32_t* action, const float* adv, const float* advStats, const float* ret,
+                const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
+                cudaStream_t st, const int* slotIdx) {
+    MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "policy_loss: bad shape");
+    k_policy_loss<<<grid_rows(rows, 128), 128, 0, st>>>(static_cast<const __nv_bfloat16*>(head), action, adv,
+                                                         advStats, ret, oldLogProb, static_cast<__nv_bfloat16*>(dZ),
+                                                         stats, rows, actDim, hp, status_ptr(), slotIdx);
+    return check_launch("k_policy_loss");
+}
+
+int gaussian_loss_parts(int rows) { return grid_rows(rows, kGaussRowsPerCta); }
+
+int gaussian_loss(const void* head, const float* action, const float* adv, const float* advStats, const float* ret,
+                  const float* oldLogProb, void* dZ, float* stats, const void* logStd, float* partial, int rows,
+                  int actDim, LossHyper hp, cudaStream_t st, const int* slotIdx) {
+    MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "gaussian_loss: bad shape");
+    k_gaussian_loss<<<gaussian_loss_parts(rows), kGaussRowsPerCta, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(head), action, adv, advStats, ret, oldLogProb,
+        static_cast<__nv_bfloat16*>(dZ), stats, static_cast<const __nv_bfloat16*>(logStd), partial, rows, actDim, hp,
+        slotIdx);
+    return check_launch("k_gaussian_loss");
+}
+
+int gae(const float* reward, const uint8_t* done, const float* value, const void* bootHead, float* adv, float* ret,
+        int rows, int horizon, int actDim, float gamma, float lambda, cudaStream_t st) {
+    MG_CHECK_ARG(rows > 0 && horizon > 0, "gae: bad shape");
+    k_gae<<<grid_rows(rows, 128), 128, 0, st>>>(reward, done, value, static_cast<const __nv_bfloat16*>(bootHead), adv,
+                                                 ret, rows, horizon, actDim, gamma, lambda);
+    return check_launch("k_gae");
+}
+
+int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStream_t st) {
+    MG_CHECK_ARG(rows > 0 && slots > 0, "advantage_stats: bad shape");
+    k_adv_stats<<<slots, 1024, 0, st>>>(adv, out, rows);
+    return check_launch("k_adv_stats");
+}
+
+int grad_table_layout(GradSegmentTable& tab) {
+    int b = 0;
+    for (int i = 0; i < tab.n; i++) {
+        b += (int)((tab.seg[i].count + 1023) / 1024);
+        tab.seg[i].blockEnd = b;
+    }
+    return b;
+}
+
+int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st) {
+    MG_CHECK_ARG(tab.n > 0 && tab.n <= kMaxGradSegments, "grad_finalize: bad segment count");
+    const int nblocks = tab.seg[tab.n - 1].blockEnd;
+    MG_CHECK_ARG(nblocks > 0, "grad_finalize: empty");
+    k_grad_finalize<<<nblocks, 256, 0, st>>>(tab, grad, normPartial);
+    return check_launch("k_grad_finalize");
+}
+
+int grad_scale_norm_blocks(int64_t count) { return (int)((count + 1023) / 1024); }
+
+int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st) {
+    k_grad_scale_norm<<<grad_scale_norm_blocks(count), 256, 0, st>>>(grad, count, scale, normPartial);
+    return check_launch("k_grad_scale_norm");
+}
+
+int adam(float* param, const float* grad, float* mom, float* var, void* weights, const float* normPartial, int nNorm,
+         int64_t count, AdamHyper hp, const float* betaPow, float* normSqOut, cudaStream_t st) {
+    MG_CHECK_ARG(count > 0 && nNorm > 0, "adam: bad shape");
+    const int blocks = (int)std::min<int64_t>((count + 255) / 256, 148 * 8);
+    k_adam<<<blocks, 256, 0, st>>>(param, grad, mom, var, static_cast<__nv_bfloat16*>(weights), normPartial, nNorm,
+                                   count, hp, betaPow, normSqOut);
+    return check_launch("k_adam");
+}
+
+int stats_mean(const float* stats, int rows, float* out, cudaStream_t st) {
+    k_stats_mean<<<1, 256, 0, st>>>(stats, rows, out);
+    return check_launch("k_stats_mean");
+}
+
+}  // namespace mg
+
+// ------------------------------------------------------------------ C ABI
+
+using mg::LossHyper;
+using mg::AdamHyper;
+
+#define MG_STREAM(s) reinterpret_cast<cudaStream_t>(s)
+
+extern "C" {
+
+int mg_input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int in_dim, int out_dim,
+                     mg_stream_t s) {
+    return mg::input_forward(obs, w, b, out, rows, in_dim, out_dim, MG_STREAM(s));
+}
+
+int mg_input_backward_partials(const float* obs, const void* dZ, float* partial, int rows, int in_dim, int out_dim,
+                               mg_stream_t s) {
+    return mg::input_backward(obs, dZ, partial, rows, in_dim, out_dim, MG_STREAM(s));
+}
+
+int mg_input_backward_num_partials(int rows) { return mg::input_backward_parts(rows); }
+
+int mg_layernorm_forward(const void* x, void* x_norm, void* out, const void* gamma, const void* beta, float* stdev,
+                         int rows, int cols, mg_stream_t s) {
+    return mg::layernorm_forward(x, x_norm, out, gamma, beta, stdev, rows, cols, MG_STREAM(s));
+}
+
+int mg_layernorm_backward(void* dZ, const void* x_norm, const void* gamma, const float* stdev, void* resid,
+                          float* partial, int rows, int cols, mg_stream_t s) {
+    return mg::layernorm_backward(dZ, x_norm, gamma, stdev, resid, partial, rows, cols, MG_STREAM(s));
+}
+
+int mg_layernorm_backward_num_partials(int rows) { return mg::layernorm_backward_parts(rows); }
+
+int mg_sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* log_prob, float* value, int rows,
+                          int act_dim, mg_stream_t s) {
+    return mg::sample_categorical(head, rng, action, log_prob, value, rows, act_dim, MG_STREAM(s));
+}
+
+int mg_sample_gaussian(const void* head, const void* log_std, uint32_t* rng, float* action, float* log_prob,
+                       float* value, int rows, int act_dim, mg_stream_t s) {
+    return mg::sample_gaussian(head, log_std, rng, action, log_prob, value, rows, act_dim, MG_STREAM(s));
+}
+
+int mg_policy_loss(const void* head, const int32_t* action, const float* adv, const float* adv_stats,
+                   const float* ret, const float* old_log_prob, void* dZ, float* stats, int rows, int act_dim,
+                   float clip, float value_coef, float entropy_coef, mg_stream_t s) {
+    LossHyper hp{clip, value_coef, entropy_coef};
+    return mg::policy_loss(head, action, adv, adv_stats, ret, old_log_prob, dZ, stats, rows, act_dim, hp,
+                           MG_STREAM(s));
+}
+
+int mg_gaussian_loss(const void* head, const float* action, const float* adv, const float* adv_stats,
+                     const float* ret, const float* old_log_prob, void* dZ, float* stats, const void* log_std,
+                     float* dlogstd_partial, int rows, int act_dim, float clip, float value_coef, float entropy_coef,
+                     mg_stream_t s) {
+    LossHyper hp{clip, value_coef, entropy_coef};
+    return mg::gaussian_loss(head, action, adv, adv_stats, ret, old_log_prob, dZ, stats, log_std, dlogstd_partial,
+                             rows, act_dim, hp, MG_STREAM(s));
+}
+
+int mg_gaussian_loss_num_partials(int rows) { return mg::gaussian_loss_parts(rows); }
+
+int mg_gae(const float* reward, const uint8_t* done, const float* value, const void* bootstrap_head, float* adv,
+           float* ret, int rows, int horizon, int act_dim, float gamma, float lambda, mg_stream_t s) {
+    return mg::gae(reward, done, value, bootstrap_head, adv, ret, rows, horizon, act_dim, gamma, lambda, MG_STREAM(s));
+}
+
+int mg_advantage_stats(const float* adv, float* stats_out, int rows, int slots, mg_stream_t s) {
+    return mg::advantage_stats(adv, stats_out, rows, slots, MG_STREAM(s));
+}
+
+int mg_reduce_partials(const float* partial, int64_t part_stride, int nparts, int64_t count, float* out,
+                       int round_bf16, float* norm_partial, mg_stream_t s) {
+    MG_CHECK_ARG(partial && out && norm_partial && nparts > 0 && count > 0, "reduce_partials: bad arguments");
+    mg::GradSegmentTable tab{};
+    tab.n = 1;
+    tab.seg[0].src = partial;
+    tab.seg[0].partStride = part_stride;
+    tab.seg[0].nparts = nparts;
+    tab.seg[0].count = count;
+    tab.seg[0].dstOffset = 0;
+    tab.seg[0].roundBf16 = round_bf16;
+    mg::grad_table_layout(tab);
+    return mg::grad_finalize(tab, out, norm_partial, MG_STREAM(s));
+}
+
+int mg_reduce_partials_num_norm_partials(int64_t count) { return (int)((count + 1023) / 1024); }
+
+int mg_adam_step(float* master, const float* grad, float* momentum, float* variance, void* weights,
+                 const float* norm_partial, int n_norm_partials, int64_t count, float lr, float beta1_pow,
+                 float beta2_pow, float max_grad_norm, float* norm_sq_out, mg_stream_t s) {
+    AdamHyper hp{lr, max_grad_norm, beta1_pow, beta2_pow};
+    return mg::adam(master, grad, momentum, variance, weights, norm_partial, n_norm_partials, count, hp, nullptr,
+                    norm_sq_out, MG_STREAM(s));
+}
+
+int mg_stats_mean(const float* stats, int rows, float* out5, mg_stream_t s) {
+    return mg::stats_mean(stats, rows, out5, MG_STREAM(s));
+}
+
+}  // extern "C"

@@ -1,0 +1,79 @@
+// Internal host interface of the row-wise policy kernels (policy.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mg {
+
+// PPO loss coefficients (model/policy.metal:5-12).
+struct LossHyper {
+    float clip;
+    float valueCoef;
+    float entropyCoef;
+};
+
+// Adam settings (model/optimizer.metal:5-15); betas (0.9, 0.999), eps 1e-8 fixed.
+struct AdamHyper {
+    float lr;
+    float maxGradNorm;
+    float beta1Pow;  // used when no device beta-power pointer is given
+    float beta2Pow;
+};
+
+// One parameter's gradient: `nparts` partial sums, `partStride` floats apart,
+// each `count` long, summed into grad[dstOffset ...].
+struct GradSegment {
+    const float* src;
+    int64_t partStride;
+    int64_t count;
+    int64_t dstOffset;
+    int nparts;
+    int roundBf16;  // 1: round the sum to bf16 (GEMM weight gradients)
+    int blockEnd;   // filled by grad_table_layout
+    int pad;
+};
+
+constexpr int kMaxGradSegments = 40;
+struct GradSegmentTable {
+    GradSegment seg[kMaxGradSegments];
+    int n;
+};
+
+// Loss kernels and the input projection take an optional device slot index
+// (slotIdx[0]) that selects slot s of the slot-major rollout buffers.
+// slotIdx (device, optional): read obs at obs + slotIdx[0] * slotStride.
+int input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int inDim, int outDim,
+                  cudaStream_t st, const int* slotIdx = nullptr, int64_t slotStride = 0);
+int input_backward_parts(int rows);
+int input_backward(const float* obs, const void* dZ, float* partial, int rows, int inDim, int outDim,
+                   cudaStream_t st, const int* slotIdx = nullptr, int64_t slotStride = 0);
+int layernorm_forward(const void* x, void* xNorm, void* out, const void* gamma, const void* beta, float* stdev,
+                      int rows, int cols, cudaStream_t st);
+int layernorm_backward_parts(int rows);
+int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, void* resid,
+                       float* partial, int rows, int cols, cudaStream_t st);
+int sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* logProb, float* value, int rows,
+                       int actDim, cudaStream_t st);
+int sample_gaussian(const void* head, const void* logStd, uint32_t* rng, float* action, float* logProb,
+                    float* value, int rows, int actDim, cudaStream_t st);
+int policy_loss(const void* head, const int32_t* action, const float* adv, const float* advStats, const float* ret,
+                const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
+                cudaStream_t st, const int* slotIdx = nullptr);
+int gaussian_loss_parts(int rows);
+int gaussian_loss(const void* head, const float* action, const float* adv, const float* advStats, const float* ret,
+                  const float* oldLogProb, void* dZ, float* stats, const void* logStd, float* partial, int rows,
+                  int actDim, LossHyper hp, cudaStream_t st, const int* slotIdx = nullptr);
+int gae(const float* reward, const uint8_t* done, const float* value, const void* bootHead, float* adv, float* ret,
+        int rows, int horizon, int actDim, float gamma, float lambda, cudaStream_t st);
+int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStream_t st);
+// Fills blockEnd of every segment; returns the number of CTAs (= norm partials).
+int grad_table_layout(GradSegmentTable& tab);
+int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st);
+int grad_scale_norm_blocks(int64_t count);
+int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st);
+int adam(float* param, const float* grad, float* mom, float* var, void* weights, const float* normPartial, int nNorm,
+         int64_t count, AdamHyper hp, const float* betaPow, float* normSqOut, cudaStream_t st);
+int stats_mean(const float* stats, int rows, float* out, cudaStream_t st);
+
+}  // namespace mg

@@ -21,6 +21,7 @@ enum DeviceError : int {
     kDevTimeoutEmpty = 2,  // MMA never released a stage
     kDevTimeoutDone = 3,   // accumulator never completed
     kDevBadShape = 4,
+    kDevBadAction = 5,     // an action index outside [0, ACT_DIM) reached the loss
 };
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait

@@ -244,6 +244,11 @@ ORC_API void orc_policy_loss(const uint16_t* head, const int32_t* action, const 
             entropy -= mg_expf(logp) * logp;
         }
         const uint32_t a = (uint32_t)action[row];
+        if (a >= actDim) {  // invalid action: no gradient, NaN statistics
+            for (uint32_t j = 0; j < headDim; j++) dz[j] = 0;
+            for (int k = 0; k < 5; k++) stats[(size_t)row * 5 + k] = NAN;
+            continue;
+        }
         const float A = adv[row];
         const float logpA = bf2f(h[a]) - lse;
         const float ratio = mg_expf(logpA - oldLogProb[row]);

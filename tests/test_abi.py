@@ -1,0 +1,60 @@
+"""The C ABI: every function declared in include/metalgym_b200.h is exported
+by the built library and has a ctypes signature; no compute (CPU only)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_functions():
+    text = (ROOT / "include" / "metalgym_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"typedef struct mg_env_ops \{.*?\} mg_env_ops;", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mg_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_matches_ctypes_table():
+    from metalgym_b200._abi import SIGNATURES
+
+    assert declared_functions() == sorted(SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    import metalgym_b200
+
+    if not metalgym_b200.LIB_PATH.exists():
+        pytest.fail("libmetalgym_b200.so not built: run __graft_entry__.build()")
+    lib = ctypes.CDLL(str(metalgym_b200.LIB_PATH))
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_builtin_envs_registered_and_sized():
+    """Loading the library registers the reference's three example envs with
+    the reference's struct sizes (no GPU work)."""
+    import metalgym_b200
+    from metalgym_b200 import _env_ops_info
+
+    lib = metalgym_b200.lib()
+    names = {lib.mg_env_name(i).decode() for i in range(lib.mg_env_count())}
+    assert {"rollout_cartpole", "rollout_cartpole_continuous", "rollout_voxelnav"} <= names
+    from orc import ENV_SIZES
+
+    for name, (sb, ab, ob, od, ad, cont) in ENV_SIZES.items():
+        info = _env_ops_info(name)
+        assert info == dict(state_bytes=sb, action_bytes=ab, obs_bytes=ob, obs_dim=od, act_dim=ad,
+                            continuous=int(cont)), name
+
+
+def test_errors_are_reported_without_a_gpu():
+    import metalgym_b200
+
+    lib = metalgym_b200.lib()
+    rc = lib.mg_env_step(b"no_such_env", None, None, None, None, None, None, None, 4, None)
+    assert rc == 5  # MG_ERR_NOT_FOUND
+    assert b"no_such_env" in lib.mg_last_error()
+    rc = lib.mg_gemm_bf16(None, 0, 64, None, 0, 64, 128, 128, 64, 0, None, 128, None, 0, 1, None)
+    assert rc == 1  # MG_ERR_ARGUMENT (checked before any CUDA call)
