@@ -206,6 +206,113 @@ int mg_adam_step(float* master, const float* grad, float* momentum, float* varia
 /* Column means of the [rows][5] loss statistics (model/ppo.h:925-943). */
 int mg_stats_mean(const float* stats, int rows, float* out5, mg_stream_t stream);
 
+/* ---------------------------------------------------------------- sessions */
+
+/* A gym session: the env buffers of gym.h:15-121 on one device, with its
+ * own stream. Replaces Gym<Env>'s Metal device, queue and shared buffers. */
+typedef struct mg_gym_s* mg_gym_t;
+/* A PPO session borrowing a gym (model/ppo.h:145-147): parameters, rollout
+ * slots, activations and the collect / train CUDA graphs. */
+typedef struct mg_ppo_s* mg_ppo_t;
+
+enum mg_gym_buffer { MG_GYM_STATES = 0, MG_GYM_ACTIONS = 1, MG_GYM_OBS = 2, MG_GYM_REWARD = 3, MG_GYM_DONE = 4,
+                     MG_GYM_RNG = 5 };
+enum mg_ppo_buffer {
+    MG_PPO_OBS_SLOTS = 0,    /* (T+1) x rows x OBS_DIM fp32   (model/ppo.h:470) */
+    MG_PPO_ACTION_SLOTS = 1, /* T x rows x Action              (model/ppo.h:471) */
+    MG_PPO_LOGP_SLOTS = 2,   /* T x rows fp32 */
+    MG_PPO_VALUE_SLOTS = 3,  /* T x rows fp32                   (model/ppo.h:474) */
+    MG_PPO_REWARD_SLOTS = 4, /* T x rows fp32                   (model/ppo.h:472) */
+    MG_PPO_DONE_SLOTS = 5,   /* T x rows uint8                  (model/ppo.h:473) */
+    MG_PPO_ADV_SLOTS = 6,    /* T x rows fp32                   (model/ppo.h:475) */
+    MG_PPO_RET_SLOTS = 7,    /* T x rows fp32                   (model/ppo.h:476) */
+    MG_PPO_HEAD = 8,         /* rows x 64 bf16: head of the last collect / forward (model/ppo.h:450-452) */
+    MG_PPO_WEIGHTS = 9,      /* opt_count bf16 weight arena     (model/ppo.h:266) */
+    MG_PPO_MASTER = 10,      /* opt_count fp32 master           (model/ppo.h:269) */
+    MG_PPO_MOMENTUM = 11,    /* opt_count fp32 Adam m */
+    MG_PPO_VARIANCE = 12,    /* opt_count fp32 Adam v */
+    MG_PPO_GRAD = 13,        /* opt_count fp32 gradient of the last minibatch */
+    MG_PPO_STATS = 14,       /* rows x 5 fp32 loss statistics of the last minibatch */
+    MG_PPO_ADV_STATS = 15,   /* T x {mean, 1/(std + 1e-8)} per-slot advantage statistics */
+    MG_PPO_TRAIN_HEAD = 16   /* rows x 64 bf16: head of the last minibatch forward */
+};
+
+/* Gym(int p) of gym.h:36-72 (+ optional seed, first env id for sharded
+ * multi-GPU gyms, device; -1 = current). done starts at 1, rng per
+ * mg_env_init. */
+int mg_gym_create(const char* kernel_name, int parallels, uint32_t seed, uint32_t first_env_id, int device,
+                  mg_gym_t* gym);
+int mg_gym_destroy(mg_gym_t gym);
+/* parallels, state/action/obs bytes, obs_dim, act_dim, continuous, device. */
+int mg_gym_info(mg_gym_t gym, uint32_t out[8]);
+/* gym.run (gym.h:110-121): uploads parallels actions from host memory
+ * (skipped if actions_host is NULL), steps every env once, copies the first
+ * reward_count rewards back and waits. */
+int mg_gym_run(mg_gym_t gym, const void* actions_host, float* reward_host, int reward_count);
+/* `steps` device-side steps with the random policy of mg_env_ops.run_random
+ * (obs / reward of the last step are left in the live buffers). Asynchronous. */
+int mg_gym_run_random(mg_gym_t gym, int steps, int mode);
+int mg_gym_buffer(mg_gym_t gym, int which, void** dev_ptr, size_t* bytes);
+/* Synchronous copies of a whole gym buffer (at most `bytes`). */
+int mg_gym_download(mg_gym_t gym, int which, void* host, size_t bytes);
+int mg_gym_upload(mg_gym_t gym, int which, const void* host, size_t bytes);
+int mg_gym_stream(mg_gym_t gym, mg_stream_t* stream);
+int mg_gym_synchronize(mg_gym_t gym);
+
+/* PPOModel(gym, e, s, layers, lr, T, seed) of model/ppo.h:274-446: seeded
+ * init, parameter layout, slots. Fails (instead of exit(1)) on bad sizes. */
+int mg_ppo_create(mg_gym_t gym, int embed, int scale, int layers, float lr, int horizon, uint32_t seed,
+                  mg_ppo_t* model);
+int mg_ppo_destroy(mg_ppo_t model);
+/* rows, obs_dim, act_dim, embed, hidden, layers, horizon, opt_count,
+ * opt_float_count, parameter count, continuous, action bytes. */
+int mg_ppo_info(mg_ppo_t model, uint64_t out[12]);
+/* Parameter i in creation order (inW, inB, {ln.g, ln.b, up, down} x L,
+ * lnF.g, lnF.b, head, [logStd]): element offset, count, gradient kind. */
+int mg_ppo_param_info(mg_ppo_t model, int i, uint64_t* offset, uint32_t* count, int* grad_is_float);
+/* collect() (model/ppo.h:716-751); blocks until done. */
+int mg_ppo_collect(mg_ppo_t model);
+/* train(epochs) (model/ppo.h:918-923); blocks until done. */
+int mg_ppo_train(mg_ppo_t model, int epochs);
+/* trainSlot(t) (model/ppo.h:906-916); blocks until done. */
+int mg_ppo_train_slot(mg_ppo_t model, int t);
+/* forward() on the gym's live obs (model/ppo.h:628-634); blocks. */
+int mg_ppo_forward(mg_ppo_t model);
+/* lastStats() (model/ppo.h:925-943): policy, value, entropy, approxKl,
+ * clipFrac, gradNorm (pre-clip). */
+int mg_ppo_last_stats(mg_ppo_t model, float out6[6]);
+/* The public hyperparameter fields of model/ppo.h:186-191 (read on every
+ * collect / train call): clip, valueCoef, entropyCoef, maxGradNorm, gamma, lambda. */
+int mg_ppo_set_hyper(mg_ppo_t model, float clip, float value_coef, float entropy_coef, float max_grad_norm,
+                     float gamma, float lambda);
+int mg_ppo_get_hyper(mg_ppo_t model, float out6[6]);
+/* setLogStd / logStdValue (model/ppo.h:454-469), continuous envs only. */
+int mg_ppo_set_log_std(mg_ppo_t model, float v);
+int mg_ppo_log_std(mg_ppo_t model, int k, float* out);
+/* Adam step counter (model/ppo.h:265, 874). */
+int mg_ppo_step_counter(mg_ppo_t model, float* out);
+int mg_ppo_set_step_counter(mg_ppo_t model, float step);
+/* Device pointer / synchronous copies of a model buffer (mg_ppo_buffer);
+ * slot selects one slot of a slotted buffer, -1 the whole buffer. */
+int mg_ppo_buffer(mg_ppo_t model, int which, int slot, void** dev_ptr, size_t* bytes);
+int mg_ppo_download(mg_ppo_t model, int which, int slot, void* host, size_t bytes);
+int mg_ppo_upload(mg_ppo_t model, int which, int slot, const void* host, size_t bytes);
+/* Data parallelism (no counterpart in the reference): with world > 1 each
+ * minibatch's gradient is summed over the ranks of `comm` (an ncclComm_t)
+ * and divided by world before the norm clip and Adam. */
+int mg_ppo_set_comm(mg_ppo_t model, void* comm, int rank, int world);
+
+/* ---------------------------------------------------------------- NCCL / host memory */
+
+/* NCCL communicator helpers (libnccl.so.2 is loaded on first use). */
+int mg_comm_unique_id(void* out128);
+int mg_comm_init(int world, int rank, const void* id128, int device, void** comm);
+int mg_comm_destroy(void* comm);
+int mg_allreduce_sum_f32(float* data, size_t count, void* comm, mg_stream_t stream);
+/* Pinned host memory for the host mirrors of the drop-in API (zeroed). */
+int mg_host_alloc(size_t bytes, void** out);
+int mg_host_free(void* p);
+
 #ifdef __cplusplus
 }
 #endif

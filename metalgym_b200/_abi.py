@@ -48,4 +48,41 @@ SIGNATURES = {
     "mg_reduce_partials_num_norm_partials": (I, [C.c_int64]),
     "mg_adam_step": (I, [P, P, P, P, P, P, I, C.c_int64, F, F, F, F, P, P]),
     "mg_stats_mean": (I, [P, I, P, P]),
+    # sessions
+    "mg_gym_create": (I, [S, I, U, U, I, C.POINTER(P)]),
+    "mg_gym_destroy": (I, [P]),
+    "mg_gym_info": (I, [P, P]),
+    "mg_gym_run": (I, [P, P, P, I]),
+    "mg_gym_run_random": (I, [P, I, I]),
+    "mg_gym_buffer": (I, [P, I, C.POINTER(P), C.POINTER(C.c_size_t)]),
+    "mg_gym_download": (I, [P, I, P, C.c_size_t]),
+    "mg_gym_upload": (I, [P, I, P, C.c_size_t]),
+    "mg_gym_stream": (I, [P, C.POINTER(P)]),
+    "mg_gym_synchronize": (I, [P]),
+    "mg_ppo_create": (I, [P, I, I, I, F, I, U, C.POINTER(P)]),
+    "mg_ppo_destroy": (I, [P]),
+    "mg_ppo_info": (I, [P, P]),
+    "mg_ppo_param_info": (I, [P, I, C.POINTER(U64), C.POINTER(U), PI]),
+    "mg_ppo_collect": (I, [P]),
+    "mg_ppo_train": (I, [P, I]),
+    "mg_ppo_train_slot": (I, [P, I]),
+    "mg_ppo_forward": (I, [P]),
+    "mg_ppo_last_stats": (I, [P, P]),
+    "mg_ppo_set_hyper": (I, [P, F, F, F, F, F, F]),
+    "mg_ppo_get_hyper": (I, [P, P]),
+    "mg_ppo_set_log_std": (I, [P, F]),
+    "mg_ppo_log_std": (I, [P, I, PF]),
+    "mg_ppo_step_counter": (I, [P, PF]),
+    "mg_ppo_set_step_counter": (I, [P, F]),
+    "mg_ppo_buffer": (I, [P, I, I, C.POINTER(P), C.POINTER(C.c_size_t)]),
+    "mg_ppo_download": (I, [P, I, I, P, C.c_size_t]),
+    "mg_ppo_upload": (I, [P, I, I, P, C.c_size_t]),
+    "mg_ppo_set_comm": (I, [P, P, I, I]),
+    # NCCL / host memory
+    "mg_comm_unique_id": (I, [P]),
+    "mg_comm_init": (I, [I, I, P, I, C.POINTER(P)]),
+    "mg_comm_destroy": (I, [P]),
+    "mg_allreduce_sum_f32": (I, [P, C.c_size_t, P, P]),
+    "mg_host_alloc": (I, [C.c_size_t, C.POINTER(P)]),
+    "mg_host_free": (I, [P]),
 }

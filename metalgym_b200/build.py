@@ -32,6 +32,8 @@ SOURCES: dict[str, list[str]] = {
     "policy.cu": [],
     "envs.cu": [],
     "envs_builtin.cu": ["--fmad=false"],
+    "engine.cu": [],
+    "capi_session.cu": [],
 }
 
 

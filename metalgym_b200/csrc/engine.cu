@@ -1,0 +1,756 @@
+// PPO engine: the orchestration of model/ppo.h (PPOModel) and gym.h (Gym)
+// rebuilt on the B200 kernels of this library.
+//
+//   collect()  model/ppo.h:716-751  one CUDA graph: T x (forward, fused
+//              sample + env step) + bootstrap forward + GAE + per-slot
+//              advantage statistics
+//   train(e)   model/ppo.h:918-923  one CUDA graph for all e x T minibatches;
+//              the host shuffles the slot order with the seeded mt19937 and
+//              computes the Adam bias-correction powers (model/ppo.h:873-880),
+//              the graph reads them from device memory per minibatch
+//   minibatch  model/ppo.h:906-916  forward (activations saved), loss,
+//              backward (dX GEMMs with fused mask / LayerNorm-backward +
+//              residual epilogues, split-K dW GEMMs into fp32 partials),
+//              gradient finalisation + norm, [all-reduce], Adam
+#include "engine.h"
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+
+#include "gemm.h"
+#include "runtime.h"
+
+namespace mg {
+
+namespace {
+
+constexpr int kHead = 64;  // model/ppo.h:116
+
+template <class T>
+int dalloc(T** p, size_t bytes) {
+    void* v = nullptr;
+    cudaError_t e = cudaMalloc(&v, bytes ? bytes : 16);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    *p = static_cast<T*>(v);
+    return MG_OK;
+}
+
+#define MG_TRY(expr)              \
+    do {                          \
+        int mg_rc_ = (expr);      \
+        if (mg_rc_) return mg_rc_; \
+    } while (0)
+
+// ---- NCCL, loaded on first use (the process may already hold torch's copy)
+struct Nccl {
+    decltype(&ncclGetUniqueId) getUniqueId = nullptr;
+    decltype(&ncclCommInitRank) commInitRank = nullptr;
+    decltype(&ncclCommDestroy) commDestroy = nullptr;
+    decltype(&ncclAllReduce) allReduce = nullptr;
+    decltype(&ncclGetErrorString) errorString = nullptr;
+    bool ok = false;
+};
+
+Nccl& nccl() {
+    static Nccl n;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (h) {
+            n.getUniqueId = reinterpret_cast<decltype(&ncclGetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+            n.commInitRank = reinterpret_cast<decltype(&ncclCommInitRank)>(dlsym(h, "ncclCommInitRank"));
+            n.commDestroy = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));
+            n.allReduce = reinterpret_cast<decltype(&ncclAllReduce)>(dlsym(h, "ncclAllReduce"));
+            n.errorString = reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
+            n.ok = n.getUniqueId && n.commInitRank && n.commDestroy && n.allReduce && n.errorString;
+        }
+    }
+    return n;
+}
+
+int nccl_fail(ncclResult_t r, const char* what) {
+    Nccl& n = nccl();
+    return fail(MG_ERR_COMM, std::string(what) + ": " + (n.errorString ? n.errorString(r) : "nccl error"));
+}
+
+uint16_t host_f2bf(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+float host_bf2f(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+int splits_for(int M, int N, int K, int bn) {
+    const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    int s = (256 + tiles - 1) / tiles;
+    const int maxS = K / 256 > 1 ? K / 256 : 1;
+    if (s > maxS) s = maxS;
+    if (s < 1) s = 1;
+    return gemm_effective_splits(K, s);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ gym
+
+GymCore::~GymCore() {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    cudaFree(states);
+    cudaFree(actions);
+    cudaFree(obs);
+    cudaFree(reward);
+    cudaFree(done);
+    cudaFree(rng);
+    cudaFree(obsRing);
+    cudaFree(rewardRing);
+    cudaFree(doneRing);
+    cudaFreeHost(hostActions);
+    cudaFreeHost(hostReward);
+    if (stream) cudaStreamDestroy(stream);
+    cudaSetDevice(cur);
+}
+
+// gym.h:36-72
+int gym_create(const char* name, int n, uint32_t seed, uint32_t firstEnvId, int device, GymCore** out) {
+    const mg_env_ops* ops = mg_env_find(name);
+    if (!ops) return fail(MG_ERR_NOT_FOUND, std::string("no environment registered as '") + (name ? name : "") + "'");
+    MG_CHECK_ARG(n > 0, "gym: parallels must be > 0");
+    if (device >= 0) MG_CUDA_TRY(cudaSetDevice(device));
+    else MG_CUDA_TRY(cudaGetDevice(&device));
+    GymCore* g = new GymCore();
+    g->ops = ops;
+    g->n = n;
+    g->device = device;
+    g->seed = seed;
+    g->firstEnvId = firstEnvId;
+    int rc = MG_OK;
+    auto chk = [&](cudaError_t e, const char* w) {
+        if (e != cudaSuccess && rc == MG_OK) rc = cuda_fail(e, w);
+    };
+    chk(cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking), "stream");
+    if (!rc) rc = dalloc(&g->states, (size_t)n * ops->state_bytes);
+    if (!rc) rc = dalloc(&g->actions, (size_t)n * ops->action_bytes);
+    if (!rc) rc = dalloc(&g->obs, (size_t)n * ops->obs_bytes);
+    if (!rc) rc = dalloc(&g->reward, (size_t)n * 4);
+    if (!rc) rc = dalloc(&g->done, (size_t)n);
+    if (!rc) rc = dalloc(&g->rng, (size_t)n * 4);
+    if (!rc) chk(cudaMallocHost(&g->hostActions, (size_t)n * ops->action_bytes), "cudaMallocHost");
+    if (!rc) chk(cudaMallocHost(reinterpret_cast<void**>(&g->hostReward), (size_t)n * 4), "cudaMallocHost");
+    if (!rc) {
+        std::memset(g->hostActions, 0, (size_t)n * ops->action_bytes);
+        chk(cudaMemsetAsync(g->actions, 0, (size_t)n * ops->action_bytes, g->stream), "memset actions");
+        chk(cudaMemsetAsync(g->obs, 0, (size_t)n * ops->obs_bytes, g->stream), "memset obs");
+        chk(cudaMemsetAsync(g->reward, 0, (size_t)n * 4, g->stream), "memset reward");
+    }
+    if (!rc) rc = mg_env_init(name, g->states, g->done, g->rng, n, seed, firstEnvId, reinterpret_cast<mg_stream_t>(g->stream));
+    if (!rc) chk(cudaStreamSynchronize(g->stream), "gym init sync");
+    if (rc) {
+        delete g;
+        return rc;
+    }
+    status_ptr();  // resolve the status word before any graph capture
+    *out = g;
+    return MG_OK;
+}
+
+// ------------------------------------------------------------------ engine
+
+PpoEngine::PpoEngine(GymCore* g, int embed, int scale, int layers, float learningRate, int horizon, uint32_t s)
+    : gym(g), R(g->n), O((int)g->ops->obs_dim), A((int)g->ops->act_dim), E(embed), H(embed * scale), L(layers),
+      T(horizon), cont(g->ops->continuous != 0), actBytes(g->ops->action_bytes), lr(learningRate), seed(s) {}
+
+PpoEngine::~PpoEngine() {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(gym->device);
+    cudaStreamSynchronize(gym->stream);
+    if (collectExec) cudaGraphExecDestroy(collectExec);
+    if (trainExec) cudaGraphExecDestroy(trainExec);
+    void* ptrs[] = {weights, master, mom, var, grad, obsSlots, actionSlots, logpSlots, valueSlots, rewardSlots,
+                    advSlots, retSlots, doneSlots, advStats, dLogits, dStream, dBranch, dV, stats, headPart,
+                    lnFPart, inPart, lsPart, normPartial, normSq, statsMean, schedSlot, schedBetaPow};
+    for (void* p : ptrs) cudaFree(p);
+    for (auto* p : upPart) cudaFree(p);
+    for (auto* p : downPart) cudaFree(p);
+    for (auto* p : lnPart) cudaFree(p);
+    auto freeActs = [](ActSet& a, bool shared) {
+        cudaFree(a.h);
+        cudaFree(a.fXn);
+        cudaFree(a.fOut);
+        cudaFree(a.fSd);
+        cudaFree(a.head);
+        const size_t n = shared ? 1 : a.v.size();
+        for (size_t i = 0; i < n && i < a.v.size(); i++) {
+            cudaFree(a.lnXn[i]);
+            cudaFree(a.lnOut[i]);
+            cudaFree(a.lnSd[i]);
+            cudaFree(a.v[i]);
+        }
+    };
+    freeActs(trainActs, false);
+    freeActs(collectActs, true);
+    cudaFreeHost(hostSchedSlot);
+    cudaFreeHost(hostSchedBetaPow);
+    cudaFreeHost(hostStats);
+    cudaSetDevice(cur);
+}
+
+int PpoEngine::init() {
+    // model/ppo.h:290-298, with the run-time width limits of this build
+    // (no compile-time N_EMBED_CFG; rows need not be a multiple of 64).
+    MG_CHECK_ARG(E == 64 || E == 128 || E == 256 || E == 512, "PPOModel: embedDim must be 64, 128, 256 or 512");
+    MG_CHECK_ARG(H % 64 == 0 && H > 0 && H <= 8192, "PPOModel: hidden (embed * scale) must be a positive multiple of 64");
+    MG_CHECK_ARG(L >= 1 && 6 + 4 * L <= kMaxGradSegments, "PPOModel: layers must be in [1, 8]");
+    MG_CHECK_ARG(T >= 1, "PPOModel: horizon must be >= 1");
+    MG_CHECK_ARG(A + 1 <= kHead, "PPOModel: ACT_DIM + value must fit one 64-wide head");
+    MG_CHECK_ARG(O >= 1 && O <= 256, "PPOModel: OBS_DIM must be in [1, 256]");
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    cudaStream_t st = gym->stream;
+
+    // ---- parameters: model/ppo.h:375-445 (seeded normal init rounded to bf16)
+    std::vector<std::vector<uint16_t>> init;
+    auto add = [&](uint32_t count, bool gf) {
+        params.push_back(ParamSpec{count, gf, 0});
+        init.emplace_back(count, (uint16_t)0);
+        return (uint32_t)(params.size() - 1);
+    };
+    std::mt19937 rng(seed);
+    auto normal = [&](uint32_t p, float sd) {
+        std::normal_distribution<float> dist(0.0f, sd);
+        for (auto& x : init[p]) x = host_f2bf(dist(rng));
+    };
+    auto constant = [&](uint32_t p, float v) { std::fill(init[p].begin(), init[p].end(), host_f2bf(v)); };
+    pInW = add((uint32_t)(O * E), true);
+    normal(pInW, 1.0f / std::sqrt((float)O));
+    pInB = add((uint32_t)E, true);
+    constant(pInB, 0.0f);
+    for (int n = 0; n < L; n++) {
+        pLnG.push_back(add((uint32_t)E, true));
+        constant(pLnG.back(), 1.0f);
+        pLnB.push_back(add((uint32_t)E, true));
+        constant(pLnB.back(), 0.0f);
+        pUp.push_back(add((uint32_t)(E * H), false));
+        normal(pUp.back(), std::sqrt(2.0f / (float)E));
+        pDown.push_back(add((uint32_t)(H * E), false));
+        normal(pDown.back(), 1.0f / std::sqrt((float)H) / std::sqrt((float)L));
+    }
+    pLnFg = add((uint32_t)E, true);
+    constant(pLnFg, 1.0f);
+    pLnFb = add((uint32_t)E, true);
+    constant(pLnFb, 0.0f);
+    pHead = add((uint32_t)(E * kHead), false);
+    {
+        std::normal_distribution<float> policyDist(0.0f, 0.01f);
+        std::normal_distribution<float> valueDist(0.0f, 1.0f / std::sqrt((float)E));
+        for (int k = 0; k < E; k++)
+            for (int n = 0; n < kHead; n++) {
+                float x = 0.0f;
+                if (n < A) x = policyDist(rng);
+                else if (n == A) x = valueDist(rng);
+                init[pHead][(size_t)k * kHead + n] = host_f2bf(x);
+            }
+    }
+    pLogStd = UINT32_MAX;
+    if (cont) {
+        pLogStd = add((uint32_t)A, true);
+        constant(pLogStd, 0.0f);  // INIT_LOG_STD (model/ppo.h:115)
+    }
+    uint64_t total = 0;
+    for (int pass = 0; pass < 2; pass++) {
+        for (auto& sp : params) {
+            if (sp.gradIsFloat != (pass == 0)) continue;
+            sp.offset = total;
+            total += (sp.count + 127) / 128 * 128;
+        }
+        if (pass == 0) optFloatCount = total;
+    }
+    optCount = total;
+    {
+        std::vector<uint16_t> w(optCount, 0);
+        std::vector<float> m(optCount, 0.0f);
+        for (size_t p = 0; p < params.size(); p++)
+            for (uint32_t i = 0; i < params[p].count; i++) {
+                w[params[p].offset + i] = init[p][i];
+                m[params[p].offset + i] = host_bf2f(init[p][i]);
+            }
+        MG_TRY(dalloc(&weights, optCount * 2));
+        MG_TRY(dalloc(&master, optCount * 4));
+        MG_TRY(dalloc(&mom, optCount * 4));
+        MG_TRY(dalloc(&var, optCount * 4));
+        MG_TRY(dalloc(&grad, optCount * 4));
+        MG_CUDA_TRY(cudaMemcpy(weights, w.data(), optCount * 2, cudaMemcpyHostToDevice));
+        MG_CUDA_TRY(cudaMemcpy(master, m.data(), optCount * 4, cudaMemcpyHostToDevice));
+        MG_CUDA_TRY(cudaMemset(mom, 0, optCount * 4));
+        MG_CUDA_TRY(cudaMemset(var, 0, optCount * 4));
+        MG_CUDA_TRY(cudaMemset(grad, 0, optCount * 4));
+    }
+
+    // ---- rollout slots (model/ppo.h:336-348)
+    const size_t slotCount = (size_t)T * R;
+    MG_TRY(dalloc(&obsSlots, (size_t)(T + 1) * R * O * 4));
+    MG_TRY(dalloc(&actionSlots, slotCount * actBytes));
+    MG_TRY(dalloc(&logpSlots, slotCount * 4));
+    MG_TRY(dalloc(&valueSlots, slotCount * 4));
+    MG_TRY(dalloc(&rewardSlots, slotCount * 4));
+    MG_TRY(dalloc(&doneSlots, slotCount));
+    MG_TRY(dalloc(&advSlots, slotCount * 4));
+    MG_TRY(dalloc(&retSlots, slotCount * 4));
+    MG_TRY(dalloc(&advStats, (size_t)T * 2 * 4));
+    MG_CUDA_TRY(cudaMemset(actionSlots, 0, slotCount * actBytes));
+    MG_CUDA_TRY(cudaMemset(obsSlots, 0, (size_t)(T + 1) * R * O * 4));
+    slotOrder.resize(T);
+    for (int t = 0; t < T; t++) slotOrder[t] = (uint32_t)t;
+    hostRng.seed(seed);
+
+    // ---- activations: train keeps every block's, collect shares one set
+    auto allocActs = [&](ActSet& a, int rows, bool shared) -> int {
+        MG_TRY(dalloc(&a.h, (size_t)rows * E * 2));
+        MG_TRY(dalloc(&a.fXn, (size_t)rows * E * 2));
+        MG_TRY(dalloc(&a.fOut, (size_t)rows * E * 2));
+        MG_TRY(dalloc(&a.fSd, (size_t)rows * 4));
+        MG_TRY(dalloc(&a.head, (size_t)rows * kHead * 2));
+        a.lnXn.resize(L);
+        a.lnOut.resize(L);
+        a.lnSd.resize(L);
+        a.v.resize(L);
+        for (int n = 0; n < L; n++) {
+            if (shared && n > 0) {
+                a.lnXn[n] = a.lnXn[0];
+                a.lnOut[n] = a.lnOut[0];
+                a.lnSd[n] = a.lnSd[0];
+                a.v[n] = a.v[0];
+                continue;
+            }
+            MG_TRY(dalloc(&a.lnXn[n], (size_t)rows * E * 2));
+            MG_TRY(dalloc(&a.lnOut[n], (size_t)rows * E * 2));
+            MG_TRY(dalloc(&a.lnSd[n], (size_t)rows * 4));
+            MG_TRY(dalloc(&a.v[n], (size_t)rows * H * 2));
+        }
+        return MG_OK;
+    };
+    MG_TRY(allocActs(trainActs, R, false));
+    MG_TRY(allocActs(collectActs, R, true));
+    MG_CUDA_TRY(cudaMemset(collectActs.head, 0, (size_t)R * kHead * 2));
+    MG_TRY(dalloc(&dLogits, (size_t)R * kHead * 2));
+    MG_TRY(dalloc(&dStream, (size_t)R * E * 2));
+    MG_TRY(dalloc(&dBranch, (size_t)R * E * 2));
+    MG_TRY(dalloc(&dV, (size_t)R * H * 2));
+    MG_TRY(dalloc(&stats, (size_t)R * 5 * 4));
+    MG_CUDA_TRY(cudaMemset(stats, 0, (size_t)R * 5 * 4));
+
+    // ---- gradient partials and the finalisation table
+    upSplits = splits_for(E, H, R, H >= 128 ? 128 : 64);
+    downSplits = splits_for(H, E, R, E >= 128 ? 128 : 64);
+    headSplits = splits_for(E, kHead, R, 64);
+    upPart.resize(L);
+    downPart.resize(L);
+    lnPart.resize(L);
+    const int pLn = layernorm_backward_parts(R);
+    const int pIn = input_backward_parts(R);
+    const int pGs = gaussian_loss_parts(R);
+    for (int n = 0; n < L; n++) {
+        MG_TRY(dalloc(&upPart[n], (size_t)upSplits * E * H * 4));
+        MG_TRY(dalloc(&downPart[n], (size_t)downSplits * H * E * 4));
+        MG_TRY(dalloc(&lnPart[n], (size_t)pLn * 2 * E * 4));
+    }
+    MG_TRY(dalloc(&headPart, (size_t)headSplits * E * kHead * 4));
+    MG_TRY(dalloc(&lnFPart, (size_t)pLn * 2 * E * 4));
+    MG_TRY(dalloc(&inPart, (size_t)pIn * (O + 1) * E * 4));
+    MG_TRY(dalloc(&lsPart, (size_t)pGs * (A > 0 ? A : 1) * 4));
+    GradSegmentTable& tb = gradTable;
+    tb.n = 0;
+    auto seg = [&](const float* src, int64_t stride, int nparts, int64_t count, uint32_t p, int round) {
+        GradSegment& s = tb.seg[tb.n++];
+        s.src = src;
+        s.partStride = stride;
+        s.nparts = nparts;
+        s.count = count;
+        s.dstOffset = (int64_t)params[p].offset;
+        s.roundBf16 = round;
+    };
+    seg(inPart, (int64_t)(O + 1) * E, pIn, (int64_t)O * E, pInW, 0);
+    seg(inPart + (size_t)O * E, (int64_t)(O + 1) * E, pIn, E, pInB, 0);
+    for (int n = 0; n < L; n++) {
+        seg(lnPart[n], 2 * E, pLn, E, pLnG[n], 0);
+        seg(lnPart[n] + E, 2 * E, pLn, E, pLnB[n], 0);
+        seg(upPart[n], (int64_t)E * H, upSplits, (int64_t)E * H, pUp[n], 1);
+        seg(downPart[n], (int64_t)H * E, downSplits, (int64_t)H * E, pDown[n], 1);
+    }
+    seg(lnFPart, 2 * E, pLn, E, pLnFg, 0);
+    seg(lnFPart + E, 2 * E, pLn, E, pLnFb, 0);
+    seg(headPart, (int64_t)E * kHead, headSplits, (int64_t)E * kHead, pHead, 1);
+    if (cont) seg(lsPart, A, pGs, A, pLogStd, 0);
+    nNorm = grad_table_layout(tb);
+    const int nNormAll = std::max(nNorm, grad_scale_norm_blocks((int64_t)optCount));
+    MG_TRY(dalloc(&normPartial, (size_t)nNormAll * 4));
+    MG_TRY(dalloc(&normSq, 4));
+    MG_TRY(dalloc(&statsMean, 8 * 4));
+    MG_CUDA_TRY(cudaMemset(normSq, 0, 4));
+    MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostStats), 8 * 4));
+    MG_TRY(ensureSchedule(4 * T));
+    MG_CUDA_TRY(cudaStreamSynchronize(st));
+    return MG_OK;
+}
+
+int PpoEngine::ensureSchedule(int n) {
+    if (n <= maxSchedule) return MG_OK;
+    cudaStreamSynchronize(gym->stream);
+    cudaFree(schedSlot);
+    cudaFree(schedBetaPow);
+    cudaFreeHost(hostSchedSlot);
+    cudaFreeHost(hostSchedBetaPow);
+    MG_TRY(dalloc(&schedSlot, (size_t)n * 4));
+    MG_TRY(dalloc(&schedBetaPow, (size_t)n * 2 * 4));
+    MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostSchedSlot), (size_t)n * 4));
+    MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostSchedBetaPow), (size_t)n * 2 * 4));
+    maxSchedule = n;
+    // a captured graph holds the old pointers
+    if (trainExec) {
+        cudaGraphExecDestroy(trainExec);
+        trainExec = nullptr;
+    }
+    return MG_OK;
+}
+
+int PpoEngine::checkStatus(const char* what) {
+    MG_CUDA_TRY(cudaStreamSynchronize(gym->stream));
+    int st = 0;
+    MG_CUDA_TRY(cudaMemcpy(&st, status_ptr(), sizeof(int), cudaMemcpyDeviceToHost));
+    if (st != 0) {
+        cudaMemset(status_ptr(), 0, sizeof(int));
+        return fail(MG_ERR_DEVICE, std::string(what) + ": device status " + std::to_string(st));
+    }
+    return MG_OK;
+}
+
+// model/ppo.h:575-626: input -> L x [LN -> up (ReLU) -> down (+ skip)] -> LN -> head.
+int PpoEngine::forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st) {
+    const uint16_t* W = weights;
+    auto w = [&](uint32_t p) { return static_cast<const void*>(W + params[p].offset); };
+    MG_TRY(input_forward(obs, w(pInW), w(pInB), a.h, rows, O, E, st));
+    for (int n = 0; n < L; n++) {
+        MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
+        GemmCall up;
+        up.A = a.lnOut[n]; up.lda = E;
+        up.B = w(pUp[n]); up.b_mn = true; up.ldb = H;
+        up.M = rows; up.N = H; up.K = E;
+        up.epilogue = 1;  // ReLU
+        up.out = a.v[n]; up.ldo = H;
+        MG_TRY(gemm_bf16(up, st));
+        GemmCall down;
+        down.A = a.v[n]; down.lda = H;
+        down.B = w(pDown[n]); down.b_mn = true; down.ldb = E;
+        down.M = rows; down.N = E; down.K = H;
+        down.epilogue = 2;  // + skip, in place on the stream
+        down.aux = a.h; down.ldaux = E;
+        down.out = a.h; down.ldo = E;
+        MG_TRY(gemm_bf16(down, st));
+    }
+    MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, rows, E, st));
+    GemmCall hd;
+    hd.A = a.fOut; hd.lda = E;
+    hd.B = w(pHead); hd.b_mn = true; hd.ldb = kHead;
+    hd.M = rows; hd.N = kHead; hd.K = E;
+    hd.epilogue = 0;
+    hd.out = a.head; hd.ldo = kHead;
+    return gemm_bf16(hd, st);
+}
+
+// One minibatch = one slot (model/ppo.h:906-916); the slot index and the
+// Adam bias-correction powers are read from the device schedule at j.
+int PpoEngine::minibatch(int j, cudaStream_t st) {
+    const int* slot = schedSlot + j;
+    ActSet& a = trainActs;
+    auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
+    // forward with activations saved (input reads obs slot `slot`)
+    MG_TRY(input_forward(obsSlots, w(pInW), w(pInB), a.h, R, O, E, st, slot, (int64_t)R * O));
+    for (int n = 0; n < L; n++) {
+        MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], R, E, st));
+        GemmCall up;
+        up.A = a.lnOut[n]; up.lda = E;
+        up.B = w(pUp[n]); up.b_mn = true; up.ldb = H;
+        up.M = R; up.N = H; up.K = E;
+        up.epilogue = 1;
+        up.out = a.v[n]; up.ldo = H;
+        MG_TRY(gemm_bf16(up, st));
+        GemmCall down;
+        down.A = a.v[n]; down.lda = H;
+        down.B = w(pDown[n]); down.b_mn = true; down.ldb = E;
+        down.M = R; down.N = E; down.K = H;
+        down.epilogue = 2;
+        down.aux = a.h; down.ldaux = E;
+        down.out = a.h; down.ldo = E;
+        MG_TRY(gemm_bf16(down, st));
+    }
+    MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, R, E, st));
+    {
+        GemmCall hd;
+        hd.A = a.fOut; hd.lda = E;
+        hd.B = w(pHead); hd.b_mn = true; hd.ldb = kHead;
+        hd.M = R; hd.N = kHead; hd.K = E;
+        hd.out = a.head; hd.ldo = kHead;
+        MG_TRY(gemm_bf16(hd, st));
+    }
+    // loss (model/ppo.h:753-781): per-slot advantage statistics from collect()
+    const LossHyper lh{hp.clip, hp.valueCoef, hp.entropyCoef};
+    if (cont)
+        MG_TRY(gaussian_loss(a.head, static_cast<const float*>(actionSlots), advSlots, advStats, retSlots, logpSlots,
+                             dLogits, stats, w(pLogStd), lsPart, R, A, lh, st, slot));
+    else
+        MG_TRY(policy_loss(a.head, static_cast<const int32_t*>(actionSlots), advSlots, advStats, retSlots, logpSlots,
+                           dLogits, stats, R, A, lh, st, slot));
+    // backward (model/ppo.h:793-865)
+    {
+        GemmCall dx;  // dStream = dLogits W_head^T (model/linear.metal:40-60)
+        dx.A = dLogits; dx.lda = kHead;
+        dx.B = w(pHead); dx.ldb = kHead;  // [E][64] = [N][K], K-major
+        dx.M = R; dx.N = E; dx.K = kHead;
+        dx.out = dStream; dx.ldo = E;
+        MG_TRY(gemm_bf16(dx, st));
+        GemmCall dw;  // dW_head = X_F^T dLogits (model/linear.metal:71-93)
+        dw.A = a.fOut; dw.a_mn = true; dw.lda = E;
+        dw.B = dLogits; dw.b_mn = true; dw.ldb = kHead;
+        dw.M = E; dw.N = kHead; dw.K = R;
+        dw.epilogue = 4; dw.splits = headSplits;
+        dw.out = headPart; dw.ldo = kHead;
+        MG_TRY(gemm_bf16(dw, st));
+    }
+    MG_TRY(layernorm_backward(dStream, a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, R, E, st));
+    for (int n = L - 1; n >= 0; n--) {
+        GemmCall g1;  // dV = bf16(dStream Dp^T) * (V > 0) (model/mlp.metal:88-127)
+        g1.A = dStream; g1.lda = E;
+        g1.B = w(pDown[n]); g1.ldb = E;  // Dp [H][E] = [N][K]
+        g1.M = R; g1.N = H; g1.K = E;
+        g1.epilogue = 3; g1.aux = a.v[n]; g1.ldaux = H;
+        g1.out = dV; g1.ldo = H;
+        MG_TRY(gemm_bf16(g1, st));
+        GemmCall g2;  // dUp = X^T dV (model/mlp.metal:167-208)
+        g2.A = a.lnOut[n]; g2.a_mn = true; g2.lda = E;
+        g2.B = dV; g2.b_mn = true; g2.ldb = H;
+        g2.M = E; g2.N = H; g2.K = R;
+        g2.epilogue = 4; g2.splits = upSplits;
+        g2.out = upPart[n]; g2.ldo = H;
+        MG_TRY(gemm_bf16(g2, st));
+        GemmCall g3;  // dDp = V^T dStream
+        g3.A = a.v[n]; g3.a_mn = true; g3.lda = H;
+        g3.B = dStream; g3.b_mn = true; g3.ldb = E;
+        g3.M = H; g3.N = E; g3.K = R;
+        g3.epilogue = 4; g3.splits = downSplits;
+        g3.out = downPart[n]; g3.ldo = E;
+        MG_TRY(gemm_bf16(g3, st));
+        GemmCall g4;  // dBranch = dV Up^T (model/mlp.metal:131-153)
+        g4.A = dV; g4.lda = H;
+        g4.B = w(pUp[n]); g4.ldb = H;  // Up [E][H] = [N][K]
+        g4.M = R; g4.N = E; g4.K = H;
+        g4.out = dBranch; g4.ldo = E;
+        MG_TRY(gemm_bf16(g4, st));
+        // LayerNorm backward, then dStream += dBranch (model/ppo.h:851-852)
+        MG_TRY(layernorm_backward(dBranch, a.lnXn[n], w(pLnG[n]), a.lnSd[n], dStream, lnPart[n], R, E, st));
+    }
+    MG_TRY(input_backward(obsSlots, dStream, inPart, R, O, E, st, slot, (int64_t)R * O));
+    // gradient sums + norm (model/ppo.h:873-890), [all-reduce], Adam (:891-903)
+    MG_TRY(grad_finalize(gradTable, grad, normPartial, st));
+    int nn = nNorm;
+    if (world > 1) {
+        Nccl& nc = nccl();
+        ncclResult_t r = nc.allReduce(grad, grad, (size_t)optCount, ncclFloat, ncclSum, static_cast<ncclComm_t>(comm), st);
+        if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
+        nn = grad_scale_norm_blocks((int64_t)optCount);
+        MG_TRY(grad_scale_norm(grad, (int64_t)optCount, 1.0f / (float)world, normPartial, st));
+    }
+    const AdamHyper ah{lr, hp.maxGradNorm, 0.0f, 0.0f};
+    return adam(master, grad, mom, var, weights, normPartial, nn, (int64_t)optCount, ah, schedBetaPow + 2 * j, normSq,
+                st);
+}
+
+int PpoEngine::captureCollect() {
+    cudaStream_t st = gym->stream;
+    if (collectExec) {
+        cudaGraphExecDestroy(collectExec);
+        collectExec = nullptr;
+    }
+    MG_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+    int rc = MG_OK;
+    const void* logStd = cont ? static_cast<const void*>(weights + params[pLogStd].offset) : nullptr;
+    const mg_env_ops* ops = gym->ops;
+    for (int t = 0; t < T && !rc; t++) {
+        rc = forwardOn(obsSlots + (size_t)t * R * O, R, collectActs, st);
+        if (!rc)
+            rc = ops->collect_step(collectActs.head, logStd, gym->states,
+                                   static_cast<char*>(actionSlots) + (size_t)t * R * actBytes, logpSlots + (size_t)t * R,
+                                   valueSlots + (size_t)t * R, obsSlots + (size_t)(t + 1) * R * O,
+                                   rewardSlots + (size_t)t * R, gym->done, doneSlots + (size_t)t * R, gym->rng, R,
+                                   reinterpret_cast<mg_stream_t>(st));
+    }
+    if (!rc) rc = forwardOn(obsSlots + (size_t)T * R * O, R, collectActs, st);
+    if (!rc) rc = gae(rewardSlots, doneSlots, valueSlots, collectActs.head, advSlots, retSlots, R, T, A, hp.gamma,
+                      hp.lambda, st);
+    if (!rc) rc = advantage_stats(advSlots, advStats, R, T, st);
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "collect capture");
+    e = cudaGraphInstantiate(&collectExec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "collect graph instantiate");
+    collectHp = hp;
+    return MG_OK;
+}
+
+int PpoEngine::captureTrain(int minibatches) {
+    cudaStream_t st = gym->stream;
+    MG_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+    int rc = MG_OK;
+    for (int j = 0; j < minibatches && !rc; j++) rc = minibatch(j, st);
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "train capture");
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "train graph instantiate");
+    if (trainExec) cudaGraphExecDestroy(trainExec);
+    trainExec = exec;
+    trainExecMinibatches = minibatches;
+    trainHp = hp;
+    return MG_OK;
+}
+
+// model/ppo.h:716-751
+int PpoEngine::collect() {
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    cudaStream_t st = gym->stream;
+    if (!rolloutStarted) {
+        int rc = gym->ops->step(gym->states, actionSlots, obsSlots, rewardSlots, gym->done, nullptr, gym->rng, R,
+                                reinterpret_cast<mg_stream_t>(st));
+        if (rc) return fail(rc, "collect: first env step failed");
+        rolloutStarted = true;
+    } else {
+        MG_CUDA_TRY(cudaMemcpyAsync(obsSlots, obsSlots + (size_t)T * R * O, (size_t)R * O * 4,
+                                    cudaMemcpyDeviceToDevice, st));
+    }
+    if (!collectExec || !(collectHp == hp)) MG_TRY(captureCollect());
+    MG_CUDA_TRY(cudaGraphLaunch(collectExec, st));
+    return checkStatus("collect");
+}
+
+// Fills the device schedule for n minibatches: slot order (model/ppo.h:918-923)
+// and the host beta powers of each Adam step (model/ppo.h:874-880).
+static void schedule_step(PpoEngine& e, int k, uint32_t slot) {
+    e.stepCounter += 1.0f;
+    e.hostSchedSlot[k] = (int)slot;
+    e.hostSchedBetaPow[2 * k] = std::pow(0.9f, e.stepCounter);
+    e.hostSchedBetaPow[2 * k + 1] = std::pow(0.999f, e.stepCounter);
+}
+
+int PpoEngine::train(int epochs) {
+    MG_CHECK_ARG(epochs >= 0, "train: epochs must be >= 0");
+    if (epochs == 0) return MG_OK;
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    cudaStream_t st = gym->stream;
+    const int n = epochs * T;
+    MG_TRY(ensureSchedule(n));
+    int k = 0;
+    for (int e = 0; e < epochs; e++) {
+        std::shuffle(slotOrder.begin(), slotOrder.end(), hostRng);
+        for (uint32_t t : slotOrder) schedule_step(*this, k++, t);
+    }
+    MG_CUDA_TRY(cudaMemcpyAsync(schedSlot, hostSchedSlot, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+    MG_CUDA_TRY(cudaMemcpyAsync(schedBetaPow, hostSchedBetaPow, (size_t)n * 8, cudaMemcpyHostToDevice, st));
+    if (!trainExec || trainExecMinibatches != n || !(trainHp == hp)) MG_TRY(captureTrain(n));
+    MG_CUDA_TRY(cudaGraphLaunch(trainExec, st));
+    return checkStatus("train");
+}
+
+int PpoEngine::trainSlot(int t) {
+    MG_CHECK_ARG(t >= 0 && t < T, "trainSlot: slot out of range");
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    cudaStream_t st = gym->stream;
+    schedule_step(*this, 0, (uint32_t)t);
+    MG_CUDA_TRY(cudaMemcpyAsync(schedSlot, hostSchedSlot, 4, cudaMemcpyHostToDevice, st));
+    MG_CUDA_TRY(cudaMemcpyAsync(schedBetaPow, hostSchedBetaPow, 8, cudaMemcpyHostToDevice, st));
+    // single minibatches run eagerly (no graph): trainSlot is the manual path
+    MG_TRY(minibatch(0, st));
+    return checkStatus("trainSlot");
+}
+
+int PpoEngine::forward() {
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    MG_TRY(forwardOn(static_cast<const float*>(gym->obs), R, collectActs, gym->stream));
+    return checkStatus("forward");
+}
+
+// model/ppo.h:925-943 (means on the device; gradNorm is the pre-clip norm)
+int PpoEngine::lastStats(float out6[6]) {
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    cudaStream_t st = gym->stream;
+    MG_TRY(stats_mean(stats, R, statsMean, st));
+    MG_CUDA_TRY(cudaMemcpyAsync(hostStats, statsMean, 5 * 4, cudaMemcpyDeviceToHost, st));
+    MG_CUDA_TRY(cudaMemcpyAsync(hostStats + 5, normSq, 4, cudaMemcpyDeviceToHost, st));
+    MG_CUDA_TRY(cudaStreamSynchronize(st));
+    for (int i = 0; i < 5; i++) out6[i] = hostStats[i];
+    out6[5] = std::sqrt(hostStats[5]);
+    return MG_OK;
+}
+
+// model/ppo.h:460-469
+int PpoEngine::setLogStd(float v) {
+    MG_CHECK_ARG(cont, "setLogStd needs a continuous Env::Action");
+    std::vector<float> m(A, v);
+    std::vector<uint16_t> w(A, host_f2bf(v));
+    const size_t off = params[pLogStd].offset;
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    MG_CUDA_TRY(cudaStreamSynchronize(gym->stream));
+    MG_CUDA_TRY(cudaMemcpy(master + off, m.data(), A * 4, cudaMemcpyHostToDevice));
+    MG_CUDA_TRY(cudaMemcpy(weights + off, w.data(), A * 2, cudaMemcpyHostToDevice));
+    return MG_OK;
+}
+
+int PpoEngine::logStd(int k, float* out) {
+    MG_CHECK_ARG(cont, "logStdValue needs a continuous Env::Action");
+    MG_CHECK_ARG(k >= 0 && k < A, "logStdValue: index out of range");
+    uint16_t h = 0;
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    MG_CUDA_TRY(cudaStreamSynchronize(gym->stream));
+    MG_CUDA_TRY(cudaMemcpy(&h, weights + params[pLogStd].offset + k, 2, cudaMemcpyDeviceToHost));
+    *out = host_bf2f(h);
+    return MG_OK;
+}
+
+int PpoEngine::setComm(void* c, int r, int w) {
+    MG_CHECK_ARG(w >= 1 && r >= 0 && r < w, "setComm: bad rank / world size");
+    MG_CHECK_ARG(w == 1 || c, "setComm: a communicator is needed for world size > 1");
+    if (w > 1 && !nccl().ok) return fail(MG_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
+    comm = c;
+    rank = r;
+    world = w;
+    if (trainExec) {
+        cudaGraphExecDestroy(trainExec);
+        trainExec = nullptr;
+    }
+    return MG_OK;
+}
+
+}  // namespace mg

@@ -1,0 +1,212 @@
+"""The PPO engine (collect / train through the mg_ppo_* C ABI) vs the oracle.
+
+collect() is checked by a teacher-forced replay on the CPU: the oracle model
+(same seed, hence bit-identical initial weights) runs the forward pass on
+the GPU's observation slots, the host build of the environment steps with
+the GPU's actions, and the reference's GAE runs on the GPU's rewards / dones
+/ values. Env outputs, RNG words and GAE are bit-exact; values / log-probs
+come from bf16 GEMMs with a different accumulation order and must agree
+within rel 1e-2 (BF16 operands, fp32 accumulation); sampled actions may
+differ only where the oracle's logits move a draw across a CDF boundary
+(< 1% of rows).
+
+trainSlot(t) is checked against the oracle's minibatch on identical state:
+loss statistics rel 1e-2, per-parameter gradients relative L2 error < 3e-2,
+Adam update direction agreeing on > 97% of the weights with a clear gradient.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from orc import ENV_IDS, ENV_SIZES, bf16_to_f32, ptr, seed_words
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+HEAD = 64
+
+
+def make(name, R, E, s, L, T, seed=0, lr=3e-4):
+    from metalgym_b200.session import Gym, PPOModel
+
+    gym = Gym(name, R, seed=0)
+    model = PPOModel(gym, E, s, L, lr, T, seed)
+    return gym, model
+
+
+def oracle_model(oracle, model, seed):
+    ad = model.act_dim
+    return oracle.orc_model_create(model.rows, model.obs_dim, ad, int(model.continuous), model.embed,
+                                   model.hidden // model.embed, model.layers, 3e-4, model.horizon, seed)
+
+
+def arr(oracle, fn, m, n, dtype):
+    p = getattr(oracle, fn)(m)
+    return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(np.ctypeslib.as_ctypes_type(dtype))), shape=(n,))
+
+
+@pytest.mark.parametrize("name", ["rollout_cartpole", "rollout_cartpole_continuous", "rollout_voxelnav"])
+def test_init_and_layout_match_reference_restatement(mg, oracle, name):
+    gym, model = make(name, 256, 128, 4, 2, 4, seed=3)
+    om = oracle_model(oracle, model, 3)
+    assert oracle.orc_model_opt_count(om) == model.opt_count
+    assert oracle.orc_model_opt_float_count(om) == model.opt_float_count
+    for i in range(model.param_count):
+        o, c, g = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_int()
+        oracle.orc_model_param_info(om, i, ctypes.byref(o), ctypes.byref(c), ctypes.byref(g))
+        assert model.param_info(i) == (o.value, c.value, bool(g.value))
+    n = model.opt_count
+    assert np.array_equal(model.download("weights").view(np.uint16), arr(oracle, "orc_model_weights", om, n, np.uint16))
+    assert np.array_equal(model.download("master").view(np.float32), arr(oracle, "orc_model_master", om, n, np.float32))
+    oracle.orc_model_destroy(om)
+
+
+def replay_collect(oracle, hostenv, model, name, seed):
+    """Teacher-forced CPU replay of one collect() from a fresh gym."""
+    which = ENV_IDS[name]
+    sb, ab, ob, od, ad, cont = ENV_SIZES[name]
+    R, T = model.rows, model.horizon
+    obs = model.slots("obs")
+    act = model.slots("actions")
+    logp = model.slots("logp")
+    val = model.slots("value")
+    rew = model.slots("reward")
+    done = model.slots("done")
+    adv = model.slots("adv")
+    ret = model.slots("ret")
+    om = oracle_model(oracle, model, seed)
+    hs = np.zeros(R * sb, np.uint8)
+    hd = np.ones(R, np.uint8)
+    hg = seed_words(R)
+    ho = np.zeros((R, od), np.float32)
+    hr = np.zeros(R, np.float32)
+    zero = np.zeros((R, ad), np.float32) if cont else np.zeros(R, np.int32)
+    hostenv.hostenv_rollout(which, ptr(hs), ptr(zero), ptr(ho), ptr(hr), ptr(hd), ptr(hg), R, 8)
+    assert np.array_equal(obs[0].view(np.uint32), ho.view(np.uint32)), "first obs slot"
+    head = np.zeros((R, HEAD), np.uint16)
+    mismatched = 0
+    logstd = None
+    if cont:
+        off, cnt, _ = model.param_info(model.param_count - 1)
+        logstd = model.download("weights").view(np.uint16)[off:off + cnt].copy()
+    for t in range(T):
+        oracle.orc_model_forward(om, ptr(np.ascontiguousarray(obs[t])), R, ptr(head))
+        hv = bf16_to_f32(head[:, ad])
+        np.testing.assert_allclose(val[t], hv, rtol=1e-2, atol=1e-2 * max(1.0, np.abs(hv).max()))
+        a_gpu = np.ascontiguousarray(act[t])
+        lp = np.zeros(R, np.float32)
+        v = np.zeros(R, np.float32)
+        if cont:
+            a_or = np.zeros((R, ad), np.float32)
+            oracle.orc_sample_gaussian(ptr(head), ptr(hg), ptr(a_or), ptr(lp), ptr(v), R, ad, HEAD, ptr(logstd))
+            np.testing.assert_allclose(a_or, a_gpu, rtol=1e-2, atol=2e-2)
+        else:
+            a_or = np.zeros(R, np.int32)
+            oracle.orc_sample_action(ptr(head), ptr(hg), ptr(a_or), ptr(lp), ptr(v), R, ad, HEAD)
+            mismatched += int((a_or != a_gpu).sum())
+            same = a_or == a_gpu
+            np.testing.assert_allclose(logp[t][same], lp[same], rtol=1e-2, atol=2e-2)
+        # the env steps with the GPU's actions (teacher forcing): bit-exact
+        hostenv.hostenv_rollout(which, ptr(hs), ptr(a_gpu), ptr(ho), ptr(hr), ptr(hd), ptr(hg), R, 8)
+        assert np.array_equal(obs[t + 1].view(np.uint32), ho.view(np.uint32)), f"obs slot {t + 1}"
+        assert np.array_equal(rew[t].view(np.uint32), hr.view(np.uint32)), f"reward slot {t}"
+        assert np.array_equal(done[t], hd), f"done slot {t}"
+    if not cont:
+        assert mismatched <= max(2, 0.01 * R * T), f"{mismatched} sampled actions differ"
+    # bootstrap value and the reference GAE on the GPU's buffers: bit-exact
+    gpu_head = model.download("head").view(np.uint16).reshape(R, HEAD)
+    oracle.orc_model_forward(om, ptr(np.ascontiguousarray(obs[T])), R, ptr(head))
+    boot = bf16_to_f32(gpu_head[:, ad]).copy()
+    np.testing.assert_allclose(boot, bf16_to_f32(head[:, ad]), rtol=1e-2, atol=1e-2)
+    hadv = np.zeros(T * R, np.float32)
+    hret = np.zeros(T * R, np.float32)
+    hyper = model.hyper()
+    oracle.orc_gae(ptr(rew), ptr(done), ptr(np.ascontiguousarray(val)), ptr(boot), ptr(hadv), ptr(hret), R, T,
+                   hyper["gamma"], hyper["lambda"])
+    assert np.array_equal(adv.reshape(-1).view(np.uint32), hadv.view(np.uint32))
+    assert np.array_equal(ret.reshape(-1).view(np.uint32), hret.view(np.uint32))
+    # the env's RNG words after T draws + resets
+    assert np.array_equal(model.gym.download("rng").view(np.uint32), hg)
+    oracle.orc_model_destroy(om)
+
+
+@pytest.mark.parametrize("name,R,T", [("rollout_cartpole", 1024, 8), ("rollout_cartpole_continuous", 512, 6),
+                                      ("rollout_voxelnav", 256, 4)])
+def test_collect_teacher_forced(mg, oracle, hostenv, name, R, T):
+    gym, model = make(name, R, 128, 4, 2, T, seed=1)
+    model.collect()
+    replay_collect(oracle, hostenv, model, name, 1)
+    # per-slot advantage statistics (model/gae.metal:42-77)
+    st = model.download("adv_stats").view(np.float32).reshape(T, 2)
+    a = model.slots("adv").astype(np.float64)
+    np.testing.assert_allclose(st[:, 0], a.mean(1), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(st[:, 1], 1.0 / (a.std(1) + 1e-8), rtol=1e-4)
+
+
+def test_second_collect_continues_from_last_obs(mg):
+    gym, model = make("rollout_cartpole", 512, 128, 4, 1, 4)
+    model.collect()
+    last = model.slots("obs")[4].copy()
+    model.collect()
+    assert np.array_equal(model.slots("obs")[0], last)
+
+
+@pytest.mark.parametrize("name", ["rollout_cartpole", "rollout_cartpole_continuous"])
+def test_train_slot_matches_oracle(mg, oracle, name):
+    R, T, E, s, L = 1024, 4, 128, 4, 2
+    gym, model = make(name, R, E, s, L, T, seed=2)
+    model.collect()
+    om = oracle_model(oracle, model, 2)
+    n = model.opt_count
+    # identical optimiser state on both sides
+    for fn, buf, dt in [("orc_model_weights", "weights", np.uint16), ("orc_model_master", "master", np.float32),
+                        ("orc_model_momentum", "momentum", np.float32), ("orc_model_variance", "variance", np.float32)]:
+        arr(oracle, fn, om, n, dt)[:] = model.download(buf).view(dt)
+    t = 2
+    obs = np.ascontiguousarray(model.slots("obs")[t])
+    act = np.ascontiguousarray(model.slots("actions")[t])
+    adv = np.ascontiguousarray(model.slots("adv")[t])
+    ret = np.ascontiguousarray(model.slots("ret")[t])
+    logp = np.ascontiguousarray(model.slots("logp")[t])
+    stats = np.zeros((R, 5), np.float32)
+    nsq = np.zeros(1, np.float32)
+    m0 = model.download("master").view(np.float32).copy()
+    oracle.orc_model_set_step_counter(om, model.step_counter())
+    oracle.orc_model_train_minibatch(om, ptr(obs), ptr(act), ptr(adv), ptr(ret), ptr(logp), R, ptr(stats), ptr(nsq))
+    model.train_slot(t)
+    ls = model.last_stats()
+    ref = stats.mean(0)
+    for k, key in enumerate(("policy", "value", "entropy", "approxKl", "clipFrac")):
+        np.testing.assert_allclose(ls[key], ref[k], rtol=2e-2, atol=2e-3, err_msg=key)
+    np.testing.assert_allclose(ls["gradNorm"], np.sqrt(nsq[0]), rtol=2e-2)
+    g_gpu = model.download("grad").view(np.float32)
+    g_orc = arr(oracle, "orc_model_grad", om, n, np.float32)
+    for i in range(model.param_count):
+        off, cnt, _ = model.param_info(i)
+        a, b = g_gpu[off:off + cnt], g_orc[off:off + cnt]
+        err = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-12)
+        assert err < 3e-2, f"param {i}: relative gradient error {err:.3g}"
+    m1 = model.download("master").view(np.float32)
+    o1 = arr(oracle, "orc_model_master", om, n, np.float32)
+    clear = np.abs(g_orc) > 1e-3 * np.abs(g_orc).max()
+    agree = (np.sign(m1 - m0) == np.sign(o1 - m0))[clear].mean()
+    assert agree > 0.97, agree
+    assert model.step_counter() == oracle.orc_model_step_counter(om)
+    oracle.orc_model_destroy(om)
+
+
+def test_full_loop_runs_and_learns(mg):
+    """collect + train(4) at the CartPole config: finite statistics, every
+    minibatch applied, and the policy improves (mean episode length)."""
+    gym, model = make("rollout_cartpole", 4096, 128, 4, 2, 32)
+    lengths = []
+    for it in range(12):
+        model.collect()
+        done = model.slots("done")
+        lengths.append(done.size / max(1, int(done.sum())))
+        model.train(4)
+        st = model.last_stats()
+        assert all(np.isfinite(v) for v in st.values()), st
+    assert model.step_counter() == 12 * 4 * 32
+    assert np.mean(lengths[-3:]) > 1.5 * np.mean(lengths[:2]), lengths
