@@ -1,0 +1,465 @@
+"""Benchmark of the MetalGym hot path on B200: env steps/s for the raw env
+step, collect() (policy + env + GAE) and the full PPO loop (collect + train),
+on BASELINE configs 1-3 (CartPole, 4096 envs per GPU, T = 32, residual MLP
+128 -> 512 -> 128 x 2 blocks, 4 epochs, minibatch = one 4096-row slot).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
+
+One step = one PPO iteration (collect() + train(4)) = envs x T env steps per
+GPU. The headline `value` is the full-loop throughput, device-timed with CUDA
+events on the engine's stream (inputs resident, L2 flushed by a 256 MiB write
+between timed steps, outside the events), max over ranks; `e2e` is the same
+loop through the C ABI as a host program drives it (wall clock, including the
+per-call synchronisation, the schedule upload and the LossStats / done-slot
+read-back). With N > 1 (torchrun, one process per GPU) every rank steps its
+own 4096 envs (disjoint env ids / RNG streams) and the gradients are
+all-reduced with NCCL once per minibatch (weak scaling).
+
+`--impl reference` times the reference's CPU implementation of the same
+loop on the host cores: its own environment and per-thread kernels compiled
+from source (oracle/_ref) and the C++ restatement of its PPO arithmetic
+(oracle/), on a bounded sample of each step.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ENV = "rollout_cartpole"
+ENVS_PER_GPU = 4096
+HORIZON = 32
+EMBED, SCALE, LAYERS, EPOCHS, LR = 128, 4, 2, 4, 3e-4
+RAW_STEPS = 1000
+L2_FLUSH_BYTES = 256 << 20
+METRIC = "env steps/s: raw step, with policy, full PPO loop (CartPole, VoxelNav) @1-8 GPU"
+REFERENCE_M4_FULL_LOOP = 296e3  # reference README, CartPole full loop, 2 blocks (Apple M4; context only)
+
+
+def flops_per_row(obs_dim, act_dim, E, H, L):
+    """Algorithmic forward / backward FLOPs per row (head counts act_dim + 1 columns)."""
+    fwd = 2 * obs_dim * E + L * 4 * E * H + 2 * E * (act_dim + 1)
+    bwd = 2 * fwd - 2 * obs_dim * E  # dX and dW for every GEMM; no dX for the input layer
+    return fwd, bwd
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples (SM clock, throttle reasons) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.proc or not self.file:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9 and f[1].replace(".", "").isdigit():
+                rows.append(f)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+# ------------------------------------------------------------------ our arm
+
+def run_mine(args, rank, world, local_rank, dist):
+    import torch
+
+    import metalgym_b200
+    from metalgym_b200.session import Gym, PPOModel
+
+    torch.cuda.set_device(local_rank)
+    lib = metalgym_b200.lib()
+    gym = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=rank * ENVS_PER_GPU, device=local_rank)
+    model = PPOModel(gym, EMBED, SCALE, LAYERS, LR, HORIZON, seed=0)
+    comm = None
+    if world > 1:
+        idbuf = (ctypes.c_char * 128)()
+        if rank == 0:
+            metalgym_b200.check(lib.mg_comm_unique_id(idbuf))
+        obj = [bytes(idbuf)]
+        dist.broadcast_object_list(obj, src=0)
+        ctypes.memmove(idbuf, obj[0], 128)
+        comm = ctypes.c_void_p()
+        metalgym_b200.check(lib.mg_comm_init(world, rank, idbuf, local_rank, ctypes.byref(comm)))
+        model.set_comm(comm, rank, world)
+    stream = torch.cuda.ExternalStream(gym.stream(), device=local_rank)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{local_rank}")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def iteration():
+        model.collect()
+        model.train(EPOCHS)
+
+    for _ in range(args.warmup):
+        iteration()
+    barrier()
+    torch.cuda.synchronize()
+    # ---- device-timed full loop
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with Clocks(local_rank) as clk:
+        for k in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.fill_(float(k))
+                starts[k].record(stream)
+            iteration()
+            with torch.cuda.stream(stream):
+                ends[k].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    ms = max_over_ranks(ms, dist)
+    steps_per_iter = ENVS_PER_GPU * HORIZON
+    value = steps_per_iter * world / (ms / 1e3)
+    collect_k, train_k = model.graph_kernels()
+
+    # ---- e2e: the loop as a host program drives it through the C ABI
+    done_host = np.zeros(HORIZON * ENVS_PER_GPU, np.uint8)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        iteration()
+        model.last_stats()  # 24 B
+        metalgym_b200.check(lib.mg_ppo_download(model.handle, 5, -1, done_host.ctypes.data, done_host.nbytes))
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    e2e_s = max_over_ranks(e2e_s, dist)
+    e2e = {"value": steps_per_iter * world / e2e_s, "unit": "env steps/s",
+           "h2d_bytes_per_step": EPOCHS * HORIZON * 12, "d2h_bytes_per_step": done_host.nbytes + 24 + 4 * 3,
+           "api": "mg_ppo_collect + mg_ppo_train(4) + mg_ppo_last_stats + done-slot download"}
+
+    legs = {}
+    # ---- collect only
+    cs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ce = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for k in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(float(k))
+            cs[k].record(stream)
+        model.collect()
+        with torch.cuda.stream(stream):
+            ce[k].record(stream)
+    torch.cuda.synchronize()
+    cms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(cs, ce)) / args.steps, dist)
+    legs["collect"] = {"value": steps_per_iter * world / (cms / 1e3), "ms_per_call": cms}
+    legs["full_loop"] = {"value": value, "ms_per_iteration": ms}
+
+    # ---- raw env step (config 1): fused multi-step kernel and the gym.run loop
+    raw = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=rank * ENVS_PER_GPU, device=local_rank)
+    rstream = torch.cuda.ExternalStream(raw.stream(), device=local_rank)
+    raw.run_random(RAW_STEPS)
+    raw.synchronize()
+    rs, re_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(rstream):
+        rs.record(rstream)
+    raw.run_random(RAW_STEPS)
+    with torch.cuda.stream(rstream):
+        re_.record(rstream)
+    raw.synchronize()
+    rms = max_over_ranks(rs.elapsed_time(re_), dist)
+    legs["raw_env"] = {"value": RAW_STEPS * ENVS_PER_GPU * world / (rms / 1e3), "steps": RAW_STEPS,
+                       "kernel": "one launch, 1000 fused steps (random policy drawn on the env's RNG)"}
+    # gym.run loop with host actions / rewards (the reference benchmark's loop)
+    pinned = ctypes.c_void_p()
+    metalgym_b200.check(lib.mg_host_alloc(ENVS_PER_GPU * 8, ctypes.byref(pinned)))
+    acts = np.ctypeslib.as_array(ctypes.cast(pinned, ctypes.POINTER(ctypes.c_int32)), shape=(ENVS_PER_GPU,))
+    rew = np.ctypeslib.as_array(ctypes.cast(pinned.value + ENVS_PER_GPU * 4, ctypes.POINTER(ctypes.c_float)),
+                                shape=(ENVS_PER_GPU,))
+    acts[:] = 0
+    for _ in range(10):
+        lib.mg_gym_run(raw.handle, acts.ctypes.data, rew.ctypes.data, ENVS_PER_GPU)
+    t0 = time.perf_counter()
+    for _ in range(RAW_STEPS):
+        lib.mg_gym_run(raw.handle, acts.ctypes.data, rew.ctypes.data, ENVS_PER_GPU)
+    run_s = max_over_ranks((time.perf_counter() - t0) / RAW_STEPS, dist)
+    legs["raw_env"]["gym_run_e2e"] = ENVS_PER_GPU * world / run_s
+    lib.mg_host_free(pinned)
+
+    # ---- dominant kernel, timed live: see profiles/ for the launch-share list
+    roof = dominant_kernel_roofline(lib, torch, local_rank, stream)
+
+    result = None
+    if rank == 0:
+        fwd, bwd = flops_per_row(4, 2, EMBED, EMBED * SCALE, LAYERS)
+        result = {
+            "metric": METRIC, "value": value, "unit": "env steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / REFERENCE_M4_FULL_LOOP, "dtype": "bf16", "data": "synthetic (simulated CartPole)",
+            "config": {"workload": "CartPole full PPO loop (BASELINE configs[2]): collect() + train(4) per step",
+                       "envs_per_gpu": ENVS_PER_GPU, "horizon": HORIZON, "embed": EMBED,
+                       "hidden": EMBED * SCALE, "blocks": LAYERS, "epochs": EPOCHS,
+                       "minibatch": "one slot (4096 rows)", "parallelism": f"dp{world}",
+                       "l2": "flushed between timed steps (256 MiB write, outside the events)",
+                       "env_steps_per_step": steps_per_iter * world,
+                       "flop_per_env_step": (HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd)},
+            "legs": legs, "e2e": e2e, "roofline": roof,
+            "gpu_launches": args.steps * (collect_k + train_k),
+            "gpu_launches_per_step": {"collect_graph": collect_k, "train_graph": train_k},
+            "clocks": clk.summary(),
+        }
+    if comm is not None:
+        lib.mg_comm_destroy(comm)
+    return result
+
+
+def max_over_ranks(x, dist):
+    if dist is None:
+        return x
+    import torch
+
+    t = torch.tensor([float(x)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dominant_kernel_roofline(lib, torch, dev, stream):
+    """The tcgen05 GEMM with the largest share of the loop's GPU time
+    (profiles/launches_full_loop.md): the up-projection shape of the policy,
+    rows x hidden x embed = 4096 x 512 x 128, ReLU epilogue. Timed alone,
+    back to back on the engine's stream with CUDA events."""
+    M, N, K = ENVS_PER_GPU, EMBED * SCALE, EMBED
+    a = torch.randn(M, K, device=f"cuda:{dev}").bfloat16()
+    b = torch.randn(K, N, device=f"cuda:{dev}").bfloat16()
+    o = torch.empty(M, N, device=f"cuda:{dev}", dtype=torch.bfloat16)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    for _ in range(5):
+        lib.mg_gemm_bf16(a.data_ptr(), 0, K, b.data_ptr(), 1, N, M, N, K, 1, o.data_ptr(), N, None, 0, 1, sp)
+    iters = 200
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        s.record(stream)
+    for _ in range(iters):
+        lib.mg_gemm_bf16(a.data_ptr(), 0, K, b.data_ptr(), 1, N, M, N, K, 1, o.data_ptr(), N, None, 0, 1, sp)
+    with torch.cuda.stream(stream):
+        e.record(stream)
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1e3 / iters
+    flops = 2.0 * M * N * K
+    achieved = flops / (us * 1e-6) / 1e12
+    _, peak, kind = measured_peaks()
+    traffic = profile_traffic()
+    return {"kernel": "gemm_tc_kernel<128, K-major A, MN-major B, ReLU> (MLP up-projection, 4096x512x128)",
+            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_kind": f"{kind} bf16 burst", "us_per_launch": us, "flop_per_launch": flops,
+            "traffic": traffic}
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "gemm_up_4096x512x128.md"
+    if p.exists():
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+# ------------------------------------------------------------------ CPU baselines
+
+def cpu_full_loop(seconds_budget=20.0, threads=None):
+    """The reference's CPU path for the full loop: its environment compiled
+    from source (oracle/_ref) and the C++ restatement of its PPO arithmetic,
+    OpenMP over rows on all host cores. Bounded sample: one collect() (the
+    whole T-step rollout of 4096 envs) and as many of the 128 minibatches as
+    fit in the budget; the iteration time is extrapolated to 128 minibatches."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    from orc import load_hostenv, load_oracle, load_ref, ptr, seed_words  # noqa: F401
+
+    threads = threads or os.cpu_count()
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    orc = load_oracle()
+    ref = load_ref()
+    env_lib = ref if ref is not None else load_hostenv()
+    env_fn = ctypes.cast(env_lib.ref_rollout if ref is not None else env_lib.hostenv_rollout, ctypes.c_void_p)
+    R, T, O = ENVS_PER_GPU, HORIZON, 4
+    m = orc.orc_model_create(R, O, 2, 0, EMBED, SCALE, LAYERS, LR, T, 0)
+    states = np.zeros(R * 20, np.uint8)
+    done = np.ones(R, np.uint8)
+    rng = seed_words(R)
+    obs = np.zeros((T + 1) * R * O, np.float32)
+    act = np.zeros(T * R, np.int32)
+    lp, val, rew, adv, ret = (np.zeros(T * R, np.float32) for _ in range(5))
+    dns = np.zeros(T * R, np.uint8)
+    started = ctypes.c_int(0)
+    t0 = time.perf_counter()
+    orc.orc_model_collect(m, env_fn, 0, ptr(states), ptr(done), ptr(rng), ptr(obs), ptr(act), ptr(lp), ptr(val),
+                          ptr(rew), ptr(dns), ptr(adv), ptr(ret), ctypes.byref(started), None, threads)
+    t_collect = time.perf_counter() - t0
+    stats = np.zeros((R, 5), np.float32)
+    nsq = np.zeros(1, np.float32)
+    n_mb, t_mb = 0, 0.0
+    while n_mb < 4 * T and (n_mb < 2 or t_collect + t_mb < seconds_budget):
+        t = n_mb % T
+        t1 = time.perf_counter()
+        orc.orc_model_train_minibatch(m, ptr(obs[t * R * O:(t + 1) * R * O]), ptr(act[t * R:(t + 1) * R]),
+                                      ptr(adv[t * R:(t + 1) * R]), ptr(ret[t * R:(t + 1) * R]),
+                                      ptr(lp[t * R:(t + 1) * R]), R, ptr(stats), ptr(nsq))
+        t_mb += time.perf_counter() - t1
+        n_mb += 1
+    orc.orc_model_destroy(m)
+    per_iter = t_collect + (t_mb / n_mb) * EPOCHS * T
+    return {"value": R * T / per_iter, "unit": "env steps/s", "cores": threads,
+            "kind": "reference" if ref is not None else "port",
+            "sample": f"1 collect (4096 envs x 32 steps, {t_collect:.2f} s) + {n_mb} of 128 minibatches "
+                      f"({t_mb / n_mb:.3f} s each), iteration time extrapolated",
+            "env_code": "reference sources (oracle/_ref)" if ref is not None else "host build of the env port",
+            "policy_code": "oracle restatement of model/ppo.h + model/*.metal"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path on this box's host cores."""
+    if rank != 0:
+        return None
+    vals = []
+    for _ in range(max(1, min(args.steps, 3))):
+        vals.append(cpu_full_loop(seconds_budget=15.0)["value"])
+    base = cpu_full_loop(seconds_budget=5.0)
+    v = statistics.median(vals)
+    fwd, bwd = flops_per_row(4, 2, EMBED, EMBED * SCALE, LAYERS)
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "env steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ENVS_PER_GPU * HORIZON / v * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": v / REFERENCE_M4_FULL_LOOP, "dtype": "bf16",
+            "data": "synthetic (simulated CartPole)",
+            "config": {"workload": "CartPole full PPO loop (BASELINE configs[2]): collect() + train(4) per step",
+                       "envs_per_gpu": ENVS_PER_GPU, "horizon": HORIZON, "embed": EMBED, "hidden": EMBED * SCALE,
+                       "blocks": LAYERS, "epochs": EPOCHS, "minibatch": "one slot (4096 rows)",
+                       "parallelism": "host cores (OpenMP)",
+                       "flop_per_env_step": (HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd)},
+            "cpu_baseline": {"value": v, "unit": "env steps/s", "cores": base["cores"], "kind": base["kind"],
+                             "sample": base["sample"]},
+            "e2e": {"value": v, "unit": "env steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_raw_env(seconds_budget=10.0):
+    """Config 1 on the host: the reference's own sampleAction (all-zero head)
+    and rollout<CartPole> compiled from source, OpenMP over envs."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    from orc import load_ref, ptr, seed_words
+
+    ref = load_ref()
+    if ref is None:
+        return None
+    threads = os.cpu_count()
+    n = ENVS_PER_GPU
+    states = np.zeros(n * 20, np.uint8)
+    obs = np.zeros(n * 16, np.uint8)
+    rew = np.zeros(n, np.float32)
+    done = np.ones(n, np.uint8)
+    rng = seed_words(n)
+    head = np.zeros((n, 64), np.uint16)
+    act = np.zeros(n, np.uint32)
+    lp = np.zeros(n, np.float32)
+    v = np.zeros(n, np.float32)
+    steps = 0
+    t0 = time.perf_counter()
+    while steps < RAW_STEPS and time.perf_counter() - t0 < seconds_budget:
+        ref.ref_sample_action(ptr(head), ptr(rng), ptr(act), ptr(lp), ptr(v), n, 2, 64)
+        ref.ref_rollout(0, ptr(states), ptr(act), ptr(obs), ptr(rew), ptr(done), ptr(rng), n, threads)
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": steps * n / dt, "unit": "env steps/s", "cores": threads, "kind": "reference",
+            "sample": f"{steps} steps x {n} envs (sampler single-threaded, env OpenMP)"}
+
+
+# ------------------------------------------------------------------ main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device(f"cuda:{local_rank}"))
+        dist = tdist
+    result = run_mine(args, rank, world, local_rank, dist)
+    if rank == 0 and result is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_full_loop()
+            raw = cpu_raw_env()
+            if raw is not None:
+                result["legs"]["raw_env"]["cpu_baseline"] = raw
+        print(json.dumps(result), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -297,6 +297,9 @@ int mg_ppo_set_step_counter(mg_ppo_t model, float step);
 int mg_ppo_buffer(mg_ppo_t model, int which, int slot, void** dev_ptr, size_t* bytes);
 int mg_ppo_download(mg_ppo_t model, int which, int slot, void* host, size_t bytes);
 int mg_ppo_upload(mg_ppo_t model, int which, int slot, const void* host, size_t bytes);
+/* Kernel launches in one replay of the captured collect() and train() graphs
+ * (0 before the first call); no counterpart in the reference. */
+int mg_ppo_graph_kernels(mg_ppo_t model, uint64_t out2[2]);
 /* Data parallelism (no counterpart in the reference): with world > 1 each
  * minibatch's gradient is summed over the ranks of `comm` (an ncclComm_t)
  * and divided by world before the norm clip and Adam. */

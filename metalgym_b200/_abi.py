@@ -77,6 +77,7 @@ SIGNATURES = {
     "mg_ppo_buffer": (I, [P, I, I, C.POINTER(P), C.POINTER(C.c_size_t)]),
     "mg_ppo_download": (I, [P, I, I, P, C.c_size_t]),
     "mg_ppo_upload": (I, [P, I, I, P, C.c_size_t]),
+    "mg_ppo_graph_kernels": (I, [P, P]),
     "mg_ppo_set_comm": (I, [P, P, I, I]),
     # NCCL / host memory
     "mg_comm_unique_id": (I, [P]),

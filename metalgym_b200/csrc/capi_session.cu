@@ -309,6 +309,13 @@ int mg_ppo_upload(mg_ppo_t model, int which, int slot, const void* host, size_t 
     return copy_checked(p, host, bytes, n, cudaMemcpyHostToDevice, P(model)->gym->stream);
 }
 
+int mg_ppo_graph_kernels(mg_ppo_t model, uint64_t out2[2]) {
+    MG_CHECK_ARG(model && out2, "mg_ppo_graph_kernels: null argument");
+    out2[0] = P(model)->collectKernels;
+    out2[1] = P(model)->trainKernels;
+    return MG_OK;
+}
+
 int mg_ppo_set_comm(mg_ppo_t model, void* comm, int rank, int world) {
     MG_CHECK_ARG(model, "null model");
     return P(model)->setComm(comm, rank, world);

@@ -92,6 +92,20 @@ float host_bf2f(uint16_t h) {
     return f;
 }
 
+// Kernel nodes in a captured graph (the launches one replay makes).
+size_t count_kernel_nodes(cudaGraph_t g) {
+    size_t n = 0;
+    if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess || n == 0) return 0;
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) return 0;
+    size_t k = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
+    }
+    return k;
+}
+
 int splits_for(int M, int N, int K, int bn) {
     const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
     int s = (256 + tiles - 1) / tiles;
@@ -608,6 +622,7 @@ int PpoEngine::captureCollect() {
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "collect capture");
+    collectKernels = count_kernel_nodes(graph);
     e = cudaGraphInstantiate(&collectExec, graph, 0);
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) return cuda_fail(e, "collect graph instantiate");
@@ -627,6 +642,7 @@ int PpoEngine::captureTrain(int minibatches) {
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "train capture");
+    trainKernels = count_kernel_nodes(graph);
     cudaGraphExec_t exec = nullptr;
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);

@@ -138,6 +138,7 @@ class PpoEngine {
     // graphs
     cudaGraphExec_t collectExec = nullptr;
     cudaGraphExec_t trainExec = nullptr;
+    size_t collectKernels = 0, trainKernels = 0;  // kernel nodes of the captured graphs
     int trainExecMinibatches = 0;
     PpoHyper collectHp, trainHp;
 

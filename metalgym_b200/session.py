@@ -166,6 +166,12 @@ class PPOModel:
     def set_step_counter(self, v: float):
         check(lib().mg_ppo_set_step_counter(self._h, v))
 
+    def graph_kernels(self) -> tuple[int, int]:
+        """Kernel launches per replay of the collect and train graphs."""
+        v = (C.c_uint64 * 2)()
+        check(lib().mg_ppo_graph_kernels(self._h, v))
+        return int(v[0]), int(v[1])
+
     def set_comm(self, comm, rank: int, world: int):
         check(lib().mg_ppo_set_comm(self._h, comm, rank, world))
 

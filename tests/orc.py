@@ -21,8 +21,22 @@ REF_LIB = ROOT / "oracle" / "_ref" / "libmg_ref.so"
 HOSTENV_LIB = ROOT / "tests" / "_build" / "libmg_hostenv.so"
 REFERENCE_TREE = Path(os.environ.get("METALGYM_REFERENCE", "/root/reference"))
 
-P, I, U, F, D = C.c_void_p, C.c_int, C.c_uint32, C.c_float, C.c_double
+I, U, F, D = C.c_int, C.c_uint32, C.c_float, C.c_double
 U16 = C.c_uint16
+
+
+class P(C.c_void_p):
+    """Pointer argument that also accepts a numpy array: the array object is
+    the call's argument, so it stays alive until the C function returns (a
+    raw address of a temporary array could be freed before the call)."""
+
+    @classmethod
+    def from_param(cls, obj):
+        if isinstance(obj, np.ndarray):
+            if not obj.flags["C_CONTIGUOUS"]:
+                raise ValueError("array argument must be C-contiguous")
+            return obj.ctypes.data_as(C.c_void_p)
+        return C.c_void_p.from_param(obj)
 
 
 def _sig(lib, name, res, args):
@@ -113,9 +127,10 @@ def load_hostenv():
 
 # ---------------------------------------------------------------- helpers
 
-def ptr(a: np.ndarray) -> int:
+def ptr(a: np.ndarray) -> np.ndarray:
+    """The array itself, checked contiguous: the bindings take arrays, not addresses."""
     assert a.flags["C_CONTIGUOUS"]
-    return a.ctypes.data
+    return a
 
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
