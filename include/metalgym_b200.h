@@ -316,6 +316,31 @@ int mg_allreduce_sum_f32(float* data, size_t count, void* comm, mg_stream_t stre
 int mg_host_alloc(size_t bytes, void** out);
 int mg_host_free(void* p);
 
+/* ---------------------------------------------------------------- no-allocation variant */
+
+/* Scratch held by mg_weight_grad_noalloc: 16 MiB of device memory per GPU. */
+#define MG_WEIGHT_GRAD_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* No counterpart in the reference. The weight gradient of the PPO backward
+ * pass, dw_out[m][n] = sum_r x[r][m] * dz[r][n] (x bf16 [rows][in_features],
+ * dz bf16 [rows][out_features], dw_out fp32 [in_features][out_features],
+ * rounded to bf16 values if round_bf16), for callers that cannot allocate
+ * device memory: code inside a framework that owns all device memory (a
+ * custom call or plugin that must not allocate while enqueuing) or a program
+ * that allocates nothing after start-up. It computes what mg_gemm_bf16 with
+ * MG_EPI_F32 and `splits` followed by mg_reduce_partials computes, but keeps
+ * the split-K partials in a fixed scratch array inside the library
+ * (MG_WEIGHT_GRAD_NOALLOC_SCRATCH_BYTES on every GPU that loads it, held
+ * until the process exits) and calls no allocator. Sizes whose scratch need
+ * (effective splits x in_features x out_features x 4 bytes, plus 4 bytes
+ * per 1024 outputs) exceeds that are rejected with MG_ERR_ARGUMENT. The
+ * first call on a device looks up the scratch address on that device; make
+ * that first call before any stream capture. All calls share the scratch and
+ * it keeps the last call's contents (every call overwrites what it reads), so
+ * calls that overlap on the GPU race. Asynchronous on `stream`. */
+int mg_weight_grad_noalloc(const void* x, const void* dz, int rows, int in_features, int out_features, int splits,
+                           int round_bf16, float* dw_out, mg_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,4 +86,6 @@ SIGNATURES = {
     "mg_allreduce_sum_f32": (I, [P, C.c_size_t, P, P]),
     "mg_host_alloc": (I, [C.c_size_t, C.POINTER(P)]),
     "mg_host_free": (I, [P]),
+    # no-allocation variant
+    "mg_weight_grad_noalloc": (I, [P, P, I, I, I, I, I, P, P]),
 }

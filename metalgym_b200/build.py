@@ -34,6 +34,7 @@ SOURCES: dict[str, list[str]] = {
     "envs_builtin.cu": ["--fmad=false"],
     "engine.cu": [],
     "capi_session.cu": [],
+    "noalloc.cu": [],
 }
 
 
