@@ -1,0 +1,4 @@
+// Drop-in include path: a host program written against the reference
+// (`#include "gym.h"`) compiles unchanged with -I<this include directory>.
+#pragma once
+#include "metalgym/gym.h"

@@ -136,13 +136,13 @@ int mg_env_collect_step(const char* kernel_name, const void* head, const void* l
  * Replaces inputForward (model/input.metal:11-27). */
 int mg_input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int in_dim, int out_dim,
                      mg_stream_t stream);
-/* Per-128-row partial sums of dW = obs^T dZ and db = sum_r dZ: partial holds
- * mg_input_backward_num_partials(rows) blocks of (in_dim + 1) x out_dim fp32
+/* Per-row-range partial sums of dW = obs^T dZ and db = sum_r dZ: partial holds
+ * mg_input_backward_num_partials(rows, in_dim, out_dim) blocks of (in_dim + 1) x out_dim fp32
  * (rows 0..in_dim-1: dW, row in_dim: db). Replaces inputBackward
  * (model/input.metal:38-60), whose chunk sums go to fp32 atomics. */
 int mg_input_backward_partials(const float* obs, const void* dZ, float* partial, int rows, int in_dim, int out_dim,
                                mg_stream_t stream);
-int mg_input_backward_num_partials(int rows);
+int mg_input_backward_num_partials(int rows, int in_dim, int out_dim);
 /* Row LayerNorm, eps 1e-5: x_norm = bf16(x-hat), out = bf16(gamma x-hat + beta),
  * stdev = sqrt(var + eps); cols in {64, 128, 256, 512, 1024}.
  * Replaces layernormForward (model/layernorm.metal:10-71). */

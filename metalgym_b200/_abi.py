@@ -33,7 +33,7 @@ SIGNATURES = {
     # policy kernels
     "mg_input_forward": (I, [P, P, P, P, I, I, I, P]),
     "mg_input_backward_partials": (I, [P, P, P, I, I, I, P]),
-    "mg_input_backward_num_partials": (I, [I]),
+    "mg_input_backward_num_partials": (I, [I, I, I]),
     "mg_layernorm_forward": (I, [P, P, P, P, P, P, I, I, P]),
     "mg_layernorm_backward": (I, [P, P, P, P, P, P, I, I, P]),
     "mg_layernorm_backward_num_partials": (I, [I]),

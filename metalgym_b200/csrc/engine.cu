@@ -375,7 +375,7 @@ int PpoEngine::init() {
     downPart.resize(L);
     lnPart.resize(L);
     const int pLn = layernorm_backward_parts(R);
-    const int pIn = input_backward_parts(R);
+    const int pIn = input_backward_parts(R, O, E);
     const int pGs = gaussian_loss_parts(R);
     for (int n = 0; n < L; n++) {
         MG_TRY(dalloc(&upPart[n], (size_t)upSplits * E * H * 4));

@@ -10,8 +10,9 @@ namespace mg {
 
 namespace {
 
-constexpr int kLnRowsPerCta = 64;      // LayerNorm backward: rows per CTA (8 warps x 8 rows)
-constexpr int kInputRowsPerCta = 128;  // input backward: rows per CTA
+constexpr int kLnRowsPerCta = 16;       // LayerNorm backward: rows per CTA (8 warps x 2 rows)
+constexpr int kInputRowChunk = 16;      // input backward: rows loaded per unrolled step
+constexpr int64_t kInputPartialBudget = 8 << 20;  // bytes of input-backward partials at most
 constexpr int kGaussRowsPerCta = 256;  // Gaussian loss: rows per CTA
 
 // ------------------------------------------------------------------ input
@@ -47,16 +48,18 @@ __global__ void k_input_forward(const float* __restrict__ obs, const __nv_bfloat
     }
 }
 
-// model/input.metal:38-60: per-CTA partial sums over a chunk of rows of
-// dW[k, c] = sum_r obs[r, k] dZ[r, c] and db[c] = sum_r dZ[r, c].
-// partial[blockIdx] = [(inDim + 1) x outDim]: rows 0..inDim-1 dW, row inDim db.
+// model/input.metal:38-60: per-CTA partial sums over a contiguous range of
+// rowsPerCta rows of dW[k, c] = sum_r obs[r, k] dZ[r, c] and db[c] = sum_r
+// dZ[r, c]; partial[blockIdx] = [(inDim + 1) x outDim]: rows 0..inDim-1 dW,
+// row inDim db. One thread per column; 16 rows of dZ are loaded at a time
+// into registers (independent loads), obs rows come from shared memory.
 __global__ void k_input_backward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ dZ,
-                                 float* __restrict__ partial, int rows, int inDim, int outDim,
+                                 float* __restrict__ partial, int rows, int inDim, int outDim, int rowsPerCta,
                                  const int* __restrict__ slotIdx, int64_t slotStride) {
-    extern __shared__ float s_obs[];  // kInputRowsPerCta x inDim
+    extern __shared__ float s_obs[];  // rowsPerCta x inDim
     if (slotIdx) obs += (int64_t)(*slotIdx) * slotStride;
-    const int r0 = blockIdx.x * kInputRowsPerCta;
-    const int nr = min(kInputRowsPerCta, rows - r0);
+    const int r0 = blockIdx.x * rowsPerCta;
+    const int nr = min(rowsPerCta, rows - r0);
     for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) s_obs[i] = obs[(size_t)r0 * inDim + i];
     __syncthreads();
     float* part = partial + (size_t)blockIdx.x * (inDim + 1) * outDim;
@@ -66,12 +69,20 @@ __global__ void k_input_backward(const float* __restrict__ obs, const __nv_bfloa
             float acc[8];
 #pragma unroll
             for (int k = 0; k < 8; k++) acc[k] = 0.0f;
-            for (int r = 0; r < nr; r++) {
-                const float d = bf(dZ[(size_t)(r0 + r) * outDim + c]);
-                if (k0 == 0) accB = __fadd_rn(accB, d);
+            for (int rb = 0; rb < nr; rb += kInputRowChunk) {
+                float d[kInputRowChunk];
 #pragma unroll
-                for (int k = 0; k < 8; k++)
-                    if (k0 + k < inDim) acc[k] = __fadd_rn(acc[k], __fmul_rn(s_obs[r * inDim + k0 + k], d));
+                for (int i = 0; i < kInputRowChunk; i++)
+                    d[i] = (rb + i < nr) ? bf(dZ[(size_t)(r0 + rb + i) * outDim + c]) : 0.0f;
+#pragma unroll
+                for (int i = 0; i < kInputRowChunk; i++) {
+                    if (rb + i >= nr) break;
+                    if (k0 == 0) accB = __fadd_rn(accB, d[i]);
+                    const float* o = s_obs + (rb + i) * inDim + k0;
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        if (k0 + k < inDim) acc[k] = __fadd_rn(acc[k], __fmul_rn(o[k], d[i]));
+                }
             }
 #pragma unroll
             for (int k = 0; k < 8; k++)
@@ -161,6 +172,7 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
     }
     const int r0 = blockIdx.x * kLnRowsPerCta;
     const int r1 = min(rows, r0 + kLnRowsPerCta);
+#pragma unroll 2
     for (int r = r0 + warp; r < r1; r += 8) {
         float dz[VPT], xn[VPT], dxn[VPT];
         const size_t base = (size_t)r * E + c0;
@@ -608,16 +620,30 @@ int input_forward(const float* obs, const void* w, const void* b, void* out, int
     return check_launch("k_input_forward");
 }
 
-int input_backward_parts(int rows) { return grid_rows(rows, kInputRowsPerCta); }
+// Rows per CTA of the input backward: 16, or more when the partial sums of
+// that many CTAs would exceed kInputPartialBudget bytes.
+static int input_rows_per_cta(int rows, int inDim, int outDim) {
+    const int64_t perPart = (int64_t)(inDim + 1) * outDim * 4;
+    const int64_t maxParts = std::max<int64_t>(1, kInputPartialBudget / perPart);
+    int rpc = kInputRowChunk;
+    while ((rows + rpc - 1) / rpc > maxParts) rpc += kInputRowChunk;
+    return rpc;
+}
+
+int input_backward_parts(int rows, int inDim, int outDim) {
+    return grid_rows(rows, input_rows_per_cta(rows, inDim, outDim));
+}
 
 int input_backward(const float* obs, const void* dZ, float* partial, int rows, int inDim, int outDim,
                    cudaStream_t st, const int* slotIdx, int64_t slotStride) {
     MG_CHECK_ARG(rows > 0 && inDim > 0 && inDim <= 256 && outDim > 0 && outDim <= 1024, "input_backward: bad shape");
-    const size_t sm = (size_t)kInputRowsPerCta * inDim * 4;
+    const int rpc = input_rows_per_cta(rows, inDim, outDim);
+    const size_t sm = (size_t)rpc * inDim * 4;
+    MG_CHECK_ARG(sm <= 200 * 1024, "input_backward: rows per CTA x in_dim too large for shared memory");
     if (sm > 48 * 1024)
         MG_CUDA_TRY(cudaFuncSetAttribute(k_input_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    k_input_backward<<<input_backward_parts(rows), std::min(outDim, 1024), sm, st>>>(
-        obs, static_cast<const __nv_bfloat16*>(dZ), partial, rows, inDim, outDim, slotIdx, slotStride);
+    k_input_backward<<<grid_rows(rows, rpc), std::min(outDim, 1024), sm, st>>>(
+        obs, static_cast<const __nv_bfloat16*>(dZ), partial, rows, inDim, outDim, rpc, slotIdx, slotStride);
     return check_launch("k_input_backward");
 }
 
@@ -682,7 +708,7 @@ int policy_loss(const void* head, const int32_t* action, const float* adv, const
                 const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
                 cudaStream_t st, const int* slotIdx) {
     MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "policy_loss: bad shape");
-    k_policy_loss<<<grid_rows(rows, 128), 128, 0, st>>>(static_cast<const __nv_bfloat16*>(head), action, adv,
+    k_policy_loss<<<grid_rows(rows, 64), 64, 0, st>>>(static_cast<const __nv_bfloat16*>(head), action, adv,
                                                          advStats, ret, oldLogProb, static_cast<__nv_bfloat16*>(dZ),
                                                          stats, rows, actDim, hp, status_ptr(), slotIdx);
     return check_launch("k_policy_loss");
@@ -774,7 +800,9 @@ int mg_input_backward_partials(const float* obs, const void* dZ, float* partial,
     return mg::input_backward(obs, dZ, partial, rows, in_dim, out_dim, MG_STREAM(s));
 }
 
-int mg_input_backward_num_partials(int rows) { return mg::input_backward_parts(rows); }
+int mg_input_backward_num_partials(int rows, int in_dim, int out_dim) {
+    return mg::input_backward_parts(rows, in_dim, out_dim);
+}
 
 int mg_layernorm_forward(const void* x, void* x_norm, void* out, const void* gamma, const void* beta, float* stdev,
                          int rows, int cols, mg_stream_t s) {

@@ -45,7 +45,7 @@ struct GradSegmentTable {
 // slotIdx (device, optional): read obs at obs + slotIdx[0] * slotStride.
 int input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int inDim, int outDim,
                   cudaStream_t st, const int* slotIdx = nullptr, int64_t slotStride = 0);
-int input_backward_parts(int rows);
+int input_backward_parts(int rows, int inDim, int outDim);
 int input_backward(const float* obs, const void* dZ, float* partial, int rows, int inDim, int outDim,
                    cudaStream_t st, const int* slotIdx = nullptr, int64_t slotStride = 0);
 int layernorm_forward(const void* x, void* xNorm, void* out, const void* gamma, const void* beta, float* stdev,

@@ -307,7 +307,7 @@ def test_input_projection(mg, oracle):
                                out.data_ptr(), R, O, E, None))
     sync_status(mg)
     assert np.array_equal(host(out, np.uint16, (R, E)), g["in_out"])
-    P = mg.mg_input_backward_num_partials(R)
+    P = mg.mg_input_backward_num_partials(R, O, E)
     part = torch.zeros(P * (O + 1) * E, dtype=torch.float32, device="cuda")
     ok(mg, mg.mg_input_backward_partials(dev(g["in_obs"]).data_ptr(), dev(g["in_dz"]).data_ptr(), part.data_ptr(), R,
                                          O, E, None))
