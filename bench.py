@@ -155,12 +155,20 @@ def run_mine(args, rank, world, local_rank, dist):
     # ---- device-timed full loop
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # Under a profiler started with --profile-from-start off, only the first
+    # timed iteration is inside the profiled range.
+    profile_range = os.environ.get("MG_PROFILE_FIRST_TIMED_STEP") == "1"
     with Clocks(local_rank) as clk:
         for k in range(args.steps):
             with torch.cuda.stream(stream):
                 flush.fill_(float(k))
                 starts[k].record(stream)
+            if profile_range and k == 0:
+                torch.cuda.synchronize()
+                torch.cuda.profiler.start()
             iteration()
+            if profile_range and k == 0:
+                torch.cuda.profiler.stop()
             with torch.cuda.stream(stream):
                 ends[k].record(stream)
         torch.cuda.synchronize()

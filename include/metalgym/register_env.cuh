@@ -20,6 +20,7 @@
 #include <type_traits>
 
 #include "../metalgym_b200.h"
+#include "pdl.cuh"
 #include "sampling.cuh"
 
 namespace mg {
@@ -83,6 +84,8 @@ template <class Env>
 __global__ void env_step_kernel(typename Env::State* states, const typename Env::Action* actions,
                                 typename Env::Obs* obs, float* reward, uint8_t* done, uint8_t* doneCopy, uint32_t* rng,
                                 int n) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     uint32_t w = rng[i];
@@ -113,6 +116,8 @@ template <class Env>
 __global__ void env_run_random_kernel(typename Env::State* states, typename Env::Obs* obsRing, float* rewardRing,
                                       uint8_t* doneRing, uint8_t* done, uint32_t* rng, int n, int steps, int ring,
                                       int mode) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     uint32_t w = rng[i];
@@ -155,6 +160,8 @@ __global__ void env_collect_step_kernel(const __nv_bfloat16* head, const __nv_bf
                                         typename Env::State* states, typename Env::Action* actionOut, float* logpOut,
                                         float* valueOut, typename Env::Obs* obsOut, float* rewardOut, uint8_t* done,
                                         uint8_t* doneSlot, uint32_t* rng, int n) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     uint32_t w = rng[i];
@@ -192,7 +199,7 @@ struct EnvLaunchers {
     static int step(void* states, const void* actions, void* obs, float* reward, uint8_t* done, uint8_t* doneCopy,
                     uint32_t* rng, int n, mg_stream_t s) {
         if (n <= 0) return MG_ERR_ARGUMENT;
-        env_step_kernel<Env><<<grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s)>>>(
+        MG_LAUNCH(env_step_kernel<Env>, grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s), 
             static_cast<typename T::State*>(states), static_cast<const typename T::Action*>(actions),
             static_cast<typename T::Obs*>(obs), reward, done, doneCopy, rng, n);
         return cudaGetLastError() == cudaSuccess ? MG_OK : MG_ERR_CUDA;
@@ -200,7 +207,7 @@ struct EnvLaunchers {
     static int run_random(void* states, void* obsRing, float* rewardRing, uint8_t* doneRing, uint8_t* done,
                           uint32_t* rng, int n, int steps, int ring, int mode, mg_stream_t s) {
         if (n <= 0 || steps < 0 || ring <= 0) return MG_ERR_ARGUMENT;
-        env_run_random_kernel<Env><<<grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s)>>>(
+        MG_LAUNCH(env_run_random_kernel<Env>, grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s), 
             static_cast<typename T::State*>(states), static_cast<typename T::Obs*>(obsRing), rewardRing, doneRing,
             done, rng, n, steps, ring, mode);
         return cudaGetLastError() == cudaSuccess ? MG_OK : MG_ERR_CUDA;
@@ -209,7 +216,7 @@ struct EnvLaunchers {
                             float* valueOut, void* obsOut, float* rewardOut, uint8_t* done, uint8_t* doneSlot,
                             uint32_t* rng, int n, mg_stream_t s) {
         if (n <= 0) return MG_ERR_ARGUMENT;
-        env_collect_step_kernel<Env><<<grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s)>>>(
+        MG_LAUNCH(env_collect_step_kernel<Env>, grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s), 
             static_cast<const __nv_bfloat16*>(head), static_cast<const __nv_bfloat16*>(logStd),
             static_cast<typename T::State*>(states), static_cast<typename T::Action*>(actionOut), logpOut, valueOut,
             static_cast<typename T::Obs*>(obsOut), rewardOut, done, doneSlot, rng, n);

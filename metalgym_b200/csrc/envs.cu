@@ -4,6 +4,7 @@
 #include <mutex>
 #include <string>
 
+#include "metalgym/pdl.cuh"
 #include "metalgym/rng.h"
 #include "runtime.h"
 
@@ -26,6 +27,8 @@ Registry& registry() {
 // gym.h:54-61: done = 1 (the first step resets every env), one seeded
 // xorshift word per env.
 __global__ void k_env_init(uint8_t* done, uint32_t* rng, int n, uint32_t seed, uint32_t first) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     done[i] = 1;
@@ -86,7 +89,7 @@ int mg_env_init(const char* kernel_name, void* states, uint8_t* done, uint32_t* 
     MG_CHECK_ARG(states && done && rng && n > 0, "mg_env_init: bad arguments");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     MG_CUDA_TRY(cudaMemsetAsync(states, 0, (size_t)n * o->state_bytes, st));
-    mg::k_env_init<<<(n + 255) / 256, 256, 0, st>>>(done, rng, n, seed, first_env_id);
+    MG_LAUNCH(mg::k_env_init, (n + 255) / 256, 256, 0, st, done, rng, n, seed, first_env_id);
     return mg::check_launch("k_env_init");
 }
 

@@ -19,7 +19,7 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
         attr_done |= 1ull << (dev & 63);
     }
     dim3 grid((p.M + S::BM - 1) / S::BM, (p.N + BN - 1) / BN, splits);
-    kern<<<grid, 128, S::SMEM_BYTES, st>>>(ta, tb, p);
+    MG_CUDA_TRY(mg_launch(kern, grid, dim3(128), (size_t)S::SMEM_BYTES, st, ta, tb, p));
     return check_launch("gemm_tc_kernel");
 }
 

@@ -17,6 +17,7 @@
 // No cluster launch and no multicast: every CTA loads its own tiles.
 #pragma once
 
+#include "metalgym/pdl.cuh"
 #include "ptx.cuh"
 
 namespace mg {
@@ -93,6 +94,7 @@ __global__ void __launch_bounds__(128, 1)
     uint64_t* done = empty + S::STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
+    mg_pdl_trigger();
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * S::BM;
@@ -119,6 +121,7 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    mg_pdl_wait();  // operands and aux come from the previous kernel
 
     if (warp == 0 && lane == 0) {
         // ---- TMA producer

@@ -23,6 +23,8 @@ template <int VPT>
 __global__ void k_input_forward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ w,
                                 const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int rows,
                                 int inDim, int outDim, const int* __restrict__ slotIdx, int64_t slotStride) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     extern __shared__ float s_w[];  // inDim x outDim as fp32
     if (slotIdx) obs += (int64_t)(*slotIdx) * slotStride;
     for (int i = threadIdx.x; i < inDim * outDim; i += blockDim.x) s_w[i] = bf(w[i]);
@@ -56,6 +58,8 @@ __global__ void k_input_forward(const float* __restrict__ obs, const __nv_bfloat
 __global__ void k_input_backward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ dZ,
                                  float* __restrict__ partial, int rows, int inDim, int outDim, int rowsPerCta,
                                  const int* __restrict__ slotIdx, int64_t slotStride) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     extern __shared__ float s_obs[];  // rowsPerCta x inDim
     if (slotIdx) obs += (int64_t)(*slotIdx) * slotStride;
     const int r0 = blockIdx.x * rowsPerCta;
@@ -100,6 +104,8 @@ template <int VPT>
 __global__ void k_layernorm_forward(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ xNorm,
                                     __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gamma,
                                     const __nv_bfloat16* __restrict__ beta, float* __restrict__ stdev, int rows) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     constexpr int E = VPT * 32;
     const int lane = threadIdx.x & 31;
     const int c0 = lane * VPT;
@@ -158,6 +164,8 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
                                                             const float* __restrict__ stdev,
                                                             __nv_bfloat16* __restrict__ resid,
                                                             float* __restrict__ partial, int rows) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     constexpr int E = VPT * 32;
     __shared__ float s_red[8][2 * E];
     const int lane = threadIdx.x & 31;
@@ -232,6 +240,8 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
 __global__ void k_sample_categorical(const __nv_bfloat16* __restrict__ head, uint32_t* __restrict__ rng,
                                      int32_t* __restrict__ action, float* __restrict__ logProb,
                                      float* __restrict__ value, int rows, int actDim) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     uint32_t s = rng[r];
@@ -245,6 +255,8 @@ __global__ void k_sample_categorical(const __nv_bfloat16* __restrict__ head, uin
 __global__ void k_sample_gaussian(const __nv_bfloat16* __restrict__ head, const __nv_bfloat16* __restrict__ logStd,
                                   uint32_t* __restrict__ rng, float* __restrict__ action, float* __restrict__ logProb,
                                   float* __restrict__ value, int rows, int actDim) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     uint32_t s = rng[r];
@@ -266,6 +278,8 @@ __global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int3
                               const float* __restrict__ ret, const float* __restrict__ oldLogProb,
                               __nv_bfloat16* __restrict__ dZ, float* __restrict__ stats, int rows, int actDim,
                               LossHyper hp, int* status, const int* __restrict__ slotIdx) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     if (slotIdx) {  // slot-major rollout buffers: slot s starts at s * rows
@@ -332,6 +346,8 @@ __global__ void __launch_bounds__(kGaussRowsPerCta) k_gaussian_loss(
     const float* __restrict__ advStats, const float* __restrict__ ret, const float* __restrict__ oldLogProb,
     __nv_bfloat16* __restrict__ dZ, float* __restrict__ stats, const __nv_bfloat16* __restrict__ logStd,
     float* __restrict__ partial, int rows, int actDim, LossHyper hp, const int* __restrict__ slotIdx) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     __shared__ float s_gls[kGaussRowsPerCta];
     if (slotIdx) {
         const int64_t s = *slotIdx;
@@ -413,6 +429,8 @@ __global__ void k_gae(const float* __restrict__ reward, const uint8_t* __restric
                       const float* __restrict__ value, const __nv_bfloat16* __restrict__ bootHead,
                       float* __restrict__ advantage, float* __restrict__ ret, int rows, int horizon, int actDim,
                       float gamma, float lambda) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows) return;
     float lastAdv = 0.0f;
@@ -433,6 +451,8 @@ __global__ void k_gae(const float* __restrict__ reward, const uint8_t* __restric
 // model/gae.metal:42-77 statistics: for minibatch (slot) s, mean and
 // inv = 1 / (population std + 1e-8) of adv[s * rows .. s * rows + rows).
 __global__ void __launch_bounds__(1024) k_adv_stats(const float* __restrict__ adv, float* __restrict__ out, int rows) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     __shared__ float s_part[32];
     __shared__ float s_mean;
     const float* a = adv + (size_t)blockIdx.x * rows;
@@ -478,6 +498,8 @@ __global__ void __launch_bounds__(1024) k_adv_stats(const float* __restrict__ ad
 // squares per CTA for the global norm (model/optimizer.metal:23-34).
 __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ GradSegmentTable tab,
                                                        float* __restrict__ grad, float* __restrict__ normPartial) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     __shared__ float s_red[8];
     int b = blockIdx.x, si = 0;
     while (si < tab.n - 1 && b >= tab.seg[si].blockEnd) si++;
@@ -510,6 +532,8 @@ __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ G
 // cross-GPU all-reduce, which also rescales the sum to a mean).
 __global__ void __launch_bounds__(256) k_grad_scale_norm(float* __restrict__ grad, int64_t count, float scale,
                                                          float* __restrict__ normPartial) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     __shared__ float s_red[8];
     float sq = 0.0f;
     const int64_t i0 = (int64_t)blockIdx.x * 1024;
@@ -540,6 +564,8 @@ __global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const f
                                               const float* __restrict__ normPartial, int nNorm, int64_t count,
                                               AdamHyper hp, const float* __restrict__ betaPow,
                                               float* __restrict__ normSqOut) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     __shared__ float s_scale;
     if (threadIdx.x < 32) {
         float s = 0.0f;
@@ -575,6 +601,8 @@ __global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const f
 
 // LossStats (model/ppo.h:925-943): column means of the rows x 5 stats.
 __global__ void __launch_bounds__(256) k_stats_mean(const float* __restrict__ stats, int rows, float* __restrict__ out) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
     __shared__ float s_red[8][5];
     float acc[5] = {0, 0, 0, 0, 0};
     for (int r = threadIdx.x; r < rows; r += blockDim.x)
@@ -610,7 +638,7 @@ int input_forward(const float* obs, const void* w, const void* b, void* out, int
     case V:                                                                                        \
         if (sm > 48 * 1024)                                                                        \
             MG_CUDA_TRY(cudaFuncSetAttribute(k_input_forward<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
-        k_input_forward<V><<<blocks, 256, sm, st>>>(obs, W, B, O, rows, inDim, outDim, slotIdx, slotStride); \
+        MG_LAUNCH(k_input_forward<V>, blocks, 256, sm, st, obs, W, B, O, rows, inDim, outDim, slotIdx, slotStride); \
         break;
     switch (outDim / 32) {
         MG_IN_FWD(2) MG_IN_FWD(4) MG_IN_FWD(8) MG_IN_FWD(16) MG_IN_FWD(32)
@@ -642,7 +670,7 @@ int input_backward(const float* obs, const void* dZ, float* partial, int rows, i
     MG_CHECK_ARG(sm <= 200 * 1024, "input_backward: rows per CTA x in_dim too large for shared memory");
     if (sm > 48 * 1024)
         MG_CUDA_TRY(cudaFuncSetAttribute(k_input_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    k_input_backward<<<grid_rows(rows, rpc), std::min(outDim, 1024), sm, st>>>(
+    MG_LAUNCH(k_input_backward, grid_rows(rows, rpc), std::min(outDim, 1024), sm, st, 
         obs, static_cast<const __nv_bfloat16*>(dZ), partial, rows, inDim, outDim, rpc, slotIdx, slotStride);
     return check_launch("k_input_backward");
 }
@@ -657,11 +685,11 @@ int layernorm_forward(const void* x, void* xNorm, void* out, const void* gamma, 
     auto G = static_cast<const __nv_bfloat16*>(gamma);
     auto Bt = static_cast<const __nv_bfloat16*>(beta);
     switch (cols) {
-        case 64: k_layernorm_forward<2><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
-        case 128: k_layernorm_forward<4><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
-        case 256: k_layernorm_forward<8><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
-        case 512: k_layernorm_forward<16><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
-        case 1024: k_layernorm_forward<32><<<blocks, 256, 0, st>>>(X, XN, Y, G, Bt, stdev, rows); break;
+        case 64: MG_LAUNCH(k_layernorm_forward<2>, blocks, 256, 0, st, X, XN, Y, G, Bt, stdev, rows); break;
+        case 128: MG_LAUNCH(k_layernorm_forward<4>, blocks, 256, 0, st, X, XN, Y, G, Bt, stdev, rows); break;
+        case 256: MG_LAUNCH(k_layernorm_forward<8>, blocks, 256, 0, st, X, XN, Y, G, Bt, stdev, rows); break;
+        case 512: MG_LAUNCH(k_layernorm_forward<16>, blocks, 256, 0, st, X, XN, Y, G, Bt, stdev, rows); break;
+        case 1024: MG_LAUNCH(k_layernorm_forward<32>, blocks, 256, 0, st, X, XN, Y, G, Bt, stdev, rows); break;
         default: return fail(MG_ERR_ARGUMENT, "layernorm: cols must be 64, 128, 256, 512 or 1024");
     }
     return check_launch("k_layernorm_forward");
@@ -678,10 +706,10 @@ int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const flo
     auto G = static_cast<const __nv_bfloat16*>(gamma);
     auto R = static_cast<__nv_bfloat16*>(resid);
     switch (cols) {
-        case 64: k_layernorm_backward<2><<<blocks, 256, 0, st>>>(DZ, XN, G, stdev, R, partial, rows); break;
-        case 128: k_layernorm_backward<4><<<blocks, 256, 0, st>>>(DZ, XN, G, stdev, R, partial, rows); break;
-        case 256: k_layernorm_backward<8><<<blocks, 256, 0, st>>>(DZ, XN, G, stdev, R, partial, rows); break;
-        case 512: k_layernorm_backward<16><<<blocks, 256, 0, st>>>(DZ, XN, G, stdev, R, partial, rows); break;
+        case 64: MG_LAUNCH(k_layernorm_backward<2>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows); break;
+        case 128: MG_LAUNCH(k_layernorm_backward<4>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows); break;
+        case 256: MG_LAUNCH(k_layernorm_backward<8>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows); break;
+        case 512: MG_LAUNCH(k_layernorm_backward<16>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows); break;
         default: return fail(MG_ERR_ARGUMENT, "layernorm_backward: cols must be 64, 128, 256 or 512");
     }
     return check_launch("k_layernorm_backward");
@@ -690,7 +718,7 @@ int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const flo
 int sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* logProb, float* value, int rows,
                        int actDim, cudaStream_t st) {
     MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "sample_categorical: bad shape");
-    k_sample_categorical<<<grid_rows(rows, 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(head), rng, action,
+    MG_LAUNCH(k_sample_categorical, grid_rows(rows, 256), 256, 0, st, static_cast<const __nv_bfloat16*>(head), rng, action,
                                                                 logProb, value, rows, actDim);
     return check_launch("k_sample_categorical");
 }
@@ -698,7 +726,7 @@ int sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* 
 int sample_gaussian(const void* head, const void* logStd, uint32_t* rng, float* action, float* logProb,
                     float* value, int rows, int actDim, cudaStream_t st) {
     MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "sample_gaussian: bad shape");
-    k_sample_gaussian<<<grid_rows(rows, 256), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(head),
+    MG_LAUNCH(k_sample_gaussian, grid_rows(rows, 256), 256, 0, st, static_cast<const __nv_bfloat16*>(head),
                                                              static_cast<const __nv_bfloat16*>(logStd), rng, action,
                                                              logProb, value, rows, actDim);
     return check_launch("k_sample_gaussian");
@@ -708,7 +736,7 @@ int policy_loss(const void* head, const int32_t* action, const float* adv, const
                 const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
                 cudaStream_t st, const int* slotIdx) {
     MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "policy_loss: bad shape");
-    k_policy_loss<<<grid_rows(rows, 64), 64, 0, st>>>(static_cast<const __nv_bfloat16*>(head), action, adv,
+    MG_LAUNCH(k_policy_loss, grid_rows(rows, 64), 64, 0, st, static_cast<const __nv_bfloat16*>(head), action, adv,
                                                          advStats, ret, oldLogProb, static_cast<__nv_bfloat16*>(dZ),
                                                          stats, rows, actDim, hp, status_ptr(), slotIdx);
     return check_launch("k_policy_loss");
@@ -720,7 +748,7 @@ int gaussian_loss(const void* head, const float* action, const float* adv, const
                   const float* oldLogProb, void* dZ, float* stats, const void* logStd, float* partial, int rows,
                   int actDim, LossHyper hp, cudaStream_t st, const int* slotIdx) {
     MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "gaussian_loss: bad shape");
-    k_gaussian_loss<<<gaussian_loss_parts(rows), kGaussRowsPerCta, 0, st>>>(
+    MG_LAUNCH(k_gaussian_loss, gaussian_loss_parts(rows), kGaussRowsPerCta, 0, st, 
         static_cast<const __nv_bfloat16*>(head), action, adv, advStats, ret, oldLogProb,
         static_cast<__nv_bfloat16*>(dZ), stats, static_cast<const __nv_bfloat16*>(logStd), partial, rows, actDim, hp,
         slotIdx);
@@ -730,14 +758,14 @@ int gaussian_loss(const void* head, const float* action, const float* adv, const
 int gae(const float* reward, const uint8_t* done, const float* value, const void* bootHead, float* adv, float* ret,
         int rows, int horizon, int actDim, float gamma, float lambda, cudaStream_t st) {
     MG_CHECK_ARG(rows > 0 && horizon > 0, "gae: bad shape");
-    k_gae<<<grid_rows(rows, 128), 128, 0, st>>>(reward, done, value, static_cast<const __nv_bfloat16*>(bootHead), adv,
+    MG_LAUNCH(k_gae, grid_rows(rows, 128), 128, 0, st, reward, done, value, static_cast<const __nv_bfloat16*>(bootHead), adv,
                                                  ret, rows, horizon, actDim, gamma, lambda);
     return check_launch("k_gae");
 }
 
 int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStream_t st) {
     MG_CHECK_ARG(rows > 0 && slots > 0, "advantage_stats: bad shape");
-    k_adv_stats<<<slots, 1024, 0, st>>>(adv, out, rows);
+    MG_LAUNCH(k_adv_stats, slots, 1024, 0, st, adv, out, rows);
     return check_launch("k_adv_stats");
 }
 
@@ -754,14 +782,14 @@ int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, 
     MG_CHECK_ARG(tab.n > 0 && tab.n <= kMaxGradSegments, "grad_finalize: bad segment count");
     const int nblocks = tab.seg[tab.n - 1].blockEnd;
     MG_CHECK_ARG(nblocks > 0, "grad_finalize: empty");
-    k_grad_finalize<<<nblocks, 256, 0, st>>>(tab, grad, normPartial);
+    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, normPartial);
     return check_launch("k_grad_finalize");
 }
 
 int grad_scale_norm_blocks(int64_t count) { return (int)((count + 1023) / 1024); }
 
 int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st) {
-    k_grad_scale_norm<<<grad_scale_norm_blocks(count), 256, 0, st>>>(grad, count, scale, normPartial);
+    MG_LAUNCH(k_grad_scale_norm, grad_scale_norm_blocks(count), 256, 0, st, grad, count, scale, normPartial);
     return check_launch("k_grad_scale_norm");
 }
 
@@ -769,13 +797,13 @@ int adam(float* param, const float* grad, float* mom, float* var, void* weights,
          int64_t count, AdamHyper hp, const float* betaPow, float* normSqOut, cudaStream_t st) {
     MG_CHECK_ARG(count > 0 && nNorm > 0, "adam: bad shape");
     const int blocks = (int)std::min<int64_t>((count + 255) / 256, 148 * 8);
-    k_adam<<<blocks, 256, 0, st>>>(param, grad, mom, var, static_cast<__nv_bfloat16*>(weights), normPartial, nNorm,
+    MG_LAUNCH(k_adam, blocks, 256, 0, st, param, grad, mom, var, static_cast<__nv_bfloat16*>(weights), normPartial, nNorm,
                                    count, hp, betaPow, normSqOut);
     return check_launch("k_adam");
 }
 
 int stats_mean(const float* stats, int rows, float* out, cudaStream_t st) {
-    k_stats_mean<<<1, 256, 0, st>>>(stats, rows, out);
+    MG_LAUNCH(k_stats_mean, 1, 256, 0, st, stats, rows, out);
     return check_launch("k_stats_mean");
 }
 

@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "metalgym/pdl.cuh"
 #include "metalgym/sampling.cuh"
 #include "ptx.cuh"
 
