@@ -279,22 +279,28 @@ def max_over_ranks(x, dist):
 
 def dominant_kernel_roofline(lib, torch, dev, stream):
     """The tcgen05 GEMM with the largest share of the loop's GPU time
-    (profiles/launches_full_loop.md): the up-projection shape of the policy,
-    rows x hidden x embed = 4096 x 512 x 128, ReLU epilogue. Timed alone,
+    (profiles/launches_full_loop*.md): the policy's down-projection with the
+    fused residual add, rows x embed x hidden = 4096 x 128 x 512. Timed alone,
     back to back on the engine's stream with CUDA events."""
-    M, N, K = ENVS_PER_GPU, EMBED * SCALE, EMBED
-    a = torch.randn(M, K, device=f"cuda:{dev}").bfloat16()
-    b = torch.randn(K, N, device=f"cuda:{dev}").bfloat16()
+    M, N, K = ENVS_PER_GPU, EMBED, EMBED * SCALE
+    a = torch.relu(torch.randn(M, K, device=f"cuda:{dev}")).bfloat16()
+    b = (torch.randn(K, N, device=f"cuda:{dev}") / 16).bfloat16()
+    h = torch.randn(M, N, device=f"cuda:{dev}").bfloat16()
     o = torch.empty(M, N, device=f"cuda:{dev}", dtype=torch.bfloat16)
     sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def launch():
+        return lib.mg_gemm_bf16(a.data_ptr(), 0, K, b.data_ptr(), 1, N, M, N, K, 2, o.data_ptr(), N, h.data_ptr(), N,
+                                1, sp)
+
     for _ in range(5):
-        lib.mg_gemm_bf16(a.data_ptr(), 0, K, b.data_ptr(), 1, N, M, N, K, 1, o.data_ptr(), N, None, 0, 1, sp)
+        launch()
     iters = 200
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         s.record(stream)
     for _ in range(iters):
-        lib.mg_gemm_bf16(a.data_ptr(), 0, K, b.data_ptr(), 1, N, M, N, K, 1, o.data_ptr(), N, None, 0, 1, sp)
+        launch()
     with torch.cuda.stream(stream):
         e.record(stream)
     torch.cuda.synchronize()
@@ -302,16 +308,15 @@ def dominant_kernel_roofline(lib, torch, dev, stream):
     flops = 2.0 * M * N * K
     achieved = flops / (us * 1e-6) / 1e12
     _, peak, kind = measured_peaks()
-    traffic = profile_traffic()
-    return {"kernel": "gemm_tc_kernel<128, K-major A, MN-major B, ReLU> (MLP up-projection, 4096x512x128)",
+    return {"kernel": "gemm_tc_kernel<64, K-major A, MN-major B, +residual> (MLP down-projection, 4096x128x512)",
             "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_kind": f"{kind} bf16 burst", "us_per_launch": us, "flop_per_launch": flops,
-            "traffic": traffic}
+            "traffic": profile_traffic()}
 
 
 def profile_traffic():
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "gemm_up_4096x512x128.md"
+    p = ROOT / "profiles" / "gemm_down_4096x128x512.md"
     if p.exists():
         m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
         if m:

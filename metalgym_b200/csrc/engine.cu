@@ -197,7 +197,8 @@ PpoEngine::~PpoEngine() {
     if (trainExec) cudaGraphExecDestroy(trainExec);
     void* ptrs[] = {weights, master, mom, var, grad, obsSlots, actionSlots, logpSlots, valueSlots, rewardSlots,
                     advSlots, retSlots, doneSlots, advStats, dLogits, dStream, dBranch, dV, stats, headPart,
-                    lnFPart, inPart, lsPart, normPartial, normSq, statsMean, schedSlot, schedBetaPow};
+                    lnFPart, inPart, lsPart, normPartial, normSq, normCounter, statsMean, schedSlot,
+                    schedBetaPow};
     for (void* p : ptrs) cudaFree(p);
     for (auto* p : upPart) cudaFree(p);
     for (auto* p : downPart) cudaFree(p);
@@ -413,6 +414,8 @@ int PpoEngine::init() {
     const int nNormAll = std::max(nNorm, grad_scale_norm_blocks((int64_t)optCount));
     MG_TRY(dalloc(&normPartial, (size_t)nNormAll * 4));
     MG_TRY(dalloc(&normSq, 4));
+    MG_TRY(dalloc(&normCounter, 4));
+    MG_CUDA_TRY(cudaMemset(normCounter, 0, 4));
     MG_TRY(dalloc(&statsMean, 8 * 4));
     MG_CUDA_TRY(cudaMemset(normSq, 0, 4));
     MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostStats), 8 * 4));
@@ -578,18 +581,17 @@ int PpoEngine::minibatch(int j, cudaStream_t st) {
     }
     MG_TRY(input_backward(obsSlots, dStream, inPart, R, O, E, st, slot, (int64_t)R * O));
     // gradient sums + norm (model/ppo.h:873-890), [all-reduce], Adam (:891-903)
-    MG_TRY(grad_finalize(gradTable, grad, normPartial, st));
-    int nn = nNorm;
+    // the finalisation's last CTA leaves the squared norm in normSq
+    MG_TRY(grad_finalize(gradTable, grad, normPartial, st, normCounter, normSq));
     if (world > 1) {
         Nccl& nc = nccl();
         ncclResult_t r = nc.allReduce(grad, grad, (size_t)optCount, ncclFloat, ncclSum, static_cast<ncclComm_t>(comm), st);
         if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
-        nn = grad_scale_norm_blocks((int64_t)optCount);
-        MG_TRY(grad_scale_norm(grad, (int64_t)optCount, 1.0f / (float)world, normPartial, st));
+        MG_TRY(grad_scale_norm(grad, (int64_t)optCount, 1.0f / (float)world, normPartial, st, normCounter, normSq));
     }
     const AdamHyper ah{lr, hp.maxGradNorm, 0.0f, 0.0f};
-    return adam(master, grad, mom, var, weights, normPartial, nn, (int64_t)optCount, ah, schedBetaPow + 2 * j, normSq,
-                st);
+    return adam(master, grad, mom, var, weights, normPartial, 0, (int64_t)optCount, ah, schedBetaPow + 2 * j, nullptr,
+                st, normSq);
 }
 
 int PpoEngine::captureCollect() {

@@ -125,6 +125,7 @@ class PpoEngine {
     int nNorm = 0;  // CTAs of the finalize kernel = norm partials
     float* normPartial = nullptr;
     float* normSq = nullptr;
+    unsigned int* normCounter = nullptr;  // last-CTA detection of the norm reduction
     float* statsMean = nullptr;  // 5 floats
     // per-minibatch schedule: slot index and bias-correction powers
     int maxSchedule = 0;

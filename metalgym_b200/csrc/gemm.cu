@@ -58,7 +58,12 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
     MG_CHECK_ARG(!(c.epilogue == kEpiBf16Resid || c.epilogue == kEpiBf16Mask) || (c.aux && c.ldaux % 8 == 0),
                  "gemm: this epilogue needs aux with ldaux a multiple of 8");
     int bn = c.bn;
-    if (bn == 0) bn = c.N >= 128 ? 128 : 64;
+    if (bn == 0) {
+        // 128-wide output tiles, or 64-wide ones when 128-wide tiles would
+        // leave most of the 148 SMs idle (small row counts)
+        const int tiles128 = ((c.M + 127) / 128) * ((c.N + 127) / 128) * c.splits;
+        bn = (c.N >= 128 && tiles128 >= 148) ? 128 : 64;
+    }
     MG_CHECK_ARG(bn == 64 || bn == 128 || bn == 256, "gemm: tile N must be 64, 128 or 256");
 
     int kPerSplit = (c.K + c.splits - 1) / c.splits;

@@ -10,7 +10,7 @@ namespace mg {
 
 namespace {
 
-constexpr int kLnRowsPerCta = 16;       // LayerNorm backward: rows per CTA (8 warps x 2 rows)
+constexpr int kLnRowsPerCta = 8;        // LayerNorm backward: rows per CTA (one row per warp)
 constexpr int kInputRowChunk = 16;      // input backward: rows loaded per unrolled step
 constexpr int64_t kInputPartialBudget = 8 << 20;  // bytes of input-backward partials at most
 constexpr int kGaussRowsPerCta = 256;  // Gaussian loss: rows per CTA
@@ -292,13 +292,24 @@ __global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int3
     }
     const float scale = __fdiv_rn(1.0f, (float)rows);
     const __nv_bfloat16* h = head + (size_t)r * kHeadDim;
+    // exp(logp_j) is needed twice (entropy, gradient): keep up to kCache of them
+    constexpr int kCache = 8;
+    float probCache[kCache];
     float rowMax = -INFINITY;
     for (int j = 0; j < actDim; j++) rowMax = fmaxf(rowMax, bf(h[j]));
     float sum = 0.0f;
     for (int j = 0; j < actDim; j++) sum = __fadd_rn(sum, mg_expf(__fsub_rn(bf(h[j]), rowMax)));
     const float lse = __fadd_rn(rowMax, mg_logf(sum));
     float entropy = 0.0f;
-    for (int j = 0; j < actDim; j++) {
+#pragma unroll
+    for (int j = 0; j < kCache; j++) {
+        if (j < actDim) {
+            const float logp = __fsub_rn(bf(h[j]), lse);
+            probCache[j] = mg_expf(logp);
+            entropy = __fsub_rn(entropy, __fmul_rn(probCache[j], logp));
+        }
+    }
+    for (int j = kCache; j < actDim; j++) {
         const float logp = __fsub_rn(bf(h[j]), lse);
         entropy = __fsub_rn(entropy, __fmul_rn(mg_expf(logp), logp));
     }
@@ -320,7 +331,14 @@ __global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int3
     __nv_bfloat16* pz = reinterpret_cast<__nv_bfloat16*>(packed);
     for (int j = 0; j < actDim; j++) {
         const float logp = __fsub_rn(bf(h[j]), lse);
-        const float prob = mg_expf(logp);
+        float prob;
+        if (j < kCache) {
+#pragma unroll
+            for (int q = 0; q < kCache; q++)
+                if (q == j) prob = probCache[q];
+        } else {
+            prob = mg_expf(logp);
+        }
         const float g = __fadd_rn(__fmul_rn(gLogp, __fsub_rn(j == a ? 1.0f : 0.0f, prob)),
                                   __fmul_rn(__fmul_rn(hp.entropyCoef, prob), __fadd_rn(logp, entropy)));
         pz[j] = tobf(__fmul_rn(g, scale));
@@ -497,26 +515,36 @@ __global__ void __launch_bounds__(1024) k_adv_stats(const float* __restrict__ ad
 // LayerNorm / input / log-std sums stay fp32) and writes one partial sum of
 // squares per CTA for the global norm (model/optimizer.metal:23-34).
 __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ GradSegmentTable tab,
-                                                       float* __restrict__ grad, float* __restrict__ normPartial) {
+                                                       float* __restrict__ grad, float* __restrict__ normPartial,
+                                                       unsigned int* __restrict__ counter,
+                                                       float* __restrict__ normSqOut) {
     mg_pdl_trigger();
     mg_pdl_wait();
     __shared__ float s_red[8];
+    __shared__ bool s_last;
     int b = blockIdx.x, si = 0;
     while (si < tab.n - 1 && b >= tab.seg[si].blockEnd) si++;
     const GradSegment& sg = tab.seg[si];
     const int blockBase = si == 0 ? 0 : tab.seg[si - 1].blockEnd;
-    const int64_t i0 = (int64_t)(b - blockBase) * 1024;
+    const int64_t i = (int64_t)(b - blockBase) * 256 + threadIdx.x;
     float sq = 0.0f;
-    for (int j = 0; j < 4; j++) {
-        const int64_t i = i0 + j * 256 + threadIdx.x;
-        if (i < sg.count) {
-            float acc = 0.0f;
-            const float* src = sg.src + i;
-            for (int p = 0; p < sg.nparts; p++) acc = __fadd_rn(acc, src[(size_t)p * sg.partStride]);
-            if (sg.roundBf16) acc = rbf(acc);
-            grad[sg.dstOffset + i] = acc;
-            sq = __fadd_rn(sq, __fmul_rn(acc, acc));
+    if (i < sg.count) {
+        // sum of the partials in increasing p, with 8 loads in flight at a time
+        const float* src = sg.src + i;
+        const int64_t st = sg.partStride;
+        float acc = 0.0f;
+        int p = 0;
+        for (; p + 8 <= sg.nparts; p += 8) {
+            float v[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) v[q] = src[(int64_t)(p + q) * st];
+#pragma unroll
+            for (int q = 0; q < 8; q++) acc = __fadd_rn(acc, v[q]);
         }
+        for (; p < sg.nparts; p++) acc = __fadd_rn(acc, src[(int64_t)p * st]);
+        if (sg.roundBf16) acc = rbf(acc);
+        grad[sg.dstOffset + i] = acc;
+        sq = __fmul_rn(acc, acc);
     }
     sq = warp_sum(sq);
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = sq;
@@ -525,13 +553,36 @@ __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ G
         float t = 0.0f;
         for (int w = 0; w < 8; w++) t = __fadd_rn(t, s_red[w]);
         normPartial[blockIdx.x] = t;
+        s_last = false;
+        if (counter) {
+            __threadfence();
+            s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+        }
+    }
+    __syncthreads();
+    // the last CTA to finish sums every CTA's partial in index order
+    if (counter && s_last) {
+        __threadfence();
+        float t = 0.0f;
+        for (int k = threadIdx.x; k < (int)gridDim.x; k += 256) t = __fadd_rn(t, __ldcg(&normPartial[k]));
+        t = warp_sum(t);
+        if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = t;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float u = 0.0f;
+            for (int w = 0; w < 8; w++) u = __fadd_rn(u, s_red[w]);
+            *normSqOut = u;
+            *counter = 0u;  // ready for the next launch
+        }
     }
 }
 
 // Sum of squares of grad[0..count) in fixed-size CTA partials (used after a
 // cross-GPU all-reduce, which also rescales the sum to a mean).
 __global__ void __launch_bounds__(256) k_grad_scale_norm(float* __restrict__ grad, int64_t count, float scale,
-                                                         float* __restrict__ normPartial) {
+                                                         float* __restrict__ normPartial,
+                                                         unsigned int* __restrict__ counter,
+                                                         float* __restrict__ normSqOut) {
     mg_pdl_trigger();
     mg_pdl_wait();
     __shared__ float s_red[8];
@@ -548,10 +599,31 @@ __global__ void __launch_bounds__(256) k_grad_scale_norm(float* __restrict__ gra
     sq = warp_sum(sq);
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = sq;
     __syncthreads();
+    __shared__ bool s_last;
     if (threadIdx.x == 0) {
         float t = 0.0f;
         for (int w = 0; w < 8; w++) t = __fadd_rn(t, s_red[w]);
         normPartial[blockIdx.x] = t;
+        s_last = false;
+        if (counter) {
+            __threadfence();
+            s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+        }
+    }
+    __syncthreads();
+    if (counter && s_last) {
+        __threadfence();
+        float t = 0.0f;
+        for (int k = threadIdx.x; k < (int)gridDim.x; k += 256) t = __fadd_rn(t, __ldcg(&normPartial[k]));
+        t = warp_sum(t);
+        if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = t;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float u = 0.0f;
+            for (int w = 0; w < 8; w++) u = __fadd_rn(u, s_red[w]);
+            *normSqOut = u;
+            *counter = 0u;
+        }
     }
 }
 
@@ -563,20 +635,24 @@ __global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const f
                                               __nv_bfloat16* __restrict__ weights,
                                               const float* __restrict__ normPartial, int nNorm, int64_t count,
                                               AdamHyper hp, const float* __restrict__ betaPow,
-                                              float* __restrict__ normSqOut) {
+                                              float* __restrict__ normSqOut, const float* __restrict__ normSqIn) {
     mg_pdl_trigger();
     mg_pdl_wait();
     __shared__ float s_scale;
     if (threadIdx.x < 32) {
         float s = 0.0f;
-        for (int i = threadIdx.x; i < nNorm; i += 32) s = __fadd_rn(s, normPartial[i]);
-        s = warp_sum(s);
+        if (normSqIn) {
+            s = *normSqIn;
+        } else {
+            for (int i = threadIdx.x; i < nNorm; i += 32) s = __fadd_rn(s, normPartial[i]);
+            s = warp_sum(s);
+        }
         if (threadIdx.x == 0) {
             const float norm = __fsqrt_rn(s);
             s_scale = (hp.maxGradNorm > 0.0f && norm > hp.maxGradNorm)
                           ? __fdiv_rn(hp.maxGradNorm, __fadd_rn(norm, 1e-6f))
                           : 1.0f;
-            if (blockIdx.x == 0 && normSqOut) *normSqOut = s;
+            if (blockIdx.x == 0 && normSqOut && !normSqIn) *normSqOut = s;
         }
     }
     __syncthreads();
@@ -772,33 +848,36 @@ int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStrea
 int grad_table_layout(GradSegmentTable& tab) {
     int b = 0;
     for (int i = 0; i < tab.n; i++) {
-        b += (int)((tab.seg[i].count + 1023) / 1024);
+        b += (int)((tab.seg[i].count + 255) / 256);
         tab.seg[i].blockEnd = b;
     }
     return b;
 }
 
-int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st) {
+int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st,
+                  unsigned int* counter, float* normSqOut) {
     MG_CHECK_ARG(tab.n > 0 && tab.n <= kMaxGradSegments, "grad_finalize: bad segment count");
     const int nblocks = tab.seg[tab.n - 1].blockEnd;
     MG_CHECK_ARG(nblocks > 0, "grad_finalize: empty");
-    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, normPartial);
+    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, normPartial, counter, normSqOut);
     return check_launch("k_grad_finalize");
 }
 
 int grad_scale_norm_blocks(int64_t count) { return (int)((count + 1023) / 1024); }
 
-int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st) {
-    MG_LAUNCH(k_grad_scale_norm, grad_scale_norm_blocks(count), 256, 0, st, grad, count, scale, normPartial);
+int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st,
+                    unsigned int* counter, float* normSqOut) {
+    MG_LAUNCH(k_grad_scale_norm, grad_scale_norm_blocks(count), 256, 0, st, grad, count, scale, normPartial, counter,
+              normSqOut);
     return check_launch("k_grad_scale_norm");
 }
 
 int adam(float* param, const float* grad, float* mom, float* var, void* weights, const float* normPartial, int nNorm,
-         int64_t count, AdamHyper hp, const float* betaPow, float* normSqOut, cudaStream_t st) {
-    MG_CHECK_ARG(count > 0 && nNorm > 0, "adam: bad shape");
+         int64_t count, AdamHyper hp, const float* betaPow, float* normSqOut, cudaStream_t st, const float* normSqIn) {
+    MG_CHECK_ARG(count > 0 && (nNorm > 0 || normSqIn), "adam: bad shape");
     const int blocks = (int)std::min<int64_t>((count + 255) / 256, 148 * 8);
     MG_LAUNCH(k_adam, blocks, 256, 0, st, param, grad, mom, var, static_cast<__nv_bfloat16*>(weights), normPartial, nNorm,
-                                   count, hp, betaPow, normSqOut);
+                                   count, hp, betaPow, normSqOut, normSqIn);
     return check_launch("k_adam");
 }
 
@@ -897,7 +976,7 @@ int mg_reduce_partials(const float* partial, int64_t part_stride, int nparts, in
     return mg::grad_finalize(tab, out, norm_partial, MG_STREAM(s));
 }
 
-int mg_reduce_partials_num_norm_partials(int64_t count) { return (int)((count + 1023) / 1024); }
+int mg_reduce_partials_num_norm_partials(int64_t count) { return (int)((count + 255) / 256); }
 
 int mg_adam_step(float* master, const float* grad, float* momentum, float* variance, void* weights,
                  const float* norm_partial, int n_norm_partials, int64_t count, float lr, float beta1_pow,

@@ -69,11 +69,17 @@ int gae(const float* reward, const uint8_t* done, const float* value, const void
 int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStream_t st);
 // Fills blockEnd of every segment; returns the number of CTAs (= norm partials).
 int grad_table_layout(GradSegmentTable& tab);
-int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st);
+// With counter (a zeroed device word) and normSqOut, the last CTA also sums
+// the per-CTA partials into *normSqOut and re-zeroes the counter.
+int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st,
+                  unsigned int* counter = nullptr, float* normSqOut = nullptr);
 int grad_scale_norm_blocks(int64_t count);
-int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st);
+int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st,
+                    unsigned int* counter = nullptr, float* normSqOut = nullptr);
+// normSqIn (optional): the squared gradient norm, instead of summing normPartial.
 int adam(float* param, const float* grad, float* mom, float* var, void* weights, const float* normPartial, int nNorm,
-         int64_t count, AdamHyper hp, const float* betaPow, float* normSqOut, cudaStream_t st);
+         int64_t count, AdamHyper hp, const float* betaPow, float* normSqOut, cudaStream_t st,
+         const float* normSqIn = nullptr);
 int stats_mean(const float* stats, int rows, float* out, cudaStream_t st);
 
 }  // namespace mg

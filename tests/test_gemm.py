@@ -99,3 +99,17 @@ def test_gemm_weight_grad_splitk(mg, shape, splits):
     ref = reference(X.t(), dZ, "f32")
     scale = ref.abs().max().item()
     torch.testing.assert_close(total, ref, rtol=2e-3, atol=1e-3 * scale)
+
+
+def test_gemm_down_projection_single_launch(mg):
+    """One launch of the policy's down-projection with the fused residual add
+    (rows x embed x hidden = 4096 x 128 x 512): the kernel the profiles
+    capture (ncu -k regex:gemm_tc_kernel -c 1 on this test)."""
+    M, N, K = 4096, 128, 512
+    g = torch.Generator(device="cuda").manual_seed(21)
+    V = torch.relu(torch.randn(M, K, device="cuda", generator=g)).bfloat16()
+    Dp = (torch.randn(K, N, device="cuda", generator=g) / 16).bfloat16()
+    h = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    out = run_gemm(mg, V, 0, Dp, 1, M, N, K, "resid", aux=h)
+    ref = reference(V, Dp, "resid", h)
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2 * ref.abs().max().item())
