@@ -1,7 +1,8 @@
 """Benchmark of the MetalGym hot path on B200: env steps/s for the raw env
 step, collect() (policy + env + GAE) and the full PPO loop (collect + train),
-on BASELINE configs 1-3 (CartPole, 4096 envs per GPU, T = 32, residual MLP
-128 -> 512 -> 128 x 2 blocks, 4 epochs, minibatch = one 4096-row slot).
+on the reference README's CartPole configuration (4096 envs per GPU, T = 32,
+residual MLP 128 -> 512 -> 128 x 2 blocks, 4 epochs, minibatch = one 4096-row
+slot).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
 
@@ -278,10 +279,11 @@ def max_over_ranks(x, dist):
 
 
 def dominant_kernel_roofline(lib, torch, dev, stream):
-    """The tcgen05 GEMM with the largest share of the loop's GPU time
-    (profiles/launches_full_loop*.md): the policy's down-projection with the
-    fused residual add, rows x embed x hidden = 4096 x 128 x 512. Timed alone,
-    back to back on the engine's stream with CUDA events."""
+    """The tcgen05 GEMM with the largest share of the loop's GPU time (ncu
+    launch list of one iteration): the policy's down-projection with the fused
+    residual add, rows x embed x hidden = 4096 x 128 x 512. Timed alone, back
+    to back on the engine's stream with CUDA events; the DRAM traffic per
+    launch comes from the committed ncu summary of the same launch."""
     M, N, K = ENVS_PER_GPU, EMBED, EMBED * SCALE
     a = torch.relu(torch.randn(M, K, device=f"cuda:{dev}")).bfloat16()
     b = (torch.randn(K, N, device=f"cuda:{dev}") / 16).bfloat16()
