@@ -191,7 +191,7 @@ def run_mine(args, rank, world, local_rank, dist):
     e2e_s = (time.perf_counter() - t0) / args.steps
     e2e_s = max_over_ranks(e2e_s, dist)
     e2e = {"value": steps_per_iter * world / e2e_s, "unit": "env steps/s",
-           "h2d_bytes_per_step": EPOCHS * HORIZON * 12, "d2h_bytes_per_step": done_host.nbytes + 24 + 4 * 3,
+           "h2d_bytes_per_step": EPOCHS * HORIZON * 32, "d2h_bytes_per_step": done_host.nbytes + 24 + 4 * 3,
            "api": "mg_ppo_collect + mg_ppo_train(4) + mg_ppo_last_stats + done-slot download"}
 
     legs = {}
@@ -259,8 +259,9 @@ def run_mine(args, rank, world, local_rank, dist):
                        "env_steps_per_step": steps_per_iter * world,
                        "flop_per_env_step": (HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd)},
             "legs": legs, "e2e": e2e, "roofline": roof,
-            "gpu_launches": args.steps * (collect_k + train_k),
-            "gpu_launches_per_step": {"collect_graph": collect_k, "train_graph": train_k},
+            "gpu_launches": args.steps * (collect_k + EPOCHS * train_k),
+            "gpu_launches_per_step": {"collect_graph": collect_k, "train_graph_per_epoch": train_k,
+                                      "epochs": EPOCHS},
             "clocks": clk.summary(),
         }
     if comm is not None:

@@ -15,7 +15,10 @@
 // caller's RNG, exactly as model/ppo.h:636-702. Slot accessors and
 // headValue() read pinned host mirrors refreshed after device work (see
 // gym.h). Extensions: no compile-time N_EMBED_CFG (embed 64/128/256/512),
-// setComm() for data parallelism over NCCL.
+// setComm() for data parallelism over NCCL, and the field minibatchRows
+// (0, the default, keeps the reference's one-slot minibatches; B > 0 trains
+// on B rollout rows per minibatch, every row once per epoch in a random
+// order).
 #pragma once
 
 #include <cmath>
@@ -64,6 +67,7 @@ struct PPOModel {
     float maxGradNorm = 0.5f;  // 0 disables clipping
     float gamma = 0.99f;
     float lambda = 0.95f;
+    uint32_t minibatchRows = 0;  // extension: 0 = one time slot per minibatch
 
     PPOModel(Gym<Env>& g, int e, int s, int layers, float learningRate, int T = 32, uint32_t seed = 0)
         : gym(g), parallels(g.parallels), horizon((uint32_t)T), embedDim((uint32_t)e), mlpScale((uint32_t)s),
@@ -230,6 +234,7 @@ struct PPOModel {
     void pushHyper() {
         metalgym::check_or_exit(mg_ppo_set_hyper(handle, clip, valueCoef, entropyCoef, maxGradNorm, gamma, lambda),
                                 "hyperparameters");
+        metalgym::check_or_exit(mg_ppo_set_minibatch_rows(handle, (int)minibatchRows), "minibatchRows");
     }
     void afterDeviceWork(int headSource) {
         for (bool& s : stale_) s = true;

@@ -276,6 +276,22 @@ int mg_ppo_collect(mg_ppo_t model);
 int mg_ppo_train(mg_ppo_t model, int epochs);
 /* trainSlot(t) (model/ppo.h:906-916); blocks until done. */
 int mg_ppo_train_slot(mg_ppo_t model, int t);
+/* Rows per training minibatch (no counterpart in the reference, whose
+ * minibatch is always one time slot, model/ppo.h:906-923). 0 (the default)
+ * keeps the reference's slot minibatches; B > 0 makes every epoch of
+ * train() visit the horizon x parallels rollout rows once, in a keyed random
+ * order (a 4-round Feistel permutation, include/metalgym/rowmap.h), B rows
+ * per minibatch, each minibatch normalising advantages over its own rows.
+ * B must divide horizon x parallels. */
+int mg_ppo_set_minibatch_rows(mg_ppo_t model, int rows);
+int mg_ppo_minibatch_rows(mg_ppo_t model, int* out);
+/* One row-mode minibatch over rollout rows perm(base .. base + B - 1) of the
+ * permutation keyed by key[4], with an Adam step; blocks (the manual path
+ * of row mode, as mg_ppo_train_slot is of slot mode). */
+int mg_ppo_train_rows(mg_ppo_t model, const uint32_t key[4], uint32_t base);
+/* Host evaluation of that permutation: out[q] = flat slot-major rollout row
+ * (t * parallels + env) read by minibatch row q, q < rows. */
+int mg_minibatch_rows(const uint32_t key[4], uint32_t base, uint32_t rows, uint64_t total, uint64_t* out);
 /* forward() on the gym's live obs (model/ppo.h:628-634); blocks. */
 int mg_ppo_forward(mg_ppo_t model);
 /* lastStats() (model/ppo.h:925-943): policy, value, entropy, approxKl,

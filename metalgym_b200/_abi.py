@@ -66,6 +66,10 @@ SIGNATURES = {
     "mg_ppo_collect": (I, [P]),
     "mg_ppo_train": (I, [P, I]),
     "mg_ppo_train_slot": (I, [P, I]),
+    "mg_ppo_set_minibatch_rows": (I, [P, I]),
+    "mg_ppo_minibatch_rows": (I, [P, PI]),
+    "mg_ppo_train_rows": (I, [P, P, U]),
+    "mg_minibatch_rows": (I, [P, U, U, U64, P]),
     "mg_ppo_forward": (I, [P]),
     "mg_ppo_last_stats": (I, [P, P]),
     "mg_ppo_set_hyper": (I, [P, F, F, F, F, F, F]),

@@ -57,9 +57,9 @@ int ppo_buffer(PpoEngine* e, int which, int slot, void** p, size_t* bytes) {
         case MG_PPO_MOMENTUM: *p = e->mom; *bytes = e->optCount * 4; return MG_OK;
         case MG_PPO_VARIANCE: *p = e->var; *bytes = e->optCount * 4; return MG_OK;
         case MG_PPO_GRAD: *p = e->grad; *bytes = e->optCount * 4; return MG_OK;
-        case MG_PPO_STATS: *p = e->stats; *bytes = R * 5 * 4; return MG_OK;
+        case MG_PPO_STATS: *p = e->stats; *bytes = (size_t)e->trainBufRows * 5 * 4; return MG_OK;
         case MG_PPO_ADV_STATS: *p = e->advStats; *bytes = T * 2 * 4; return MG_OK;
-        case MG_PPO_TRAIN_HEAD: *p = e->trainActs.head; *bytes = R * 64 * 2; return MG_OK;
+        case MG_PPO_TRAIN_HEAD: *p = e->trainActs.head; *bytes = (size_t)e->trainBufRows * 64 * 2; return MG_OK;
     }
     return mg::fail(MG_ERR_ARGUMENT, "unknown model buffer id");
 }
@@ -233,6 +233,28 @@ int mg_ppo_train(mg_ppo_t model, int epochs) {
 }
 int mg_ppo_train_slot(mg_ppo_t model, int t) {
     return model ? P(model)->trainSlot(t) : mg::fail(MG_ERR_ARGUMENT, "null model");
+}
+int mg_ppo_set_minibatch_rows(mg_ppo_t model, int rows) {
+    return model ? P(model)->setMinibatchRows(rows) : mg::fail(MG_ERR_ARGUMENT, "null model");
+}
+int mg_ppo_minibatch_rows(mg_ppo_t model, int* out) {
+    MG_CHECK_ARG(model && out, "mg_ppo_minibatch_rows: null argument");
+    *out = P(model)->mbRows;
+    return MG_OK;
+}
+int mg_ppo_train_rows(mg_ppo_t model, const uint32_t key[4], uint32_t base) {
+    MG_CHECK_ARG(model && key, "mg_ppo_train_rows: null argument");
+    return P(model)->trainRows(key, base);
+}
+int mg_minibatch_rows(const uint32_t key[4], uint32_t base, uint32_t rows, uint64_t total, uint64_t* out) {
+    MG_CHECK_ARG(key && out, "mg_minibatch_rows: null argument");
+    MG_CHECK_ARG(total > 0 && (uint64_t)base + rows <= total, "mg_minibatch_rows: base + rows exceeds total");
+    MgMinibatch m{};
+    for (int i = 0; i < 4; i++) m.key[i] = key[i];
+    m.base = base;
+    m.slot = -1;
+    for (uint32_t q = 0; q < rows; q++) out[q] = mg_minibatch_row(m, q, 0, total);
+    return MG_OK;
 }
 int mg_ppo_forward(mg_ppo_t model) { return model ? P(model)->forward() : mg::fail(MG_ERR_ARGUMENT, "null model"); }
 int mg_ppo_last_stats(mg_ppo_t model, float out6[6]) {

@@ -4,8 +4,9 @@
 //   collect()  model/ppo.h:716-751  one CUDA graph: T x (forward, fused
 //              sample + env step) + bootstrap forward + GAE + per-slot
 //              advantage statistics
-//   train(e)   model/ppo.h:918-923  one CUDA graph for all e x T minibatches;
-//              the host shuffles the slot order with the seeded mt19937 and
+//   train(e)   model/ppo.h:918-923  one CUDA graph per epoch, replayed e
+//              times; the host shuffles the slot order with the seeded
+//              mt19937 (or draws the epoch's row-permutation key) and
 //              computes the Adam bias-correction powers (model/ppo.h:873-880),
 //              the graph reads them from device memory per minibatch
 //   minibatch  model/ppo.h:906-916  forward (activations saved), loss,
@@ -106,6 +107,48 @@ size_t count_kernel_nodes(cudaGraph_t g) {
     return k;
 }
 
+int alloc_acts(ActSet& a, int rows, int E, int H, int L, bool shared) {
+    MG_TRY(dalloc(&a.h, (size_t)rows * E * 2));
+    MG_TRY(dalloc(&a.fXn, (size_t)rows * E * 2));
+    MG_TRY(dalloc(&a.fOut, (size_t)rows * E * 2));
+    MG_TRY(dalloc(&a.fSd, (size_t)rows * 4));
+    MG_TRY(dalloc(&a.head, (size_t)rows * kHead * 2));
+    a.lnXn.assign(L, nullptr);
+    a.lnOut.assign(L, nullptr);
+    a.lnSd.assign(L, nullptr);
+    a.v.assign(L, nullptr);
+    for (int n = 0; n < L; n++) {
+        if (shared && n > 0) {
+            a.lnXn[n] = a.lnXn[0];
+            a.lnOut[n] = a.lnOut[0];
+            a.lnSd[n] = a.lnSd[0];
+            a.v[n] = a.v[0];
+            continue;
+        }
+        MG_TRY(dalloc(&a.lnXn[n], (size_t)rows * E * 2));
+        MG_TRY(dalloc(&a.lnOut[n], (size_t)rows * E * 2));
+        MG_TRY(dalloc(&a.lnSd[n], (size_t)rows * 4));
+        MG_TRY(dalloc(&a.v[n], (size_t)rows * H * 2));
+    }
+    return MG_OK;
+}
+
+void free_acts(ActSet& a, bool shared) {
+    cudaFree(a.h);
+    cudaFree(a.fXn);
+    cudaFree(a.fOut);
+    cudaFree(a.fSd);
+    cudaFree(a.head);
+    const size_t n = shared ? std::min<size_t>(1, a.v.size()) : a.v.size();
+    for (size_t i = 0; i < n; i++) {
+        cudaFree(a.lnXn[i]);
+        cudaFree(a.lnOut[i]);
+        cudaFree(a.lnSd[i]);
+        cudaFree(a.v[i]);
+    }
+    a = ActSet{};
+}
+
 int splits_for(int M, int N, int K, int bn) {
     const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
     int s = (256 + tiles - 1) / tiles;
@@ -195,31 +238,13 @@ PpoEngine::~PpoEngine() {
     cudaStreamSynchronize(gym->stream);
     if (collectExec) cudaGraphExecDestroy(collectExec);
     if (trainExec) cudaGraphExecDestroy(trainExec);
+    freeTrain();
+    free_acts(collectActs, true);
     void* ptrs[] = {weights, master, mom, var, grad, obsSlots, actionSlots, logpSlots, valueSlots, rewardSlots,
-                    advSlots, retSlots, doneSlots, advStats, dLogits, dStream, dBranch, dV, stats, headPart,
-                    lnFPart, inPart, lsPart, normPartial, normSq, normCounter, statsMean, schedSlot,
+                    advSlots, retSlots, doneSlots, advStats, mbAdvStats, normSq, normCounter, statsMean, sched,
                     schedBetaPow};
     for (void* p : ptrs) cudaFree(p);
-    for (auto* p : upPart) cudaFree(p);
-    for (auto* p : downPart) cudaFree(p);
-    for (auto* p : lnPart) cudaFree(p);
-    auto freeActs = [](ActSet& a, bool shared) {
-        cudaFree(a.h);
-        cudaFree(a.fXn);
-        cudaFree(a.fOut);
-        cudaFree(a.fSd);
-        cudaFree(a.head);
-        const size_t n = shared ? 1 : a.v.size();
-        for (size_t i = 0; i < n && i < a.v.size(); i++) {
-            cudaFree(a.lnXn[i]);
-            cudaFree(a.lnOut[i]);
-            cudaFree(a.lnSd[i]);
-            cudaFree(a.v[i]);
-        }
-    };
-    freeActs(trainActs, false);
-    freeActs(collectActs, true);
-    cudaFreeHost(hostSchedSlot);
+    cudaFreeHost(hostSched);
     cudaFreeHost(hostSchedBetaPow);
     cudaFreeHost(hostStats);
     cudaSetDevice(cur);
@@ -326,58 +351,55 @@ int PpoEngine::init() {
     MG_TRY(dalloc(&advSlots, slotCount * 4));
     MG_TRY(dalloc(&retSlots, slotCount * 4));
     MG_TRY(dalloc(&advStats, (size_t)T * 2 * 4));
+    MG_TRY(dalloc(&mbAdvStats, 2 * 4));
     MG_CUDA_TRY(cudaMemset(actionSlots, 0, slotCount * actBytes));
     MG_CUDA_TRY(cudaMemset(obsSlots, 0, (size_t)(T + 1) * R * O * 4));
     slotOrder.resize(T);
     for (int t = 0; t < T; t++) slotOrder[t] = (uint32_t)t;
     hostRng.seed(seed);
 
-    // ---- activations: train keeps every block's, collect shares one set
-    auto allocActs = [&](ActSet& a, int rows, bool shared) -> int {
-        MG_TRY(dalloc(&a.h, (size_t)rows * E * 2));
-        MG_TRY(dalloc(&a.fXn, (size_t)rows * E * 2));
-        MG_TRY(dalloc(&a.fOut, (size_t)rows * E * 2));
-        MG_TRY(dalloc(&a.fSd, (size_t)rows * 4));
-        MG_TRY(dalloc(&a.head, (size_t)rows * kHead * 2));
-        a.lnXn.resize(L);
-        a.lnOut.resize(L);
-        a.lnSd.resize(L);
-        a.v.resize(L);
-        for (int n = 0; n < L; n++) {
-            if (shared && n > 0) {
-                a.lnXn[n] = a.lnXn[0];
-                a.lnOut[n] = a.lnOut[0];
-                a.lnSd[n] = a.lnSd[0];
-                a.v[n] = a.v[0];
-                continue;
-            }
-            MG_TRY(dalloc(&a.lnXn[n], (size_t)rows * E * 2));
-            MG_TRY(dalloc(&a.lnOut[n], (size_t)rows * E * 2));
-            MG_TRY(dalloc(&a.lnSd[n], (size_t)rows * 4));
-            MG_TRY(dalloc(&a.v[n], (size_t)rows * H * 2));
-        }
-        return MG_OK;
-    };
-    MG_TRY(allocActs(trainActs, R, false));
-    MG_TRY(allocActs(collectActs, R, true));
+    // ---- activations: collect shares one set across blocks; the training
+    // buffers (every block's activations, partials) follow the minibatch rows
+    MG_TRY(alloc_acts(collectActs, R, E, H, L, true));
     MG_CUDA_TRY(cudaMemset(collectActs.head, 0, (size_t)R * kHead * 2));
-    MG_TRY(dalloc(&dLogits, (size_t)R * kHead * 2));
-    MG_TRY(dalloc(&dStream, (size_t)R * E * 2));
-    MG_TRY(dalloc(&dBranch, (size_t)R * E * 2));
-    MG_TRY(dalloc(&dV, (size_t)R * H * 2));
-    MG_TRY(dalloc(&stats, (size_t)R * 5 * 4));
-    MG_CUDA_TRY(cudaMemset(stats, 0, (size_t)R * 5 * 4));
+    MG_TRY(allocTrain(R));
+    MG_TRY(dalloc(&normSq, 4));
+    MG_TRY(dalloc(&normCounter, 4));
+    MG_CUDA_TRY(cudaMemset(normCounter, 0, 4));
+    MG_TRY(dalloc(&statsMean, 8 * 4));
+    MG_CUDA_TRY(cudaMemset(normSq, 0, 4));
+    MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostStats), 8 * 4));
+    MG_TRY(ensureSchedule(T, 4 * T));
+    MG_CUDA_TRY(cudaStreamSynchronize(st));
+    return MG_OK;
+}
 
-    // ---- gradient partials and the finalisation table
-    upSplits = splits_for(E, H, R, H >= 128 ? 128 : 64);
-    downSplits = splits_for(H, E, R, E >= 128 ? 128 : 64);
-    headSplits = splits_for(E, kHead, R, 64);
-    upPart.resize(L);
-    downPart.resize(L);
-    lnPart.resize(L);
-    const int pLn = layernorm_backward_parts(R);
-    const int pIn = input_backward_parts(R, O, E);
-    const int pGs = gaussian_loss_parts(R);
+// Training buffers for minibatches of `rows` rows: every block's saved
+// activations, the backward temporaries, per-row statistics, the gradient
+// partials and the finalisation table (split counts follow the row count).
+int PpoEngine::allocTrain(int rows) {
+    MG_CUDA_TRY(cudaStreamSynchronize(gym->stream));
+    freeTrain();
+    if (trainExec) {  // a captured graph holds the old pointers
+        cudaGraphExecDestroy(trainExec);
+        trainExec = nullptr;
+    }
+    MG_TRY(alloc_acts(trainActs, rows, E, H, L, false));
+    MG_TRY(dalloc(&dLogits, (size_t)rows * kHead * 2));
+    MG_TRY(dalloc(&dStream, (size_t)rows * E * 2));
+    MG_TRY(dalloc(&dBranch, (size_t)rows * E * 2));
+    MG_TRY(dalloc(&dV, (size_t)rows * H * 2));
+    MG_TRY(dalloc(&stats, (size_t)rows * 5 * 4));
+    MG_CUDA_TRY(cudaMemset(stats, 0, (size_t)rows * 5 * 4));
+    upSplits = splits_for(E, H, rows, H >= 128 ? 128 : 64);
+    downSplits = splits_for(H, E, rows, E >= 128 ? 128 : 64);
+    headSplits = splits_for(E, kHead, rows, 64);
+    upPart.assign(L, nullptr);
+    downPart.assign(L, nullptr);
+    lnPart.assign(L, nullptr);
+    const int pLn = layernorm_backward_parts(rows);
+    const int pIn = input_backward_parts(rows, O, E);
+    const int pGs = gaussian_loss_parts(rows);
     for (int n = 0; n < L; n++) {
         MG_TRY(dalloc(&upPart[n], (size_t)upSplits * E * H * 4));
         MG_TRY(dalloc(&downPart[n], (size_t)downSplits * H * E * 4));
@@ -388,7 +410,7 @@ int PpoEngine::init() {
     MG_TRY(dalloc(&inPart, (size_t)pIn * (O + 1) * E * 4));
     MG_TRY(dalloc(&lsPart, (size_t)pGs * (A > 0 ? A : 1) * 4));
     GradSegmentTable& tb = gradTable;
-    tb.n = 0;
+    tb = GradSegmentTable{};
     auto seg = [&](const float* src, int64_t stride, int nparts, int64_t count, uint32_t p, int round) {
         GradSegment& s = tb.seg[tb.n++];
         s.src = src;
@@ -413,33 +435,57 @@ int PpoEngine::init() {
     nNorm = grad_table_layout(tb);
     const int nNormAll = std::max(nNorm, grad_scale_norm_blocks((int64_t)optCount));
     MG_TRY(dalloc(&normPartial, (size_t)nNormAll * 4));
-    MG_TRY(dalloc(&normSq, 4));
-    MG_TRY(dalloc(&normCounter, 4));
-    MG_CUDA_TRY(cudaMemset(normCounter, 0, 4));
-    MG_TRY(dalloc(&statsMean, 8 * 4));
-    MG_CUDA_TRY(cudaMemset(normSq, 0, 4));
-    MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostStats), 8 * 4));
-    MG_TRY(ensureSchedule(4 * T));
-    MG_CUDA_TRY(cudaStreamSynchronize(st));
+    trainBufRows = rows;
     return MG_OK;
 }
 
-int PpoEngine::ensureSchedule(int n) {
-    if (n <= maxSchedule) return MG_OK;
-    cudaStreamSynchronize(gym->stream);
-    cudaFree(schedSlot);
-    cudaFree(schedBetaPow);
-    cudaFreeHost(hostSchedSlot);
-    cudaFreeHost(hostSchedBetaPow);
-    MG_TRY(dalloc(&schedSlot, (size_t)n * 4));
-    MG_TRY(dalloc(&schedBetaPow, (size_t)n * 2 * 4));
-    MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostSchedSlot), (size_t)n * 4));
-    MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostSchedBetaPow), (size_t)n * 2 * 4));
-    maxSchedule = n;
-    // a captured graph holds the old pointers
-    if (trainExec) {
-        cudaGraphExecDestroy(trainExec);
-        trainExec = nullptr;
+void PpoEngine::freeTrain() {
+    free_acts(trainActs, false);
+    float** fs[] = {&stats, &headPart, &lnFPart, &inPart, &lsPart, &normPartial};
+    for (float** p : fs) {
+        cudaFree(*p);
+        *p = nullptr;
+    }
+    void** vs[] = {&dLogits, &dStream, &dBranch, &dV};
+    for (void** p : vs) {
+        cudaFree(*p);
+        *p = nullptr;
+    }
+    for (auto* p : upPart) cudaFree(p);
+    for (auto* p : downPart) cudaFree(p);
+    for (auto* p : lnPart) cudaFree(p);
+    upPart.clear();
+    downPart.clear();
+    lnPart.clear();
+    trainBufRows = 0;
+}
+
+// Device schedule of `device` minibatches (one epoch) and its pinned host
+// staging of `host` minibatches (all epochs of a train call).
+int PpoEngine::ensureSchedule(int device, int host) {
+    if (host > maxHostSchedule) {
+        cudaStreamSynchronize(gym->stream);
+        cudaFreeHost(hostSched);
+        cudaFreeHost(hostSchedBetaPow);
+        hostSched = nullptr;
+        hostSchedBetaPow = nullptr;
+        MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostSched), (size_t)host * sizeof(MgMinibatch)));
+        MG_CUDA_TRY(cudaMallocHost(reinterpret_cast<void**>(&hostSchedBetaPow), (size_t)host * 2 * 4));
+        maxHostSchedule = host;
+    }
+    if (device > maxSchedule) {
+        cudaStreamSynchronize(gym->stream);
+        cudaFree(sched);
+        cudaFree(schedBetaPow);
+        sched = nullptr;
+        schedBetaPow = nullptr;
+        MG_TRY(dalloc(&sched, (size_t)device * sizeof(MgMinibatch)));
+        MG_TRY(dalloc(&schedBetaPow, (size_t)device * 2 * 4));
+        maxSchedule = device;
+        if (trainExec) {  // a captured graph holds the old pointers
+            cudaGraphExecDestroy(trainExec);
+            trainExec = nullptr;
+        }
     }
     return MG_OK;
 }
@@ -488,98 +534,106 @@ int PpoEngine::forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st)
     return gemm_bf16(hd, st);
 }
 
-// One minibatch = one slot (model/ppo.h:906-916); the slot index and the
-// Adam bias-correction powers are read from the device schedule at j.
-int PpoEngine::minibatch(int j, cudaStream_t st) {
-    const int* slot = schedSlot + j;
+// One minibatch (model/ppo.h:906-916): one time slot, or in row mode B
+// permuted rollout rows; which rows, and the Adam bias-correction powers,
+// are read from the device schedule at j.
+int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
+    const int rows = trainBufRows;
+    const RowMap rm{sched + j, (uint64_t)R, (uint64_t)T * R};
     ActSet& a = trainActs;
     auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
-    // forward with activations saved (input reads obs slot `slot`)
-    MG_TRY(input_forward(obsSlots, w(pInW), w(pInB), a.h, R, O, E, st, slot, (int64_t)R * O));
+    // forward with activations saved (the input gathers the minibatch's obs rows)
+    MG_TRY(input_forward(obsSlots, w(pInW), w(pInB), a.h, rows, O, E, st, rm));
     for (int n = 0; n < L; n++) {
-        MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], R, E, st));
+        MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
         GemmCall up;
         up.A = a.lnOut[n]; up.lda = E;
         up.B = w(pUp[n]); up.b_mn = true; up.ldb = H;
-        up.M = R; up.N = H; up.K = E;
+        up.M = rows; up.N = H; up.K = E;
         up.epilogue = 1;
         up.out = a.v[n]; up.ldo = H;
         MG_TRY(gemm_bf16(up, st));
         GemmCall down;
         down.A = a.v[n]; down.lda = H;
         down.B = w(pDown[n]); down.b_mn = true; down.ldb = E;
-        down.M = R; down.N = E; down.K = H;
+        down.M = rows; down.N = E; down.K = H;
         down.epilogue = 2;
         down.aux = a.h; down.ldaux = E;
         down.out = a.h; down.ldo = E;
         MG_TRY(gemm_bf16(down, st));
     }
-    MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, R, E, st));
+    MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, rows, E, st));
     {
         GemmCall hd;
         hd.A = a.fOut; hd.lda = E;
         hd.B = w(pHead); hd.b_mn = true; hd.ldb = kHead;
-        hd.M = R; hd.N = kHead; hd.K = E;
+        hd.M = rows; hd.N = kHead; hd.K = E;
         hd.out = a.head; hd.ldo = kHead;
         MG_TRY(gemm_bf16(hd, st));
     }
-    // loss (model/ppo.h:753-781): per-slot advantage statistics from collect()
+    // loss (model/ppo.h:753-781): per-slot advantage statistics from
+    // collect(), or in row mode the statistics of this minibatch's rows
     const LossHyper lh{hp.clip, hp.valueCoef, hp.entropyCoef};
+    const float* as = advStats;
+    if (rowMode) {
+        MG_TRY(advantage_stats_rows(advSlots, rm, rows, mbAdvStats, st));
+        as = mbAdvStats;
+    }
     if (cont)
-        MG_TRY(gaussian_loss(a.head, static_cast<const float*>(actionSlots), advSlots, advStats, retSlots, logpSlots,
-                             dLogits, stats, w(pLogStd), lsPart, R, A, lh, st, slot));
+        MG_TRY(gaussian_loss(a.head, static_cast<const float*>(actionSlots), advSlots, as, retSlots, logpSlots,
+                             dLogits, stats, w(pLogStd), lsPart, rows, A, lh, st, rm));
     else
-        MG_TRY(policy_loss(a.head, static_cast<const int32_t*>(actionSlots), advSlots, advStats, retSlots, logpSlots,
-                           dLogits, stats, R, A, lh, st, slot));
+        MG_TRY(policy_loss(a.head, static_cast<const int32_t*>(actionSlots), advSlots, as, retSlots, logpSlots,
+                           dLogits, stats, rows, A, lh, st, rm));
     // backward (model/ppo.h:793-865)
     {
         GemmCall dx;  // dStream = dLogits W_head^T (model/linear.metal:40-60)
         dx.A = dLogits; dx.lda = kHead;
         dx.B = w(pHead); dx.ldb = kHead;  // [E][64] = [N][K], K-major
-        dx.M = R; dx.N = E; dx.K = kHead;
+        dx.M = rows; dx.N = E; dx.K = kHead;
         dx.out = dStream; dx.ldo = E;
         MG_TRY(gemm_bf16(dx, st));
         GemmCall dw;  // dW_head = X_F^T dLogits (model/linear.metal:71-93)
         dw.A = a.fOut; dw.a_mn = true; dw.lda = E;
         dw.B = dLogits; dw.b_mn = true; dw.ldb = kHead;
-        dw.M = E; dw.N = kHead; dw.K = R;
+        dw.M = E; dw.N = kHead; dw.K = rows;
         dw.epilogue = 4; dw.splits = headSplits;
         dw.out = headPart; dw.ldo = kHead;
         MG_TRY(gemm_bf16(dw, st));
     }
-    MG_TRY(layernorm_backward(dStream, a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, R, E, st));
+    MG_TRY(layernorm_backward(dStream, a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, rows, E, st));
     for (int n = L - 1; n >= 0; n--) {
         GemmCall g1;  // dV = bf16(dStream Dp^T) * (V > 0) (model/mlp.metal:88-127)
         g1.A = dStream; g1.lda = E;
         g1.B = w(pDown[n]); g1.ldb = E;  // Dp [H][E] = [N][K]
-        g1.M = R; g1.N = H; g1.K = E;
+        g1.M = rows; g1.N = H; g1.K = E;
         g1.epilogue = 3; g1.aux = a.v[n]; g1.ldaux = H;
         g1.out = dV; g1.ldo = H;
         MG_TRY(gemm_bf16(g1, st));
         GemmCall g2;  // dUp = X^T dV (model/mlp.metal:167-208)
         g2.A = a.lnOut[n]; g2.a_mn = true; g2.lda = E;
         g2.B = dV; g2.b_mn = true; g2.ldb = H;
-        g2.M = E; g2.N = H; g2.K = R;
+        g2.M = E; g2.N = H; g2.K = rows;
         g2.epilogue = 4; g2.splits = upSplits;
         g2.out = upPart[n]; g2.ldo = H;
         MG_TRY(gemm_bf16(g2, st));
         GemmCall g3;  // dDp = V^T dStream
         g3.A = a.v[n]; g3.a_mn = true; g3.lda = H;
         g3.B = dStream; g3.b_mn = true; g3.ldb = E;
-        g3.M = H; g3.N = E; g3.K = R;
+        g3.M = H; g3.N = E; g3.K = rows;
         g3.epilogue = 4; g3.splits = downSplits;
         g3.out = downPart[n]; g3.ldo = E;
         MG_TRY(gemm_bf16(g3, st));
         GemmCall g4;  // dBranch = dV Up^T (model/mlp.metal:131-153)
         g4.A = dV; g4.lda = H;
         g4.B = w(pUp[n]); g4.ldb = H;  // Up [E][H] = [N][K]
-        g4.M = R; g4.N = E; g4.K = H;
+        g4.M = rows; g4.N = E; g4.K = H;
         g4.out = dBranch; g4.ldo = E;
         MG_TRY(gemm_bf16(g4, st));
         // LayerNorm backward, then dStream += dBranch (model/ppo.h:851-852)
-        MG_TRY(layernorm_backward(dBranch, a.lnXn[n], w(pLnG[n]), a.lnSd[n], dStream, lnPart[n], R, E, st));
+        MG_TRY(layernorm_backward(dBranch, a.lnXn[n], w(pLnG[n]), a.lnSd[n], dStream, lnPart[n], rows, E, st));
     }
-    MG_TRY(input_backward(obsSlots, dStream, inPart, R, O, E, st, slot, (int64_t)R * O));
+    MG_TRY(input_backward(obsSlots, dStream, inPart, rows, O, E, st, rm));
     // gradient sums + norm (model/ppo.h:873-890), [all-reduce], Adam (:891-903)
     // the finalisation's last CTA leaves the squared norm in normSq
     MG_TRY(grad_finalize(gradTable, grad, normPartial, st, normCounter, normSq));
@@ -632,11 +686,11 @@ int PpoEngine::captureCollect() {
     return MG_OK;
 }
 
-int PpoEngine::captureTrain(int minibatches) {
+int PpoEngine::captureTrain(int minibatches, bool rowMode) {
     cudaStream_t st = gym->stream;
     MG_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
     int rc = MG_OK;
-    for (int j = 0; j < minibatches && !rc; j++) rc = minibatch(j, st);
+    for (int j = 0; j < minibatches && !rc; j++) rc = minibatch(j, rowMode, st);
     cudaGraph_t graph = nullptr;
     cudaError_t e = cudaStreamEndCapture(st, &graph);
     if (rc) {
@@ -652,6 +706,7 @@ int PpoEngine::captureTrain(int minibatches) {
     if (trainExec) cudaGraphExecDestroy(trainExec);
     trainExec = exec;
     trainExecMinibatches = minibatches;
+    trainExecRowMode = rowMode;
     trainHp = hp;
     return MG_OK;
 }
@@ -674,13 +729,40 @@ int PpoEngine::collect() {
     return checkStatus("collect");
 }
 
-// Fills the device schedule for n minibatches: slot order (model/ppo.h:918-923)
-// and the host beta powers of each Adam step (model/ppo.h:874-880).
-static void schedule_step(PpoEngine& e, int k, uint32_t slot) {
+// Host schedule entry k: the minibatch's rows (a slot, model/ppo.h:918-923,
+// or a row-permutation key and base) and the beta powers of its Adam step
+// (model/ppo.h:874-880).
+static void schedule_step(PpoEngine& e, int k, const MgMinibatch& mb) {
     e.stepCounter += 1.0f;
-    e.hostSchedSlot[k] = (int)slot;
+    e.hostSched[k] = mb;
     e.hostSchedBetaPow[2 * k] = std::pow(0.9f, e.stepCounter);
     e.hostSchedBetaPow[2 * k + 1] = std::pow(0.999f, e.stepCounter);
+}
+
+static MgMinibatch slot_minibatch(uint32_t t) {
+    MgMinibatch m{};
+    m.slot = (int32_t)t;
+    return m;
+}
+
+static MgMinibatch row_minibatch(const uint32_t key[4], uint32_t base) {
+    MgMinibatch m{};
+    for (int i = 0; i < 4; i++) m.key[i] = key[i];
+    m.base = base;
+    m.slot = -1;
+    return m;
+}
+
+int PpoEngine::setMinibatchRows(int rows) {
+    MG_CHECK_ARG(rows >= 0, "minibatchRows must be >= 0");
+    if (rows > 0) {
+        const int64_t total = (int64_t)T * R;
+        MG_CHECK_ARG(rows <= total && total % rows == 0,
+                     "minibatchRows must divide horizon x parallels (" + std::to_string(total) + ")");
+        MG_CHECK_ARG(total < (int64_t)1 << 31, "row-mode minibatches need horizon x parallels < 2^31");
+    }
+    mbRows = rows;
+    return MG_OK;
 }
 
 int PpoEngine::train(int epochs) {
@@ -688,17 +770,32 @@ int PpoEngine::train(int epochs) {
     if (epochs == 0) return MG_OK;
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
-    const int n = epochs * T;
-    MG_TRY(ensureSchedule(n));
+    const bool rowMode = mbRows > 0;
+    const int rows = rowMode ? mbRows : R;
+    if (trainBufRows != rows) MG_TRY(allocTrain(rows));
+    const int nmb = rowMode ? (int)((int64_t)T * R / mbRows) : T;
+    MG_TRY(ensureSchedule(nmb, epochs * nmb));
     int k = 0;
     for (int e = 0; e < epochs; e++) {
-        std::shuffle(slotOrder.begin(), slotOrder.end(), hostRng);
-        for (uint32_t t : slotOrder) schedule_step(*this, k++, t);
+        if (rowMode) {
+            // every epoch visits the T x R rows once, in a new keyed order
+            uint32_t key[4];
+            for (auto& w : key) w = (uint32_t)hostRng();
+            for (int m = 0; m < nmb; m++) schedule_step(*this, k++, row_minibatch(key, (uint32_t)m * (uint32_t)rows));
+        } else {
+            std::shuffle(slotOrder.begin(), slotOrder.end(), hostRng);
+            for (uint32_t t : slotOrder) schedule_step(*this, k++, slot_minibatch(t));
+        }
     }
-    MG_CUDA_TRY(cudaMemcpyAsync(schedSlot, hostSchedSlot, (size_t)n * 4, cudaMemcpyHostToDevice, st));
-    MG_CUDA_TRY(cudaMemcpyAsync(schedBetaPow, hostSchedBetaPow, (size_t)n * 8, cudaMemcpyHostToDevice, st));
-    if (!trainExec || trainExecMinibatches != n || !(trainHp == hp)) MG_TRY(captureTrain(n));
-    MG_CUDA_TRY(cudaGraphLaunch(trainExec, st));
+    if (!trainExec || trainExecMinibatches != nmb || trainExecRowMode != rowMode || !(trainHp == hp))
+        MG_TRY(captureTrain(nmb, rowMode));
+    for (int e = 0; e < epochs; e++) {
+        MG_CUDA_TRY(cudaMemcpyAsync(sched, hostSched + (size_t)e * nmb, (size_t)nmb * sizeof(MgMinibatch),
+                                    cudaMemcpyHostToDevice, st));
+        MG_CUDA_TRY(cudaMemcpyAsync(schedBetaPow, hostSchedBetaPow + (size_t)e * nmb * 2, (size_t)nmb * 8,
+                                    cudaMemcpyHostToDevice, st));
+        MG_CUDA_TRY(cudaGraphLaunch(trainExec, st));
+    }
     return checkStatus("train");
 }
 
@@ -706,12 +803,28 @@ int PpoEngine::trainSlot(int t) {
     MG_CHECK_ARG(t >= 0 && t < T, "trainSlot: slot out of range");
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
-    schedule_step(*this, 0, (uint32_t)t);
-    MG_CUDA_TRY(cudaMemcpyAsync(schedSlot, hostSchedSlot, 4, cudaMemcpyHostToDevice, st));
+    if (trainBufRows != R) MG_TRY(allocTrain(R));
+    MG_TRY(ensureSchedule(1, 1));
+    schedule_step(*this, 0, slot_minibatch((uint32_t)t));
+    MG_CUDA_TRY(cudaMemcpyAsync(sched, hostSched, sizeof(MgMinibatch), cudaMemcpyHostToDevice, st));
     MG_CUDA_TRY(cudaMemcpyAsync(schedBetaPow, hostSchedBetaPow, 8, cudaMemcpyHostToDevice, st));
     // single minibatches run eagerly (no graph): trainSlot is the manual path
-    MG_TRY(minibatch(0, st));
+    MG_TRY(minibatch(0, false, st));
     return checkStatus("trainSlot");
+}
+
+int PpoEngine::trainRows(const uint32_t key[4], uint32_t base) {
+    MG_CHECK_ARG(mbRows > 0, "trainRows: set minibatchRows first");
+    MG_CHECK_ARG((int64_t)base + mbRows <= (int64_t)T * R, "trainRows: base + minibatchRows exceeds the rollout");
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    cudaStream_t st = gym->stream;
+    if (trainBufRows != mbRows) MG_TRY(allocTrain(mbRows));
+    MG_TRY(ensureSchedule(1, 1));
+    schedule_step(*this, 0, row_minibatch(key, base));
+    MG_CUDA_TRY(cudaMemcpyAsync(sched, hostSched, sizeof(MgMinibatch), cudaMemcpyHostToDevice, st));
+    MG_CUDA_TRY(cudaMemcpyAsync(schedBetaPow, hostSchedBetaPow, 8, cudaMemcpyHostToDevice, st));
+    MG_TRY(minibatch(0, true, st));
+    return checkStatus("trainRows");
 }
 
 int PpoEngine::forward() {
@@ -724,7 +837,7 @@ int PpoEngine::forward() {
 int PpoEngine::lastStats(float out6[6]) {
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
-    MG_TRY(stats_mean(stats, R, statsMean, st));
+    MG_TRY(stats_mean(stats, trainBufRows, statsMean, st));
     MG_CUDA_TRY(cudaMemcpyAsync(hostStats, statsMean, 5 * 4, cudaMemcpyDeviceToHost, st));
     MG_CUDA_TRY(cudaMemcpyAsync(hostStats + 5, normSq, 4, cudaMemcpyDeviceToHost, st));
     MG_CUDA_TRY(cudaStreamSynchronize(st));

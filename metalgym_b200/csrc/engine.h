@@ -54,15 +54,15 @@ struct PpoHyper {
 
 // Per-forward activation pointers (collect shares one set across blocks).
 struct ActSet {
-    void* h;                  // residual stream, R x E bf16 (updated in place)
+    void* h = nullptr;        // residual stream, R x E bf16 (updated in place)
     std::vector<void*> lnXn;  // per block, R x E
     std::vector<void*> lnOut;
     std::vector<float*> lnSd;
     std::vector<void*> v;     // per block, R x H (post-ReLU)
-    void* fXn;
-    void* fOut;
-    float* fSd;
-    void* head;  // R x 64
+    void* fXn = nullptr;
+    void* fOut = nullptr;
+    float* fSd = nullptr;
+    void* head = nullptr;  // R x 64
 };
 
 struct ParamSpec {
@@ -80,6 +80,11 @@ class PpoEngine {
     int collect();
     int train(int epochs);
     int trainSlot(int t);
+    // Minibatch rows of train(): 0 = one time slot per minibatch (the
+    // reference); B > 0 = B rollout rows drawn without replacement per epoch.
+    int setMinibatchRows(int rows);
+    // One row-mode minibatch with explicit permutation key and base (tests).
+    int trainRows(const uint32_t key[4], uint32_t base);
     int forward();  // on the gym's live obs; head in the collect activations
     int lastStats(float out6[6]);
     int setLogStd(float v);
@@ -95,7 +100,9 @@ class PpoEngine {
     PpoHyper hp;
     bool rolloutStarted = false;
     float stepCounter = 0.0f;  // model/ppo.h:265 (float, as the reference)
-    std::mt19937 hostRng;      // slot shuffle (model/ppo.h:349, 920)
+    std::mt19937 hostRng;      // slot shuffle (model/ppo.h:349, 920), row-mode keys
+    int mbRows = 0;            // 0: slot mode; > 0: rows per row-mode minibatch
+    int trainBufRows = 0;      // rows the training buffers are sized for
     std::vector<uint32_t> slotOrder;
 
     std::vector<ParamSpec> params;
@@ -112,7 +119,8 @@ class PpoEngine {
     float *logpSlots = nullptr, *valueSlots = nullptr, *rewardSlots = nullptr, *advSlots = nullptr,
           *retSlots = nullptr;
     uint8_t* doneSlots = nullptr;
-    float* advStats = nullptr;  // T x {mean, inv}
+    float* advStats = nullptr;    // T x {mean, inv}
+    float* mbAdvStats = nullptr;  // {mean, inv} of the current row-mode minibatch
     // activations
     ActSet collectActs, trainActs;
     void *dLogits = nullptr, *dStream = nullptr, *dBranch = nullptr, *dV = nullptr;
@@ -127,11 +135,12 @@ class PpoEngine {
     float* normSq = nullptr;
     unsigned int* normCounter = nullptr;  // last-CTA detection of the norm reduction
     float* statsMean = nullptr;  // 5 floats
-    // per-minibatch schedule: slot index and bias-correction powers
-    int maxSchedule = 0;
-    int* schedSlot = nullptr;      // device
-    float* schedBetaPow = nullptr;  // device, 2 per minibatch
-    int* hostSchedSlot = nullptr;   // pinned
+    // per-minibatch schedule: rows (slot or permutation key) and the Adam
+    // bias-correction powers; the device holds one epoch, the host all epochs
+    int maxSchedule = 0, maxHostSchedule = 0;
+    MgMinibatch* sched = nullptr;       // device
+    float* schedBetaPow = nullptr;      // device, 2 per minibatch
+    MgMinibatch* hostSched = nullptr;   // pinned
     float* hostSchedBetaPow = nullptr;
     // host-side LossStats readback
     float* hostStats = nullptr;  // pinned, 6 floats
@@ -140,7 +149,8 @@ class PpoEngine {
     cudaGraphExec_t collectExec = nullptr;
     cudaGraphExec_t trainExec = nullptr;
     size_t collectKernels = 0, trainKernels = 0;  // kernel nodes of the captured graphs
-    int trainExecMinibatches = 0;
+    int trainExecMinibatches = 0;  // per replay (one epoch)
+    bool trainExecRowMode = false;
     PpoHyper collectHp, trainHp;
 
     // multi-GPU
@@ -149,10 +159,12 @@ class PpoEngine {
 
    private:
     int forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st);
-    int minibatch(int j, cudaStream_t st);  // reads schedSlot[j], schedBetaPow[j]
+    int minibatch(int j, bool rowMode, cudaStream_t st);  // reads sched[j], schedBetaPow[2j..]
     int captureCollect();
-    int captureTrain(int minibatches);
-    int ensureSchedule(int n);
+    int captureTrain(int minibatches, bool rowMode);
+    int ensureSchedule(int device, int host);
+    int allocTrain(int rows);
+    void freeTrain();
     int checkStatus(const char* what);
 };
 

@@ -22,11 +22,11 @@ constexpr int kGaussRowsPerCta = 256;  // Gaussian loss: rows per CTA
 template <int VPT>
 __global__ void k_input_forward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ w,
                                 const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int rows,
-                                int inDim, int outDim, const int* __restrict__ slotIdx, int64_t slotStride) {
+                                int inDim, int outDim, RowMap rm) {
     mg_pdl_trigger();
     mg_pdl_wait();
     extern __shared__ float s_w[];  // inDim x outDim as fp32
-    if (slotIdx) obs += (int64_t)(*slotIdx) * slotStride;
+    const MgMinibatch* mb = rm.mb;
     for (int i = threadIdx.x; i < inDim * outDim; i += blockDim.x) s_w[i] = bf(w[i]);
     __syncthreads();
     const int lane = threadIdx.x & 31;
@@ -38,7 +38,7 @@ __global__ void k_input_forward(const float* __restrict__ obs, const __nv_bfloat
         float acc[VPT];
 #pragma unroll
         for (int j = 0; j < VPT; j++) acc[j] = b[j];
-        const float* o = obs + (size_t)r * inDim;
+        const float* o = obs + (size_t)(mb ? mg_minibatch_row(*mb, r, rm.envRows, rm.total) : (uint64_t)r) * inDim;
         for (int k = 0; k < inDim; k++) {
             const float ok = o[k];
 #pragma unroll
@@ -57,14 +57,17 @@ __global__ void k_input_forward(const float* __restrict__ obs, const __nv_bfloat
 // into registers (independent loads), obs rows come from shared memory.
 __global__ void k_input_backward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ dZ,
                                  float* __restrict__ partial, int rows, int inDim, int outDim, int rowsPerCta,
-                                 const int* __restrict__ slotIdx, int64_t slotStride) {
+                                 RowMap rm) {
     mg_pdl_trigger();
     mg_pdl_wait();
     extern __shared__ float s_obs[];  // rowsPerCta x inDim
-    if (slotIdx) obs += (int64_t)(*slotIdx) * slotStride;
     const int r0 = blockIdx.x * rowsPerCta;
     const int nr = min(rowsPerCta, rows - r0);
-    for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) s_obs[i] = obs[(size_t)r0 * inDim + i];
+    for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) {
+        const int r = r0 + i / inDim;
+        const uint64_t g = rm.mb ? mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : (uint64_t)r;
+        s_obs[i] = obs[g * inDim + i % inDim];
+    }
     __syncthreads();
     float* part = partial + (size_t)blockIdx.x * (inDim + 1) * outDim;
     for (int c = threadIdx.x; c < outDim; c += blockDim.x) {
@@ -277,19 +280,14 @@ __global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int3
                               const float* __restrict__ adv, const float* __restrict__ advStats,
                               const float* __restrict__ ret, const float* __restrict__ oldLogProb,
                               __nv_bfloat16* __restrict__ dZ, float* __restrict__ stats, int rows, int actDim,
-                              LossHyper hp, int* status, const int* __restrict__ slotIdx) {
+                              LossHyper hp, int* status, RowMap rm) {
     mg_pdl_trigger();
     mg_pdl_wait();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
-    if (slotIdx) {  // slot-major rollout buffers: slot s starts at s * rows
-        const int64_t s = *slotIdx;
-        action += s * rows;
-        adv += s * rows;
-        ret += s * rows;
-        oldLogProb += s * rows;
-        if (advStats) advStats += 2 * s;
-    }
+    // minibatch row r reads rollout row g of the slot-major buffers
+    const int64_t g = rm.mb ? (int64_t)mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : r;
+    if (rm.mb && rm.mb->slot >= 0 && advStats) advStats += 2 * rm.mb->slot;  // per-slot statistics
     const float scale = __fdiv_rn(1.0f, (float)rows);
     const __nv_bfloat16* h = head + (size_t)r * kHeadDim;
     // exp(logp_j) is needed twice (entropy, gradient): keep up to kCache of them
@@ -313,14 +311,14 @@ __global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int3
         const float logp = __fsub_rn(bf(h[j]), lse);
         entropy = __fsub_rn(entropy, __fmul_rn(mg_expf(logp), logp));
     }
-    const int a = action[r];
+    const int a = action[g];
     if (a < 0 || a >= actDim) {  // never index the head with an invalid action
         record_error(status, kDevBadAction);
         return;
     }
-    const float A = norm_adv(adv, advStats, r);
+    const float A = norm_adv(adv, advStats, g);
     const float logpA = __fsub_rn(bf(h[a]), lse);
-    const float ratio = mg_expf(__fsub_rn(logpA, oldLogProb[r]));
+    const float ratio = mg_expf(__fsub_rn(logpA, oldLogProb[g]));
     const float surr1 = __fmul_rn(ratio, A);
     const float surr2 = __fmul_rn(fminf(fmaxf(ratio, __fsub_rn(1.0f, hp.clip)), __fadd_rn(1.0f, hp.clip)), A);
     const float policyLoss = -fminf(surr1, surr2);
@@ -343,7 +341,7 @@ __global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int3
                                   __fmul_rn(__fmul_rn(hp.entropyCoef, prob), __fadd_rn(logp, entropy)));
         pz[j] = tobf(__fmul_rn(g, scale));
     }
-    const float vErr = __fsub_rn(bf(h[actDim]), ret[r]);
+    const float vErr = __fsub_rn(bf(h[actDim]), ret[g]);
     pz[actDim] = tobf(__fmul_rn(__fmul_rn(hp.valueCoef, vErr), scale));
     uint4* dst = reinterpret_cast<uint4*>(dZ + (size_t)r * kHeadDim);
     const uint4* src = reinterpret_cast<const uint4*>(packed);
@@ -353,7 +351,7 @@ __global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int3
     st[0] = policyLoss;
     st[1] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, hp.valueCoef), vErr), vErr);
     st[2] = entropy;
-    st[3] = __fsub_rn(oldLogProb[r], logpA);
+    st[3] = __fsub_rn(oldLogProb[g], logpA);
     st[4] = (fabsf(__fsub_rn(ratio, 1.0f)) > hp.clip) ? 1.0f : 0.0f;
 }
 
@@ -363,25 +361,19 @@ __global__ void __launch_bounds__(kGaussRowsPerCta) k_gaussian_loss(
     const __nv_bfloat16* __restrict__ head, const float* __restrict__ action, const float* __restrict__ adv,
     const float* __restrict__ advStats, const float* __restrict__ ret, const float* __restrict__ oldLogProb,
     __nv_bfloat16* __restrict__ dZ, float* __restrict__ stats, const __nv_bfloat16* __restrict__ logStd,
-    float* __restrict__ partial, int rows, int actDim, LossHyper hp, const int* __restrict__ slotIdx) {
+    float* __restrict__ partial, int rows, int actDim, LossHyper hp, RowMap rm) {
     mg_pdl_trigger();
     mg_pdl_wait();
     __shared__ float s_gls[kGaussRowsPerCta];
-    if (slotIdx) {
-        const int64_t s = *slotIdx;
-        action += s * rows * actDim;
-        adv += s * rows;
-        ret += s * rows;
-        oldLogProb += s * rows;
-        if (advStats) advStats += 2 * s;
-    }
+    if (rm.mb && rm.mb->slot >= 0 && advStats) advStats += 2 * rm.mb->slot;  // per-slot statistics
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t g = (r < rows && rm.mb) ? (int64_t)mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : r;
     const bool live = r < rows;
     const float scale = __fdiv_rn(1.0f, (float)rows);
     float gLogp = 0.0f;
     if (live) {
         const __nv_bfloat16* h = head + (size_t)r * kHeadDim;
-        const float* act = action + (size_t)r * actDim;
+        const float* act = action + (size_t)g * actDim;
         float logp = 0.0f, entropy = 0.0f;
         for (int k = 0; k < actDim; k++) {
             const float ls = bf(logStd[k]);
@@ -389,8 +381,8 @@ __global__ void __launch_bounds__(kGaussRowsPerCta) k_gaussian_loss(
             logp = __fadd_rn(logp, __fsub_rn(__fsub_rn(__fmul_rn(__fmul_rn(-0.5f, d), d), ls), kLogSqrt2Pi));
             entropy = __fadd_rn(entropy, __fadd_rn(__fadd_rn(ls, kLogSqrt2Pi), 0.5f));
         }
-        const float A = norm_adv(adv, advStats, r);
-        const float ratio = mg_expf(__fsub_rn(logp, oldLogProb[r]));
+        const float A = norm_adv(adv, advStats, g);
+        const float ratio = mg_expf(__fsub_rn(logp, oldLogProb[g]));
         const float surr1 = __fmul_rn(ratio, A);
         const float surr2 = __fmul_rn(fminf(fmaxf(ratio, __fsub_rn(1.0f, hp.clip)), __fadd_rn(1.0f, hp.clip)), A);
         const float policyLoss = -fminf(surr1, surr2);
@@ -405,7 +397,7 @@ __global__ void __launch_bounds__(kGaussRowsPerCta) k_gaussian_loss(
             const float d = __fmul_rn(__fsub_rn(act[k], bf(h[k])), invStd);
             pz[k] = tobf(__fmul_rn(__fmul_rn(__fmul_rn(gLogp, d), invStd), scale));
         }
-        const float vErr = __fsub_rn(bf(h[actDim]), ret[r]);
+        const float vErr = __fsub_rn(bf(h[actDim]), ret[g]);
         pz[actDim] = tobf(__fmul_rn(__fmul_rn(hp.valueCoef, vErr), scale));
         uint4* dst = reinterpret_cast<uint4*>(dZ + (size_t)r * kHeadDim);
         const uint4* src = reinterpret_cast<const uint4*>(packed);
@@ -415,7 +407,7 @@ __global__ void __launch_bounds__(kGaussRowsPerCta) k_gaussian_loss(
         st[0] = policyLoss;
         st[1] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, hp.valueCoef), vErr), vErr);
         st[2] = entropy;
-        st[3] = __fsub_rn(oldLogProb[r], logp);
+        st[3] = __fsub_rn(oldLogProb[g], logp);
         st[4] = (fabsf(__fsub_rn(ratio, 1.0f)) > hp.clip) ? 1.0f : 0.0f;
     }
     for (int k = 0; k < actDim; k++) {
@@ -423,7 +415,7 @@ __global__ void __launch_bounds__(kGaussRowsPerCta) k_gaussian_loss(
         if (live) {
             const float ls = bf(logStd[k]);
             const float invStd = mg_expf(-ls);
-            const float d = __fmul_rn(__fsub_rn(action[(size_t)r * actDim + k], bf(head[(size_t)r * kHeadDim + k])),
+            const float d = __fmul_rn(__fsub_rn(action[(size_t)g * actDim + k], bf(head[(size_t)r * kHeadDim + k])),
                                       invStd);
             gls = __fmul_rn(__fsub_rn(__fmul_rn(gLogp, __fsub_rn(__fmul_rn(d, d), 1.0f)), hp.entropyCoef), scale);
         }
@@ -503,6 +495,47 @@ __global__ void __launch_bounds__(1024) k_adv_stats(const float* __restrict__ ad
             const float var = __fdiv_rn(t, (float)rows);
             out[2 * blockIdx.x] = mean;
             out[2 * blockIdx.x + 1] = __fdiv_rn(1.0f, __fadd_rn(__fsqrt_rn(var), 1e-8f));
+        }
+    }
+}
+
+// The same statistics over the rows of one row-mode minibatch, gathered
+// through its row map; one CTA.
+__global__ void __launch_bounds__(1024) k_adv_stats_rows(const float* __restrict__ adv, RowMap rm, int rows,
+                                                         float* __restrict__ out) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
+    __shared__ float s_part[32];
+    __shared__ float s_mean;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float s = 0.0f;
+    for (int q = threadIdx.x; q < rows; q += blockDim.x)
+        s = __fadd_rn(s, adv[mg_minibatch_row(*rm.mb, q, rm.envRows, rm.total)]);
+    s = warp_sum(s);
+    if (lane == 0) s_part[warp] = s;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < nw ? s_part[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) s_mean = __fdiv_rn(t, (float)rows);
+    }
+    __syncthreads();
+    const float mean = s_mean;
+    float v = 0.0f;
+    for (int q = threadIdx.x; q < rows; q += blockDim.x) {
+        const float d = __fsub_rn(adv[mg_minibatch_row(*rm.mb, q, rm.envRows, rm.total)], mean);
+        v = __fadd_rn(v, __fmul_rn(d, d));
+    }
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) s_part[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < nw ? s_part[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) {
+            out[0] = mean;
+            out[1] = __fdiv_rn(1.0f, __fadd_rn(__fsqrt_rn(__fdiv_rn(t, (float)rows)), 1e-8f));
         }
     }
 }
@@ -702,7 +735,7 @@ int grid_rows(int rows, int rowsPerCta) { return (rows + rowsPerCta - 1) / rowsP
 // ------------------------------------------------------------ host launchers
 
 int input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int inDim, int outDim,
-                  cudaStream_t st, const int* slotIdx, int64_t slotStride) {
+                  cudaStream_t st, RowMap rm) {
     MG_CHECK_ARG(rows > 0 && inDim > 0 && outDim % 64 == 0 && outDim <= 1024, "input_forward: bad shape");
     MG_CHECK_ARG(inDim * outDim * 4 <= 160 * 1024, "input_forward: weight too large for shared memory");
     const int blocks = std::min(grid_rows(rows, 8), 148 * 8);
@@ -714,7 +747,7 @@ int input_forward(const float* obs, const void* w, const void* b, void* out, int
     case V:                                                                                        \
         if (sm > 48 * 1024)                                                                        \
             MG_CUDA_TRY(cudaFuncSetAttribute(k_input_forward<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
-        MG_LAUNCH(k_input_forward<V>, blocks, 256, sm, st, obs, W, B, O, rows, inDim, outDim, slotIdx, slotStride); \
+        MG_LAUNCH(k_input_forward<V>, blocks, 256, sm, st, obs, W, B, O, rows, inDim, outDim, rm); \
         break;
     switch (outDim / 32) {
         MG_IN_FWD(2) MG_IN_FWD(4) MG_IN_FWD(8) MG_IN_FWD(16) MG_IN_FWD(32)
@@ -739,7 +772,7 @@ int input_backward_parts(int rows, int inDim, int outDim) {
 }
 
 int input_backward(const float* obs, const void* dZ, float* partial, int rows, int inDim, int outDim,
-                   cudaStream_t st, const int* slotIdx, int64_t slotStride) {
+                   cudaStream_t st, RowMap rm) {
     MG_CHECK_ARG(rows > 0 && inDim > 0 && inDim <= 256 && outDim > 0 && outDim <= 1024, "input_backward: bad shape");
     const int rpc = input_rows_per_cta(rows, inDim, outDim);
     const size_t sm = (size_t)rpc * inDim * 4;
@@ -747,7 +780,7 @@ int input_backward(const float* obs, const void* dZ, float* partial, int rows, i
     if (sm > 48 * 1024)
         MG_CUDA_TRY(cudaFuncSetAttribute(k_input_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
     MG_LAUNCH(k_input_backward, grid_rows(rows, rpc), std::min(outDim, 1024), sm, st, 
-        obs, static_cast<const __nv_bfloat16*>(dZ), partial, rows, inDim, outDim, rpc, slotIdx, slotStride);
+        obs, static_cast<const __nv_bfloat16*>(dZ), partial, rows, inDim, outDim, rpc, rm);
     return check_launch("k_input_backward");
 }
 
@@ -810,11 +843,11 @@ int sample_gaussian(const void* head, const void* logStd, uint32_t* rng, float* 
 
 int policy_loss(const void* head, const int32_t* action, const float* adv, const float* advStats, const float* ret,
                 const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
-                cudaStream_t st, const int* slotIdx) {
+                cudaStream_t st, RowMap rm) {
     MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "policy_loss: bad shape");
     MG_LAUNCH(k_policy_loss, grid_rows(rows, 64), 64, 0, st, static_cast<const __nv_bfloat16*>(head), action, adv,
                                                          advStats, ret, oldLogProb, static_cast<__nv_bfloat16*>(dZ),
-                                                         stats, rows, actDim, hp, status_ptr(), slotIdx);
+                                                         stats, rows, actDim, hp, status_ptr(), rm);
     return check_launch("k_policy_loss");
 }
 
@@ -822,12 +855,12 @@ int gaussian_loss_parts(int rows) { return grid_rows(rows, kGaussRowsPerCta); }
 
 int gaussian_loss(const void* head, const float* action, const float* adv, const float* advStats, const float* ret,
                   const float* oldLogProb, void* dZ, float* stats, const void* logStd, float* partial, int rows,
-                  int actDim, LossHyper hp, cudaStream_t st, const int* slotIdx) {
+                  int actDim, LossHyper hp, cudaStream_t st, RowMap rm) {
     MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "gaussian_loss: bad shape");
     MG_LAUNCH(k_gaussian_loss, gaussian_loss_parts(rows), kGaussRowsPerCta, 0, st, 
         static_cast<const __nv_bfloat16*>(head), action, adv, advStats, ret, oldLogProb,
         static_cast<__nv_bfloat16*>(dZ), stats, static_cast<const __nv_bfloat16*>(logStd), partial, rows, actDim, hp,
-        slotIdx);
+        rm);
     return check_launch("k_gaussian_loss");
 }
 
@@ -837,6 +870,12 @@ int gae(const float* reward, const uint8_t* done, const float* value, const void
     MG_LAUNCH(k_gae, grid_rows(rows, 128), 128, 0, st, reward, done, value, static_cast<const __nv_bfloat16*>(bootHead), adv,
                                                  ret, rows, horizon, actDim, gamma, lambda);
     return check_launch("k_gae");
+}
+
+int advantage_stats_rows(const float* adv, RowMap rm, int rows, float* out, cudaStream_t st) {
+    MG_CHECK_ARG(rm.mb && rows > 0, "advantage_stats_rows: needs a row map");
+    MG_LAUNCH(k_adv_stats_rows, 1, 1024, 0, st, adv, rm, rows, out);
+    return check_launch("k_adv_stats_rows");
 }
 
 int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStream_t st) {

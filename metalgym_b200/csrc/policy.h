@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "metalgym/rowmap.h"
+
 namespace mg {
 
 // PPO loss coefficients (model/policy.metal:5-12).
@@ -40,14 +42,21 @@ struct GradSegmentTable {
     int n;
 };
 
-// Loss kernels and the input projection take an optional device slot index
-// (slotIdx[0]) that selects slot s of the slot-major rollout buffers.
-// slotIdx (device, optional): read obs at obs + slotIdx[0] * slotStride.
+// Where the rows of a training minibatch come from: with mb (a device
+// pointer to the minibatch's schedule entry), row q of the kernel reads
+// rollout row mg_minibatch_row(*mb, q, envRows, total) of the slot-major
+// buffers; without it, row q reads row q.
+struct RowMap {
+    const MgMinibatch* mb;
+    uint64_t envRows;  // R, rows per slot
+    uint64_t total;    // T * R
+};
+
 int input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int inDim, int outDim,
-                  cudaStream_t st, const int* slotIdx = nullptr, int64_t slotStride = 0);
+                  cudaStream_t st, RowMap rm = RowMap{nullptr, 0, 0});
 int input_backward_parts(int rows, int inDim, int outDim);
 int input_backward(const float* obs, const void* dZ, float* partial, int rows, int inDim, int outDim,
-                   cudaStream_t st, const int* slotIdx = nullptr, int64_t slotStride = 0);
+                   cudaStream_t st, RowMap rm = RowMap{nullptr, 0, 0});
 int layernorm_forward(const void* x, void* xNorm, void* out, const void* gamma, const void* beta, float* stdev,
                       int rows, int cols, cudaStream_t st);
 int layernorm_backward_parts(int rows);
@@ -59,14 +68,16 @@ int sample_gaussian(const void* head, const void* logStd, uint32_t* rng, float* 
                     float* value, int rows, int actDim, cudaStream_t st);
 int policy_loss(const void* head, const int32_t* action, const float* adv, const float* advStats, const float* ret,
                 const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
-                cudaStream_t st, const int* slotIdx = nullptr);
+                cudaStream_t st, RowMap rm = RowMap{nullptr, 0, 0});
 int gaussian_loss_parts(int rows);
 int gaussian_loss(const void* head, const float* action, const float* adv, const float* advStats, const float* ret,
                   const float* oldLogProb, void* dZ, float* stats, const void* logStd, float* partial, int rows,
-                  int actDim, LossHyper hp, cudaStream_t st, const int* slotIdx = nullptr);
+                  int actDim, LossHyper hp, cudaStream_t st, RowMap rm = RowMap{nullptr, 0, 0});
 int gae(const float* reward, const uint8_t* done, const float* value, const void* bootHead, float* adv, float* ret,
         int rows, int horizon, int actDim, float gamma, float lambda, cudaStream_t st);
 int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStream_t st);
+// {mean, 1/(std + 1e-8)} of adv over the rows of one row-mode minibatch.
+int advantage_stats_rows(const float* adv, RowMap rm, int rows, float* out, cudaStream_t st);
 // Fills blockEnd of every segment; returns the number of CTAs (= norm partials).
 int grad_table_layout(GradSegmentTable& tab);
 // With counter (a zeroed device word) and normSqOut, the last CTA also sums

@@ -142,6 +142,23 @@ class PPOModel:
     def train_slot(self, t: int):
         check(lib().mg_ppo_train_slot(self._h, t), "trainSlot")
 
+    @property
+    def minibatch_rows(self) -> int:
+        """Rows per training minibatch: 0 = one time slot (the reference)."""
+        v = C.c_int()
+        check(lib().mg_ppo_minibatch_rows(self._h, C.byref(v)))
+        return v.value
+
+    @minibatch_rows.setter
+    def minibatch_rows(self, rows: int):
+        check(lib().mg_ppo_set_minibatch_rows(self._h, int(rows)), "minibatchRows")
+
+    def train_rows(self, key, base: int):
+        """One row-mode minibatch over rows perm(base .. base + B - 1) of the
+        permutation keyed by the four words of key."""
+        k = (C.c_uint32 * 4)(*[int(x) & 0xFFFFFFFF for x in key])
+        check(lib().mg_ppo_train_rows(self._h, k, int(base)), "trainRows")
+
     def forward(self):
         check(lib().mg_ppo_forward(self._h), "forward")
 
@@ -209,3 +226,15 @@ class PPOModel:
         if which == "done":
             return raw.reshape(T, R)
         return raw.view(np.float32).reshape(T, R)
+
+
+def minibatch_rows(key, base: int, rows: int, total: int):
+    """Flat slot-major rollout rows read by rows q < rows of the row-mode
+    minibatch starting at permuted position base (host evaluation of the
+    same permutation the kernels use)."""
+    k = (C.c_uint32 * 4)(*[int(x) & 0xFFFFFFFF for x in key])
+    out = np.zeros(rows, np.uint64)
+    check(lib().mg_minibatch_rows(k, int(base), int(rows), int(total), out.ctypes.data_as(C.c_void_p)),
+          "mg_minibatch_rows")
+    return out
+

@@ -152,29 +152,17 @@ def test_second_collect_continues_from_last_obs(mg):
     assert np.array_equal(model.slots("obs")[0], last)
 
 
-@pytest.mark.parametrize("name", ["rollout_cartpole", "rollout_cartpole_continuous"])
-def test_train_slot_matches_oracle(mg, oracle, name):
-    R, T, E, s, L = 1024, 4, 128, 4, 2
-    gym, model = make(name, R, E, s, L, T, seed=2)
-    model.collect()
-    om = oracle_model(oracle, model, 2)
+def copy_optimiser_state(oracle, om, model):
     n = model.opt_count
-    # identical optimiser state on both sides
     for fn, buf, dt in [("orc_model_weights", "weights", np.uint16), ("orc_model_master", "master", np.float32),
                         ("orc_model_momentum", "momentum", np.float32), ("orc_model_variance", "variance", np.float32)]:
         arr(oracle, fn, om, n, dt)[:] = model.download(buf).view(dt)
-    t = 2
-    obs = np.ascontiguousarray(model.slots("obs")[t])
-    act = np.ascontiguousarray(model.slots("actions")[t])
-    adv = np.ascontiguousarray(model.slots("adv")[t])
-    ret = np.ascontiguousarray(model.slots("ret")[t])
-    logp = np.ascontiguousarray(model.slots("logp")[t])
-    stats = np.zeros((R, 5), np.float32)
-    nsq = np.zeros(1, np.float32)
-    m0 = model.download("master").view(np.float32).copy()
-    oracle.orc_model_set_step_counter(om, model.step_counter())
-    oracle.orc_model_train_minibatch(om, ptr(obs), ptr(act), ptr(adv), ptr(ret), ptr(logp), R, ptr(stats), ptr(nsq))
-    model.train_slot(t)
+
+
+def compare_minibatch(oracle, om, model, stats, nsq, m0):
+    """The GPU's last minibatch (statistics, gradient, Adam step) against the
+    oracle's on the same rows and optimiser state."""
+    n = model.opt_count
     ls = model.last_stats()
     ref = stats.mean(0)
     for k, key in enumerate(("policy", "value", "entropy", "approxKl", "clipFrac")):
@@ -193,7 +181,93 @@ def test_train_slot_matches_oracle(mg, oracle, name):
     agree = (np.sign(m1 - m0) == np.sign(o1 - m0))[clear].mean()
     assert agree > 0.97, agree
     assert model.step_counter() == oracle.orc_model_step_counter(om)
+
+
+@pytest.mark.parametrize("name", ["rollout_cartpole", "rollout_cartpole_continuous"])
+def test_train_slot_matches_oracle(mg, oracle, name):
+    R, T, E, s, L = 1024, 4, 128, 4, 2
+    gym, model = make(name, R, E, s, L, T, seed=2)
+    model.collect()
+    om = oracle_model(oracle, model, 2)
+    copy_optimiser_state(oracle, om, model)
+    t = 2
+    obs = np.ascontiguousarray(model.slots("obs")[t])
+    act = np.ascontiguousarray(model.slots("actions")[t])
+    adv = np.ascontiguousarray(model.slots("adv")[t])
+    ret = np.ascontiguousarray(model.slots("ret")[t])
+    logp = np.ascontiguousarray(model.slots("logp")[t])
+    stats = np.zeros((R, 5), np.float32)
+    nsq = np.zeros(1, np.float32)
+    m0 = model.download("master").view(np.float32).copy()
+    oracle.orc_model_set_step_counter(om, model.step_counter())
+    oracle.orc_model_train_minibatch(om, ptr(obs), ptr(act), ptr(adv), ptr(ret), ptr(logp), R, ptr(stats), ptr(nsq))
+    model.train_slot(t)
+    compare_minibatch(oracle, om, model, stats, nsq, m0)
     oracle.orc_model_destroy(om)
+
+
+@pytest.mark.parametrize("name", ["rollout_cartpole", "rollout_cartpole_continuous"])
+def test_train_rows_matches_oracle(mg, oracle, name):
+    """A row-mode minibatch (B rows gathered across slots through the keyed
+    permutation, advantages normalised over those rows) against the oracle's
+    minibatch on the same rows, gathered on the host."""
+    from metalgym_b200.session import minibatch_rows
+
+    R, T, E, s, L, B = 1024, 4, 128, 4, 2, 512
+    gym, model = make(name, R, E, s, L, T, seed=4)
+    model.collect()
+    model.minibatch_rows = B
+    om = oracle_model(oracle, model, 4)
+    copy_optimiser_state(oracle, om, model)
+    key, base = [0x9E3779B9, 0x7F4A7C15, 0x2545F491, 0x61C88647], 3 * B
+    idx = minibatch_rows(key, base, B, T * R).astype(np.int64)
+    t, i = idx // R, idx % R
+    assert len(np.unique(t)) == T  # the minibatch mixes every slot
+    obs = np.ascontiguousarray(model.slots("obs")[t, i])
+    act = np.ascontiguousarray(model.slots("actions")[t, i])
+    adv = np.ascontiguousarray(model.slots("adv")[t, i])
+    ret = np.ascontiguousarray(model.slots("ret")[t, i])
+    logp = np.ascontiguousarray(model.slots("logp")[t, i])
+    stats = np.zeros((B, 5), np.float32)
+    nsq = np.zeros(1, np.float32)
+    m0 = model.download("master").view(np.float32).copy()
+    oracle.orc_model_set_step_counter(om, model.step_counter())
+    oracle.orc_model_train_minibatch(om, ptr(obs), ptr(act), ptr(adv), ptr(ret), ptr(logp), B, ptr(stats), ptr(nsq))
+    model.train_rows(key, base)
+    compare_minibatch(oracle, om, model, stats, nsq, m0)
+    oracle.orc_model_destroy(om)
+
+
+def test_row_mode_loop_runs_and_learns(mg):
+    """train(4) with 2048-row minibatches (every rollout row once per epoch):
+    step counter, finite statistics, improving episodes; then back to slot
+    minibatches on the same model."""
+    gym, model = make("rollout_cartpole", 4096, 128, 4, 2, 32)
+    model.minibatch_rows = 2048
+    lengths = []
+    for it in range(10):
+        model.collect()
+        done = model.slots("done")
+        lengths.append(done.size / max(1, int(done.sum())))
+        model.train(4)
+        st = model.last_stats()
+        assert all(np.isfinite(v) for v in st.values()), st
+    assert model.step_counter() == 10 * 4 * 64
+    assert np.mean(lengths[-3:]) > 1.5 * np.mean(lengths[:2]), lengths
+    model.minibatch_rows = 0
+    model.collect()
+    model.train(1)
+    assert model.step_counter() == 10 * 4 * 64 + 32
+
+
+def test_row_mode_rejects_non_dividing_rows(mg):
+    gym, model = make("rollout_cartpole", 1000, 64, 2, 1, 4)
+    from metalgym_b200 import MgError
+
+    with pytest.raises(MgError, match="divide"):
+        model.minibatch_rows = 3000
+    model.minibatch_rows = 500
+    assert model.minibatch_rows == 500
 
 
 def test_full_loop_runs_and_learns(mg):
