@@ -121,22 +121,16 @@ def run_mine(args, rank, world, local_rank, dist):
     import torch
 
     import metalgym_b200
+    from metalgym_b200.dist import env_shard, nccl_comm
     from metalgym_b200.session import Gym, PPOModel
 
     torch.cuda.set_device(local_rank)
     lib = metalgym_b200.lib()
-    gym = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=rank * ENVS_PER_GPU, device=local_rank)
+    gym = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=env_shard(rank, ENVS_PER_GPU), device=local_rank)
     model = PPOModel(gym, EMBED, SCALE, LAYERS, LR, HORIZON, seed=0)
     comm = None
     if world > 1:
-        idbuf = (ctypes.c_char * 128)()
-        if rank == 0:
-            metalgym_b200.check(lib.mg_comm_unique_id(idbuf))
-        obj = [bytes(idbuf)]
-        dist.broadcast_object_list(obj, src=0)
-        ctypes.memmove(idbuf, obj[0], 128)
-        comm = ctypes.c_void_p()
-        metalgym_b200.check(lib.mg_comm_init(world, rank, idbuf, local_rank, ctypes.byref(comm)))
+        comm = nccl_comm(dist, rank, world, local_rank)
         model.set_comm(comm, rank, world)
     stream = torch.cuda.ExternalStream(gym.stream(), device=local_rank)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{local_rank}")
@@ -211,7 +205,7 @@ def run_mine(args, rank, world, local_rank, dist):
     legs["full_loop"] = {"value": value, "ms_per_iteration": ms}
 
     # ---- raw env step (config 1): fused multi-step kernel and the gym.run loop
-    raw = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=rank * ENVS_PER_GPU, device=local_rank)
+    raw = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=env_shard(rank, ENVS_PER_GPU), device=local_rank)
     rstream = torch.cuda.ExternalStream(raw.stream(), device=local_rank)
     raw.run_random(RAW_STEPS)
     raw.synchronize()
@@ -241,6 +235,11 @@ def run_mine(args, rank, world, local_rank, dist):
     legs["raw_env"]["gym_run_e2e"] = ENVS_PER_GPU * world / run_s
     lib.mg_host_free(pinned)
 
+    # ---- the full loop at the other two configurations (weak scaling per GPU)
+    if not args.no_extra_legs:
+        for name, cfg in EXTRA_LOOPS.items():
+            legs[name] = extra_loop_leg(cfg, rank, world, local_rank, comm, flush, dist)
+
     # ---- dominant kernel, timed live: see profiles/ for the launch-share list
     roof = dominant_kernel_roofline(lib, torch, local_rank, stream)
 
@@ -264,19 +263,80 @@ def run_mine(args, rank, world, local_rank, dist):
                                       "epochs": EPOCHS},
             "clocks": clk.summary(),
         }
+    model.close()  # the train graph holds NCCL calls: release it before the communicator
+    gym.close()
+    raw.close()
     if comm is not None:
         lib.mg_comm_destroy(comm)
     return result
 
 
-def max_over_ranks(x, dist):
-    if dist is None:
-        return x
+# (env, envs per GPU, embed, scale, blocks,
+# minibatch rows, timed iterations, warm-up iterations)
+EXTRA_LOOPS = {
+    "c4_cartpole_continuous_full_loop": dict(env="rollout_cartpole_continuous", envs=16384, embed=128, scale=4,
+                                             blocks=2, minibatch=8192, steps=3, warmup=2),
+    "c5_voxelnav_full_loop": dict(env="rollout_voxelnav", envs=262144, embed=256, scale=4, blocks=4,
+                                  minibatch=32768, steps=2, warmup=1),
+}
+
+
+def extra_loop_leg(cfg, rank, world, local_rank, comm, flush, dist):
+    """collect() + train(4) at another configuration, device-timed like the
+    headline (CUDA events on the engine stream, L2 flushed between steps)."""
     import torch
 
-    t = torch.tensor([float(x)], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from metalgym_b200.dist import env_shard
+    from metalgym_b200.session import Gym, PPOModel
+
+    n = cfg["envs"]
+    gym = Gym(cfg["env"], n, seed=0, first_env_id=env_shard(rank, n), device=local_rank)
+    model = PPOModel(gym, cfg["embed"], cfg["scale"], cfg["blocks"], LR, HORIZON, seed=0)
+    model.minibatch_rows = cfg["minibatch"]
+    if comm is not None:
+        model.set_comm(comm, rank, world)
+    stream = torch.cuda.ExternalStream(gym.stream(), device=local_rank)
+    for _ in range(cfg["warmup"]):
+        model.collect()
+        model.train(EPOCHS)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(cfg["steps"])]
+    cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(cfg["steps"])]
+    for k, (s0, s1) in enumerate(ev):
+        with torch.cuda.stream(stream):
+            flush.fill_(float(k))
+            s0.record(stream)
+            cev[k][0].record(stream)
+        model.collect()
+        with torch.cuda.stream(stream):
+            cev[k][1].record(stream)
+        model.train(EPOCHS)
+        with torch.cuda.stream(stream):
+            s1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / len(ev), dist)
+    cms = max_over_ranks(sum(a.elapsed_time(b) for a, b in cev) / len(cev), dist)
+    st = model.last_stats()
+    fwd, bwd = flops_per_row(model.obs_dim, model.act_dim, cfg["embed"], cfg["embed"] * cfg["scale"], cfg["blocks"])
+    steps_per_iter = n * HORIZON
+    flop = steps_per_iter * ((HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd))
+    out = {"value": steps_per_iter * world / (ms / 1e3), "unit": "env steps/s", "ms_per_iteration": ms,
+           "collect_ms": cms, "envs_per_gpu": n, "horizon": HORIZON, "embed": cfg["embed"],
+           "hidden": cfg["embed"] * cfg["scale"], "blocks": cfg["blocks"], "epochs": EPOCHS,
+           "minibatch_rows": cfg["minibatch"], "minibatches_per_iteration": EPOCHS * steps_per_iter // cfg["minibatch"],
+           "steps": cfg["steps"], "warmup": cfg["warmup"],
+           "achieved_tflops": flop / (ms / 1e3) / 1e12, "last_stats": {k: float(v) for k, v in st.items()}}
+    model.close()
+    gym.close()
+    return out
+
+
+def max_over_ranks(x, dist):
+    from metalgym_b200.dist import max_over_ranks as mor
+
+    return mor(x, dist, device="cuda")
 
 
 def dominant_kernel_roofline(lib, torch, dev, stream):
@@ -443,6 +503,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-legs", action="store_true", help="skip the configs[3] / configs[4] loops")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

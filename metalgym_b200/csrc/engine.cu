@@ -698,7 +698,8 @@ int PpoEngine::captureTrain(int minibatches, bool rowMode) {
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "train capture");
-    trainKernels = count_kernel_nodes(graph);
+    // this library's kernels: the all-reduce adds one NCCL kernel per minibatch
+    trainKernels = count_kernel_nodes(graph) - (world > 1 ? (size_t)minibatches : 0);
     cudaGraphExec_t exec = nullptr;
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);

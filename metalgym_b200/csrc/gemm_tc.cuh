@@ -14,7 +14,7 @@
 //                  (one output row per thread) and applies the fused op.
 // Operands may be K-major (rows of K contiguous) or MN-major (K rows of M or N
 // contiguous), which covers X W, dZ W^T and X^T dZ without transposes.
-// No cluster launch and no multicast: every CTA loads its own tiles.
+// No cluster launch: every CTA loads its own tiles.
 #pragma once
 
 #include "metalgym/pdl.cuh"

@@ -1,0 +1,195 @@
+"""One rank of the data-parallel tests, launched by torch.distributed.run.
+
+--mode cpu (gloo, no GPU): the host logic of metalgym_b200.dist (comm-id
+  broadcast, max over ranks, env shards) and the data-parallel update
+  semantics on the oracle: every rank takes the gradient of its own rows,
+  the sum over ranks is scaled by 1/world, the clip and Adam run on every
+  rank; the ranks' weights must stay bit-identical and equal a single
+  process that averages the shards' gradients itself.
+--mode gpu (one GPU per rank, NCCL for the gradient, gloo for the host):
+  a rank's all-reduced gradient must equal the average over ranks of the
+  gradients that an identical model without the communicator computes on
+  the same rollout, bit for bit; after train() the weight digests of all
+  ranks agree.
+
+Rank 0 prints one JSON line; the exit status is 0 when every check passed.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+
+def oracle_shard(orc, rows, rank, seed=3):
+    """A synthetic minibatch of `rows` CartPole-shaped rows for one rank."""
+    rng = np.random.default_rng(100 + rank)
+    obs = rng.normal(0, 0.5, (rows, 4)).astype(np.float32)
+    act = rng.integers(0, 2, rows).astype(np.int32)
+    adv = rng.normal(0, 1, rows).astype(np.float32)
+    ret = rng.normal(1, 0.5, rows).astype(np.float32)
+    logp = (np.log(0.5) + rng.normal(0, 0.05, rows)).astype(np.float32)
+    return obs, act, adv, ret, logp
+
+
+def oracle_arrays(orc, om, n):
+    import ctypes as C
+
+    def view(fn, dt):
+        p = getattr(orc, fn)(om)
+        return np.ctypeslib.as_array(C.cast(p, C.POINTER(np.ctypeslib.as_ctypes_type(dt))), shape=(n,))
+
+    return dict(weights=view("orc_model_weights", np.uint16), master=view("orc_model_master", np.float32),
+                mom=view("orc_model_momentum", np.float32), var=view("orc_model_variance", np.float32),
+                grad=view("orc_model_grad", np.float32))
+
+
+def oracle_gradient(orc, om, shard, rows):
+    stats = np.zeros((rows, 5), np.float32)
+    nsq = np.zeros(1, np.float32)
+    orc.orc_model_gradient(om, *shard, rows, stats, nsq)
+
+
+def oracle_step(orc, om, a, grad, lr, max_norm):
+    """Clip + Adam on the given (already averaged) gradient: model/ppo.h:873-903."""
+    step = orc.orc_model_step_counter(om) + 1.0
+    orc.orc_model_set_step_counter(om, step)
+    nsq = float(np.dot(grad.astype(np.float64), grad.astype(np.float64)))
+    orc.orc_adam_step(a["master"], grad, a["mom"], a["var"], a["weights"], nsq, len(grad), lr,
+                      np.float32(0.9) ** np.float32(step), np.float32(0.999) ** np.float32(step), max_norm)
+
+
+def digest(a):
+    import hashlib
+
+    return hashlib.sha256(a["weights"].tobytes() + a["master"].tobytes()).hexdigest()
+
+
+def run_cpu(rank, world, dist):
+    from orc import load_oracle
+
+    from metalgym_b200.dist import broadcast_comm_id, env_shard, max_over_ranks
+
+    out = {}
+    cid = broadcast_comm_id(dist, rank, lambda: os.urandom(128))
+    ids = [None] * world
+    dist.all_gather_object(ids, cid)
+    out["comm_id_shared"] = all(i == ids[0] for i in ids)
+    out["max_over_ranks"] = max_over_ranks(rank + 1.5, dist, device="cpu") == world - 1 + 1.5
+    shards = [set(range(env_shard(r, 64), env_shard(r, 64) + 64)) for r in range(world)]
+    out["shards_disjoint"] = len(set().union(*shards)) == 64 * world
+
+    import torch
+
+    orc = load_oracle()
+    rows, lr, max_norm = 256, 3e-4, 0.5
+    om = orc.orc_model_create(rows, 4, 2, 0, 64, 2, 1, lr, 4, 3)
+    n = orc.orc_model_opt_count(om)
+    a = oracle_arrays(orc, om, n)
+    for it in range(3):
+        oracle_gradient(orc, om, oracle_shard(orc, rows, rank + world * it), rows)
+        g = torch.from_numpy(a["grad"].copy())
+        dist.all_reduce(g)
+        avg = (g.numpy() * np.float32(1.0 / world)).astype(np.float32)
+        oracle_step(orc, om, a, avg, lr, max_norm)
+    mine = digest(a)
+    digests = [None] * world
+    dist.all_gather_object(digests, mine)
+    out["ranks_identical"] = all(d == mine for d in digests)
+    if rank == 0:
+        # one process holding every shard: average the shards' gradients itself
+        om1 = orc.orc_model_create(rows, 4, 2, 0, 64, 2, 1, lr, 4, 3)
+        b = oracle_arrays(orc, om1, n)
+        for it in range(3):
+            acc = np.zeros(n, np.float32)
+            for r in range(world):
+                oracle_gradient(orc, om1, oracle_shard(orc, rows, r + world * it), rows)
+                acc = (acc + b["grad"]).astype(np.float32)
+            oracle_step(orc, om1, b, (acc * np.float32(1.0 / world)).astype(np.float32), lr, max_norm)
+        out["equals_single_process"] = digest(b) == mine
+        orc.orc_model_destroy(om1)
+    orc.orc_model_destroy(om)
+    return out
+
+
+def run_gpu(rank, world, local, dist):
+    import torch
+
+    from metalgym_b200.dist import destroy_comm, env_shard, nccl_comm, weights_digest
+    from metalgym_b200.session import Gym, PPOModel
+
+    torch.cuda.set_device(local)
+    R, T = 1024, 4
+    out = {}
+    gym = Gym("rollout_cartpole", R, seed=0, first_env_id=env_shard(rank, R), device=local)
+    model = PPOModel(gym, 128, 4, 2, 3e-4, T, seed=7)
+    comm = nccl_comm(dist, rank, world, local)
+    model.set_comm(comm, rank, world)
+    model.collect()
+    # an identical model without the communicator, on the same rollout
+    gym1 = Gym("rollout_cartpole", R, seed=0, first_env_id=env_shard(rank, R), device=local)
+    solo = PPOModel(gym1, 128, 4, 2, 3e-4, T, seed=7)
+    for buf in ("obs", "actions", "logp", "value", "reward", "done", "adv", "ret", "adv_stats", "weights", "master",
+                "momentum", "variance"):
+        solo.upload(buf, model.download(buf))
+    solo.set_step_counter(model.step_counter())
+    model.train_slot(1)
+    solo.train_slot(1)
+    g_dp = model.download("grad").view(np.float32)
+    g_local = torch.from_numpy(solo.download("grad").view(np.float32).copy())
+    dist.all_reduce(g_local)
+    g_avg = (g_local.numpy() * np.float32(1.0 / world)).astype(np.float32)
+    out["grad_mismatches"] = int((g_dp != g_avg).sum())
+    out["grad_max_abs_diff"] = float(np.abs(g_dp - g_avg).max())
+    # full train() through the captured graph (one all-reduce per minibatch)
+    for _ in range(2):
+        model.collect()
+        model.train(2)
+    mine = weights_digest(model)
+    digests = [None] * world
+    dist.all_gather_object(digests, mine)
+    out["ranks_identical"] = all(d == mine for d in digests)
+    st = model.last_stats()
+    out["stats_finite"] = bool(all(np.isfinite(v) for v in st.values()))
+    solo.close()
+    gym1.close()
+    model.close()  # releases the train graph that holds the NCCL calls
+    gym.close()
+    destroy_comm(comm)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", choices=["cpu", "gpu"], required=True)
+    args = ap.parse_args()
+    import torch.distributed as dist
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    try:
+        out = run_cpu(rank, world, dist) if args.mode == "cpu" else run_gpu(rank, world, local, dist)
+        results = [None] * world
+        dist.all_gather_object(results, out)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+    ok = all(v is True or (k == "grad_mismatches" and v == 0) or k == "grad_max_abs_diff"
+             for r in results for k, v in r.items())
+    if rank == 0:
+        print(json.dumps({"ok": ok, "world": world, "ranks": results}), flush=True)
+    sys.exit(0 if ok else 1)
+
+
+if __name__ == "__main__":
+    main()

@@ -260,6 +260,61 @@ def test_row_mode_loop_runs_and_learns(mg):
     assert model.step_counter() == 10 * 4 * 64 + 32
 
 
+def test_train_rows_matches_oracle_voxelnav_widths(mg, oracle):
+    """A row-mode minibatch at the VoxelNav policy widths of the scale-out
+    configuration (embed 256, hidden 1024, 4 blocks, 40 observations, 6
+    actions) against the oracle, on a small rollout."""
+    from metalgym_b200.session import minibatch_rows
+
+    R, T, E, s, L, B = 512, 4, 256, 4, 4, 256
+    gym, model = make("rollout_voxelnav", R, E, s, L, T, seed=5)
+    model.collect()
+    model.minibatch_rows = B
+    om = oracle_model(oracle, model, 5)
+    copy_optimiser_state(oracle, om, model)
+    key, base = [11, 22, 33, 44], 2 * B
+    idx = minibatch_rows(key, base, B, T * R).astype(np.int64)
+    t, i = idx // R, idx % R
+    cols = [np.ascontiguousarray(model.slots(k)[t, i]) for k in ("obs", "actions", "adv", "ret", "logp")]
+    stats = np.zeros((B, 5), np.float32)
+    nsq = np.zeros(1, np.float32)
+    m0 = model.download("master").view(np.float32).copy()
+    oracle.orc_model_set_step_counter(om, model.step_counter())
+    oracle.orc_model_train_minibatch(om, *[ptr(c) for c in cols], B, ptr(stats), ptr(nsq))
+    model.train_rows(key, base)
+    compare_minibatch(oracle, om, model, stats, nsq, m0)
+    oracle.orc_model_destroy(om)
+
+
+def test_config4_continuous_full_size(mg):
+    """CartPoleContinuous at its benchmark shape: 16384 envs, T = 32, embed
+    128, 2 blocks, 8192-row minibatches (64 per epoch), 4 epochs."""
+    gym, model = make("rollout_cartpole_continuous", 16384, 128, 4, 2, 32)
+    model.minibatch_rows = 8192
+    for it in range(3):
+        model.collect()
+        model.train(4)
+        st = model.last_stats()
+        assert all(np.isfinite(v) for v in st.values()), st
+    assert model.step_counter() == 3 * 4 * 64
+    assert np.isfinite(model.log_std_value(0))
+
+
+def test_config5_voxelnav_full_size(mg):
+    """VoxelNav at the scale-out shape of one GPU: 262144 envs, T = 32,
+    embed 256, hidden 1024, 4 blocks, 32768-row minibatches (256 per epoch):
+    one collect and one epoch."""
+    gym, model = make("rollout_voxelnav", 262144, 256, 4, 4, 32)
+    model.minibatch_rows = 32768
+    model.collect()
+    adv = model.slots("adv")
+    assert np.isfinite(adv).all() and adv.std() > 0
+    model.train(1)
+    st = model.last_stats()
+    assert all(np.isfinite(v) for v in st.values()), st
+    assert model.step_counter() == 256
+
+
 def test_row_mode_rejects_non_dividing_rows(mg):
     gym, model = make("rollout_cartpole", 1000, 64, 2, 1, 4)
     from metalgym_b200 import MgError
