@@ -190,7 +190,7 @@ int mg_gae(const float* reward, const uint8_t* done, const float* value, const v
  * model/gae.metal:42-77). */
 int mg_advantage_stats(const float* adv, float* stats_out, int rows, int slots, mg_stream_t stream);
 /* out[i] = sum_p partial[p * part_stride + i] (rounded to bf16 if round_bf16),
- * and per-256-element sums of squares into norm_partial
+ * and per-1024-element sums of squares into norm_partial
  * (mg_reduce_partials_num_norm_partials(count) floats). Replaces
  * reducePartials (model/elementwise.metal:21-31) and gradNormSq
  * (model/optimizer.metal:23-34). */
@@ -349,7 +349,7 @@ int mg_host_free(void* p);
  * (MG_WEIGHT_GRAD_NOALLOC_SCRATCH_BYTES on every GPU that loads it, held
  * until the process exits) and calls no allocator. Sizes whose scratch need
  * (effective splits x in_features x out_features x 4 bytes, plus 4 bytes
- * per 256 outputs) exceeds that are rejected with MG_ERR_ARGUMENT. The
+ * per 1024 outputs) exceeds that are rejected with MG_ERR_ARGUMENT. The
  * first call on a device looks up the scratch address on that device; make
  * that first call before any stream capture. All calls share the scratch and
  * it keeps the last call's contents (every call overwrites what it reads), so

@@ -241,7 +241,7 @@ PpoEngine::~PpoEngine() {
     freeTrain();
     free_acts(collectActs, true);
     void* ptrs[] = {weights, master, mom, var, grad, obsSlots, actionSlots, logpSlots, valueSlots, rewardSlots,
-                    advSlots, retSlots, doneSlots, advStats, mbAdvStats, normSq, normCounter, statsMean, sched,
+                    advSlots, retSlots, doneSlots, advStats, mbAdvStats, advPartial, advCounter, normSq, normCounter, statsMean, sched,
                     schedBetaPow};
     for (void* p : ptrs) cudaFree(p);
     cudaFreeHost(hostSched);
@@ -352,6 +352,9 @@ int PpoEngine::init() {
     MG_TRY(dalloc(&retSlots, slotCount * 4));
     MG_TRY(dalloc(&advStats, (size_t)T * 2 * 4));
     MG_TRY(dalloc(&mbAdvStats, 2 * 4));
+    MG_TRY(dalloc(&advPartial, (size_t)2 * kAdvStatsMaxCtas * 8));
+    MG_TRY(dalloc(&advCounter, 4));
+    MG_CUDA_TRY(cudaMemset(advCounter, 0, 4));
     MG_CUDA_TRY(cudaMemset(actionSlots, 0, slotCount * actBytes));
     MG_CUDA_TRY(cudaMemset(obsSlots, 0, (size_t)(T + 1) * R * O * 4));
     slotOrder.resize(T);
@@ -576,7 +579,7 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     const LossHyper lh{hp.clip, hp.valueCoef, hp.entropyCoef};
     const float* as = advStats;
     if (rowMode) {
-        MG_TRY(advantage_stats_rows(advSlots, rm, rows, mbAdvStats, st));
+        MG_TRY(advantage_stats_rows(advSlots, rm, rows, mbAdvStats, advPartial, advCounter, st));
         as = mbAdvStats;
     }
     if (cont)

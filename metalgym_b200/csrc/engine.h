@@ -121,6 +121,8 @@ class PpoEngine {
     uint8_t* doneSlots = nullptr;
     float* advStats = nullptr;    // T x {mean, inv}
     float* mbAdvStats = nullptr;  // {mean, inv} of the current row-mode minibatch
+    double* advPartial = nullptr;           // its per-CTA sums
+    unsigned int* advCounter = nullptr;     // last-CTA detection
     // activations
     ActSet collectActs, trainActs;
     void *dLogits = nullptr, *dStream = nullptr, *dBranch = nullptr, *dV = nullptr;

@@ -58,7 +58,7 @@ extern "C" int mg_weight_grad_noalloc(const void* x, const void* dz, int rows, i
                  "mg_weight_grad_noalloc: in_features must be a multiple of 8 and out_features of 32");
     const int nsplit = mg::gemm_effective_splits(rows, splits);
     const size_t count = (size_t)in_features * out_features;
-    const size_t normParts = (count + 255) / 256;
+    const size_t normParts = (count + mg::kGradPerCta - 1) / mg::kGradPerCta;
     const size_t need = ((size_t)nsplit * count + normParts) * sizeof(float);
     if (need > kScratchBytes)
         return mg::fail(MG_ERR_ARGUMENT, "mg_weight_grad_noalloc: needs " + std::to_string(need) +
@@ -95,6 +95,6 @@ extern "C" int mg_weight_grad_noalloc(const void* x, const void* dz, int rows, i
     tab.seg[0].count = (int64_t)count;
     tab.seg[0].dstOffset = 0;
     tab.seg[0].roundBf16 = round_bf16 ? 1 : 0;
-    mg::grad_table_layout(tab);
+    mg::grad_table_layout(tab, false);  // one norm partial per 1024 elements
     return mg::grad_finalize(tab, dw_out, scratch + (size_t)nsplit * count, st);
 }

@@ -10,92 +10,134 @@ namespace mg {
 
 namespace {
 
-constexpr int kLnRowsPerCta = 8;        // LayerNorm backward: rows per CTA (one row per warp)
-constexpr int kInputRowChunk = 16;      // input backward: rows loaded per unrolled step
-constexpr int64_t kInputPartialBudget = 8 << 20;  // bytes of input-backward partials at most
+constexpr int kMaxRowParts = 296;       // row-reduction kernels: at most two partial sums per SM
+constexpr int64_t kInputPartialBudget = 32 << 20;  // bytes of input-backward partials at most
+constexpr int kInputSmemBudget = 96 * 1024;        // bytes of staged rows per input-backward CTA
 constexpr int kGaussRowsPerCta = 256;  // Gaussian loss: rows per CTA
 
 // ------------------------------------------------------------------ input
 
 // model/input.metal:11-27: out[r, c] = bf16(b[c] + sum_k obs[r, k] * W[k, c]),
-// summed in k order with separate roundings. One warp per row.
-template <int VPT>
-__global__ void k_input_forward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ w,
-                                const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int rows,
-                                int inDim, int outDim, RowMap rm) {
+// summed in k order with separate roundings. W sits in shared memory as
+// fp32; each warp computes RPW rows at a time (their observations staged in
+// shared memory), lane l owning the column pairs 2l + 64j, so every weight
+// read serves RPW rows and the shared-memory reads are conflict-free.
+template <int VPT, int RPW>
+__global__ void __launch_bounds__(256) k_input_forward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ w,
+                                                       const __nv_bfloat16* __restrict__ bias,
+                                                       __nv_bfloat16* __restrict__ out, int rows, int inDim, int outDim,
+                                                       RowMap rm) {
+    constexpr int NP = VPT / 2;  // column pairs per lane
     mg_pdl_trigger();
     mg_pdl_wait();
-    extern __shared__ float s_w[];  // inDim x outDim as fp32
-    const MgMinibatch* mb = rm.mb;
+    extern __shared__ float s_w[];  // inDim x outDim as fp32, then per warp RPW x inDim observations
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    float* s_obs = s_w + inDim * outDim + warp * RPW * inDim;
     for (int i = threadIdx.x; i < inDim * outDim; i += blockDim.x) s_w[i] = bf(w[i]);
     __syncthreads();
-    const int lane = threadIdx.x & 31;
-    const int c0 = lane * VPT;
-    float b[VPT];
+    float2 b[NP];
 #pragma unroll
-    for (int j = 0; j < VPT; j++) b[j] = bf(bias[c0 + j]);
-    for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += gridDim.x * (blockDim.x >> 5)) {
-        float acc[VPT];
-#pragma unroll
-        for (int j = 0; j < VPT; j++) acc[j] = b[j];
-        const float* o = obs + (size_t)(mb ? mg_minibatch_row(*mb, r, rm.envRows, rm.total) : (uint64_t)r) * inDim;
-        for (int k = 0; k < inDim; k++) {
-            const float ok = o[k];
-#pragma unroll
-            for (int j = 0; j < VPT; j++) acc[j] = __fadd_rn(acc[j], __fmul_rn(ok, s_w[k * outDim + c0 + j]));
+    for (int j = 0; j < NP; j++) b[j] = make_float2(bf(bias[2 * lane + 64 * j]), bf(bias[2 * lane + 64 * j + 1]));
+    for (int r0 = (blockIdx.x * nwarps + warp) * RPW; r0 < rows; r0 += gridDim.x * nwarps * RPW) {
+        for (int i = lane; i < RPW * inDim; i += 32) {
+            const int r = r0 + i / inDim;
+            float v = 0.0f;
+            if (r < rows) {
+                const uint64_t g = rm.mb ? mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : (uint64_t)r;
+                v = obs[g * inDim + i % inDim];
+            }
+            s_obs[i] = v;
         }
-        __nv_bfloat16* dst = out + (size_t)r * outDim + c0;
+        __syncwarp();
+        float2 acc[RPW][NP];
 #pragma unroll
-        for (int j = 0; j < VPT; j += 2) *reinterpret_cast<__nv_bfloat162*>(dst + j) = __floats2bfloat162_rn(acc[j], acc[j + 1]);
+        for (int q = 0; q < RPW; q++)
+#pragma unroll
+            for (int j = 0; j < NP; j++) acc[q][j] = b[j];
+        for (int k = 0; k < inDim; k++) {
+            float2 wk[NP];
+#pragma unroll
+            for (int j = 0; j < NP; j++) wk[j] = *reinterpret_cast<const float2*>(s_w + k * outDim + 2 * lane + 64 * j);
+#pragma unroll
+            for (int q = 0; q < RPW; q++) {
+                const float o = s_obs[q * inDim + k];
+#pragma unroll
+                for (int j = 0; j < NP; j++) {
+                    acc[q][j].x = __fadd_rn(acc[q][j].x, __fmul_rn(o, wk[j].x));
+                    acc[q][j].y = __fadd_rn(acc[q][j].y, __fmul_rn(o, wk[j].y));
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < RPW; q++) {
+            if (r0 + q >= rows) break;
+            __nv_bfloat16* dst = out + (size_t)(r0 + q) * outDim + 2 * lane;
+#pragma unroll
+            for (int j = 0; j < NP; j++)
+                *reinterpret_cast<__nv_bfloat162*>(dst + 64 * j) = __floats2bfloat162_rn(acc[q][j].x, acc[q][j].y);
+        }
+        __syncwarp();
     }
 }
 
 // model/input.metal:38-60: per-CTA partial sums over a contiguous range of
 // rowsPerCta rows of dW[k, c] = sum_r obs[r, k] dZ[r, c] and db[c] = sum_r
 // dZ[r, c]; partial[blockIdx] = [(inDim + 1) x outDim]: rows 0..inDim-1 dW,
-// row inDim db. One thread per column; 16 rows of dZ are loaded at a time
-// into registers (independent loads), obs rows come from shared memory.
-__global__ void k_input_backward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ dZ,
-                                 float* __restrict__ partial, int rows, int inDim, int outDim, int rowsPerCta,
-                                 RowMap rm) {
+// row inDim db, each summed in row order. The CTA's dZ rows (bf16) and
+// observation rows (fp32, gathered through the row map) are staged in
+// shared memory; a thread owns a column and sweeps k in chunks of 8
+// registers.
+__global__ void __launch_bounds__(256) k_input_backward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ dZ,
+                                                        float* __restrict__ partial, int rows, int inDim, int outDim,
+                                                        int rowsPerCta, RowMap rm) {
     mg_pdl_trigger();
     mg_pdl_wait();
-    extern __shared__ float s_obs[];  // rowsPerCta x inDim
+    extern __shared__ float s_obs[];  // rowsPerCta x inDim fp32, then rowsPerCta x outDim bf16
     const int r0 = blockIdx.x * rowsPerCta;
     const int nr = min(rowsPerCta, rows - r0);
+    __nv_bfloat16* s_dz = reinterpret_cast<__nv_bfloat16*>(s_obs + rowsPerCta * inDim);
     for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) {
         const int r = r0 + i / inDim;
         const uint64_t g = rm.mb ? mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : (uint64_t)r;
         s_obs[i] = obs[g * inDim + i % inDim];
     }
+    {
+        // dZ rows r0 .. r0 + nr are contiguous: 16-byte copies
+        const uint4* src = reinterpret_cast<const uint4*>(dZ + (size_t)r0 * outDim);
+        uint4* dst = reinterpret_cast<uint4*>(s_dz);
+        const int n16 = nr * outDim / 8;
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
+    }
     __syncthreads();
     float* part = partial + (size_t)blockIdx.x * (inDim + 1) * outDim;
     for (int c = threadIdx.x; c < outDim; c += blockDim.x) {
         float accB = 0.0f;
+        for (int r = 0; r < nr; r++) accB = __fadd_rn(accB, bf(s_dz[r * outDim + c]));
+        part[(size_t)inDim * outDim + c] = accB;
         for (int k0 = 0; k0 < inDim; k0 += 8) {
             float acc[8];
 #pragma unroll
             for (int k = 0; k < 8; k++) acc[k] = 0.0f;
-            for (int rb = 0; rb < nr; rb += kInputRowChunk) {
-                float d[kInputRowChunk];
+            if (k0 + 8 <= inDim) {
+                for (int r = 0; r < nr; r++) {
+                    const float d = bf(s_dz[r * outDim + c]);
+                    const float* o = s_obs + r * inDim + k0;
 #pragma unroll
-                for (int i = 0; i < kInputRowChunk; i++)
-                    d[i] = (rb + i < nr) ? bf(dZ[(size_t)(r0 + rb + i) * outDim + c]) : 0.0f;
-#pragma unroll
-                for (int i = 0; i < kInputRowChunk; i++) {
-                    if (rb + i >= nr) break;
-                    if (k0 == 0) accB = __fadd_rn(accB, d[i]);
-                    const float* o = s_obs + (rb + i) * inDim + k0;
+                    for (int k = 0; k < 8; k++) acc[k] = __fadd_rn(acc[k], __fmul_rn(o[k], d));
+                }
+            } else {
+                for (int r = 0; r < nr; r++) {
+                    const float d = bf(s_dz[r * outDim + c]);
+                    const float* o = s_obs + r * inDim + k0;
 #pragma unroll
                     for (int k = 0; k < 8; k++)
-                        if (k0 + k < inDim) acc[k] = __fadd_rn(acc[k], __fmul_rn(o[k], d[i]));
+                        if (k0 + k < inDim) acc[k] = __fadd_rn(acc[k], __fmul_rn(o[k], d));
                 }
             }
 #pragma unroll
             for (int k = 0; k < 8; k++)
                 if (k0 + k < inDim) part[(size_t)(k0 + k) * outDim + c] = acc[k];
         }
-        part[(size_t)inDim * outDim + c] = accB;
     }
 }
 
@@ -166,7 +208,7 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
                                                             const __nv_bfloat16* __restrict__ gamma,
                                                             const float* __restrict__ stdev,
                                                             __nv_bfloat16* __restrict__ resid,
-                                                            float* __restrict__ partial, int rows) {
+                                                            float* __restrict__ partial, int rows, int rowsPerCta) {
     mg_pdl_trigger();
     mg_pdl_wait();
     constexpr int E = VPT * 32;
@@ -181,8 +223,8 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
         dg[j] = 0.0f;
         db[j] = 0.0f;
     }
-    const int r0 = blockIdx.x * kLnRowsPerCta;
-    const int r1 = min(rows, r0 + kLnRowsPerCta);
+    const int r0 = blockIdx.x * rowsPerCta;
+    const int r1 = min(rows, r0 + rowsPerCta);
 #pragma unroll 2
     for (int r = r0 + warp; r < r1; r += 8) {
         float dz[VPT], xn[VPT], dxn[VPT];
@@ -500,42 +542,55 @@ __global__ void __launch_bounds__(1024) k_adv_stats(const float* __restrict__ ad
 }
 
 // The same statistics over the rows of one row-mode minibatch, gathered
-// through its row map; one CTA.
-__global__ void __launch_bounds__(1024) k_adv_stats_rows(const float* __restrict__ adv, RowMap rm, int rows,
-                                                         float* __restrict__ out) {
+// through its row map: every CTA sums its rows' values and squares in fp64,
+// the last CTA to finish adds the CTA sums in index order (deterministic)
+// and writes {mean, 1/(std + 1e-8)}.
+__global__ void __launch_bounds__(256) k_adv_stats_rows(const float* __restrict__ adv, RowMap rm, int rows,
+                                                        float* __restrict__ out, double* __restrict__ part,
+                                                        unsigned int* __restrict__ counter) {
     mg_pdl_trigger();
     mg_pdl_wait();
-    __shared__ float s_part[32];
-    __shared__ float s_mean;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    float s = 0.0f;
-    for (int q = threadIdx.x; q < rows; q += blockDim.x)
-        s = __fadd_rn(s, adv[mg_minibatch_row(*rm.mb, q, rm.envRows, rm.total)]);
-    s = warp_sum(s);
-    if (lane == 0) s_part[warp] = s;
-    __syncthreads();
-    if (warp == 0) {
-        float t = lane < nw ? s_part[lane] : 0.0f;
-        t = warp_sum(t);
-        if (lane == 0) s_mean = __fdiv_rn(t, (float)rows);
+    __shared__ double s_a[8], s_b[8];
+    __shared__ bool s_last;
+    double a = 0.0, b = 0.0;
+    for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < rows; q += gridDim.x * blockDim.x) {
+        const double v = adv[mg_minibatch_row(*rm.mb, q, rm.envRows, rm.total)];
+        a += v;
+        b += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, o);
+        b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        s_a[warp] = a;
+        s_b[warp] = b;
     }
     __syncthreads();
-    const float mean = s_mean;
-    float v = 0.0f;
-    for (int q = threadIdx.x; q < rows; q += blockDim.x) {
-        const float d = __fsub_rn(adv[mg_minibatch_row(*rm.mb, q, rm.envRows, rm.total)], mean);
-        v = __fadd_rn(v, __fmul_rn(d, d));
-    }
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) s_part[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        float t = lane < nw ? s_part[lane] : 0.0f;
-        t = warp_sum(t);
-        if (lane == 0) {
-            out[0] = mean;
-            out[1] = __fdiv_rn(1.0f, __fadd_rn(__fsqrt_rn(__fdiv_rn(t, (float)rows)), 1e-8f));
+    if (threadIdx.x == 0) {
+        double ta = 0.0, tb = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
+            ta += s_a[w];
+            tb += s_b[w];
+        }
+        part[2 * blockIdx.x] = ta;
+        part[2 * blockIdx.x + 1] = tb;
+        __threadfence();
+        s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+        if (s_last) {
+            __threadfence();
+            double sa = 0.0, sb = 0.0;
+            for (int k = 0; k < (int)gridDim.x; k++) {
+                sa += __ldcg(&part[2 * k]);
+                sb += __ldcg(&part[2 * k + 1]);
+            }
+            const double mean = sa / rows;
+            const double var = fmax(sb / rows - mean * mean, 0.0);
+            out[0] = (float)mean;
+            out[1] = __fdiv_rn(1.0f, __fadd_rn(__fsqrt_rn((float)var), 1e-8f));
+            *counter = 0u;  // ready for the next launch
         }
     }
 }
@@ -559,25 +614,96 @@ __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ G
     while (si < tab.n - 1 && b >= tab.seg[si].blockEnd) si++;
     const GradSegment& sg = tab.seg[si];
     const int blockBase = si == 0 ? 0 : tab.seg[si - 1].blockEnd;
-    const int64_t i = (int64_t)(b - blockBase) * 256 + threadIdx.x;
+    const int64_t st = sg.partStride;
     float sq = 0.0f;
-    if (i < sg.count) {
-        // sum of the partials in increasing p, with 8 loads in flight at a time
+    if (sg.deep) {
+        // many partials: 128 elements per CTA, warp w sums partials w, w + 8,
+        // ...; warp 0 adds the eight warp sums in warp order
+        __shared__ float4 s_dp[8][32];
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        const int64_t i = (int64_t)(b - blockBase) * kGradPerCtaDeep + lane * 4;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < sg.count) {
+            const bool v4 = sg.vec4 && i + 3 < sg.count;
+            int p = warp;
+            for (; p + 24 < sg.nparts && v4; p += 32) {
+                float4 v[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) v[q] = *reinterpret_cast<const float4*>(sg.src + (int64_t)(p + 8 * q) * st + i);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    acc.x = __fadd_rn(acc.x, v[q].x);
+                    acc.y = __fadd_rn(acc.y, v[q].y);
+                    acc.z = __fadd_rn(acc.z, v[q].z);
+                    acc.w = __fadd_rn(acc.w, v[q].w);
+                }
+            }
+            for (; p < sg.nparts; p += 8) {
+                const float* src = sg.src + (int64_t)p * st + i;
+                acc.x = __fadd_rn(acc.x, src[0]);
+                if (i + 1 < sg.count) acc.y = __fadd_rn(acc.y, src[1]);
+                if (i + 2 < sg.count) acc.z = __fadd_rn(acc.z, src[2]);
+                if (i + 3 < sg.count) acc.w = __fadd_rn(acc.w, src[3]);
+            }
+        }
+        s_dp[warp][lane] = acc;
+        __syncthreads();
+        if (warp == 0 && i < sg.count) {
+            float4 t = s_dp[0][lane];
+            for (int w = 1; w < 8; w++) {
+                const float4 u = s_dp[w][lane];
+                t.x = __fadd_rn(t.x, u.x);
+                t.y = __fadd_rn(t.y, u.y);
+                t.z = __fadd_rn(t.z, u.z);
+                t.w = __fadd_rn(t.w, u.w);
+            }
+            if (sg.roundBf16) t = make_float4(rbf(t.x), rbf(t.y), rbf(t.z), rbf(t.w));
+            const float tv[4] = {t.x, t.y, t.z, t.w};
+            for (int e = 0; e < 4 && i + e < sg.count; e++) {
+                grad[sg.dstOffset + i + e] = tv[e];
+                sq = __fadd_rn(sq, __fmul_rn(tv[e], tv[e]));
+            }
+        }
+    } else if (sg.vec4 && (int64_t)(b - blockBase) * kGradPerCta + threadIdx.x * 4 + 3 < sg.count) {
+        // each thread sums 4 consecutive elements over the partials, in increasing p
+        const int64_t i = (int64_t)(b - blockBase) * kGradPerCta + threadIdx.x * 4;
         const float* src = sg.src + i;
-        const int64_t st = sg.partStride;
-        float acc = 0.0f;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         int p = 0;
         for (; p + 8 <= sg.nparts; p += 8) {
-            float v[8];
+            float4 v[8];
 #pragma unroll
-            for (int q = 0; q < 8; q++) v[q] = src[(int64_t)(p + q) * st];
+            for (int q = 0; q < 8; q++) v[q] = *reinterpret_cast<const float4*>(src + (int64_t)(p + q) * st);
 #pragma unroll
-            for (int q = 0; q < 8; q++) acc = __fadd_rn(acc, v[q]);
+            for (int q = 0; q < 8; q++) {
+                acc.x = __fadd_rn(acc.x, v[q].x);
+                acc.y = __fadd_rn(acc.y, v[q].y);
+                acc.z = __fadd_rn(acc.z, v[q].z);
+                acc.w = __fadd_rn(acc.w, v[q].w);
+            }
         }
-        for (; p < sg.nparts; p++) acc = __fadd_rn(acc, src[(int64_t)p * st]);
-        if (sg.roundBf16) acc = rbf(acc);
-        grad[sg.dstOffset + i] = acc;
-        sq = __fmul_rn(acc, acc);
+        for (; p < sg.nparts; p++) {
+            const float4 v = *reinterpret_cast<const float4*>(src + (int64_t)p * st);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        if (sg.roundBf16) acc = make_float4(rbf(acc.x), rbf(acc.y), rbf(acc.z), rbf(acc.w));
+        *reinterpret_cast<float4*>(grad + sg.dstOffset + i) = acc;
+        sq = __fadd_rn(__fadd_rn(__fmul_rn(acc.x, acc.x), __fmul_rn(acc.y, acc.y)),
+                       __fadd_rn(__fmul_rn(acc.z, acc.z), __fmul_rn(acc.w, acc.w)));
+    } else {
+        const int64_t i = (int64_t)(b - blockBase) * kGradPerCta + threadIdx.x * 4;
+        for (int e = 0; e < 4; e++) {
+            if (i + e >= sg.count) break;
+            const float* src = sg.src + i + e;
+            float acc = 0.0f;
+            for (int p = 0; p < sg.nparts; p++) acc = __fadd_rn(acc, src[(int64_t)p * st]);
+            if (sg.roundBf16) acc = rbf(acc);
+            grad[sg.dstOffset + i + e] = acc;
+            sq = __fadd_rn(sq, __fmul_rn(acc, acc));
+        }
     }
     sq = warp_sum(sq);
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = sq;
@@ -738,33 +864,39 @@ int input_forward(const float* obs, const void* w, const void* b, void* out, int
                   cudaStream_t st, RowMap rm) {
     MG_CHECK_ARG(rows > 0 && inDim > 0 && outDim % 64 == 0 && outDim <= 1024, "input_forward: bad shape");
     MG_CHECK_ARG(inDim * outDim * 4 <= 160 * 1024, "input_forward: weight too large for shared memory");
-    const int blocks = std::min(grid_rows(rows, 8), 148 * 8);
-    const size_t sm = (size_t)inDim * outDim * 4;
     auto W = static_cast<const __nv_bfloat16*>(w);
     auto B = static_cast<const __nv_bfloat16*>(b);
     auto O = static_cast<__nv_bfloat16*>(out);
-#define MG_IN_FWD(V)                                                                               \
-    case V:                                                                                        \
-        if (sm > 48 * 1024)                                                                        \
-            MG_CUDA_TRY(cudaFuncSetAttribute(k_input_forward<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)); \
-        MG_LAUNCH(k_input_forward<V>, blocks, 256, sm, st, obs, W, B, O, rows, inDim, outDim, rm); \
-        break;
+#define MG_IN_FWD(V, RPW)                                                                                     \
+    case V: {                                                                                                 \
+        const size_t sm = ((size_t)inDim * outDim + 8 * RPW * inDim) * 4;                                     \
+        const int blocks = std::min(grid_rows(rows, 8 * RPW), 148 * 4);                                       \
+        auto kern = &k_input_forward<V, RPW>;                                                                 \
+        if (sm > 48 * 1024)                                                                                   \
+            MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));    \
+        MG_LAUNCH(kern, blocks, 256, sm, st, obs, W, B, O, rows, inDim, outDim, rm);                          \
+        break;                                                                                                \
+    }
     switch (outDim / 32) {
-        MG_IN_FWD(2) MG_IN_FWD(4) MG_IN_FWD(8) MG_IN_FWD(16) MG_IN_FWD(32)
+        MG_IN_FWD(2, 4) MG_IN_FWD(4, 4) MG_IN_FWD(8, 4) MG_IN_FWD(16, 2) MG_IN_FWD(32, 1)
         default: return fail(MG_ERR_ARGUMENT, "input_forward: out_dim must be 64, 128, 256, 512 or 1024");
     }
 #undef MG_IN_FWD
     return check_launch("k_input_forward");
 }
 
-// Rows per CTA of the input backward: 16, or more when the partial sums of
-// that many CTAs would exceed kInputPartialBudget bytes.
+// Rows per CTA of the input backward: at least 16, a multiple of 8, enough
+// to keep the partial sums at kMaxRowParts or fewer and within
+// kInputPartialBudget bytes, as far as kInputSmemBudget bytes of staged rows
+// allow.
 static int input_rows_per_cta(int rows, int inDim, int outDim) {
     const int64_t perPart = (int64_t)(inDim + 1) * outDim * 4;
-    const int64_t maxParts = std::max<int64_t>(1, kInputPartialBudget / perPart);
-    int rpc = kInputRowChunk;
-    while ((rows + rpc - 1) / rpc > maxParts) rpc += kInputRowChunk;
-    return rpc;
+    const int64_t maxParts = std::max<int64_t>(1, std::min<int64_t>(kMaxRowParts, kInputPartialBudget / perPart));
+    const int perRowSmem = inDim * 4 + outDim * 2;
+    const int maxRpc = std::max(8, (int)(kInputSmemBudget / perRowSmem) / 8 * 8);
+    int rpc = std::max<int64_t>(16, (rows + maxParts - 1) / maxParts);
+    rpc = (rpc + 7) / 8 * 8;
+    return std::min(rpc, maxRpc);
 }
 
 int input_backward_parts(int rows, int inDim, int outDim) {
@@ -773,13 +905,15 @@ int input_backward_parts(int rows, int inDim, int outDim) {
 
 int input_backward(const float* obs, const void* dZ, float* partial, int rows, int inDim, int outDim,
                    cudaStream_t st, RowMap rm) {
-    MG_CHECK_ARG(rows > 0 && inDim > 0 && inDim <= 256 && outDim > 0 && outDim <= 1024, "input_backward: bad shape");
+    MG_CHECK_ARG(rows > 0 && inDim > 0 && inDim <= 256 && outDim > 0 && outDim <= 1024 && outDim % 8 == 0,
+                 "input_backward: bad shape");
+    MG_CHECK_ARG((reinterpret_cast<uintptr_t>(dZ) & 15) == 0, "input_backward: dZ must be 16-byte aligned");
     const int rpc = input_rows_per_cta(rows, inDim, outDim);
-    const size_t sm = (size_t)rpc * inDim * 4;
-    MG_CHECK_ARG(sm <= 200 * 1024, "input_backward: rows per CTA x in_dim too large for shared memory");
+    const size_t sm = (size_t)rpc * inDim * 4 + (size_t)rpc * outDim * 2;
+    MG_CHECK_ARG(sm <= 200 * 1024, "input_backward: rows per CTA x widths too large for shared memory");
     if (sm > 48 * 1024)
         MG_CUDA_TRY(cudaFuncSetAttribute(k_input_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    MG_LAUNCH(k_input_backward, grid_rows(rows, rpc), std::min(outDim, 1024), sm, st, 
+    MG_LAUNCH(k_input_backward, grid_rows(rows, rpc), std::min(outDim, 256), sm, st,
         obs, static_cast<const __nv_bfloat16*>(dZ), partial, rows, inDim, outDim, rpc, rm);
     return check_launch("k_input_backward");
 }
@@ -804,21 +938,29 @@ int layernorm_forward(const void* x, void* xNorm, void* out, const void* gamma, 
     return check_launch("k_layernorm_forward");
 }
 
-int layernorm_backward_parts(int rows) { return grid_rows(rows, kLnRowsPerCta); }
+// Rows per CTA of the LayerNorm backward: a multiple of 8 (one row per warp
+// at a time) that keeps the partial sums at kMaxRowParts or fewer.
+static int ln_rows_per_cta(int rows) {
+    const int rpc = std::max(8, (rows + kMaxRowParts - 1) / kMaxRowParts);
+    return (rpc + 7) / 8 * 8;
+}
+
+int layernorm_backward_parts(int rows) { return grid_rows(rows, ln_rows_per_cta(rows)); }
 
 int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, void* resid,
                        float* partial, int rows, int cols, cudaStream_t st) {
     MG_CHECK_ARG(rows > 0, "layernorm_backward: rows must be > 0");
-    const int blocks = layernorm_backward_parts(rows);
+    const int rpc = ln_rows_per_cta(rows);
+    const int blocks = grid_rows(rows, rpc);
     auto DZ = static_cast<__nv_bfloat16*>(dZ);
     auto XN = static_cast<const __nv_bfloat16*>(xNorm);
     auto G = static_cast<const __nv_bfloat16*>(gamma);
     auto R = static_cast<__nv_bfloat16*>(resid);
     switch (cols) {
-        case 64: MG_LAUNCH(k_layernorm_backward<2>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows); break;
-        case 128: MG_LAUNCH(k_layernorm_backward<4>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows); break;
-        case 256: MG_LAUNCH(k_layernorm_backward<8>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows); break;
-        case 512: MG_LAUNCH(k_layernorm_backward<16>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows); break;
+        case 64: MG_LAUNCH(k_layernorm_backward<2>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows, rpc); break;
+        case 128: MG_LAUNCH(k_layernorm_backward<4>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows, rpc); break;
+        case 256: MG_LAUNCH(k_layernorm_backward<8>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows, rpc); break;
+        case 512: MG_LAUNCH(k_layernorm_backward<16>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows, rpc); break;
         default: return fail(MG_ERR_ARGUMENT, "layernorm_backward: cols must be 64, 128, 256 or 512");
     }
     return check_launch("k_layernorm_backward");
@@ -872,9 +1014,11 @@ int gae(const float* reward, const uint8_t* done, const float* value, const void
     return check_launch("k_gae");
 }
 
-int advantage_stats_rows(const float* adv, RowMap rm, int rows, float* out, cudaStream_t st) {
-    MG_CHECK_ARG(rm.mb && rows > 0, "advantage_stats_rows: needs a row map");
-    MG_LAUNCH(k_adv_stats_rows, 1, 1024, 0, st, adv, rm, rows, out);
+int advantage_stats_rows(const float* adv, RowMap rm, int rows, float* out, double* partial,
+                         unsigned int* counter, cudaStream_t st) {
+    MG_CHECK_ARG(rm.mb && rows > 0 && partial && counter, "advantage_stats_rows: needs a row map and scratch");
+    const int blocks = std::min(kAdvStatsMaxCtas, (rows + 255) / 256);
+    MG_LAUNCH(k_adv_stats_rows, blocks, 256, 0, st, adv, rm, rows, out, partial, counter);
     return check_launch("k_adv_stats_rows");
 }
 
@@ -884,20 +1028,30 @@ int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStrea
     return check_launch("k_adv_stats");
 }
 
-int grad_table_layout(GradSegmentTable& tab) {
+int grad_table_layout(GradSegmentTable& tab, bool allowDeep) {
     int b = 0;
     for (int i = 0; i < tab.n; i++) {
-        b += (int)((tab.seg[i].count + 255) / 256);
-        tab.seg[i].blockEnd = b;
+        GradSegment& g = tab.seg[i];
+        g.deep = allowDeep && g.nparts > kGradDeepParts ? 1 : 0;
+        const int per = g.deep ? kGradPerCtaDeep : kGradPerCta;
+        b += (int)((g.count + per - 1) / per);
+        g.blockEnd = b;
     }
     return b;
 }
 
-int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st,
+int grad_finalize(const GradSegmentTable& table, float* grad, float* normPartial, cudaStream_t st,
                   unsigned int* counter, float* normSqOut) {
-    MG_CHECK_ARG(tab.n > 0 && tab.n <= kMaxGradSegments, "grad_finalize: bad segment count");
-    const int nblocks = tab.seg[tab.n - 1].blockEnd;
+    MG_CHECK_ARG(table.n > 0 && table.n <= kMaxGradSegments, "grad_finalize: bad segment count");
+    const int nblocks = table.seg[table.n - 1].blockEnd;
     MG_CHECK_ARG(nblocks > 0, "grad_finalize: empty");
+    // 16-byte loads and stores where every address of the segment allows them
+    GradSegmentTable tab = table;
+    for (int k = 0; k < tab.n; k++) {
+        GradSegment& g = tab.seg[k];
+        g.vec4 = (reinterpret_cast<uintptr_t>(g.src) % 16 == 0) && g.partStride % 4 == 0 && g.dstOffset % 4 == 0 &&
+                 (reinterpret_cast<uintptr_t>(grad) % 16 == 0);
+    }
     MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, normPartial, counter, normSqOut);
     return check_launch("k_grad_finalize");
 }
@@ -1011,11 +1165,11 @@ int mg_reduce_partials(const float* partial, int64_t part_stride, int nparts, in
     tab.seg[0].count = count;
     tab.seg[0].dstOffset = 0;
     tab.seg[0].roundBf16 = round_bf16;
-    mg::grad_table_layout(tab);
+    mg::grad_table_layout(tab, false);  // one norm partial per 1024 elements
     return mg::grad_finalize(tab, out, norm_partial, MG_STREAM(s));
 }
 
-int mg_reduce_partials_num_norm_partials(int64_t count) { return (int)((count + 255) / 256); }
+int mg_reduce_partials_num_norm_partials(int64_t count) { return (int)((count + mg::kGradPerCta - 1) / mg::kGradPerCta); }
 
 int mg_adam_step(float* master, const float* grad, float* momentum, float* variance, void* weights,
                  const float* norm_partial, int n_norm_partials, int64_t count, float lr, float beta1_pow,

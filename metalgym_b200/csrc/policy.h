@@ -33,8 +33,18 @@ struct GradSegment {
     int nparts;
     int roundBf16;  // 1: round the sum to bf16 (GEMM weight gradients)
     int blockEnd;   // filled by grad_table_layout
+    int deep;       // filled by grad_table_layout: nparts > kGradDeepParts
+    int vec4;       // set by grad_finalize: 16-byte aligned addresses and strides
     int pad;
 };
+
+// Gradient elements per CTA of the finalisation (one norm partial each):
+// kGradPerCta for segments of few partials (a thread sums 4 elements over
+// all partials), kGradPerCtaDeep for segments of more than kGradDeepParts
+// partials (the CTA's 8 warps split the partials of 128 elements).
+constexpr int kGradPerCta = 1024;
+constexpr int kGradPerCtaDeep = 128;
+constexpr int kGradDeepParts = 32;
 
 constexpr int kMaxGradSegments = 40;
 struct GradSegmentTable {
@@ -76,10 +86,14 @@ int gaussian_loss(const void* head, const float* action, const float* adv, const
 int gae(const float* reward, const uint8_t* done, const float* value, const void* bootHead, float* adv, float* ret,
         int rows, int horizon, int actDim, float gamma, float lambda, cudaStream_t st);
 int advantage_stats(const float* adv, float* out, int rows, int slots, cudaStream_t st);
-// {mean, 1/(std + 1e-8)} of adv over the rows of one row-mode minibatch.
-int advantage_stats_rows(const float* adv, RowMap rm, int rows, float* out, cudaStream_t st);
-// Fills blockEnd of every segment; returns the number of CTAs (= norm partials).
-int grad_table_layout(GradSegmentTable& tab);
+// {mean, 1/(std + 1e-8)} of adv over the rows of one row-mode minibatch;
+// scratch: 2 x kAdvStatsMaxCtas doubles and a zeroed counter (left zeroed).
+constexpr int kAdvStatsMaxCtas = 296;
+int advantage_stats_rows(const float* adv, RowMap rm, int rows, float* out, double* partial,
+                         unsigned int* counter, cudaStream_t st);
+// Fills blockEnd (and deep, when allowDeep) of every segment; returns the
+// number of CTAs (= norm partials).
+int grad_table_layout(GradSegmentTable& tab, bool allowDeep = true);
 // With counter (a zeroed device word) and normSqOut, the last CTA also sums
 // the per-CTA partials into *normSqOut and re-zeroes the counter.
 int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st,
