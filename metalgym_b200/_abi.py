@@ -21,6 +21,7 @@ SIGNATURES = {
     "mg_device_status": (I, [I, PI]),
     # GEMM
     "mg_gemm_bf16": (I, [P, I, I, P, I, I, I, I, I, I, P, I, P, I, I, P]),
+    "mg_gemm_bf16_tiled": (I, [P, I, I, P, I, I, I, I, I, I, P, I, P, I, I, I, I, P]),
     # environments
     "mg_env_register": (I, [P]),
     "mg_env_find": (P, [S]),

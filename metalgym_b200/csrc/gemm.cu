@@ -1,6 +1,7 @@
 // Host launcher for the tcgen05 GEMM engine (gemm_tc.cuh) and its C ABI.
 #include "gemm.h"
 #include "gemm_tc.cuh"
+#include "gemm_tc_persist.cuh"
 #include "runtime.h"
 
 namespace mg {
@@ -23,8 +24,38 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
     return check_launch("gemm_tc_kernel");
 }
 
+// The persistent kernel: one CTA per SM (or fewer when there are fewer units).
+template <int BN, bool AMN, bool BMN, int EPI>
+int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits,
+                      cudaStream_t st) {
+    using S = PersistShape<BN>;
+    auto kern = gemm_tc_persistent<BN, AMN, BMN, EPI>;
+    static uint64_t attr_done = 0;  // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done & (1ull << (dev & 63)))) {
+        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES));
+        attr_done |= 1ull << (dev & 63);
+    }
+    const int units = p.tilesM * p.tilesN * splits;
+    const int grid = std::min(units, num_sms());
+    MG_CUDA_TRY(mg_launch(kern, dim3(grid), dim3(192), (size_t)S::SMEM_BYTES, st, ta, tb, p));
+    return check_launch("gemm_tc_persistent");
+}
+
 template <int BN, bool AMN, bool BMN>
-int by_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits, cudaStream_t st) {
+int by_epi(int epi, bool persist, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits,
+           cudaStream_t st) {
+    if (persist && BN >= 128) {
+        switch (epi) {
+            case kEpiBf16: return launch_persistent<BN, AMN, BMN, kEpiBf16>(ta, tb, p, splits, st);
+            case kEpiBf16Relu: return launch_persistent<BN, AMN, BMN, kEpiBf16Relu>(ta, tb, p, splits, st);
+            case kEpiBf16Resid: return launch_persistent<BN, AMN, BMN, kEpiBf16Resid>(ta, tb, p, splits, st);
+            case kEpiBf16Mask: return launch_persistent<BN, AMN, BMN, kEpiBf16Mask>(ta, tb, p, splits, st);
+            case kEpiF32: return launch_persistent<BN, AMN, BMN, kEpiF32>(ta, tb, p, splits, st);
+        }
+        return fail(MG_ERR_ARGUMENT, "unknown GEMM epilogue");
+    }
     switch (epi) {
         case kEpiBf16: return launch_one<BN, AMN, BMN, kEpiBf16>(ta, tb, p, splits, st);
         case kEpiBf16Relu: return launch_one<BN, AMN, BMN, kEpiBf16Relu>(ta, tb, p, splits, st);
@@ -36,12 +67,12 @@ int by_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmPara
 }
 
 template <int BN>
-int by_major(bool amn, bool bmn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-             int splits, cudaStream_t st) {
-    if (!amn && !bmn) return by_epi<BN, false, false>(epi, ta, tb, p, splits, st);
-    if (!amn && bmn) return by_epi<BN, false, true>(epi, ta, tb, p, splits, st);
-    if (amn && !bmn) return by_epi<BN, true, false>(epi, ta, tb, p, splits, st);
-    return by_epi<BN, true, true>(epi, ta, tb, p, splits, st);
+int by_major(bool amn, bool bmn, int epi, bool persist, const CUtensorMap& ta, const CUtensorMap& tb,
+             const GemmParams& p, int splits, cudaStream_t st) {
+    if (!amn && !bmn) return by_epi<BN, false, false>(epi, persist, ta, tb, p, splits, st);
+    if (!amn && bmn) return by_epi<BN, false, true>(epi, persist, ta, tb, p, splits, st);
+    if (amn && !bmn) return by_epi<BN, true, false>(epi, persist, ta, tb, p, splits, st);
+    return by_epi<BN, true, true>(epi, persist, ta, tb, p, splits, st);
 }
 
 }  // namespace
@@ -57,18 +88,35 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
     MG_CHECK_ARG(c.splits == 1 || c.epilogue == kEpiF32, "gemm: split-K needs the fp32 epilogue");
     MG_CHECK_ARG(!(c.epilogue == kEpiBf16Resid || c.epilogue == kEpiBf16Mask) || (c.aux && c.ldaux % 8 == 0),
                  "gemm: this epilogue needs aux with ldaux a multiple of 8");
-    int bn = c.bn;
-    if (bn == 0) {
-        // 128-wide output tiles, or 64-wide ones when 128-wide tiles would
-        // leave most of the 148 SMs idle (small row counts)
-        const int tiles128 = ((c.M + 127) / 128) * ((c.N + 127) / 128) * c.splits;
-        bn = (c.N >= 128 && tiles128 >= 148) ? 128 : 64;
-    }
-    MG_CHECK_ARG(bn == 64 || bn == 128 || bn == 256, "gemm: tile N must be 64, 128 or 256");
-
     int kPerSplit = (c.K + c.splits - 1) / c.splits;
     kPerSplit = (kPerSplit + 63) / 64 * 64;
     const int splits = (c.K + kPerSplit - 1) / kPerSplit;
+
+    int bn = c.bn;
+    bool persist = c.persistent == 1;
+    if (bn == 0) {
+        const int sms = num_sms();
+        const int tiles128 = ((c.M + 127) / 128) * ((c.N + 127) / 128) * splits;
+        const int tiles256 = ((c.M + 127) / 128) * ((c.N + 255) / 256) * splits;
+        if (c.persistent != 0 && c.N >= 256 && c.K >= 1024 && tiles256 >= sms) {
+            // long K: persistent with 256-wide tiles (half the shared-memory
+            // traffic per MMA of 128-wide ones)
+            bn = 256;
+            persist = true;
+        } else if (c.persistent != 0 && c.N >= 128 && tiles128 >= sms) {
+            // at least a tile per SM: persistent, epilogue of one tile
+            // overlapped with the main loop of the next
+            bn = 128;
+            persist = true;
+        } else {
+            // one CTA per tile: 128-wide output tiles, or 64-wide ones when
+            // 128-wide tiles would leave most of the SMs idle (small row counts)
+            bn = (c.N >= 128 && tiles128 >= sms) ? 128 : 64;
+            persist = false;
+        }
+    }
+    MG_CHECK_ARG(bn == 64 || bn == 128 || bn == 256, "gemm: tile N must be 64, 128 or 256");
+    MG_CHECK_ARG(!persist || bn >= 128, "gemm: the persistent kernel needs tile N 128 or 256");
 
     CUtensorMap ta, tb;
     int rc = c.a_mn ? make_tmap_bf16(&ta, c.A, c.M, c.K, c.lda, 64) : make_tmap_bf16(&ta, c.A, c.K, c.M, c.lda, 128);
@@ -86,10 +134,13 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
     p.aux = static_cast<const __nv_bfloat16*>(c.aux);
     p.ldaux = c.ldaux;
     p.status = status_ptr();
+    p.tilesM = (c.M + 127) / 128;
+    p.tilesN = (c.N + bn - 1) / bn;
+    p.splits = splits;
     switch (bn) {
-        case 64: return by_major<64>(c.a_mn, c.b_mn, c.epilogue, ta, tb, p, splits, st);
-        case 128: return by_major<128>(c.a_mn, c.b_mn, c.epilogue, ta, tb, p, splits, st);
-        default: return by_major<256>(c.a_mn, c.b_mn, c.epilogue, ta, tb, p, splits, st);
+        case 64: return by_major<64>(c.a_mn, c.b_mn, c.epilogue, false, ta, tb, p, splits, st);
+        case 128: return by_major<128>(c.a_mn, c.b_mn, c.epilogue, persist, ta, tb, p, splits, st);
+        default: return by_major<256>(c.a_mn, c.b_mn, c.epilogue, persist, ta, tb, p, splits, st);
     }
 }
 
@@ -114,5 +165,30 @@ extern "C" int mg_gemm_bf16(const void* A_dev, int a_mn_major, int lda, const vo
     c.aux = aux_dev;
     c.ldaux = ldaux;
     c.splits = splits;
+    return mg::gemm_bf16(c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mg_gemm_bf16_tiled(const void* A_dev, int a_mn_major, int lda, const void* B_dev, int b_mn_major,
+                                  int ldb, int M, int N, int K, int epilogue, void* out_dev, int ldo,
+                                  const void* aux_dev, int ldaux, int splits, int tile_n, int persistent,
+                                  mg_stream_t stream) {
+    mg::GemmCall c;
+    c.A = A_dev;
+    c.a_mn = a_mn_major != 0;
+    c.lda = lda;
+    c.B = B_dev;
+    c.b_mn = b_mn_major != 0;
+    c.ldb = ldb;
+    c.M = M;
+    c.N = N;
+    c.K = K;
+    c.epilogue = epilogue;
+    c.out = out_dev;
+    c.ldo = ldo;
+    c.aux = aux_dev;
+    c.ldaux = ldaux;
+    c.splits = splits;
+    c.bn = tile_n;
+    c.persistent = tile_n == 0 ? (persistent ? -1 : 0) : (persistent ? 1 : 0);
     return mg::gemm_bf16(c, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -20,6 +20,7 @@ struct GemmCall {
     int ldaux = 0;
     int splits = 1;
     int bn = 0;  // output tile width (64 / 128 / 256); 0 = choose
+    int persistent = -1;  // 1: persistent kernel (bn 128 / 256), 0: one CTA per tile, -1: choose
 };
 
 int gemm_bf16(const GemmCall& c, cudaStream_t st);

@@ -33,6 +33,7 @@ enum GemmEpilogue : int {
 struct GemmParams {
     int M, N, K;
     int kPerSplit;  // multiple of 64
+    int tilesM, tilesN, splits;  // work units of the persistent kernel
     void* out;
     int ldo;
     const __nv_bfloat16* aux;
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(128, 1)
 
     // ---- epilogue: thread (warp, lane) owns output row m0 + 32 warp + lane
     __syncwarp();
-    const bool ready = (nk == 0) || mbar_wait(done, 0, p.status, kDevTimeoutDone);
+    const bool ready = (nk == 0) || mbar_wait_warp(done, 0, p.status, kDevTimeoutDone);
     tc_fence_after();
     const int row = m0 + warp * 32 + lane;
     if (ready) {

@@ -1,0 +1,234 @@
+// Persistent tcgen05 GEMM for large problems: one CTA per SM walks the
+// output tiles (and K splits) in a fixed round-robin order, with its
+// accumulator double-buffered in tensor memory so that the epilogue of one
+// tile overlaps the main loop of the next.
+//
+// Warp roles (192 threads):
+//   warp 0     TMA producer: A and B tiles into a STAGES-deep shared ring
+//   warp 1     MMA issuer: 128 x BN x 16 tcgen05.mma into accumulator a
+//              (columns a * BN of a 2 * BN column allocation), commit to
+//              tfull[a] when the tile's K range is done
+//   warps 2-5  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, i.e.
+//              output rows 32 (w % 4) + lane of the tile, applies the
+//              epilogue and stores; each warp then arrives on tempty[a]
+//
+// Units are numbered with the N tile fastest, so the CTAs working at the same
+// time share A tiles through L2. Same operand layouts, epilogues and
+// rounding as gemm_tc_kernel; every wait is bounded (ptx.cuh).
+#pragma once
+
+#include "gemm_tc.cuh"
+
+namespace mg {
+
+template <int BN>
+struct PersistShape {
+    static constexpr int BM = 128;
+    static constexpr int BK = 64;
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (256 or 512 columns)
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// One 32-column chunk of one output row: epilogue and store.
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int col, int z, float* v) {
+    if (EPI == kEpiF32) {
+        float* o = static_cast<float*>(p.out) + (size_t)z * p.M * p.ldo + (size_t)row * p.ldo + col;
+        float4* o4 = reinterpret_cast<float4*>(o);
+#pragma unroll
+        for (int i = 0; i < 8; i++) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + col;
+        if (EPI == kEpiBf16Relu) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const float r = round_bf16(v[i]);
+                v[i] = r > 0.0f ? r : r * 0.0f;
+            }
+        } else if (EPI == kEpiBf16Resid) {
+            float a[32];
+            load_bf16x32(p.aux + (size_t)row * p.ldaux + col, a);
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = a[i] + round_bf16(v[i]);
+        } else if (EPI == kEpiBf16Mask) {
+            float a[32];
+            load_bf16x32(p.aux + (size_t)row * p.ldaux + col, a);
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = round_bf16(v[i]) * (a[i] > 0.0f ? 1.0f : 0.0f);
+        }
+        store_bf16x32(o, v);
+    }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const GemmParams p) {
+    using S = PersistShape<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::STAGES * S::STAGE_BYTES);
+    uint64_t* empty = full + S::STAGES;
+    uint64_t* tfull = empty + S::STAGES;  // [2]
+    uint64_t* tempty = tfull + 2;         // [2]
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    mg_pdl_trigger();
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tilesMN = p.tilesM * p.tilesN;
+    const int units = tilesMN * p.splits;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, S::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    mg_pdl_wait();  // operands and aux come from the previous kernel
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer
+            int it = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const int nt = u % p.tilesN;
+                const int mt = (u / p.tilesN) % p.tilesM;
+                const int z = u / tilesMN;
+                const int m0 = mt * S::BM, n0 = nt * BN;
+                const int kBegin = z * p.kPerSplit;
+                const int kEnd = min(p.K, kBegin + p.kPerSplit);
+                for (int k0 = kBegin; k0 < kEnd; k0 += S::BK) {
+                    const int s = it % S::STAGES;
+                    const uint32_t ph = (it / S::STAGES) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, p.status, kDevTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    it++;
+                    uint8_t* sA = smem + s * S::STAGE_BYTES;
+                    uint8_t* sB = sA + S::A_BYTES;
+                    mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
+                    if (A_MN) {
+                        tma_load_2d(sA, &tmA, m0, k0, &full[s]);
+                        tma_load_2d(sA + 8192, &tmA, m0 + 64, k0, &full[s]);
+                    } else {
+                        tma_load_2d(sA, &tmA, k0, m0, &full[s]);
+                    }
+                    if (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; j++) tma_load_2d(sB + j * 8192, &tmB, n0 + 64 * j, k0, &full[s]);
+                    } else {
+                        tma_load_2d(sB, &tmB, k0, n0, &full[s]);
+                    }
+                }
+            }
+            // Drain: every issued copy has landed before the CTA can exit.
+            for (int k = it - S::STAGES < 0 ? 0 : it - S::STAGES; k < it; k++)
+                mbar_wait(&full[k % S::STAGES], (k / S::STAGES) & 1, p.status, kDevTimeoutFull);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            constexpr uint32_t idesc = idesc_bf16_f32(BN, A_MN, B_MN);
+            int it = 0, t = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, t++) {
+                const int z = u / tilesMN;
+                const int kBegin = z * p.kPerSplit;
+                const int kEnd = min(p.K, kBegin + p.kPerSplit);
+                const int a = t & 1;
+                // the epilogue has emptied accumulator a (its previous use was tile t - 2)
+                if (!mbar_wait(&tempty[a], ((t >> 1) & 1) ^ 1, p.status, kDevTimeoutEmpty)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(a * BN);
+                bool first = true;
+                for (int k0 = kBegin; k0 < kEnd; k0 += S::BK) {
+                    const int s = it % S::STAGES;
+                    const uint32_t ph = (it / S::STAGES) & 1;
+                    if (!mbar_wait(&full[s], ph, p.status, kDevTimeoutFull)) {
+                        ok = false;
+                        break;
+                    }
+                    it++;
+                    tc_fence_after();
+                    const uint32_t aBase = smem_u32(smem + s * S::STAGE_BYTES);
+                    const uint32_t bBase = aBase + S::A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint64_t ad = A_MN ? smem_desc_sw128(aBase + kk * 2048, 8192, 1024)
+                                                 : smem_desc_sw128(aBase + kk * 32, 16, 1024);
+                        const uint64_t bd = B_MN ? smem_desc_sw128(bBase + kk * 2048, 8192, 1024)
+                                                 : smem_desc_sw128(bBase + kk * 32, 16, 1024);
+                        tc_mma_bf16(acc, ad, bd, idesc, first ? 0u : 1u);
+                        first = false;
+                    }
+                    tc_commit(&empty[s]);
+                }
+                if (ok) tc_commit(&tfull[a]);
+            }
+            // Always commit: `done` then covers every MMA issued, also after a
+            // timeout, so TMEM is never freed under a running MMA.
+            tc_commit(done);
+        }
+    } else {
+        // ---- epilogue: thread owns row 32 (warp % 4) + lane of each tile
+        const int q = warp & 3;
+        int t = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, t++) {
+            const int nt = u % p.tilesN;
+            const int mt = (u / p.tilesN) % p.tilesM;
+            const int z = u / tilesMN;
+            const int a = t & 1;
+            if (!mbar_wait_warp(&tfull[a], (t >> 1) & 1, p.status, kDevTimeoutDone)) break;
+            tc_fence_after();
+            const int row = mt * S::BM + q * 32 + lane;
+            const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; c++) {
+                const int col = nt * BN + c * 32;
+                float v[32];
+                tmem_ld32(acc + (uint32_t)(c * 32), v);
+                if (c == BN / 32 - 1) {
+                    // the whole accumulator is in registers or stored: release it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[a]);
+                }
+                if (row < p.M && col < p.N) epilogue_chunk<EPI>(p, row, col, z, v);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        mbar_wait(done, 0, p.status, kDevTimeoutDone);
+        tc_fence_after();
+        tmem_dealloc(tmem, S::TMEM_COLS);
+    }
+}
+
+}  // namespace mg

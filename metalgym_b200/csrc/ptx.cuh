@@ -78,6 +78,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     return true;
 }
 
+// The same wait for a whole warp with a warp-uniform result (lane 0 waits,
+// the others then see the completed phase at once), so that the warp's
+// .sync.aligned instructions after it are never reached by part of the warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, code) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (ok && (threadIdx.x & 31) != 0) ok = mbar_wait(bar, parity, status, code) ? 1 : 0;
+    return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(

@@ -40,6 +40,18 @@ int cuda_fail(cudaError_t e, const char* what) {
     return fail(MG_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+int num_sms() {
+    static int cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
 int* status_ptr() {
     constexpr int kMaxDevices = 64;
     static int* cache[kMaxDevices] = {};

@@ -31,6 +31,8 @@ int cuda_fail(cudaError_t e, const char* what);
 // Device address of the status word of the current device (a __device__ int
 // in runtime.cu, looked up once per device with cudaGetSymbolAddress).
 int* status_ptr();
+// Streaming multiprocessors of the current device (cached per device).
+int num_sms();
 
 // 2D bf16 tensor map with 128-byte swizzle: `inner` contiguous elements per
 // row, `outer` rows, `row_stride` elements between rows, box of 64 x box_outer.
