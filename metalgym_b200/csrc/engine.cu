@@ -247,6 +247,13 @@ PpoEngine::~PpoEngine() {
     cudaFreeHost(hostSched);
     cudaFreeHost(hostSchedBetaPow);
     cudaFreeHost(hostStats);
+    if (side) {
+        cudaStreamSynchronize(side);
+        cudaStreamDestroy(side);
+    }
+    for (auto ev : forkEv)
+        if (ev) cudaEventDestroy(ev);
+    if (joinEv) cudaEventDestroy(joinEv);
     cudaSetDevice(cur);
 }
 
@@ -351,6 +358,10 @@ int PpoEngine::init() {
     MG_TRY(dalloc(&advSlots, slotCount * 4));
     MG_TRY(dalloc(&retSlots, slotCount * 4));
     MG_TRY(dalloc(&advStats, (size_t)T * 2 * 4));
+    MG_CUDA_TRY(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
+    forkEv.assign(L + 1, nullptr);
+    for (auto& ev : forkEv) MG_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    MG_CUDA_TRY(cudaEventCreateWithFlags(&joinEv, cudaEventDisableTiming));
     MG_TRY(dalloc(&mbAdvStats, 2 * 4));
     MG_TRY(dalloc(&advPartial, (size_t)2 * kAdvStatsMaxCtas * 8));
     MG_TRY(dalloc(&advCounter, 4));
@@ -389,9 +400,11 @@ int PpoEngine::allocTrain(int rows) {
     }
     MG_TRY(alloc_acts(trainActs, rows, E, H, L, false));
     MG_TRY(dalloc(&dLogits, (size_t)rows * kHead * 2));
-    MG_TRY(dalloc(&dStream, (size_t)rows * E * 2));
     MG_TRY(dalloc(&dBranch, (size_t)rows * E * 2));
-    MG_TRY(dalloc(&dV, (size_t)rows * H * 2));
+    dS.assign(L + 1, nullptr);
+    dVs.assign(L, nullptr);
+    for (int n = 0; n <= L; n++) MG_TRY(dalloc(&dS[n], (size_t)rows * E * 2));
+    for (int n = 0; n < L; n++) MG_TRY(dalloc(&dVs[n], (size_t)rows * H * 2));
     MG_TRY(dalloc(&stats, (size_t)rows * 5 * 4));
     MG_CUDA_TRY(cudaMemset(stats, 0, (size_t)rows * 5 * 4));
     upSplits = splits_for(E, H, rows, H >= 128 ? 128 : 64);
@@ -449,11 +462,15 @@ void PpoEngine::freeTrain() {
         cudaFree(*p);
         *p = nullptr;
     }
-    void** vs[] = {&dLogits, &dStream, &dBranch, &dV};
+    void** vs[] = {&dLogits, &dBranch};
     for (void** p : vs) {
         cudaFree(*p);
         *p = nullptr;
     }
+    for (void* p : dS) cudaFree(p);
+    for (void* p : dVs) cudaFree(p);
+    dS.clear();
+    dVs.clear();
     for (auto* p : upPart) cudaFree(p);
     for (auto* p : downPart) cudaFree(p);
     for (auto* p : lnPart) cudaFree(p);
@@ -588,55 +605,68 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     else
         MG_TRY(policy_loss(a.head, static_cast<const int32_t*>(actionSlots), advSlots, as, retSlots, logpSlots,
                            dLogits, stats, rows, A, lh, st, rm));
-    // backward (model/ppo.h:793-865)
+    // backward (model/ppo.h:793-865). The input-gradient chain runs on st;
+    // each weight-gradient GEMM is forked to the side stream as soon as its
+    // operands exist (they are never overwritten within the minibatch) and
+    // the side stream is joined before the gradient finalisation.
+    auto fork = [&](int k) -> int {
+        MG_CUDA_TRY(cudaEventRecord(forkEv[k], st));
+        MG_CUDA_TRY(cudaStreamWaitEvent(side, forkEv[k], 0));
+        return MG_OK;
+    };
+    MG_TRY(fork(L));
     {
-        GemmCall dx;  // dStream = dLogits W_head^T (model/linear.metal:40-60)
-        dx.A = dLogits; dx.lda = kHead;
-        dx.B = w(pHead); dx.ldb = kHead;  // [E][64] = [N][K], K-major
-        dx.M = rows; dx.N = E; dx.K = kHead;
-        dx.out = dStream; dx.ldo = E;
-        MG_TRY(gemm_bf16(dx, st));
         GemmCall dw;  // dW_head = X_F^T dLogits (model/linear.metal:71-93)
         dw.A = a.fOut; dw.a_mn = true; dw.lda = E;
         dw.B = dLogits; dw.b_mn = true; dw.ldb = kHead;
         dw.M = E; dw.N = kHead; dw.K = rows;
         dw.epilogue = 4; dw.splits = headSplits;
         dw.out = headPart; dw.ldo = kHead;
-        MG_TRY(gemm_bf16(dw, st));
+        MG_TRY(gemm_bf16(dw, side));
+        GemmCall dx;  // dS[L] = dLogits W_head^T (model/linear.metal:40-60)
+        dx.A = dLogits; dx.lda = kHead;
+        dx.B = w(pHead); dx.ldb = kHead;  // [E][64] = [N][K], K-major
+        dx.M = rows; dx.N = E; dx.K = kHead;
+        dx.out = dS[L]; dx.ldo = E;
+        MG_TRY(gemm_bf16(dx, st));
     }
-    MG_TRY(layernorm_backward(dStream, a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, rows, E, st));
+    MG_TRY(layernorm_backward(dS[L], a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, rows, E, st));
     for (int n = L - 1; n >= 0; n--) {
-        GemmCall g1;  // dV = bf16(dStream Dp^T) * (V > 0) (model/mlp.metal:88-127)
-        g1.A = dStream; g1.lda = E;
+        GemmCall g1;  // dV = bf16(dS Dp^T) * (V > 0) (model/mlp.metal:88-127)
+        g1.A = dS[n + 1]; g1.lda = E;
         g1.B = w(pDown[n]); g1.ldb = E;  // Dp [H][E] = [N][K]
         g1.M = rows; g1.N = H; g1.K = E;
         g1.epilogue = 3; g1.aux = a.v[n]; g1.ldaux = H;
-        g1.out = dV; g1.ldo = H;
+        g1.out = dVs[n]; g1.ldo = H;
         MG_TRY(gemm_bf16(g1, st));
+        MG_TRY(fork(n));
         GemmCall g2;  // dUp = X^T dV (model/mlp.metal:167-208)
         g2.A = a.lnOut[n]; g2.a_mn = true; g2.lda = E;
-        g2.B = dV; g2.b_mn = true; g2.ldb = H;
+        g2.B = dVs[n]; g2.b_mn = true; g2.ldb = H;
         g2.M = E; g2.N = H; g2.K = rows;
         g2.epilogue = 4; g2.splits = upSplits;
         g2.out = upPart[n]; g2.ldo = H;
-        MG_TRY(gemm_bf16(g2, st));
-        GemmCall g3;  // dDp = V^T dStream
+        MG_TRY(gemm_bf16(g2, side));
+        GemmCall g3;  // dDp = V^T dS
         g3.A = a.v[n]; g3.a_mn = true; g3.lda = H;
-        g3.B = dStream; g3.b_mn = true; g3.ldb = E;
+        g3.B = dS[n + 1]; g3.b_mn = true; g3.ldb = E;
         g3.M = H; g3.N = E; g3.K = rows;
         g3.epilogue = 4; g3.splits = downSplits;
         g3.out = downPart[n]; g3.ldo = E;
-        MG_TRY(gemm_bf16(g3, st));
+        MG_TRY(gemm_bf16(g3, side));
         GemmCall g4;  // dBranch = dV Up^T (model/mlp.metal:131-153)
-        g4.A = dV; g4.lda = H;
+        g4.A = dVs[n]; g4.lda = H;
         g4.B = w(pUp[n]); g4.ldb = H;  // Up [E][H] = [N][K]
         g4.M = rows; g4.N = E; g4.K = H;
         g4.out = dBranch; g4.ldo = E;
         MG_TRY(gemm_bf16(g4, st));
-        // LayerNorm backward, then dStream += dBranch (model/ppo.h:851-852)
-        MG_TRY(layernorm_backward(dBranch, a.lnXn[n], w(pLnG[n]), a.lnSd[n], dStream, lnPart[n], rows, E, st));
+        // LayerNorm backward, then dS[n] = dS[n + 1] + dBranch (model/ppo.h:851-852)
+        MG_TRY(layernorm_backward(dBranch, a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1], lnPart[n], rows, E, st,
+                                  dS[n]));
     }
-    MG_TRY(input_backward(obsSlots, dStream, inPart, rows, O, E, st, rm));
+    MG_TRY(input_backward(obsSlots, dS[0], inPart, rows, O, E, st, rm));
+    MG_CUDA_TRY(cudaEventRecord(joinEv, side));
+    MG_CUDA_TRY(cudaStreamWaitEvent(st, joinEv, 0));
     // gradient sums + norm (model/ppo.h:873-890), [all-reduce], Adam (:891-903)
     // the finalisation's last CTA leaves the squared norm in normSq
     MG_TRY(grad_finalize(gradTable, grad, normPartial, st, normCounter, normSq));

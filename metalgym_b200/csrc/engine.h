@@ -125,7 +125,15 @@ class PpoEngine {
     unsigned int* advCounter = nullptr;     // last-CTA detection
     // activations
     ActSet collectActs, trainActs;
-    void *dLogits = nullptr, *dStream = nullptr, *dBranch = nullptr, *dV = nullptr;
+    void *dLogits = nullptr, *dBranch = nullptr;
+    std::vector<void*> dS;   // L + 1: dS[n + 1] = gradient at the output of block n, dS[L] from the head
+    std::vector<void*> dVs;  // L: masked gradient of each block's hidden layer
+    // the weight-gradient GEMMs run on a side stream, forked from the
+    // input-gradient chain when their operands are ready and joined before
+    // the gradient finalisation
+    cudaStream_t side = nullptr;
+    std::vector<cudaEvent_t> forkEv;  // L + 1
+    cudaEvent_t joinEv = nullptr;
     float* stats = nullptr;  // R x 5
     // gradient partials
     std::vector<float*> upPart, downPart, lnPart;

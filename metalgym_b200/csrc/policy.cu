@@ -199,7 +199,8 @@ __global__ void k_layernorm_forward(const __nv_bfloat16* __restrict__ x, __nv_bf
 // model/layernorm.metal:74-127 (+ model/elementwise.metal:4-13 when resid is
 // given). Per row: dxhat = bf16(dz * gamma); dx = bf16((dxhat - mean(dxhat)
 // - xhat * mean(bf16(dxhat * xhat))) / sigma). Without resid dx overwrites dZ;
-// with resid, resid = bf16(dx + resid) and dZ is left as is. dgamma
+// with resid, residOut = bf16(dx + resid) (residOut may be resid) and dZ is
+// left as is. dgamma
 // (sum of bf16(xhat * dz)) and dbeta (sum of dz) are summed over this CTA's
 // rows into partial[blockIdx] = [dgamma (E) | dbeta (E)].
 template <int VPT>
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
                                                             const __nv_bfloat16* __restrict__ xNorm,
                                                             const __nv_bfloat16* __restrict__ gamma,
                                                             const float* __restrict__ stdev,
-                                                            __nv_bfloat16* __restrict__ resid,
+                                                            const __nv_bfloat16* resid, __nv_bfloat16* residOut,
                                                             float* __restrict__ partial, int rows, int rowsPerCta) {
     mg_pdl_trigger();
     mg_pdl_wait();
@@ -256,9 +257,9 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
         if (resid) {
 #pragma unroll
             for (int j = 0; j < VPT; j += 2) {
-                __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(resid + base + j);
-                const float2 o = __bfloat1622float2(*p);
-                *p = __floats2bfloat162_rn(__fadd_rn(rbf(dx[j]), o.x), __fadd_rn(rbf(dx[j + 1]), o.y));
+                const float2 o = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(resid + base + j));
+                *reinterpret_cast<__nv_bfloat162*>(residOut + base + j) =
+                    __floats2bfloat162_rn(__fadd_rn(rbf(dx[j]), o.x), __fadd_rn(rbf(dx[j + 1]), o.y));
             }
         } else {
 #pragma unroll
@@ -947,20 +948,21 @@ static int ln_rows_per_cta(int rows) {
 
 int layernorm_backward_parts(int rows) { return grid_rows(rows, ln_rows_per_cta(rows)); }
 
-int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, void* resid,
-                       float* partial, int rows, int cols, cudaStream_t st) {
+int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, const void* resid,
+                       float* partial, int rows, int cols, cudaStream_t st, void* residOut) {
     MG_CHECK_ARG(rows > 0, "layernorm_backward: rows must be > 0");
     const int rpc = ln_rows_per_cta(rows);
     const int blocks = grid_rows(rows, rpc);
     auto DZ = static_cast<__nv_bfloat16*>(dZ);
     auto XN = static_cast<const __nv_bfloat16*>(xNorm);
     auto G = static_cast<const __nv_bfloat16*>(gamma);
-    auto R = static_cast<__nv_bfloat16*>(resid);
+    auto R = static_cast<const __nv_bfloat16*>(resid);
+    auto RO = static_cast<__nv_bfloat16*>(residOut ? residOut : const_cast<void*>(resid));
     switch (cols) {
-        case 64: MG_LAUNCH(k_layernorm_backward<2>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows, rpc); break;
-        case 128: MG_LAUNCH(k_layernorm_backward<4>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows, rpc); break;
-        case 256: MG_LAUNCH(k_layernorm_backward<8>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows, rpc); break;
-        case 512: MG_LAUNCH(k_layernorm_backward<16>, blocks, 256, 0, st, DZ, XN, G, stdev, R, partial, rows, rpc); break;
+        case 64: MG_LAUNCH(k_layernorm_backward<2>, blocks, 256, 0, st, DZ, XN, G, stdev, R, RO, partial, rows, rpc); break;
+        case 128: MG_LAUNCH(k_layernorm_backward<4>, blocks, 256, 0, st, DZ, XN, G, stdev, R, RO, partial, rows, rpc); break;
+        case 256: MG_LAUNCH(k_layernorm_backward<8>, blocks, 256, 0, st, DZ, XN, G, stdev, R, RO, partial, rows, rpc); break;
+        case 512: MG_LAUNCH(k_layernorm_backward<16>, blocks, 256, 0, st, DZ, XN, G, stdev, R, RO, partial, rows, rpc); break;
         default: return fail(MG_ERR_ARGUMENT, "layernorm_backward: cols must be 64, 128, 256 or 512");
     }
     return check_launch("k_layernorm_backward");

@@ -70,8 +70,8 @@ int input_backward(const float* obs, const void* dZ, float* partial, int rows, i
 int layernorm_forward(const void* x, void* xNorm, void* out, const void* gamma, const void* beta, float* stdev,
                       int rows, int cols, cudaStream_t st);
 int layernorm_backward_parts(int rows);
-int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, void* resid,
-                       float* partial, int rows, int cols, cudaStream_t st);
+int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, const void* resid,
+                       float* partial, int rows, int cols, cudaStream_t st, void* residOut = nullptr);
 int sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* logProb, float* value, int rows,
                        int actDim, cudaStream_t st);
 int sample_gaussian(const void* head, const void* logStd, uint32_t* rng, float* action, float* logProb,
