@@ -165,6 +165,16 @@ int mg_layernorm_forward(const void* x, void* x_norm, void* out, const void* gam
 int mg_layernorm_backward(void* dZ, const void* x_norm, const void* gamma, const float* stdev, void* resid,
                           float* partial, int rows, int cols, mg_stream_t stream);
 int mg_layernorm_backward_num_partials(int rows);
+/* One residual MLP block forward in one kernel (no single counterpart in the
+ * reference: it fuses layernormForward, model/layernorm.metal:10-71,
+ * mlpForwardOne/Two, model/mlp.metal:18-86, and residualAdd,
+ * model/elementwise.metal:4-13): x_norm, ln_out, stdev = LayerNorm(h) as
+ * mg_layernorm_forward computes them (bit-identical), v = relu(bf16(ln_out
+ * up)) ([rows][hidden]), h = bf16(h + bf16(v down)) in place. up: [embed]
+ * [hidden], down: [hidden][embed], row-major bf16; embed 64 or 128, hidden a
+ * multiple of 128. */
+int mg_block_forward(void* h, const void* gamma, const void* beta, const void* up, const void* down, void* x_norm,
+                     void* ln_out, float* stdev, void* v, int rows, int embed, int hidden, mg_stream_t stream);
 /* Categorical draw per head row (bf16 [rows][64]; logits in 0..act_dim-1,
  * value at act_dim), advancing rng once. Replaces sampleAction
  * (model/sample.metal:18-47). */

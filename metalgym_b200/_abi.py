@@ -21,6 +21,7 @@ SIGNATURES = {
     "mg_device_status": (I, [I, PI]),
     # GEMM
     "mg_gemm_bf16": (I, [P, I, I, P, I, I, I, I, I, I, P, I, P, I, I, P]),
+    "mg_block_forward": (I, [P, P, P, P, P, P, P, P, P, I, I, I, P]),
     "mg_gemm_bf16_tiled": (I, [P, I, I, P, I, I, I, I, I, I, P, I, P, I, I, I, I, P]),
     # environments
     "mg_env_register": (I, [P]),

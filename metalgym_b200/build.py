@@ -30,6 +30,7 @@ SOURCES: dict[str, list[str]] = {
     "runtime.cu": [],
     "gemm.cu": [],
     "policy.cu": [],
+    "block_fwd.cu": [],
     "envs.cu": [],
     "envs_builtin.cu": ["--fmad=false"],
     "engine.cu": [],

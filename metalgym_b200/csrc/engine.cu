@@ -23,6 +23,7 @@
 #include <cstring>
 #include <string>
 
+#include "block.h"
 #include "gemm.h"
 #include "runtime.h"
 
@@ -268,6 +269,7 @@ int PpoEngine::init() {
     MG_CHECK_ARG(O >= 1 && O <= 256, "PPOModel: OBS_DIM must be in [1, 256]");
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
+    fusedBlocks = block_forward_supported(E, H);
 
     // ---- parameters: model/ppo.h:375-445 (seeded normal init rounded to bf16)
     std::vector<std::vector<uint16_t>> init;
@@ -521,12 +523,32 @@ int PpoEngine::checkStatus(const char* what) {
     return MG_OK;
 }
 
+// Arguments of the fused block kernel for block n over an activation set.
+BlockFwdArgs PpoEngine::blockArgs(ActSet& a, int n, int rows) {
+    BlockFwdArgs b{};
+    b.h = static_cast<__nv_bfloat16*>(a.h);
+    b.gamma = reinterpret_cast<const __nv_bfloat16*>(weights + params[pLnG[n]].offset);
+    b.beta = reinterpret_cast<const __nv_bfloat16*>(weights + params[pLnB[n]].offset);
+    b.xNorm = static_cast<__nv_bfloat16*>(a.lnXn[n]);
+    b.lnOut = static_cast<__nv_bfloat16*>(a.lnOut[n]);
+    b.stdev = a.lnSd[n];
+    b.V = static_cast<__nv_bfloat16*>(a.v[n]);
+    b.rows = rows;
+    b.E = E;
+    b.H = H;
+    return b;
+}
+
 // model/ppo.h:575-626: input -> L x [LN -> up (ReLU) -> down (+ skip)] -> LN -> head.
 int PpoEngine::forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st) {
     const uint16_t* W = weights;
     auto w = [&](uint32_t p) { return static_cast<const void*>(W + params[p].offset); };
     MG_TRY(input_forward(obs, w(pInW), w(pInB), a.h, rows, O, E, st));
     for (int n = 0; n < L; n++) {
+        if (useFusedBlock(rows)) {
+            MG_TRY(block_forward(blockArgs(a, n, rows), w(pUp[n]), w(pDown[n]), st));
+            continue;
+        }
         MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
         GemmCall up;
         up.A = a.lnOut[n]; up.lda = E;
@@ -565,6 +587,10 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     // forward with activations saved (the input gathers the minibatch's obs rows)
     MG_TRY(input_forward(obsSlots, w(pInW), w(pInB), a.h, rows, O, E, st, rm));
     for (int n = 0; n < L; n++) {
+        if (useFusedBlock(rows)) {
+            MG_TRY(block_forward(blockArgs(a, n, rows), w(pUp[n]), w(pDown[n]), st));
+            continue;
+        }
         MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
         GemmCall up;
         up.A = a.lnOut[n]; up.lda = E;

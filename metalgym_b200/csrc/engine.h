@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "../../include/metalgym_b200.h"
+#include "block.h"
 #include "policy.h"
 
 namespace mg {
@@ -163,12 +164,21 @@ class PpoEngine {
     bool trainExecRowMode = false;
     PpoHyper collectHp, trainHp;
 
+    // one fused kernel per residual block forward (block_fwd.cu) where the
+    // widths allow it and there are enough row tiles to fill the GPU (with
+    // few tiles the chain of LayerNorm + two GEMMs, spread over more CTAs,
+    // is faster), else LayerNorm + two GEMMs
+    bool fusedBlocks = false;
+    bool useFusedBlock(int rows) const { return fusedBlocks && rows >= kFusedBlockMinRows; }
+    static constexpr int kFusedBlockMinRows = 8192;
+
     // multi-GPU
     void* comm = nullptr;
     int rank = 0, world = 1;
 
    private:
     int forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st);
+    BlockFwdArgs blockArgs(ActSet& a, int n, int rows);
     int minibatch(int j, bool rowMode, cudaStream_t st);  // reads sched[j], schedBetaPow[2j..]
     int captureCollect();
     int captureTrain(int minibatches, bool rowMode);
