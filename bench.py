@@ -339,26 +339,10 @@ def max_over_ranks(x, dist):
     return mor(x, dist, device="cuda")
 
 
-def dominant_kernel_roofline(lib, torch, dev, stream):
-    """The tcgen05 GEMM with the largest share of the loop's GPU time (ncu
-    launch list of one iteration): the policy's down-projection with the fused
-    residual add, rows x embed x hidden = 4096 x 128 x 512. Timed alone, back
-    to back on the engine's stream with CUDA events; the DRAM traffic per
-    launch comes from the committed ncu summary of the same launch."""
-    M, N, K = ENVS_PER_GPU, EMBED, EMBED * SCALE
-    a = torch.relu(torch.randn(M, K, device=f"cuda:{dev}")).bfloat16()
-    b = (torch.randn(K, N, device=f"cuda:{dev}") / 16).bfloat16()
-    h = torch.randn(M, N, device=f"cuda:{dev}").bfloat16()
-    o = torch.empty(M, N, device=f"cuda:{dev}", dtype=torch.bfloat16)
-    sp = ctypes.c_void_p(stream.cuda_stream)
-
-    def launch():
-        return lib.mg_gemm_bf16(a.data_ptr(), 0, K, b.data_ptr(), 1, N, M, N, K, 2, o.data_ptr(), N, h.data_ptr(), N,
-                                1, sp)
-
+def _time_launches(launch, torch, stream, iters=200):
+    """Average device time of `launch` run back to back on `stream` (CUDA events)."""
     for _ in range(5):
         launch()
-    iters = 200
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         s.record(stream)
@@ -367,19 +351,72 @@ def dominant_kernel_roofline(lib, torch, dev, stream):
     with torch.cuda.stream(stream):
         e.record(stream)
     torch.cuda.synchronize()
-    us = s.elapsed_time(e) * 1e3 / iters
+    return s.elapsed_time(e) * 1e3 / iters
+
+
+def dominant_kernel_roofline(lib, torch, dev, stream):
+    """The kernel with the largest share of the loop's GPU time in the ncu
+    launch list of one CartPole iteration (profiles/launches_c3_full_loop.md):
+    the split-K weight-gradient GEMM gemm_tc_kernel<64, MN-major A, MN-major B,
+    fp32 partials>, 5 launches per minibatch. Timed here on its largest shape,
+    dUp = lnOut^T dV (embed x hidden x rows = 128 x 512 x 4096, 16 K-splits),
+    alone and back to back on the engine's stream with CUDA events.
+
+    Its algorithmic traffic is the two operands (4096 x 128 + 4096 x 512 bf16)
+    and the reduced gradient (128 x 512 fp32); its FLOPs are 2 x 128 x 512 x
+    4096. At the measured peaks the bytes take longer than the FLOPs, so the
+    bound is HBM. The DRAM traffic per launch comes from the committed ncu
+    capture of the same launch (profiles/gemm_wgrad_128x512x4096_split16.md);
+    the fp32 split partials stay in L2 there."""
+    M, N, K, splits = EMBED, EMBED * SCALE, ENVS_PER_GPU, 16
+    a = torch.randn(K, M, device=f"cuda:{dev}").bfloat16()   # lnOut, rows x embed
+    b = torch.randn(K, N, device=f"cuda:{dev}").bfloat16()   # dV, rows x hidden
+    o = torch.empty(splits, M, N, device=f"cuda:{dev}", dtype=torch.float32)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def launch():
+        return lib.mg_gemm_bf16(a.data_ptr(), 1, M, b.data_ptr(), 1, N, M, N, K, 4, o.data_ptr(), N, None, 0,
+                                splits, sp)
+
+    us = _time_launches(launch, torch, stream)
     flops = 2.0 * M * N * K
-    achieved = flops / (us * 1e-6) / 1e12
-    _, peak, kind = measured_peaks()
-    return {"kernel": "gemm_tc_kernel<64, K-major A, MN-major B, +residual> (MLP down-projection, 4096x128x512)",
-            "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "peak_kind": f"{kind} bf16 burst", "us_per_launch": us, "flop_per_launch": flops,
-            "traffic": profile_traffic()}
+    alg_bytes = (K * M + K * N) * 2 + M * N * 4
+    hbm, tflops, kind = measured_peaks()
+    t_mem, t_flop = alg_bytes / (hbm * 1e9), flops / (tflops * 1e12)
+    achieved = alg_bytes / (us * 1e-6) / 1e9
+    roof = {"kernel": "gemm_tc_kernel<64, MN-major A, MN-major B, fp32 split-K partials> "
+                      "(weight gradient dUp, 128x512x4096, 16 splits)",
+            "bound": "hbm" if t_mem >= t_flop else "tensor", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm, "peak_kind": f"{kind} HBM copy", "us_per_launch": us,
+            "algorithmic_bytes_per_launch": alg_bytes, "flop_per_launch": flops,
+            "tensor_frac": flops / (us * 1e-6) / 1e12 / tflops,
+            "traffic": profile_traffic("gemm_wgrad_128x512x4096_split16.md")}
+
+    # the longest kernel on the critical path of a minibatch: the down-projection
+    # with the fused residual add (rows x embed x hidden = 4096 x 128 x 512)
+    Md, Nd, Kd = ENVS_PER_GPU, EMBED, EMBED * SCALE
+    va = torch.relu(torch.randn(Md, Kd, device=f"cuda:{dev}")).bfloat16()
+    vb = (torch.randn(Kd, Nd, device=f"cuda:{dev}") / 16).bfloat16()
+    vh = torch.randn(Md, Nd, device=f"cuda:{dev}").bfloat16()
+    vo = torch.empty(Md, Nd, device=f"cuda:{dev}", dtype=torch.bfloat16)
+
+    def launch_down():
+        return lib.mg_gemm_bf16(va.data_ptr(), 0, Kd, vb.data_ptr(), 1, Nd, Md, Nd, Kd, 2, vo.data_ptr(), Nd,
+                                vh.data_ptr(), Nd, 1, sp)
+
+    usd = _time_launches(launch_down, torch, stream)
+    fd = 2.0 * Md * Nd * Kd
+    roof["critical_path_kernel"] = {
+        "kernel": "gemm_tc_kernel<64, K-major A, MN-major B, +residual> (MLP down-projection, 4096x128x512)",
+        "bound": "tensor", "achieved": fd / (usd * 1e-6) / 1e12, "peak": tflops, "unit": "TFLOP/s",
+        "frac": fd / (usd * 1e-6) / 1e12 / tflops, "us_per_launch": usd, "flop_per_launch": fd,
+        "traffic": profile_traffic("gemm_down_4096x128x512.md")}
+    return roof
 
 
-def profile_traffic():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "gemm_down_4096x128x512.md"
+def profile_traffic(name):
+    """DRAM bytes per launch from a committed ncu summary under profiles/."""
+    p = ROOT / "profiles" / name
     if p.exists():
         m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
         if m:
@@ -496,6 +533,39 @@ def cpu_raw_env(seconds_budget=10.0):
 
 # ------------------------------------------------------------------ main
 
+def profile_minibatch(which):
+    """Builds the configuration's model, collects once, runs one minibatch and
+    one forward as warm-up, then one minibatch and one forward inside the
+    profiler range."""
+    import torch
+
+    from metalgym_b200.session import Gym, PPOModel
+
+    env, n, embed, blocks, rows = {
+        "c3": (ENV, ENVS_PER_GPU, EMBED, LAYERS, 0),
+        "c4": ("rollout_cartpole_continuous", 16384, 128, 2, 8192),
+        "c5": ("rollout_voxelnav", 262144, 256, 4, 32768)}[which]
+    gym = Gym(env, n, seed=0)
+    model = PPOModel(gym, embed, SCALE, blocks, LR, HORIZON, seed=0)
+    model.minibatch_rows = rows
+    model.collect()
+
+    def minibatch(k):
+        if rows:
+            model.train_rows([1, 2, 3, 4], k * rows)
+        else:
+            model.train_slot(k % HORIZON)
+
+    minibatch(0)
+    model.forward()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    minibatch(1)
+    model.forward()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -504,7 +574,13 @@ def main():
     ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-legs", action="store_true", help="skip the configs[3] / configs[4] loops")
+    ap.add_argument("--profile-minibatch", choices=["c3", "c4", "c5"],
+                    help="profiling driver: one training minibatch and one forward of that configuration, "
+                         "bracketed by cudaProfilerStart / Stop (for ncu --profile-from-start off); no JSON line")
     args = ap.parse_args()
+    if args.profile_minibatch:
+        profile_minibatch(args.profile_minibatch)
+        return
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
