@@ -145,6 +145,14 @@ int mg_env_collect_step(const char* kernel_name, const void* head, const void* l
  * Replaces inputForward (model/input.metal:11-27). */
 int mg_input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int in_dim, int out_dim,
                      mg_stream_t stream);
+/* mg_input_forward followed, in the same kernel, by the first block's
+ * LayerNorm of every output row (x_norm, ln_out, stdev exactly as
+ * mg_layernorm_forward computes them). No single counterpart in the
+ * reference: inputForward (model/input.metal:11-27) then layernormForward
+ * (model/layernorm.metal:10-71). */
+int mg_input_forward_layernorm(const float* obs, const void* w, const void* b, void* out, const void* gamma,
+                               const void* beta, void* x_norm, void* ln_out, float* stdev, int rows, int in_dim,
+                               int out_dim, mg_stream_t stream);
 /* Per-row-range partial sums of dW = obs^T dZ and db = sum_r dZ: partial holds
  * mg_input_backward_num_partials(rows, in_dim, out_dim) blocks of (in_dim + 1) x out_dim fp32
  * (rows 0..in_dim-1: dW, row in_dim: db). Replaces inputBackward

@@ -34,6 +34,7 @@ SIGNATURES = {
     "mg_env_collect_step": (I, [S, P, P, P, P, P, P, P, P, P, P, P, I, P]),
     # policy kernels
     "mg_input_forward": (I, [P, P, P, P, I, I, I, P]),
+    "mg_input_forward_layernorm": (I, [P, P, P, P, P, P, P, P, P, I, I, I, P]),
     "mg_input_backward_partials": (I, [P, P, P, I, I, I, P]),
     "mg_input_backward_num_partials": (I, [I, I, I]),
     "mg_layernorm_forward": (I, [P, P, P, P, P, P, I, I, P]),

@@ -543,6 +543,8 @@ BlockFwdArgs PpoEngine::blockArgs(ActSet& a, int n, int rows) {
 int PpoEngine::forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st) {
     const uint16_t* W = weights;
     auto w = [&](uint32_t p) { return static_cast<const void*>(W + params[p].offset); };
+    // (input_forward can also end with block 0's LayerNorm; measured in a
+    // CUDA graph at 4096 rows the two kernels are faster: 5.25 against 5.87 µs)
     MG_TRY(input_forward(obs, w(pInW), w(pInB), a.h, rows, O, E, st));
     for (int n = 0; n < L; n++) {
         if (useFusedBlock(rows)) {

@@ -22,17 +22,34 @@ constexpr int kGaussRowsPerCta = 256;  // Gaussian loss: rows per CTA
 // fp32; each warp computes RPW rows at a time (their observations staged in
 // shared memory), lane l owning the column pairs 2l + 64j, so every weight
 // read serves RPW rows and the shared-memory reads are conflict-free.
-template <int VPT, int RPW>
+//
+// With LN, the first block's LayerNorm of each output row follows in the same
+// kernel (k_layernorm_forward's arithmetic and summation order exactly: the
+// row's bf16 values pass through shared memory so that lane l reads columns
+// l*VPT .. l*VPT + VPT - 1).
+template <int VPT, int RPW, bool LN>
 __global__ void __launch_bounds__(256) k_input_forward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ w,
                                                        const __nv_bfloat16* __restrict__ bias,
                                                        __nv_bfloat16* __restrict__ out, int rows, int inDim, int outDim,
-                                                       RowMap rm) {
+                                                       RowMap rm, LnOutputs ln) {
     constexpr int NP = VPT / 2;  // column pairs per lane
     mg_pdl_trigger();
     mg_pdl_wait();
-    extern __shared__ float s_w[];  // inDim x outDim as fp32, then per warp RPW x inDim observations
+    // inDim x outDim weights as fp32, then per warp RPW x inDim observations,
+    // then (LN) per warp RPW x outDim bf16 output rows
+    extern __shared__ float s_w[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     float* s_obs = s_w + inDim * outDim + warp * RPW * inDim;
+    __nv_bfloat16* s_row = reinterpret_cast<__nv_bfloat16*>(s_w + inDim * outDim + nwarps * RPW * inDim) +
+                           (size_t)warp * RPW * outDim;
+    float g[VPT], bt[VPT];
+    if (LN) {
+#pragma unroll
+        for (int j = 0; j < VPT; j++) {
+            g[j] = bf(ln.gamma[lane * VPT + j]);
+            bt[j] = bf(ln.beta[lane * VPT + j]);
+        }
+    }
     for (int i = threadIdx.x; i < inDim * outDim; i += blockDim.x) s_w[i] = bf(w[i]);
     __syncthreads();
     float2 b[NP];
@@ -73,8 +90,47 @@ __global__ void __launch_bounds__(256) k_input_forward(const float* __restrict__
             if (r0 + q >= rows) break;
             __nv_bfloat16* dst = out + (size_t)(r0 + q) * outDim + 2 * lane;
 #pragma unroll
-            for (int j = 0; j < NP; j++)
-                *reinterpret_cast<__nv_bfloat162*>(dst + 64 * j) = __floats2bfloat162_rn(acc[q][j].x, acc[q][j].y);
+            for (int j = 0; j < NP; j++) {
+                const __nv_bfloat162 hv = __floats2bfloat162_rn(acc[q][j].x, acc[q][j].y);
+                *reinterpret_cast<__nv_bfloat162*>(dst + 64 * j) = hv;
+                if (LN) *reinterpret_cast<__nv_bfloat162*>(s_row + q * outDim + 2 * lane + 64 * j) = hv;
+            }
+        }
+        if (LN) {
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < RPW; q++) {
+                const int r = r0 + q;
+                if (r >= rows) break;
+                // k_layernorm_forward on the row (lane l: columns l*VPT ..)
+                float v[VPT];
+#pragma unroll
+                for (int j = 0; j < VPT; j++) v[j] = bf(s_row[q * outDim + lane * VPT + j]);
+                float sum = 0.0f;
+#pragma unroll
+                for (int j = 0; j < VPT; j++) sum = __fadd_rn(sum, v[j]);
+                const float mean = __fdiv_rn(warp_sum(sum), (float)outDim);
+                float sq = 0.0f;
+#pragma unroll
+                for (int j = 0; j < VPT; j++) {
+                    const float d = __fsub_rn(v[j], mean);
+                    sq = __fadd_rn(sq, __fmul_rn(d, d));
+                }
+                const float var = __fdiv_rn(warp_sum(sq), (float)outDim);
+                const float sd = __fsqrt_rn(__fadd_rn(var, 1e-5f));
+                const float rstd = __fdiv_rn(1.0f, sd);
+                if (lane == 0) ln.stdev[r] = sd;
+                __nv_bfloat16* xo = ln.xNorm + (size_t)r * outDim + lane * VPT;
+                __nv_bfloat16* yo = ln.out + (size_t)r * outDim + lane * VPT;
+#pragma unroll
+                for (int j = 0; j < VPT; j += 2) {
+                    const float x0 = __fmul_rn(__fsub_rn(v[j], mean), rstd);
+                    const float x1 = __fmul_rn(__fsub_rn(v[j + 1], mean), rstd);
+                    *reinterpret_cast<__nv_bfloat162*>(xo + j) = __floats2bfloat162_rn(x0, x1);
+                    *reinterpret_cast<__nv_bfloat162*>(yo + j) = __floats2bfloat162_rn(
+                        __fadd_rn(__fmul_rn(g[j], x0), bt[j]), __fadd_rn(__fmul_rn(g[j + 1], x1), bt[j + 1]));
+                }
+            }
         }
         __syncwarp();
     }
@@ -862,20 +918,21 @@ int grid_rows(int rows, int rowsPerCta) { return (rows + rowsPerCta - 1) / rowsP
 // ------------------------------------------------------------ host launchers
 
 int input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int inDim, int outDim,
-                  cudaStream_t st, RowMap rm) {
+                  cudaStream_t st, RowMap rm, const LnOutputs* ln) {
     MG_CHECK_ARG(rows > 0 && inDim > 0 && outDim % 64 == 0 && outDim <= 1024, "input_forward: bad shape");
     MG_CHECK_ARG(inDim * outDim * 4 <= 160 * 1024, "input_forward: weight too large for shared memory");
     auto W = static_cast<const __nv_bfloat16*>(w);
     auto B = static_cast<const __nv_bfloat16*>(b);
     auto O = static_cast<__nv_bfloat16*>(out);
+    const LnOutputs lno = ln ? *ln : LnOutputs{};
 #define MG_IN_FWD(V, RPW)                                                                                     \
     case V: {                                                                                                 \
-        const size_t sm = ((size_t)inDim * outDim + 8 * RPW * inDim) * 4;                                     \
+        const size_t sm = ((size_t)inDim * outDim + 8 * RPW * inDim) * 4 + (ln ? (size_t)8 * RPW * outDim * 2 : 0); \
         const int blocks = std::min(grid_rows(rows, 8 * RPW), 148 * 4);                                       \
-        auto kern = &k_input_forward<V, RPW>;                                                                 \
+        auto kern = ln ? &k_input_forward<V, RPW, true> : &k_input_forward<V, RPW, false>;                    \
         if (sm > 48 * 1024)                                                                                   \
             MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));    \
-        MG_LAUNCH(kern, blocks, 256, sm, st, obs, W, B, O, rows, inDim, outDim, rm);                          \
+        MG_LAUNCH(kern, blocks, 256, sm, st, obs, W, B, O, rows, inDim, outDim, rm, lno);                     \
         break;                                                                                                \
     }
     switch (outDim / 32) {
@@ -1095,6 +1152,15 @@ extern "C" {
 int mg_input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int in_dim, int out_dim,
                      mg_stream_t s) {
     return mg::input_forward(obs, w, b, out, rows, in_dim, out_dim, MG_STREAM(s));
+}
+
+int mg_input_forward_layernorm(const float* obs, const void* w, const void* b, void* out, const void* gamma,
+                               const void* beta, void* x_norm, void* ln_out, float* stdev, int rows, int in_dim,
+                               int out_dim, mg_stream_t s) {
+    MG_CHECK_ARG(gamma && beta && x_norm && ln_out && stdev, "input_forward_layernorm: null LayerNorm argument");
+    mg::LnOutputs ln{static_cast<const __nv_bfloat16*>(gamma), static_cast<const __nv_bfloat16*>(beta),
+                     static_cast<__nv_bfloat16*>(x_norm), static_cast<__nv_bfloat16*>(ln_out), stdev};
+    return mg::input_forward(obs, w, b, out, rows, in_dim, out_dim, MG_STREAM(s), mg::RowMap{nullptr, 0, 0}, &ln);
 }
 
 int mg_input_backward_partials(const float* obs, const void* dZ, float* partial, int rows, int in_dim, int out_dim,

@@ -1,6 +1,7 @@
 // Internal host interface of the row-wise policy kernels (policy.cu).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -62,8 +63,19 @@ struct RowMap {
     uint64_t total;    // T * R
 };
 
+// LayerNorm outputs of a kernel that ends with the next LayerNorm of its rows.
+struct LnOutputs {
+    const __nv_bfloat16* gamma;
+    const __nv_bfloat16* beta;
+    __nv_bfloat16* xNorm;
+    __nv_bfloat16* out;
+    float* stdev;
+};
+
+// With ln, the LayerNorm of the output rows (as layernorm_forward computes
+// it, bit-identical) is written too.
 int input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int inDim, int outDim,
-                  cudaStream_t st, RowMap rm = RowMap{nullptr, 0, 0});
+                  cudaStream_t st, RowMap rm = RowMap{nullptr, 0, 0}, const LnOutputs* ln = nullptr);
 int input_backward_parts(int rows, int inDim, int outDim);
 int input_backward(const float* obs, const void* dZ, float* partial, int rows, int inDim, int outDim,
                    cudaStream_t st, RowMap rm = RowMap{nullptr, 0, 0});

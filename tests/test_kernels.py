@@ -317,6 +317,33 @@ def test_input_projection(mg, oracle):
     np.testing.assert_allclose(tot[O], g["in_db"], rtol=1e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("R,O,E", [(256, 40, 128), (1000, 4, 128), (4096, 4, 128), (300, 40, 256), (64, 8, 64)])
+def test_input_projection_with_layernorm(mg, R, O, E):
+    """The input projection with block 0's LayerNorm fused in: the projection
+    bit-identical to mg_input_forward, the LayerNorm outputs bit-identical to
+    mg_layernorm_forward on that projection."""
+    rs = np.random.default_rng(R + O + E)
+    obs = rs.standard_normal((R, O)).astype(np.float32)
+    w = bf16_round((rs.standard_normal((O, E)) / np.sqrt(O)).astype(np.float32))
+    b = bf16_round((rs.standard_normal(E) * 0.1).astype(np.float32))
+    gam = bf16_round((1 + rs.standard_normal(E) * 0.1).astype(np.float32))
+    bet = bf16_round((rs.standard_normal(E) * 0.1).astype(np.float32))
+    h_ref = torch.zeros(R * E, dtype=torch.int16, device="cuda")
+    xn_ref, y_ref = torch.zeros_like(h_ref), torch.zeros_like(h_ref)
+    sd_ref = torch.zeros(R, dtype=torch.float32, device="cuda")
+    d_obs, d_w, d_b, d_g, d_bt = dev(obs), dev(w), dev(b), dev(gam), dev(bet)
+    ok(mg, mg.mg_input_forward(d_obs.data_ptr(), d_w.data_ptr(), d_b.data_ptr(), h_ref.data_ptr(), R, O, E, None))
+    ok(mg, mg.mg_layernorm_forward(h_ref.data_ptr(), xn_ref.data_ptr(), y_ref.data_ptr(), d_g.data_ptr(),
+                                   d_bt.data_ptr(), sd_ref.data_ptr(), R, E, None))
+    h, xn, y = torch.zeros_like(h_ref), torch.zeros_like(h_ref), torch.zeros_like(h_ref)
+    sd = torch.zeros_like(sd_ref)
+    ok(mg, mg.mg_input_forward_layernorm(d_obs.data_ptr(), d_w.data_ptr(), d_b.data_ptr(), h.data_ptr(),
+                                         d_g.data_ptr(), d_bt.data_ptr(), xn.data_ptr(), y.data_ptr(), sd.data_ptr(),
+                                         R, O, E, None))
+    sync_status(mg)
+    assert torch.equal(h, h_ref) and torch.equal(xn, xn_ref) and torch.equal(y, y_ref) and torch.equal(sd, sd_ref)
+
+
 def bf16_close(a_u16, b_u16, max_ulps=1, min_exact=0.99):
     d = np.abs(a_u16.astype(np.int32) - b_u16.astype(np.int32))
     assert d.max() <= max_ulps, d.max()
