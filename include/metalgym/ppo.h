@@ -15,7 +15,8 @@
 // caller's RNG, exactly as model/ppo.h:636-702. Slot accessors and
 // headValue() read pinned host mirrors refreshed after device work (see
 // gym.h). Extensions: no compile-time N_EMBED_CFG (embed 64/128/256/512),
-// setComm() for data parallelism over NCCL, and the field minibatchRows
+// setComm() for data parallelism over NCCL, save() / load() checkpoints of the
+// training state, and the field minibatchRows
 // (0, the default, keeps the reference's one-slot minibatches; B > 0 trains
 // on B rollout rows per minibatch, every row once per epoch in a random
 // order).
@@ -228,6 +229,26 @@ struct PPOModel {
     // ---- extension: data parallelism (ncclComm_t from mg_comm_init)
     void setComm(void* comm, int rank, int world) {
         metalgym::check_or_exit(mg_ppo_set_comm(handle, comm, rank, world), "setComm");
+    }
+    // Extension: checkpoint / resume of the whole training state (mg_ppo_save).
+    void save(const char* path) {
+        pushHyper();
+        metalgym::check_or_exit(mg_ppo_save(handle, path), "save");
+    }
+    void load(const char* path) {
+        metalgym::check_or_exit(mg_ppo_load(handle, path), "load");
+        float h[6];
+        metalgym::check_or_exit(mg_ppo_get_hyper(handle, h), "load");
+        clip = h[0];
+        valueCoef = h[1];
+        entropyCoef = h[2];
+        maxGradNorm = h[3];
+        gamma = h[4];
+        lambda = h[5];
+        int rows = 0;
+        metalgym::check_or_exit(mg_ppo_minibatch_rows(handle, &rows), "load");
+        minibatchRows = (uint32_t)rows;
+        afterDeviceWork(MG_PPO_HEAD);
     }
 
    private:

@@ -303,6 +303,15 @@ int mg_ppo_collect(mg_ppo_t model);
 int mg_ppo_train(mg_ppo_t model, int epochs);
 /* trainSlot(t) (model/ppo.h:906-916); blocks until done. */
 int mg_ppo_train_slot(mg_ppo_t model, int t);
+/* Checkpoint of the training state (no counterpart in the reference, which
+ * has none): weights, fp32 master, Adam moments, step counter, learning rate,
+ * hyperparameters, minibatch rows, the host shuffle generator and the
+ * rollout position (last observation, env states, done flags, RNG words of
+ * the model's gym). mg_ppo_load restores it into a model of the same shapes
+ * and environment; training then continues exactly as from the saved model.
+ * Blocks until done. */
+int mg_ppo_save(mg_ppo_t model, const char* path);
+int mg_ppo_load(mg_ppo_t model, const char* path);
 /* Rows per training minibatch (no counterpart in the reference, whose
  * minibatch is always one time slot, model/ppo.h:906-923). 0 (the default)
  * keeps the reference's slot minibatches; B > 0 makes every epoch of

@@ -234,6 +234,12 @@ int mg_ppo_train(mg_ppo_t model, int epochs) {
 int mg_ppo_train_slot(mg_ppo_t model, int t) {
     return model ? P(model)->trainSlot(t) : mg::fail(MG_ERR_ARGUMENT, "null model");
 }
+int mg_ppo_save(mg_ppo_t model, const char* path) {
+    return model ? P(model)->save(path) : mg::fail(MG_ERR_ARGUMENT, "null model");
+}
+int mg_ppo_load(mg_ppo_t model, const char* path) {
+    return model ? P(model)->load(path) : mg::fail(MG_ERR_ARGUMENT, "null model");
+}
 int mg_ppo_set_minibatch_rows(mg_ppo_t model, int rows) {
     return model ? P(model)->setMinibatchRows(rows) : mg::fail(MG_ERR_ARGUMENT, "null model");
 }

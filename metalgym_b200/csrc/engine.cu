@@ -20,7 +20,9 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
+#include <sstream>
 #include <string>
 
 #include "block.h"
@@ -929,6 +931,140 @@ int PpoEngine::logStd(int k, float* out) {
     MG_CUDA_TRY(cudaStreamSynchronize(gym->stream));
     MG_CUDA_TRY(cudaMemcpy(&h, weights + params[pLogStd].offset + k, 2, cudaMemcpyDeviceToHost));
     *out = host_bf2f(h);
+    return MG_OK;
+}
+
+// ------------------------------------------------------------ checkpoints
+
+namespace {
+
+constexpr char kCkptMagic[8] = {'M', 'G', 'C', 'K', 'P', 'T', '0', '1'};
+
+struct CkptHeader {
+    char magic[8];
+    uint32_t rows, obsDim, actDim, embed, hidden, layers, horizon, continuous;
+    uint32_t stateBytes, obsBytes, actionBytes, paramCount;
+    uint64_t optCount;
+    float stepCounter, lr;
+    int32_t minibatchRows, rolloutStarted;
+    float hyper[6];  // clip, valueCoef, entropyCoef, maxGradNorm, gamma, lambda
+    uint32_t rngTextBytes;
+};
+
+struct File {
+    FILE* f = nullptr;
+    ~File() {
+        if (f) fclose(f);
+    }
+};
+
+// Device buffer <-> file through a host staging vector.
+int write_dev(FILE* f, const void* dev, size_t bytes) {
+    std::vector<char> h(bytes);
+    MG_CUDA_TRY(cudaMemcpy(h.data(), dev, bytes, cudaMemcpyDeviceToHost));
+    if (fwrite(h.data(), 1, bytes, f) != bytes) return fail(MG_ERR_ARGUMENT, "checkpoint: write failed");
+    return MG_OK;
+}
+int read_dev(FILE* f, void* dev, size_t bytes) {
+    std::vector<char> h(bytes);
+    if (fread(h.data(), 1, bytes, f) != bytes) return fail(MG_ERR_ARGUMENT, "checkpoint: file truncated");
+    MG_CUDA_TRY(cudaMemcpy(dev, h.data(), bytes, cudaMemcpyHostToDevice));
+    return MG_OK;
+}
+
+}  // namespace
+
+int PpoEngine::save(const char* path) {
+    MG_CHECK_ARG(path && *path, "save: empty path");
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    MG_CUDA_TRY(cudaStreamSynchronize(gym->stream));
+    File file;
+    file.f = fopen(path, "wb");
+    if (!file.f) return fail(MG_ERR_ARGUMENT, std::string("save: cannot open ") + path);
+    std::ostringstream rs;
+    rs << hostRng;
+    const std::string rng = rs.str();
+    CkptHeader h{};
+    std::memcpy(h.magic, kCkptMagic, 8);
+    h.rows = R; h.obsDim = O; h.actDim = A; h.embed = E; h.hidden = H; h.layers = L; h.horizon = T;
+    h.continuous = cont ? 1 : 0;
+    h.stateBytes = (uint32_t)gym->ops->state_bytes;
+    h.obsBytes = (uint32_t)gym->ops->obs_bytes;
+    h.actionBytes = (uint32_t)actBytes;
+    h.paramCount = (uint32_t)params.size();
+    h.optCount = optCount;
+    h.stepCounter = stepCounter;
+    h.lr = lr;
+    h.minibatchRows = mbRows;
+    h.rolloutStarted = rolloutStarted ? 1 : 0;
+    const float hy[6] = {hp.clip, hp.valueCoef, hp.entropyCoef, hp.maxGradNorm, hp.gamma, hp.lambda};
+    std::memcpy(h.hyper, hy, sizeof(hy));
+    h.rngTextBytes = (uint32_t)rng.size();
+    FILE* f = file.f;
+    if (fwrite(&h, sizeof(h), 1, f) != 1 || fwrite(rng.data(), 1, rng.size(), f) != rng.size() ||
+        fwrite(slotOrder.data(), 4, slotOrder.size(), f) != slotOrder.size())
+        return fail(MG_ERR_ARGUMENT, "save: write failed");
+    MG_TRY(write_dev(f, weights, optCount * 2));
+    MG_TRY(write_dev(f, master, optCount * 4));
+    MG_TRY(write_dev(f, mom, optCount * 4));
+    MG_TRY(write_dev(f, var, optCount * 4));
+    MG_TRY(write_dev(f, obsSlots + (size_t)T * R * O, (size_t)R * O * 4));  // next collect's first obs
+    MG_TRY(write_dev(f, gym->states, (size_t)R * h.stateBytes));
+    MG_TRY(write_dev(f, gym->done, (size_t)R));
+    MG_TRY(write_dev(f, gym->rng, (size_t)R * 4));
+    MG_TRY(write_dev(f, gym->obs, (size_t)R * h.obsBytes));
+    return MG_OK;
+}
+
+int PpoEngine::load(const char* path) {
+    MG_CHECK_ARG(path && *path, "load: empty path");
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    MG_CUDA_TRY(cudaStreamSynchronize(gym->stream));
+    File file;
+    file.f = fopen(path, "rb");
+    if (!file.f) return fail(MG_ERR_ARGUMENT, std::string("load: cannot open ") + path);
+    FILE* f = file.f;
+    CkptHeader h{};
+    if (fread(&h, sizeof(h), 1, f) != 1 || std::memcmp(h.magic, kCkptMagic, 8) != 0)
+        return fail(MG_ERR_ARGUMENT, "load: not a metalgym_b200 checkpoint");
+    const bool same = h.rows == (uint32_t)R && h.obsDim == (uint32_t)O && h.actDim == (uint32_t)A &&
+                      h.embed == (uint32_t)E && h.hidden == (uint32_t)H && h.layers == (uint32_t)L &&
+                      h.horizon == (uint32_t)T && h.continuous == (cont ? 1u : 0u) &&
+                      h.stateBytes == gym->ops->state_bytes && h.obsBytes == gym->ops->obs_bytes &&
+                      h.actionBytes == actBytes && h.paramCount == params.size() && h.optCount == optCount;
+    if (!same) return fail(MG_ERR_ARGUMENT, "load: checkpoint of a different model or environment shape");
+    std::string rng(h.rngTextBytes, '\0');
+    std::vector<uint32_t> order(T);
+    if (fread(&rng[0], 1, rng.size(), f) != rng.size() || fread(order.data(), 4, order.size(), f) != order.size())
+        return fail(MG_ERR_ARGUMENT, "load: file truncated");
+    MG_TRY(read_dev(f, weights, optCount * 2));
+    MG_TRY(read_dev(f, master, optCount * 4));
+    MG_TRY(read_dev(f, mom, optCount * 4));
+    MG_TRY(read_dev(f, var, optCount * 4));
+    MG_TRY(read_dev(f, obsSlots + (size_t)T * R * O, (size_t)R * O * 4));
+    MG_TRY(read_dev(f, gym->states, (size_t)R * h.stateBytes));
+    MG_TRY(read_dev(f, gym->done, (size_t)R));
+    MG_TRY(read_dev(f, gym->rng, (size_t)R * 4));
+    MG_TRY(read_dev(f, gym->obs, (size_t)R * h.obsBytes));
+    std::istringstream rs(rng);
+    rs >> hostRng;
+    if (rs.fail()) return fail(MG_ERR_ARGUMENT, "load: bad generator state");
+    slotOrder = order;
+    stepCounter = h.stepCounter;
+    lr = h.lr;
+    rolloutStarted = h.rolloutStarted != 0;
+    hp.clip = h.hyper[0];
+    hp.valueCoef = h.hyper[1];
+    hp.entropyCoef = h.hyper[2];
+    hp.maxGradNorm = h.hyper[3];
+    hp.gamma = h.hyper[4];
+    hp.lambda = h.hyper[5];
+    MG_TRY(setMinibatchRows(h.minibatchRows));
+    // a captured train graph holds lr in its Adam launches
+    if (trainExec) {
+        cudaGraphExecDestroy(trainExec);
+        trainExec = nullptr;
+    }
     return MG_OK;
 }
 

@@ -91,6 +91,12 @@ class PpoEngine {
     int setLogStd(float v);
     int logStd(int k, float* out);
     int setComm(void* comm, int rank, int world);
+    // Checkpoint of the whole training state: parameters and Adam moments,
+    // step counter, the host shuffle generator, the last rollout observation
+    // and the gym's env states / done flags / RNG words, so that training
+    // resumed from it continues exactly as it would have.
+    int save(const char* path);
+    int load(const char* path);
 
     GymCore* gym;
     int R, O, A, E, H, L, T;

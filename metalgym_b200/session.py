@@ -142,6 +142,14 @@ class PPOModel:
     def train_slot(self, t: int):
         check(lib().mg_ppo_train_slot(self._h, t), "trainSlot")
 
+    def save(self, path) -> None:
+        """Checkpoint of the training state (mg_ppo_save)."""
+        check(lib().mg_ppo_save(self._h, str(path).encode()), "save")
+
+    def load(self, path) -> None:
+        """Restores a checkpoint of a model of the same shapes (mg_ppo_load)."""
+        check(lib().mg_ppo_load(self._h, str(path).encode()), "load")
+
     @property
     def minibatch_rows(self) -> int:
         """Rows per training minibatch: 0 = one time slot (the reference)."""

@@ -315,6 +315,42 @@ def test_config5_voxelnav_full_size(mg):
     assert model.step_counter() == 256
 
 
+@pytest.mark.parametrize("name,rows", [("rollout_cartpole", 0), ("rollout_cartpole_continuous", 512)])
+def test_checkpoint_resume_is_exact(mg, tmp_path, name, rows):
+    """Training resumed from a checkpoint continues exactly: a fresh model
+    (different seed) loaded from the checkpoint reaches the same weights,
+    Adam state and rollout as the model that kept going."""
+    gym, model = make(name, 1024, 128, 4, 2, 4, seed=1)
+    model.minibatch_rows = rows
+    for _ in range(2):
+        model.collect()
+        model.train(2)
+    ck = tmp_path / "state.ckpt"
+    model.save(ck)
+    for _ in range(2):
+        model.collect()
+        model.train(2)
+    gym2, model2 = make(name, 1024, 128, 4, 2, 4, seed=9)
+    model2.load(ck)
+    assert model2.minibatch_rows == rows
+    for _ in range(2):
+        model2.collect()
+        model2.train(2)
+    for buf in ("weights", "master", "momentum", "variance", "obs", "actions", "reward", "done"):
+        assert np.array_equal(model.download(buf), model2.download(buf)), buf
+    assert model.step_counter() == model2.step_counter()
+
+
+def test_checkpoint_rejects_other_shapes(mg, tmp_path):
+    from metalgym_b200 import MgError
+
+    gym, model = make("rollout_cartpole", 512, 128, 4, 2, 4)
+    model.save(tmp_path / "a.ckpt")
+    gym2, model2 = make("rollout_cartpole", 512, 64, 4, 2, 4)
+    with pytest.raises(MgError, match="different model"):
+        model2.load(tmp_path / "a.ckpt")
+
+
 def test_row_mode_rejects_non_dividing_rows(mg):
     gym, model = make("rollout_cartpole", 1000, 64, 2, 1, 4)
     from metalgym_b200 import MgError
