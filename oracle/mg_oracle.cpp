@@ -404,6 +404,9 @@ struct OrcModel {
     uint32_t pInW, pInB, pLnFg, pLnFb, pHead, pLogStd;
     std::vector<uint32_t> pLnG, pLnB, pUp, pDown;
 
+    std::mt19937 hostRng;            // slot shuffle (model/ppo.h:349, 920), seeded with the model seed
+    std::vector<uint32_t> slotOrder;
+
     const uint16_t* W(uint32_t p) const { return weights.data() + params[p].offset; }
     float* G(uint32_t p) { return grad.data() + params[p].offset; }
 };
@@ -422,6 +425,9 @@ ORC_API OrcModel* orc_model_create(uint32_t rows, uint32_t obsDim, uint32_t actD
     m->L = layers;
     m->T = horizon;
     m->lr = lr;
+    m->hostRng.seed(seed);
+    m->slotOrder.resize(horizon);
+    for (uint32_t t = 0; t < horizon; t++) m->slotOrder[t] = t;
     std::vector<std::vector<uint16_t>> init;
     auto add = [&](uint32_t count, bool gf) {
         m->params.push_back(ParamSpec{count, gf, 0});
@@ -654,6 +660,35 @@ ORC_API void orc_model_train_minibatch(OrcModel* m, const float* obs, const void
     const float b2p = std::pow(0.999f, m->stepCounter);
     orc_adam_step(m->master.data(), m->grad.data(), m->mom.data(), m->var.data(), m->weights.data(), *normSq,
                   m->optCount, m->lr, b1p, b2p, m->maxGradNorm);
+}
+
+// model/ppo.h:918-923 over caller-owned slot buffers (layouts of
+// orc_model_collect): per epoch the slot order is shuffled with the model's
+// mt19937 and every slot is one minibatch (orc_model_train_minibatch).
+// lastStats (optional) gets the mean LossStats of the last minibatch
+// (policy, value, entropy, approxKl, clipFrac, gradNorm).
+ORC_API void orc_model_train(OrcModel* m, const float* obsSlots, const void* actionSlots, const float* logProbSlots,
+                             const float* advSlots, const float* retSlots, uint32_t epochs, float* lastStats) {
+    const uint32_t R = m->rows, O = m->obsDim;
+    const size_t actBytes = m->continuous ? (size_t)m->actDim * 4 : 4;
+    std::vector<float> stats((size_t)R * 5);
+    float nsq = 0.0f;
+    for (uint32_t e = 0; e < epochs; e++) {
+        std::shuffle(m->slotOrder.begin(), m->slotOrder.end(), m->hostRng);
+        for (uint32_t t : m->slotOrder)
+            orc_model_train_minibatch(m, obsSlots + (size_t)t * R * O,
+                                      static_cast<const char*>(actionSlots) + (size_t)t * R * actBytes,
+                                      advSlots + (size_t)t * R, retSlots + (size_t)t * R,
+                                      logProbSlots + (size_t)t * R, R, stats.data(), &nsq);
+    }
+    if (lastStats) {
+        for (int k = 0; k < 5; k++) {
+            double acc = 0.0;
+            for (uint32_t r = 0; r < R; r++) acc += stats[(size_t)r * 5 + k];
+            lastStats[k] = (float)(acc / R);
+        }
+        lastStats[5] = std::sqrt(nsq);
+    }
 }
 
 // model/ppo.h:716-751

@@ -83,6 +83,13 @@ void orc_model_train_minibatch(OrcModel* m, const float* obs, const void* action
 void orc_model_gradient(OrcModel* m, const float* obs, const void* actions, const float* advantages,
                         const float* returns, const float* oldLogProb, uint32_t rows, float* stats, float* normSq);
 
+// train(epochs) (model/ppo.h:918-923) over caller-owned slot buffers: per epoch
+// the slot order is shuffled with the model's mt19937 (seeded with the model
+// seed) and each slot is one minibatch. lastStats (optional, 6 floats): mean
+// LossStats of the last minibatch.
+void orc_model_train(OrcModel* m, const float* obsSlots, const void* actionSlots, const float* logProbSlots,
+                     const float* advSlots, const float* retSlots, uint32_t epochs, float* lastStats);
+
 // Environment step callback with the signature of oracle/_ref's ref_rollout
 // (or any host build of an Environment): steps n envs once.
 typedef void (*orc_env_fn)(int which, void* states, const void* actions, void* obs, float* reward, uint8_t* done,

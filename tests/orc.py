@@ -82,6 +82,7 @@ def load_oracle():
     _sig(lib, "orc_model_train_minibatch", None, [P, P, P, P, P, P, U, P, P])
     _sig(lib, "orc_model_gradient", None, [P, P, P, P, P, P, U, P, P])
     _sig(lib, "orc_model_collect", None, [P, P, I, P, P, P, P, P, P, P, P, P, P, P, P, P, I])
+    _sig(lib, "orc_model_train", None, [P, P, P, P, P, P, U, P])
     return lib
 
 
