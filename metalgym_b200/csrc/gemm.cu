@@ -28,7 +28,17 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
 template <int BN, bool AMN, bool BMN, int EPI>
 int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits,
                       cudaStream_t st) {
-    using S = PersistShape<BN>;
+    using S = PersistShape<BN, EPI>;
+    // output / aux maps of the staged epilogue: boxes of 64 columns x 32 rows
+    EpiMaps em{};
+    if (S::STAGED) {
+        int rc = make_tmap_bf16(&em.out, p.out, p.N, p.M, p.ldo, 32);
+        if (rc) return rc;
+        if (EPI == kEpiBf16Resid || EPI == kEpiBf16Mask) {
+            rc = make_tmap_bf16(&em.aux, p.aux, p.N, p.M, p.ldaux, 32);
+            if (rc) return rc;
+        }
+    }
     auto kern = gemm_tc_persistent<BN, AMN, BMN, EPI>;
     static uint64_t attr_done = 0;  // one bit per device
     int dev = 0;
@@ -39,7 +49,7 @@ int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPa
     }
     const int units = p.tilesM * p.tilesN * splits;
     const int grid = std::min(units, num_sms());
-    MG_CUDA_TRY(mg_launch(kern, dim3(grid), dim3(192), (size_t)S::SMEM_BYTES, st, ta, tb, p));
+    MG_CUDA_TRY(mg_launch(kern, dim3(grid), dim3(192), (size_t)S::SMEM_BYTES, st, ta, tb, em, p));
     return check_launch("gemm_tc_persistent");
 }
 

@@ -10,7 +10,11 @@
 //              tfull[a] when the tile's K range is done
 //   warps 2-5  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, i.e.
 //              output rows 32 (w % 4) + lane of the tile, applies the
-//              epilogue and stores; each warp then arrives on tempty[a]
+//              epilogue and arrives on tempty[a]. bf16 outputs go through a
+//              per-warp shared-memory slab (32 rows x BN, 128-byte swizzled)
+//              that one lane stores with TMA; the aux operand of the residual
+//              and mask epilogues is loaded into the same slab by TMA first.
+//              fp32 split-K partials are stored directly.
 //
 // Units are numbered with the N tile fastest, so the CTAs working at the same
 // time share A tiles through L2. Same operand layouts, epilogues and
@@ -21,17 +25,27 @@
 
 namespace mg {
 
-template <int BN>
+template <int BN, int EPI>
 struct PersistShape {
     static constexpr int BM = 128;
     static constexpr int BK = 64;
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr bool STAGED = EPI != kEpiF32;         // bf16 output through shared memory + TMA
+    static constexpr int SLAB = 32 * BN * 2;                 // per epilogue warp: 32 rows x BN bf16
+    static constexpr int STAGES = STAGED ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int SLAB_OFF = STAGES * STAGE_BYTES;
+    static constexpr int BAR_OFF = SLAB_OFF + (STAGED ? 4 * SLAB : 0);
     static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (256 or 512 columns)
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int SMEM_BYTES = BAR_OFF + 256 /*barriers*/ + 1024 /*align*/;
 };
+
+// Byte offset of 16-byte chunk k (8 bf16, 0..BN/8-1) of slab row r (0..31)
+// in a slab of 64-column boxes of 32 rows x 128 bytes, 128-byte swizzled.
+__device__ __forceinline__ uint32_t slab_offset(int r, int k) {
+    return (uint32_t)((k >> 3) * 4096 + r * 128 + (((k & 7) ^ (r & 7)) << 4));
+}
 
 // One 32-column chunk of one output row: epilogue and store.
 template <int EPI>
@@ -64,19 +78,26 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
     }
 }
 
+// Output and aux tensor maps of the staged epilogue (boxes of 64 columns x 32 rows).
+struct EpiMaps {
+    CUtensorMap out, aux;
+};
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const GemmParams p) {
-    using S = PersistShape<BN>;
+                       const __grid_constant__ EpiMaps em, const GemmParams p) {
+    using S = PersistShape<BN, EPI>;
+    constexpr bool HAS_AUX = EPI == kEpiBf16Resid || EPI == kEpiBf16Mask;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::STAGES * S::STAGE_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
     uint64_t* empty = full + S::STAGES;
     uint64_t* tfull = empty + S::STAGES;  // [2]
     uint64_t* tempty = tfull + 2;         // [2]
     uint64_t* done = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* auxFull = done + 1;         // [4], one per epilogue warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(auxFull + 4);
 
     mg_pdl_trigger();
     const int warp = threadIdx.x >> 5;
@@ -94,9 +115,12 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
         }
         mbar_init(done, 1);
+        for (int w = 0; w < 4; w++) mbar_init(&auxFull[w], 1);
         fence_barrier_init();
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
+        if (S::STAGED) prefetch_tensormap(&em.out);
+        if (HAS_AUX) prefetch_tensormap(&em.aux);
     }
     if (warp == 2) {
         tmem_alloc(tmem_slot, S::TMEM_COLS);
@@ -196,19 +220,36 @@ __global__ void __launch_bounds__(192, 1)
     } else {
         // ---- epilogue: thread owns row 32 (warp % 4) + lane of each tile
         const int q = warp & 3;
+        uint8_t* slab = smem + S::SLAB_OFF + q * S::SLAB;
         int t = 0;
+        int auxWaited = 0;  // aux loads this warp has seen land
         for (int u = blockIdx.x; u < units; u += gridDim.x, t++) {
             const int nt = u % p.tilesN;
             const int mt = (u / p.tilesN) % p.tilesM;
             const int z = u / tilesMN;
             const int a = t & 1;
+            const int row0 = mt * S::BM + q * 32;  // first row of this warp's slab
+            const int n0 = nt * BN;
+            if (S::STAGED && lane == 0) {
+                bulk_wait_read<0>();  // the previous tile's store has read the slab
+                if (HAS_AUX) {
+                    mbar_arrive_expect_tx(&auxFull[q], S::SLAB);
+#pragma unroll
+                    for (int j = 0; j < BN / 64; j++) tma_load_2d(slab + j * 4096, &em.aux, n0 + 64 * j, row0, &auxFull[q]);
+                }
+            }
+            __syncwarp();
             if (!mbar_wait_warp(&tfull[a], (t >> 1) & 1, p.status, kDevTimeoutDone)) break;
+            if (HAS_AUX) {
+                if (!mbar_wait_warp(&auxFull[q], t & 1, p.status, kDevTimeoutFull)) break;
+                auxWaited = t + 1;
+            }
             tc_fence_after();
-            const int row = mt * S::BM + q * 32 + lane;
+            const int row = row0 + lane;
             const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
 #pragma unroll 1
             for (int c = 0; c < BN / 32; c++) {
-                const int col = nt * BN + c * 32;
+                const int col = n0 + c * 32;
                 float v[32];
                 tmem_ld32(acc + (uint32_t)(c * 32), v);
                 if (c == BN / 32 - 1) {
@@ -217,9 +258,60 @@ __global__ void __launch_bounds__(192, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[a]);
                 }
-                if (row < p.M && col < p.N) epilogue_chunk<EPI>(p, row, col, z, v);
+                if (!S::STAGED) {
+                    if (row < p.M && col < p.N) epilogue_chunk<EPI>(p, row, col, z, v);
+                    continue;
+                }
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    uint4* cell = reinterpret_cast<uint4*>(slab + slab_offset(lane, c * 4 + k));
+                    float x[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) x[i] = v[8 * k + i];
+                    if (EPI == kEpiBf16Relu) {
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float r = round_bf16(x[i]);
+                            x[i] = r > 0.0f ? r : r * 0.0f;
+                        }
+                    } else if (HAS_AUX) {
+                        const uint4 w = *cell;
+                        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+                        float au[8];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            au[2 * i] = __uint_as_float(ww[i] << 16);
+                            au[2 * i + 1] = __uint_as_float(ww[i] & 0xffff0000u);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            x[i] = EPI == kEpiBf16Resid ? au[i] + round_bf16(x[i])
+                                                        : round_bf16(x[i]) * (au[i] > 0.0f ? 1.0f : 0.0f);
+                    }
+                    uint32_t o[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        __nv_bfloat162 h2 = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+                        o[i] = *reinterpret_cast<uint32_t*>(&h2);
+                    }
+                    *cell = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            if (S::STAGED) {
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int j = 0; j < BN / 64; j++)
+                        if (n0 + 64 * j < p.N && row0 < p.M) tma_store_2d(&em.out, n0 + 64 * j, row0, slab + j * 4096);
+                    bulk_commit();
+                }
             }
         }
+        // after a timeout: the aux load issued for tile t has landed before the CTA exits
+        if (HAS_AUX && lane == 0 && auxWaited < t + 1 && t < (units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x)
+            mbar_wait(&auxFull[q], t & 1, p.status, kDevTimeoutFull);
+        if (S::STAGED && lane == 0) bulk_wait<0>();  // every store complete before the CTA exits
     }
 
     tc_fence_before();
