@@ -139,10 +139,11 @@ __global__ void __launch_bounds__(256) k_input_forward(const float* __restrict__
 // model/input.metal:38-60: per-CTA partial sums over a contiguous range of
 // rowsPerCta rows of dW[k, c] = sum_r obs[r, k] dZ[r, c] and db[c] = sum_r
 // dZ[r, c]; partial[blockIdx] = [(inDim + 1) x outDim]: rows 0..inDim-1 dW,
-// row inDim db, each summed in row order. The CTA's dZ rows (bf16) and
-// observation rows (fp32, gathered through the row map) are staged in
-// shared memory; a thread owns a column and sweeps k in chunks of 8
-// registers.
+// row inDim db, each summed in row order with fused multiply-adds (the
+// reference's order of these sums is unspecified: fp32 atomics). The CTA's
+// dZ rows (bf16) and observation rows (fp32, gathered through the row map)
+// are staged in shared memory; a thread owns a column and sweeps k in
+// chunks of 8 registers.
 __global__ void __launch_bounds__(256) k_input_backward(const float* __restrict__ obs, const __nv_bfloat16* __restrict__ dZ,
                                                         float* __restrict__ partial, int rows, int inDim, int outDim,
                                                         int rowsPerCta, RowMap rm) {
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(256) k_input_backward(const float* __restrict_
                     const float d = bf(s_dz[r * outDim + c]);
                     const float* o = s_obs + r * inDim + k0;
 #pragma unroll
-                    for (int k = 0; k < 8; k++) acc[k] = __fadd_rn(acc[k], __fmul_rn(o[k], d));
+                    for (int k = 0; k < 8; k++) acc[k] = __fmaf_rn(o[k], d, acc[k]);
                 }
             } else {
                 for (int r = 0; r < nr; r++) {
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(256) k_input_backward(const float* __restrict_
                     const float* o = s_obs + r * inDim + k0;
 #pragma unroll
                     for (int k = 0; k < 8; k++)
-                        if (k0 + k < inDim) acc[k] = __fadd_rn(acc[k], __fmul_rn(o[k], d));
+                        if (k0 + k < inDim) acc[k] = __fmaf_rn(o[k], d, acc[k]);
                 }
             }
 #pragma unroll
@@ -282,45 +283,63 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
     }
     const int r0 = blockIdx.x * rowsPerCta;
     const int r1 = min(rows, r0 + rowsPerCta);
-#pragma unroll 2
-    for (int r = r0 + warp; r < r1; r += 8) {
-        float dz[VPT], xn[VPT], dxn[VPT];
-        const size_t base = (size_t)r * E + c0;
+    // rows r and r + 8 of the warp per step: both rows' loads are issued before
+    // either row is computed (two rows of memory in flight per warp); the sums
+    // run over the rows in the same order as one row at a time
+    for (int r = r0 + warp; r < r1; r += 16) {
+        float dz[2][VPT], xn[2][VPT], rs[2][VPT], sdv[2];
+        const bool two = r + 8 < r1;
 #pragma unroll
-        for (int j = 0; j < VPT; j += 2) {
-            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dZ + base + j));
-            const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xNorm + base + j));
-            dz[j] = a.x;
-            dz[j + 1] = a.y;
-            xn[j] = c.x;
-            xn[j + 1] = c.y;
-        }
-        float s1 = 0.0f, s2 = 0.0f;
-#pragma unroll
-        for (int j = 0; j < VPT; j++) {
-            dg[j] = __fadd_rn(dg[j], rbf(__fmul_rn(xn[j], dz[j])));
-            db[j] = __fadd_rn(db[j], dz[j]);
-            dxn[j] = rbf(__fmul_rn(dz[j], g[j]));
-            s1 = __fadd_rn(s1, dxn[j]);
-            s2 = __fadd_rn(s2, rbf(__fmul_rn(dxn[j], xn[j])));
-        }
-        const float m1 = __fdiv_rn(warp_sum(s1), (float)E);
-        const float m2 = __fdiv_rn(warp_sum(s2), (float)E);
-        const float rdev = __fdiv_rn(1.0f, stdev[r]);
-        float dx[VPT];
-#pragma unroll
-        for (int j = 0; j < VPT; j++) dx[j] = __fmul_rn(rdev, __fsub_rn(__fsub_rn(dxn[j], m1), __fmul_rn(xn[j], m2)));
-        if (resid) {
+        for (int k = 0; k < 2; k++) {
+            if (k == 1 && !two) break;
+            const size_t base = (size_t)(r + 8 * k) * E + c0;
 #pragma unroll
             for (int j = 0; j < VPT; j += 2) {
-                const float2 o = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(resid + base + j));
-                *reinterpret_cast<__nv_bfloat162*>(residOut + base + j) =
-                    __floats2bfloat162_rn(__fadd_rn(rbf(dx[j]), o.x), __fadd_rn(rbf(dx[j + 1]), o.y));
+                const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dZ + base + j));
+                const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xNorm + base + j));
+                dz[k][j] = a.x;
+                dz[k][j + 1] = a.y;
+                xn[k][j] = c.x;
+                xn[k][j + 1] = c.y;
+                if (resid) {
+                    const float2 o = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(resid + base + j));
+                    rs[k][j] = o.x;
+                    rs[k][j + 1] = o.y;
+                }
             }
-        } else {
+            sdv[k] = stdev[r + 8 * k];
+        }
 #pragma unroll
-            for (int j = 0; j < VPT; j += 2)
-                *reinterpret_cast<__nv_bfloat162*>(dZ + base + j) = __floats2bfloat162_rn(dx[j], dx[j + 1]);
+        for (int k = 0; k < 2; k++) {
+            if (k == 1 && !two) break;
+            const size_t base = (size_t)(r + 8 * k) * E + c0;
+            float dxn[VPT];
+            float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < VPT; j++) {
+                dg[j] = __fadd_rn(dg[j], rbf(__fmul_rn(xn[k][j], dz[k][j])));
+                db[j] = __fadd_rn(db[j], dz[k][j]);
+                dxn[j] = rbf(__fmul_rn(dz[k][j], g[j]));
+                s1 = __fadd_rn(s1, dxn[j]);
+                s2 = __fadd_rn(s2, rbf(__fmul_rn(dxn[j], xn[k][j])));
+            }
+            const float m1 = __fdiv_rn(warp_sum(s1), (float)E);
+            const float m2 = __fdiv_rn(warp_sum(s2), (float)E);
+            const float rdev = __fdiv_rn(1.0f, sdv[k]);
+            float dx[VPT];
+#pragma unroll
+            for (int j = 0; j < VPT; j++)
+                dx[j] = __fmul_rn(rdev, __fsub_rn(__fsub_rn(dxn[j], m1), __fmul_rn(xn[k][j], m2)));
+            if (resid) {
+#pragma unroll
+                for (int j = 0; j < VPT; j += 2)
+                    *reinterpret_cast<__nv_bfloat162*>(residOut + base + j) = __floats2bfloat162_rn(
+                        __fadd_rn(rbf(dx[j]), rs[k][j]), __fadd_rn(rbf(dx[j + 1]), rs[k][j + 1]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < VPT; j += 2)
+                    *reinterpret_cast<__nv_bfloat162*>(dZ + base + j) = __floats2bfloat162_rn(dx[j], dx[j + 1]);
+            }
         }
     }
 #pragma unroll
