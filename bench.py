@@ -121,7 +121,7 @@ def run_mine(args, rank, world, local_rank, dist):
     import torch
 
     import metalgym_b200
-    from metalgym_b200.dist import env_shard, nccl_comm
+    from metalgym_b200.dist import env_shard, nccl_comm, p2p_allreduce
     from metalgym_b200.session import Gym, PPOModel
 
     torch.cuda.set_device(local_rank)
@@ -129,9 +129,19 @@ def run_mine(args, rank, world, local_rank, dist):
     gym = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=env_shard(rank, ENVS_PER_GPU), device=local_rank)
     model = PPOModel(gym, EMBED, SCALE, LAYERS, LR, HORIZON, seed=0)
     comm = None
-    if world > 1:
+
+    def connect(m):
+        """The gradient all-reduce of a model: NCCL, or the library's own over NVLink peer memory."""
+        if world == 1:
+            return
+        if args.allreduce == "nccl":
+            m.set_comm(comm, rank, world)
+        else:
+            p2p_allreduce(m, dist, rank, world)
+
+    if world > 1 and args.allreduce == "nccl":
         comm = nccl_comm(dist, rank, world, local_rank)
-        model.set_comm(comm, rank, world)
+    connect(model)
     stream = torch.cuda.ExternalStream(gym.stream(), device=local_rank)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{local_rank}")
 
@@ -238,7 +248,7 @@ def run_mine(args, rank, world, local_rank, dist):
     # ---- the full loop at the other two configurations (weak scaling per GPU)
     if not args.no_extra_legs:
         for name, cfg in EXTRA_LOOPS.items():
-            legs[name] = extra_loop_leg(cfg, rank, world, local_rank, comm, flush, dist)
+            legs[name] = extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist)
 
     # ---- dominant kernel, timed live: see profiles/ for the launch-share list
     roof = dominant_kernel_roofline(lib, torch, local_rank, stream)
@@ -254,6 +264,8 @@ def run_mine(args, rank, world, local_rank, dist):
                        "envs_per_gpu": ENVS_PER_GPU, "horizon": HORIZON, "embed": EMBED,
                        "hidden": EMBED * SCALE, "blocks": LAYERS, "epochs": EPOCHS,
                        "minibatch": "one slot (4096 rows)", "parallelism": f"dp{world}",
+                       "allreduce": ("none" if world == 1 else
+                                     "NVLink peer memory (library kernels)" if args.allreduce == "p2p" else "NCCL"),
                        "l2": "flushed between timed steps (256 MiB write, outside the events)",
                        "env_steps_per_step": steps_per_iter * world,
                        "flop_per_env_step": (HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd)},
@@ -281,7 +293,7 @@ EXTRA_LOOPS = {
 }
 
 
-def extra_loop_leg(cfg, rank, world, local_rank, comm, flush, dist):
+def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist):
     """collect() + train(4) at another configuration, device-timed like the
     headline (CUDA events on the engine stream, L2 flushed between steps)."""
     import torch
@@ -293,8 +305,7 @@ def extra_loop_leg(cfg, rank, world, local_rank, comm, flush, dist):
     gym = Gym(cfg["env"], n, seed=0, first_env_id=env_shard(rank, n), device=local_rank)
     model = PPOModel(gym, cfg["embed"], cfg["scale"], cfg["blocks"], LR, HORIZON, seed=0)
     model.minibatch_rows = cfg["minibatch"]
-    if comm is not None:
-        model.set_comm(comm, rank, world)
+    connect(model)
     stream = torch.cuda.ExternalStream(gym.stream(), device=local_rank)
     for _ in range(cfg["warmup"]):
         model.collect()
@@ -574,6 +585,9 @@ def main():
     ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-legs", action="store_true", help="skip the configs[3] / configs[4] loops")
+    ap.add_argument("--allreduce", choices=["nccl", "p2p"], default="nccl",
+                    help="N > 1: gradient all-reduce with NCCL (default; measured faster at 8 GPUs) or the "
+                         "library's own kernel over NVLink peer memory")
     ap.add_argument("--profile-minibatch", choices=["c3", "c4", "c5"],
                     help="profiling driver: one training minibatch and one forward of that configuration, "
                          "bracketed by cudaProfilerStart / Stop (for ncu --profile-from-start off); no JSON line")

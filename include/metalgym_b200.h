@@ -303,6 +303,16 @@ int mg_ppo_collect(mg_ppo_t model);
 int mg_ppo_train(mg_ppo_t model, int epochs);
 /* trainSlot(t) (model/ppo.h:906-916); blocks until done. */
 int mg_ppo_train_slot(mg_ppo_t model, int t);
+/* Gradient all-reduce over NVLink peer memory instead of NCCL (no counterpart
+ * in the reference). Every rank calls mg_ppo_p2p_handle (allocates its
+ * exchange region, returns its 64-byte CUDA IPC handle), the host exchanges
+ * the handles, every rank calls mg_ppo_p2p_open with all of them in rank
+ * order, and the host synchronises the ranks once before the first train().
+ * train() then reduces each minibatch's gradient with one kernel that reads
+ * the other ranks' regions over NVLink (every rank sums in rank order: the
+ * ranks' weights stay bit-identical). world <= 16, one GPU per rank. */
+int mg_ppo_p2p_handle(mg_ppo_t model, void* out64);
+int mg_ppo_p2p_open(mg_ppo_t model, const void* handles, int rank, int world);
 /* Checkpoint of the training state (no counterpart in the reference, which
  * has none): weights, fp32 master, Adam moments, step counter, learning rate,
  * hyperparameters, minibatch rows, the host shuffle generator and the

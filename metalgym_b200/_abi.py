@@ -69,6 +69,8 @@ SIGNATURES = {
     "mg_ppo_collect": (I, [P]),
     "mg_ppo_train": (I, [P, I]),
     "mg_ppo_train_slot": (I, [P, I]),
+    "mg_ppo_p2p_handle": (I, [P, P]),
+    "mg_ppo_p2p_open": (I, [P, P, I, I]),
     "mg_ppo_save": (I, [P, S]),
     "mg_ppo_load": (I, [P, S]),
     "mg_ppo_set_minibatch_rows": (I, [P, I]),

@@ -33,6 +33,7 @@ SOURCES: dict[str, list[str]] = {
     "block_fwd.cu": [],
     "envs.cu": [],
     "envs_builtin.cu": ["--fmad=false"],
+    "p2p.cu": [],
     "engine.cu": [],
     "capi_session.cu": [],
     "noalloc.cu": [],

@@ -234,6 +234,12 @@ int mg_ppo_train(mg_ppo_t model, int epochs) {
 int mg_ppo_train_slot(mg_ppo_t model, int t) {
     return model ? P(model)->trainSlot(t) : mg::fail(MG_ERR_ARGUMENT, "null model");
 }
+int mg_ppo_p2p_handle(mg_ppo_t model, void* out64) {
+    return model ? P(model)->p2pHandle(out64) : mg::fail(MG_ERR_ARGUMENT, "null model");
+}
+int mg_ppo_p2p_open(mg_ppo_t model, const void* handles, int rank, int world) {
+    return model ? P(model)->p2pOpen(handles, rank, world) : mg::fail(MG_ERR_ARGUMENT, "null model");
+}
 int mg_ppo_save(mg_ppo_t model, const char* path) {
     return model ? P(model)->save(path) : mg::fail(MG_ERR_ARGUMENT, "null model");
 }

@@ -254,6 +254,10 @@ PpoEngine::~PpoEngine() {
         cudaStreamSynchronize(side);
         cudaStreamDestroy(side);
     }
+    for (void* q : p2pOpened) cudaIpcCloseMemHandle(q);
+    if (p2pRegion) cudaFree(p2pRegion);
+    cudaFree(p2pSeq);
+    cudaFree(p2pCounter);
     for (auto ev : forkEv)
         if (ev) cudaEventDestroy(ev);
     if (joinEv) cudaEventDestroy(joinEv);
@@ -453,7 +457,7 @@ int PpoEngine::allocTrain(int rows) {
     seg(headPart, (int64_t)E * kHead, headSplits, (int64_t)E * kHead, pHead, 1);
     if (cont) seg(lsPart, A, pGs, A, pLogStd, 0);
     nNorm = grad_table_layout(tb);
-    const int nNormAll = std::max(nNorm, grad_scale_norm_blocks((int64_t)optCount));
+    const int nNormAll = std::max(std::max(nNorm, grad_scale_norm_blocks((int64_t)optCount)), p2p_blocks());
     MG_TRY(dalloc(&normPartial, (size_t)nNormAll * 4));
     trainBufRows = rows;
     return MG_OK;
@@ -698,6 +702,17 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     MG_CUDA_TRY(cudaEventRecord(joinEv, side));
     MG_CUDA_TRY(cudaStreamWaitEvent(st, joinEv, 0));
     // gradient sums + norm (model/ppo.h:873-890), [all-reduce], Adam (:891-903)
+    if (p2pOn) {
+        // sums into this minibatch's exchange buffer, then the all-reduce over
+        // peer memory leaves the averaged gradient in grad and its norm in normSq
+        float* x0 = reinterpret_cast<float*>(static_cast<unsigned char*>(p2pRegion) + p2pTable.xOff[0]);
+        float* x1 = reinterpret_cast<float*>(static_cast<unsigned char*>(p2pRegion) + p2pTable.xOff[1]);
+        MG_TRY(grad_finalize(gradTable, x0, normPartial, st, nullptr, nullptr, x1, p2pSeq));
+        MG_TRY(p2p_allreduce(p2pTable, (int64_t)optCount, grad, p2pSeq, p2pCounter, normPartial, normSq, st));
+        const AdamHyper ah{lr, hp.maxGradNorm, 0.0f, 0.0f};
+        return adam(master, grad, mom, var, weights, normPartial, 0, (int64_t)optCount, ah, schedBetaPow + 2 * j,
+                    nullptr, st, normSq);
+    }
     // the finalisation's last CTA leaves the squared norm in normSq
     MG_TRY(grad_finalize(gradTable, grad, normPartial, st, normCounter, normSq));
     if (world > 1) {
@@ -761,8 +776,8 @@ int PpoEngine::captureTrain(int minibatches, bool rowMode) {
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "train capture");
-    // this library's kernels: the all-reduce adds one NCCL kernel per minibatch
-    trainKernels = count_kernel_nodes(graph) - (world > 1 ? (size_t)minibatches : 0);
+    // this library's kernels: the NCCL all-reduce adds one NCCL kernel per minibatch
+    trainKernels = count_kernel_nodes(graph) - (world > 1 && !p2pOn ? (size_t)minibatches : 0);
     cudaGraphExec_t exec = nullptr;
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
@@ -1061,6 +1076,70 @@ int PpoEngine::load(const char* path) {
     hp.lambda = h.hyper[5];
     MG_TRY(setMinibatchRows(h.minibatchRows));
     // a captured train graph holds lr in its Adam launches
+    if (trainExec) {
+        cudaGraphExecDestroy(trainExec);
+        trainExec = nullptr;
+    }
+    return MG_OK;
+}
+
+// ------------------------------------------------------------ peer all-reduce
+
+// Allocates this rank's exchange region (zeroed: flags, buffers and their
+// padding) and returns its CUDA IPC handle (64 bytes).
+int PpoEngine::p2pHandle(void* out64) {
+    MG_CHECK_ARG(out64, "p2pHandle: null output");
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    if (!p2pRegion) {
+        const size_t bytes = p2p_region_bytes((int64_t)optCount);
+        MG_CUDA_TRY(cudaMalloc(&p2pRegion, bytes));
+        MG_CUDA_TRY(cudaMemset(p2pRegion, 0, bytes));
+        MG_TRY(dalloc(&p2pSeq, 4));
+        MG_TRY(dalloc(&p2pCounter, 4));
+        MG_CUDA_TRY(cudaMemset(p2pSeq, 0, 4));
+        MG_CUDA_TRY(cudaMemset(p2pCounter, 0, 4));
+        MG_CUDA_TRY(cudaDeviceSynchronize());
+    }
+    cudaIpcMemHandle_t h;
+    MG_CUDA_TRY(cudaIpcGetMemHandle(&h, p2pRegion));
+    std::memcpy(out64, &h, sizeof(h));
+    return MG_OK;
+}
+
+// Opens the other ranks' regions (handles: world x 64 bytes, rank order) and
+// switches train() to the peer all-reduce. Every rank must have called
+// p2pHandle before any rank trains; the caller synchronises the ranks after
+// this call (a host barrier) before the first train().
+int PpoEngine::p2pOpen(const void* handles, int r, int w) {
+    MG_CHECK_ARG(handles && w >= 2 && w <= kP2PMaxRanks && r >= 0 && r < w, "p2pOpen: bad rank / world size");
+    MG_CHECK_ARG(p2pRegion, "p2pOpen: call p2pHandle first");
+    MG_CHECK_ARG(!p2pOn, "p2pOpen: already open");
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    P2PTable t{};
+    for (int p = 0; p < w; p++) {
+        if (p == r) {
+            t.base[p] = static_cast<unsigned char*>(p2pRegion);
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const char*>(handles) + (size_t)p * sizeof(h), sizeof(h));
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (void* q : p2pOpened) cudaIpcCloseMemHandle(q);
+            p2pOpened.clear();
+            return cuda_fail(e, "cudaIpcOpenMemHandle");
+        }
+        p2pOpened.push_back(ptr);
+        t.base[p] = static_cast<unsigned char*>(ptr);
+    }
+    p2p_layout(t, (int64_t)optCount);
+    t.rank = r;
+    t.world = w;
+    p2pTable = t;
+    p2pOn = true;
+    rank = r;
+    world = w;
     if (trainExec) {
         cudaGraphExecDestroy(trainExec);
         trainExec = nullptr;

@@ -12,6 +12,7 @@
 
 #include "../../include/metalgym_b200.h"
 #include "block.h"
+#include "p2p.h"
 #include "policy.h"
 
 namespace mg {
@@ -178,9 +179,18 @@ class PpoEngine {
     bool useFusedBlock(int rows) const { return fusedBlocks && rows >= kFusedBlockMinRows; }
     static constexpr int kFusedBlockMinRows = 8192;
 
-    // multi-GPU
+    // multi-GPU: NCCL all-reduce (setComm) or the all-reduce over NVLink peer
+    // memory (p2p.cu: p2pHandle on every rank, exchange, p2pOpen)
     void* comm = nullptr;
     int rank = 0, world = 1;
+    void* p2pRegion = nullptr;           // this rank's exchange region (IPC-shared)
+    std::vector<void*> p2pOpened;        // peers' regions opened here
+    P2PTable p2pTable{};
+    bool p2pOn = false;
+    unsigned int* p2pSeq = nullptr;      // device minibatch counter of the exchange
+    unsigned int* p2pCounter = nullptr;  // last-CTA detection of the gather
+    int p2pHandle(void* out64);
+    int p2pOpen(const void* handles, int rank, int world);
 
    private:
     int forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st);

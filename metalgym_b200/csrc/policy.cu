@@ -679,11 +679,15 @@ __global__ void __launch_bounds__(256) k_adv_stats_rows(const float* __restrict_
 // LayerNorm / input / log-std sums stay fp32) and writes one partial sum of
 // squares per CTA for the global norm (model/optimizer.metal:23-34).
 __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ GradSegmentTable tab,
-                                                       float* __restrict__ grad, float* __restrict__ normPartial,
+                                                       float* gradA, float* gradB, const unsigned int* sel,
+                                                       float* __restrict__ normPartial,
                                                        unsigned int* __restrict__ counter,
                                                        float* __restrict__ normSqOut) {
     mg_pdl_trigger();
     mg_pdl_wait();
+    // with sel (the peer all-reduce's minibatch counter): gradB when the next
+    // count is odd, else gradA; without it: gradA
+    float* __restrict__ grad = (sel && ((*sel + 1u) & 1u)) ? gradB : gradA;
     __shared__ float s_red[8];
     __shared__ bool s_last;
     int b = blockIdx.x, si = 0;
@@ -1119,7 +1123,7 @@ int grad_table_layout(GradSegmentTable& tab, bool allowDeep) {
 }
 
 int grad_finalize(const GradSegmentTable& table, float* grad, float* normPartial, cudaStream_t st,
-                  unsigned int* counter, float* normSqOut) {
+                  unsigned int* counter, float* normSqOut, float* grad2, const unsigned int* sel) {
     MG_CHECK_ARG(table.n > 0 && table.n <= kMaxGradSegments, "grad_finalize: bad segment count");
     const int nblocks = table.seg[table.n - 1].blockEnd;
     MG_CHECK_ARG(nblocks > 0, "grad_finalize: empty");
@@ -1130,7 +1134,7 @@ int grad_finalize(const GradSegmentTable& table, float* grad, float* normPartial
         g.vec4 = (reinterpret_cast<uintptr_t>(g.src) % 16 == 0) && g.partStride % 4 == 0 && g.dstOffset % 4 == 0 &&
                  (reinterpret_cast<uintptr_t>(grad) % 16 == 0);
     }
-    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, normPartial, counter, normSqOut);
+    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, grad2, sel, normPartial, counter, normSqOut);
     return check_launch("k_grad_finalize");
 }
 

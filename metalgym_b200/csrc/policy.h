@@ -108,8 +108,11 @@ int advantage_stats_rows(const float* adv, RowMap rm, int rows, float* out, doub
 int grad_table_layout(GradSegmentTable& tab, bool allowDeep = true);
 // With counter (a zeroed device word) and normSqOut, the last CTA also sums
 // the per-CTA partials into *normSqOut and re-zeroes the counter.
+// With sel (a device counter): the sums go to grad2 when *sel + 1 is odd, else
+// to grad (the two exchange buffers of the peer all-reduce).
 int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st,
-                  unsigned int* counter = nullptr, float* normSqOut = nullptr);
+                  unsigned int* counter = nullptr, float* normSqOut = nullptr, float* grad2 = nullptr,
+                  const unsigned int* sel = nullptr);
 int grad_scale_norm_blocks(int64_t count);
 int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st,
                     unsigned int* counter = nullptr, float* normSqOut = nullptr);

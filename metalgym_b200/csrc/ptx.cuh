@@ -22,6 +22,7 @@ enum DeviceError : int {
     kDevTimeoutDone = 3,   // accumulator never completed
     kDevBadShape = 4,
     kDevBadAction = 5,     // an action index outside [0, ACT_DIM) reached the loss
+    kDevTimeoutPeer = 6,   // another GPU never announced its part of an exchange
 };
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait

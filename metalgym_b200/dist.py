@@ -11,6 +11,8 @@ torch.distributed process group of any backend (NCCL or gloo):
 * broadcast_comm_id / nccl_comm: rank 0 makes the 128-byte NCCL id, the
   process group carries it to the other ranks, each rank joins the
   communicator on its device.
+* p2p_allreduce: the alternative to NCCL, the library's own all-reduce over
+  NVLink peer memory; the process group carries the CUDA IPC handles.
 * max_over_ranks: the device time of a step is the slowest rank's.
 * weights_digest: a hash of a rank's weight arena and fp32 master copy; the
   all-reduced gradient, clip and Adam are computed identically everywhere, so
@@ -57,6 +59,17 @@ def nccl_comm(dist, rank: int, world: int, device: int) -> ctypes.c_void_p:
 def destroy_comm(comm) -> None:
     if comm:
         check(lib().mg_comm_destroy(comm), "mg_comm_destroy")
+
+
+def p2p_allreduce(model, dist, rank: int, world: int) -> None:
+    """Switches the model's per-minibatch gradient all-reduce to the kernels
+    over NVLink peer memory: exchanges every rank's region handle over the
+    process group, opens them all, then synchronises the ranks."""
+    mine = model.p2p_handle()
+    handles = [None] * world
+    dist.all_gather_object(handles, mine)
+    model.p2p_open(handles, rank, world)
+    dist.barrier()
 
 
 def max_over_ranks(x: float, dist, device: str = "cuda") -> float:

@@ -142,6 +142,18 @@ class PPOModel:
     def train_slot(self, t: int):
         check(lib().mg_ppo_train_slot(self._h, t), "trainSlot")
 
+    def p2p_handle(self) -> bytes:
+        """This rank's 64-byte exchange-region handle (mg_ppo_p2p_handle)."""
+        buf = (C.c_char * 64)()
+        check(lib().mg_ppo_p2p_handle(self._h, buf), "p2p_handle")
+        return bytes(buf)
+
+    def p2p_open(self, handles: list, rank: int, world: int) -> None:
+        """Opens every rank's region (handles in rank order; mg_ppo_p2p_open)."""
+        blob = b"".join(handles)
+        buf = (C.c_char * len(blob)).from_buffer_copy(blob)
+        check(lib().mg_ppo_p2p_open(self._h, buf, rank, world), "p2p_open")
+
     def save(self, path) -> None:
         """Checkpoint of the training state (mg_ppo_save)."""
         check(lib().mg_ppo_save(self._h, str(path).encode()), "save")

@@ -6,7 +6,8 @@
   the sum over ranks is scaled by 1/world, the clip and Adam run on every
   rank; the ranks' weights must stay bit-identical and equal a single
   process that averages the shards' gradients itself.
---mode gpu (one GPU per rank, NCCL for the gradient, gloo for the host):
+--mode gpu (one GPU per rank, NCCL or the library's own all-reduce over
+  NVLink peer memory (--allreduce p2p) for the gradient, gloo for the host):
   a rank's all-reduced gradient must equal the average over ranks of the
   gradients that an identical model without the communicator computes on
   the same rollout, bit for bit; after train() the weight digests of all
@@ -121,10 +122,10 @@ def run_cpu(rank, world, dist):
     return out
 
 
-def run_gpu(rank, world, local, dist):
+def run_gpu(rank, world, local, dist, allreduce):
     import torch
 
-    from metalgym_b200.dist import destroy_comm, env_shard, nccl_comm, weights_digest
+    from metalgym_b200.dist import destroy_comm, env_shard, nccl_comm, p2p_allreduce, weights_digest
     from metalgym_b200.session import Gym, PPOModel
 
     torch.cuda.set_device(local)
@@ -132,8 +133,12 @@ def run_gpu(rank, world, local, dist):
     out = {}
     gym = Gym("rollout_cartpole", R, seed=0, first_env_id=env_shard(rank, R), device=local)
     model = PPOModel(gym, 128, 4, 2, 3e-4, T, seed=7)
-    comm = nccl_comm(dist, rank, world, local)
-    model.set_comm(comm, rank, world)
+    comm = None
+    if allreduce == "nccl":
+        comm = nccl_comm(dist, rank, world, local)
+        model.set_comm(comm, rank, world)
+    else:
+        p2p_allreduce(model, dist, rank, world)
     model.collect()
     # an identical model without the communicator, on the same rollout
     gym1 = Gym("rollout_cartpole", R, seed=0, first_env_id=env_shard(rank, R), device=local)
@@ -171,6 +176,7 @@ def run_gpu(rank, world, local, dist):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--mode", choices=["cpu", "gpu"], required=True)
+    ap.add_argument("--allreduce", choices=["nccl", "p2p"], default="nccl")
     args = ap.parse_args()
     import torch.distributed as dist
 
@@ -178,7 +184,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     try:
-        out = run_cpu(rank, world, dist) if args.mode == "cpu" else run_gpu(rank, world, local, dist)
+        out = run_cpu(rank, world, dist) if args.mode == "cpu" else run_gpu(rank, world, local, dist, args.allreduce)
         results = [None] * world
         dist.all_gather_object(results, out)
     finally:

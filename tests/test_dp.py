@@ -2,9 +2,10 @@
 (one process per rank; tests/dp_worker.py is the rank program).
 
 CPU (gloo): the host logic of metalgym_b200.dist and the all-reduce update
-semantics on the oracle. GPU (two B200s, NCCL): the product's all-reduced
-gradient against the per-rank gradients, bit for bit, and bit-identical
-weights across ranks after train(); skipped with fewer than two GPUs.
+semantics on the oracle. GPU (two B200s, NCCL or the library's all-reduce
+over NVLink peer memory): the product's all-reduced gradient against the
+per-rank gradients, bit for bit, and bit-identical weights across ranks after
+train(); skipped with fewer than two GPUs.
 """
 import json
 import socket
@@ -23,10 +24,10 @@ def free_port():
         return s.getsockname()[1]
 
 
-def launch(mode, nproc=2, limit=600):
+def launch(mode, nproc=2, limit=600, extra=()):
     cmd = ["timeout", "-k", "30", str(limit), sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", str(nproc), "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
-           str(ROOT / "tests" / "dp_worker.py"), "--mode", mode]
+           str(ROOT / "tests" / "dp_worker.py"), "--mode", mode, *extra]
     p = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT)
     lines = [l for l in p.stdout.splitlines() if l.startswith("{")]
     assert p.returncode == 0 and lines, f"rc={p.returncode}\n{p.stdout[-3000:]}\n{p.stderr[-3000:]}"
@@ -40,12 +41,13 @@ def test_data_parallel_host_logic_gloo(oracle):
 
 
 @pytest.mark.gpu
-def test_data_parallel_two_gpus_nccl(mg):
+@pytest.mark.parametrize("allreduce", ["nccl", "p2p"])
+def test_data_parallel_two_gpus(mg, allreduce):
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    res = launch("gpu")
+    res = launch("gpu", extra=("--allreduce", allreduce))
     assert res["ok"], res
     for r in res["ranks"]:
         assert r["grad_mismatches"] == 0, r
