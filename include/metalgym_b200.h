@@ -79,7 +79,7 @@ int mg_gemm_bf16(const void* A_dev, int a_mn_major, int lda, const void* B_dev, 
                  int N, int K, int epilogue, void* out_dev, int ldo, const void* aux_dev, int ldaux, int splits,
                  mg_stream_t stream);
 /* mg_gemm_bf16 with the kernel chosen by the caller (no counterpart in the
- * reference): tile_n = output tile width 64, 128 or 256 (0 = the library's
+ * reference): tile_n = output tile width 32 (K-major B only), 64, 128 or 256 (0 = the library's
  * choice, persistent then only allows the persistent kernel); persistent = 1
  * selects the persistent kernel (one CTA per SM walking the tiles with the
  * accumulator double-buffered in tensor memory; tile_n 128 or 256), 0 the

@@ -85,6 +85,14 @@ int by_major(bool amn, bool bmn, int epi, bool persist, const CUtensorMap& ta, c
     return by_epi<BN, true, true>(epi, persist, ta, tb, p, splits, st);
 }
 
+// 32-wide tiles: K-major B only (a 32-column MN-major B box would be 64
+// bytes wide, not the 128-byte swizzle atom).
+int by_major32(bool amn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits,
+               cudaStream_t st) {
+    return amn ? by_epi<32, true, false>(epi, false, ta, tb, p, splits, st)
+               : by_epi<32, false, false>(epi, false, ta, tb, p, splits, st);
+}
+
 }  // namespace
 
 int gemm_bf16(const GemmCall& c, cudaStream_t st) {
@@ -120,12 +128,15 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
             persist = true;
         } else {
             // one CTA per tile: 128-wide output tiles, or 64-wide ones when
-            // 128-wide tiles would leave most of the SMs idle (small row counts)
-            bn = (c.N >= 128 && tiles128 >= sms) ? 128 : 64;
+            // 128-wide tiles would leave most of the SMs idle (small row
+            // counts), or 32-wide ones (K-major B) when even 64-wide ones would
+            const int tiles64 = ((c.M + 127) / 128) * ((c.N + 63) / 64) * splits;
+            bn = (c.N >= 128 && tiles128 >= sms) ? 128 : (!c.b_mn && tiles64 < sms / 2) ? 32 : 64;
             persist = false;
         }
     }
-    MG_CHECK_ARG(bn == 64 || bn == 128 || bn == 256, "gemm: tile N must be 64, 128 or 256");
+    MG_CHECK_ARG(bn == 32 || bn == 64 || bn == 128 || bn == 256, "gemm: tile N must be 32, 64, 128 or 256");
+    MG_CHECK_ARG(bn != 32 || !c.b_mn, "gemm: 32-wide tiles need a K-major B");
     MG_CHECK_ARG(!persist || bn >= 128, "gemm: the persistent kernel needs tile N 128 or 256");
 
     CUtensorMap ta, tb;
@@ -148,6 +159,7 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
     p.tilesN = (c.N + bn - 1) / bn;
     p.splits = splits;
     switch (bn) {
+        case 32: return by_major32(c.a_mn, c.epilogue, ta, tb, p, splits, st);
         case 64: return by_major<64>(c.a_mn, c.b_mn, c.epilogue, false, ta, tb, p, splits, st);
         case 128: return by_major<128>(c.a_mn, c.b_mn, c.epilogue, persist, ta, tb, p, splits, st);
         default: return by_major<256>(c.a_mn, c.b_mn, c.epilogue, persist, ta, tb, p, splits, st);

@@ -125,6 +125,21 @@ def test_gemm_down_projection_single_launch(mg):
 # tiles than SMs (so each CTA walks several units and reuses both
 # accumulators), ragged M / N / K and every epilogue.
 KERNELS = [(128, 1), (256, 1), (256, 0)]
+
+
+@pytest.mark.parametrize("epi", ["bf16", "resid", "mask"])
+@pytest.mark.parametrize("shape", [(4096, 128, 512), (1000, 96, 200)])
+def test_gemm_32_wide_tiles(mg, epi, shape):
+    """32-wide output tiles (K-major B), used for small-N products such as
+    dBranch = dV Up^T at 4096 rows."""
+    M, N, K = shape
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + len(epi))
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn(K, N, device="cuda", generator=g).bfloat16()
+    aux = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    out = run_gemm(mg, A, 0, B, 0, M, N, K, epi, aux=aux, tile_n=32, persistent=0)
+    ref = reference(A, B, epi, aux)
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2 * ref.abs().max().item())
 BIG_SHAPES = [
     (8192, 1024, 256),   # up-projection at the scale-out widths (train minibatch 8192 rows)
     (4096, 256, 1024),   # down-projection
