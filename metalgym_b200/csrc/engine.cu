@@ -616,15 +616,6 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         down.out = a.h; down.ldo = E;
         MG_TRY(gemm_bf16(down, st));
     }
-    MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, rows, E, st));
-    {
-        GemmCall hd;
-        hd.A = a.fOut; hd.lda = E;
-        hd.B = w(pHead); hd.b_mn = true; hd.ldb = kHead;
-        hd.M = rows; hd.N = kHead; hd.K = E;
-        hd.out = a.head; hd.ldo = kHead;
-        MG_TRY(gemm_bf16(hd, st));
-    }
     // loss (model/ppo.h:753-781): per-slot advantage statistics from
     // collect(), or in row mode the statistics of this minibatch's rows
     const LossHyper lh{hp.clip, hp.valueCoef, hp.entropyCoef};
@@ -633,12 +624,28 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         MG_TRY(advantage_stats_rows(advSlots, rm, rows, mbAdvStats, advPartial, advCounter, st));
         as = mbAdvStats;
     }
+    MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, rows, E, st));
+    {
+        GemmCall hd;
+        hd.A = a.fOut; hd.lda = E;
+        hd.B = w(pHead); hd.b_mn = true; hd.ldb = kHead;
+        hd.M = rows; hd.N = kHead; hd.K = E;
+        hd.out = a.head; hd.ldo = kHead;
+        // the categorical loss runs in the head GEMM's epilogue (each epilogue
+        // thread holds a whole head row); the Gaussian loss, whose log-std
+        // gradient is a batch sum, has its own kernel
+        PolicyLossRows pl{};
+        if (!cont) {
+            pl = policy_loss_rows(static_cast<const int32_t*>(actionSlots), advSlots, as, retSlots, logpSlots, dLogits,
+                                  stats, rows, A, lh, rm);
+            hd.epilogue = 5;  // bf16 head + policy loss
+            hd.loss = &pl;
+        }
+        MG_TRY(gemm_bf16(hd, st));
+    }
     if (cont)
         MG_TRY(gaussian_loss(a.head, static_cast<const float*>(actionSlots), advSlots, as, retSlots, logpSlots,
                              dLogits, stats, w(pLogStd), lsPart, rows, A, lh, st, rm));
-    else
-        MG_TRY(policy_loss(a.head, static_cast<const int32_t*>(actionSlots), advSlots, as, retSlots, logpSlots,
-                           dLogits, stats, rows, A, lh, st, rm));
     // backward (model/ppo.h:793-865). The input-gradient chain runs on st;
     // each weight-gradient GEMM is forked to the side stream as soon as its
     // operands exist (they are never overwritten within the minibatch) and

@@ -72,6 +72,9 @@ int by_epi(int epi, bool persist, const CUtensorMap& ta, const CUtensorMap& tb, 
         case kEpiBf16Resid: return launch_one<BN, AMN, BMN, kEpiBf16Resid>(ta, tb, p, splits, st);
         case kEpiBf16Mask: return launch_one<BN, AMN, BMN, kEpiBf16Mask>(ta, tb, p, splits, st);
         case kEpiF32: return launch_one<BN, AMN, BMN, kEpiF32>(ta, tb, p, splits, st);
+        case kEpiPolicyLoss:
+            if constexpr (BN == 64) return launch_one<64, AMN, BMN, kEpiPolicyLoss>(ta, tb, p, splits, st);
+            break;
     }
     return fail(MG_ERR_ARGUMENT, "unknown GEMM epilogue");
 }
@@ -106,6 +109,8 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
     MG_CHECK_ARG(c.splits == 1 || c.epilogue == kEpiF32, "gemm: split-K needs the fp32 epilogue");
     MG_CHECK_ARG(!(c.epilogue == kEpiBf16Resid || c.epilogue == kEpiBf16Mask) || (c.aux && c.ldaux % 8 == 0),
                  "gemm: this epilogue needs aux with ldaux a multiple of 8");
+    MG_CHECK_ARG(c.epilogue != kEpiPolicyLoss || (c.N == 64 && c.ldo == 64 && c.splits == 1 && c.loss),
+                 "gemm: the policy-loss epilogue needs the 64-column head and its loss arguments");
     int kPerSplit = (c.K + c.splits - 1) / c.splits;
     kPerSplit = (kPerSplit + 63) / 64 * 64;
     const int splits = (c.K + kPerSplit - 1) / kPerSplit;
@@ -135,6 +140,10 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
             persist = false;
         }
     }
+    if (c.epilogue == kEpiPolicyLoss) {
+        bn = 64;  // one tile spans the head row
+        persist = false;
+    }
     MG_CHECK_ARG(bn == 32 || bn == 64 || bn == 128 || bn == 256, "gemm: tile N must be 32, 64, 128 or 256");
     MG_CHECK_ARG(bn != 32 || !c.b_mn, "gemm: 32-wide tiles need a K-major B");
     MG_CHECK_ARG(!persist || bn >= 128, "gemm: the persistent kernel needs tile N 128 or 256");
@@ -155,6 +164,7 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
     p.aux = static_cast<const __nv_bfloat16*>(c.aux);
     p.ldaux = c.ldaux;
     p.status = status_ptr();
+    if (c.loss) p.loss = *c.loss;
     p.tilesM = (c.M + 127) / 128;
     p.tilesN = (c.N + bn - 1) / bn;
     p.splits = splits;

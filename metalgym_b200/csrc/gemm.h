@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include "loss_row.cuh"
+
 namespace mg {
 
 struct GemmCall {
@@ -21,6 +23,7 @@ struct GemmCall {
     int splits = 1;
     int bn = 0;  // output tile width (64 / 128 / 256); 0 = choose
     int persistent = -1;  // 1: persistent kernel (bn 128 / 256), 0: one CTA per tile, -1: choose
+    const PolicyLossRows* loss = nullptr;  // epilogue 5 (policy loss)
 };
 
 int gemm_bf16(const GemmCall& c, cudaStream_t st);

@@ -17,6 +17,7 @@
 // No cluster launch: every CTA loads its own tiles.
 #pragma once
 
+#include "loss_row.cuh"
 #include "metalgym/pdl.cuh"
 #include "ptx.cuh"
 
@@ -28,12 +29,14 @@ enum GemmEpilogue : int {
     kEpiBf16Resid = 2,  // out = bf16(aux + bf16(acc))                     (mlp.metal:85 + elementwise.metal:4-13)
     kEpiBf16Mask = 3,   // out = bf16(acc) * (aux > 0)                     (model/mlp.metal:119-126)
     kEpiF32 = 4,        // out_f32 = acc (split z writes slice z of M x N)
+    kEpiPolicyLoss = 5, // out_bf16 = bf16(acc) (the policy head), then the categorical PPO loss of each row
 };
 
 struct GemmParams {
     int M, N, K;
     int kPerSplit;  // multiple of 64
     int tilesM, tilesN, splits;  // work units of the persistent kernel
+    PolicyLossRows loss;         // kEpiPolicyLoss: the loss of each output row
     void* out;
     int ldo;
     const __nv_bfloat16* aux;
@@ -222,6 +225,9 @@ __global__ void __launch_bounds__(128, 1)
                 store_bf16x32(o, v);
             }
         }
+        // the thread's whole head row is stored (one tile spans the 64 columns)
+        if (EPI == kEpiPolicyLoss && row < p.M)
+            policy_loss_row(p.loss, row, static_cast<const __nv_bfloat16*>(p.out) + (size_t)row * p.ldo, p.status);
     }
     tc_fence_before();
     __syncthreads();

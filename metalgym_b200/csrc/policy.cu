@@ -2,6 +2,7 @@
 // The dense products live in gemm.cu; everything else lives here.
 #include <algorithm>
 
+#include "loss_row.cuh"
 #include "policy.h"
 #include "policy_kernels.cuh"
 #include "runtime.h"
@@ -393,84 +394,13 @@ __device__ __forceinline__ float norm_adv(const float* adv, const float* advStat
     return advStats ? __fmul_rn(__fsub_rn(adv[r], advStats[0]), advStats[1]) : adv[r];
 }
 
-// model/policy.metal:14-69. One thread per row.
-__global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const int32_t* __restrict__ action,
-                              const float* __restrict__ adv, const float* __restrict__ advStats,
-                              const float* __restrict__ ret, const float* __restrict__ oldLogProb,
-                              __nv_bfloat16* __restrict__ dZ, float* __restrict__ stats, int rows, int actDim,
-                              LossHyper hp, int* status, RowMap rm) {
+// model/policy.metal:14-69. One thread per row (policy_loss_row).
+__global__ void k_policy_loss(const __nv_bfloat16* __restrict__ head, const PolicyLossRows L, int* status) {
     mg_pdl_trigger();
     mg_pdl_wait();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= rows) return;
-    // minibatch row r reads rollout row g of the slot-major buffers
-    const int64_t g = rm.mb ? (int64_t)mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : r;
-    if (rm.mb && rm.mb->slot >= 0 && advStats) advStats += 2 * rm.mb->slot;  // per-slot statistics
-    const float scale = __fdiv_rn(1.0f, (float)rows);
-    const __nv_bfloat16* h = head + (size_t)r * kHeadDim;
-    // exp(logp_j) is needed twice (entropy, gradient): keep up to kCache of them
-    constexpr int kCache = 8;
-    float probCache[kCache];
-    float rowMax = -INFINITY;
-    for (int j = 0; j < actDim; j++) rowMax = fmaxf(rowMax, bf(h[j]));
-    float sum = 0.0f;
-    for (int j = 0; j < actDim; j++) sum = __fadd_rn(sum, mg_expf(__fsub_rn(bf(h[j]), rowMax)));
-    const float lse = __fadd_rn(rowMax, mg_logf(sum));
-    float entropy = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kCache; j++) {
-        if (j < actDim) {
-            const float logp = __fsub_rn(bf(h[j]), lse);
-            probCache[j] = mg_expf(logp);
-            entropy = __fsub_rn(entropy, __fmul_rn(probCache[j], logp));
-        }
-    }
-    for (int j = kCache; j < actDim; j++) {
-        const float logp = __fsub_rn(bf(h[j]), lse);
-        entropy = __fsub_rn(entropy, __fmul_rn(mg_expf(logp), logp));
-    }
-    const int a = action[g];
-    if (a < 0 || a >= actDim) {  // never index the head with an invalid action
-        record_error(status, kDevBadAction);
-        return;
-    }
-    const float A = norm_adv(adv, advStats, g);
-    const float logpA = __fsub_rn(bf(h[a]), lse);
-    const float ratio = mg_expf(__fsub_rn(logpA, oldLogProb[g]));
-    const float surr1 = __fmul_rn(ratio, A);
-    const float surr2 = __fmul_rn(fminf(fmaxf(ratio, __fsub_rn(1.0f, hp.clip)), __fadd_rn(1.0f, hp.clip)), A);
-    const float policyLoss = -fminf(surr1, surr2);
-    const float gLogp = (surr1 <= surr2) ? __fmul_rn(-A, ratio) : 0.0f;
-    uint32_t packed[kHeadDim / 2];
-#pragma unroll
-    for (int i = 0; i < kHeadDim / 2; i++) packed[i] = 0;
-    __nv_bfloat16* pz = reinterpret_cast<__nv_bfloat16*>(packed);
-    for (int j = 0; j < actDim; j++) {
-        const float logp = __fsub_rn(bf(h[j]), lse);
-        float prob;
-        if (j < kCache) {
-#pragma unroll
-            for (int q = 0; q < kCache; q++)
-                if (q == j) prob = probCache[q];
-        } else {
-            prob = mg_expf(logp);
-        }
-        const float g = __fadd_rn(__fmul_rn(gLogp, __fsub_rn(j == a ? 1.0f : 0.0f, prob)),
-                                  __fmul_rn(__fmul_rn(hp.entropyCoef, prob), __fadd_rn(logp, entropy)));
-        pz[j] = tobf(__fmul_rn(g, scale));
-    }
-    const float vErr = __fsub_rn(bf(h[actDim]), ret[g]);
-    pz[actDim] = tobf(__fmul_rn(__fmul_rn(hp.valueCoef, vErr), scale));
-    uint4* dst = reinterpret_cast<uint4*>(dZ + (size_t)r * kHeadDim);
-    const uint4* src = reinterpret_cast<const uint4*>(packed);
-#pragma unroll
-    for (int i = 0; i < kHeadDim / 8; i++) dst[i] = src[i];
-    float* st = stats + (size_t)r * 5;
-    st[0] = policyLoss;
-    st[1] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, hp.valueCoef), vErr), vErr);
-    st[2] = entropy;
-    st[3] = __fsub_rn(oldLogProb[g], logpA);
-    st[4] = (fabsf(__fsub_rn(ratio, 1.0f)) > hp.clip) ? 1.0f : 0.0f;
+    if (r >= L.rows) return;
+    policy_loss_row(L, r, head + (size_t)r * kHeadDim, status);
 }
 
 // model/gaussian.metal:76-135. One thread per row; the log-std gradient is a
@@ -1065,13 +995,34 @@ int sample_gaussian(const void* head, const void* logStd, uint32_t* rng, float* 
     return check_launch("k_sample_gaussian");
 }
 
+PolicyLossRows policy_loss_rows(const int32_t* action, const float* adv, const float* advStats, const float* ret,
+                                const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
+                                RowMap rm) {
+    PolicyLossRows L{};
+    L.action = action;
+    L.adv = adv;
+    L.advStats = advStats;
+    L.ret = ret;
+    L.oldLogProb = oldLogProb;
+    L.dZ = static_cast<__nv_bfloat16*>(dZ);
+    L.stats = stats;
+    L.mb = rm.mb;
+    L.envRows = rm.envRows;
+    L.total = rm.total;
+    L.rows = rows;
+    L.actDim = actDim;
+    L.clip = hp.clip;
+    L.valueCoef = hp.valueCoef;
+    L.entropyCoef = hp.entropyCoef;
+    return L;
+}
+
 int policy_loss(const void* head, const int32_t* action, const float* adv, const float* advStats, const float* ret,
                 const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
                 cudaStream_t st, RowMap rm) {
     MG_CHECK_ARG(rows > 0 && actDim >= 1 && actDim < kHeadDim, "policy_loss: bad shape");
-    MG_LAUNCH(k_policy_loss, grid_rows(rows, 64), 64, 0, st, static_cast<const __nv_bfloat16*>(head), action, adv,
-                                                         advStats, ret, oldLogProb, static_cast<__nv_bfloat16*>(dZ),
-                                                         stats, rows, actDim, hp, status_ptr(), rm);
+    const PolicyLossRows L = policy_loss_rows(action, adv, advStats, ret, oldLogProb, dZ, stats, rows, actDim, hp, rm);
+    MG_LAUNCH(k_policy_loss, grid_rows(rows, 64), 64, 0, st, static_cast<const __nv_bfloat16*>(head), L, status_ptr());
     return check_launch("k_policy_loss");
 }
 

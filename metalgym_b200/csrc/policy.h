@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "loss_row.cuh"
 #include "metalgym/rowmap.h"
 
 namespace mg {
@@ -88,6 +89,10 @@ int sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* 
                        int actDim, cudaStream_t st);
 int sample_gaussian(const void* head, const void* logStd, uint32_t* rng, float* action, float* logProb,
                     float* value, int rows, int actDim, cudaStream_t st);
+// The loss arguments as the fused head-GEMM epilogue takes them.
+PolicyLossRows policy_loss_rows(const int32_t* action, const float* adv, const float* advStats, const float* ret,
+                                const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
+                                RowMap rm);
 int policy_loss(const void* head, const int32_t* action, const float* adv, const float* advStats, const float* ret,
                 const float* oldLogProb, void* dZ, float* stats, int rows, int actDim, LossHyper hp,
                 cudaStream_t st, RowMap rm = RowMap{nullptr, 0, 0});

@@ -206,6 +206,31 @@ def test_train_slot_matches_oracle(mg, oracle, name):
     oracle.orc_model_destroy(om)
 
 
+def test_fused_head_loss_matches_standalone_loss(mg):
+    """The categorical loss computed in the head GEMM's epilogue gives the
+    same per-row statistics, bit for bit, as the standalone loss kernel on the
+    same head rows."""
+    R, T = 1024, 4
+    gym, model = make("rollout_cartpole", R, 128, 4, 2, T, seed=6)
+    model.collect()
+    t = 3
+    model.train_slot(t)
+    head = torch.from_numpy(model.download("train_head").view(np.int16).copy()).cuda()
+    st = model.download("adv_stats").view(np.float32)[2 * t:2 * t + 2].copy()
+    cols = [torch.from_numpy(np.ascontiguousarray(model.slots(k)[t])).cuda()
+            for k in ("actions", "adv", "ret", "logp")]
+    d_st = torch.from_numpy(st).cuda()
+    dz = torch.zeros(R * HEAD, dtype=torch.int16, device="cuda")
+    stats = torch.zeros(R * 5, dtype=torch.float32, device="cuda")
+    hyp = model.hyper()
+    rc = mg.mg_policy_loss(head.data_ptr(), cols[0].data_ptr(), cols[1].data_ptr(), d_st.data_ptr(),
+                           cols[2].data_ptr(), cols[3].data_ptr(), dz.data_ptr(), stats.data_ptr(), R, 2,
+                           hyp["clip"], hyp["valueCoef"], hyp["entropyCoef"], None)
+    assert rc == 0, mg.mg_last_error()
+    torch.cuda.synchronize()
+    assert np.array_equal(stats.cpu().numpy(), model.download("stats").view(np.float32))
+
+
 @pytest.mark.parametrize("name", ["rollout_cartpole", "rollout_cartpole_continuous"])
 def test_train_rows_matches_oracle(mg, oracle, name):
     """A row-mode minibatch (B rows gathered across slots through the keyed
