@@ -84,6 +84,36 @@ int mg_gemm_bf16(const void* A_dev, int a_mn_major, int lda, const void* B_dev, 
  * selects the persistent kernel (one CTA per SM walking the tiles with the
  * accumulator double-buffered in tensor memory; tile_n 128 or 256), 0 the
  * one-CTA-per-tile kernel. Same results. */
+/* The residual down-projection followed, in the same kernel, by the next
+ * LayerNorm of every output row (no single counterpart in the reference:
+ * mlpForwardTwo, model/mlp.metal:60-86, residualAdd, model/elementwise.
+ * metal:4-13, then layernormForward, model/layernorm.metal:10-71):
+ * h = bf16(h + bf16(A B)) in place ([M][N], N = 128 or 256), then x_norm,
+ * ln_out, stdev exactly as mg_layernorm_forward computes them from h. A is
+ * K-major [M][lda]; B as in mg_gemm_bf16. Persistent kernel, one output tile
+ * per 128 rows x N. */
+int mg_gemm_bf16_resid_layernorm(const void* A_dev, int lda, const void* B_dev, int b_mn_major, int ldb, int M,
+                                 int N, int K, void* h_dev, const void* gamma, const void* beta, void* x_norm,
+                                 void* ln_out, float* stdev, mg_stream_t stream);
+/* The same two layers for 128-wide rows at few rows (CartPole's 4096): K is
+ * split over a cluster of mg_gemm_rows_splits(K) CTAs whose fp32 partial
+ * tiles are summed in split order through distributed shared memory, then
+ * one warp per row applies the epilogue. h = bf16(h + bf16(A B)) in place
+ * ([M][128]) followed by x_norm, ln_out, stdev exactly as
+ * mg_layernorm_forward computes them from h. */
+int mg_gemm_rows_resid_layernorm(const void* A_dev, int lda, const void* B_dev, int b_mn_major, int ldb, int M,
+                                 int K, void* h_dev, const void* gamma, const void* beta, void* x_norm, void* ln_out,
+                                 float* stdev, mg_stream_t stream);
+/* The branch gradient of a residual block and its LayerNorm backward in one
+ * kernel (model/mlp.metal:131-153, then layernormBackward, model/layernorm.
+ * metal:74-127, and the skip add, model/ppo.h:851-852): dz = bf16(A B)
+ * ([M][128], K split as above), then resid_out and the dgamma / dbeta
+ * partials exactly as mg_layernorm_backward computes them from dz with
+ * resid. Rows per partial (8, 16 or 32) must divide 32. */
+int mg_gemm_rows_layernorm_backward(const void* A_dev, int lda, const void* B_dev, int b_mn_major, int ldb, int M,
+                                    int K, const void* x_norm, const void* gamma, const float* stdev,
+                                    const void* resid, void* resid_out, float* partial, mg_stream_t stream);
+int mg_gemm_rows_splits(int K);
 int mg_gemm_bf16_tiled(const void* A_dev, int a_mn_major, int lda, const void* B_dev, int b_mn_major, int ldb,
                        int M, int N, int K, int epilogue, void* out_dev, int ldo, const void* aux_dev, int ldaux,
                        int splits, int tile_n, int persistent, mg_stream_t stream);

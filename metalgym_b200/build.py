@@ -29,6 +29,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relax
 SOURCES: dict[str, list[str]] = {
     "runtime.cu": [],
     "gemm.cu": [],
+    "gemm_rows.cu": [],
     "policy.cu": [],
     "block_fwd.cu": [],
     "envs.cu": [],

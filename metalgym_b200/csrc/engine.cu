@@ -276,6 +276,8 @@ int PpoEngine::init() {
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
     fusedBlocks = block_forward_supported(E, H);
+    lnEpilogue = E == 128 || E == 256;
+    rowsKernels = gemm_rows_supported(E, H);
 
     // ---- parameters: model/ppo.h:375-445 (seeded normal init rounded to bf16)
     std::vector<std::vector<uint16_t>> init;
@@ -545,6 +547,58 @@ BlockFwdArgs PpoEngine::blockArgs(ActSet& a, int n, int rows) {
     return b;
 }
 
+// The residual blocks and the final LayerNorm of a forward pass
+// (model/ppo.h:590-615), after the input layer wrote a.h. Per block either
+// the fused block kernel, or LayerNorm + up GEMM (ReLU) + down GEMM (+ skip);
+// with the LayerNorm epilogue the down GEMM of block n also computes the
+// LayerNorm that follows it (block n + 1's, or the final one), which then has
+// no kernel of its own.
+int PpoEngine::blocksForward(ActSet& a, int rows, cudaStream_t st) {
+    auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
+    auto bw = [&](uint32_t p) { return reinterpret_cast<const __nv_bfloat16*>(weights + params[p].offset); };
+    const bool fused = useFusedBlock(rows);
+    const bool rowsK = !fused && useRowsKernels(rows);
+    const bool lnEpi = !fused && (rowsK || useLnEpilogue(rows));
+    for (int n = 0; n < L; n++) {
+        if (fused) {
+            MG_TRY(block_forward(blockArgs(a, n, rows), w(pUp[n]), w(pDown[n]), st));
+            continue;
+        }
+        if (n == 0 || !lnEpi)
+            MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
+        GemmCall up;
+        up.A = a.lnOut[n]; up.lda = E;
+        up.B = w(pUp[n]); up.b_mn = true; up.ldb = H;
+        up.M = rows; up.N = H; up.K = E;
+        up.epilogue = kEpiBf16Relu;
+        up.out = a.v[n]; up.ldo = H;
+        MG_TRY(gemm_bf16(up, st));
+        GemmCall down;
+        down.A = a.v[n]; down.lda = H;
+        down.B = w(pDown[n]); down.b_mn = true; down.ldb = E;
+        down.M = rows; down.N = E; down.K = H;
+        down.epilogue = kEpiBf16Resid;  // + skip, in place on the stream
+        down.aux = a.h; down.ldaux = E;
+        down.out = a.h; down.ldo = E;
+        LnOutputs ln;
+        if (lnEpi) {
+            ln = n + 1 < L ? LnOutputs{bw(pLnG[n + 1]), bw(pLnB[n + 1]), static_cast<__nv_bfloat16*>(a.lnXn[n + 1]),
+                                       static_cast<__nv_bfloat16*>(a.lnOut[n + 1]), a.lnSd[n + 1]}
+                           : LnOutputs{bw(pLnFg), bw(pLnFb), static_cast<__nv_bfloat16*>(a.fXn),
+                                       static_cast<__nv_bfloat16*>(a.fOut), a.fSd};
+            down.epilogue = kEpiResidLN;
+            down.ln = &ln;
+        }
+        if (rowsK) {
+            MG_TRY(gemm_rows_resid_layernorm(a.v[n], H, w(pDown[n]), true, E, rows, H, a.h, ln, st));
+            continue;
+        }
+        MG_TRY(gemm_bf16(down, st));
+    }
+    if (!lnEpi || L == 0) MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, rows, E, st));
+    return 0;
+}
+
 // model/ppo.h:575-626: input -> L x [LN -> up (ReLU) -> down (+ skip)] -> LN -> head.
 int PpoEngine::forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st) {
     const uint16_t* W = weights;
@@ -552,29 +606,7 @@ int PpoEngine::forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st)
     // (input_forward can also end with block 0's LayerNorm; measured in a
     // CUDA graph at 4096 rows the two kernels are faster: 5.25 against 5.87 µs)
     MG_TRY(input_forward(obs, w(pInW), w(pInB), a.h, rows, O, E, st));
-    for (int n = 0; n < L; n++) {
-        if (useFusedBlock(rows)) {
-            MG_TRY(block_forward(blockArgs(a, n, rows), w(pUp[n]), w(pDown[n]), st));
-            continue;
-        }
-        MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
-        GemmCall up;
-        up.A = a.lnOut[n]; up.lda = E;
-        up.B = w(pUp[n]); up.b_mn = true; up.ldb = H;
-        up.M = rows; up.N = H; up.K = E;
-        up.epilogue = 1;  // ReLU
-        up.out = a.v[n]; up.ldo = H;
-        MG_TRY(gemm_bf16(up, st));
-        GemmCall down;
-        down.A = a.v[n]; down.lda = H;
-        down.B = w(pDown[n]); down.b_mn = true; down.ldb = E;
-        down.M = rows; down.N = E; down.K = H;
-        down.epilogue = 2;  // + skip, in place on the stream
-        down.aux = a.h; down.ldaux = E;
-        down.out = a.h; down.ldo = E;
-        MG_TRY(gemm_bf16(down, st));
-    }
-    MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, rows, E, st));
+    MG_TRY(blocksForward(a, rows, st));
     GemmCall hd;
     hd.A = a.fOut; hd.lda = E;
     hd.B = w(pHead); hd.b_mn = true; hd.ldb = kHead;
@@ -594,28 +626,7 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
     // forward with activations saved (the input gathers the minibatch's obs rows)
     MG_TRY(input_forward(obsSlots, w(pInW), w(pInB), a.h, rows, O, E, st, rm));
-    for (int n = 0; n < L; n++) {
-        if (useFusedBlock(rows)) {
-            MG_TRY(block_forward(blockArgs(a, n, rows), w(pUp[n]), w(pDown[n]), st));
-            continue;
-        }
-        MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
-        GemmCall up;
-        up.A = a.lnOut[n]; up.lda = E;
-        up.B = w(pUp[n]); up.b_mn = true; up.ldb = H;
-        up.M = rows; up.N = H; up.K = E;
-        up.epilogue = 1;
-        up.out = a.v[n]; up.ldo = H;
-        MG_TRY(gemm_bf16(up, st));
-        GemmCall down;
-        down.A = a.v[n]; down.lda = H;
-        down.B = w(pDown[n]); down.b_mn = true; down.ldb = E;
-        down.M = rows; down.N = E; down.K = H;
-        down.epilogue = 2;
-        down.aux = a.h; down.ldaux = E;
-        down.out = a.h; down.ldo = E;
-        MG_TRY(gemm_bf16(down, st));
-    }
+    MG_TRY(blocksForward(a, rows, st));
     // loss (model/ppo.h:753-781): per-slot advantage statistics from
     // collect(), or in row mode the statistics of this minibatch's rows
     const LossHyper lh{hp.clip, hp.valueCoef, hp.entropyCoef};
@@ -624,7 +635,6 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         MG_TRY(advantage_stats_rows(advSlots, rm, rows, mbAdvStats, advPartial, advCounter, st));
         as = mbAdvStats;
     }
-    MG_TRY(layernorm_forward(a.h, a.fXn, a.fOut, w(pLnFg), w(pLnFb), a.fSd, rows, E, st));
     {
         GemmCall hd;
         hd.A = a.fOut; hd.lda = E;
@@ -695,6 +705,12 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         g3.epilogue = 4; g3.splits = downSplits;
         g3.out = downPart[n]; g3.ldo = E;
         MG_TRY(gemm_bf16(g3, side));
+        if (useRowsKernels(rows) && gemm_rows_ln_backward_supported(rows)) {
+            // dBranch and the LayerNorm backward with the skip add in one kernel
+            MG_TRY(gemm_rows_layernorm_backward(dVs[n], H, w(pUp[n]), false, H, rows, H, a.lnXn[n], w(pLnG[n]),
+                                                a.lnSd[n], dS[n + 1], dS[n], lnPart[n], st));
+            continue;
+        }
         GemmCall g4;  // dBranch = dV Up^T (model/mlp.metal:131-153)
         g4.A = dVs[n]; g4.lda = H;
         g4.B = w(pUp[n]); g4.ldb = H;  // Up [E][H] = [N][K]

@@ -178,6 +178,20 @@ class PpoEngine {
     bool fusedBlocks = false;
     bool useFusedBlock(int rows) const { return fusedBlocks && rows >= kFusedBlockMinRows; }
     static constexpr int kFusedBlockMinRows = 8192;
+    // the down GEMM of the unfused chain ends with the next LayerNorm
+    // (gemm_tc_persist.cuh, kEpiResidLN) where the embedding width is one
+    // output tile (128 or 256)
+    bool lnEpilogue = false;
+    bool useLnEpilogue(int rows) const { return lnEpilogue && rows >= kLnEpilogueMinRows; }
+    static constexpr int kLnEpilogueMinRows = 16384;
+    // the down projection and the branch gradient as cluster split-K products
+    // that end with the LayerNorm forward / backward (gemm_rows.cu). Measured
+    // in CUDA graphs at 2048-8192 rows of width 128 they are slower than the
+    // GEMM + LayerNorm pairs they replace (10.2 against 8.2 us at 4096 rows),
+    // so no row count selects them yet (kRowsKernelsMaxRows = 0)
+    bool rowsKernels = false;
+    bool useRowsKernels(int rows) const { return rowsKernels && rows <= kRowsKernelsMaxRows; }
+    static constexpr int kRowsKernelsMaxRows = 0;
 
     // multi-GPU: NCCL all-reduce (setComm) or the all-reduce over NVLink peer
     // memory (p2p.cu: p2pHandle on every rank, exchange, p2pOpen)
@@ -194,6 +208,7 @@ class PpoEngine {
 
    private:
     int forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st);
+    int blocksForward(ActSet& a, int rows, cudaStream_t st);
     BlockFwdArgs blockArgs(ActSet& a, int n, int rows);
     int minibatch(int j, bool rowMode, cudaStream_t st);  // reads sched[j], schedBetaPow[2j..]
     int captureCollect();

@@ -34,8 +34,12 @@ int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPa
     if (S::STAGED) {
         int rc = make_tmap_bf16(&em.out, p.out, p.N, p.M, p.ldo, 32);
         if (rc) return rc;
-        if (EPI == kEpiBf16Resid || EPI == kEpiBf16Mask) {
+        if (EPI == kEpiBf16Resid || EPI == kEpiBf16Mask || EPI == kEpiResidLN) {
             rc = make_tmap_bf16(&em.aux, p.aux, p.N, p.M, p.ldaux, 32);
+            if (rc) return rc;
+        }
+        if (EPI == kEpiResidLN) {
+            rc = make_tmap_bf16(&em.ln, p.ln.out, p.N, p.M, p.N, 32);
             if (rc) return rc;
         }
     }
@@ -56,15 +60,18 @@ int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPa
 template <int BN, bool AMN, bool BMN>
 int by_epi(int epi, bool persist, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits,
            cudaStream_t st) {
-    if (persist && BN >= 128) {
+    if constexpr (BN >= 128) {
+        if (persist) {
         switch (epi) {
             case kEpiBf16: return launch_persistent<BN, AMN, BMN, kEpiBf16>(ta, tb, p, splits, st);
             case kEpiBf16Relu: return launch_persistent<BN, AMN, BMN, kEpiBf16Relu>(ta, tb, p, splits, st);
             case kEpiBf16Resid: return launch_persistent<BN, AMN, BMN, kEpiBf16Resid>(ta, tb, p, splits, st);
             case kEpiBf16Mask: return launch_persistent<BN, AMN, BMN, kEpiBf16Mask>(ta, tb, p, splits, st);
             case kEpiF32: return launch_persistent<BN, AMN, BMN, kEpiF32>(ta, tb, p, splits, st);
+            case kEpiResidLN: return launch_persistent<BN, AMN, BMN, kEpiResidLN>(ta, tb, p, splits, st);
         }
         return fail(MG_ERR_ARGUMENT, "unknown GEMM epilogue");
+        }
     }
     switch (epi) {
         case kEpiBf16: return launch_one<BN, AMN, BMN, kEpiBf16>(ta, tb, p, splits, st);
@@ -111,6 +118,9 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
                  "gemm: this epilogue needs aux with ldaux a multiple of 8");
     MG_CHECK_ARG(c.epilogue != kEpiPolicyLoss || (c.N == 64 && c.ldo == 64 && c.splits == 1 && c.loss),
                  "gemm: the policy-loss epilogue needs the 64-column head and its loss arguments");
+    MG_CHECK_ARG(c.epilogue != kEpiResidLN ||
+                     ((c.N == 128 || c.N == 256) && c.ldo == c.N && c.ldaux == c.N && c.splits == 1 && c.ln),
+                 "gemm: the LayerNorm epilogue needs 128 or 256 dense columns and its LayerNorm arguments");
     int kPerSplit = (c.K + c.splits - 1) / c.splits;
     kPerSplit = (kPerSplit + 63) / 64 * 64;
     const int splits = (c.K + kPerSplit - 1) / kPerSplit;
@@ -144,6 +154,10 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
         bn = 64;  // one tile spans the head row
         persist = false;
     }
+    if (c.epilogue == kEpiResidLN) {
+        bn = c.N;  // one tile spans the row; persistent, staged epilogue
+        persist = true;
+    }
     MG_CHECK_ARG(bn == 32 || bn == 64 || bn == 128 || bn == 256, "gemm: tile N must be 32, 64, 128 or 256");
     MG_CHECK_ARG(bn != 32 || !c.b_mn, "gemm: 32-wide tiles need a K-major B");
     MG_CHECK_ARG(!persist || bn >= 128, "gemm: the persistent kernel needs tile N 128 or 256");
@@ -165,6 +179,7 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
     p.ldaux = c.ldaux;
     p.status = status_ptr();
     if (c.loss) p.loss = *c.loss;
+    if (c.ln) p.ln = *c.ln;
     p.tilesM = (c.M + 127) / 128;
     p.tilesN = (c.N + bn - 1) / bn;
     p.splits = splits;
@@ -222,5 +237,29 @@ extern "C" int mg_gemm_bf16_tiled(const void* A_dev, int a_mn_major, int lda, co
     c.splits = splits;
     c.bn = tile_n;
     c.persistent = tile_n == 0 ? (persistent ? -1 : 0) : (persistent ? 1 : 0);
+    return mg::gemm_bf16(c, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mg_gemm_bf16_resid_layernorm(const void* A_dev, int lda, const void* B_dev, int b_mn_major, int ldb,
+                                            int M, int N, int K, void* h_dev, const void* gamma, const void* beta,
+                                            void* x_norm, void* ln_out, float* stdev, mg_stream_t stream) {
+    MG_CHECK_ARG(h_dev && gamma && beta && x_norm && ln_out && stdev, "mg_gemm_bf16_resid_layernorm: null argument");
+    mg::LnOutputs ln{static_cast<const __nv_bfloat16*>(gamma), static_cast<const __nv_bfloat16*>(beta),
+                     static_cast<__nv_bfloat16*>(x_norm), static_cast<__nv_bfloat16*>(ln_out), stdev};
+    mg::GemmCall c;
+    c.A = A_dev;
+    c.lda = lda;
+    c.B = B_dev;
+    c.b_mn = b_mn_major != 0;
+    c.ldb = ldb;
+    c.M = M;
+    c.N = N;
+    c.K = K;
+    c.epilogue = mg::kEpiResidLN;
+    c.out = h_dev;
+    c.ldo = N;
+    c.aux = h_dev;
+    c.ldaux = N;
+    c.ln = &ln;
     return mg::gemm_bf16(c, reinterpret_cast<cudaStream_t>(stream));
 }

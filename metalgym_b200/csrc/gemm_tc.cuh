@@ -17,26 +17,20 @@
 // No cluster launch: every CTA loads its own tiles.
 #pragma once
 
-#include "loss_row.cuh"
+#include "gemm.h"
+#include "row_epilogues.cuh"
 #include "metalgym/pdl.cuh"
 #include "ptx.cuh"
 
 namespace mg {
 
-enum GemmEpilogue : int {
-    kEpiBf16 = 0,       // out_bf16 = bf16(acc)
-    kEpiBf16Relu = 1,   // v = bf16(acc); out = v > 0 ? v : v * 0          (model/mlp.metal:49-56)
-    kEpiBf16Resid = 2,  // out = bf16(aux + bf16(acc))                     (mlp.metal:85 + elementwise.metal:4-13)
-    kEpiBf16Mask = 3,   // out = bf16(acc) * (aux > 0)                     (model/mlp.metal:119-126)
-    kEpiF32 = 4,        // out_f32 = acc (split z writes slice z of M x N)
-    kEpiPolicyLoss = 5, // out_bf16 = bf16(acc) (the policy head), then the categorical PPO loss of each row
-};
 
 struct GemmParams {
     int M, N, K;
     int kPerSplit;  // multiple of 64
     int tilesM, tilesN, splits;  // work units of the persistent kernel
     PolicyLossRows loss;         // kEpiPolicyLoss: the loss of each output row
+    LnOutputs ln;                // kEpiResidLN: the LayerNorm of each output row
     void* out;
     int ldo;
     const __nv_bfloat16* aux;

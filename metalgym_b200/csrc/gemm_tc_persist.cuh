@@ -37,8 +37,9 @@ struct PersistShape {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int SLAB_OFF = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFF = SLAB_OFF + (STAGED ? 4 * SLAB : 0);
-    static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (256 or 512 columns)
-    static constexpr int SMEM_BYTES = BAR_OFF + 256 /*barriers*/ + 1024 /*align*/;
+    static constexpr int GB_OFF = BAR_OFF + 256;  // kEpiResidLN: gamma, beta as fp32
+    static constexpr int TMEM_COLS = 2 * BN;      // two accumulators (256 or 512 columns)
+    static constexpr int SMEM_BYTES = GB_OFF + (EPI == kEpiResidLN ? 2 * BN * 4 : 0) + 1024 /*align*/;
 };
 
 // Byte offset of 16-byte chunk k (8 bf16, 0..BN/8-1) of slab row r (0..31)
@@ -78,9 +79,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int row, int
     }
 }
 
-// Output and aux tensor maps of the staged epilogue (boxes of 64 columns x 32 rows).
+// Output, aux and LayerNorm-output tensor maps of the staged epilogue (boxes
+// of 64 columns x 32 rows).
 struct EpiMaps {
-    CUtensorMap out, aux;
+    CUtensorMap out, aux, ln;
 };
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
@@ -88,7 +90,7 @@ __global__ void __launch_bounds__(192, 1)
     gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ EpiMaps em, const GemmParams p) {
     using S = PersistShape<BN, EPI>;
-    constexpr bool HAS_AUX = EPI == kEpiBf16Resid || EPI == kEpiBf16Mask;
+    constexpr bool HAS_AUX = EPI == kEpiBf16Resid || EPI == kEpiBf16Mask || EPI == kEpiResidLN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
@@ -98,6 +100,7 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* done = tempty + 2;
     uint64_t* auxFull = done + 1;         // [4], one per epilogue warp
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(auxFull + 4);
+    float* s_gb = reinterpret_cast<float*>(smem + S::GB_OFF);  // kEpiResidLN: gamma[BN], beta[BN]
 
     mg_pdl_trigger();
     const int warp = threadIdx.x >> 5;
@@ -121,6 +124,13 @@ __global__ void __launch_bounds__(192, 1)
         prefetch_tensormap(&tmB);
         if (S::STAGED) prefetch_tensormap(&em.out);
         if (HAS_AUX) prefetch_tensormap(&em.aux);
+        if (EPI == kEpiResidLN) prefetch_tensormap(&em.ln);
+    }
+    if (EPI == kEpiResidLN) {
+        for (int i = threadIdx.x; i < BN; i += blockDim.x) {
+            s_gb[i] = __bfloat162float(p.ln.gamma[i]);
+            s_gb[BN + i] = __bfloat162float(p.ln.beta[i]);
+        }
     }
     if (warp == 2) {
         tmem_alloc(tmem_slot, S::TMEM_COLS);
@@ -274,7 +284,7 @@ __global__ void __launch_bounds__(192, 1)
                             const float r = round_bf16(x[i]);
                             x[i] = r > 0.0f ? r : r * 0.0f;
                         }
-                    } else if (HAS_AUX) {
+                    } else if (HAS_AUX) {  // residual, LayerNorm-ending residual, mask
                         const uint4 w = *cell;
                         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
                         float au[8];
@@ -285,8 +295,8 @@ __global__ void __launch_bounds__(192, 1)
                         }
 #pragma unroll
                         for (int i = 0; i < 8; i++)
-                            x[i] = EPI == kEpiBf16Resid ? au[i] + round_bf16(x[i])
-                                                        : round_bf16(x[i]) * (au[i] > 0.0f ? 1.0f : 0.0f);
+                            x[i] = EPI == kEpiBf16Mask ? round_bf16(x[i]) * (au[i] > 0.0f ? 1.0f : 0.0f)
+                                                       : au[i] + round_bf16(x[i]);
                     }
                     uint32_t o[4];
 #pragma unroll
@@ -304,6 +314,106 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                     for (int j = 0; j < BN / 64; j++)
                         if (n0 + 64 * j < p.N && row0 < p.M) tma_store_2d(&em.out, n0 + 64 * j, row0, slab + j * 4096);
+                    bulk_commit();
+                }
+            }
+            if constexpr (EPI == kEpiResidLN) {
+                // the LayerNorm of the warp's 32 rows now in the slab: one row
+                // across the lanes at a time (lane l: columns l VPT ..), eight
+                // rows side by side, in k_layernorm_forward's arithmetic and
+                // summation order (bit-identical to it)
+                constexpr int VPT = BN / 32;
+                float g[VPT], bb[VPT];
+#pragma unroll
+                for (int j = 0; j < VPT; j++) {
+                    g[j] = s_gb[lane * VPT + j];
+                    bb[j] = s_gb[BN + lane * VPT + j];
+                }
+                // lane l's VPT columns of a slab row: a whole 16-byte chunk
+                // (BN 256) or half of one (BN 128)
+                const uint32_t cellOff = VPT == 8 ? 0u : (uint32_t)(lane & 1) * 8u;
+                const int cellChunk = VPT == 8 ? lane : lane >> 1;
+#pragma unroll 1
+                for (int r0 = 0; r0 < 32; r0 += 8) {
+                    float v[8][VPT], mean[8], sq[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        const uint8_t* cell = slab + slab_offset(r0 + u, cellChunk) + cellOff;
+                        uint32_t w[VPT / 2];
+                        if constexpr (VPT == 8) {
+                            const uint4 x = *reinterpret_cast<const uint4*>(cell);
+                            w[0] = x.x;
+                            w[1] = x.y;
+                            w[2] = x.z;
+                            w[3] = x.w;
+                        } else {
+                            const uint2 x = *reinterpret_cast<const uint2*>(cell);
+                            w[0] = x.x;
+                            w[1] = x.y;
+                        }
+                        float sm = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < VPT / 2; i++) {
+                            v[u][2 * i] = __uint_as_float(w[i] << 16);
+                            v[u][2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+                        }
+#pragma unroll
+                        for (int j = 0; j < VPT; j++) sm = __fadd_rn(sm, v[u][j]);
+                        mean[u] = sm;
+                    }
+                    warp_sum_n<8>(mean);
+#pragma unroll
+                    for (int u = 0; u < 8; u++) mean[u] = __fdiv_rn(mean[u], (float)BN);
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        sq[u] = 0.0f;
+#pragma unroll
+                        for (int j = 0; j < VPT; j++) {
+                            const float d = __fsub_rn(v[u][j], mean[u]);
+                            sq[u] = __fadd_rn(sq[u], __fmul_rn(d, d));
+                        }
+                    }
+                    warp_sum_n<8>(sq);
+                    // lnOut replaces h in the slab: the h store must have read it
+                    if (r0 == 0) {
+                        if (lane == 0) bulk_wait_read<0>();
+                        __syncwarp();
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        const int rowU = row0 + r0 + u;
+                        const float sd = __fsqrt_rn(__fadd_rn(__fdiv_rn(sq[u], (float)BN), 1e-5f));
+                        const float rstd = __fdiv_rn(1.0f, sd);
+                        if (lane == 0 && rowU < p.M) p.ln.stdev[rowU] = sd;
+                        uint32_t xw[VPT / 2], yw[VPT / 2];
+#pragma unroll
+                        for (int i = 0; i < VPT / 2; i++) {
+                            const float x0 = __fmul_rn(__fsub_rn(v[u][2 * i], mean[u]), rstd);
+                            const float x1 = __fmul_rn(__fsub_rn(v[u][2 * i + 1], mean[u]), rstd);
+                            __nv_bfloat162 xh = __floats2bfloat162_rn(x0, x1);
+                            __nv_bfloat162 yh = __floats2bfloat162_rn(__fadd_rn(__fmul_rn(g[2 * i], x0), bb[2 * i]),
+                                                                      __fadd_rn(__fmul_rn(g[2 * i + 1], x1), bb[2 * i + 1]));
+                            xw[i] = *reinterpret_cast<uint32_t*>(&xh);
+                            yw[i] = *reinterpret_cast<uint32_t*>(&yh);
+                        }
+                        uint8_t* cell = slab + slab_offset(r0 + u, cellChunk) + cellOff;
+                        __nv_bfloat16* xdst = p.ln.xNorm + (size_t)rowU * BN + lane * VPT;
+                        if constexpr (VPT == 8) {
+                            if (rowU < p.M)
+                                *reinterpret_cast<uint4*>(xdst) = make_uint4(xw[0], xw[1], xw[2], xw[3]);
+                            *reinterpret_cast<uint4*>(cell) = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+                        } else {
+                            if (rowU < p.M) *reinterpret_cast<uint2*>(xdst) = make_uint2(xw[0], xw[1]);
+                            *reinterpret_cast<uint2*>(cell) = make_uint2(yw[0], yw[1]);
+                        }
+                    }
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int j = 0; j < BN / 64; j++)
+                        if (row0 < p.M) tma_store_2d(&em.ln, 64 * j, row0, slab + j * 4096);
                     bulk_commit();
                 }
             }

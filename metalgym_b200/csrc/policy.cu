@@ -2,7 +2,7 @@
 // The dense products live in gemm.cu; everything else lives here.
 #include <algorithm>
 
-#include "loss_row.cuh"
+#include "row_epilogues.cuh"
 #include "policy.h"
 #include "policy_kernels.cuh"
 #include "runtime.h"
@@ -957,6 +957,7 @@ static int ln_rows_per_cta(int rows) {
 }
 
 int layernorm_backward_parts(int rows) { return grid_rows(rows, ln_rows_per_cta(rows)); }
+int layernorm_rows_per_part(int rows) { return ln_rows_per_cta(rows); }
 
 int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, const void* resid,
                        float* partial, int rows, int cols, cudaStream_t st, void* residOut) {

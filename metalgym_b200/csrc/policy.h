@@ -5,7 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "loss_row.cuh"
+#include "row_epilogues.cuh"
 #include "metalgym/rowmap.h"
 
 namespace mg {
@@ -64,15 +64,6 @@ struct RowMap {
     uint64_t total;    // T * R
 };
 
-// LayerNorm outputs of a kernel that ends with the next LayerNorm of its rows.
-struct LnOutputs {
-    const __nv_bfloat16* gamma;
-    const __nv_bfloat16* beta;
-    __nv_bfloat16* xNorm;
-    __nv_bfloat16* out;
-    float* stdev;
-};
-
 // With ln, the LayerNorm of the output rows (as layernorm_forward computes
 // it, bit-identical) is written too.
 int input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int inDim, int outDim,
@@ -83,6 +74,7 @@ int input_backward(const float* obs, const void* dZ, float* partial, int rows, i
 int layernorm_forward(const void* x, void* xNorm, void* out, const void* gamma, const void* beta, float* stdev,
                       int rows, int cols, cudaStream_t st);
 int layernorm_backward_parts(int rows);
+int layernorm_rows_per_part(int rows);  // rows per dgamma / dbeta partial of layernorm_backward
 int layernorm_backward(void* dZ, const void* xNorm, const void* gamma, const float* stdev, const void* resid,
                        float* partial, int rows, int cols, cudaStream_t st, void* residOut = nullptr);
 int sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* logProb, float* value, int rows,

@@ -122,6 +122,41 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// warp_sum of N independent values, each summed exactly as warp_sum sums it,
+// with the N shuffles of a butterfly stage issued back to back: the
+// shuffles of one chain are not overlapped by the compiler, those of
+// independent chains written this way are.
+template <int N>
+__device__ __forceinline__ void warp_sum_n(float* v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float t[N];
+#pragma unroll
+        for (int u = 0; u < N; u++) t[u] = __shfl_xor_sync(0xffffffffu, v[u], o);
+#pragma unroll
+        for (int u = 0; u < N; u++) v[u] = __fadd_rn(v[u], t[u]);
+    }
+}
+
+// Sum over the warp, xor butterfly 16, 8, 4, 2, 1 (every lane gets the sum).
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Every thread of every CTA of the cluster; orders this CTA's shared-memory
+// writes before the other CTAs' reads after it.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),

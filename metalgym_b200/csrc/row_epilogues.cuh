@@ -1,6 +1,7 @@
-// The categorical PPO loss of one row (model/policy.metal:14-69), shared by
-// the standalone loss kernel and the policy-head GEMM's fused epilogue, so
-// both give the same bits.
+// Row computations shared by standalone row kernels and fused GEMM
+// epilogues, so that both give the same bits: the categorical PPO loss of one
+// row (model/policy.metal:14-69) and the arguments of a LayerNorm that ends a
+// kernel.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -13,6 +14,15 @@
 namespace mg {
 
 constexpr int kLossHeadDim = 64;  // head columns (model/ppo.h:116)
+
+// LayerNorm outputs of a kernel that ends with the next LayerNorm of its rows.
+struct LnOutputs {
+    const __nv_bfloat16* gamma;
+    const __nv_bfloat16* beta;
+    __nv_bfloat16* xNorm;
+    __nv_bfloat16* out;
+    float* stdev;
+};
 
 // Inputs and outputs of the loss of a minibatch's rows. Minibatch row r
 // reads rollout row mg_minibatch_row(*mb, r, envRows, total) of action / adv
