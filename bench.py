@@ -404,24 +404,34 @@ def dominant_kernel_roofline(lib, torch, dev, stream):
             "traffic": profile_traffic("gemm_wgrad_128x512x4096_split16.md")}
 
     # the longest kernel on the critical path of a minibatch: the down-projection
-    # with the fused residual add (rows x embed x hidden = 4096 x 128 x 512)
+    # with the residual add and the next LayerNorm, K split over a cluster of
+    # 4 CTAs (rows x embed x hidden = 4096 x 128 x 512)
     Md, Nd, Kd = ENVS_PER_GPU, EMBED, EMBED * SCALE
     va = torch.relu(torch.randn(Md, Kd, device=f"cuda:{dev}")).bfloat16()
     vb = (torch.randn(Kd, Nd, device=f"cuda:{dev}") / 16).bfloat16()
     vh = torch.randn(Md, Nd, device=f"cuda:{dev}").bfloat16()
-    vo = torch.empty(Md, Nd, device=f"cuda:{dev}", dtype=torch.bfloat16)
+    vg = torch.ones(Nd, device=f"cuda:{dev}").bfloat16()
+    vbt = torch.zeros(Nd, device=f"cuda:{dev}").bfloat16()
+    vxn = torch.empty_like(vh)
+    vy = torch.empty_like(vh)
+    vsd = torch.empty(Md, device=f"cuda:{dev}")
 
     def launch_down():
-        return lib.mg_gemm_bf16(va.data_ptr(), 0, Kd, vb.data_ptr(), 1, Nd, Md, Nd, Kd, 2, vo.data_ptr(), Nd,
-                                vh.data_ptr(), Nd, 1, sp)
+        return lib.mg_gemm_rows_resid_layernorm(va.data_ptr(), Kd, vb.data_ptr(), 1, Nd, Md, Kd, vh.data_ptr(),
+                                                vg.data_ptr(), vbt.data_ptr(), vxn.data_ptr(), vy.data_ptr(),
+                                                vsd.data_ptr(), sp)
 
     usd = _time_launches(launch_down, torch, stream)
     fd = 2.0 * Md * Nd * Kd
+    # bytes: V and Dp read, h read and written, x-hat, LayerNorm out, sigma written
+    bd = (Md * Kd + Kd * Nd + 4 * Md * Nd) * 2 + Md * 4
     roof["critical_path_kernel"] = {
-        "kernel": "gemm_tc_kernel<64, K-major A, MN-major B, +residual> (MLP down-projection, 4096x128x512)",
-        "bound": "tensor", "achieved": fd / (usd * 1e-6) / 1e12, "peak": tflops, "unit": "TFLOP/s",
-        "frac": fd / (usd * 1e-6) / 1e12 / tflops, "us_per_launch": usd, "flop_per_launch": fd,
-        "traffic": profile_traffic("gemm_down_4096x128x512.md")}
+        "kernel": "k_gemm_rows<MN-major B, residual + LayerNorm> (down-projection + next LayerNorm, "
+                  "4096x128x512, K split over a 4-CTA cluster)",
+        "bound": "latency (neither roof)", "achieved": fd / (usd * 1e-6) / 1e12, "peak": tflops, "unit": "TFLOP/s",
+        "frac": fd / (usd * 1e-6) / 1e12 / tflops, "hbm_frac": bd / (usd * 1e-6) / 1e9 / hbm,
+        "us_per_launch": usd, "flop_per_launch": fd, "algorithmic_bytes_per_launch": bd,
+        "traffic": profile_traffic("gemm_rows_down_layernorm_4096x128x512.md")}
     return roof
 
 

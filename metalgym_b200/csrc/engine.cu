@@ -556,8 +556,8 @@ BlockFwdArgs PpoEngine::blockArgs(ActSet& a, int n, int rows) {
 int PpoEngine::blocksForward(ActSet& a, int rows, cudaStream_t st) {
     auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
     auto bw = [&](uint32_t p) { return reinterpret_cast<const __nv_bfloat16*>(weights + params[p].offset); };
-    const bool fused = useFusedBlock(rows);
-    const bool rowsK = !fused && useRowsKernels(rows);
+    const bool rowsK = useRowsForward(rows);
+    const bool fused = !rowsK && useFusedBlock(rows);
     const bool lnEpi = !fused && (rowsK || useLnEpilogue(rows));
     for (int n = 0; n < L; n++) {
         if (fused) {
@@ -705,7 +705,7 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         g3.epilogue = 4; g3.splits = downSplits;
         g3.out = downPart[n]; g3.ldo = E;
         MG_TRY(gemm_bf16(g3, side));
-        if (useRowsKernels(rows) && gemm_rows_ln_backward_supported(rows)) {
+        if (useRowsBackward(rows) && gemm_rows_ln_backward_supported(rows)) {
             // dBranch and the LayerNorm backward with the skip add in one kernel
             MG_TRY(gemm_rows_layernorm_backward(dVs[n], H, w(pUp[n]), false, H, rows, H, a.lnXn[n], w(pLnG[n]),
                                                 a.lnSd[n], dS[n + 1], dS[n], lnPart[n], st));

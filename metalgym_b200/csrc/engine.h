@@ -185,13 +185,17 @@ class PpoEngine {
     bool useLnEpilogue(int rows) const { return lnEpilogue && rows >= kLnEpilogueMinRows; }
     static constexpr int kLnEpilogueMinRows = 16384;
     // the down projection and the branch gradient as cluster split-K products
-    // that end with the LayerNorm forward / backward (gemm_rows.cu). Measured
-    // in CUDA graphs at 2048-8192 rows of width 128 they are slower than the
-    // GEMM + LayerNorm pairs they replace (10.2 against 8.2 us at 4096 rows),
-    // so no row count selects them yet (kRowsKernelsMaxRows = 0)
+    // that end with the LayerNorm forward / backward (gemm_rows.cu): at 4096
+    // rows of width 128 (128 CTAs) faster than the GEMM + LayerNorm pairs
+    // they replace (in CUDA graphs: 6.6 against 8.2 us forward, 7.4 against
+    // 8.5 us backward). The forward one takes precedence over the fused block
+    // kernel up to 4096 rows; the backward one applies up to 8192 rows
+    // (10.9 against 11.1 us there).
     bool rowsKernels = false;
-    bool useRowsKernels(int rows) const { return rowsKernels && rows <= kRowsKernelsMaxRows; }
-    static constexpr int kRowsKernelsMaxRows = 0;
+    bool useRowsForward(int rows) const { return rowsKernels && rows <= kRowsForwardMaxRows; }
+    bool useRowsBackward(int rows) const { return rowsKernels && rows <= kRowsBackwardMaxRows; }
+    static constexpr int kRowsForwardMaxRows = 4096;
+    static constexpr int kRowsBackwardMaxRows = 8192;
 
     // multi-GPU: NCCL all-reduce (setComm) or the all-reduce over NVLink peer
     // memory (p2p.cu: p2pHandle on every rank, exchange, p2pOpen)

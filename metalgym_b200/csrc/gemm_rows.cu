@@ -42,18 +42,27 @@ namespace {
 
 constexpr int kRowsBM = 128;
 constexpr int kRowsBN = 128;
-constexpr int kRowsStages = 4;
+constexpr int kRowsStages = 2;
 constexpr uint32_t kRowsCluster = 4;  // CTAs per cluster = K splits; each ends 32 rows of the tile
+// 16 warps: all copy the accumulator out of TMEM (quadrant w % 4, columns
+// 32 (w / 4) ..), and two rows per warp give the row epilogue enough warps to
+// hide its latency (four warps of eight rows each were latency bound)
+constexpr int kRowsThreads = 512;
 constexpr int kRowsA = kRowsBM * 64 * 2;  // 16 KB per 64-wide K block
 constexpr int kRowsB = kRowsBN * 64 * 2;
 constexpr int kRowsStage = kRowsA + kRowsB;
-constexpr int kRowsRing = kRowsStages * kRowsStage;  // 128 KB
+constexpr int kRowsRing = kRowsStages * kRowsStage;  // 64 KB
 // after the MMAs the ring holds the fp32 partial tile (64 KB, read by the
-// whole cluster) and the LayerNorm-backward column sums (32 KB, this CTA)
+// whole cluster); the LayerNorm-backward column sums (32 KB, this CTA) follow
+// it. About 97 KB in all: two CTAs fit on an SM, so the next kernel's CTAs
+// can start (programmatic dependent launch) beside this one's.
 constexpr int kRowsTile = kRowsBM * kRowsBN * 4;
-constexpr int kRowsRedOff = kRowsTile;
-constexpr int kRowsSmem = kRowsRing + 256 + 1024;
-static_assert(kRowsRedOff + 4 * 8 * 2 * kRowsBN * 4 <= kRowsRing, "column sums must fit in the ring");
+constexpr int kRowsRedOff = kRowsRing;
+constexpr int kRowsRedBytes = 4 * 8 * 2 * kRowsBN * 4;
+constexpr int kRowsSmem = kRowsRing + kRowsRedBytes + 256 + 1024;
+static_assert(kRowsTile <= kRowsRing, "the partial tile must fit in the ring");
+constexpr int kRowsSmemOnePerSm = 120 * 1024;  // more than half an SM's 228 KB
+static_assert(kRowsSmemOnePerSm >= kRowsSmem, "");
 
 enum RowsEpilogue : int { kRowsResidLN = 0, kRowsLNBackward = 1 };
 
@@ -86,12 +95,15 @@ __device__ __forceinline__ void bf4_store(__nv_bfloat16* p, float a, float b, fl
 }
 
 template <bool B_MN, int EPI, int RPC>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kRowsThreads, 2)
     k_gemm_rows(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const RowsParams p) {
     constexpr int E = kRowsBN;
+    // x / E as x * (1 / E): exact for a power of two; 1 / x as the correctly
+    // rounded reciprocal: the same values as the LayerNorm kernels' divisions
+    constexpr float kInvE = 1.0f / E;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRowsRing);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRowsRing + kRowsRedBytes);
     uint64_t* empty = full + kRowsStages;
     uint64_t* done = empty + kRowsStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -168,26 +180,25 @@ __global__ void __launch_bounds__(128, 1)
     }
 
     // ---- this CTA's fp32 partial tile into shared memory (the ring is free
-    // once `done` fired: every MMA, and so every read of the ring, completed)
+    // once `done` fired: every MMA, and so every read of the ring, completed).
+    // Warp w reads TMEM lanes 32 (w % 4) .. (its quadrant), columns 32 (w / 4) ..
     __syncwarp();
     const bool ready = (nk == 0) || mbar_wait_warp(done, 0, p.status, kDevTimeoutDone);
     tc_fence_after();
     {
-        const int tr = warp * 32 + lane;
-#pragma unroll 1
-        for (int c = 0; c < kRowsBN / 32; c++) {
-            float v[32];
-            if (ready && nk > 0) {
-                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
-            } else {
+        const int qd = warp & 3, cc = warp >> 2;
+        const int tr = qd * 32 + lane;
+        float v[32];
+        if (ready && nk > 0) {
+            tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(cc * 32), v);
+        } else {
 #pragma unroll
-                for (int i = 0; i < 32; i++) v[i] = 0.0f;
-            }
-#pragma unroll
-            for (int k = 0; k < 8; k++)
-                *reinterpret_cast<float4*>(smem + tile_offset(tr, c * 8 + k)) =
-                    make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+            for (int i = 0; i < 32; i++) v[i] = 0.0f;
         }
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            *reinterpret_cast<float4*>(smem + tile_offset(tr, cc * 8 + k)) =
+                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
     }
     tc_fence_before();
     __syncthreads();
@@ -198,29 +209,42 @@ __global__ void __launch_bounds__(128, 1)
     }
     cluster_sync();  // every partial tile of the cluster is complete
 
-    // ---- rows [32 q, 32 q + 32) of the tile: warp w takes 8 of them. Row
-    // order (as k_layernorm_backward with RPC rows per CTA and 8 warps): per
-    // group g of RPC rows, "virtual warps" v = w and w + 4 take rows v, v + 8, ..
-    // The eight rows are computed side by side (their warp sums interleave);
-    // loads and stores of rows past M are skipped, their values are unused.
+    // ---- rows [32 q, 32 q + 32) of the tile, NR per warp, computed side by
+    // side (their warp sums interleave); loads and stores of rows past M are
+    // skipped, their values unused. LayerNorm backward row order (that of
+    // k_layernorm_backward with RPC rows per CTA and 8 warps): per group g of
+    // RPC rows, virtual warp v takes rows v, v + 8, .. and sums its dgamma /
+    // dbeta over them in that order; virtual warp (g, v) is warp 8 g + v (mod
+    // 16) here.
     constexpr int G = 32 / RPC;
     constexpr int J = RPC / 8;
+    constexpr int NR = EPI == kRowsResidLN ? 2 : (RPC == 32 ? 4 : 2);
+    const bool active = EPI == kRowsResidLN || RPC != 32 || warp < 8;
     const int c0 = lane * 4;
-    int rows[8];
-    bool live[8];
-    float4 acc[8];
+    int rows[NR];
+    bool live[NR];
+    float4 acc[NR];
 #pragma unroll
-    for (int t = 0; t < 8; t++) {
-        const int s = t & 1, j = (t >> 1) % J, g = (t >> 1) / J;
-        const int tr = 32 * (int)q + g * RPC + warp + 4 * s + 8 * j;
+    for (int t = 0; t < NR; t++) {
+        int tl;  // row within this CTA's 32
+        if (EPI == kRowsResidLN) {
+            tl = warp + 16 * t;
+        } else {
+            const int pr = warp + 16 * (t / J), j = t % J;
+            tl = (pr / 8) * RPC + (pr % 8) + 8 * j;
+        }
+        const int tr = 32 * (int)q + tl;
         rows[t] = m0 + tr;
-        live[t] = rows[t] < p.M;
-        const uint8_t* cell = smem + tile_offset(tr, lane);
-        float4 a = *reinterpret_cast<const float4*>(__cluster_map_shared_rank(cell, 0));
+        live[t] = active && rows[t] < p.M;
+        const uint8_t* cell = smem + tile_offset(tr & 127, lane);
+        float4 a = make_float4(0, 0, 0, 0);
+        if (active) {
+            a = *reinterpret_cast<const float4*>(__cluster_map_shared_rank(cell, 0));
 #pragma unroll
-        for (uint32_t r = 1; r < kRowsCluster; r++) {
-            const float4 b = *reinterpret_cast<const float4*>(__cluster_map_shared_rank(cell, r));
-            a = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+            for (uint32_t r = 1; r < kRowsCluster; r++) {
+                const float4 b = *reinterpret_cast<const float4*>(__cluster_map_shared_rank(cell, r));
+                a = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+            }
         }
         acc[t] = a;
     }
@@ -228,9 +252,9 @@ __global__ void __launch_bounds__(128, 1)
     if (EPI == kRowsResidLN) {
         const float4 gm = bf4_load(p.ln.gamma + c0), bt = bf4_load(p.ln.beta + c0);
         const float g[4] = {gm.x, gm.y, gm.z, gm.w}, b[4] = {bt.x, bt.y, bt.z, bt.w};
-        float v[8][4], mean[8], rstd[8];
+        float v[NR][4], ms[2 * NR];  // ms: row sums (0..NR-1), sums of squares (NR..)
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
+        for (int t = 0; t < NR; t++) {
             const float4 hin = live[t] ? bf4_load(p.resid + (size_t)rows[t] * E + c0) : make_float4(0, 0, 0, 0);
             // the residual add of the down projection (kEpiBf16Resid), then h as bf16
             v[t][0] = round_bf16(hin.x + round_bf16(acc[t].x));
@@ -241,35 +265,31 @@ __global__ void __launch_bounds__(128, 1)
             float sm = 0.0f;
 #pragma unroll
             for (int i = 0; i < 4; i++) sm = __fadd_rn(sm, v[t][i]);
-            mean[t] = sm;
+            ms[t] = sm;
         }
-        warp_sum_n<8>(mean);
+        warp_sum_n<NR>(ms);
 #pragma unroll
-        for (int t = 0; t < 8; t++) mean[t] = __fdiv_rn(mean[t], (float)E);
-        float sq[8];
-#pragma unroll
-        for (int t = 0; t < 8; t++) {
-            sq[t] = 0.0f;
+        for (int t = 0; t < NR; t++) {
+            ms[t] = __fmul_rn(ms[t], kInvE);
+            float sq = 0.0f;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const float d = __fsub_rn(v[t][i], mean[t]);
-                sq[t] = __fadd_rn(sq[t], __fmul_rn(d, d));
+                const float d = __fsub_rn(v[t][i], ms[t]);
+                sq = __fadd_rn(sq, __fmul_rn(d, d));
             }
+            ms[NR + t] = sq;
         }
-        warp_sum_n<8>(sq);
+        warp_sum_n<NR>(ms + NR);
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
-            const float sd = __fsqrt_rn(__fadd_rn(__fdiv_rn(sq[t], (float)E), 1e-5f));
-            rstd[t] = __fdiv_rn(1.0f, sd);
-            if (lane == 0 && live[t]) p.ln.stdev[rows[t]] = sd;
-        }
-#pragma unroll
-        for (int t = 0; t < 8; t++) {
+        for (int t = 0; t < NR; t++) {
+            const float sd = __fsqrt_rn(__fadd_rn(__fmul_rn(ms[NR + t], kInvE), 1e-5f));
+            const float rstd = __frcp_rn(sd);
             if (!live[t]) continue;
+            if (lane == 0) p.ln.stdev[rows[t]] = sd;
             float xn[4], y[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                xn[i] = __fmul_rn(__fsub_rn(v[t][i], mean[t]), rstd[t]);
+                xn[i] = __fmul_rn(__fsub_rn(v[t][i], ms[t]), rstd);
                 y[i] = __fadd_rn(__fmul_rn(g[i], xn[i]), b[i]);
             }
             bf4_store(p.ln.xNorm + (size_t)rows[t] * E + c0, xn[0], xn[1], xn[2], xn[3]);
@@ -279,72 +299,67 @@ __global__ void __launch_bounds__(128, 1)
         float* red = reinterpret_cast<float*>(smem + kRowsRedOff);  // [G][8 virtual warps][dgamma | dbeta]
         const float4 gm = bf4_load(p.gamma + c0);
         const float g[4] = {gm.x, gm.y, gm.z, gm.w};
-        float xn[8][4], dxn[8][4], s12[16], rdev[8];  // s12: row sums of dxn (0..7), of dxn x-hat (8..15)
-        float* s1 = s12;
-        float* s2 = s12 + 8;
-        float dg[2][4], db[2][4];
+        float xn[NR][4], dxn[NR][4], s12[2 * NR], rdev[NR];  // s12: sums of dxn (0..NR-1), of dxn x-hat (NR..)
+        float dg[4], db[4];
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
-            const int s = t & 1;
+        for (int t = 0; t < NR; t++) {
             const float4 x4 = live[t] ? bf4_load(p.xNorm + (size_t)rows[t] * E + c0) : make_float4(0, 0, 0, 0);
-            rdev[t] = __fdiv_rn(1.0f, live[t] ? p.stdev[rows[t]] : 1.0f);
+            rdev[t] = __frcp_rn(live[t] ? p.stdev[rows[t]] : 1.0f);
             xn[t][0] = x4.x;
             xn[t][1] = x4.y;
             xn[t][2] = x4.z;
             xn[t][3] = x4.w;
             const float dz[4] = {round_bf16(acc[t].x), round_bf16(acc[t].y), round_bf16(acc[t].z),
                                  round_bf16(acc[t].w)};
-            if ((t >> 1) % J == 0) {
+            if (t % J == 0) {
 #pragma unroll
-                for (int i = 0; i < 4; i++) dg[s][i] = db[s][i] = 0.0f;
+                for (int i = 0; i < 4; i++) dg[i] = db[i] = 0.0f;
             }
-            s1[t] = 0.0f;
-            s2[t] = 0.0f;
+            s12[t] = 0.0f;
+            s12[NR + t] = 0.0f;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 if (live[t]) {
-                    dg[s][i] = __fadd_rn(dg[s][i], rbf(__fmul_rn(xn[t][i], dz[i])));
-                    db[s][i] = __fadd_rn(db[s][i], dz[i]);
+                    dg[i] = __fadd_rn(dg[i], rbf(__fmul_rn(xn[t][i], dz[i])));
+                    db[i] = __fadd_rn(db[i], dz[i]);
                 }
                 dxn[t][i] = rbf(__fmul_rn(dz[i], g[i]));
-                s1[t] = __fadd_rn(s1[t], dxn[t][i]);
-                s2[t] = __fadd_rn(s2[t], rbf(__fmul_rn(dxn[t][i], xn[t][i])));
+                s12[t] = __fadd_rn(s12[t], dxn[t][i]);
+                s12[NR + t] = __fadd_rn(s12[NR + t], rbf(__fmul_rn(dxn[t][i], xn[t][i])));
             }
-            if ((t >> 1) % J == J - 1) {
-                const int grp = (t >> 1) / J;
-                float* dst = red + ((size_t)grp * 8 + warp + 4 * s) * 2 * E;
-                *reinterpret_cast<float4*>(dst + c0) = make_float4(dg[s][0], dg[s][1], dg[s][2], dg[s][3]);
-                *reinterpret_cast<float4*>(dst + E + c0) = make_float4(db[s][0], db[s][1], db[s][2], db[s][3]);
+            if (t % J == J - 1 && active) {
+                const int pr = warp + 16 * (t / J);  // virtual warp (pr / 8, pr % 8)
+                float* dst = red + (size_t)pr * 2 * E;
+                *reinterpret_cast<float4*>(dst + c0) = make_float4(dg[0], dg[1], dg[2], dg[3]);
+                *reinterpret_cast<float4*>(dst + E + c0) = make_float4(db[0], db[1], db[2], db[3]);
             }
         }
-        warp_sum_n<16>(s12);
+        warp_sum_n<2 * NR>(s12);
 #pragma unroll
-        for (int t = 0; t < 16; t++) s12[t] = __fdiv_rn(s12[t], (float)E);
+        for (int t = 0; t < 2 * NR; t++) s12[t] = __fmul_rn(s12[t], kInvE);
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
+        for (int t = 0; t < NR; t++) {
             if (!live[t]) continue;
             const float4 rs = bf4_load(p.resid + (size_t)rows[t] * E + c0);
             const float r4[4] = {rs.x, rs.y, rs.z, rs.w};
             float o[4];
 #pragma unroll
             for (int i = 0; i < 4; i++)
-                o[i] = __fadd_rn(
-                    rbf(__fmul_rn(rdev[t], __fsub_rn(__fsub_rn(dxn[t][i], s1[t]), __fmul_rn(xn[t][i], s2[t])))),
-                    r4[i]);
+                o[i] = __fadd_rn(rbf(__fmul_rn(rdev[t], __fsub_rn(__fsub_rn(dxn[t][i], s12[t]),
+                                                                   __fmul_rn(xn[t][i], s12[NR + t])))),
+                                 r4[i]);
             bf4_store(p.out + (size_t)rows[t] * E + c0, o[0], o[1], o[2], o[3]);
         }
         __syncthreads();
-        // one partial per group of RPC rows: the virtual warps' sums in order
-#pragma unroll
-        for (int grp = 0; grp < G; grp++) {
+        // one partial per group of RPC rows: its virtual warps' sums in order
+        for (int i = threadIdx.x; i < G * 2 * E; i += blockDim.x) {
+            const int grp = i / (2 * E), c = i % (2 * E);
             const int first = m0 + 32 * (int)q + grp * RPC;
-            if (first >= p.M) break;
-            for (int i = threadIdx.x; i < 2 * E; i += blockDim.x) {
-                float sacc = 0.0f;
+            if (first >= p.M) continue;
+            float sacc = 0.0f;
 #pragma unroll
-                for (int v = 0; v < 8; v++) sacc = __fadd_rn(sacc, red[((size_t)grp * 8 + v) * 2 * E + i]);
-                p.partial[(size_t)(first / RPC) * 2 * E + i] = sacc;
-            }
+            for (int v = 0; v < 8; v++) sacc = __fadd_rn(sacc, red[((size_t)grp * 8 + v) * 2 * E + c]);
+            p.partial[(size_t)(first / RPC) * 2 * E + c] = sacc;
         }
     }
     cluster_sync();  // no CTA leaves while another still reads its partial tile
@@ -357,13 +372,17 @@ int launch_rows(const CUtensorMap& ta, const CUtensorMap& tb, const RowsParams& 
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_done & (1ull << (dev & 63)))) {
-        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmem));
+        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemOnePerSm));
         attr_done |= 1ull << (dev & 63);
     }
+    const int grid = ((p.M + kRowsBM - 1) / kRowsBM) * ks;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(((p.M + kRowsBM - 1) / kRowsBM) * ks));
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = kRowsSmem;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kRowsThreads);
+    // a grid that fits the SMs one CTA each asks for more shared memory than
+    // two CTAs could share, so that every CTA gets an SM of its own (packed
+    // two to an SM, half the SMs would idle: 8.7 against 6.7 us at 4096 rows)
+    cfg.dynamicSmemBytes = grid <= num_sms() ? kRowsSmemOnePerSm : kRowsSmem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;

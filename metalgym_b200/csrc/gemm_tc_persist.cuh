@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(192, 1)
                     }
                     warp_sum_n<8>(mean);
 #pragma unroll
-                    for (int u = 0; u < 8; u++) mean[u] = __fdiv_rn(mean[u], (float)BN);
+                    for (int u = 0; u < 8; u++) mean[u] = __fmul_rn(mean[u], 1.0f / BN);  // exact: BN is a power of two
 #pragma unroll
                     for (int u = 0; u < 8; u++) {
                         sq[u] = 0.0f;
@@ -382,8 +382,8 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                     for (int u = 0; u < 8; u++) {
                         const int rowU = row0 + r0 + u;
-                        const float sd = __fsqrt_rn(__fadd_rn(__fdiv_rn(sq[u], (float)BN), 1e-5f));
-                        const float rstd = __fdiv_rn(1.0f, sd);
+                        const float sd = __fsqrt_rn(__fadd_rn(__fmul_rn(sq[u], 1.0f / BN), 1e-5f));
+                        const float rstd = __frcp_rn(sd);  // = __fdiv_rn(1, sd): both correctly rounded
                         if (lane == 0 && rowU < p.M) p.ln.stdev[rowU] = sd;
                         uint32_t xw[VPT / 2], yw[VPT / 2];
 #pragma unroll
