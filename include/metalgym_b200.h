@@ -114,6 +114,27 @@ int mg_gemm_rows_layernorm_backward(const void* A_dev, int lda, const void* B_de
                                     int K, const void* x_norm, const void* gamma, const float* stdev,
                                     const void* resid, void* resid_out, float* partial, mg_stream_t stream);
 int mg_gemm_rows_splits(int K);
+/* One residual block per kernel for embed 128, hidden 512 (model/mlp.metal:
+ * 18-86 and the skip add, model/elementwise.metal:4-13, then the LayerNorm that
+ * follows, model/layernorm.metal:10-71): v = relu(ln_out w_up) ([rows][512],
+ * saved), h += v w_down in place ([rows][128]), then x_norm, next_ln_out,
+ * stdev of h under gamma, beta. A 4-CTA cluster per 128 rows, CTA q owning
+ * hidden columns 128q..; bit-identical to mg_gemm_bf16 (ReLU) followed by
+ * mg_gemm_rows_resid_layernorm. */
+int mg_block_cluster_forward(const void* ln_out, const void* w_up, const void* w_down, void* h, void* v,
+                             const void* gamma, const void* beta, void* x_norm, void* next_ln_out, float* stdev,
+                             int rows, mg_stream_t stream);
+/* Its backward (model/mlp.metal:88-208, model/layernorm.metal:74-127,
+ * model/ppo.h:851-852): dV = bf16(dS w_down^T) * (v > 0) (saved), then
+ * resid_out and the dgamma / dbeta partials as mg_gemm_rows_layernorm_backward
+ * computes them from dV w_up^T, and the weight-gradient partial sums of each
+ * 128-row tile t: up_part[t] = ln_out_t^T dV_t ([128][512] fp32), down_part[t]
+ * = v_t^T dS_t ([512][128] fp32) — what mg_gemm_bf16 writes as split-K
+ * partials with one split per 128 rows. Bit-identical to those kernels. */
+int mg_block_cluster_backward(const void* dS, const void* w_down, const void* v, const void* w_up, void* dV,
+                              const void* ln_out, float* up_part, float* down_part, const void* x_norm,
+                              const void* gamma, const float* stdev, const void* resid, void* resid_out,
+                              float* partial, int rows, mg_stream_t stream);
 int mg_gemm_bf16_tiled(const void* A_dev, int a_mn_major, int lda, const void* B_dev, int b_mn_major, int ldb,
                        int M, int N, int K, int epilogue, void* out_dev, int ldo, const void* aux_dev, int ldaux,
                        int splits, int tile_n, int persistent, mg_stream_t stream);

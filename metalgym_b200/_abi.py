@@ -26,6 +26,8 @@ SIGNATURES = {
     "mg_gemm_rows_resid_layernorm": (I, [P, I, P, I, I, I, I, P, P, P, P, P, P, P]),
     "mg_gemm_rows_layernorm_backward": (I, [P, I, P, I, I, I, I, P, P, P, P, P, P, P]),
     "mg_gemm_rows_splits": (I, [I]),
+    "mg_block_cluster_forward": (I, [P, P, P, P, P, P, P, P, P, P, I, P]),
+    "mg_block_cluster_backward": (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, P]),
     "mg_gemm_bf16_tiled": (I, [P, I, I, P, I, I, I, I, I, I, P, I, P, I, I, I, I, P]),
     # environments
     "mg_env_register": (I, [P]),

@@ -32,6 +32,7 @@ SOURCES: dict[str, list[str]] = {
     "gemm_rows.cu": [],
     "policy.cu": [],
     "block_fwd.cu": [],
+    "block_cluster.cu": [],
     "envs.cu": [],
     "envs_builtin.cu": ["--fmad=false"],
     "p2p.cu": [],

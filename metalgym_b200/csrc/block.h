@@ -1,4 +1,4 @@
-// Fused residual-block kernels of the policy (block_fwd.cu).
+// Fused residual-block kernels of the policy (block_fwd.cu, block_cluster.cu).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -23,5 +23,22 @@ struct BlockFwdArgs {
 bool block_forward_supported(int E, int H);
 // up: Up [E][H], down: Dp [H][E] (row-major bf16).
 int block_forward(const BlockFwdArgs& a, const void* up, const void* down, cudaStream_t st);
+
+// One residual block per kernel on 4-CTA clusters (block_cluster.cu), embed
+// 128 and hidden 512. Forward: V = relu(lnOut Up) (saved), h += V Dp in place,
+// then the LayerNorm `next` of h. Backward: dV = bf16(dS Dp^T) * (V > 0)
+// (saved), dz = bf16(dV Up^T), residOut = resid + LayerNorm backward of dz
+// (xNorm, gamma, stdev of the block's LayerNorm) with the dgamma / dbeta
+// partials of layernorm_backward. Bit-identical to the separate kernels.
+struct LnOutputs;
+bool block_cluster_supported(int E, int H);
+int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown, void* h, void* v,
+                          const LnOutputs& next, int M, cudaStream_t st);
+// It also writes the weight-gradient partial sums of each 128-row tile t:
+// upPart[t] = lnOut_t^T dV_t ([128][512]), downPart[t] = V_t^T dS_t ([512][128]).
+int block_cluster_backward(const void* dS, const void* wDown, const void* v, const void* wUp, void* dV,
+                           const void* lnOut, float* upPart, float* downPart, const void* xNorm, const void* gamma,
+                           const float* stdev, const void* resid, void* residOut, float* partial, int M,
+                           cudaStream_t st);
 
 }  // namespace mg

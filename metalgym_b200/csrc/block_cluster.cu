@@ -1,0 +1,429 @@
+// One residual block of the CartPole-sized policy (embed 128, hidden 512) per
+// kernel, forward and backward, on clusters of 4 CTAs per 128-row tile:
+//
+// forward (model/mlp.metal:18-86, model/elementwise.metal:4-13, then the
+// LayerNorm that follows, model/layernorm.metal:10-71):
+//   CTA q   V_q = relu(bf16(lnOut W_up[:, 128q : 128q + 128]))   (tcgen05, K = 128)
+//           V_q -> global V (kept for the backward) and, swizzled, into
+//           shared memory as the A operand of
+//           P_q = V_q W_down[128q : 128q + 128, :]                (tcgen05, K = 128)
+//   cluster h = bf16(h + bf16(P_0 + P_1 + P_2 + P_3)), then the next
+//           LayerNorm (rows_epilogue.cuh; CTA q ends rows 32q .. 32q + 31)
+//
+// backward (model/mlp.metal:88-153, model/layernorm.metal:74-127,
+// model/ppo.h:851-852):
+//   CTA q   dV_q = bf16(dS W_down[128q : 128q + 128, :]^T) * (V_q > 0)
+//           dV_q -> global dV and into shared memory
+//           Q_q = dV_q W_up[:, 128q : 128q + 128]^T
+//           the tile's weight-gradient partials (model/mlp.metal:155-208):
+//           dW_up[:, 128q..] += lnOut^T dV_q, dW_down[128q.., :] += V_q^T dS
+//           (sums over the tile's 128 rows, one fp32 partial per row tile;
+//           the gradient finalisation adds the tiles in order)
+//   cluster dz = bf16(Q_0 + .. + Q_3), LayerNorm backward of dz plus the skip
+//           gradient, dgamma / dbeta partials
+//
+// The hidden activation of a block never makes a round trip through another
+// kernel: four launches per block (LayerNorm aside) become one, on 128 CTAs at
+// 4096 rows. Every product is the one the separate kernels compute (the same
+// K order per output element; the down / branch products split K as the row
+// kernels of gemm_rows.cu do), so the outputs are bit-identical to the up or
+// dV GEMM followed by the row kernel. Every wait is bounded; both cluster
+// barriers are reached by every thread on every path.
+#include "block.h"
+#include "gemm.h"
+#include "gemm_tc.cuh"
+#include "policy.h"
+#include "rows_epilogue.cuh"
+#include "runtime.h"
+
+namespace mg {
+
+namespace {
+
+constexpr int kBcHidden = kRowsBN * (int)kRowsCluster;  // 512: CTA q owns hidden columns 128q ..
+constexpr int kBcTile = 128 * 128 * 2;                  // one bf16 operand tile, 32 KB (two 64-wide K blocks)
+// shared memory (offsets from the 1024-aligned base)
+//   forward:  A1 lnOut | B1 W_up slice | B2 W_down slice | A2 V_q      | barriers
+//   backward: A1 dS    | B1 W_down sl. | B2 W_up slice   | M  V_q      | A2 dV_q | LN lnOut | barriers
+// after the second product the fp32 tile (64 KB) reuses A1 + B1, and the
+// LayerNorm-backward column sums (32 KB) reuse M
+constexpr int kBcA1 = 0, kBcB1 = kBcTile, kBcB2 = 2 * kBcTile;
+constexpr int kBcFwdA2 = 3 * kBcTile, kBcFwdBar = 4 * kBcTile;
+constexpr int kBcBwdM = 3 * kBcTile, kBcBwdA2 = 4 * kBcTile, kBcBwdLn = 5 * kBcTile, kBcBwdBar = 6 * kBcTile;
+static_assert(kRowsTile <= 2 * kBcTile && kRowsRedBytes <= kBcTile && kBcBwdM == kBcB2 + kBcTile, "");
+constexpr int kBcFwdSmem = kBcFwdBar + 256 + 1024;
+constexpr int kBcBwdSmem = kBcBwdBar + 256 + 1024;
+
+struct BcParams {
+    int M;
+    __nv_bfloat16* vOut;  // forward: V [M][512]; backward: dV [M][512]
+    float* upPart;        // backward: [tile][128][512] partial sums of dW_up over each 128-row tile
+    float* downPart;      // backward: [tile][512][128] partial sums of dW_down
+    RowsEpi e;
+    int* status;
+};
+
+// SW128 K-major byte offset of the 16-byte chunk c (columns 8c .. 8c + 7, c in
+// 0..15) of row r of a 128 x 128 bf16 tile: two 64-column blocks of 16 KB.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
+    return (uint32_t)((c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// The first product's accumulator (TMEM columns 0..127) through the ReLU
+// (forward) or the V > 0 mask (backward) into the A operand of the second
+// product: warp w converts rows 32 (w % 4) .., columns 32 (w / 4) .. .
+template <bool BWD>
+__device__ __forceinline__ void bc_hidden_tile(uint8_t* smem, int a2Off, uint32_t acc, bool valid) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qd = warp & 3, cc = warp >> 2;
+    const int r = qd * 32 + lane;
+    float v[32];
+    if (valid) {
+        tmem_ld32(acc + ((uint32_t)(qd * 32) << 16) + (uint32_t)(cc * 32), v);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t off = sw128_offset(r, cc * 4 + j);
+        float x[8];
+        if (BWD) {  // kEpiBf16Mask: bf16(acc) * (V > 0)
+            const uint4 m = *reinterpret_cast<const uint4*>(smem + kBcBwdM + off);
+            const uint32_t mw[4] = {m.x, m.y, m.z, m.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float m0 = __uint_as_float(mw[i] << 16), m1 = __uint_as_float(mw[i] & 0xffff0000u);
+                x[2 * i] = round_bf16(v[8 * j + 2 * i]) * (m0 > 0.0f ? 1.0f : 0.0f);
+                x[2 * i + 1] = round_bf16(v[8 * j + 2 * i + 1]) * (m1 > 0.0f ? 1.0f : 0.0f);
+            }
+        } else {  // kEpiBf16Relu: v = bf16(acc); v > 0 ? v : v * 0
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float b = round_bf16(v[8 * j + i]);
+                x[i] = b > 0.0f ? b : b * 0.0f;
+            }
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+            o[i] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(smem + a2Off + off) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// Eight tcgen05.mma (K = 128) of a 128 x 128 product into TMEM.
+template <bool B_MN>
+__device__ __forceinline__ void bc_mma(uint32_t d, uint32_t aBase, uint32_t bBase) {
+    constexpr uint32_t idesc = idesc_bf16_f32(128, false, B_MN);
+#pragma unroll
+    for (int kb = 0; kb < 2; kb++)
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            const uint64_t ad = smem_desc_sw128(aBase + kb * 16384 + kk * 32, 16, 1024);
+            // MN-major B: per 64-row K block two 64-wide N boxes (8 KB apart);
+            // K-major B: one 16 KB box of 128 N rows per 64-wide K block
+            const uint64_t bd = B_MN ? smem_desc_sw128(bBase + kb * 16384 + kk * 2048, 8192, 1024)
+                                     : smem_desc_sw128(bBase + kb * 16384 + kk * 32, 16, 1024);
+            tc_mma_bf16(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        }
+}
+
+// Maps (all SW128, 64-wide boxes):
+//   forward:  a = lnOut [M][128] (box 64 x 128 rows), b1 = W_up [128][512]
+//             (MN-major, box 64 x 64), b2 = W_down [512][128] (MN-major,
+//             box 64 x 64), v = V [M][512] (box 64 x 128, TMA store)
+//   backward: a = dS [M][128], b1 = W_down [512][128] as [N][K] (box 64 x 128
+//             rows), b2 = W_up [128][512] as [N][K] (box 64 x 128 rows),
+//             v = V [M][512] (load: the mask), dv = dV [M][512] (store)
+struct BcMaps {
+    CUtensorMap a, b1, b2, v, dv, ln;
+};
+
+// A 128 x 128 product over the tile's 128 rows (K) with both operands
+// MN-major: A^T B for A [K][M] and B [K][N] tiles as TMA writes them (two
+// 64-wide column blocks of 128 rows, 16 KB apart).
+__device__ __forceinline__ void bc_mma_tn(uint32_t d, uint32_t aBase, uint32_t bBase) {
+    constexpr uint32_t idesc = idesc_bf16_f32(128, true, true);
+#pragma unroll
+    for (int kk = 0; kk < 8; kk++) {
+        const uint64_t ad = smem_desc_sw128(aBase + kk * 2048, 16384, 1024);
+        const uint64_t bd = smem_desc_sw128(bBase + kk * 2048, 16384, 1024);
+        tc_mma_bf16(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+    }
+}
+
+// A 128 x 128 fp32 accumulator to global rows of `ld` floats through the
+// swizzled staging tile `stage` (64 KB of free shared memory): TMEM -> stage
+// (rows_tmem_to_tile), then each warp writes whole 512-byte rows, lane l the
+// 16 bytes of columns 4l..4l+3. Every thread of the CTA takes part.
+__device__ __forceinline__ void bc_tmem_to_global(uint8_t* stage, float* dst, int ld, uint32_t acc, bool valid) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    rows_tmem_to_tile(stage, acc, valid);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int r = warp + 16 * i;
+        *reinterpret_cast<float4*>(dst + (size_t)r * ld + lane * 4) =
+            *reinterpret_cast<const float4*>(stage + tile_offset(r, lane));
+    }
+    __syncthreads();  // the stage may be reused
+}
+
+template <bool BWD, int RPC>
+__global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_constant__ BcMaps tm, const BcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int A2 = BWD ? kBcBwdA2 : kBcFwdA2;
+    constexpr uint32_t kTmemCols = BWD ? 512 : 256;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (BWD ? kBcBwdBar : kBcFwdBar));
+    uint64_t* full1 = bars;      // A1 + B1 (+ the mask)
+    uint64_t* full2 = bars + 1;  // B2
+    uint64_t* mma1 = bars + 2;
+    uint64_t* mma2 = bars + 3;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+
+    mg_pdl_trigger();
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t q = cluster_ctarank();
+    const int m0 = (int)(blockIdx.x / kRowsCluster) * kRowsBM;
+    const int h0 = (int)q * kRowsBN;  // this CTA's hidden columns
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 4; i++) mbar_init(&bars[i], 1);
+        fence_barrier_init();
+        prefetch_tensormap(&tm.a);
+        prefetch_tensormap(&tm.b1);
+        prefetch_tensormap(&tm.b2);
+        prefetch_tensormap(&tm.v);
+        if (BWD) {
+            prefetch_tensormap(&tm.dv);
+            prefetch_tensormap(&tm.ln);
+        }
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, kTmemCols);  // 128-column accumulators: 2 (forward), 4 (backward)
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    mg_pdl_wait();  // activations and weights come from earlier kernels
+
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(full1, 2 * kBcTile + (BWD ? kBcTile : 0));
+        for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcA1 + kb * 16384, &tm.a, 64 * kb, m0, full1);
+        if (!BWD) {
+            // W_up[k][h0 + n]: K rows 64 kb.., N boxes h0 + 64 j
+            for (int kb = 0; kb < 2; kb++)
+                for (int j = 0; j < 2; j++)
+                    tma_load_2d(smem + kBcB1 + kb * 16384 + j * 8192, &tm.b1, h0 + 64 * j, 64 * kb, full1);
+        } else {
+            // W_down rows h0 .. h0 + 127 as [N][K = 128]; the mask V[m0.., h0..]
+            for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcB1 + kb * 16384, &tm.b1, 64 * kb, h0, full1);
+            for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcBwdM + kb * 16384, &tm.v, h0 + 64 * kb, m0, full1);
+        }
+        mbar_arrive_expect_tx(full2, kBcTile * (BWD ? 2 : 1));
+        if (BWD)  // the block's LayerNorm output, for dW_up
+            for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcBwdLn + kb * 16384, &tm.ln, 64 * kb, m0, full2);
+        if (!BWD) {
+            // W_down[h0 + k][n]: K rows h0 + 64 kb.., N boxes 64 j
+            for (int kb = 0; kb < 2; kb++)
+                for (int j = 0; j < 2; j++)
+                    tma_load_2d(smem + kBcB2 + kb * 16384 + j * 8192, &tm.b2, 64 * j, h0 + 64 * kb, full2);
+        } else {
+            // W_up as [N = 128][K = 512], K columns h0 + 64 kb ..
+            for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcB2 + kb * 16384, &tm.b2, h0 + 64 * kb, 0, full2);
+        }
+    } else if (warp == 1 && lane == 0) {
+        if (mbar_wait(full1, 0, p.status, kDevTimeoutFull)) {
+            tc_fence_after();
+            bc_mma<!BWD>(tmem, smem_u32(smem + kBcA1), smem_u32(smem + kBcB1));
+            tc_commit(mma1);
+            // dW_down partial = V_q^T dS (TMEM columns 384..511), covered by mma2's commit
+            if (BWD) bc_mma_tn(tmem + 384, smem_u32(smem + kBcBwdM), smem_u32(smem + kBcA1));
+        } else {
+            tc_commit(mma1);  // always: covers whatever was issued
+        }
+    }
+
+    // ---- the hidden tile: ReLU (forward) or mask (backward) into A2
+    __syncwarp();
+    bool ok = mbar_wait_warp(mma1, 0, p.status, kDevTimeoutDone);
+    // the mask tile arrived with full1: observe that phase before reading it
+    if (BWD && ok) ok = mbar_wait_warp(full1, 0, p.status, kDevTimeoutFull);
+    tc_fence_after();
+    bc_hidden_tile<BWD>(smem, A2, tmem, ok);
+    fence_async_smem();  // generic writes of A2 -> visible to the tensor core and TMA
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+        // V_q / dV_q to global memory (the backward reads V, the weight gradient reads dV)
+        for (int kb = 0; kb < 2; kb++)
+            if (m0 < p.M) tma_store_2d(BWD ? &tm.dv : &tm.v, h0 + 64 * kb, m0, smem + A2 + kb * 16384);
+        bulk_commit();
+    } else if (warp == 1 && lane == 0) {
+        if (mbar_wait(full2, 0, p.status, kDevTimeoutFull)) {
+            tc_fence_after();
+            bc_mma<!BWD ? true : false>(tmem + 128, smem_u32(smem + A2), smem_u32(smem + kBcB2));
+            // dW_up partial = lnOut^T dV_q (TMEM columns 256..383)
+            if (BWD) bc_mma_tn(tmem + 256, smem_u32(smem + kBcBwdLn), smem_u32(smem + A2));
+        }
+        tc_commit(mma2);
+    }
+
+    // ---- the second product's partial tile into shared memory (reusing A1 + B1)
+    __syncwarp();
+    const bool ok2 = mbar_wait_warp(mma2, 0, p.status, kDevTimeoutDone);
+    tc_fence_after();
+    rows_tmem_to_tile(smem, tmem + 128, ok && ok2);
+    if (BWD) {
+        // this tile's weight-gradient partial sums: dW_up[:, h0..], dW_down[h0.., :]
+        const size_t t = (size_t)(m0 / kRowsBM);
+        // (staged in B2 + M: both free once the products completed; M holds
+        // the LayerNorm-backward column sums only after the cluster barrier)
+        uint8_t* stage = smem + kBcB2;
+        bc_tmem_to_global(stage, p.upPart + t * kRowsBN * kBcHidden + h0, kBcHidden, tmem + 256, ok && ok2);
+        bc_tmem_to_global(stage, p.downPart + t * kBcHidden * kRowsBN + (size_t)h0 * kRowsBN, kRowsBN, tmem + 384,
+                          ok && ok2);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        if (!(ok && ok2)) {  // no MMA may run on freed TMEM
+            mbar_wait(mma1, 0, p.status, kDevTimeoutDone);
+            mbar_wait(mma2, 0, p.status, kDevTimeoutDone);
+        }
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+    if (!ok) {
+        // a product that timed out may leave its TMA loads in flight: let them land
+        if (threadIdx.x == 0) {
+            mbar_wait(full1, 0, p.status, kDevTimeoutFull);
+            mbar_wait(full2, 0, p.status, kDevTimeoutFull);
+        }
+    }
+    cluster_sync();  // every partial tile of the cluster is complete
+
+    rows_cluster_epilogue<BWD ? kRowsLNBackward : kRowsResidLN, RPC>(
+        smem, reinterpret_cast<float*>(smem + kBcBwdM), q, m0, p.e);
+
+    if (threadIdx.x == 0) bulk_wait<0>();  // the V / dV store is complete
+    cluster_sync();  // no CTA leaves while another still reads its partial tile
+}
+
+template <bool BWD, int RPC>
+int launch_bc(const BcMaps& tm, const BcParams& p, cudaStream_t st) {
+    auto kern = k_block_cluster<BWD, RPC>;
+    constexpr int smemBytes = BWD ? kBcBwdSmem : kBcFwdSmem;
+    static uint64_t attr_done = 0;  // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done & (1ull << (dev & 63)))) {
+        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smemBytes));
+        attr_done |= 1ull << (dev & 63);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(((p.M + kRowsBM - 1) / kRowsBM) * kRowsCluster));
+    cfg.blockDim = dim3(kRowsThreads);
+    cfg.dynamicSmemBytes = smemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kRowsCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tm, p));
+    return check_launch("k_block_cluster");
+}
+
+}  // namespace
+
+bool block_cluster_supported(int E, int H) { return E == kRowsBN && H == kBcHidden; }
+
+int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown, void* h, void* v, const LnOutputs& next,
+                          int M, cudaStream_t st) {
+    MG_CHECK_ARG(lnOut && wUp && wDown && h && v && next.gamma && next.beta && next.xNorm && next.out && next.stdev,
+                 "block_cluster_forward: null argument");
+    MG_CHECK_ARG(M > 0, "block_cluster_forward: M must be > 0");
+    BcMaps tm{};
+    int rc = make_tmap_bf16(&tm.a, lnOut, kRowsBN, M, kRowsBN, 128);
+    if (!rc) rc = make_tmap_bf16(&tm.b1, wUp, kBcHidden, kRowsBN, kBcHidden, 64);
+    if (!rc) rc = make_tmap_bf16(&tm.b2, wDown, kRowsBN, kBcHidden, kRowsBN, 64);
+    if (!rc) rc = make_tmap_bf16(&tm.v, v, kBcHidden, M, kBcHidden, 128);
+    if (rc) return rc;
+    BcParams p{};
+    p.M = M;
+    p.vOut = static_cast<__nv_bfloat16*>(v);
+    p.e.M = M;
+    p.e.resid = static_cast<const __nv_bfloat16*>(h);
+    p.e.out = static_cast<__nv_bfloat16*>(h);
+    p.e.ln = next;
+    p.status = status_ptr();
+    return launch_bc<false, 32>(tm, p, st);
+}
+
+int block_cluster_backward(const void* dS, const void* wDown, const void* v, const void* wUp, void* dV,
+                           const void* lnOut, float* upPart, float* downPart, const void* xNorm, const void* gamma,
+                           const float* stdev, const void* resid, void* residOut, float* partial, int M,
+                           cudaStream_t st) {
+    MG_CHECK_ARG(dS && wDown && v && wUp && dV && lnOut && upPart && downPart && xNorm && gamma && stdev &&
+                     residOut && partial,
+                 "block_cluster_backward: null argument");
+    MG_CHECK_ARG(M > 0 && gemm_rows_ln_backward_supported(M),
+                 "block_cluster_backward: the LayerNorm backward partial groups at this row count do not divide 32 rows");
+    BcMaps tm{};
+    int rc = make_tmap_bf16(&tm.a, dS, kRowsBN, M, kRowsBN, 128);
+    if (!rc) rc = make_tmap_bf16(&tm.b1, wDown, kRowsBN, kBcHidden, kRowsBN, 128);
+    if (!rc) rc = make_tmap_bf16(&tm.b2, wUp, kBcHidden, kRowsBN, kBcHidden, 128);
+    if (!rc) rc = make_tmap_bf16(&tm.v, v, kBcHidden, M, kBcHidden, 128);
+    if (!rc) rc = make_tmap_bf16(&tm.dv, dV, kBcHidden, M, kBcHidden, 128);
+    if (!rc) rc = make_tmap_bf16(&tm.ln, lnOut, kRowsBN, M, kRowsBN, 128);
+    if (rc) return rc;
+    BcParams p{};
+    p.M = M;
+    p.vOut = static_cast<__nv_bfloat16*>(dV);
+    p.upPart = upPart;
+    p.downPart = downPart;
+    p.e.M = M;
+    p.e.resid = static_cast<const __nv_bfloat16*>(resid);
+    p.e.out = static_cast<__nv_bfloat16*>(residOut);
+    p.e.gamma = static_cast<const __nv_bfloat16*>(gamma);
+    p.e.xNorm = static_cast<const __nv_bfloat16*>(xNorm);
+    p.e.stdev = stdev;
+    p.e.partial = partial;
+    p.status = status_ptr();
+    switch (layernorm_rows_per_part(M)) {
+        case 8: return launch_bc<true, 8>(tm, p, st);
+        case 16: return launch_bc<true, 16>(tm, p, st);
+        default: return launch_bc<true, 32>(tm, p, st);
+    }
+}
+
+}  // namespace mg
+
+extern "C" int mg_block_cluster_forward(const void* ln_out, const void* w_up, const void* w_down, void* h, void* v,
+                                        const void* gamma, const void* beta, void* x_norm, void* next_ln_out,
+                                        float* stdev, int rows, mg_stream_t stream) {
+    const mg::LnOutputs ln{static_cast<const __nv_bfloat16*>(gamma), static_cast<const __nv_bfloat16*>(beta),
+                           static_cast<__nv_bfloat16*>(x_norm), static_cast<__nv_bfloat16*>(next_ln_out), stdev};
+    return mg::block_cluster_forward(ln_out, w_up, w_down, h, v, ln, rows, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mg_block_cluster_backward(const void* dS, const void* w_down, const void* v, const void* w_up, void* dV,
+                                         const void* ln_out, float* up_part, float* down_part, const void* x_norm,
+                                         const void* gamma, const float* stdev, const void* resid, void* resid_out,
+                                         float* partial, int rows, mg_stream_t stream) {
+    return mg::block_cluster_backward(dS, w_down, v, w_up, dV, ln_out, up_part, down_part, x_norm, gamma, stdev,
+                                      resid, resid_out, partial, rows, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -278,6 +278,7 @@ int PpoEngine::init() {
     fusedBlocks = block_forward_supported(E, H);
     lnEpilogue = E == 128 || E == 256;
     rowsKernels = gemm_rows_supported(E, H);
+    clusterBlocks = block_cluster_supported(E, H);
 
     // ---- parameters: model/ppo.h:375-445 (seeded normal init rounded to bf16)
     std::vector<std::vector<uint16_t>> init;
@@ -419,6 +420,10 @@ int PpoEngine::allocTrain(int rows) {
     MG_CUDA_TRY(cudaMemset(stats, 0, (size_t)rows * 5 * 4));
     upSplits = splits_for(E, H, rows, H >= 128 ? 128 : 64);
     downSplits = splits_for(H, E, rows, E >= 128 ? 128 : 64);
+    if (useBlockClusterBackward(rows)) {
+        // the block kernels write one weight-gradient partial per 128-row tile
+        upSplits = downSplits = (rows + 127) / 128;
+    }
     headSplits = splits_for(E, kHead, rows, 64);
     upPart.assign(L, nullptr);
     downPart.assign(L, nullptr);
@@ -556,9 +561,10 @@ BlockFwdArgs PpoEngine::blockArgs(ActSet& a, int n, int rows) {
 int PpoEngine::blocksForward(ActSet& a, int rows, cudaStream_t st) {
     auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
     auto bw = [&](uint32_t p) { return reinterpret_cast<const __nv_bfloat16*>(weights + params[p].offset); };
-    const bool rowsK = useRowsForward(rows);
-    const bool fused = !rowsK && useFusedBlock(rows);
-    const bool lnEpi = !fused && (rowsK || useLnEpilogue(rows));
+    const bool cluster = useBlockClusterForward(rows);
+    const bool rowsK = !cluster && useRowsForward(rows);
+    const bool fused = !cluster && !rowsK && useFusedBlock(rows);
+    const bool lnEpi = !fused && (cluster || rowsK || useLnEpilogue(rows));
     for (int n = 0; n < L; n++) {
         if (fused) {
             MG_TRY(block_forward(blockArgs(a, n, rows), w(pUp[n]), w(pDown[n]), st));
@@ -566,6 +572,16 @@ int PpoEngine::blocksForward(ActSet& a, int rows, cudaStream_t st) {
         }
         if (n == 0 || !lnEpi)
             MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
+        if (cluster) {
+            // up (ReLU), down (+ skip) and the next LayerNorm in one kernel
+            const LnOutputs next =
+                n + 1 < L ? LnOutputs{bw(pLnG[n + 1]), bw(pLnB[n + 1]), static_cast<__nv_bfloat16*>(a.lnXn[n + 1]),
+                                      static_cast<__nv_bfloat16*>(a.lnOut[n + 1]), a.lnSd[n + 1]}
+                          : LnOutputs{bw(pLnFg), bw(pLnFb), static_cast<__nv_bfloat16*>(a.fXn),
+                                      static_cast<__nv_bfloat16*>(a.fOut), a.fSd};
+            MG_TRY(block_cluster_forward(a.lnOut[n], w(pUp[n]), w(pDown[n]), a.h, a.v[n], next, rows, st));
+            continue;
+        }
         GemmCall up;
         up.A = a.lnOut[n]; up.lda = E;
         up.B = w(pUp[n]); up.b_mn = true; up.ldb = H;
@@ -682,14 +698,24 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         MG_TRY(gemm_bf16(dx, st));
     }
     MG_TRY(layernorm_backward(dS[L], a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, rows, E, st));
+    const bool clusterBwd = useBlockClusterBackward(rows);
     for (int n = L - 1; n >= 0; n--) {
-        GemmCall g1;  // dV = bf16(dS Dp^T) * (V > 0) (model/mlp.metal:88-127)
-        g1.A = dS[n + 1]; g1.lda = E;
-        g1.B = w(pDown[n]); g1.ldb = E;  // Dp [H][E] = [N][K]
-        g1.M = rows; g1.N = H; g1.K = E;
-        g1.epilogue = 3; g1.aux = a.v[n]; g1.ldaux = H;
-        g1.out = dVs[n]; g1.ldo = H;
-        MG_TRY(gemm_bf16(g1, st));
+        if (clusterBwd) {
+            // dV, dBranch, the LayerNorm backward with the skip add and both
+            // weight-gradient partials in one kernel
+            MG_TRY(block_cluster_backward(dS[n + 1], w(pDown[n]), a.v[n], w(pUp[n]), dVs[n], a.lnOut[n], upPart[n],
+                                          downPart[n], a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1], dS[n], lnPart[n],
+                                          rows, st));
+            continue;
+        } else {
+            GemmCall g1;  // dV = bf16(dS Dp^T) * (V > 0) (model/mlp.metal:88-127)
+            g1.A = dS[n + 1]; g1.lda = E;
+            g1.B = w(pDown[n]); g1.ldb = E;  // Dp [H][E] = [N][K]
+            g1.M = rows; g1.N = H; g1.K = E;
+            g1.epilogue = 3; g1.aux = a.v[n]; g1.ldaux = H;
+            g1.out = dVs[n]; g1.ldo = H;
+            MG_TRY(gemm_bf16(g1, st));
+        }
         MG_TRY(fork(n));
         GemmCall g2;  // dUp = X^T dV (model/mlp.metal:167-208)
         g2.A = a.lnOut[n]; g2.a_mn = true; g2.lda = E;

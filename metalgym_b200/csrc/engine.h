@@ -12,6 +12,7 @@
 
 #include "../../include/metalgym_b200.h"
 #include "block.h"
+#include "gemm.h"
 #include "p2p.h"
 #include "policy.h"
 
@@ -196,6 +197,18 @@ class PpoEngine {
     bool useRowsBackward(int rows) const { return rowsKernels && rows <= kRowsBackwardMaxRows; }
     static constexpr int kRowsForwardMaxRows = 4096;
     static constexpr int kRowsBackwardMaxRows = 8192;
+    // a whole residual block per kernel on 4-CTA clusters (block_cluster.cu),
+    // embed 128 and hidden 512; where it applies it replaces the row kernels,
+    // the up / dV GEMMs before them and (backward) the two weight-gradient
+    // GEMMs of the side stream. In CUDA graphs at 4096 rows: 8.3 against 11.0
+    // us forward; at 8192 rows no faster than the kernels it replaces
+    bool clusterBlocks = false;
+    bool useBlockClusterForward(int rows) const { return clusterBlocks && rows <= kClusterForwardMaxRows; }
+    bool useBlockClusterBackward(int rows) const {
+        return clusterBlocks && rows <= kClusterBackwardMaxRows && gemm_rows_ln_backward_supported(rows);
+    }
+    static constexpr int kClusterForwardMaxRows = 4096;
+    static constexpr int kClusterBackwardMaxRows = 4096;
 
     // multi-GPU: NCCL all-reduce (setComm) or the all-reduce over NVLink peer
     // memory (p2p.cu: p2pHandle on every rank, exchange, p2pOpen)
