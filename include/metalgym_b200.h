@@ -131,6 +131,21 @@ int mg_block_cluster_forward(const void* ln_out, const void* w_up, const void* w
  * 128-row tile t: up_part[t] = ln_out_t^T dV_t ([128][512] fp32), down_part[t]
  * = v_t^T dS_t ([512][128] fp32) — what mg_gemm_bf16 writes as split-K
  * partials with one split per 128 rows. Bit-identical to those kernels. */
+/* The head of a training minibatch in one kernel (embed 128, categorical
+ * head): head = bf16(f_out w_head) (linearForward, model/linear.metal:17-37),
+ * the PPO loss of every row (policyLossBackward, model/policy.metal:14-69:
+ * dZ, stats, as mg_policy_loss), dS = the final LayerNorm's backward
+ * (model/layernorm.metal:74-127) of bf16(dZ w_head^T) (linearBackward,
+ * model/linear.metal:40-60) with its dgamma / dbeta partials as
+ * mg_layernorm_backward writes them, and head_part[t] = f_out_t^T dZ_t
+ * ([128][64] fp32) for every 128-row tile t (linearBackwardDw,
+ * model/linear.metal:71-93, one split per tile). Bit-identical to those
+ * kernels. Rows per LayerNorm partial (8, 16 or 32) must divide 32. */
+int mg_head_tail(const void* f_out, const void* w_head, void* head, const int32_t* action, const float* adv,
+                 const float* adv_stats, const float* ret, const float* old_log_prob, void* dZ, float* stats, int rows,
+                 int act_dim, float clip, float value_coef, float entropy_coef, float* head_part,
+                 const void* gamma_f, const void* x_norm_f, const float* stdev_f, void* dS, float* ln_partial,
+                 mg_stream_t stream);
 int mg_block_cluster_backward(const void* dS, const void* w_down, const void* v, const void* w_up, void* dV,
                               const void* ln_out, float* up_part, float* down_part, const void* x_norm,
                               const void* gamma, const float* stdev, const void* resid, void* resid_out,

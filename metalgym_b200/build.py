@@ -33,6 +33,7 @@ SOURCES: dict[str, list[str]] = {
     "policy.cu": [],
     "block_fwd.cu": [],
     "block_cluster.cu": [],
+    "head_tail.cu": [],
     "envs.cu": [],
     "envs_builtin.cu": ["--fmad=false"],
     "p2p.cu": [],

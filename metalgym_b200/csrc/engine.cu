@@ -231,14 +231,17 @@ int gym_create(const char* name, int n, uint32_t seed, uint32_t firstEnvId, int 
 // ------------------------------------------------------------------ engine
 
 PpoEngine::PpoEngine(GymCore* g, int embed, int scale, int layers, float learningRate, int horizon, uint32_t s)
-    : gym(g), R(g->n), O((int)g->ops->obs_dim), A((int)g->ops->act_dim), E(embed), H(embed * scale), L(layers),
-      T(horizon), cont(g->ops->continuous != 0), actBytes(g->ops->action_bytes), lr(learningRate), seed(s) {}
+    : gym(g), device(g->device), R(g->n), O((int)g->ops->obs_dim), A((int)g->ops->act_dim), E(embed),
+      H(embed * scale), L(layers), T(horizon), cont(g->ops->continuous != 0), actBytes(g->ops->action_bytes),
+      lr(learningRate), seed(s) {}
 
+// Touches nothing of the gym, which may already be gone (a garbage collector
+// can finalise a borrowed gym before the model that borrowed it).
 PpoEngine::~PpoEngine() {
     int cur = 0;
     cudaGetDevice(&cur);
-    cudaSetDevice(gym->device);
-    cudaStreamSynchronize(gym->stream);
+    cudaSetDevice(device);
+    cudaDeviceSynchronize();
     if (collectExec) cudaGraphExecDestroy(collectExec);
     if (trainExec) cudaGraphExecDestroy(trainExec);
     freeTrain();
@@ -425,6 +428,7 @@ int PpoEngine::allocTrain(int rows) {
         upSplits = downSplits = (rows + 127) / 128;
     }
     headSplits = splits_for(E, kHead, rows, 64);
+    if (!cont && useHeadTail(rows)) headSplits = (rows + 127) / 128;  // one dW_head partial per 128-row tile
     upPart.assign(L, nullptr);
     downPart.assign(L, nullptr);
     lnPart.assign(L, nullptr);
@@ -651,7 +655,14 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         MG_TRY(advantage_stats_rows(advSlots, rm, rows, mbAdvStats, advPartial, advCounter, st));
         as = mbAdvStats;
     }
-    {
+    // the whole head of the minibatch in one kernel (head_tail.cu): head GEMM,
+    // loss, head dX, final LayerNorm backward and the dW_head tile partials
+    const bool headTail = !cont && useHeadTail(rows);
+    if (headTail) {
+        const PolicyLossRows pl = policy_loss_rows(static_cast<const int32_t*>(actionSlots), advSlots, as, retSlots,
+                                                   logpSlots, dLogits, stats, rows, A, lh, rm);
+        MG_TRY(head_tail(a.fOut, w(pHead), a.head, pl, headPart, w(pLnFg), a.fXn, a.fSd, dS[L], lnFPart, rows, st));
+    } else {
         GemmCall hd;
         hd.A = a.fOut; hd.lda = E;
         hd.B = w(pHead); hd.b_mn = true; hd.ldb = kHead;
@@ -676,13 +687,15 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     // each weight-gradient GEMM is forked to the side stream as soon as its
     // operands exist (they are never overwritten within the minibatch) and
     // the side stream is joined before the gradient finalisation.
+    bool forked = false;  // the side stream joins the capture only through a fork
     auto fork = [&](int k) -> int {
         MG_CUDA_TRY(cudaEventRecord(forkEv[k], st));
         MG_CUDA_TRY(cudaStreamWaitEvent(side, forkEv[k], 0));
+        forked = true;
         return MG_OK;
     };
-    MG_TRY(fork(L));
-    {
+    if (!headTail) {
+        MG_TRY(fork(L));
         GemmCall dw;  // dW_head = X_F^T dLogits (model/linear.metal:71-93)
         dw.A = a.fOut; dw.a_mn = true; dw.lda = E;
         dw.B = dLogits; dw.b_mn = true; dw.ldb = kHead;
@@ -696,8 +709,8 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         dx.M = rows; dx.N = E; dx.K = kHead;
         dx.out = dS[L]; dx.ldo = E;
         MG_TRY(gemm_bf16(dx, st));
+        MG_TRY(layernorm_backward(dS[L], a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, rows, E, st));
     }
-    MG_TRY(layernorm_backward(dS[L], a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, rows, E, st));
     const bool clusterBwd = useBlockClusterBackward(rows);
     for (int n = L - 1; n >= 0; n--) {
         if (clusterBwd) {
@@ -748,8 +761,10 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
                                   dS[n]));
     }
     MG_TRY(input_backward(obsSlots, dS[0], inPart, rows, O, E, st, rm));
-    MG_CUDA_TRY(cudaEventRecord(joinEv, side));
-    MG_CUDA_TRY(cudaStreamWaitEvent(st, joinEv, 0));
+    if (forked) {
+        MG_CUDA_TRY(cudaEventRecord(joinEv, side));
+        MG_CUDA_TRY(cudaStreamWaitEvent(st, joinEv, 0));
+    }
     // gradient sums + norm (model/ppo.h:873-890), [all-reduce], Adam (:891-903)
     if (p2pOn) {
         // sums into this minibatch's exchange buffer, then the all-reduce over

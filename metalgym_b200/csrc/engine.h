@@ -101,6 +101,7 @@ class PpoEngine {
     int load(const char* path);
 
     GymCore* gym;
+    int device;  // the gym's device, kept for the destructor
     int R, O, A, E, H, L, T;
     bool cont;
     size_t actBytes;
@@ -207,6 +208,10 @@ class PpoEngine {
     bool useBlockClusterBackward(int rows) const {
         return clusterBlocks && rows <= kClusterBackwardMaxRows && gemm_rows_ln_backward_supported(rows);
     }
+    // the head GEMM, loss, head dX, final LayerNorm backward and dW_head
+    // partials in one kernel (head_tail.cu), categorical head, embed 128
+    bool useHeadTail(int rows) const { return E == 128 && rows <= kHeadTailMaxRows && head_tail_supported(E, rows); }
+    static constexpr int kHeadTailMaxRows = 4096;
     static constexpr int kClusterForwardMaxRows = 4096;
     static constexpr int kClusterBackwardMaxRows = 4096;
 

@@ -50,6 +50,15 @@ bool gemm_rows_ln_backward_supported(int M);
 // h = bf16(h + bf16(A B)) in place, then the LayerNorm of h into ln
 int gemm_rows_resid_layernorm(const void* A, int lda, const void* B, bool b_mn, int ldb, int M, int K, void* h,
                               const LnOutputs& ln, cudaStream_t st);
+// The head of the training minibatch in one kernel (head_tail.cu), embed 128,
+// categorical: head = bf16(fOut wHead), the PPO loss (dZ, statistics), dS =
+// LayerNorm-F backward of bf16(dZ wHead^T) and the dW_head partial of each
+// 128-row tile (headPart [tile][128][64]); bit-identical to the separate
+// kernels.
+bool head_tail_supported(int E, int M);
+int head_tail(const void* fOut, const void* wHead, void* head, const PolicyLossRows& loss, float* headPart,
+              const void* gammaF, const void* xNormF, const float* stdevF, void* dS, float* lnPart, int M,
+              cudaStream_t st);
 // dz = bf16(A B); residOut = resid + LayerNorm backward of dz; dgamma / dbeta
 // partials exactly as layernorm_backward writes them
 int gemm_rows_layernorm_backward(const void* A, int lda, const void* B, bool b_mn, int ldb, int M, int K,

@@ -45,9 +45,11 @@ struct PolicyLossRows {
 __device__ __forceinline__ float loss_bf(__nv_bfloat16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ __nv_bfloat16 loss_tobf(float x) { return __float2bfloat16_rn(x); }
 
-// Row r of the minibatch, its head row h (64 bf16). Returns false (and
-// records kDevBadAction) for an action outside [0, actDim).
-__device__ inline bool policy_loss_row(const PolicyLossRows& L, int r, const __nv_bfloat16* h, int* status) {
+// Row r of the minibatch, its head row h (64 bf16): the row's dZ (64 bf16,
+// packed in pairs) and its 5 statistics. Returns false (and records
+// kDevBadAction) for an action outside [0, actDim).
+__device__ inline bool policy_loss_compute(const PolicyLossRows& L, int r, const __nv_bfloat16* h, int* status,
+                                           uint32_t* packed, float* st) {
     const int64_t g = L.mb ? (int64_t)mg_minibatch_row(*L.mb, r, L.envRows, L.total) : r;
     const float* advStats = L.advStats;
     if (L.mb && L.mb->slot >= 0 && advStats) advStats += 2 * L.mb->slot;  // per-slot statistics
@@ -87,7 +89,6 @@ __device__ inline bool policy_loss_row(const PolicyLossRows& L, int r, const __n
     const float surr2 = __fmul_rn(fminf(fmaxf(ratio, __fsub_rn(1.0f, L.clip)), __fadd_rn(1.0f, L.clip)), A);
     const float policyLoss = -fminf(surr1, surr2);
     const float gLogp = (surr1 <= surr2) ? __fmul_rn(-A, ratio) : 0.0f;
-    uint32_t packed[kLossHeadDim / 2];
 #pragma unroll
     for (int i = 0; i < kLossHeadDim / 2; i++) packed[i] = 0;
     __nv_bfloat16* pz = reinterpret_cast<__nv_bfloat16*>(packed);
@@ -107,16 +108,26 @@ __device__ inline bool policy_loss_row(const PolicyLossRows& L, int r, const __n
     }
     const float vErr = __fsub_rn(loss_bf(h[actDim]), L.ret[g]);
     pz[actDim] = loss_tobf(__fmul_rn(__fmul_rn(L.valueCoef, vErr), scale));
-    uint4* dst = reinterpret_cast<uint4*>(L.dZ + (size_t)r * kLossHeadDim);
-    const uint4* src = reinterpret_cast<const uint4*>(packed);
-#pragma unroll
-    for (int i = 0; i < kLossHeadDim / 8; i++) dst[i] = src[i];
-    float* st = L.stats + (size_t)r * 5;
     st[0] = policyLoss;
     st[1] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, L.valueCoef), vErr), vErr);
     st[2] = entropy;
     st[3] = __fsub_rn(L.oldLogProb[g], logpA);
     st[4] = (fabsf(__fsub_rn(ratio, 1.0f)) > L.clip) ? 1.0f : 0.0f;
+    return true;
+}
+
+// The loss of row r written to L.dZ and L.stats.
+__device__ inline bool policy_loss_row(const PolicyLossRows& L, int r, const __nv_bfloat16* h, int* status) {
+    uint32_t packed[kLossHeadDim / 2];
+    float st[5];
+    if (!policy_loss_compute(L, r, h, status, packed, st)) return false;
+    uint4* dst = reinterpret_cast<uint4*>(L.dZ + (size_t)r * kLossHeadDim);
+    const uint4* src = reinterpret_cast<const uint4*>(packed);
+#pragma unroll
+    for (int i = 0; i < kLossHeadDim / 8; i++) dst[i] = src[i];
+    float* so = L.stats + (size_t)r * 5;
+#pragma unroll
+    for (int i = 0; i < 5; i++) so[i] = st[i];
     return true;
 }
 

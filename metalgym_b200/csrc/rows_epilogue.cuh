@@ -81,7 +81,8 @@ __device__ __forceinline__ void rows_tmem_to_tile(uint8_t* tile, uint32_t acc, b
 // rows of the tile (tile rows of the cluster at the same offset `smem` in
 // every CTA), the sum of the 4 tiles in CTA order, then the epilogue. `red`:
 // kRowsRedBytes of this CTA's shared memory, unused by the tiles.
-template <int EPI, int RPC>
+// NSUM = 1: the tile is this CTA's own and complete (no cluster).
+template <int EPI, int RPC, int NSUM = (int)kRowsCluster>
 __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red, uint32_t q, int m0,
                                                       const RowsEpi& e) {
     constexpr int E = kRowsBN;
@@ -118,7 +119,9 @@ __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red,
         live[t] = active && rows[t] < e.M;
         const uint8_t* cell = smem + tile_offset(tr & 127, lane);
         float4 a = make_float4(0, 0, 0, 0);
-        if (active) {
+        if (active && NSUM == 1) {
+            a = *reinterpret_cast<const float4*>(cell);
+        } else if (active) {
             a = *reinterpret_cast<const float4*>(__cluster_map_shared_rank(cell, 0));
 #pragma unroll
             for (uint32_t r = 1; r < kRowsCluster; r++) {

@@ -6,6 +6,7 @@ with device buffers read back as numpy arrays.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -36,6 +37,9 @@ class Gym:
 
     def close(self):
         if self._h:
+            # a model borrows its gym (model/ppo.h:145-147): close the models first
+            for m in list(getattr(self, "_models", ())):
+                m.close()
             lib().mg_gym_destroy(self._h)
             self._h = C.c_void_p()
 
@@ -97,6 +101,9 @@ class PPOModel:
     def __init__(self, gym: Gym, embed: int, scale: int, layers: int, lr: float, horizon: int = 32, seed: int = 0):
         self.gym = gym
         self._h = C.c_void_p()
+        if not hasattr(gym, "_models"):
+            gym._models = weakref.WeakSet()
+        gym._models.add(self)
         check(lib().mg_ppo_create(gym.handle, embed, scale, layers, lr, horizon, seed, C.byref(self._h)),
               "mg_ppo_create")
         info = (C.c_uint64 * 12)()
