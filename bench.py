@@ -367,71 +367,78 @@ def _time_launches(launch, torch, stream, iters=200):
 
 def dominant_kernel_roofline(lib, torch, dev, stream):
     """The kernel with the largest share of the loop's GPU time in the ncu
-    launch list of one CartPole iteration (profiles/launches_c3_full_loop.md):
-    the split-K weight-gradient GEMM gemm_tc_kernel<64, MN-major A, MN-major B,
-    fp32 partials>, 5 launches per minibatch. Timed here on its largest shape,
-    dUp = lnOut^T dV (embed x hidden x rows = 128 x 512 x 4096, 16 K-splits),
-    alone and back to back on the engine's stream with CUDA events.
+    launch list of one CartPole minibatch (profiles/launches_c3_minibatch.md):
+    the residual-block backward on 4-CTA clusters, k_block_cluster<backward>,
+    two launches per minibatch. Timed here at the minibatch's shape (4096 rows,
+    embed 128, hidden 512) alone and back to back on the engine's stream with
+    CUDA events.
 
-    Its algorithmic traffic is the two operands (4096 x 128 + 4096 x 512 bf16)
-    and the reduced gradient (128 x 512 fp32); its FLOPs are 2 x 128 x 512 x
-    4096. At the measured peaks the bytes take longer than the FLOPs, so the
-    bound is HBM. The DRAM traffic per launch comes from the committed ncu
-    capture of the same launch (profiles/gemm_wgrad_128x512x4096_split16.md);
-    the fp32 split partials stay in L2 there."""
-    M, N, K, splits = EMBED, EMBED * SCALE, ENVS_PER_GPU, 16
-    a = torch.randn(K, M, device=f"cuda:{dev}").bfloat16()   # lnOut, rows x embed
-    b = torch.randn(K, N, device=f"cuda:{dev}").bfloat16()   # dV, rows x hidden
-    o = torch.empty(splits, M, N, device=f"cuda:{dev}", dtype=torch.float32)
+    Per launch it computes four 4096 x 128 x 512 products (dV, the branch
+    gradient, and the two weight-gradient partials: 2.15 GFLOP) and moves
+    dS, V, the LayerNorm output and x-hat in, dV, the new dS, the LayerNorm
+    partials and 32 tiles of fp32 weight-gradient partials out (28.5 MB): at
+    the measured peaks the bytes take longer than the FLOPs, so the roof is
+    HBM. The DRAM traffic per launch comes from the committed ncu capture of
+    the same launch (profiles/block_cluster_backward_4096x128x512.md)."""
+    R, E, H = ENVS_PER_GPU, EMBED, EMBED * SCALE
+    d = f"cuda:{dev}"
+    tiles = (R + 127) // 128
+    dS1 = torch.randn(R, E, device=d).bfloat16()
+    dS0 = torch.empty_like(dS1)
+    v = torch.relu(torch.randn(R, H, device=d)).bfloat16()
+    dv = torch.empty_like(v)
+    ln_out = torch.randn(R, E, device=d).bfloat16()
+    xn = torch.randn(R, E, device=d).bfloat16()
+    g = torch.ones(E, device=d).bfloat16()
+    bt = torch.zeros(E, device=d).bfloat16()
+    sd = 0.5 + torch.rand(R, device=d)
+    up = (torch.randn(E, H, device=d) / E ** 0.5).bfloat16()
+    dn = (torch.randn(H, E, device=d) / H ** 0.5).bfloat16()
+    upp = torch.empty(tiles, E, H, device=d)
+    dnp = torch.empty(tiles, H, E, device=d)
+    part = torch.empty(lib.mg_layernorm_backward_num_partials(R), 2 * E, device=d)
+    h = torch.randn(R, E, device=d).bfloat16()
+    y = torch.empty_like(h)
     sp = ctypes.c_void_p(stream.cuda_stream)
 
-    def launch():
-        return lib.mg_gemm_bf16(a.data_ptr(), 1, M, b.data_ptr(), 1, N, M, N, K, 4, o.data_ptr(), N, None, 0,
-                                splits, sp)
+    def launch_bwd():
+        return lib.mg_block_cluster_backward(dS1.data_ptr(), dn.data_ptr(), v.data_ptr(), up.data_ptr(),
+                                             dv.data_ptr(), ln_out.data_ptr(), upp.data_ptr(), dnp.data_ptr(),
+                                             xn.data_ptr(), g.data_ptr(), sd.data_ptr(), dS1.data_ptr(),
+                                             dS0.data_ptr(), part.data_ptr(), R, sp)
 
-    us = _time_launches(launch, torch, stream)
-    flops = 2.0 * M * N * K
-    alg_bytes = (K * M + K * N) * 2 + M * N * 4
+    us = _time_launches(launch_bwd, torch, stream)
+    flops = 4 * 2.0 * R * E * H
+    alg_bytes = (R * E * 2 * 4 + R * H * 2 * 2 + 2 * E * H * 2 + R * 4 + part.numel() * 4
+                 + 2 * tiles * E * H * 4)
     hbm, tflops, kind = measured_peaks()
     t_mem, t_flop = alg_bytes / (hbm * 1e9), flops / (tflops * 1e12)
     achieved = alg_bytes / (us * 1e-6) / 1e9
-    roof = {"kernel": "gemm_tc_kernel<64, MN-major A, MN-major B, fp32 split-K partials> "
-                      "(weight gradient dUp, 128x512x4096, 16 splits)",
+    roof = {"kernel": "k_block_cluster<backward> (residual-block backward on 4-CTA clusters: dV, branch gradient, "
+                      "LayerNorm backward + skip, weight-gradient tile partials; 4096 rows, 128 x 512)",
             "bound": "hbm" if t_mem >= t_flop else "tensor", "achieved": achieved, "peak": hbm, "unit": "GB/s",
             "frac": achieved / hbm, "peak_kind": f"{kind} HBM copy", "us_per_launch": us,
             "algorithmic_bytes_per_launch": alg_bytes, "flop_per_launch": flops,
             "tensor_frac": flops / (us * 1e-6) / 1e12 / tflops,
-            "traffic": profile_traffic("gemm_wgrad_128x512x4096_split16.md")}
+            "traffic": profile_traffic("block_cluster_backward_4096x128x512.md")}
 
-    # the longest kernel on the critical path of a minibatch: the down-projection
-    # with the residual add and the next LayerNorm, K split over a cluster of
-    # 4 CTAs (rows x embed x hidden = 4096 x 128 x 512)
-    Md, Nd, Kd = ENVS_PER_GPU, EMBED, EMBED * SCALE
-    va = torch.relu(torch.randn(Md, Kd, device=f"cuda:{dev}")).bfloat16()
-    vb = (torch.randn(Kd, Nd, device=f"cuda:{dev}") / 16).bfloat16()
-    vh = torch.randn(Md, Nd, device=f"cuda:{dev}").bfloat16()
-    vg = torch.ones(Nd, device=f"cuda:{dev}").bfloat16()
-    vbt = torch.zeros(Nd, device=f"cuda:{dev}").bfloat16()
-    vxn = torch.empty_like(vh)
-    vy = torch.empty_like(vh)
-    vsd = torch.empty(Md, device=f"cuda:{dev}")
+    # the forward of a residual block on 4-CTA clusters (up, ReLU, down, skip,
+    # the next LayerNorm), two launches per minibatch and per collect step
+    def launch_fwd():
+        return lib.mg_block_cluster_forward(ln_out.data_ptr(), up.data_ptr(), dn.data_ptr(), h.data_ptr(),
+                                            v.data_ptr(), g.data_ptr(), bt.data_ptr(), xn.data_ptr(), y.data_ptr(),
+                                            sd.data_ptr(), R, sp)
 
-    def launch_down():
-        return lib.mg_gemm_rows_resid_layernorm(va.data_ptr(), Kd, vb.data_ptr(), 1, Nd, Md, Kd, vh.data_ptr(),
-                                                vg.data_ptr(), vbt.data_ptr(), vxn.data_ptr(), vy.data_ptr(),
-                                                vsd.data_ptr(), sp)
-
-    usd = _time_launches(launch_down, torch, stream)
-    fd = 2.0 * Md * Nd * Kd
-    # bytes: V and Dp read, h read and written, x-hat, LayerNorm out, sigma written
-    bd = (Md * Kd + Kd * Nd + 4 * Md * Nd) * 2 + Md * 4
+    usf = _time_launches(launch_fwd, torch, stream)
+    ff = 2 * 2.0 * R * E * H
+    bf = R * E * 2 * 5 + R * H * 2 + 2 * E * H * 2 + R * 4
     roof["critical_path_kernel"] = {
-        "kernel": "k_gemm_rows<MN-major B, residual + LayerNorm> (down-projection + next LayerNorm, "
-                  "4096x128x512, K split over a 4-CTA cluster)",
-        "bound": "latency (neither roof)", "achieved": fd / (usd * 1e-6) / 1e12, "peak": tflops, "unit": "TFLOP/s",
-        "frac": fd / (usd * 1e-6) / 1e12 / tflops, "hbm_frac": bd / (usd * 1e-6) / 1e9 / hbm,
-        "us_per_launch": usd, "flop_per_launch": fd, "algorithmic_bytes_per_launch": bd,
-        "traffic": profile_traffic("gemm_rows_down_layernorm_4096x128x512.md")}
+        "kernel": "k_block_cluster<forward> (residual block on 4-CTA clusters + next LayerNorm, 4096 x 128 x 512)",
+        "bound": "hbm" if bf / (hbm * 1e9) >= ff / (tflops * 1e12) else "tensor",
+        "achieved": bf / (usf * 1e-6) / 1e9, "peak": hbm, "unit": "GB/s",
+        "frac": bf / (usf * 1e-6) / 1e9 / hbm, "tensor_frac": ff / (usf * 1e-6) / 1e12 / tflops,
+        "us_per_launch": usf, "flop_per_launch": ff, "algorithmic_bytes_per_launch": bf,
+        "traffic": profile_traffic("block_cluster_forward_4096x128x512.md")}
     return roof
 
 
