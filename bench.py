@@ -405,7 +405,7 @@ def dominant_kernel_roofline(lib, torch, dev, stream):
         return lib.mg_block_cluster_backward(dS1.data_ptr(), dn.data_ptr(), v.data_ptr(), up.data_ptr(),
                                              dv.data_ptr(), ln_out.data_ptr(), upp.data_ptr(), dnp.data_ptr(),
                                              xn.data_ptr(), g.data_ptr(), sd.data_ptr(), dS1.data_ptr(),
-                                             dS0.data_ptr(), part.data_ptr(), R, sp)
+                                             dS0.data_ptr(), part.data_ptr(), None, 0, None, R, sp)
 
     us = _time_launches(launch_bwd, torch, stream)
     flops = 4 * 2.0 * R * E * H

@@ -130,7 +130,11 @@ int mg_block_cluster_forward(const void* ln_out, const void* w_up, const void* w
  * computes them from dV w_up^T, and the weight-gradient partial sums of each
  * 128-row tile t: up_part[t] = ln_out_t^T dV_t ([128][512] fp32), down_part[t]
  * = v_t^T dS_t ([512][128] fp32) — what mg_gemm_bf16 writes as split-K
- * partials with one split per 128 rows. Bit-identical to those kernels. */
+ * partials with one split per 128 rows. Bit-identical to those kernels. With
+ * obs (the first block: resid_out is then the input layer's dZ), also the
+ * input layer's gradient partials (inputBackward, model/input.metal:38-60)
+ * as mg_input_backward_partials writes them when it takes 16 rows per
+ * partial (in_dim <= 32). */
 /* The head of a training minibatch in one kernel (embed 128, categorical
  * head): head = bf16(f_out w_head) (linearForward, model/linear.metal:17-37),
  * the PPO loss of every row (policyLossBackward, model/policy.metal:14-69:
@@ -149,7 +153,8 @@ int mg_head_tail(const void* f_out, const void* w_head, void* head, const int32_
 int mg_block_cluster_backward(const void* dS, const void* w_down, const void* v, const void* w_up, void* dV,
                               const void* ln_out, float* up_part, float* down_part, const void* x_norm,
                               const void* gamma, const float* stdev, const void* resid, void* resid_out,
-                              float* partial, int rows, mg_stream_t stream);
+                              float* partial, const float* obs, int in_dim, float* in_partial, int rows,
+                              mg_stream_t stream);
 int mg_gemm_bf16_tiled(const void* A_dev, int a_mn_major, int lda, const void* B_dev, int b_mn_major, int ldb,
                        int M, int N, int K, int epilogue, void* out_dev, int ldo, const void* aux_dev, int ldaux,
                        int splits, int tile_n, int persistent, mg_stream_t stream);

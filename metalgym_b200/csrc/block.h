@@ -3,6 +3,9 @@
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "metalgym/rowmap.h"
 
 namespace mg {
 
@@ -36,9 +39,20 @@ int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown,
                           const LnOutputs& next, int M, cudaStream_t st);
 // It also writes the weight-gradient partial sums of each 128-row tile t:
 // upPart[t] = lnOut_t^T dV_t ([128][512]), downPart[t] = V_t^T dS_t ([512][128]).
+// With `in` (the first block), the rows written are the input layer's dZ,
+// and the kernel also writes its gradient partials as input_backward does at
+// 16 rows per partial (the caller checks that input_backward partitions so).
+constexpr int kBlockClusterMaxInputDim = 32;
+struct BlockClusterInput {
+    const float* obs;          // observations [*][inDim] fp32
+    const MgMinibatch* mb;     // minibatch row map (null: row r reads observation r)
+    uint64_t envRows, total;
+    int inDim;                 // <= kBlockClusterMaxInputDim
+    float* partial;            // [rows / 16][(inDim + 1) x 128]
+};
 int block_cluster_backward(const void* dS, const void* wDown, const void* v, const void* wUp, void* dV,
                            const void* lnOut, float* upPart, float* downPart, const void* xNorm, const void* gamma,
                            const float* stdev, const void* resid, void* residOut, float* partial, int M,
-                           cudaStream_t st);
+                           cudaStream_t st, const BlockClusterInput* in = nullptr);
 
 }  // namespace mg

@@ -51,6 +51,8 @@ constexpr int kBcA1 = 0, kBcB1 = kBcTile, kBcB2 = 2 * kBcTile;
 constexpr int kBcFwdA2 = 3 * kBcTile, kBcFwdBar = 4 * kBcTile;
 constexpr int kBcBwdM = 3 * kBcTile, kBcBwdA2 = 4 * kBcTile, kBcBwdLn = 5 * kBcTile, kBcBwdBar = 6 * kBcTile;
 static_assert(kRowsTile <= 2 * kBcTile && kRowsRedBytes <= kBcTile && kBcBwdM == kBcB2 + kBcTile, "");
+static_assert((32 * kRowsBN + 32 * kRowsInputMaxDim) * 4 <= kBcTile, "the input-gradient staging fits the lnOut tile");
+static_assert(kBlockClusterMaxInputDim == kRowsInputMaxDim, "");
 constexpr int kBcFwdSmem = kBcFwdBar + 256 + 1024;
 constexpr int kBcBwdSmem = kBcBwdBar + 256 + 1024;
 
@@ -311,8 +313,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_
     }
     cluster_sync();  // every partial tile of the cluster is complete
 
-    rows_cluster_epilogue<BWD ? kRowsLNBackward : kRowsResidLN, RPC>(
-        smem, reinterpret_cast<float*>(smem + kBcBwdM), q, m0, p.e);
+    RowsEpi e = p.e;
+    if (BWD) e.inStage = reinterpret_cast<float*>(smem + kBcBwdLn);  // the lnOut tile is no longer needed
+    rows_cluster_epilogue<BWD ? kRowsLNBackward : kRowsResidLN, RPC>(smem, reinterpret_cast<float*>(smem + kBcBwdM),
+                                                                    q, m0, e);
 
     if (threadIdx.x == 0) bulk_wait<0>();  // the V / dV store is complete
     cluster_sync();  // no CTA leaves while another still reads its partial tile
@@ -376,7 +380,7 @@ int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown,
 int block_cluster_backward(const void* dS, const void* wDown, const void* v, const void* wUp, void* dV,
                            const void* lnOut, float* upPart, float* downPart, const void* xNorm, const void* gamma,
                            const float* stdev, const void* resid, void* residOut, float* partial, int M,
-                           cudaStream_t st) {
+                           cudaStream_t st, const BlockClusterInput* in) {
     MG_CHECK_ARG(dS && wDown && v && wUp && dV && lnOut && upPart && downPart && xNorm && gamma && stdev &&
                      residOut && partial,
                  "block_cluster_backward: null argument");
@@ -402,6 +406,16 @@ int block_cluster_backward(const void* dS, const void* wDown, const void* v, con
     p.e.xNorm = static_cast<const __nv_bfloat16*>(xNorm);
     p.e.stdev = stdev;
     p.e.partial = partial;
+    if (in) {
+        MG_CHECK_ARG(in->obs && in->partial && in->inDim > 0 && in->inDim <= kRowsInputMaxDim,
+                     "block_cluster_backward: bad input-layer arguments");
+        p.e.inObs = in->obs;
+        p.e.inMb = in->mb;
+        p.e.inEnvRows = in->envRows;
+        p.e.inTotal = in->total;
+        p.e.inDim = in->inDim;
+        p.e.inPartial = in->partial;
+    }
     p.status = status_ptr();
     switch (layernorm_rows_per_part(M)) {
         case 8: return launch_bc<true, 8>(tm, p, st);
@@ -423,7 +437,10 @@ extern "C" int mg_block_cluster_forward(const void* ln_out, const void* w_up, co
 extern "C" int mg_block_cluster_backward(const void* dS, const void* w_down, const void* v, const void* w_up, void* dV,
                                          const void* ln_out, float* up_part, float* down_part, const void* x_norm,
                                          const void* gamma, const float* stdev, const void* resid, void* resid_out,
-                                         float* partial, int rows, mg_stream_t stream) {
+                                         float* partial, const float* obs, int in_dim, float* in_partial, int rows,
+                                         mg_stream_t stream) {
+    const mg::BlockClusterInput in{obs, nullptr, 0, 0, in_dim, in_partial};
     return mg::block_cluster_backward(dS, w_down, v, w_up, dV, ln_out, up_part, down_part, x_norm, gamma, stdev,
-                                      resid, resid_out, partial, rows, reinterpret_cast<cudaStream_t>(stream));
+                                      resid, resid_out, partial, rows, reinterpret_cast<cudaStream_t>(stream),
+                                      obs ? &in : nullptr);
 }

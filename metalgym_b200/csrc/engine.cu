@@ -712,13 +712,17 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         MG_TRY(layernorm_backward(dS[L], a.fXn, w(pLnFg), a.fSd, nullptr, lnFPart, rows, E, st));
     }
     const bool clusterBwd = useBlockClusterBackward(rows);
+    // the first block's kernel also sums the input layer's gradient partials
+    // (the same 16-row partials input_backward writes at these row counts)
+    const bool inputFused = clusterBwd && inputGradFusable(rows);
     for (int n = L - 1; n >= 0; n--) {
         if (clusterBwd) {
             // dV, dBranch, the LayerNorm backward with the skip add and both
             // weight-gradient partials in one kernel
+            const BlockClusterInput in{obsSlots, rm.mb, rm.envRows, rm.total, O, inPart};
             MG_TRY(block_cluster_backward(dS[n + 1], w(pDown[n]), a.v[n], w(pUp[n]), dVs[n], a.lnOut[n], upPart[n],
                                           downPart[n], a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1], dS[n], lnPart[n],
-                                          rows, st));
+                                          rows, st, n == 0 && inputFused ? &in : nullptr));
             continue;
         } else {
             GemmCall g1;  // dV = bf16(dS Dp^T) * (V > 0) (model/mlp.metal:88-127)
@@ -760,7 +764,7 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         MG_TRY(layernorm_backward(dBranch, a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1], lnPart[n], rows, E, st,
                                   dS[n]));
     }
-    MG_TRY(input_backward(obsSlots, dS[0], inPart, rows, O, E, st, rm));
+    if (!inputFused) MG_TRY(input_backward(obsSlots, dS[0], inPart, rows, O, E, st, rm));
     if (forked) {
         MG_CUDA_TRY(cudaEventRecord(joinEv, side));
         MG_CUDA_TRY(cudaStreamWaitEvent(st, joinEv, 0));

@@ -212,6 +212,9 @@ class PpoEngine {
     // partials in one kernel (head_tail.cu), categorical head, embed 128
     bool useHeadTail(int rows) const { return E == 128 && rows <= kHeadTailMaxRows && head_tail_supported(E, rows); }
     static constexpr int kHeadTailMaxRows = 4096;
+    bool inputGradFusable(int rows) const {
+        return O <= kBlockClusterMaxInputDim && input_backward_parts(rows, O, E) == (rows + 15) / 16;
+    }
     static constexpr int kClusterForwardMaxRows = 4096;
     static constexpr int kClusterBackwardMaxRows = 4096;
 

@@ -39,7 +39,20 @@ struct RowsEpi {
     const __nv_bfloat16* xNorm;
     const float* stdev;
     float* partial;  // [M / RPC][dgamma (128) | dbeta (128)]
+    // kRowsLNBackward, optional (inPartial set): the input layer's gradient
+    // partials of the output rows (the rows are then the input layer's dZ), as
+    // k_input_backward computes them with 16 rows per partial:
+    // inPartial[row / 16][(inDim + 1) x 128], dW rows then db. Row r of the
+    // minibatch reads observation mg_minibatch_row(*inMb, r, ..) (row r
+    // without inMb). inStage: 32 x 128 + 32 x inDim floats of shared memory.
+    const float* inObs;
+    const MgMinibatch* inMb;
+    uint64_t inEnvRows, inTotal;
+    int inDim;
+    float* inPartial;
+    float* inStage;
 };
+constexpr int kRowsInputMaxDim = 32;
 
 // Byte offset of the 16-byte column chunk k (columns 4k..4k+3) of tile row r in
 // an fp32 tile: rows of 512 bytes, chunks XOR-swizzled by the row, so a warp
@@ -235,8 +248,50 @@ __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red,
                 o[3] = __fadd_rn(rbf(o[3]), rs.w);
             }
             bf4_store(e.out + (size_t)rows[t] * E + c0, o[0], o[1], o[2], o[3]);
+            if (e.inPartial)  // the stored (bf16) values, for the input layer's gradient
+                *reinterpret_cast<float4*>(e.inStage + (rows[t] - m0 - 32 * (int)q) * E + c0) =
+                    make_float4(rbf(o[0]), rbf(o[1]), rbf(o[2]), rbf(o[3]));
+        }
+        if (e.inPartial) {
+            float* sObs = e.inStage + 32 * E;
+            for (int i = threadIdx.x; i < 32 * e.inDim; i += blockDim.x) {
+                const int row = m0 + 32 * (int)q + i / e.inDim;
+                if (row >= e.M) continue;
+                const uint64_t g = e.inMb ? mg_minibatch_row(*e.inMb, row, e.inEnvRows, e.inTotal) : (uint64_t)row;
+                sObs[i] = e.inObs[g * e.inDim + i % e.inDim];
+            }
         }
         __syncthreads();
+        if (e.inPartial) {
+            // k_input_backward's sums over each 16 rows, in row order
+            const float* sObs = e.inStage + 32 * E;
+            for (int i = threadIdx.x; i < 2 * E; i += blockDim.x) {
+                const int half = i / E, c = i % E;
+                const int first = m0 + 32 * (int)q + 16 * half;
+                if (first >= e.M) continue;
+                const int nr = min(16, e.M - first);
+                const float* d = e.inStage + (16 * half) * E + c;
+                const float* ob = sObs + (16 * half) * e.inDim;
+                float* part = e.inPartial + (size_t)(first / 16) * (e.inDim + 1) * E;
+                float accB = 0.0f;
+                for (int r = 0; r < nr; r++) accB = __fadd_rn(accB, d[r * E]);
+                part[(size_t)e.inDim * E + c] = accB;
+                for (int k0 = 0; k0 < e.inDim; k0 += 8) {
+                    float acc[8];
+#pragma unroll
+                    for (int k = 0; k < 8; k++) acc[k] = 0.0f;
+                    for (int r = 0; r < nr; r++) {
+                        const float dv = d[r * E];
+#pragma unroll
+                        for (int k = 0; k < 8; k++)
+                            if (k0 + k < e.inDim) acc[k] = __fmaf_rn(ob[r * e.inDim + k0 + k], dv, acc[k]);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        if (k0 + k < e.inDim) part[(size_t)(k0 + k) * E + c] = acc[k];
+                }
+            }
+        }
         // one partial per group of RPC rows: its virtual warps' sums in order
         for (int i = threadIdx.x; i < G * 2 * E; i += blockDim.x) {
             const int grp = i / (2 * E), c = i % (2 * E);

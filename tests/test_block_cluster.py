@@ -91,6 +91,17 @@ def test_block_cluster_backward_bit_exact(mg, rows):
     dn_ref = torch.empty(tiles, H, E, device="cuda")
     assert mg.mg_gemm_bf16(v.data_ptr(), 1, H, dS1.data_ptr(), 1, E, H, E, rows, 4, dn_ref.data_ptr(), E,
                            None, 0, tiles, None) == 0, mg.mg_last_error()
+    # the input layer's gradient partials of the output rows (first block), where
+    # the separate kernel also takes 16 rows per partial
+    O = 4
+    obs = torch.randn(rows, O, device="cuda", generator=gen)
+    fuse_input = mg.mg_input_backward_num_partials(rows, O, E) == (rows + 15) // 16
+    in_ref = in_part = None
+    if fuse_input:
+        in_ref = torch.empty((rows + 15) // 16, O + 1, E, device="cuda")
+        assert mg.mg_input_backward_partials(obs.data_ptr(), out_ref.data_ptr(), in_ref.data_ptr(), rows, O, E,
+                                             None) == 0, mg.mg_last_error()
+        in_part = torch.full_like(in_ref, float("nan"))
     # one kernel
     dv = torch.full_like(dv_ref, float("nan"))
     out = torch.full_like(dS1, float("nan"))
@@ -100,8 +111,11 @@ def test_block_cluster_backward_bit_exact(mg, rows):
     rc = mg.mg_block_cluster_backward(dS1.data_ptr(), dn.data_ptr(), v.data_ptr(), up.data_ptr(), dv.data_ptr(),
                                       ln_out.data_ptr(), up_part.data_ptr(), dn_part.data_ptr(), xn.data_ptr(),
                                       g.data_ptr(), sd.data_ptr(), dS1.data_ptr(), out.data_ptr(), part.data_ptr(),
-                                      rows, None)
+                                      obs.data_ptr() if fuse_input else None, O,
+                                      in_part.data_ptr() if fuse_input else None, rows, None)
     assert rc == 0, mg.mg_last_error()
     status_ok(mg)
     for got, ref in ((dv, dv_ref), (out, out_ref), (part, part_ref), (up_part, up_ref), (dn_part, dn_ref)):
         assert torch.equal(bits(got), bits(ref))
+    if fuse_input:
+        assert torch.equal(in_part, in_ref)
