@@ -124,6 +124,17 @@ int mg_gemm_rows_splits(int K);
 int mg_block_cluster_forward(const void* ln_out, const void* w_up, const void* w_down, void* h, void* v,
                              const void* gamma, const void* beta, void* x_norm, void* next_ln_out, float* stdev,
                              int rows, mg_stream_t stream);
+/* The first block's forward with the input layer and the first LayerNorm in
+ * the same kernel (inputForward, model/input.metal:11-27; layernormForward,
+ * model/layernorm.metal:10-71): h = bf16(b_in + obs w_in) ([rows][128], obs
+ * [rows][in_dim] fp32, in_dim <= 32), then x_norm0, ln_out0, stdev0 of h,
+ * then mg_block_cluster_forward on ln_out0. Bit-identical to
+ * mg_input_forward, mg_layernorm_forward and mg_block_cluster_forward. */
+int mg_block_cluster_forward_input(const float* obs, int in_dim, const void* w_in, const void* b_in,
+                                   const void* gamma0, const void* beta0, void* x_norm0, void* ln_out0,
+                                   float* stdev0, const void* w_up, const void* w_down, void* h, void* v,
+                                   const void* gamma, const void* beta, void* x_norm, void* next_ln_out,
+                                   float* stdev, int rows, mg_stream_t stream);
 /* Its backward (model/mlp.metal:88-208, model/layernorm.metal:74-127,
  * model/ppo.h:851-852): dV = bf16(dS w_down^T) * (v > 0) (saved), then
  * resid_out and the dgamma / dbeta partials as mg_gemm_rows_layernorm_backward

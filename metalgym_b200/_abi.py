@@ -27,6 +27,7 @@ SIGNATURES = {
     "mg_gemm_rows_layernorm_backward": (I, [P, I, P, I, I, I, I, P, P, P, P, P, P, P]),
     "mg_gemm_rows_splits": (I, [I]),
     "mg_head_tail": (I, [P, P, P, P, P, P, P, P, P, P, I, I, F, F, F, P, P, P, P, P, P, P]),
+    "mg_block_cluster_forward_input": (I, [P, I] + [P] * 16 + [I, P]),
     "mg_block_cluster_forward": (I, [P, P, P, P, P, P, P, P, P, P, I, P]),
     "mg_block_cluster_backward": (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I, P, I, P]),
     "mg_gemm_bf16_tiled": (I, [P, I, I, P, I, I, I, I, I, I, P, I, P, I, I, I, I, P]),

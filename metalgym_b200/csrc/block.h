@@ -34,15 +34,32 @@ int block_forward(const BlockFwdArgs& a, const void* up, const void* down, cudaS
 // (xNorm, gamma, stdev of the block's LayerNorm) with the dgamma / dbeta
 // partials of layernorm_backward. Bit-identical to the separate kernels.
 struct LnOutputs;
+constexpr int kBlockClusterMaxInputDim = 32;
 bool block_cluster_supported(int E, int H);
+// With `in` (the first block), the kernel first computes the input layer
+// (h = b + obs W, written to h) and the first LayerNorm (x-hat, sigma; its
+// output written to lnOut) itself, exactly as input_forward and
+// layernorm_forward do; lnOut is then an output.
+struct BlockClusterForwardInput {
+    const float* obs;       // [*][inDim] fp32
+    const MgMinibatch* mb;  // row map (null: row r reads observation r)
+    uint64_t envRows, total;
+    int inDim;              // <= kBlockClusterMaxInputDim
+    const void* w;          // [inDim][128] bf16
+    const void* b;          // [128] bf16
+    const void* gamma;      // the first LayerNorm
+    const void* beta;
+    void* xNorm;
+    float* stdev;
+};
 int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown, void* h, void* v,
-                          const LnOutputs& next, int M, cudaStream_t st);
+                          const LnOutputs& next, int M, cudaStream_t st,
+                          const BlockClusterForwardInput* in = nullptr);
 // It also writes the weight-gradient partial sums of each 128-row tile t:
 // upPart[t] = lnOut_t^T dV_t ([128][512]), downPart[t] = V_t^T dS_t ([512][128]).
 // With `in` (the first block), the rows written are the input layer's dZ,
 // and the kernel also writes its gradient partials as input_backward does at
 // 16 rows per partial (the caller checks that input_backward partitions so).
-constexpr int kBlockClusterMaxInputDim = 32;
 struct BlockClusterInput {
     const float* obs;          // observations [*][inDim] fp32
     const MgMinibatch* mb;     // minibatch row map (null: row r reads observation r)

@@ -53,11 +53,28 @@ constexpr int kBcBwdM = 3 * kBcTile, kBcBwdA2 = 4 * kBcTile, kBcBwdLn = 5 * kBcT
 static_assert(kRowsTile <= 2 * kBcTile && kRowsRedBytes <= kBcTile && kBcBwdM == kBcB2 + kBcTile, "");
 static_assert((32 * kRowsBN + 32 * kRowsInputMaxDim) * 4 <= kBcTile, "the input-gradient staging fits the lnOut tile");
 static_assert(kBlockClusterMaxInputDim == kRowsInputMaxDim, "");
+static_assert((kRowsInputMaxDim * kRowsBN + 32 * kRowsInputMaxDim) * 4 <= kBcTile, "the input staging fits A2");
 constexpr int kBcFwdSmem = kBcFwdBar + 256 + 1024;
 constexpr int kBcBwdSmem = kBcBwdBar + 256 + 1024;
 
+// The input layer and the first LayerNorm computed in the first block's
+// forward kernel (model/input.metal:11-27, model/layernorm.metal:10-71): h =
+// bf16(b + sum_k obs[k] W[k][:]) in k_input_forward's order, then its LayerNorm
+// (ln: x-hat, out, sigma), whose output is the block's A operand.
+struct BcInput {
+    const float* obs;       // [*][inDim] fp32
+    const MgMinibatch* mb;  // row map (null: row r reads observation r)
+    uint64_t envRows, total;
+    int inDim;              // <= kRowsInputMaxDim
+    const __nv_bfloat16* w;  // [inDim][128]
+    const __nv_bfloat16* b;  // [128]
+    __nv_bfloat16* h;        // [M][128]
+    LnOutputs ln;
+};
+
 struct BcParams {
     int M;
+    BcInput in;
     __nv_bfloat16* vOut;  // forward: V [M][512]; backward: dV [M][512]
     float* upPart;        // backward: [tile][128][512] partial sums of dW_up over each 128-row tile
     float* downPart;      // backward: [tile][512][128] partial sums of dW_down
@@ -174,7 +191,103 @@ __device__ __forceinline__ void bc_tmem_to_global(uint8_t* stage, float* dst, in
     __syncthreads();  // the stage may be reused
 }
 
-template <bool BWD, int RPC>
+// The input layer and the first LayerNorm of this CTA's 32 rows (two per
+// warp, lane l: columns 4l..4l+3), their LayerNorm output written into the A
+// tile of every CTA of the cluster. `stage`: free shared memory for the input
+// weights (fp32) and the rows' observations.
+__device__ __forceinline__ void bc_input_prologue(uint8_t* smem, float* stage, uint32_t q, int m0, int M,
+                                                  const BcInput& in) {
+    constexpr int E = kRowsBN;
+    constexpr float kInvE = 1.0f / E;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = lane * 4;
+    float* sW = stage;                    // [inDim][128]
+    float* sObs = stage + in.inDim * E;   // [32][inDim]
+    for (int i = threadIdx.x; i < in.inDim * E; i += blockDim.x) sW[i] = __bfloat162float(in.w[i]);
+    for (int i = threadIdx.x; i < 32 * in.inDim; i += blockDim.x) {
+        const int row = m0 + 32 * (int)q + i / in.inDim;
+        float o = 0.0f;
+        if (row < M) {
+            const uint64_t g = in.mb ? mg_minibatch_row(*in.mb, row, in.envRows, in.total) : (uint64_t)row;
+            o = in.obs[g * in.inDim + i % in.inDim];
+        }
+        sObs[i] = o;
+    }
+    __syncthreads();
+    const float4 bias = bf4_load(in.b + c0);
+    const float4 gm = bf4_load(in.ln.gamma + c0), bt = bf4_load(in.ln.beta + c0);
+    const float g[4] = {gm.x, gm.y, gm.z, gm.w}, bb[4] = {bt.x, bt.y, bt.z, bt.w};
+    float v[2][4], ms[4];
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const int tl = warp + 16 * t;
+        const float* ob = sObs + tl * in.inDim;
+        float acc[4] = {bias.x, bias.y, bias.z, bias.w};
+        for (int k = 0; k < in.inDim; k++) {
+            const float o = ob[k];
+            const float4 wk = *reinterpret_cast<const float4*>(sW + k * E + c0);
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(o, wk.x));
+            acc[1] = __fadd_rn(acc[1], __fmul_rn(o, wk.y));
+            acc[2] = __fadd_rn(acc[2], __fmul_rn(o, wk.z));
+            acc[3] = __fadd_rn(acc[3], __fmul_rn(o, wk.w));
+        }
+        float sm = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            v[t][i] = round_bf16(acc[i]);
+            sm = __fadd_rn(sm, v[t][i]);
+        }
+        ms[t] = sm;
+        const int row = m0 + 32 * (int)q + tl;
+        if (row < M) bf4_store(in.h + (size_t)row * E + c0, v[t][0], v[t][1], v[t][2], v[t][3]);
+    }
+    warp_sum_n<2>(ms);
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        ms[t] = __fmul_rn(ms[t], kInvE);
+        float sq = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float d = __fsub_rn(v[t][i], ms[t]);
+            sq = __fadd_rn(sq, __fmul_rn(d, d));
+        }
+        ms[2 + t] = sq;
+    }
+    warp_sum_n<2>(ms + 2);
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const int tl = warp + 16 * t;
+        const int r = 32 * (int)q + tl;  // row of the tile
+        const int row = m0 + r;
+        const float sd = __fsqrt_rn(__fadd_rn(__fmul_rn(ms[2 + t], kInvE), 1e-5f));
+        const float rstd = __frcp_rn(sd);
+        float xn[4], y[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            xn[i] = __fmul_rn(__fsub_rn(v[t][i], ms[t]), rstd);
+            y[i] = __fadd_rn(__fmul_rn(g[i], xn[i]), bb[i]);
+        }
+        __nv_bfloat162 y01 = __floats2bfloat162_rn(y[0], y[1]), y23 = __floats2bfloat162_rn(y[2], y[3]);
+        uint2 yw = make_uint2(*reinterpret_cast<uint32_t*>(&y01), *reinterpret_cast<uint32_t*>(&y23));
+        if (row < M) {
+            if (lane == 0) in.ln.stdev[row] = sd;
+            bf4_store(in.ln.xNorm + (size_t)row * E + c0, xn[0], xn[1], xn[2], xn[3]);
+            *reinterpret_cast<uint2*>(in.ln.out + (size_t)row * E + c0) = yw;
+        } else {
+            yw = make_uint2(0u, 0u);
+        }
+        if (t == 0) cluster_wait();  // every CTA of the cluster has started
+        // columns 4 lane .. of tile row r in the 128-byte swizzled K-major A tile
+        const uint32_t off = sw128_offset(r, lane >> 1) + (uint32_t)(lane & 1) * 8u;
+#pragma unroll
+        for (uint32_t dst = 0; dst < kRowsCluster; dst++)
+            *reinterpret_cast<uint2*>(__cluster_map_shared_rank(smem + kBcA1 + off, dst)) = yw;
+    }
+    // the A tiles are read by the tensor core (async proxy) after the cluster barrier
+    asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+}
+
+template <bool BWD, int RPC, bool INPUT = false>
 __global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_constant__ BcMaps tm, const BcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -214,11 +327,13 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (INPUT) cluster_arrive_relaxed();  // this CTA has started (waited on before the peers' A tiles are written)
     mg_pdl_wait();  // activations and weights come from earlier kernels
 
     if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(full1, 2 * kBcTile + (BWD ? kBcTile : 0));
-        for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcA1 + kb * 16384, &tm.a, 64 * kb, m0, full1);
+        mbar_arrive_expect_tx(full1, (INPUT ? 1 : 2) * kBcTile + (BWD ? kBcTile : 0));
+        if (!INPUT)
+            for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcA1 + kb * 16384, &tm.a, 64 * kb, m0, full1);
         if (!BWD) {
             // W_up[k][h0 + n]: K rows 64 kb.., N boxes h0 + 64 j
             for (int kb = 0; kb < 2; kb++)
@@ -241,7 +356,14 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_
             // W_up as [N = 128][K = 512], K columns h0 + 64 kb ..
             for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcB2 + kb * 16384, &tm.b2, h0 + 64 * kb, 0, full2);
         }
-    } else if (warp == 1 && lane == 0) {
+    }
+    if (INPUT) {
+        // the A tile is computed here: the input layer and the first LayerNorm
+        bc_input_prologue(smem, reinterpret_cast<float*>(smem + A2), q, m0, p.M, p.in);
+        cluster_sync();  // every CTA's rows are in every CTA's A tile
+        tc_fence_after();
+    }
+    if (warp == 1 && lane == 0) {
         if (mbar_wait(full1, 0, p.status, kDevTimeoutFull)) {
             tc_fence_after();
             bc_mma<!BWD>(tmem, smem_u32(smem + kBcA1), smem_u32(smem + kBcB1));
@@ -322,9 +444,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_
     cluster_sync();  // no CTA leaves while another still reads its partial tile
 }
 
-template <bool BWD, int RPC>
+template <bool BWD, int RPC, bool INPUT = false>
 int launch_bc(const BcMaps& tm, const BcParams& p, cudaStream_t st) {
-    auto kern = k_block_cluster<BWD, RPC>;
+    auto kern = k_block_cluster<BWD, RPC, INPUT>;
     constexpr int smemBytes = BWD ? kBcBwdSmem : kBcFwdSmem;
     static uint64_t attr_done = 0;  // one bit per device
     int dev = 0;
@@ -356,10 +478,14 @@ int launch_bc(const BcMaps& tm, const BcParams& p, cudaStream_t st) {
 bool block_cluster_supported(int E, int H) { return E == kRowsBN && H == kBcHidden; }
 
 int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown, void* h, void* v, const LnOutputs& next,
-                          int M, cudaStream_t st) {
+                          int M, cudaStream_t st, const BlockClusterForwardInput* in) {
     MG_CHECK_ARG(lnOut && wUp && wDown && h && v && next.gamma && next.beta && next.xNorm && next.out && next.stdev,
                  "block_cluster_forward: null argument");
     MG_CHECK_ARG(M > 0, "block_cluster_forward: M must be > 0");
+    if (in)
+        MG_CHECK_ARG(in->obs && in->w && in->b && in->gamma && in->beta && in->xNorm && in->stdev && in->inDim > 0 &&
+                         in->inDim <= kRowsInputMaxDim,
+                     "block_cluster_forward: bad input-layer arguments");
     BcMaps tm{};
     int rc = make_tmap_bf16(&tm.a, lnOut, kRowsBN, M, kRowsBN, 128);
     if (!rc) rc = make_tmap_bf16(&tm.b1, wUp, kBcHidden, kRowsBN, kBcHidden, 64);
@@ -374,6 +500,16 @@ int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown,
     p.e.out = static_cast<__nv_bfloat16*>(h);
     p.e.ln = next;
     p.status = status_ptr();
+    if (in) {
+        p.in = BcInput{in->obs, in->mb, in->envRows, in->total, in->inDim,
+                       static_cast<const __nv_bfloat16*>(in->w), static_cast<const __nv_bfloat16*>(in->b),
+                       static_cast<__nv_bfloat16*>(h),
+                       LnOutputs{static_cast<const __nv_bfloat16*>(in->gamma),
+                                 static_cast<const __nv_bfloat16*>(in->beta),
+                                 static_cast<__nv_bfloat16*>(in->xNorm),
+                                 static_cast<__nv_bfloat16*>(const_cast<void*>(lnOut)), in->stdev}};
+        return launch_bc<false, 32, true>(tm, p, st);
+    }
     return launch_bc<false, 32>(tm, p, st);
 }
 
@@ -432,6 +568,18 @@ extern "C" int mg_block_cluster_forward(const void* ln_out, const void* w_up, co
     const mg::LnOutputs ln{static_cast<const __nv_bfloat16*>(gamma), static_cast<const __nv_bfloat16*>(beta),
                            static_cast<__nv_bfloat16*>(x_norm), static_cast<__nv_bfloat16*>(next_ln_out), stdev};
     return mg::block_cluster_forward(ln_out, w_up, w_down, h, v, ln, rows, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mg_block_cluster_forward_input(const float* obs, int in_dim, const void* w_in, const void* b_in,
+                                              const void* gamma0, const void* beta0, void* x_norm0, void* ln_out0,
+                                              float* stdev0, const void* w_up, const void* w_down, void* h, void* v,
+                                              const void* gamma, const void* beta, void* x_norm, void* next_ln_out,
+                                              float* stdev, int rows, mg_stream_t stream) {
+    const mg::LnOutputs ln{static_cast<const __nv_bfloat16*>(gamma), static_cast<const __nv_bfloat16*>(beta),
+                           static_cast<__nv_bfloat16*>(x_norm), static_cast<__nv_bfloat16*>(next_ln_out), stdev};
+    const mg::BlockClusterForwardInput in{obs, nullptr, 0, 0, in_dim, w_in, b_in, gamma0, beta0, x_norm0, stdev0};
+    return mg::block_cluster_forward(ln_out0, w_up, w_down, h, v, ln, rows, reinterpret_cast<cudaStream_t>(stream),
+                                     &in);
 }
 
 extern "C" int mg_block_cluster_backward(const void* dS, const void* w_down, const void* v, const void* w_up, void* dV,

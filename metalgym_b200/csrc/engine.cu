@@ -556,25 +556,29 @@ BlockFwdArgs PpoEngine::blockArgs(ActSet& a, int n, int rows) {
     return b;
 }
 
-// The residual blocks and the final LayerNorm of a forward pass
-// (model/ppo.h:590-615), after the input layer wrote a.h. Per block either
+// The input layer, the residual blocks and the final LayerNorm of a forward
+// pass (model/ppo.h:575-615). Per block either
 // the fused block kernel, or LayerNorm + up GEMM (ReLU) + down GEMM (+ skip);
 // with the LayerNorm epilogue the down GEMM of block n also computes the
 // LayerNorm that follows it (block n + 1's, or the final one), which then has
 // no kernel of its own.
-int PpoEngine::blocksForward(ActSet& a, int rows, cudaStream_t st) {
+int PpoEngine::blocksForward(const float* obs, const RowMap& rm, ActSet& a, int rows, cudaStream_t st) {
     auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
     auto bw = [&](uint32_t p) { return reinterpret_cast<const __nv_bfloat16*>(weights + params[p].offset); };
     const bool cluster = useBlockClusterForward(rows);
     const bool rowsK = !cluster && useRowsForward(rows);
     const bool fused = !cluster && !rowsK && useFusedBlock(rows);
     const bool lnEpi = !fused && (cluster || rowsK || useLnEpilogue(rows));
+    // the first block's kernel also computes the input layer and the first LayerNorm
+    const bool inputInBlock = cluster && L > 0 && O <= kBlockClusterMaxInputDim;
+    // model/input.metal:11-27 (the input gathers the minibatch's observation rows through rm)
+    if (!inputInBlock) MG_TRY(input_forward(obs, w(pInW), w(pInB), a.h, rows, O, E, st, rm));
     for (int n = 0; n < L; n++) {
         if (fused) {
             MG_TRY(block_forward(blockArgs(a, n, rows), w(pUp[n]), w(pDown[n]), st));
             continue;
         }
-        if (n == 0 || !lnEpi)
+        if ((n == 0 && !inputInBlock) || !lnEpi)
             MG_TRY(layernorm_forward(a.h, a.lnXn[n], a.lnOut[n], w(pLnG[n]), w(pLnB[n]), a.lnSd[n], rows, E, st));
         if (cluster) {
             // up (ReLU), down (+ skip) and the next LayerNorm in one kernel
@@ -583,7 +587,10 @@ int PpoEngine::blocksForward(ActSet& a, int rows, cudaStream_t st) {
                                       static_cast<__nv_bfloat16*>(a.lnOut[n + 1]), a.lnSd[n + 1]}
                           : LnOutputs{bw(pLnFg), bw(pLnFb), static_cast<__nv_bfloat16*>(a.fXn),
                                       static_cast<__nv_bfloat16*>(a.fOut), a.fSd};
-            MG_TRY(block_cluster_forward(a.lnOut[n], w(pUp[n]), w(pDown[n]), a.h, a.v[n], next, rows, st));
+            const BlockClusterForwardInput in{obs, rm.mb, rm.envRows, rm.total, O, w(pInW), w(pInB), w(pLnG[0]),
+                                              w(pLnB[0]), a.lnXn[0], a.lnSd[0]};
+            MG_TRY(block_cluster_forward(a.lnOut[n], w(pUp[n]), w(pDown[n]), a.h, a.v[n], next, rows, st,
+                                         n == 0 && inputInBlock ? &in : nullptr));
             continue;
         }
         GemmCall up;
@@ -625,8 +632,7 @@ int PpoEngine::forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st)
     auto w = [&](uint32_t p) { return static_cast<const void*>(W + params[p].offset); };
     // (input_forward can also end with block 0's LayerNorm; measured in a
     // CUDA graph at 4096 rows the two kernels are faster: 5.25 against 5.87 µs)
-    MG_TRY(input_forward(obs, w(pInW), w(pInB), a.h, rows, O, E, st));
-    MG_TRY(blocksForward(a, rows, st));
+    MG_TRY(blocksForward(obs, RowMap{nullptr, 0, 0}, a, rows, st));
     GemmCall hd;
     hd.A = a.fOut; hd.lda = E;
     hd.B = w(pHead); hd.b_mn = true; hd.ldb = kHead;
@@ -645,8 +651,7 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     ActSet& a = trainActs;
     auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
     // forward with activations saved (the input gathers the minibatch's obs rows)
-    MG_TRY(input_forward(obsSlots, w(pInW), w(pInB), a.h, rows, O, E, st, rm));
-    MG_TRY(blocksForward(a, rows, st));
+    MG_TRY(blocksForward(obsSlots, rm, a, rows, st));
     // loss (model/ppo.h:753-781): per-slot advantage statistics from
     // collect(), or in row mode the statistics of this minibatch's rows
     const LossHyper lh{hp.clip, hp.valueCoef, hp.entropyCoef};

@@ -233,7 +233,7 @@ class PpoEngine {
 
    private:
     int forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st);
-    int blocksForward(ActSet& a, int rows, cudaStream_t st);
+    int blocksForward(const float* obs, const RowMap& rm, ActSet& a, int rows, cudaStream_t st);
     BlockFwdArgs blockArgs(ActSet& a, int n, int rows);
     int minibatch(int j, bool rowMode, cudaStream_t st);  // reads sched[j], schedBetaPow[2j..]
     int captureCollect();

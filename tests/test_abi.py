@@ -58,3 +58,25 @@ def test_errors_are_reported_without_a_gpu():
     assert b"no_such_env" in lib.mg_last_error()
     rc = lib.mg_gemm_bf16(None, 0, 64, None, 0, 64, 128, 128, 64, 0, None, 128, None, 0, 1, None)
     assert rc == 1  # MG_ERR_ARGUMENT (checked before any CUDA call)
+
+
+def declared_parameter_counts():
+    """Number of parameters of every function the header declares."""
+    text = (ROOT / "include" / "metalgym_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"typedef struct mg_env_ops \{.*?\} mg_env_ops;", "", text, flags=re.S)
+    counts = {}
+    for m in re.finditer(r"\b(mg_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = m.group(2).strip()
+        counts[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return counts
+
+
+def test_ctypes_signatures_have_the_declared_arity():
+    """A ctypes signature with the wrong number of parameters would shift every
+    argument after the first difference."""
+    from metalgym_b200._abi import SIGNATURES
+
+    counts = declared_parameter_counts()
+    wrong = {n: (len(SIGNATURES[n][1]), counts[n]) for n in counts if len(SIGNATURES[n][1]) != counts[n]}
+    assert not wrong, wrong

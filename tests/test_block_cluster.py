@@ -119,3 +119,45 @@ def test_block_cluster_backward_bit_exact(mg, rows):
         assert torch.equal(bits(got), bits(ref))
     if fuse_input:
         assert torch.equal(in_part, in_ref)
+
+
+@pytest.mark.parametrize("rows", ROWS)
+def test_block_cluster_forward_with_input_layer_bit_exact(mg, rows):
+    """The first block's kernel computing the input layer and the first
+    LayerNorm itself, against the input kernel, the LayerNorm kernel and the
+    block kernel."""
+    O = 4
+    gen = torch.Generator(device="cuda").manual_seed(rows + 29)
+    up, dn, g, b = weights(gen)
+    g0 = (1 + 0.1 * torch.randn(E, device="cuda", generator=gen)).bfloat16()
+    b0 = (0.1 * torch.randn(E, device="cuda", generator=gen)).bfloat16()
+    w_in = (torch.randn(O, E, device="cuda", generator=gen) / 2).bfloat16()
+    b_in = (0.1 * torch.randn(E, device="cuda", generator=gen)).bfloat16()
+    obs = torch.randn(rows, O, device="cuda", generator=gen)
+    # the separate kernels
+    h_ref = torch.empty(rows, E, device="cuda", dtype=torch.bfloat16)
+    assert mg.mg_input_forward(obs.data_ptr(), w_in.data_ptr(), b_in.data_ptr(), h_ref.data_ptr(), rows, O, E,
+                               None) == 0, mg.mg_last_error()
+    xn0_ref, lo0_ref = torch.empty_like(h_ref), torch.empty_like(h_ref)
+    sd0_ref = torch.empty(rows, device="cuda")
+    assert mg.mg_layernorm_forward(h_ref.data_ptr(), xn0_ref.data_ptr(), lo0_ref.data_ptr(), g0.data_ptr(),
+                                   b0.data_ptr(), sd0_ref.data_ptr(), rows, E, None) == 0
+    v_ref = torch.empty(rows, H, device="cuda", dtype=torch.bfloat16)
+    xn_ref, y_ref = torch.empty_like(h_ref), torch.empty_like(h_ref)
+    sd_ref = torch.empty(rows, device="cuda")
+    assert mg.mg_block_cluster_forward(lo0_ref.data_ptr(), up.data_ptr(), dn.data_ptr(), h_ref.data_ptr(),
+                                       v_ref.data_ptr(), g.data_ptr(), b.data_ptr(), xn_ref.data_ptr(),
+                                       y_ref.data_ptr(), sd_ref.data_ptr(), rows, None) == 0, mg.mg_last_error()
+    # one kernel
+    nan = lambda t: torch.full_like(t, float("nan"))  # noqa: E731
+    h, xn0, lo0, sd0, v, xn, y, sd = (nan(t) for t in (h_ref, xn0_ref, lo0_ref, sd0_ref, v_ref, xn_ref, y_ref,
+                                                       sd_ref))
+    rc = mg.mg_block_cluster_forward_input(obs.data_ptr(), O, w_in.data_ptr(), b_in.data_ptr(), g0.data_ptr(),
+                                           b0.data_ptr(), xn0.data_ptr(), lo0.data_ptr(), sd0.data_ptr(),
+                                           up.data_ptr(), dn.data_ptr(), h.data_ptr(), v.data_ptr(), g.data_ptr(),
+                                           b.data_ptr(), xn.data_ptr(), y.data_ptr(), sd.data_ptr(), rows, None)
+    assert rc == 0, mg.mg_last_error()
+    status_ok(mg)
+    for got, ref in ((xn0, xn0_ref), (lo0, lo0_ref), (sd0, sd0_ref), (v, v_ref), (h, h_ref), (xn, xn_ref),
+                     (y, y_ref), (sd, sd_ref)):
+        assert torch.equal(bits(got), bits(ref))
