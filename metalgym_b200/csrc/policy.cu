@@ -603,24 +603,13 @@ __global__ void __launch_bounds__(256) k_adv_stats_rows(const float* __restrict_
 
 // ------------------------------------------------------ gradients and Adam
 
-// Sums the partials of every gradient segment into the flat fp32 gradient
-// arena (model/elementwise.metal:21-31 for the GEMM weights, whose sum is
-// rounded to bf16 as the reference's bf16 gradient arena stores it; the
-// LayerNorm / input / log-std sums stay fp32) and writes one partial sum of
-// squares per CTA for the global norm (model/optimizer.metal:23-34).
-__global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ GradSegmentTable tab,
-                                                       float* gradA, float* gradB, const unsigned int* sel,
-                                                       float* __restrict__ normPartial,
-                                                       unsigned int* __restrict__ counter,
-                                                       float* __restrict__ normSqOut) {
-    mg_pdl_trigger();
-    mg_pdl_wait();
-    // with sel (the peer all-reduce's minibatch counter): gradB when the next
-    // count is odd, else gradA; without it: gradA
-    float* __restrict__ grad = (sel && ((*sel + 1u) & 1u)) ? gradB : gradA;
+// Virtual block b of the finalisation (k_grad_finalize's CTA b): its
+// gradient elements summed over their partials into grad, the block's sum of
+// squares into normPartial[b]. Every thread of the CTA calls it.
+__device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab, int b, float* __restrict__ grad,
+                                                    float* __restrict__ normPartial) {
     __shared__ float s_red[8];
-    __shared__ bool s_last;
-    int b = blockIdx.x, si = 0;
+    int si = 0;
     while (si < tab.n - 1 && b >= tab.seg[si].blockEnd) si++;
     const GradSegment& sg = tab.seg[si];
     const int blockBase = si == 0 ? 0 : tab.seg[si - 1].blockEnd;
@@ -721,7 +710,29 @@ __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ G
     if (threadIdx.x == 0) {
         float t = 0.0f;
         for (int w = 0; w < 8; w++) t = __fadd_rn(t, s_red[w]);
-        normPartial[blockIdx.x] = t;
+        normPartial[b] = t;
+    }
+}
+
+// Sums the partials of every gradient segment into the flat fp32 gradient
+// arena (model/elementwise.metal:21-31 for the GEMM weights, whose sum is
+// rounded to bf16 as the reference's bf16 gradient arena stores it; the
+// LayerNorm / input / log-std sums stay fp32) and writes one partial sum of
+// squares per CTA for the global norm (model/optimizer.metal:23-34).
+__global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ GradSegmentTable tab,
+                                                       float* gradA, float* gradB, const unsigned int* sel,
+                                                       float* __restrict__ normPartial,
+                                                       unsigned int* __restrict__ counter,
+                                                       float* __restrict__ normSqOut) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
+    // with sel (the peer all-reduce's minibatch counter): gradB when the next
+    // count is odd, else gradA; without it: gradA
+    float* __restrict__ grad = (sel && ((*sel + 1u) & 1u)) ? gradB : gradA;
+    __shared__ float s_red[8];
+    __shared__ bool s_last;
+    grad_finalize_block(tab, blockIdx.x, grad, normPartial);
+    if (threadIdx.x == 0) {
         s_last = false;
         if (counter) {
             __threadfence();
@@ -799,6 +810,30 @@ __global__ void __launch_bounds__(256) k_grad_scale_norm(float* __restrict__ gra
 // model/optimizer.metal:36-60 with the host bias-correction powers of
 // model/ppo.h:879-880 (from betaPow[0..1] if given, else the scalars).
 // Every CTA first sums the norm partials in the same order, so all agree.
+// model/optimizer.metal:36-60 on elements i0, i0 + stride, .. of [0, count),
+// the gradient scaled by the clip factor.
+__device__ __forceinline__ void adam_range(float* __restrict__ param, const float* __restrict__ grad,
+                                           float* __restrict__ mom, float* __restrict__ var,
+                                           __nv_bfloat16* __restrict__ weights, int64_t count, const AdamHyper& hp,
+                                           const float* __restrict__ betaPow, float scale, int64_t i0, int64_t stride) {
+    const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+    const float b1p = betaPow ? betaPow[0] : hp.beta1Pow;
+    const float b2p = betaPow ? betaPow[1] : hp.beta2Pow;
+    const float c1 = __fsub_rn(1.0f, b1p), c2 = __fsub_rn(1.0f, b2p);
+    for (int64_t i = i0; i < count; i += stride) {
+        const float g = __fmul_rn(grad[i], scale);
+        const float m = __fadd_rn(__fmul_rn(b1, mom[i]), __fmul_rn(__fsub_rn(1.0f, b1), g));
+        const float v = __fadd_rn(__fmul_rn(b2, var[i]), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
+        mom[i] = m;
+        var[i] = v;
+        const float mHat = __fdiv_rn(m, c1);
+        const float vHat = __fdiv_rn(v, c2);
+        const float x = __fsub_rn(param[i], __fdiv_rn(__fmul_rn(hp.lr, mHat), __fadd_rn(__fsqrt_rn(vHat), eps)));
+        param[i] = x;
+        weights[i] = tobf(x);
+    }
+}
+
 __global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const float* __restrict__ grad,
                                               float* __restrict__ mom, float* __restrict__ var,
                                               __nv_bfloat16* __restrict__ weights,
@@ -825,23 +860,8 @@ __global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const f
         }
     }
     __syncthreads();
-    const float scale = s_scale;
-    const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
-    const float b1p = betaPow ? betaPow[0] : hp.beta1Pow;
-    const float b2p = betaPow ? betaPow[1] : hp.beta2Pow;
-    const float c1 = __fsub_rn(1.0f, b1p), c2 = __fsub_rn(1.0f, b2p);
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
-        const float g = __fmul_rn(grad[i], scale);
-        const float m = __fadd_rn(__fmul_rn(b1, mom[i]), __fmul_rn(__fsub_rn(1.0f, b1), g));
-        const float v = __fadd_rn(__fmul_rn(b2, var[i]), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
-        mom[i] = m;
-        var[i] = v;
-        const float mHat = __fdiv_rn(m, c1);
-        const float vHat = __fdiv_rn(v, c2);
-        const float x = __fsub_rn(param[i], __fdiv_rn(__fmul_rn(hp.lr, mHat), __fadd_rn(__fsqrt_rn(vHat), eps)));
-        param[i] = x;
-        weights[i] = tobf(x);
-    }
+    adam_range(param, grad, mom, var, weights, count, hp, betaPow, s_scale, (int64_t)blockIdx.x * blockDim.x + threadIdx.x,
+               (int64_t)gridDim.x * blockDim.x);
 }
 
 // LossStats (model/ppo.h:925-943): column means of the rows x 5 stats.
