@@ -53,7 +53,7 @@ int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPa
     }
     const int units = p.tilesM * p.tilesN * splits;
     const int grid = std::min(units, num_sms());
-    MG_CUDA_TRY(mg_launch(kern, dim3(grid), dim3(192), (size_t)S::SMEM_BYTES, st, ta, tb, em, p));
+    MG_CUDA_TRY(mg_launch(kern, dim3(grid), dim3(S::THREADS), (size_t)S::SMEM_BYTES, st, ta, tb, em, p));
     return check_launch("gemm_tc_persistent");
 }
 

@@ -30,13 +30,20 @@ struct PersistShape {
     static constexpr int BM = 128;
     static constexpr int BK = 64;
     static constexpr bool STAGED = EPI != kEpiF32;         // bf16 output through shared memory + TMA
-    static constexpr int SLAB = 32 * BN * 2;                 // per epilogue warp: 32 rows x BN bf16
+    // epilogue warps: 8 for the staged elementwise epilogues (two per TMEM
+    // lane quadrant, each on half of the tile's columns: with four the
+    // epilogue, not the tensor core, set the pace), 4 where a thread needs its
+    // whole row (the LayerNorm epilogue) or stores fp32 directly
+    static constexpr int EW = (STAGED && EPI != kEpiResidLN) ? 8 : 4;
+    static constexpr int EPI_COLS = BN * 4 / EW;             // columns per epilogue warp
+    static constexpr int THREADS = 64 + 32 * EW;
+    static constexpr int SLAB = 32 * EPI_COLS * 2;           // per epilogue warp: 32 rows x EPI_COLS bf16
     static constexpr int STAGES = STAGED ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int SLAB_OFF = STAGES * STAGE_BYTES;
-    static constexpr int BAR_OFF = SLAB_OFF + (STAGED ? 4 * SLAB : 0);
+    static constexpr int BAR_OFF = SLAB_OFF + (STAGED ? EW * SLAB : 0);
     static constexpr int GB_OFF = BAR_OFF + 256;  // kEpiResidLN: gamma, beta as fp32
     static constexpr int TMEM_COLS = 2 * BN;      // two accumulators (256 or 512 columns)
     static constexpr int SMEM_BYTES = GB_OFF + (EPI == kEpiResidLN ? 2 * BN * 4 : 0) + 1024 /*align*/;
@@ -86,7 +93,7 @@ struct EpiMaps {
 };
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(PersistShape<BN, EPI>::THREADS, 1)
     gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ EpiMaps em, const GemmParams p) {
     using S = PersistShape<BN, EPI>;
@@ -98,8 +105,8 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* tfull = empty + S::STAGES;  // [2]
     uint64_t* tempty = tfull + 2;         // [2]
     uint64_t* done = tempty + 2;
-    uint64_t* auxFull = done + 1;         // [4], one per epilogue warp
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(auxFull + 4);
+    uint64_t* auxFull = done + 1;         // [EW], one per epilogue warp
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(auxFull + S::EW);
     float* s_gb = reinterpret_cast<float*>(smem + S::GB_OFF);  // kEpiResidLN: gamma[BN], beta[BN]
 
     mg_pdl_trigger();
@@ -115,10 +122,10 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+            mbar_init(&tempty[a], S::EW);  // one arrival per epilogue warp
         }
         mbar_init(done, 1);
-        for (int w = 0; w < 4; w++) mbar_init(&auxFull[w], 1);
+        for (int w = 0; w < S::EW; w++) mbar_init(&auxFull[w], 1);
         fence_barrier_init();
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
@@ -228,9 +235,12 @@ __global__ void __launch_bounds__(192, 1)
             tc_commit(done);
         }
     } else {
-        // ---- epilogue: thread owns row 32 (warp % 4) + lane of each tile
+        // ---- epilogue: thread owns row 32 (warp % 4) + lane of each tile, in
+        // columns [h EPI_COLS, (h + 1) EPI_COLS) (h: which of the quadrant's warps)
         const int q = warp & 3;
-        uint8_t* slab = smem + S::SLAB_OFF + q * S::SLAB;
+        const int e = warp - 2;
+        const int hc = (e / 4) * S::EPI_COLS;
+        uint8_t* slab = smem + S::SLAB_OFF + e * S::SLAB;
         int t = 0;
         int auxWaited = 0;  // aux loads this warp has seen land
         for (int u = blockIdx.x; u < units; u += gridDim.x, t++) {
@@ -243,26 +253,27 @@ __global__ void __launch_bounds__(192, 1)
             if (S::STAGED && lane == 0) {
                 bulk_wait_read<0>();  // the previous tile's store has read the slab
                 if (HAS_AUX) {
-                    mbar_arrive_expect_tx(&auxFull[q], S::SLAB);
+                    mbar_arrive_expect_tx(&auxFull[e], S::SLAB);
 #pragma unroll
-                    for (int j = 0; j < BN / 64; j++) tma_load_2d(slab + j * 4096, &em.aux, n0 + 64 * j, row0, &auxFull[q]);
+                    for (int j = 0; j < S::EPI_COLS / 64; j++)
+                        tma_load_2d(slab + j * 4096, &em.aux, n0 + hc + 64 * j, row0, &auxFull[e]);
                 }
             }
             __syncwarp();
             if (!mbar_wait_warp(&tfull[a], (t >> 1) & 1, p.status, kDevTimeoutDone)) break;
             if (HAS_AUX) {
-                if (!mbar_wait_warp(&auxFull[q], t & 1, p.status, kDevTimeoutFull)) break;
+                if (!mbar_wait_warp(&auxFull[e], t & 1, p.status, kDevTimeoutFull)) break;
                 auxWaited = t + 1;
             }
             tc_fence_after();
             const int row = row0 + lane;
-            const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+            const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN + hc);
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; c++) {
-                const int col = n0 + c * 32;
+            for (int c = 0; c < S::EPI_COLS / 32; c++) {
+                const int col = n0 + hc + c * 32;
                 float v[32];
                 tmem_ld32(acc + (uint32_t)(c * 32), v);
-                if (c == BN / 32 - 1) {
+                if (c == S::EPI_COLS / 32 - 1) {
                     // the whole accumulator is in registers or stored: release it
                     tc_fence_before();
                     __syncwarp();
@@ -312,8 +323,9 @@ __global__ void __launch_bounds__(192, 1)
                 __syncwarp();
                 if (lane == 0) {
 #pragma unroll
-                    for (int j = 0; j < BN / 64; j++)
-                        if (n0 + 64 * j < p.N && row0 < p.M) tma_store_2d(&em.out, n0 + 64 * j, row0, slab + j * 4096);
+                    for (int j = 0; j < S::EPI_COLS / 64; j++)
+                        if (n0 + hc + 64 * j < p.N && row0 < p.M)
+                            tma_store_2d(&em.out, n0 + hc + 64 * j, row0, slab + j * 4096);
                     bulk_commit();
                 }
             }
@@ -420,7 +432,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         // after a timeout: the aux load issued for tile t has landed before the CTA exits
         if (HAS_AUX && lane == 0 && auxWaited < t + 1 && t < (units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x)
-            mbar_wait(&auxFull[q], t & 1, p.status, kDevTimeoutFull);
+            mbar_wait(&auxFull[e], t & 1, p.status, kDevTimeoutFull);
         if (S::STAGED && lane == 0) bulk_wait<0>();  // every store complete before the CTA exits
     }
 
