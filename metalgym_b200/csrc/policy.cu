@@ -179,9 +179,14 @@ __global__ void __launch_bounds__(256) k_input_backward(const float* __restrict_
             if (k0 + 8 <= inDim) {
                 for (int r = 0; r < nr; r++) {
                     const float d = bf(s_dz[r * outDim + c]);
+                    const float2 d2 = make_float2(d, d);
                     const float* o = s_obs + r * inDim + k0;
 #pragma unroll
-                    for (int k = 0; k < 8; k++) acc[k] = __fmaf_rn(o[k], d, acc[k]);
+                    for (int k = 0; k < 8; k += 2) {
+                        const float2 a = f2fma_rn(make_float2(o[k], o[k + 1]), d2, make_float2(acc[k], acc[k + 1]));
+                        acc[k] = a.x;
+                        acc[k + 1] = a.y;
+                    }
                 }
             } else {
                 for (int r = 0; r < nr; r++) {
