@@ -289,45 +289,49 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
     }
     const int r0 = blockIdx.x * rowsPerCta;
     const int r1 = min(rows, r0 + rowsPerCta);
-    // rows r and r + 8 of the warp per step: both rows' loads are issued before
-    // either row is computed (two rows of memory in flight per warp); the sums
-    // run over the rows in the same order as one row at a time
-    for (int r = r0 + warp; r < r1; r += 16) {
-        float dz[2][VPT], xn[2][VPT], rs[2][VPT], sdv[2];
-        const bool two = r + 8 < r1;
+    // rows r, r + 8, r + 16, r + 24 of the warp per step: all four rows' loads
+    // (kept as packed bf16 pairs) are issued before any row is computed; the
+    // sums run over the rows in the same order as one row at a time
+    constexpr int RIF = 4;
+    constexpr int W = VPT / 2;  // bf16 pairs per lane and row
+    auto unpack = [](uint32_t w, float& a, float& b) {
+        a = __uint_as_float(w << 16);
+        b = __uint_as_float(w & 0xffff0000u);
+    };
+    for (int r = r0 + warp; r < r1; r += 8 * RIF) {
+        uint32_t wdz[RIF][W], wxn[RIF][W], wrs[RIF][W];
+        float sdv[RIF];
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
-            if (k == 1 && !two) break;
+        for (int k = 0; k < RIF; k++) {
+            if (r + 8 * k >= r1) break;
             const size_t base = (size_t)(r + 8 * k) * E + c0;
 #pragma unroll
-            for (int j = 0; j < VPT; j += 2) {
-                const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dZ + base + j));
-                const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(xNorm + base + j));
-                dz[k][j] = a.x;
-                dz[k][j + 1] = a.y;
-                xn[k][j] = c.x;
-                xn[k][j + 1] = c.y;
-                if (resid) {
-                    const float2 o = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(resid + base + j));
-                    rs[k][j] = o.x;
-                    rs[k][j + 1] = o.y;
-                }
+            for (int j = 0; j < W; j++) {
+                wdz[k][j] = *reinterpret_cast<const uint32_t*>(dZ + base + 2 * j);
+                wxn[k][j] = *reinterpret_cast<const uint32_t*>(xNorm + base + 2 * j);
+                if (resid) wrs[k][j] = *reinterpret_cast<const uint32_t*>(resid + base + 2 * j);
             }
             sdv[k] = stdev[r + 8 * k];
         }
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
-            if (k == 1 && !two) break;
+        for (int k = 0; k < RIF; k++) {
+            if (r + 8 * k >= r1) break;
             const size_t base = (size_t)(r + 8 * k) * E + c0;
+            float dz[VPT], xn[VPT];
+#pragma unroll
+            for (int j = 0; j < W; j++) {
+                unpack(wdz[k][j], dz[2 * j], dz[2 * j + 1]);
+                unpack(wxn[k][j], xn[2 * j], xn[2 * j + 1]);
+            }
             float dxn[VPT];
             float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
             for (int j = 0; j < VPT; j++) {
-                dg[j] = __fadd_rn(dg[j], rbf(__fmul_rn(xn[k][j], dz[k][j])));
-                db[j] = __fadd_rn(db[j], dz[k][j]);
-                dxn[j] = rbf(__fmul_rn(dz[k][j], g[j]));
+                dg[j] = __fadd_rn(dg[j], rbf(__fmul_rn(xn[j], dz[j])));
+                db[j] = __fadd_rn(db[j], dz[j]);
+                dxn[j] = rbf(__fmul_rn(dz[j], g[j]));
                 s1 = __fadd_rn(s1, dxn[j]);
-                s2 = __fadd_rn(s2, rbf(__fmul_rn(dxn[j], xn[k][j])));
+                s2 = __fadd_rn(s2, rbf(__fmul_rn(dxn[j], xn[j])));
             }
             const float m1 = __fdiv_rn(warp_sum(s1), (float)E);
             const float m2 = __fdiv_rn(warp_sum(s2), (float)E);
@@ -335,12 +339,15 @@ __global__ void __launch_bounds__(256) k_layernorm_backward(__nv_bfloat16* __res
             float dx[VPT];
 #pragma unroll
             for (int j = 0; j < VPT; j++)
-                dx[j] = __fmul_rn(rdev, __fsub_rn(__fsub_rn(dxn[j], m1), __fmul_rn(xn[k][j], m2)));
+                dx[j] = __fmul_rn(rdev, __fsub_rn(__fsub_rn(dxn[j], m1), __fmul_rn(xn[j], m2)));
             if (resid) {
 #pragma unroll
-                for (int j = 0; j < VPT; j += 2)
-                    *reinterpret_cast<__nv_bfloat162*>(residOut + base + j) = __floats2bfloat162_rn(
-                        __fadd_rn(rbf(dx[j]), rs[k][j]), __fadd_rn(rbf(dx[j + 1]), rs[k][j + 1]));
+                for (int j = 0; j < W; j++) {
+                    float r0f, r1f;
+                    unpack(wrs[k][j], r0f, r1f);
+                    *reinterpret_cast<__nv_bfloat162*>(residOut + base + 2 * j) = __floats2bfloat162_rn(
+                        __fadd_rn(rbf(dx[2 * j]), r0f), __fadd_rn(rbf(dx[2 * j + 1]), r1f));
+                }
             } else {
 #pragma unroll
                 for (int j = 0; j < VPT; j += 2)
@@ -674,6 +681,19 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
         const float* src = sg.src + i;
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         int p = 0;
+        // sixteen loads in flight per thread (fewer round trips to L2), then eight
+        for (; p + 16 <= sg.nparts; p += 16) {
+            float4 v[16];
+#pragma unroll
+            for (int q = 0; q < 16; q++) v[q] = *reinterpret_cast<const float4*>(src + (int64_t)(p + q) * st);
+#pragma unroll
+            for (int q = 0; q < 16; q++) {
+                acc.x = __fadd_rn(acc.x, v[q].x);
+                acc.y = __fadd_rn(acc.y, v[q].y);
+                acc.z = __fadd_rn(acc.z, v[q].z);
+                acc.w = __fadd_rn(acc.w, v[q].w);
+            }
+        }
         for (; p + 8 <= sg.nparts; p += 8) {
             float4 v[8];
 #pragma unroll
