@@ -204,6 +204,70 @@ __global__ void __launch_bounds__(256) k_input_backward(const float* __restrict_
     }
 }
 
+// The same sums with every observation column's accumulator in registers
+// (inDim <= KMAX): rows outer, so each row's dZ value and observations are
+// read from shared memory once (four at a time with VEC4) instead of once per
+// chunk of 8 columns; the additions per accumulator run in the same row order,
+// so the partials are bit-identical to k_input_backward's.
+template <int KMAX, bool VEC4>
+__global__ void __launch_bounds__(256) k_input_backward_regs(const float* __restrict__ obs,
+                                                             const __nv_bfloat16* __restrict__ dZ,
+                                                             float* __restrict__ partial, int rows, int inDim,
+                                                             int outDim, int rowsPerCta, RowMap rm) {
+    mg_pdl_trigger();
+    mg_pdl_wait();
+    extern __shared__ float s_obs[];  // rowsPerCta x inDim fp32, then rowsPerCta x outDim bf16
+    const int r0 = blockIdx.x * rowsPerCta;
+    const int nr = min(rowsPerCta, rows - r0);
+    __nv_bfloat16* s_dz = reinterpret_cast<__nv_bfloat16*>(s_obs + rowsPerCta * inDim);
+    for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) {
+        const int r = r0 + i / inDim;
+        const uint64_t g = rm.mb ? mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : (uint64_t)r;
+        s_obs[i] = obs[g * inDim + i % inDim];
+    }
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(dZ + (size_t)r0 * outDim);
+        uint4* dst = reinterpret_cast<uint4*>(s_dz);
+        const int n16 = nr * outDim / 8;
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    float* part = partial + (size_t)blockIdx.x * (inDim + 1) * outDim;
+    for (int c = threadIdx.x; c < outDim; c += blockDim.x) {
+        float acc[KMAX];
+#pragma unroll
+        for (int k = 0; k < KMAX; k++) acc[k] = 0.0f;
+        float accB = 0.0f;
+        for (int r = 0; r < nr; r++) {
+            const float d = bf(s_dz[r * outDim + c]);
+            accB = __fadd_rn(accB, d);
+            const float2 d2 = make_float2(d, d);
+            const float* o = s_obs + r * inDim;
+#pragma unroll
+            for (int k = 0; k < KMAX; k += 4) {
+                if (k >= inDim) break;
+                float4 ov;
+                if (VEC4) {
+                    ov = *reinterpret_cast<const float4*>(o + k);
+                } else {
+                    ov = make_float4(o[k], k + 1 < inDim ? o[k + 1] : 0.0f, k + 2 < inDim ? o[k + 2] : 0.0f,
+                                     k + 3 < inDim ? o[k + 3] : 0.0f);
+                }
+                const float2 a = f2fma_rn(make_float2(ov.x, ov.y), d2, make_float2(acc[k], acc[k + 1]));
+                const float2 b = f2fma_rn(make_float2(ov.z, ov.w), d2, make_float2(acc[k + 2], acc[k + 3]));
+                acc[k] = a.x;
+                acc[k + 1] = a.y;
+                acc[k + 2] = b.x;
+                acc[k + 3] = b.y;
+            }
+        }
+        part[(size_t)inDim * outDim + c] = accB;
+#pragma unroll
+        for (int k = 0; k < KMAX; k++)
+            if (k < inDim) part[(size_t)k * outDim + c] = acc[k];
+    }
+}
+
 // -------------------------------------------------------------- layernorm
 
 // model/layernorm.metal:10-71. One warp per row; lane l owns VPT consecutive
@@ -967,10 +1031,22 @@ int input_backward(const float* obs, const void* dZ, float* partial, int rows, i
     const int rpc = input_rows_per_cta(rows, inDim, outDim);
     const size_t sm = (size_t)rpc * inDim * 4 + (size_t)rpc * outDim * 2;
     MG_CHECK_ARG(sm <= 200 * 1024, "input_backward: rows per CTA x widths too large for shared memory");
+    const auto* DZ = static_cast<const __nv_bfloat16*>(dZ);
+    const int blocks = grid_rows(rows, rpc), threads = std::min(outDim, 256);
+    // the register-accumulator kernel for the observation widths of the
+    // built-in environments and their kin (rows outer), else the chunked one
+    auto regs = [&](auto kern) -> int {
+        if (sm > 48 * 1024) MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        MG_LAUNCH(kern, blocks, threads, sm, st, obs, DZ, partial, rows, inDim, outDim, rpc, rm);
+        return check_launch("k_input_backward_regs");
+    };
+    const bool v4 = inDim % 4 == 0;
+    if (inDim <= 8) return v4 ? regs(k_input_backward_regs<8, true>) : regs(k_input_backward_regs<8, false>);
+    if (inDim <= 16) return v4 ? regs(k_input_backward_regs<16, true>) : regs(k_input_backward_regs<16, false>);
+    if (inDim <= 48) return v4 ? regs(k_input_backward_regs<48, true>) : regs(k_input_backward_regs<48, false>);
     if (sm > 48 * 1024)
         MG_CUDA_TRY(cudaFuncSetAttribute(k_input_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    MG_LAUNCH(k_input_backward, grid_rows(rows, rpc), std::min(outDim, 256), sm, st,
-        obs, static_cast<const __nv_bfloat16*>(dZ), partial, rows, inDim, outDim, rpc, rm);
+    MG_LAUNCH(k_input_backward, blocks, threads, sm, st, obs, DZ, partial, rows, inDim, outDim, rpc, rm);
     return check_launch("k_input_backward");
 }
 
