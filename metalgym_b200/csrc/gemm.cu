@@ -131,7 +131,10 @@ int gemm_bf16(const GemmCall& c, cudaStream_t st) {
         const int sms = num_sms();
         const int tiles128 = ((c.M + 127) / 128) * ((c.N + 127) / 128) * splits;
         const int tiles256 = ((c.M + 127) / 128) * ((c.N + 255) / 256) * splits;
-        if (c.persistent != 0 && c.N >= 256 && (c.K >= 1024 || c.N >= 1024) && tiles256 >= sms) {
+        // split-K weight gradients: one wave of 256-wide tiles on most SMs beats
+        // two waves of 128-wide ones (fewer operand bytes through L2)
+        const int min256 = c.epilogue == kEpiF32 ? sms * 3 / 4 : sms;
+        if (c.persistent != 0 && c.N >= 256 && (c.K >= 1024 || c.N >= 1024) && tiles256 >= min256) {
             // long K: persistent with 256-wide tiles (half the shared-memory
             // traffic per MMA of 128-wide ones); wide N: the operand bytes a
             // tile pulls through L2 per output byte drop by a quarter (at
