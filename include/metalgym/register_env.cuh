@@ -198,7 +198,7 @@ struct EnvLaunchers {
 
     static int step(void* states, const void* actions, void* obs, float* reward, uint8_t* done, uint8_t* doneCopy,
                     uint32_t* rng, int n, mg_stream_t s) {
-        if (n <= 0) return MG_ERR_ARGUMENT;
+        if (n <= 0 || !states || !actions || !obs || !reward || !done || !rng) return MG_ERR_ARGUMENT;
         MG_LAUNCH(env_step_kernel<Env>, grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s), 
             static_cast<typename T::State*>(states), static_cast<const typename T::Action*>(actions),
             static_cast<typename T::Obs*>(obs), reward, done, doneCopy, rng, n);
@@ -206,7 +206,8 @@ struct EnvLaunchers {
     }
     static int run_random(void* states, void* obsRing, float* rewardRing, uint8_t* doneRing, uint8_t* done,
                           uint32_t* rng, int n, int steps, int ring, int mode, mg_stream_t s) {
-        if (n <= 0 || steps < 0 || ring <= 0) return MG_ERR_ARGUMENT;
+        if (n <= 0 || steps < 0 || ring <= 0 || !states || !obsRing || !rewardRing || !doneRing || !done || !rng)
+            return MG_ERR_ARGUMENT;
         MG_LAUNCH(env_run_random_kernel<Env>, grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s), 
             static_cast<typename T::State*>(states), static_cast<typename T::Obs*>(obsRing), rewardRing, doneRing,
             done, rng, n, steps, ring, mode);
@@ -215,7 +216,9 @@ struct EnvLaunchers {
     static int collect_step(const void* head, const void* logStd, void* states, void* actionOut, float* logpOut,
                             float* valueOut, void* obsOut, float* rewardOut, uint8_t* done, uint8_t* doneSlot,
                             uint32_t* rng, int n, mg_stream_t s) {
-        if (n <= 0) return MG_ERR_ARGUMENT;
+        if (n <= 0 || !head || (T::kContinuous && !logStd) || !states || !actionOut || !logpOut || !valueOut ||
+            !obsOut || !rewardOut || !done || !doneSlot || !rng)
+            return MG_ERR_ARGUMENT;
         MG_LAUNCH(env_collect_step_kernel<Env>, grid(n), kBlock, 0, reinterpret_cast<cudaStream_t>(s), 
             static_cast<const __nv_bfloat16*>(head), static_cast<const __nv_bfloat16*>(logStd),
             static_cast<typename T::State*>(states), static_cast<typename T::Action*>(actionOut), logpOut, valueOut,

@@ -98,7 +98,7 @@ int mg_env_step(const char* kernel_name, void* states, const void* actions, void
     const mg_env_ops* o = mg::find_or_fail(kernel_name);
     if (!o) return MG_ERR_NOT_FOUND;
     int rc = o->step(states, actions, obs, reward, done, done_copy, rng, n, stream);
-    return rc ? mg::fail(rc, "env step launch failed") : MG_OK;
+    return rc ? mg::fail(rc, rc == MG_ERR_ARGUMENT ? "mg_env_step: bad arguments" : "env step launch failed") : MG_OK;
 }
 
 int mg_env_run_random(const char* kernel_name, void* states, void* obs_ring, float* reward_ring, uint8_t* done_ring,
@@ -106,7 +106,8 @@ int mg_env_run_random(const char* kernel_name, void* states, void* obs_ring, flo
     const mg_env_ops* o = mg::find_or_fail(kernel_name);
     if (!o) return MG_ERR_NOT_FOUND;
     int rc = o->run_random(states, obs_ring, reward_ring, done_ring, done, rng, n, steps, ring, mode, stream);
-    return rc ? mg::fail(rc, "env run_random launch failed") : MG_OK;
+    return rc ? mg::fail(rc, rc == MG_ERR_ARGUMENT ? "mg_env_run_random: bad arguments" : "env run_random launch failed")
+              : MG_OK;
 }
 
 int mg_env_collect_step(const char* kernel_name, const void* head, const void* log_std, void* states,
@@ -116,7 +117,9 @@ int mg_env_collect_step(const char* kernel_name, const void* head, const void* l
     if (!o) return MG_ERR_NOT_FOUND;
     int rc = o->collect_step(head, log_std, states, action_out, logp_out, value_out, obs_out, reward_out, done,
                              done_slot, rng, n, stream);
-    return rc ? mg::fail(rc, "env collect_step launch failed") : MG_OK;
+    return rc ? mg::fail(rc, rc == MG_ERR_ARGUMENT ? "mg_env_collect_step: bad arguments"
+                                                : "env collect_step launch failed")
+              : MG_OK;
 }
 
 }  // extern "C"

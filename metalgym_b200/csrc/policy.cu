@@ -1247,12 +1247,14 @@ extern "C" {
 
 int mg_input_forward(const float* obs, const void* w, const void* b, void* out, int rows, int in_dim, int out_dim,
                      mg_stream_t s) {
+    MG_CHECK_ARG(obs && w && b && out, "input_forward: null argument");
     return mg::input_forward(obs, w, b, out, rows, in_dim, out_dim, MG_STREAM(s));
 }
 
 int mg_input_forward_layernorm(const float* obs, const void* w, const void* b, void* out, const void* gamma,
                                const void* beta, void* x_norm, void* ln_out, float* stdev, int rows, int in_dim,
                                int out_dim, mg_stream_t s) {
+    MG_CHECK_ARG(obs && w && b && out, "input_forward_layernorm: null argument");
     MG_CHECK_ARG(gamma && beta && x_norm && ln_out && stdev, "input_forward_layernorm: null LayerNorm argument");
     mg::LnOutputs ln{static_cast<const __nv_bfloat16*>(gamma), static_cast<const __nv_bfloat16*>(beta),
                      static_cast<__nv_bfloat16*>(x_norm), static_cast<__nv_bfloat16*>(ln_out), stdev};
@@ -1261,6 +1263,7 @@ int mg_input_forward_layernorm(const float* obs, const void* w, const void* b, v
 
 int mg_input_backward_partials(const float* obs, const void* dZ, float* partial, int rows, int in_dim, int out_dim,
                                mg_stream_t s) {
+    MG_CHECK_ARG(obs && dZ && partial, "input_backward: null argument");
     return mg::input_backward(obs, dZ, partial, rows, in_dim, out_dim, MG_STREAM(s));
 }
 
@@ -1270,11 +1273,13 @@ int mg_input_backward_num_partials(int rows, int in_dim, int out_dim) {
 
 int mg_layernorm_forward(const void* x, void* x_norm, void* out, const void* gamma, const void* beta, float* stdev,
                          int rows, int cols, mg_stream_t s) {
+    MG_CHECK_ARG(x && x_norm && out && gamma && beta && stdev, "layernorm_forward: null argument");
     return mg::layernorm_forward(x, x_norm, out, gamma, beta, stdev, rows, cols, MG_STREAM(s));
 }
 
 int mg_layernorm_backward(void* dZ, const void* x_norm, const void* gamma, const float* stdev, void* resid,
                           float* partial, int rows, int cols, mg_stream_t s) {
+    MG_CHECK_ARG(dZ && x_norm && gamma && stdev && partial, "layernorm_backward: null argument");
     return mg::layernorm_backward(dZ, x_norm, gamma, stdev, resid, partial, rows, cols, MG_STREAM(s));
 }
 
@@ -1282,17 +1287,20 @@ int mg_layernorm_backward_num_partials(int rows) { return mg::layernorm_backward
 
 int mg_sample_categorical(const void* head, uint32_t* rng, int32_t* action, float* log_prob, float* value, int rows,
                           int act_dim, mg_stream_t s) {
+    MG_CHECK_ARG(head && rng && action && log_prob && value, "sample_categorical: null argument");
     return mg::sample_categorical(head, rng, action, log_prob, value, rows, act_dim, MG_STREAM(s));
 }
 
 int mg_sample_gaussian(const void* head, const void* log_std, uint32_t* rng, float* action, float* log_prob,
                        float* value, int rows, int act_dim, mg_stream_t s) {
+    MG_CHECK_ARG(head && log_std && rng && action && log_prob && value, "sample_gaussian: null argument");
     return mg::sample_gaussian(head, log_std, rng, action, log_prob, value, rows, act_dim, MG_STREAM(s));
 }
 
 int mg_policy_loss(const void* head, const int32_t* action, const float* adv, const float* adv_stats,
                    const float* ret, const float* old_log_prob, void* dZ, float* stats, int rows, int act_dim,
                    float clip, float value_coef, float entropy_coef, mg_stream_t s) {
+    MG_CHECK_ARG(head && action && adv && ret && old_log_prob && dZ && stats, "policy_loss: null argument");
     LossHyper hp{clip, value_coef, entropy_coef};
     return mg::policy_loss(head, action, adv, adv_stats, ret, old_log_prob, dZ, stats, rows, act_dim, hp,
                            MG_STREAM(s));
@@ -1302,6 +1310,8 @@ int mg_gaussian_loss(const void* head, const float* action, const float* adv, co
                      const float* ret, const float* old_log_prob, void* dZ, float* stats, const void* log_std,
                      float* dlogstd_partial, int rows, int act_dim, float clip, float value_coef, float entropy_coef,
                      mg_stream_t s) {
+    MG_CHECK_ARG(head && action && adv && ret && old_log_prob && dZ && stats && log_std && dlogstd_partial,
+                 "gaussian_loss: null argument");
     LossHyper hp{clip, value_coef, entropy_coef};
     return mg::gaussian_loss(head, action, adv, adv_stats, ret, old_log_prob, dZ, stats, log_std, dlogstd_partial,
                              rows, act_dim, hp, MG_STREAM(s));
@@ -1311,10 +1321,13 @@ int mg_gaussian_loss_num_partials(int rows) { return mg::gaussian_loss_parts(row
 
 int mg_gae(const float* reward, const uint8_t* done, const float* value, const void* bootstrap_head, float* adv,
            float* ret, int rows, int horizon, int act_dim, float gamma, float lambda, mg_stream_t s) {
+    MG_CHECK_ARG(reward && done && value && bootstrap_head && adv && ret, "gae: null argument");
+    MG_CHECK_ARG(act_dim >= 1 && act_dim < mg::kHeadDim, "gae: act_dim must be in [1, 64)");
     return mg::gae(reward, done, value, bootstrap_head, adv, ret, rows, horizon, act_dim, gamma, lambda, MG_STREAM(s));
 }
 
 int mg_advantage_stats(const float* adv, float* stats_out, int rows, int slots, mg_stream_t s) {
+    MG_CHECK_ARG(adv && stats_out, "advantage_stats: null argument");
     return mg::advantage_stats(adv, stats_out, rows, slots, MG_STREAM(s));
 }
 
@@ -1338,12 +1351,14 @@ int mg_reduce_partials_num_norm_partials(int64_t count) { return (int)((count + 
 int mg_adam_step(float* master, const float* grad, float* momentum, float* variance, void* weights,
                  const float* norm_partial, int n_norm_partials, int64_t count, float lr, float beta1_pow,
                  float beta2_pow, float max_grad_norm, float* norm_sq_out, mg_stream_t s) {
+    MG_CHECK_ARG(master && grad && momentum && variance && weights && norm_partial, "adam_step: null argument");
     AdamHyper hp{lr, max_grad_norm, beta1_pow, beta2_pow};
     return mg::adam(master, grad, momentum, variance, weights, norm_partial, n_norm_partials, count, hp, nullptr,
                     norm_sq_out, MG_STREAM(s));
 }
 
 int mg_stats_mean(const float* stats, int rows, float* out5, mg_stream_t s) {
+    MG_CHECK_ARG(stats && out5 && rows > 0, "stats_mean: null argument or no rows");
     return mg::stats_mean(stats, rows, out5, MG_STREAM(s));
 }
 

@@ -80,3 +80,52 @@ def test_ctypes_signatures_have_the_declared_arity():
     counts = declared_parameter_counts()
     wrong = {n: (len(SIGNATURES[n][1]), counts[n]) for n in counts if len(SIGNATURES[n][1]) != counts[n]}
     assert not wrong, wrong
+
+
+# Entry points that only query, release or read state: null pointers are valid
+# (release / no output) or there is nothing to validate.
+_NO_ARGUMENT_CHECK = {
+    "mg_last_error", "mg_version", "mg_env_count", "mg_env_name", "mg_env_find", "mg_device_status",
+    "mg_gemm_rows_splits", "mg_input_backward_num_partials", "mg_layernorm_backward_num_partials",
+    "mg_gaussian_loss_num_partials", "mg_reduce_partials_num_norm_partials", "mg_gym_destroy", "mg_ppo_destroy",
+    "mg_comm_destroy", "mg_host_free",
+}
+
+
+def _null_pointer_arguments(argtypes):
+    """Null for every pointer, 128 for every count or width, 0.1 for every
+    float and the CartPole kernel name for every string."""
+    vals = []
+    for a in argtypes:
+        if a in (ctypes.c_int, ctypes.c_uint32, ctypes.c_int64, ctypes.c_uint64):
+            vals.append(128)
+        elif a is ctypes.c_float:
+            vals.append(0.1)
+        elif a is ctypes.c_char_p:
+            vals.append(b"rollout_cartpole")
+        else:
+            vals.append(None)
+    return vals
+
+
+def test_null_pointers_are_argument_errors():
+    """Every entry point that takes buffers rejects null ones with
+    MG_ERR_ARGUMENT and a message before it reaches CUDA, so that a caller's
+    missing buffer never becomes a kernel reading address 0."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("runs where no GPU is visible: an entry point without the check would launch")
+    import metalgym_b200
+    from metalgym_b200._abi import SIGNATURES
+
+    lib = metalgym_b200.lib()
+    wrong = {}
+    for name, (_, argtypes) in SIGNATURES.items():
+        if name in _NO_ARGUMENT_CHECK or name.startswith("mg_env_register"):
+            continue
+        rc = getattr(lib, name)(*_null_pointer_arguments(argtypes))
+        msg = lib.mg_last_error() or b""
+        if rc != 1 or not msg:
+            wrong[name] = (rc, msg.decode(errors="replace"))
+    assert not wrong, wrong
