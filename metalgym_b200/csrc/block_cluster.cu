@@ -448,13 +448,8 @@ template <bool BWD, int RPC, bool INPUT = false>
 int launch_bc(const BcMaps& tm, const BcParams& p, cudaStream_t st) {
     auto kern = k_block_cluster<BWD, RPC, INPUT>;
     constexpr int smemBytes = BWD ? kBcBwdSmem : kBcFwdSmem;
-    static uint64_t attr_done = 0;  // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done & (1ull << (dev & 63)))) {
-        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smemBytes));
-        attr_done |= 1ull << (dev & 63);
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    if (int rc = smem_limit_once(kern, smemBytes, attr_done)) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((p.M + kRowsBM - 1) / kRowsBM) * kRowsCluster));
     cfg.blockDim = dim3(kRowsThreads);

@@ -461,19 +461,13 @@ int block_forward(const BlockFwdArgs& a, const void* up, const void* down, cudaS
     const int grid = (a.rows + 127) / 128;
     if (a.E == 64) {
         using S = BlockFwdSmem<64>;
-        static bool attr = false;
-        if (!attr) {
-            MG_CUDA_TRY(cudaFuncSetAttribute(k_block_forward<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES));
-            attr = true;
-        }
+        static std::atomic<uint64_t> attr_done{0};
+        if (int rc2 = smem_limit_once(k_block_forward<64>, S::BYTES, attr_done)) return rc2;
         MG_CUDA_TRY(mg_launch(k_block_forward<64>, dim3(grid), dim3(224), (size_t)S::BYTES, st, m, args));
     } else {
         using S = BlockFwdSmem<128>;
-        static bool attr = false;
-        if (!attr) {
-            MG_CUDA_TRY(cudaFuncSetAttribute(k_block_forward<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES));
-            attr = true;
-        }
+        static std::atomic<uint64_t> attr_done{0};
+        if (int rc2 = smem_limit_once(k_block_forward<128>, S::BYTES, attr_done)) return rc2;
         MG_CUDA_TRY(mg_launch(k_block_forward<128>, dim3(grid), dim3(224), (size_t)S::BYTES, st, m, args));
     }
     return check_launch("k_block_forward");

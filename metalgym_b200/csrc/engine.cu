@@ -22,6 +22,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <sstream>
 #include <string>
 
@@ -62,9 +63,8 @@ struct Nccl {
 
 Nccl& nccl() {
     static Nccl n;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    static std::once_flag once;
+    std::call_once(once, [] {
         void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
         if (h) {
             n.getUniqueId = reinterpret_cast<decltype(&ncclGetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
@@ -74,7 +74,7 @@ Nccl& nccl() {
             n.errorString = reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
             n.ok = n.getUniqueId && n.commInitRank && n.commDestroy && n.allReduce && n.errorString;
         }
-    }
+    });
     return n;
 }
 

@@ -12,13 +12,8 @@ template <int BN, bool AMN, bool BMN, int EPI>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int splits, cudaStream_t st) {
     using S = GemmShape<BN>;
     auto kern = gemm_tc_kernel<BN, AMN, BMN, EPI>;
-    static uint64_t attr_done = 0;  // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done & (1ull << (dev & 63)))) {
-        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES));
-        attr_done |= 1ull << (dev & 63);
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    if (int rc = smem_limit_once(kern, S::SMEM_BYTES, attr_done)) return rc;
     dim3 grid((p.M + S::BM - 1) / S::BM, (p.N + BN - 1) / BN, splits);
     MG_CUDA_TRY(mg_launch(kern, grid, dim3(128), (size_t)S::SMEM_BYTES, st, ta, tb, p));
     return check_launch("gemm_tc_kernel");
@@ -44,13 +39,8 @@ int launch_persistent(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPa
         }
     }
     auto kern = gemm_tc_persistent<BN, AMN, BMN, EPI>;
-    static uint64_t attr_done = 0;  // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done & (1ull << (dev & 63)))) {
-        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES));
-        attr_done |= 1ull << (dev & 63);
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    if (int rc = smem_limit_once(kern, S::SMEM_BYTES, attr_done)) return rc;
     const int units = p.tilesM * p.tilesN * splits;
     const int grid = std::min(units, num_sms());
     MG_CUDA_TRY(mg_launch(kern, dim3(grid), dim3(S::THREADS), (size_t)S::SMEM_BYTES, st, ta, tb, em, p));

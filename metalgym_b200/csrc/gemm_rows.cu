@@ -166,13 +166,8 @@ __global__ void __launch_bounds__(kRowsThreads, 2)
 template <bool BMN, int EPI, int RPC>
 int launch_rows(const CUtensorMap& ta, const CUtensorMap& tb, const RowsParams& p, int ks, cudaStream_t st) {
     auto kern = k_gemm_rows<BMN, EPI, RPC>;
-    static uint64_t attr_done = 0;  // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done & (1ull << (dev & 63)))) {
-        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemOnePerSm));
-        attr_done |= 1ull << (dev & 63);
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    if (int rc = smem_limit_once(kern, kRowsSmemOnePerSm, attr_done)) return rc;
     const int grid = ((p.M + kRowsBM - 1) / kRowsBM) * ks;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);

@@ -228,13 +228,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 template <int RPC>
 int launch_ht(const CUtensorMap& tf, const CUtensorMap& tw, const HeadTailParams& p, cudaStream_t st) {
     auto kern = k_head_tail<RPC>;
-    static uint64_t attr_done = 0;  // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done & (1ull << (dev & 63)))) {
-        MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kHtSmem));
-        attr_done |= 1ull << (dev & 63);
-    }
+    static std::atomic<uint64_t> attr_done{0};
+    if (int rc = smem_limit_once(kern, kHtSmem, attr_done)) return rc;
     const int grid = ((p.M + kRowsBM - 1) / kRowsBM) * 4;
     MG_CUDA_TRY(mg_launch(kern, dim3(grid), dim3(kRowsThreads), (size_t)kHtSmem, st, tf, tw, p));
     return check_launch("k_head_tail");

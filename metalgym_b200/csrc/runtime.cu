@@ -41,15 +41,15 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 int num_sms() {
-    static int cache[64] = {};
+    static std::atomic<int> cache[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (!cache[dev]) {
-        int n = 0;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (!n) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cache[dev] = n;
+        cache[dev].store(n, std::memory_order_relaxed);
     }
-    return cache[dev];
+    return n;
 }
 
 int* status_ptr() {

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "../../include/metalgym_b200.h"
@@ -41,5 +42,20 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
 
 // Last launch error check (cudaGetLastError) with a message.
 int check_launch(const char* what);
+
+// Raises `kern`'s dynamic shared memory limit to `bytes` the first time it is
+// launched on the current device. The limit is a per-device attribute, so
+// `done` keeps one bit per device (one static object per kernel); concurrent
+// callers may both set it, which is harmless.
+template <class K>
+int smem_limit_once(K kern, int bytes, std::atomic<uint64_t>& done) {
+    int dev = 0;
+    MG_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return 0;
+    MG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.fetch_or(bit, std::memory_order_release);
+    return 0;
+}
 
 }  // namespace mg
