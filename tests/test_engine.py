@@ -400,3 +400,47 @@ def test_full_loop_runs_and_learns(mg):
         assert all(np.isfinite(v) for v in st.values()), st
     assert model.step_counter() == 12 * 4 * 32
     assert np.mean(lengths[-3:]) > 1.5 * np.mean(lengths[:2]), lengths
+
+
+def test_two_host_threads_train_independently(mg):
+    """Two models driven from two host threads at once on one GPU (the
+    one-rank-per-thread use) end exactly where the same models end when run
+    one after the other: no shared state between sessions, and the one-time
+    kernel set-up is safe under concurrent first calls."""
+    import threading
+
+    cases = [("rollout_cartpole", 4096, 0), ("rollout_cartpole_continuous", 1024, 512)]
+
+    def run(name, rows, mb_rows, out, key):
+        gym, model = make(name, rows, 128, 4, 2, 8, seed=3)
+        model.minibatch_rows = mb_rows
+        for _ in range(2):
+            model.collect()
+            model.train(2)
+        out[key] = {b: model.download(b) for b in ("weights", "master", "obs", "done")}
+        out[key]["stats"] = model.last_stats()
+        model.close()
+        gym.close()
+
+    together, errors = {}, []
+
+    def guarded(*a):
+        try:
+            run(*a)
+        except Exception as e:  # reported below; a thread's exception would be lost
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=guarded, args=(n, r, m, together, i)) for i, (n, r, m) in enumerate(cases)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=300)
+    assert not errors, errors
+    assert not any(t.is_alive() for t in threads)
+    alone = {}
+    for i, (n, r, m) in enumerate(cases):
+        run(n, r, m, alone, i)
+    for i in range(len(cases)):
+        for b in ("weights", "master", "obs", "done"):
+            assert np.array_equal(together[i][b], alone[i][b]), (cases[i][0], b)
+        assert together[i]["stats"] == alone[i]["stats"]
