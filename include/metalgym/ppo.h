@@ -230,6 +230,11 @@ struct PPOModel {
     void setComm(void* comm, int rank, int world) {
         metalgym::check_or_exit(mg_ppo_set_comm(handle, comm, rank, world), "setComm");
     }
+    // Extension: collect() as one persistent kernel (mg_ppo_set_collect_fused;
+    // built-in CartPole / CartPoleContinuous, embed 128, hidden 512).
+    void setFusedCollect(bool on) {
+        metalgym::check_or_exit(mg_ppo_set_collect_fused(handle, on ? 1 : 0), "setFusedCollect");
+    }
     // Extension: checkpoint / resume of the whole training state (mg_ppo_save).
     void save(const char* path) {
         pushHyper();

@@ -413,6 +413,18 @@ int mg_ppo_load(mg_ppo_t model, const char* path);
  * B must divide horizon x parallels. */
 int mg_ppo_set_minibatch_rows(mg_ppo_t model, int rows);
 int mg_ppo_minibatch_rows(mg_ppo_t model, int* out);
+/* collect() as one persistent kernel (no counterpart in the reference, whose
+ * collect() encodes about 460 dispatches, model/ppo.h:716-751): on = 1 runs
+ * every step of the rollout (policy forward on the tensor cores, sampling,
+ * reset-if-done and env step, with each env's state and RNG word kept in
+ * registers), the bootstrap forward and GAE in one launch of 4-CTA clusters,
+ * 128 envs per cluster. Built for the built-in CartPole and
+ * CartPoleContinuous environments and the policy shape embed 128, hidden 512,
+ * 1 to 4 blocks; other configurations return MG_ERR_UNSUPPORTED. 0 (the
+ * default) keeps the captured per-step graph. Up to 4096 parallels the two
+ * produce identical rollouts. */
+int mg_ppo_set_collect_fused(mg_ppo_t model, int on);
+int mg_ppo_collect_fused(mg_ppo_t model, int* out);
 /* One row-mode minibatch over rollout rows perm(base .. base + B - 1) of the
  * permutation keyed by key[4], with an Adam step; blocks (the manual path
  * of row mode, as mg_ppo_train_slot is of slot mode). */

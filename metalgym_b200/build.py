@@ -33,6 +33,8 @@ SOURCES: dict[str, list[str]] = {
     "policy.cu": [],
     "block_fwd.cu": [],
     "block_cluster.cu": [],
+    # the environment steps run inside this kernel: environment rounding rules
+    "collect_fused.cu": ["--fmad=false"],
     "head_tail.cu": [],
     "envs.cu": [],
     "envs_builtin.cu": ["--fmad=false"],

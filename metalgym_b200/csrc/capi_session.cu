@@ -254,6 +254,15 @@ int mg_ppo_minibatch_rows(mg_ppo_t model, int* out) {
     *out = P(model)->mbRows;
     return MG_OK;
 }
+int mg_ppo_set_collect_fused(mg_ppo_t model, int on) {
+    MG_CHECK_ARG(model && (on == 0 || on == 1), "mg_ppo_set_collect_fused: null model or on not 0 / 1");
+    return P(model)->setCollectFused(on != 0);
+}
+int mg_ppo_collect_fused(mg_ppo_t model, int* out) {
+    MG_CHECK_ARG(model && out, "mg_ppo_collect_fused: null argument");
+    *out = P(model)->fusedCollect ? 1 : 0;
+    return MG_OK;
+}
 int mg_ppo_train_rows(mg_ppo_t model, const uint32_t key[4], uint32_t base) {
     MG_CHECK_ARG(model && key, "mg_ppo_train_rows: null argument");
     return P(model)->trainRows(key, base);

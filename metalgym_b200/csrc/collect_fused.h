@@ -1,0 +1,49 @@
+// collect() as one persistent kernel (collect_fused.cu): host-side interface
+// used by the engine.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "metalgym_b200.h"
+
+namespace mg {
+
+constexpr int kCollectFusedMaxBlocks = 4;
+constexpr int kCollectFusedMaxInputDim = 32;
+
+// The rollout of model/ppo.h:716-751 for the policy shape embed 128, hidden
+// 512, 1..4 blocks. Device pointers; weights bf16 in the layouts of the
+// parameter arena.
+struct CollectFusedArgs {
+    int R, T, L, inDim;
+    const void* wIn;  // [inDim][128]
+    const void* bIn;  // [128]
+    // LayerNorm n (n < L: block n's; n == L: the final LayerNorm)
+    const void* lnGamma[kCollectFusedMaxBlocks + 1];
+    const void* lnBeta[kCollectFusedMaxBlocks + 1];
+    const void* wUp[kCollectFusedMaxBlocks];    // [128][512]
+    const void* wDown[kCollectFusedMaxBlocks];  // [512][128]
+    const void* wHead;                          // [128][64]
+    const void* logStd;                         // [act_dim] (continuous environments)
+    // the gym's environment buffers (read at the start, written at the end)
+    void* states;
+    uint8_t* done;
+    uint32_t* rng;
+    // rollout slots, slot-major (model/ppo.h:336-345); obs slot 0 is the input
+    float* obsSlots;  // [T + 1][R][inDim]
+    void* actionSlots;
+    float *logpSlots, *valueSlots, *rewardSlots;
+    uint8_t* doneSlots;
+    float *advSlots, *retSlots;
+    void* bootHead;  // [R][64] bf16: the head rows of the bootstrap forward
+    float gamma, lambda;
+};
+
+// True when `ops` is one of the built-in environments this library compiles
+// the fused kernel for (CartPole, CartPoleContinuous; a user environment
+// registered under the same name is not) and the policy has that shape.
+bool collect_fused_supported(const mg_env_ops* ops, int E, int H, int L, int inDim);
+int collect_fused(const mg_env_ops* ops, const CollectFusedArgs& a, cudaStream_t st);
+
+}  // namespace mg

@@ -27,6 +27,7 @@
 #include <string>
 
 #include "block.h"
+#include "collect_fused.h"
 #include "gemm.h"
 #include "runtime.h"
 
@@ -809,7 +810,44 @@ int PpoEngine::captureCollect() {
     int rc = MG_OK;
     const void* logStd = cont ? static_cast<const void*>(weights + params[pLogStd].offset) : nullptr;
     const mg_env_ops* ops = gym->ops;
-    for (int t = 0; t < T && !rc; t++) {
+    if (fusedCollect) {
+        // every step, the bootstrap forward and GAE in one kernel; the
+        // advantage statistics need every environment's column
+        CollectFusedArgs a{};
+        a.R = R;
+        a.T = T;
+        a.L = L;
+        a.inDim = O;
+        auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
+        a.wIn = w(pInW);
+        a.bIn = w(pInB);
+        for (int n = 0; n < L; n++) {
+            a.lnGamma[n] = w(pLnG[n]);
+            a.lnBeta[n] = w(pLnB[n]);
+            a.wUp[n] = w(pUp[n]);
+            a.wDown[n] = w(pDown[n]);
+        }
+        a.lnGamma[L] = w(pLnFg);
+        a.lnBeta[L] = w(pLnFb);
+        a.wHead = w(pHead);
+        a.logStd = logStd;
+        a.states = gym->states;
+        a.done = gym->done;
+        a.rng = gym->rng;
+        a.obsSlots = obsSlots;
+        a.actionSlots = actionSlots;
+        a.logpSlots = logpSlots;
+        a.valueSlots = valueSlots;
+        a.rewardSlots = rewardSlots;
+        a.doneSlots = doneSlots;
+        a.advSlots = advSlots;
+        a.retSlots = retSlots;
+        a.bootHead = collectActs.head;
+        a.gamma = hp.gamma;
+        a.lambda = hp.lambda;
+        rc = collect_fused(ops, a, st);
+    }
+    for (int t = 0; t < T && !rc && !fusedCollect; t++) {
         rc = forwardOn(obsSlots + (size_t)t * R * O, R, collectActs, st);
         if (!rc)
             rc = ops->collect_step(collectActs.head, logStd, gym->states,
@@ -818,9 +856,10 @@ int PpoEngine::captureCollect() {
                                    rewardSlots + (size_t)t * R, gym->done, doneSlots + (size_t)t * R, gym->rng, R,
                                    reinterpret_cast<mg_stream_t>(st));
     }
-    if (!rc) rc = forwardOn(obsSlots + (size_t)T * R * O, R, collectActs, st);
-    if (!rc) rc = gae(rewardSlots, doneSlots, valueSlots, collectActs.head, advSlots, retSlots, R, T, A, hp.gamma,
-                      hp.lambda, st);
+    if (!rc && !fusedCollect) rc = forwardOn(obsSlots + (size_t)T * R * O, R, collectActs, st);
+    if (!rc && !fusedCollect)
+        rc = gae(rewardSlots, doneSlots, valueSlots, collectActs.head, advSlots, retSlots, R, T, A, hp.gamma,
+                 hp.lambda, st);
     if (!rc) rc = advantage_stats(advSlots, advStats, R, T, st);
     cudaGraph_t graph = nullptr;
     cudaError_t e = cudaStreamEndCapture(st, &graph);
@@ -903,6 +942,21 @@ static MgMinibatch row_minibatch(const uint32_t key[4], uint32_t base) {
     m.base = base;
     m.slot = -1;
     return m;
+}
+
+bool PpoEngine::collectFusedApplies() const { return collect_fused_supported(gym->ops, E, H, L, O); }
+
+int PpoEngine::setCollectFused(bool on) {
+    if (on && !collectFusedApplies())
+        return fail(MG_ERR_UNSUPPORTED,
+                    "setCollectFused: no fused collect kernel for this environment and policy shape (built-in "
+                    "CartPole / CartPoleContinuous, embed 128, hidden 512, 1-4 blocks)");
+    if (on != fusedCollect && collectExec) {
+        cudaGraphExecDestroy(collectExec);  // recaptured by the next collect()
+        collectExec = nullptr;
+    }
+    fusedCollect = on;
+    return MG_OK;
 }
 
 int PpoEngine::setMinibatchRows(int rows) {

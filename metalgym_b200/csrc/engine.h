@@ -86,6 +86,11 @@ class PpoEngine {
     // Minibatch rows of train(): 0 = one time slot per minibatch (the
     // reference); B > 0 = B rollout rows drawn without replacement per epoch.
     int setMinibatchRows(int rows);
+    // collect() as one persistent kernel (collect_fused.cu) instead of the
+    // captured per-step graph; MG_ERR_UNSUPPORTED where the environment or
+    // the policy shape has no fused kernel. Off by default.
+    int setCollectFused(bool on);
+    bool collectFusedApplies() const;
     // One row-mode minibatch with explicit permutation key and base (tests).
     int trainRows(const uint32_t key[4], uint32_t base);
     int forward();  // on the gym's live obs; head in the collect activations
@@ -109,6 +114,7 @@ class PpoEngine {
     uint32_t seed;
     PpoHyper hp;
     bool rolloutStarted = false;
+    bool fusedCollect = false;  // setCollectFused
     float stepCounter = 0.0f;  // model/ppo.h:265 (float, as the reference)
     std::mt19937 hostRng;      // slot shuffle (model/ppo.h:349, 920), row-mode keys
     int mbRows = 0;            // 0: slot mode; > 0: rows per row-mode minibatch

@@ -180,6 +180,17 @@ class PPOModel:
     def minibatch_rows(self, rows: int):
         check(lib().mg_ppo_set_minibatch_rows(self._h, int(rows)), "minibatchRows")
 
+    @property
+    def collect_fused(self) -> bool:
+        """collect() as one persistent kernel (mg_ppo_set_collect_fused)."""
+        v = C.c_int()
+        check(lib().mg_ppo_collect_fused(self._h, C.byref(v)))
+        return bool(v.value)
+
+    @collect_fused.setter
+    def collect_fused(self, on: bool):
+        check(lib().mg_ppo_set_collect_fused(self._h, 1 if on else 0), "collect_fused")
+
     def train_rows(self, key, base: int):
         """One row-mode minibatch over rows perm(base .. base + B - 1) of the
         permutation keyed by the four words of key."""

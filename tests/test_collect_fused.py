@@ -1,0 +1,108 @@
+"""collect() as one persistent kernel (mg_ppo_set_collect_fused,
+metalgym_b200/csrc/collect_fused.cu) against the captured per-step graph.
+
+Both run the same products with the same K split, the same row epilogues,
+samplers and environment code, so up to 4096 parallels (where the per-step
+graph uses the cluster block kernels) the rollouts must be bit-identical:
+every slot (obs, actions, log-probs, values, rewards, dones, advantages,
+returns), the bootstrap head rows, the per-slot advantage statistics and the
+gym's env states / RNG words / done flags after collect(). Several collect()
+calls in a row with a train() between them check the carried state and the
+updated weights. A teacher-forced replay of the fused rollout against the
+CPU oracle checks it against the reference independently of the graph path.
+
+The kernel tests run when METALGYM_TEST_FUSED_COLLECT=1 is set: the kernel
+is new and has not been run on a B200 yet, so the default GPU suite does not
+launch it. The configuration checks launch nothing and always run.
+"""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+run_kernel = pytest.mark.skipif(os.environ.get("METALGYM_TEST_FUSED_COLLECT") != "1",
+                                reason="fused collect kernel not yet run on a B200 (METALGYM_TEST_FUSED_COLLECT=1)")
+
+SLOTS = ("obs", "actions", "logp", "value", "reward", "done", "adv", "ret")
+
+
+def make(name, R, L, T, seed=0, fused=False, embed=128, scale=4):
+    from metalgym_b200.session import Gym, PPOModel
+
+    gym = Gym(name, R, seed=0)
+    model = PPOModel(gym, embed, scale, L, 3e-4, T, seed)
+    if fused:
+        model.collect_fused = True
+    return gym, model
+
+
+def assert_same_rollout(ref, fused, it):
+    (g1, m1), (g2, m2) = ref, fused
+    for name in SLOTS:
+        a, b = m1.slots(name), m2.slots(name)
+        assert np.array_equal(a.view(np.uint8), b.view(np.uint8)), f"collect {it}: slot {name}"
+    for name in ("head", "adv_stats"):
+        assert np.array_equal(m1.download(name), m2.download(name)), f"collect {it}: {name}"
+    for name in ("states", "rng", "done"):
+        assert np.array_equal(g1.download(name), g2.download(name)), f"collect {it}: gym {name}"
+
+
+def test_unsupported_configurations_are_rejected(mg):
+    """No fused kernel for VoxelNav (a 1 KB state, 40 observations, embed 256)
+    or for widths other than embed 128 / hidden 512: MG_ERR_UNSUPPORTED, and
+    the model keeps the per-step graph."""
+    from metalgym_b200 import MgError
+
+    for name, embed, scale in [("rollout_voxelnav", 256, 4), ("rollout_cartpole", 64, 4),
+                               ("rollout_cartpole", 128, 2)]:
+        _, model = make(name, 256, 1, 2, embed=embed, scale=scale)
+        with pytest.raises(MgError, match="code 3"):  # MG_ERR_UNSUPPORTED
+            model.collect_fused = True
+        assert model.collect_fused is False
+    _, model = make("rollout_cartpole", 256, 2, 2)
+    model.collect_fused = True
+    assert model.collect_fused is True
+    model.collect_fused = False
+    assert model.collect_fused is False
+
+
+@run_kernel
+@pytest.mark.parametrize("name,R,L,T", [("rollout_cartpole", 4096, 2, 32), ("rollout_cartpole", 1000, 1, 8),
+                                        ("rollout_cartpole_continuous", 2048, 2, 16),
+                                        ("rollout_cartpole", 300, 4, 3)])
+def test_fused_collect_is_bit_identical_to_the_step_graph(mg, name, R, L, T):
+    ref = make(name, R, L, T, seed=3)
+    fused = make(name, R, L, T, seed=3, fused=True)
+    for it in range(3):
+        ref[1].collect()
+        fused[1].collect()
+        assert_same_rollout(ref, fused, it)
+        assert fused[1].graph_kernels()[0] == 2  # the fused kernel and the advantage statistics
+        ref[1].train(1)
+        fused[1].train(1)
+        assert np.array_equal(ref[1].download("master"), fused[1].download("master")), f"train after collect {it}"
+
+
+@run_kernel
+@pytest.mark.parametrize("name,R,T", [("rollout_cartpole", 1024, 8), ("rollout_cartpole_continuous", 512, 6)])
+def test_fused_collect_teacher_forced(mg, oracle, hostenv, name, R, T):
+    from test_engine import replay_collect
+
+    _, model = make(name, R, 2, T, seed=1, fused=True)
+    model.collect()
+    replay_collect(oracle, hostenv, model, name, 1)
+
+
+@run_kernel
+def test_fused_collect_can_be_switched_between_calls(mg):
+    """Switching paths between collect() calls recaptures the collect graph and
+    continues the same rollout."""
+    ref = make("rollout_cartpole", 512, 2, 4, seed=5)
+    mixed = make("rollout_cartpole", 512, 2, 4, seed=5)
+    for it, on in enumerate([True, False, True]):
+        mixed[1].collect_fused = on
+        ref[1].collect()
+        mixed[1].collect()
+        assert_same_rollout(ref, mixed, it)
