@@ -128,6 +128,8 @@ def run_mine(args, rank, world, local_rank, dist):
     lib = metalgym_b200.lib()
     gym = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=env_shard(rank, ENVS_PER_GPU), device=local_rank)
     model = PPOModel(gym, EMBED, SCALE, LAYERS, LR, HORIZON, seed=0)
+    if args.collect == "fused":
+        model.collect_fused = True
     comm = None
 
     def connect(m):
@@ -264,6 +266,8 @@ def run_mine(args, rank, world, local_rank, dist):
                        "envs_per_gpu": ENVS_PER_GPU, "horizon": HORIZON, "embed": EMBED,
                        "hidden": EMBED * SCALE, "blocks": LAYERS, "epochs": EPOCHS,
                        "minibatch": "one slot (4096 rows)", "parallelism": f"dp{world}",
+                       "collect": ("one persistent kernel (fused)" if args.collect == "fused" else
+                                   "captured per-step graph"),
                        "allreduce": ("none" if world == 1 else
                                      "NVLink peer memory (library kernels)" if args.allreduce == "p2p" else "NCCL"),
                        "l2": "flushed between timed steps (256 MiB write, outside the events)",
@@ -606,6 +610,9 @@ def main():
                     help="N > 1: gradient all-reduce with NCCL or the library's own kernel over NVLink peer "
                          "memory; auto (default): peer memory at 2 GPUs (12.9 against 13.4 ms per CartPole "
                          "iteration), NCCL above (faster at 8 GPUs: 19.8 against 22.6 ms)")
+    ap.add_argument("--collect", choices=["graph", "fused"], default="graph",
+                    help="collect() of the headline loop: the captured per-step graph (default) or the one "
+                         "persistent kernel of collect_fused.cu")
     ap.add_argument("--profile-minibatch", choices=["c3", "c4", "c5"],
                     help="profiling driver: one training minibatch and one forward of that configuration, "
                          "bracketed by cudaProfilerStart / Stop (for ncu --profile-from-start off); no JSON line")
