@@ -231,7 +231,8 @@ struct PPOModel {
         metalgym::check_or_exit(mg_ppo_set_comm(handle, comm, rank, world), "setComm");
     }
     // Extension: collect() as one persistent kernel (mg_ppo_set_collect_fused;
-    // built-in CartPole / CartPoleContinuous, embed 128, hidden 512).
+    // environments with a State of at most 64 bytes and at most 32
+    // observations, embed 128, hidden 512).
     void setFusedCollect(bool on) {
         metalgym::check_or_exit(mg_ppo_set_collect_fused(handle, on ? 1 : 0), "setFusedCollect");
     }

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define MG_VERSION 1
+#define MG_VERSION 2
 
 typedef struct CUstream_st* mg_stream_t;
 
@@ -197,6 +197,12 @@ typedef struct mg_env_ops {
     int (*collect_step)(const void* head, const void* log_std, void* states, void* action_out, float* logp_out,
                         float* value_out, void* obs_out, float* reward_out, uint8_t* done, uint8_t* done_slot,
                         uint32_t* rng, int n, mg_stream_t stream);
+    /* The whole of collect() in one persistent kernel instantiated for this
+     * environment (include/metalgym/detail/collect_fused.cuh), launched with
+     * the tensor maps and parameters the library prepares; NULL for
+     * environments whose State does not fit in registers (over 64 bytes) or
+     * whose observation has more than 32 floats. Added in ABI version 2. */
+    int (*collect_fused)(const void* maps, const void* params, mg_stream_t stream);
 } mg_env_ops;
 
 /* Registers an environment (called by MG_REGISTER_ENV at load time). A later
@@ -418,9 +424,11 @@ int mg_ppo_minibatch_rows(mg_ppo_t model, int* out);
  * every step of the rollout (policy forward on the tensor cores, sampling,
  * reset-if-done and env step, with each env's state and RNG word kept in
  * registers), the bootstrap forward and GAE in one launch of 4-CTA clusters,
- * 128 envs per cluster. Built for the built-in CartPole and
- * CartPoleContinuous environments and the policy shape embed 128, hidden 512,
- * 1 to 4 blocks; other configurations return MG_ERR_UNSUPPORTED. 0 (the
+ * 128 envs per cluster. MG_REGISTER_ENV instantiates the kernel for every
+ * environment whose State has at most 64 bytes and whose observation at most
+ * 32 floats (mg_env_ops.collect_fused; CartPole and CartPoleContinuous among
+ * the built-ins, not VoxelNav); the policy must be embed 128, hidden 512, 1
+ * to 4 blocks. Other configurations return MG_ERR_UNSUPPORTED. 0 (the
  * default) keeps the captured per-step graph. Up to 4096 parallels the two
  * produce identical rollouts. */
 int mg_ppo_set_collect_fused(mg_ppo_t model, int on);

@@ -59,7 +59,7 @@ class EnvOps(ctypes.Structure):
                 ("obs_bytes", ctypes.c_uint32), ("obs_dim", ctypes.c_uint32),
                 ("act_dim", ctypes.c_uint32), ("continuous", ctypes.c_uint32),
                 ("step", ctypes.c_void_p), ("run_random", ctypes.c_void_p),
-                ("collect_step", ctypes.c_void_p)]
+                ("collect_step", ctypes.c_void_p), ("collect_fused", ctypes.c_void_p)]
 
 
 def _env_ops_info(name: str) -> dict:
@@ -70,3 +70,11 @@ def _env_ops_info(name: str) -> dict:
     o = EnvOps.from_address(p)
     return dict(state_bytes=o.state_bytes, action_bytes=o.action_bytes, obs_bytes=o.obs_bytes,
                 obs_dim=o.obs_dim, act_dim=o.act_dim, continuous=o.continuous)
+
+
+def _env_has_fused_collect(name: str) -> bool:
+    """Whether the registered environment brought the persistent collect() kernel."""
+    p = lib().mg_env_find(name.encode())
+    if not p:
+        raise MgError(f"no environment registered as {name!r}")
+    return bool(EnvOps.from_address(p).collect_fused)

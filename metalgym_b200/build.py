@@ -33,8 +33,7 @@ SOURCES: dict[str, list[str]] = {
     "policy.cu": [],
     "block_fwd.cu": [],
     "block_cluster.cu": [],
-    # the environment steps run inside this kernel: environment rounding rules
-    "collect_fused.cu": ["--fmad=false"],
+    "collect_fused.cu": [],
     "head_tail.cu": [],
     "envs.cu": [],
     "envs_builtin.cu": ["--fmad=false"],

@@ -30,7 +30,6 @@
 // dV GEMM followed by the row kernel. Every wait is bounded; both cluster
 // barriers are reached by every thread on every path.
 #include "block.h"
-#include "block_tile.cuh"
 #include "gemm.h"
 #include "gemm_tc.cuh"
 #include "policy.h"

@@ -63,12 +63,6 @@ __device__ __forceinline__ float butterfly32(float* p) {
     return p[0];
 }
 
-// Byte offset of 16-byte chunk `chunk` (8 bf16, counted along K) of tile row
-// `r` in a K-major, 128-byte-swizzled operand of 64-column blocks.
-__device__ __forceinline__ uint32_t sw128_offset(int r, int chunk) {
-    return (uint32_t)((chunk >> 3) * 16384 + r * 128 + (((chunk & 7) ^ (r & 7)) << 4));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);

@@ -1,16 +1,15 @@
-// collect() as one persistent kernel (collect_fused.cu): host-side interface
-// used by the engine.
+// collect() as one persistent kernel: the host side (collect_fused.cu) that
+// prepares the launch of the kernel an environment registered
+// (include/metalgym/detail/collect_fused.cuh, mg_env_ops::collect_fused).
 #pragma once
 
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "metalgym/detail/collect_fused.cuh"
 #include "metalgym_b200.h"
 
 namespace mg {
-
-constexpr int kCollectFusedMaxBlocks = 4;
-constexpr int kCollectFusedMaxInputDim = 32;
 
 // The rollout of model/ppo.h:716-751 for the policy shape embed 128, hidden
 // 512, 1..4 blocks. Device pointers; weights bf16 in the layouts of the
@@ -40,9 +39,9 @@ struct CollectFusedArgs {
     float gamma, lambda;
 };
 
-// True when `ops` is one of the built-in environments this library compiles
-// the fused kernel for (CartPole, CartPoleContinuous; a user environment
-// registered under the same name is not) and the policy has that shape.
+// True when the environment registered a fused kernel (its State fits in
+// registers, its observation in 32 floats) and the policy has the kernel's
+// shape (embed 128, hidden 512, 1..4 blocks).
 bool collect_fused_supported(const mg_env_ops* ops, int E, int H, int L, int inDim);
 int collect_fused(const mg_env_ops* ops, const CollectFusedArgs& a, cudaStream_t st);
 

@@ -949,8 +949,9 @@ bool PpoEngine::collectFusedApplies() const { return collect_fused_supported(gym
 int PpoEngine::setCollectFused(bool on) {
     if (on && !collectFusedApplies())
         return fail(MG_ERR_UNSUPPORTED,
-                    "setCollectFused: no fused collect kernel for this environment and policy shape (built-in "
-                    "CartPole / CartPoleContinuous, embed 128, hidden 512, 1-4 blocks)");
+                    "setCollectFused: no fused collect kernel for this environment and policy shape (an "
+                    "environment with a State of at most 64 bytes and at most 32 observations; embed 128, hidden "
+                    "512, 1-4 blocks)");
     if (on != fusedCollect && collectExec) {
         cudaGraphExecDestroy(collectExec);  // recaptured by the next collect()
         collectExec = nullptr;

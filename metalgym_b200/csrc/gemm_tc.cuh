@@ -19,6 +19,7 @@
 
 #include "gemm.h"
 #include "row_epilogues.cuh"
+#include "metalgym/detail/tile.cuh"
 #include "metalgym/pdl.cuh"
 #include "ptx.cuh"
 
@@ -77,8 +78,6 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v)
         }
     }
 }
-
-__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(128, 1)

@@ -1,301 +1,5 @@
-// Inline-PTX building blocks for sm_100a: mbarriers, TMA tile loads,
-// tcgen05 (TMEM allocation, MMA, commit, loads) and bounded waits.
-//
-// Every wait in this library is bounded by wall-clock time (%globaltimer):
-// when a wait gives up it records an error code in a device status word and
-// returns false, and the caller skips the rest of its work, so a kernel can
-// never spin forever. The host reads the status word after the launch.
+// The inline-PTX building blocks live in the public device headers, where the
+// kernels that environment translation units instantiate can reach them.
 #pragma once
 
-#include <cuda.h>
-#include <cuda_bf16.h>
-#include <cuda_runtime.h>
-#include <stdint.h>
-
-namespace mg {
-
-// Status codes written to the device status word.
-enum DeviceError : int {
-    kDevOk = 0,
-    kDevTimeoutFull = 1,   // TMA data never arrived
-    kDevTimeoutEmpty = 2,  // MMA never released a stage
-    kDevTimeoutDone = 3,   // accumulator never completed
-    kDevBadShape = 4,
-    kDevBadAction = 5,     // an action index outside [0, ACT_DIM) reached the loss
-    kDevTimeoutPeer = 6,   // another GPU never announced its part of an exchange
-};
-
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ void record_error(int* status, int code) {
-    if (status) atomicCAS(status, 0, code);
-}
-
-// ---------------------------------------------------------------- mbarrier
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_barrier_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Waits for the phase with the given parity to complete, at most kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > kWaitLimitNs) {
-            record_error(status, code);
-            return false;
-        }
-    }
-    return true;
-}
-
-// The same wait for a whole warp with a warp-uniform result (lane 0 waits,
-// the others then see the completed phase at once), so that the warp's
-// .sync.aligned instructions after it are never reached by part of the warp.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code) {
-    int ok = 1;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, code) ? 1 : 0;
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (ok && (threadIdx.x & 31) != 0) ok = mbar_wait(bar, parity, status, code) ? 1 : 0;
-    return __all_sync(0xffffffffu, ok) != 0;
-}
-
-// ---------------------------------------------------------------- TMA
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-// Tiled TMA store of a shared-memory box to global memory (bulk-group
-// completion: the issuing thread commits and waits on its own groups).
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
-                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(src))
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// All but the newest N bulk groups of this thread have finished reading shared memory.
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-// All but the newest N bulk groups of this thread are complete.
-template <int N>
-__device__ __forceinline__ void bulk_wait() {
-    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-// Orders this thread's generic-proxy shared-memory writes before later
-// async-proxy reads (TMA stores, tcgen05.mma operands).
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-// warp_sum of N independent values, each summed exactly as warp_sum sums it,
-// with the N shuffles of a butterfly stage issued back to back: the
-// shuffles of one chain are not overlapped by the compiler, those of
-// independent chains written this way are.
-template <int N>
-__device__ __forceinline__ void warp_sum_n(float* v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        float t[N];
-#pragma unroll
-        for (int u = 0; u < N; u++) t[u] = __shfl_xor_sync(0xffffffffu, v[u], o);
-#pragma unroll
-        for (int u = 0; u < N; u++) v[u] = __fadd_rn(v[u], t[u]);
-    }
-}
-
-// Sum over the warp, xor butterfly 16, 8, 4, 2, 1 (every lane gets the sum).
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-
-// ---------------------------------------------------------------- paired fp32
-// Two independent IEEE round-to-nearest operations in one instruction (the
-// f32x2 forms of sm_100), at half the issue cost. A paired multiply feeding a
-// paired add is contracted into a fused multiply-add by the assembler
-// (measured: the results equal __fmaf_rn, not __fadd_rn(__fmul_rn)), so
-// where the reference rounds the product separately these must not be
-// chained; f2fma_rn is the same as two __fmaf_rn.
-__device__ __forceinline__ float2 f2mul_rn(float2 a, float2 b) {
-    float2 d;
-    asm("{.reg .b64 ra, rb, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\t"
-        "mov.b64 rb, {%4, %5};\n\t"
-        "mul.rn.f32x2 rd, ra, rb;\n\t"
-        "mov.b64 {%0, %1}, rd;}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-__device__ __forceinline__ float2 f2add_rn(float2 a, float2 b) {
-    float2 d;
-    asm("{.reg .b64 ra, rb, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\t"
-        "mov.b64 rb, {%4, %5};\n\t"
-        "add.rn.f32x2 rd, ra, rb;\n\t"
-        "mov.b64 {%0, %1}, rd;}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-__device__ __forceinline__ float2 f2fma_rn(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{.reg .b64 ra, rb, rc, rd;\n\t"
-        "mov.b64 ra, {%2, %3};\n\t"
-        "mov.b64 rb, {%4, %5};\n\t"
-        "mov.b64 rc, {%6, %7};\n\t"
-        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
-        "mov.b64 {%0, %1}, rd;}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
-}
-
-// ---------------------------------------------------------------- clusters
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// Every thread of every CTA of the cluster; orders this CTA's shared-memory
-// writes before the other CTAs' reads after it.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// The two halves of cluster_sync: distributed shared memory of another CTA
-// may be accessed only once that CTA has started, which an early relaxed
-// arrive and a later wait establish.
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
-
-// ---------------------------------------------------------------- tcgen05
-__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
-                 "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// D[tmem] (+)= A[smem] * B[smem], one instruction of shape 128 x N x 16 (bf16).
-__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Arrives on `bar` once every previously issued tcgen05.mma of this thread completes.
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets lane (base lane + i).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    tc_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// The same load without the wait: several loads can be in flight, then one
-// tc_wait_ld() before the registers are read.
-__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-
-// Shared-memory matrix descriptor for a 128-byte-swizzled bf16 tile
-// (tcgen05 descriptor format: start >> 4 in bits 0-13, leading byte offset
-// >> 4 in 16-29, stride byte offset >> 4 in 32-45, version 1 in 46-47,
-// layout SWIZZLE_128B = 2 in 61-63). Tiles start on 1024-byte boundaries.
-//  K-major tile  (rows of 64 bf16 = 128 B): SBO = 1024 (8-row groups), LBO unused (16).
-//  MN-major tile (rows of 64 MN elements per K index, boxes of 64 K rows):
-//     LBO = 8192 (next 64-element MN block), SBO = 1024 (next 8 K rows).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1u << 46;
-    d |= (uint64_t)2u << 61;
-    return d;
-}
-
-// Instruction descriptor, kind::f16: bf16 A and B, fp32 accumulator, M = 128.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t n, bool aMnMajor, bool bMnMajor) {
-    return (1u << 4)                      // D format f32
-           | (1u << 7)                    // A format bf16
-           | (1u << 10)                   // B format bf16
-           | ((aMnMajor ? 1u : 0u) << 15)  // A major
-           | ((bMnMajor ? 1u : 0u) << 16)  // B major
-           | ((n >> 3) << 17)             // N / 8
-           | ((128u >> 4) << 24);         // M / 16
-}
-
-}  // namespace mg
+#include "metalgym/detail/ptx.cuh"

@@ -18,14 +18,6 @@
 
 namespace mg {
 
-constexpr int kRowsBM = 128;
-constexpr int kRowsBN = 128;                 // the output width (the embedding)
-constexpr uint32_t kRowsCluster = 4;         // CTAs per cluster; each ends 32 rows of the tile
-// 16 warps: all copy an accumulator out of TMEM (quadrant w % 4, columns
-// 32 (w / 4) ..), and two rows per warp give the row epilogue enough warps to
-// hide its latency (four warps of eight rows each were latency bound)
-constexpr int kRowsThreads = 512;
-constexpr int kRowsTile = kRowsBM * kRowsBN * 4;        // the fp32 tile, 64 KB
 constexpr int kRowsRedBytes = 4 * 8 * 2 * kRowsBN * 4;  // LayerNorm-backward column sums, 32 KB
 
 enum RowsEpilogue : int { kRowsResidLN = 0, kRowsLNBackward = 1 };
@@ -53,42 +45,6 @@ struct RowsEpi {
     float* inStage;
 };
 constexpr int kRowsInputMaxDim = 32;
-
-// Byte offset of the 16-byte column chunk k (columns 4k..4k+3) of tile row r in
-// an fp32 tile: rows of 512 bytes, chunks XOR-swizzled by the row, so a warp
-// writing chunk k of 32 rows and a warp reading a whole row are both free of
-// bank conflicts.
-__device__ __forceinline__ uint32_t tile_offset(int r, int k) { return (uint32_t)(r * 512 + ((k ^ (r & 31)) << 4)); }
-
-__device__ __forceinline__ float4 bf4_load(const __nv_bfloat16* p) {
-    const uint2 w = *reinterpret_cast<const uint2*>(p);
-    return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
-                       __uint_as_float(w.y & 0xffff0000u));
-}
-__device__ __forceinline__ void bf4_store(__nv_bfloat16* p, float a, float b, float c, float d) {
-    __nv_bfloat162 x = __floats2bfloat162_rn(a, b), y = __floats2bfloat162_rn(c, d);
-    *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<uint32_t*>(&x), *reinterpret_cast<uint32_t*>(&y));
-}
-
-// The 128 x 128 fp32 accumulator at TMEM address acc into the fp32 tile at
-// `tile` (zeros when !valid): every one of the 16 warps copies 32 rows x 32
-// columns.
-__device__ __forceinline__ void rows_tmem_to_tile(uint8_t* tile, uint32_t acc, bool valid) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qd = warp & 3, cc = warp >> 2;
-    const int tr = qd * 32 + lane;
-    float v[32];
-    if (valid) {
-        tmem_ld32(acc + ((uint32_t)(qd * 32) << 16) + (uint32_t)(cc * 32), v);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = 0.0f;
-    }
-#pragma unroll
-    for (int k = 0; k < 8; k++)
-        *reinterpret_cast<float4*>(tile + tile_offset(tr, cc * 8 + k)) =
-            make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-}
 
 // After the cluster barrier that completes every CTA's tile: this CTA's 32
 // rows of the tile (tile rows of the cluster at the same offset `smem` in
