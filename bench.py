@@ -230,7 +230,33 @@ def run_mine(args, rank, world, local_rank, dist):
     raw.synchronize()
     rms = max_over_ranks(rs.elapsed_time(re_), dist)
     legs["raw_env"] = {"value": RAW_STEPS * ENVS_PER_GPU * world / (rms / 1e3), "steps": RAW_STEPS,
-                       "kernel": "one launch, 1000 fused steps (random policy drawn on the env's RNG)"}
+                       "kernel": "one launch, 1000 fused steps (random policy drawn on the env's RNG)",
+                       "scaling": "weak (4096 envs per GPU)"}
+    if world > 1:
+        # strong scaling: BASELINE configs[0]'s 4096 envs in all, split over the
+        # ranks. Every rank reaches the max over ranks, whatever happened.
+        n_strong = ENVS_PER_GPU // world
+        strong_ms = float("inf")
+        try:
+            sg = Gym(ENV, n_strong, seed=0, first_env_id=env_shard(rank, n_strong), device=local_rank)
+            sst = torch.cuda.ExternalStream(sg.stream(), device=local_rank)
+            sg.run_random(RAW_STEPS)
+            sg.synchronize()
+            ss, se = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(sst):
+                ss.record(sst)
+            sg.run_random(RAW_STEPS)
+            with torch.cuda.stream(sst):
+                se.record(sst)
+            sg.synchronize()
+            strong_ms = ss.elapsed_time(se)
+            sg.close()
+        except Exception as ex:  # reported in the leg; the headline run goes on
+            print(f"rank {rank}: strong-scaling raw leg failed: {ex}", file=sys.stderr, flush=True)
+        strong_ms = max_over_ranks(strong_ms, dist)
+        legs["raw_env"]["strong_4096_envs_total"] = (
+            {"value": RAW_STEPS * n_strong * world / (strong_ms / 1e3), "envs_per_gpu": n_strong}
+            if strong_ms != float("inf") else {"value": None, "error": "failed on a rank (see stderr)"})
     # gym.run loop with host actions / rewards (the reference benchmark's loop)
     pinned = ctypes.c_void_p()
     metalgym_b200.check(lib.mg_host_alloc(ENVS_PER_GPU * 8, ctypes.byref(pinned)))
