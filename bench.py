@@ -138,6 +138,8 @@ def run_mine(args, rank, world, local_rank, dist):
             return
         if args.allreduce == "nccl":
             m.set_comm(comm, rank, world)
+            if args.allreduce_overlap:
+                m.set_allreduce_overlap(True)
         else:
             p2p_allreduce(m, dist, rank, world)
 
@@ -295,7 +297,9 @@ def run_mine(args, rank, world, local_rank, dist):
                        "collect": ("one persistent kernel (fused)" if args.collect == "fused" else
                                    "captured per-step graph"),
                        "allreduce": ("none" if world == 1 else
-                                     "NVLink peer memory (library kernels)" if args.allreduce == "p2p" else "NCCL"),
+                                     "NVLink peer memory (library kernels)" if args.allreduce == "p2p" else
+                                     "NCCL, overlapped with the last backward layer" if args.allreduce_overlap else
+                                     "NCCL"),
                        "l2": "flushed between timed steps (256 MiB write, outside the events)",
                        "env_steps_per_step": steps_per_iter * world,
                        "flop_per_env_step": (HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd)},
@@ -636,6 +640,9 @@ def main():
                     help="N > 1: gradient all-reduce with NCCL or the library's own kernel over NVLink peer "
                          "memory; auto (default): peer memory at 2 GPUs (12.9 against 13.4 ms per CartPole "
                          "iteration), NCCL above (faster at 8 GPUs: 19.8 against 22.6 ms)")
+    ap.add_argument("--allreduce-overlap", action="store_true",
+                    help="N > 1 with NCCL: all-reduce all but the last backward layer's gradients on a side "
+                         "stream while that layer's backward runs (default: one all-reduce after the backward)")
     ap.add_argument("--collect", choices=["graph", "fused"], default="graph",
                     help="collect() of the headline loop: the captured per-step graph (default) or the one "
                          "persistent kernel of collect_fused.cu")

@@ -468,6 +468,13 @@ int mg_ppo_graph_kernels(mg_ppo_t model, uint64_t out2[2]);
  * minibatch's gradient is summed over the ranks of `comm` (an ncclComm_t)
  * and divided by world before the norm clip and Adam. */
 int mg_ppo_set_comm(mg_ppo_t model, void* comm, int rank, int world);
+/* With an NCCL communicator (world > 1): on = 1 all-reduces the gradients of
+ * everything but the last backward layer (block 0 and the input layer) on a
+ * side stream while that layer's backward runs, then the rest, instead of one
+ * all-reduce of the whole gradient after the backward pass. The same sums,
+ * in two grouped pairs of calls over the gradient arena's ranges. 0 (the
+ * default): one all-reduce. No counterpart in the reference (one GPU). */
+int mg_ppo_set_allreduce_overlap(mg_ppo_t model, int on);
 
 /* ---------------------------------------------------------------- NCCL / host memory */
 

@@ -84,6 +84,7 @@ SIGNATURES = {
     "mg_ppo_set_minibatch_rows": (I, [P, I]),
     "mg_ppo_minibatch_rows": (I, [P, PI]),
     "mg_ppo_set_collect_fused": (I, [P, I]),
+    "mg_ppo_set_allreduce_overlap": (I, [P, I]),
     "mg_ppo_collect_fused": (I, [P, PI]),
     "mg_ppo_train_rows": (I, [P, P, U]),
     "mg_minibatch_rows": (I, [P, U, U, U64, P]),

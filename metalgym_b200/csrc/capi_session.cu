@@ -254,6 +254,10 @@ int mg_ppo_minibatch_rows(mg_ppo_t model, int* out) {
     *out = P(model)->mbRows;
     return MG_OK;
 }
+int mg_ppo_set_allreduce_overlap(mg_ppo_t model, int on) {
+    MG_CHECK_ARG(model && (on == 0 || on == 1), "mg_ppo_set_allreduce_overlap: null model or on not 0 / 1");
+    return P(model)->setAllreduceOverlap(on != 0);
+}
 int mg_ppo_set_collect_fused(mg_ppo_t model, int on) {
     MG_CHECK_ARG(model && (on == 0 || on == 1), "mg_ppo_set_collect_fused: null model or on not 0 / 1");
     return P(model)->setCollectFused(on != 0);

@@ -59,6 +59,8 @@ struct Nccl {
     decltype(&ncclCommDestroy) commDestroy = nullptr;
     decltype(&ncclAllReduce) allReduce = nullptr;
     decltype(&ncclGetErrorString) errorString = nullptr;
+    decltype(&ncclGroupStart) groupStart = nullptr;
+    decltype(&ncclGroupEnd) groupEnd = nullptr;
     bool ok = false;
 };
 
@@ -73,7 +75,10 @@ Nccl& nccl() {
             n.commDestroy = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));
             n.allReduce = reinterpret_cast<decltype(&ncclAllReduce)>(dlsym(h, "ncclAllReduce"));
             n.errorString = reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
-            n.ok = n.getUniqueId && n.commInitRank && n.commDestroy && n.allReduce && n.errorString;
+            n.groupStart = reinterpret_cast<decltype(&ncclGroupStart)>(dlsym(h, "ncclGroupStart"));
+            n.groupEnd = reinterpret_cast<decltype(&ncclGroupEnd)>(dlsym(h, "ncclGroupEnd"));
+            n.ok = n.getUniqueId && n.commInitRank && n.commDestroy && n.allReduce && n.errorString &&
+                   n.groupStart && n.groupEnd;
         }
     });
     return n;
@@ -265,6 +270,8 @@ PpoEngine::~PpoEngine() {
     for (auto ev : forkEv)
         if (ev) cudaEventDestroy(ev);
     if (joinEv) cudaEventDestroy(joinEv);
+    for (cudaEvent_t ev : {arLateEv, arEarlyEv, arDoneEv})
+        if (ev) cudaEventDestroy(ev);
     cudaSetDevice(cur);
 }
 
@@ -377,6 +384,8 @@ int PpoEngine::init() {
     forkEv.assign(L + 1, nullptr);
     for (auto& ev : forkEv) MG_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     MG_CUDA_TRY(cudaEventCreateWithFlags(&joinEv, cudaEventDisableTiming));
+    for (cudaEvent_t* ev : {&arLateEv, &arEarlyEv, &arDoneEv})
+        MG_CUDA_TRY(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
     MG_TRY(dalloc(&mbAdvStats, 2 * 4));
     MG_TRY(dalloc(&advPartial, (size_t)2 * kAdvStatsMaxCtas * 8));
     MG_TRY(dalloc(&advCounter, 4));
@@ -447,14 +456,22 @@ int PpoEngine::allocTrain(int rows) {
     MG_TRY(dalloc(&lsPart, (size_t)pGs * (A > 0 ? A : 1) * 4));
     GradSegmentTable& tb = gradTable;
     tb = GradSegmentTable{};
+    gradTableEarly = GradSegmentTable{};
+    gradTableLate = GradSegmentTable{};
     auto seg = [&](const float* src, int64_t stride, int nparts, int64_t count, uint32_t p, int round) {
-        GradSegment& s = tb.seg[tb.n++];
+        GradSegment s{};
         s.src = src;
         s.partStride = stride;
         s.nparts = nparts;
         s.count = count;
         s.dstOffset = (int64_t)params[p].offset;
         s.roundBf16 = round;
+        tb.seg[tb.n++] = s;
+        // the overlapped all-reduce: block 0 and the input layer (the last
+        // backward layer), and everything before them in backward order
+        const bool early = p == pInW || p == pInB || p == pLnG[0] || p == pLnB[0] || p == pUp[0] || p == pDown[0];
+        GradSegmentTable& part = early ? gradTableEarly : gradTableLate;
+        part.seg[part.n++] = s;
     };
     seg(inPart, (int64_t)(O + 1) * E, pIn, (int64_t)O * E, pInW, 0);
     seg(inPart + (size_t)O * E, (int64_t)(O + 1) * E, pIn, E, pInB, 0);
@@ -471,13 +488,18 @@ int PpoEngine::allocTrain(int rows) {
     nNorm = grad_table_layout(tb);
     const int nNormAll = std::max(std::max(nNorm, grad_scale_norm_blocks((int64_t)optCount)), p2p_blocks());
     MG_TRY(dalloc(&normPartial, (size_t)nNormAll * 4));
+    // the two halves of the overlapped all-reduce's sums (their norm partials
+    // are unused: the norm is taken after the all-reduce); the late half runs
+    // on the side stream, so it writes its own partials
+    grad_table_layout(gradTableEarly);
+    MG_TRY(dalloc(&normPartialLate, (size_t)std::max(1, grad_table_layout(gradTableLate)) * 4));
     trainBufRows = rows;
     return MG_OK;
 }
 
 void PpoEngine::freeTrain() {
     free_acts(trainActs, false);
-    float** fs[] = {&stats, &headPart, &lnFPart, &inPart, &lsPart, &normPartial};
+    float** fs[] = {&stats, &headPart, &lnFPart, &inPart, &lsPart, &normPartial, &normPartialLate};
     for (float** p : fs) {
         cudaFree(*p);
         *p = nullptr;
@@ -721,7 +743,18 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     // the first block's kernel also sums the input layer's gradient partials
     // (the same 16-row partials input_backward writes at these row counts)
     const bool inputFused = clusterBwd && inputGradFusable(rows);
+    const bool overlapAr = world > 1 && !p2pOn && overlapAllreduce;
     for (int n = L - 1; n >= 0; n--) {
+        if (overlapAr && n == 0) {
+            // every gradient but block 0's and the input layer's is complete:
+            // sum and all-reduce them on the side stream while the last
+            // backward layer runs here (after the side stream's own work)
+            MG_CUDA_TRY(cudaEventRecord(arLateEv, st));
+            MG_CUDA_TRY(cudaStreamWaitEvent(side, arLateEv, 0));
+            forked = true;
+            MG_TRY(grad_finalize(gradTableLate, grad, normPartialLate, side));
+            MG_TRY(allreduceRanges(arLate, side));
+        }
         if (clusterBwd) {
             // dV, dBranch, the LayerNorm backward with the skip add and both
             // weight-gradient partials in one kernel
@@ -783,6 +816,20 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         float* x1 = reinterpret_cast<float*>(static_cast<unsigned char*>(p2pRegion) + p2pTable.xOff[1]);
         MG_TRY(grad_finalize(gradTable, x0, normPartial, st, nullptr, nullptr, x1, p2pSeq));
         MG_TRY(p2p_allreduce(p2pTable, (int64_t)optCount, grad, p2pSeq, p2pCounter, normPartial, normSq, st));
+        const AdamHyper ah{lr, hp.maxGradNorm, 0.0f, 0.0f};
+        return adam(master, grad, mom, var, weights, normPartial, 0, (int64_t)optCount, ah, schedBetaPow + 2 * j,
+                    nullptr, st, normSq);
+    }
+    if (overlapAr) {
+        // the early half: sums here, then its all-reduce after the late one
+        // on the side stream (one stream keeps the communicator's order)
+        MG_TRY(grad_finalize(gradTableEarly, grad, normPartial, st));
+        MG_CUDA_TRY(cudaEventRecord(arEarlyEv, st));
+        MG_CUDA_TRY(cudaStreamWaitEvent(side, arEarlyEv, 0));
+        MG_TRY(allreduceRanges(arEarly, side));
+        MG_CUDA_TRY(cudaEventRecord(arDoneEv, side));
+        MG_CUDA_TRY(cudaStreamWaitEvent(st, arDoneEv, 0));
+        MG_TRY(grad_scale_norm(grad, (int64_t)optCount, 1.0f / (float)world, normPartial, st, normCounter, normSq));
         const AdamHyper ah{lr, hp.maxGradNorm, 0.0f, 0.0f};
         return adam(master, grad, mom, var, weights, normPartial, 0, (int64_t)optCount, ah, schedBetaPow + 2 * j,
                     nullptr, st, normSq);
@@ -1272,6 +1319,41 @@ int PpoEngine::p2pOpen(const void* handles, int r, int w) {
         cudaGraphExecDestroy(trainExec);
         trainExec = nullptr;
     }
+    return MG_OK;
+}
+
+// The two gradient-arena ranges of each half of the overlapped all-reduce:
+// the float-gradient parameters come first in the arena, then the GEMM
+// weights, each group in parameter order, so block 0 and the input layer own
+// a prefix of both groups and the later blocks, final LayerNorm, head and
+// log-std the suffixes.
+void PpoEngine::overlapRanges() {
+    const uint64_t lateF = L > 1 ? params[pLnG[1]].offset : params[pLnFg].offset;
+    const uint64_t lateB = L > 1 ? params[pUp[1]].offset : params[pHead].offset;
+    arEarly = {{{0, lateF}, {optFloatCount, lateB}}};
+    arLate = {{{lateF, optFloatCount}, {lateB, optCount}}};
+}
+
+int PpoEngine::allreduceRanges(const ArRanges& rg, cudaStream_t s) {
+    Nccl& nc = nccl();
+    ncclResult_t r = nc.groupStart();
+    for (int i = 0; i < 2 && r == ncclSuccess; i++) {
+        const uint64_t b = rg.r[i][0], e = rg.r[i][1];
+        if (e > b) r = nc.allReduce(grad + b, grad + b, (size_t)(e - b), ncclFloat, ncclSum, static_cast<ncclComm_t>(comm), s);
+    }
+    const ncclResult_t r2 = nc.groupEnd();
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce (overlapped)");
+    if (r2 != ncclSuccess) return nccl_fail(r2, "ncclGroupEnd");
+    return MG_OK;
+}
+
+int PpoEngine::setAllreduceOverlap(bool on) {
+    overlapRanges();
+    if (on != overlapAllreduce && trainExec) {
+        cudaGraphExecDestroy(trainExec);  // recaptured by the next train()
+        trainExec = nullptr;
+    }
+    overlapAllreduce = on;
     return MG_OK;
 }
 

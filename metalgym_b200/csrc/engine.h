@@ -91,6 +91,12 @@ class PpoEngine {
     // the policy shape has no fused kernel. Off by default.
     int setCollectFused(bool on);
     bool collectFusedApplies() const;
+    // With an NCCL communicator (world > 1): all-reduce the gradients of
+    // everything but the last backward layer (block 0 and the input layer) on
+    // the side stream while that layer's backward runs, then the rest. Off by
+    // default; the sums and the averaged gradient are those of the single
+    // all-reduce.
+    int setAllreduceOverlap(bool on);
     // One row-mode minibatch with explicit permutation key and base (tests).
     int trainRows(const uint32_t key[4], uint32_t base);
     int forward();  // on the gym's live obs; head in the collect activations
@@ -232,6 +238,16 @@ class PpoEngine {
     std::vector<void*> p2pOpened;        // peers' regions opened here
     P2PTable p2pTable{};
     bool p2pOn = false;
+    bool overlapAllreduce = false;  // setAllreduceOverlap
+    struct ArRanges {
+        uint64_t r[2][2];  // [begin, end) element ranges of the gradient arena
+    };
+    ArRanges arEarly{}, arLate{};
+    GradSegmentTable gradTableEarly{}, gradTableLate{};
+    float* normPartialLate = nullptr;
+    cudaEvent_t arLateEv = nullptr, arEarlyEv = nullptr, arDoneEv = nullptr;
+    void overlapRanges();
+    int allreduceRanges(const ArRanges& rg, cudaStream_t s);
     unsigned int* p2pSeq = nullptr;      // device minibatch counter of the exchange
     unsigned int* p2pCounter = nullptr;  // last-CTA detection of the gather
     int p2pHandle(void* out64);

@@ -227,6 +227,11 @@ class PPOModel:
         check(lib().mg_ppo_graph_kernels(self._h, v))
         return int(v[0]), int(v[1])
 
+    def set_allreduce_overlap(self, on: bool):
+        """All-reduce all but the last backward layer's gradients while that
+        layer's backward runs (mg_ppo_set_allreduce_overlap; NCCL, world > 1)."""
+        check(lib().mg_ppo_set_allreduce_overlap(self._h, 1 if on else 0), "allreduce_overlap")
+
     def set_comm(self, comm, rank: int, world: int):
         check(lib().mg_ppo_set_comm(self._h, comm, rank, world))
 

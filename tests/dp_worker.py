@@ -134,9 +134,10 @@ def run_gpu(rank, world, local, dist, allreduce):
     gym = Gym("rollout_cartpole", R, seed=0, first_env_id=env_shard(rank, R), device=local)
     model = PPOModel(gym, 128, 4, 2, 3e-4, T, seed=7)
     comm = None
-    if allreduce == "nccl":
+    if allreduce in ("nccl", "nccl-overlap"):
         comm = nccl_comm(dist, rank, world, local)
         model.set_comm(comm, rank, world)
+        model.set_allreduce_overlap(allreduce == "nccl-overlap")
     else:
         p2p_allreduce(model, dist, rank, world)
     model.collect()
@@ -176,7 +177,7 @@ def run_gpu(rank, world, local, dist, allreduce):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--mode", choices=["cpu", "gpu"], required=True)
-    ap.add_argument("--allreduce", choices=["nccl", "p2p"], default="nccl")
+    ap.add_argument("--allreduce", choices=["nccl", "nccl-overlap", "p2p"], default="nccl")
     args = ap.parse_args()
     import torch.distributed as dist
 

@@ -8,6 +8,7 @@ per-rank gradients, bit for bit, and bit-identical weights across ranks after
 train(); skipped with fewer than two GPUs.
 """
 import json
+import os
 import socket
 import subprocess
 import sys
@@ -40,8 +41,16 @@ def test_data_parallel_host_logic_gloo(oracle):
     assert res["ranks"][0]["equals_single_process"] and res["ranks"][0]["ranks_identical"]
 
 
+# The overlapped all-reduce (all but the last backward layer's gradients
+# reduced on a side stream while that layer's backward runs) has not run on
+# B200s yet: its case runs with METALGYM_TEST_ALLREDUCE_OVERLAP=1.
+_OVERLAP = pytest.param("nccl-overlap", marks=pytest.mark.skipif(
+    os.environ.get("METALGYM_TEST_ALLREDUCE_OVERLAP") != "1",
+    reason="overlapped all-reduce not yet run on B200s (METALGYM_TEST_ALLREDUCE_OVERLAP=1)"))
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("allreduce", ["nccl", "p2p"])
+@pytest.mark.parametrize("allreduce", ["nccl", "p2p", _OVERLAP])
 def test_data_parallel_two_gpus(mg, allreduce):
     import torch
 
