@@ -106,3 +106,31 @@ def test_fused_collect_can_be_switched_between_calls(mg):
         ref[1].collect()
         mixed[1].collect()
         assert_same_rollout(ref, mixed, it)
+
+
+@run_kernel
+@pytest.mark.parametrize("name", ["rollout_test_walk", "rollout_test_glide"])
+def test_fused_collect_of_a_user_environment(mg, tmp_path, name):
+    """A user environment built against the public headers alone (the walk and
+    glide environments of tests/test_env_register.py) runs its own
+    instantiation of the fused kernel: bit-identical to the per-step graph."""
+    import ctypes
+    import subprocess
+
+    from test_env_register import LIB_DIR, NVCC, ROOT, USER_ENV
+
+    src = tmp_path / "walk.cu"
+    src.write_text(USER_ENV)
+    so = tmp_path / "libwalk.so"
+    r = subprocess.run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "--fmad=false",
+                        "-Xcompiler", "-fPIC", "-shared", "-I", str(ROOT / "include"), str(src), "-o", str(so),
+                        "-L", str(LIB_DIR), "-lmetalgym_b200", f"-Xlinker=-rpath,{LIB_DIR}"],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    ctypes.CDLL(str(so))
+    ref = make(name, 640, 2, 8, seed=2)
+    fused = make(name, 640, 2, 8, seed=2, fused=True)
+    for it in range(2):
+        ref[1].collect()
+        fused[1].collect()
+        assert_same_rollout(ref, fused, it)

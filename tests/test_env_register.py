@@ -70,11 +70,59 @@ struct TrailWalk {
     }
 };
 
+// A continuous walk (Gaussian head): the action is a struct of ACT_DIM floats.
+struct Glide {
+    struct State { float x, v; uint32_t t; };
+    struct Action { float push; };
+    struct Obs { float x, v; };
+    static constexpr uint32_t OBS_DIM = 2;
+    static constexpr uint32_t ACT_DIM = 1;
+    static constexpr const char* KERNEL = "rollout_test_glide";
+    __host__ __device__ static void reset(State& s, uint32_t& rng) {
+        s.x = rngUniform(rng, -0.5f, 0.5f);
+        s.v = 0.0f;
+        s.t = 0;
+    }
+    __host__ __device__ static void step(State& s, Action a, Obs& o, float& reward, uint8_t& done) {
+        s.v += 0.05f * fminf(fmaxf(a.push, -1.0f), 1.0f);
+        s.x += s.v;
+        s.t += 1;
+        o.x = s.x;
+        o.v = s.v;
+        reward = -fabsf(s.x);
+        done = s.t >= 100 ? 1 : 0;
+    }
+};
+
+// The eligibility limits: a State of 64 bytes and 32 observations qualify.
+template <int STATE_WORDS, int OBS>
+struct Sized {
+    struct State { float w[STATE_WORDS]; };
+    using Action = int;
+    struct Obs { float o[OBS]; };
+    static constexpr uint32_t OBS_DIM = OBS;
+    static constexpr uint32_t ACT_DIM = 2;
+    static constexpr const char* KERNEL = "rollout_test_sized";
+    __host__ __device__ static void reset(State& s, uint32_t& rng) {
+        for (int i = 0; i < STATE_WORDS; i++) s.w[i] = rngUniform(rng);
+    }
+    __host__ __device__ static void step(State& s, Action a, Obs& o, float& reward, uint8_t& done) {
+        for (int i = 0; i < OBS; i++) o.o[i] = s.w[i % STATE_WORDS] + (float)a;
+        reward = 0.0f;
+        done = 0;
+    }
+};
+
 static_assert(mg::collect_fused_eligible<Walk>(), "a 8-byte State fits in registers");
 static_assert(!mg::collect_fused_eligible<TrailWalk>(), "a 256-byte State is stepped in place");
+static_assert(mg::collect_fused_eligible<Glide>(), "continuous actions are supported");
+static_assert(mg::collect_fused_eligible<Sized<16, 32>>(), "64-byte State, 32 observations");
+static_assert(!mg::collect_fused_eligible<Sized<17, 4>>(), "68-byte State");
+static_assert(!mg::collect_fused_eligible<Sized<4, 33>>(), "33 observations");
 
 MG_REGISTER_ENV(Walk)
 MG_REGISTER_ENV(TrailWalk)
+MG_REGISTER_ENV(Glide)
 """
 
 
@@ -109,6 +157,8 @@ def test_user_environment_registers_with_the_fused_collect(user_env_lib):
     assert EnvOps.from_address(lib.mg_env_find(b"rollout_test_walk")).abi_version == lib.mg_version() == 2
     assert _env_has_fused_collect("rollout_test_walk")
     assert not _env_has_fused_collect("rollout_test_trail_walk")
+    assert _env_ops_info("rollout_test_glide")["continuous"] == 1
+    assert _env_has_fused_collect("rollout_test_glide")
 
 
 def test_builtin_environments_fused_collect_entries():
