@@ -475,6 +475,15 @@ int mg_ppo_set_comm(mg_ppo_t model, void* comm, int rank, int world);
  * in two grouped pairs of calls over the gradient arena's ranges. 0 (the
  * default): one all-reduce. No counterpart in the reference (one GPU). */
 int mg_ppo_set_allreduce_overlap(mg_ppo_t model, int on);
+/* Failure detection for data-parallel train() with an NCCL communicator (no
+ * counterpart in the reference): with seconds > 0, train() / trainSlot()
+ * wait for their work by polling the stream and the communicator's
+ * asynchronous error instead of blocking. When a peer reports an error, or
+ * the work has not finished after `seconds`, the communicator is aborted
+ * (ncclCommAbort: the all-reduce kernels in flight return) and the call
+ * returns MG_ERR_COMM; every later call with that communicator returns
+ * MG_ERR_COMM too. 0 (the default): block until done. */
+int mg_ppo_set_comm_timeout(mg_ppo_t model, float seconds);
 
 /* ---------------------------------------------------------------- NCCL / host memory */
 
@@ -482,6 +491,10 @@ int mg_ppo_set_allreduce_overlap(mg_ppo_t model, int on);
 int mg_comm_unique_id(void* out128);
 int mg_comm_init(int world, int rank, const void* id128, int device, void** comm);
 int mg_comm_destroy(void* comm);
+/* Aborts the communicator and its operations in flight (ncclCommAbort), for
+ * a rank that leaves a data-parallel job. The handle is freed: later
+ * mg_comm_destroy calls on it do nothing. */
+int mg_comm_abort(void* comm);
 int mg_allreduce_sum_f32(float* data, size_t count, void* comm, mg_stream_t stream);
 /* Pinned host memory for the host mirrors of the drop-in API (zeroed). */
 int mg_host_alloc(size_t bytes, void** out);

@@ -85,6 +85,7 @@ SIGNATURES = {
     "mg_ppo_minibatch_rows": (I, [P, PI]),
     "mg_ppo_set_collect_fused": (I, [P, I]),
     "mg_ppo_set_allreduce_overlap": (I, [P, I]),
+    "mg_ppo_set_comm_timeout": (I, [P, F]),
     "mg_ppo_collect_fused": (I, [P, PI]),
     "mg_ppo_train_rows": (I, [P, P, U]),
     "mg_minibatch_rows": (I, [P, U, U, U64, P]),
@@ -105,6 +106,7 @@ SIGNATURES = {
     "mg_comm_unique_id": (I, [P]),
     "mg_comm_init": (I, [I, I, P, I, C.POINTER(P)]),
     "mg_comm_destroy": (I, [P]),
+    "mg_comm_abort": (I, [P]),
     "mg_allreduce_sum_f32": (I, [P, C.c_size_t, P, P]),
     "mg_host_alloc": (I, [C.c_size_t, C.POINTER(P)]),
     "mg_host_free": (I, [P]),

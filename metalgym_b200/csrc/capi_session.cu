@@ -254,6 +254,11 @@ int mg_ppo_minibatch_rows(mg_ppo_t model, int* out) {
     *out = P(model)->mbRows;
     return MG_OK;
 }
+int mg_ppo_set_comm_timeout(mg_ppo_t model, float seconds) {
+    MG_CHECK_ARG(model && seconds >= 0.0f, "mg_ppo_set_comm_timeout: null model or negative timeout");
+    P(model)->commTimeout = seconds;
+    return MG_OK;
+}
 int mg_ppo_set_allreduce_overlap(mg_ppo_t model, int on) {
     MG_CHECK_ARG(model && (on == 0 || on == 1), "mg_ppo_set_allreduce_overlap: null model or on not 0 / 1");
     return P(model)->setAllreduceOverlap(on != 0);
@@ -398,12 +403,25 @@ int mg_comm_init(int world, int rank, const void* id128, int device, void** comm
     ncclComm_t c = nullptr;
     ncclResult_t r = fn(&c, world, id, rank);
     if (r != ncclSuccess) return mg::fail(MG_ERR_COMM, "ncclCommInitRank failed: " + std::to_string((int)r));
+    mg::comm_forget_aborted(c);  // a new communicator, whatever lived at this address before
     *comm = c;
     return MG_OK;
 }
 
+int mg_comm_abort(void* comm) {
+    MG_CHECK_ARG(comm, "mg_comm_abort: null communicator");
+    if (mg::comm_aborted(comm)) return MG_OK;  // the watchdog aborted it already
+    void* h = nccl_handle();
+    if (!h) return mg::fail(MG_ERR_COMM, "libnccl.so.2 not found");
+    auto fn = reinterpret_cast<decltype(&ncclCommAbort)>(dlsym(h, "ncclCommAbort"));
+    if (!fn) return mg::fail(MG_ERR_COMM, "ncclCommAbort not found");
+    mg::comm_mark_aborted(comm);
+    return fn(static_cast<ncclComm_t>(comm)) == ncclSuccess ? MG_OK : mg::fail(MG_ERR_COMM, "ncclCommAbort failed");
+}
+
 int mg_comm_destroy(void* comm) {
     if (!comm) return MG_OK;
+    if (mg::comm_forget_aborted(comm)) return MG_OK;  // ncclCommAbort freed it
     void* h = nccl_handle();
     if (!h) return mg::fail(MG_ERR_COMM, "libnccl.so.2 not found");
     auto fn = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));

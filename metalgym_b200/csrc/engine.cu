@@ -19,17 +19,20 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <sstream>
 #include <string>
+#include <thread>
 
 #include "block.h"
 #include "collect_fused.h"
 #include "gemm.h"
 #include "runtime.h"
+#include "watchdog.h"
 
 namespace mg {
 
@@ -61,6 +64,8 @@ struct Nccl {
     decltype(&ncclGetErrorString) errorString = nullptr;
     decltype(&ncclGroupStart) groupStart = nullptr;
     decltype(&ncclGroupEnd) groupEnd = nullptr;
+    decltype(&ncclCommGetAsyncError) getAsyncError = nullptr;
+    decltype(&ncclCommAbort) commAbort = nullptr;
     bool ok = false;
 };
 
@@ -77,8 +82,10 @@ Nccl& nccl() {
             n.errorString = reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
             n.groupStart = reinterpret_cast<decltype(&ncclGroupStart)>(dlsym(h, "ncclGroupStart"));
             n.groupEnd = reinterpret_cast<decltype(&ncclGroupEnd)>(dlsym(h, "ncclGroupEnd"));
+            n.getAsyncError = reinterpret_cast<decltype(&ncclCommGetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
+            n.commAbort = reinterpret_cast<decltype(&ncclCommAbort)>(dlsym(h, "ncclCommAbort"));
             n.ok = n.getUniqueId && n.commInitRank && n.commDestroy && n.allReduce && n.errorString &&
-                   n.groupStart && n.groupEnd;
+                   n.groupStart && n.groupEnd && n.getAsyncError && n.commAbort;
         }
     });
     return n;
@@ -552,8 +559,65 @@ int PpoEngine::ensureSchedule(int device, int host) {
     return MG_OK;
 }
 
+// Waits for the work on the gym's stream. With an NCCL communicator and a
+// timeout (setCommTimeout), the wait watches the communicator (watchdog.h):
+// a peer's asynchronous error or the deadline aborts it and fails with
+// MG_ERR_COMM instead of blocking for good.
+int PpoEngine::waitStream(const char* what) {
+    cudaStream_t st = gym->stream;
+    if (!(world > 1 && comm && !p2pOn && commTimeout > 0.0f)) {
+        MG_CUDA_TRY(cudaStreamSynchronize(st));
+        return MG_OK;
+    }
+    struct Ctx {
+        cudaStream_t st;
+        ncclComm_t comm;
+        Nccl* nc;
+        cudaError_t err;
+    } c{st, static_cast<ncclComm_t>(comm), &nccl(), cudaSuccess};
+    WatchOps o{};
+    o.ctx = &c;
+    o.done = [](void* p) -> int {
+        Ctx* x = static_cast<Ctx*>(p);
+        const cudaError_t e = cudaStreamQuery(x->st);
+        if (e == cudaSuccess) return 1;
+        if (e == cudaErrorNotReady) return 0;
+        x->err = e;
+        return -1;
+    };
+    o.peerError = [](void* p) -> int {
+        Ctx* x = static_cast<Ctx*>(p);
+        ncclResult_t a = ncclSuccess;
+        if (x->nc->getAsyncError(x->comm, &a) != ncclSuccess) return 1;
+        return a != ncclSuccess && a != ncclInProgress;
+    };
+    o.abort = [](void* p) {
+        Ctx* x = static_cast<Ctx*>(p);
+        x->nc->commAbort(x->comm);
+    };
+    o.now = [](void*) -> double {
+        return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+    };
+    o.pause = [](void*) { std::this_thread::yield(); };
+    bool drained = false;
+    const int r = watch_wait(o, (double)commTimeout, 30.0, &drained);
+    if (r == kWatchDone) return MG_OK;
+    if (r == kWatchCudaError) return cuda_fail(c.err, what);
+    comm_mark_aborted(comm);
+    if (trainExec) {  // it holds the aborted communicator (freed when it completes, if still in flight)
+        cudaGraphExecDestroy(trainExec);
+        trainExec = nullptr;
+    }
+    std::ostringstream m;
+    m << what << ": the gradient all-reduce "
+      << (r == kWatchPeerError ? "failed on a peer" : "did not finish within the communication timeout (")
+      << (r == kWatchPeerError ? "" : std::to_string(commTimeout) + " s)")
+      << "; the communicator was aborted" << (drained ? "" : ", and the stream has not drained");
+    return fail(MG_ERR_COMM, m.str());
+}
+
 int PpoEngine::checkStatus(const char* what) {
-    MG_CUDA_TRY(cudaStreamSynchronize(gym->stream));
+    MG_TRY(waitStream(what));
     int st = 0;
     MG_CUDA_TRY(cudaMemcpy(&st, status_ptr(), sizeof(int), cudaMemcpyDeviceToHost));
     if (st != 0) {
@@ -1019,9 +1083,17 @@ int PpoEngine::setMinibatchRows(int rows) {
     return MG_OK;
 }
 
+// A communicator the watchdog aborted is gone: no further training with it.
+int PpoEngine::commUsable(const char* what) {
+    if (world > 1 && comm && !p2pOn && comm_aborted(comm))
+        return fail(MG_ERR_COMM, std::string(what) + ": the communicator was aborted after a failed all-reduce");
+    return MG_OK;
+}
+
 int PpoEngine::train(int epochs) {
     MG_CHECK_ARG(epochs >= 0, "train: epochs must be >= 0");
     if (epochs == 0) return MG_OK;
+    MG_TRY(commUsable("train"));
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
     const bool rowMode = mbRows > 0;
@@ -1055,6 +1127,7 @@ int PpoEngine::train(int epochs) {
 
 int PpoEngine::trainSlot(int t) {
     MG_CHECK_ARG(t >= 0 && t < T, "trainSlot: slot out of range");
+    MG_TRY(commUsable("trainSlot"));
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
     if (trainBufRows != R) MG_TRY(allocTrain(R));
@@ -1070,6 +1143,7 @@ int PpoEngine::trainSlot(int t) {
 int PpoEngine::trainRows(const uint32_t key[4], uint32_t base) {
     MG_CHECK_ARG(mbRows > 0, "trainRows: set minibatchRows first");
     MG_CHECK_ARG((int64_t)base + mbRows <= (int64_t)T * R, "trainRows: base + minibatchRows exceeds the rollout");
+    MG_TRY(commUsable("trainRows"));
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
     if (trainBufRows != mbRows) MG_TRY(allocTrain(mbRows));
@@ -1360,6 +1434,7 @@ int PpoEngine::setAllreduceOverlap(bool on) {
 int PpoEngine::setComm(void* c, int r, int w) {
     MG_CHECK_ARG(w >= 1 && r >= 0 && r < w, "setComm: bad rank / world size");
     MG_CHECK_ARG(w == 1 || c, "setComm: a communicator is needed for world size > 1");
+    if (c && comm_aborted(c)) return fail(MG_ERR_COMM, "setComm: the communicator was aborted");
     if (w > 1 && !nccl().ok) return fail(MG_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
     comm = c;
     rank = r;

@@ -239,6 +239,7 @@ class PpoEngine {
     P2PTable p2pTable{};
     bool p2pOn = false;
     bool overlapAllreduce = false;  // setAllreduceOverlap
+    float commTimeout = 0.0f;  // seconds; > 0: train() waits through the watchdog (watchdog.h)
     struct ArRanges {
         uint64_t r[2][2];  // [begin, end) element ranges of the gradient arena
     };
@@ -264,6 +265,8 @@ class PpoEngine {
     int allocTrain(int rows);
     void freeTrain();
     int checkStatus(const char* what);
+    int waitStream(const char* what);
+    int commUsable(const char* what);
 };
 
 }  // namespace mg

@@ -2,6 +2,7 @@
 #include "runtime.h"
 
 #include <mutex>
+#include <set>
 #include <string>
 
 namespace mg {
@@ -38,6 +39,27 @@ int fail(int code, const std::string& msg) {
 
 int cuda_fail(cudaError_t e, const char* what) {
     return fail(MG_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+namespace {
+std::mutex g_comm_mu;
+std::set<const void*>& aborted_comms() {
+    static std::set<const void*> s;
+    return s;
+}
+}  // namespace
+
+void comm_mark_aborted(const void* comm) {
+    std::lock_guard<std::mutex> g(g_comm_mu);
+    aborted_comms().insert(comm);
+}
+bool comm_aborted(const void* comm) {
+    std::lock_guard<std::mutex> g(g_comm_mu);
+    return aborted_comms().count(comm) != 0;
+}
+bool comm_forget_aborted(const void* comm) {
+    std::lock_guard<std::mutex> g(g_comm_mu);
+    return aborted_comms().erase(comm) != 0;
 }
 
 int num_sms() {

@@ -32,6 +32,12 @@ int cuda_fail(cudaError_t e, const char* what);
 // Device address of the status word of the current device (a __device__ int
 // in runtime.cu, looked up once per device with cudaGetSymbolAddress).
 int* status_ptr();
+// NCCL communicators aborted by the train() watchdog (ncclCommAbort freed
+// them): their handles must not be used or destroyed again. A new
+// communicator at the same address is not aborted (comm_forget_aborted).
+void comm_mark_aborted(const void* comm);
+bool comm_aborted(const void* comm);
+bool comm_forget_aborted(const void* comm);  // true if it was aborted
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms();
 

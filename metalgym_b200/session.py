@@ -232,6 +232,12 @@ class PPOModel:
         layer's backward runs (mg_ppo_set_allreduce_overlap; NCCL, world > 1)."""
         check(lib().mg_ppo_set_allreduce_overlap(self._h, 1 if on else 0), "allreduce_overlap")
 
+    def set_comm_timeout(self, seconds: float):
+        """Failure detection of data-parallel train() (mg_ppo_set_comm_timeout):
+        > 0 turns an all-reduce that fails on a peer, or does not finish in
+        time, into an error (code 6) after aborting the communicator."""
+        check(lib().mg_ppo_set_comm_timeout(self._h, float(seconds)), "comm_timeout")
+
     def set_comm(self, comm, rank: int, world: int):
         check(lib().mg_ppo_set_comm(self._h, comm, rank, world))
 

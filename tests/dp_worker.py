@@ -174,9 +174,57 @@ def run_gpu(rank, world, local, dist, allreduce):
     return out
 
 
+def run_gpu_rank_leaves(rank, world, local, dist):
+    """Rank 0 trains with a 5 s communication timeout while rank 1 stays out
+    of the all-reduce (it leaves between steps, with nothing in flight): rank
+    0's train() must fail with MG_ERR_COMM (6) well within the deadline
+    instead of blocking, and keep failing; then rank 1 aborts its own
+    communicator. The failure is made on the host; no kernel is broken."""
+    import time
+
+    import torch
+
+    import metalgym_b200
+    from metalgym_b200 import MgError
+    from metalgym_b200.dist import destroy_comm, env_shard, nccl_comm
+    from metalgym_b200.session import Gym, PPOModel
+
+    torch.cuda.set_device(local)
+    R, T = 512, 4
+    gym = Gym("rollout_cartpole", R, seed=0, first_env_id=env_shard(rank, R), device=local)
+    model = PPOModel(gym, 128, 4, 2, 3e-4, T, seed=7)
+    comm = nccl_comm(dist, rank, world, local)
+    model.set_comm(comm, rank, world)
+    model.set_comm_timeout(5.0)
+    model.collect()
+    dist.barrier()
+    out = {}
+    if rank == 0:
+        t0 = time.time()
+        try:
+            model.train(1)
+            out["comm_error"] = False
+        except MgError as e:
+            out["comm_error"] = "code 6" in str(e)
+        out["within_deadline"] = time.time() - t0 < 60.0
+        try:
+            model.train(1)
+            out["second_comm_error"] = False
+        except MgError as e:
+            out["second_comm_error"] = "code 6" in str(e)
+    dist.barrier()  # rank 1 stayed out until rank 0 gave up
+    if rank != 0:
+        metalgym_b200.check(metalgym_b200.lib().mg_comm_abort(comm), "mg_comm_abort")
+        out["aborted"] = True
+    model.close()
+    gym.close()
+    destroy_comm(comm)  # nothing to do for an aborted communicator
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["cpu", "gpu"], required=True)
+    ap.add_argument("--mode", choices=["cpu", "gpu", "gpu-rank-leaves"], required=True)
     ap.add_argument("--allreduce", choices=["nccl", "nccl-overlap", "p2p"], default="nccl")
     args = ap.parse_args()
     import torch.distributed as dist
@@ -185,7 +233,13 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     try:
-        out = run_cpu(rank, world, dist) if args.mode == "cpu" else run_gpu(rank, world, local, dist, args.allreduce)
+        if args.mode == "cpu":
+            out = run_cpu(rank, world, dist)
+        elif args.mode == "gpu":
+            out = run_gpu(rank, world, local, dist, args.allreduce)
+        else:
+            os.environ["NCCL_NVLS_ENABLE"] = "0"  # no NVLink multicast objects when a rank leaves
+            out = run_gpu_rank_leaves(rank, world, local, dist)
         results = [None] * world
         dist.all_gather_object(results, out)
     finally:

@@ -61,3 +61,19 @@ def test_data_parallel_two_gpus(mg, allreduce):
     for r in res["ranks"]:
         assert r["grad_mismatches"] == 0, r
         assert r["ranks_identical"] and r["stats_finite"], r
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(os.environ.get("METALGYM_TEST_COMM_WATCHDOG") != "1",
+                    reason="train() watchdog not yet run on B200s (METALGYM_TEST_COMM_WATCHDOG=1)")
+def test_rank_that_leaves_turns_into_an_error_two_gpus(mg):
+    """A rank that stays out of the gradient all-reduce: the other rank's
+    train() returns MG_ERR_COMM within its communication timeout."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    res = launch("gpu-rank-leaves", limit=180)
+    assert res["ok"], res
+    r0 = res["ranks"][0]
+    assert r0["comm_error"] and r0["within_deadline"] and r0["second_comm_error"], r0
