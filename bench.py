@@ -144,6 +144,10 @@ def run_mine(args, rank, world, local_rank, dist):
             p2p_allreduce(m, dist, rank, world)
 
     if world > 1 and args.allreduce == "nccl":
+        if args.allreduce_overlap:
+            # the overlapped all-reduce runs beside the last backward layer's
+            # kernel (128 CTAs, one per SM): leave it SMs of its own
+            os.environ.setdefault("NCCL_MAX_NCHANNELS", "16")
         comm = nccl_comm(dist, rank, world, local_rank)
     connect(model)
     stream = torch.cuda.ExternalStream(gym.stream(), device=local_rank)
