@@ -477,6 +477,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_collect_fused(const __grid_
             }
         }
         pH ^= 1;
+        __syncwarp();  // the env lanes diverged (padding rows, the sampler's early exit): reconverge
         tc_fence_before();
         cluster_sync();  // every CTA's head product has read its A tile; the observations are staged
         tc_fence_after();
@@ -518,6 +519,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_collect_fused(const __grid_
     tc_fence_before();
     __syncthreads();
     if (warp == 2) {
+        __syncwarp();  // warp 2 may have been an env warp (per-lane GAE loops)
         tc_fence_after();
         tmem_dealloc(tmem, kCfTmemCols);
     }
