@@ -282,7 +282,8 @@ def run_mine(args, rank, world, local_rank, dist):
     # ---- the full loop at the other two configurations (weak scaling per GPU)
     if not args.no_extra_legs:
         for name, cfg in EXTRA_LOOPS.items():
-            legs[name] = extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist)
+            legs[name] = extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist,
+                                        fused_collect=args.collect == "fused")
 
     # ---- dominant kernel, timed live: see profiles/ for the launch-share list
     roof = dominant_kernel_roofline(lib, torch, local_rank, stream)
@@ -331,11 +332,14 @@ EXTRA_LOOPS = {
 }
 
 
-def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist):
+def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist, fused_collect=False):
     """collect() + train(4) at another configuration, device-timed like the
-    headline (CUDA events on the engine stream, L2 flushed between steps)."""
+    headline (CUDA events on the engine stream, L2 flushed between steps).
+    fused_collect: collect() as the persistent kernel where the configuration
+    has one (embed 128 / hidden 512 with a small env state; not VoxelNav)."""
     import torch
 
+    from metalgym_b200 import MgError
     from metalgym_b200.dist import env_shard
     from metalgym_b200.session import Gym, PPOModel
 
@@ -343,6 +347,11 @@ def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist):
     gym = Gym(cfg["env"], n, seed=0, first_env_id=env_shard(rank, n), device=local_rank)
     model = PPOModel(gym, cfg["embed"], cfg["scale"], cfg["blocks"], LR, HORIZON, seed=0)
     model.minibatch_rows = cfg["minibatch"]
+    if fused_collect:
+        try:
+            model.collect_fused = True
+        except MgError:
+            pass  # no fused kernel for this configuration: the per-step graph
     connect(model)
     stream = torch.cuda.ExternalStream(gym.stream(), device=local_rank)
     for _ in range(cfg["warmup"]):
@@ -372,7 +381,8 @@ def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist):
     steps_per_iter = n * HORIZON
     flop = steps_per_iter * ((HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd))
     out = {"value": steps_per_iter * world / (ms / 1e3), "unit": "env steps/s", "ms_per_iteration": ms,
-           "collect_ms": cms, "envs_per_gpu": n, "horizon": HORIZON, "embed": cfg["embed"],
+           "collect_ms": cms, "collect": "fused kernel" if model.collect_fused else "per-step graph",
+           "envs_per_gpu": n, "horizon": HORIZON, "embed": cfg["embed"],
            "hidden": cfg["embed"] * cfg["scale"], "blocks": cfg["blocks"], "epochs": EPOCHS,
            "minibatch_rows": cfg["minibatch"], "minibatches_per_iteration": EPOCHS * steps_per_iter // cfg["minibatch"],
            "steps": cfg["steps"], "warmup": cfg["warmup"],
