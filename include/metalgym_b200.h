@@ -227,6 +227,38 @@ int mg_env_collect_step(const char* kernel_name, const void* head, const void* l
                         void* action_out, float* logp_out, float* value_out, void* obs_out, float* reward_out,
                         uint8_t* done, uint8_t* done_slot, uint32_t* rng, int n, mg_stream_t stream);
 
+/* One whole collect() in the environment's persistent kernel
+ * (mg_env_ops.collect_fused), on caller-owned device buffers in the layouts of
+ * the PPO session (mg_ppo_buffer). Replaces the ~460 dispatches of collect()
+ * (model/ppo.h:716-751): horizon steps of forward, sample, reset-if-done and
+ * step, the bootstrap forward (its head rows into boot_head) and GAE
+ * (model/gae.metal:14-36); not the advantage statistics (mg_advantage_stats).
+ * Policy: embed 128, hidden 512, 1..MG_COLLECT_FUSED_MAX_BLOCKS blocks, bf16
+ * weights. MG_ERR_UNSUPPORTED for an environment without the kernel. */
+#define MG_COLLECT_FUSED_MAX_BLOCKS 4
+typedef struct mg_collect_fused_args {
+    int parallels, horizon, layers, obs_dim;
+    const void* w_in;                                         /* [obs_dim][128] */
+    const void* b_in;                                         /* [128] */
+    const void* ln_gamma[MG_COLLECT_FUSED_MAX_BLOCKS + 1];    /* blocks 0..layers-1, then the final one */
+    const void* ln_beta[MG_COLLECT_FUSED_MAX_BLOCKS + 1];
+    const void* w_up[MG_COLLECT_FUSED_MAX_BLOCKS];            /* [128][512] */
+    const void* w_down[MG_COLLECT_FUSED_MAX_BLOCKS];          /* [512][128] */
+    const void* w_head;                                       /* [128][64] */
+    const void* log_std;                                      /* [act_dim], continuous environments */
+    void* states;                                             /* the environment buffers: read, then */
+    uint8_t* done;                                            /* written back after the last step */
+    uint32_t* rng;
+    float* obs_slots;                                         /* [horizon + 1][parallels][obs_dim]; slot 0 in */
+    void* action_slots;                                       /* [horizon][parallels] actions */
+    float *logp_slots, *value_slots, *reward_slots;           /* [horizon][parallels] */
+    uint8_t* done_slots;
+    float *adv_slots, *ret_slots;
+    void* boot_head;                                          /* [parallels][64] bf16 */
+    float gamma, lambda;
+} mg_collect_fused_args;
+int mg_env_collect_fused(const char* kernel_name, const mg_collect_fused_args* args, mg_stream_t stream);
+
 /* ---------------------------------------------------------------- policy kernels */
 
 /* out[r][c] = bf16(b[c] + sum_k obs[r][k] * W[k][c]); W bf16 [in_dim][out_dim].

@@ -62,6 +62,21 @@ class EnvOps(ctypes.Structure):
                 ("collect_step", ctypes.c_void_p), ("collect_fused", ctypes.c_void_p)]
 
 
+class CollectFusedArgs(ctypes.Structure):
+    """Layout of mg_collect_fused_args (include/metalgym_b200.h)."""
+
+    _fields_ = [("parallels", ctypes.c_int), ("horizon", ctypes.c_int), ("layers", ctypes.c_int),
+                ("obs_dim", ctypes.c_int), ("w_in", ctypes.c_void_p), ("b_in", ctypes.c_void_p),
+                ("ln_gamma", ctypes.c_void_p * 5), ("ln_beta", ctypes.c_void_p * 5),
+                ("w_up", ctypes.c_void_p * 4), ("w_down", ctypes.c_void_p * 4), ("w_head", ctypes.c_void_p),
+                ("log_std", ctypes.c_void_p), ("states", ctypes.c_void_p), ("done", ctypes.c_void_p),
+                ("rng", ctypes.c_void_p), ("obs_slots", ctypes.c_void_p), ("action_slots", ctypes.c_void_p),
+                ("logp_slots", ctypes.c_void_p), ("value_slots", ctypes.c_void_p),
+                ("reward_slots", ctypes.c_void_p), ("done_slots", ctypes.c_void_p), ("adv_slots", ctypes.c_void_p),
+                ("ret_slots", ctypes.c_void_p), ("boot_head", ctypes.c_void_p), ("gamma", ctypes.c_float),
+                ("lambda_", ctypes.c_float)]
+
+
 def _env_ops_info(name: str) -> dict:
     """Sizes and dims of a registered environment."""
     p = lib().mg_env_find(name.encode())

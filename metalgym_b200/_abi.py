@@ -39,6 +39,7 @@ SIGNATURES = {
     "mg_env_init": (I, [S, P, P, P, I, U, U, P]),
     "mg_env_step": (I, [S, P, P, P, P, P, P, P, I, P]),
     "mg_env_run_random": (I, [S, P, P, P, P, P, P, I, I, I, I, P]),
+    "mg_env_collect_fused": (I, [S, P, P]),
     "mg_env_collect_step": (I, [S, P, P, P, P, P, P, P, P, P, P, P, I, P]),
     # policy kernels
     "mg_input_forward": (I, [P, P, P, P, I, I, I, P]),

@@ -4,6 +4,7 @@
 #include <mutex>
 #include <string>
 
+#include "collect_fused.h"
 #include "metalgym/pdl.cuh"
 #include "metalgym/rng.h"
 #include "runtime.h"
@@ -120,6 +121,51 @@ int mg_env_collect_step(const char* kernel_name, const void* head, const void* l
     return rc ? mg::fail(rc, rc == MG_ERR_ARGUMENT ? "mg_env_collect_step: bad arguments"
                                                 : "env collect_step launch failed")
               : MG_OK;
+}
+
+int mg_env_collect_fused(const char* kernel_name, const mg_collect_fused_args* args, mg_stream_t stream) {
+    MG_CHECK_ARG(args, "mg_env_collect_fused: null arguments");
+    const mg_env_ops* o = mg::find_or_fail(kernel_name);
+    if (!o) return MG_ERR_NOT_FOUND;
+    if (!o->collect_fused)
+        return mg::fail(MG_ERR_UNSUPPORTED, std::string("mg_env_collect_fused: '") + kernel_name +
+                                                "' has no fused collect kernel (State over 64 bytes or over 32 "
+                                                "observations)");
+    MG_CHECK_ARG(args->layers >= 1 && args->layers <= MG_COLLECT_FUSED_MAX_BLOCKS,
+                 "mg_env_collect_fused: layers must be in [1, 4]");
+    mg::CollectFusedArgs a{};
+    a.R = args->parallels;
+    a.T = args->horizon;
+    a.L = args->layers;
+    a.inDim = args->obs_dim;
+    a.wIn = args->w_in;
+    a.bIn = args->b_in;
+    for (int l = 0; l <= args->layers; l++) {
+        a.lnGamma[l] = args->ln_gamma[l];
+        a.lnBeta[l] = args->ln_beta[l];
+    }
+    for (int l = 0; l < args->layers; l++) {
+        a.wUp[l] = args->w_up[l];
+        a.wDown[l] = args->w_down[l];
+    }
+    a.wHead = args->w_head;
+    a.logStd = args->log_std;
+    a.states = args->states;
+    a.done = args->done;
+    a.rng = args->rng;
+    a.obsSlots = args->obs_slots;
+    a.actionSlots = args->action_slots;
+    a.logpSlots = args->logp_slots;
+    a.valueSlots = args->value_slots;
+    a.rewardSlots = args->reward_slots;
+    a.doneSlots = args->done_slots;
+    a.advSlots = args->adv_slots;
+    a.retSlots = args->ret_slots;
+    a.bootHead = args->boot_head;
+    a.gamma = args->gamma;
+    a.lambda = args->lambda;
+    MG_CHECK_ARG(!o->continuous || a.logStd, "mg_env_collect_fused: a continuous environment needs log_std");
+    return mg::collect_fused(o, a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -134,3 +134,48 @@ def test_fused_collect_of_a_user_environment(mg, tmp_path, name):
         ref[1].collect()
         fused[1].collect()
         assert_same_rollout(ref, fused, it)
+
+
+@run_kernel
+@pytest.mark.parametrize("name,L", [("rollout_cartpole", 2), ("rollout_cartpole_continuous", 3)])
+def test_c_entry_point_on_session_buffers(mg, name, L):
+    """mg_env_collect_fused on the buffers of a PPO session (weights located
+    by mg_ppo_param_info, slots and env buffers by mg_ppo_buffer /
+    mg_gym_buffer) continues the rollout exactly as the session's own
+    collect() does."""
+    import ctypes
+
+    import metalgym_b200
+    from metalgym_b200 import CollectFusedArgs
+
+    R, T = 768, 6
+    ref = make(name, R, L, T, seed=6)
+    mine = make(name, R, L, T, seed=6)
+    ref[1].collect()
+    mine[1].collect()
+    gym, model = mine
+    # the session's next collect() starts from the last observation slot
+    model.upload("obs", model.download("obs", T), 0)
+    w, _ = model.buffer("weights")
+    par = lambda i: w + 2 * model.param_info(i)[0]  # bf16 weights
+    a = CollectFusedArgs(parallels=R, horizon=T, layers=L, obs_dim=model.obs_dim, gamma=0.99, lambda_=0.95)
+    a.w_in, a.b_in = par(0), par(1)
+    for n in range(L):
+        a.ln_gamma[n], a.ln_beta[n], a.w_up[n], a.w_down[n] = (par(2 + 4 * n + k) for k in range(4))
+    a.ln_gamma[L], a.ln_beta[L], a.w_head = par(2 + 4 * L), par(3 + 4 * L), par(4 + 4 * L)
+    a.log_std = par(5 + 4 * L) if model.continuous else None
+    a.states, a.done, a.rng = (gym.buffer(k)[0] for k in ("states", "done", "rng"))
+    a.obs_slots, a.action_slots, a.logp_slots, a.value_slots = (model.buffer(k)[0]
+                                                                 for k in ("obs", "actions", "logp", "value"))
+    a.reward_slots, a.done_slots, a.adv_slots, a.ret_slots = (model.buffer(k)[0]
+                                                              for k in ("reward", "done", "adv", "ret"))
+    a.boot_head = model.buffer("head")[0]
+    metalgym_b200.check(metalgym_b200.lib().mg_env_collect_fused(name.encode(), ctypes.byref(a), gym.stream()),
+                        "mg_env_collect_fused")
+    gym.synchronize()
+    ref[1].collect()
+    for k in SLOTS:
+        assert np.array_equal(ref[1].slots(k).view(np.uint8), model.slots(k).view(np.uint8)), k
+    assert np.array_equal(ref[1].download("head"), model.download("head"))
+    for k in ("states", "rng", "done"):
+        assert np.array_equal(ref[0].download(k), gym.download(k)), k

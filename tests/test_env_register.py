@@ -169,3 +169,25 @@ def test_builtin_environments_fused_collect_entries():
     assert _env_has_fused_collect("rollout_cartpole")
     assert _env_has_fused_collect("rollout_cartpole_continuous")
     assert not _env_has_fused_collect("rollout_voxelnav")
+
+
+def test_collect_fused_entry_point_checks_before_the_gpu():
+    """mg_env_collect_fused rejects what it cannot run before any CUDA call:
+    an unknown environment (MG_ERR_NOT_FOUND), one without the fused kernel
+    (MG_ERR_UNSUPPORTED), a depth beyond 4 blocks or missing buffers
+    (MG_ERR_ARGUMENT)."""
+    import ctypes
+
+    import metalgym_b200
+    from metalgym_b200 import CollectFusedArgs
+
+    lib = metalgym_b200.lib()
+    a = CollectFusedArgs(parallels=256, horizon=4, layers=2, obs_dim=4, gamma=0.99, lambda_=0.95)
+    assert lib.mg_env_collect_fused(b"no_such_env", ctypes.byref(a), None) == 5
+    v = CollectFusedArgs(parallels=256, horizon=4, layers=4, obs_dim=40, gamma=0.99, lambda_=0.95)
+    assert lib.mg_env_collect_fused(b"rollout_voxelnav", ctypes.byref(v), None) == 3
+    assert b"no fused collect kernel" in lib.mg_last_error()
+    deep = CollectFusedArgs(parallels=256, horizon=4, layers=5, obs_dim=4)
+    assert lib.mg_env_collect_fused(b"rollout_cartpole", ctypes.byref(deep), None) == 1
+    assert lib.mg_env_collect_fused(b"rollout_cartpole", ctypes.byref(a), None) == 1  # no buffers
+    assert b"null" in lib.mg_last_error()
