@@ -496,6 +496,11 @@ int mg_ppo_upload(mg_ppo_t model, int which, int slot, const void* host, size_t 
 /* Kernel launches in one replay of the captured collect() and train() graphs
  * (0 before the first call); no counterpart in the reference. */
 int mg_ppo_graph_kernels(mg_ppo_t model, uint64_t out2[2]);
+/* Device time in ms of the last collect() and the last train() call (CUDA
+ * events around their graph launches; 0 before the first). Each public
+ * operation is also an NVTX range ("mg.collect", "mg.train", "mg.trainSlot",
+ * "mg.forward") for profilers. No counterpart in the reference. */
+int mg_ppo_phase_ms(mg_ppo_t model, float out2[2]);
 /* Data parallelism (no counterpart in the reference): with world > 1 each
  * minibatch's gradient is summed over the ranks of `comm` (an ncclComm_t)
  * and divided by world before the norm clip and Adam. */

@@ -87,6 +87,7 @@ SIGNATURES = {
     "mg_ppo_set_collect_fused": (I, [P, I]),
     "mg_ppo_set_allreduce_overlap": (I, [P, I]),
     "mg_ppo_set_comm_timeout": (I, [P, F]),
+    "mg_ppo_phase_ms": (I, [P, PF]),
     "mg_ppo_collect_fused": (I, [P, PI]),
     "mg_ppo_train_rows": (I, [P, P, U]),
     "mg_minibatch_rows": (I, [P, U, U, U64, P]),

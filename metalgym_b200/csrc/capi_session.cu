@@ -254,6 +254,12 @@ int mg_ppo_minibatch_rows(mg_ppo_t model, int* out) {
     *out = P(model)->mbRows;
     return MG_OK;
 }
+int mg_ppo_phase_ms(mg_ppo_t model, float out2[2]) {
+    MG_CHECK_ARG(model && out2, "mg_ppo_phase_ms: null argument");
+    out2[0] = P(model)->lastCollectMs;
+    out2[1] = P(model)->lastTrainMs;
+    return MG_OK;
+}
 int mg_ppo_set_comm_timeout(mg_ppo_t model, float seconds) {
     MG_CHECK_ARG(model && seconds >= 0.0f, "mg_ppo_set_comm_timeout: null model or negative timeout");
     P(model)->commTimeout = seconds;

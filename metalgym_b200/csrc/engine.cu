@@ -17,6 +17,7 @@
 
 #include <dlfcn.h>
 #include <nccl.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <chrono>
@@ -90,6 +91,14 @@ Nccl& nccl() {
     });
     return n;
 }
+
+// An NVTX range over one public operation (collect, train, ...): profilers
+// (ncu --nvtx, nsys) attribute the kernels launched inside it; without a
+// profiler attached the calls do nothing.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+};
 
 int nccl_fail(ncclResult_t r, const char* what) {
     Nccl& n = nccl();
@@ -279,6 +288,8 @@ PpoEngine::~PpoEngine() {
     if (joinEv) cudaEventDestroy(joinEv);
     for (cudaEvent_t ev : {arLateEv, arEarlyEv, arDoneEv})
         if (ev) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : phaseEv)
+        if (ev) cudaEventDestroy(ev);
     cudaSetDevice(cur);
 }
 
@@ -393,6 +404,7 @@ int PpoEngine::init() {
     MG_CUDA_TRY(cudaEventCreateWithFlags(&joinEv, cudaEventDisableTiming));
     for (cudaEvent_t* ev : {&arLateEv, &arEarlyEv, &arDoneEv})
         MG_CUDA_TRY(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
+    for (cudaEvent_t& ev : phaseEv) MG_CUDA_TRY(cudaEventCreate(&ev));
     MG_TRY(dalloc(&mbAdvStats, 2 * 4));
     MG_TRY(dalloc(&advPartial, (size_t)2 * kAdvStatsMaxCtas * 8));
     MG_TRY(dalloc(&advCounter, 4));
@@ -1015,6 +1027,7 @@ int PpoEngine::captureTrain(int minibatches, bool rowMode) {
 
 // model/ppo.h:716-751
 int PpoEngine::collect() {
+    NvtxRange range("mg.collect");
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
     if (!rolloutStarted) {
@@ -1027,8 +1040,12 @@ int PpoEngine::collect() {
                                     cudaMemcpyDeviceToDevice, st));
     }
     if (!collectExec || !(collectHp == hp)) MG_TRY(captureCollect());
+    MG_CUDA_TRY(cudaEventRecord(phaseEv[0], st));
     MG_CUDA_TRY(cudaGraphLaunch(collectExec, st));
-    return checkStatus("collect");
+    MG_CUDA_TRY(cudaEventRecord(phaseEv[1], st));
+    MG_TRY(checkStatus("collect"));
+    MG_CUDA_TRY(cudaEventElapsedTime(&lastCollectMs, phaseEv[0], phaseEv[1]));
+    return MG_OK;
 }
 
 // Host schedule entry k: the minibatch's rows (a slot, model/ppo.h:918-923,
@@ -1093,6 +1110,7 @@ int PpoEngine::commUsable(const char* what) {
 int PpoEngine::train(int epochs) {
     MG_CHECK_ARG(epochs >= 0, "train: epochs must be >= 0");
     if (epochs == 0) return MG_OK;
+    NvtxRange range("mg.train");
     MG_TRY(commUsable("train"));
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
@@ -1115,6 +1133,7 @@ int PpoEngine::train(int epochs) {
     }
     if (!trainExec || trainExecMinibatches != nmb || trainExecRowMode != rowMode || !(trainHp == hp))
         MG_TRY(captureTrain(nmb, rowMode));
+    MG_CUDA_TRY(cudaEventRecord(phaseEv[2], st));
     for (int e = 0; e < epochs; e++) {
         MG_CUDA_TRY(cudaMemcpyAsync(sched, hostSched + (size_t)e * nmb, (size_t)nmb * sizeof(MgMinibatch),
                                     cudaMemcpyHostToDevice, st));
@@ -1122,11 +1141,15 @@ int PpoEngine::train(int epochs) {
                                     cudaMemcpyHostToDevice, st));
         MG_CUDA_TRY(cudaGraphLaunch(trainExec, st));
     }
-    return checkStatus("train");
+    MG_CUDA_TRY(cudaEventRecord(phaseEv[3], st));
+    MG_TRY(checkStatus("train"));
+    MG_CUDA_TRY(cudaEventElapsedTime(&lastTrainMs, phaseEv[2], phaseEv[3]));
+    return MG_OK;
 }
 
 int PpoEngine::trainSlot(int t) {
     MG_CHECK_ARG(t >= 0 && t < T, "trainSlot: slot out of range");
+    NvtxRange range("mg.trainSlot");
     MG_TRY(commUsable("trainSlot"));
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     cudaStream_t st = gym->stream;
@@ -1156,6 +1179,7 @@ int PpoEngine::trainRows(const uint32_t key[4], uint32_t base) {
 }
 
 int PpoEngine::forward() {
+    NvtxRange range("mg.forward");
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     MG_TRY(forwardOn(static_cast<const float*>(gym->obs), R, collectActs, gym->stream));
     return checkStatus("forward");

@@ -239,6 +239,10 @@ class PpoEngine {
     P2PTable p2pTable{};
     bool p2pOn = false;
     bool overlapAllreduce = false;  // setAllreduceOverlap
+    // device time of the last collect() and train() (CUDA events around their
+    // graph launches, read after the blocking wait)
+    cudaEvent_t phaseEv[4] = {};
+    float lastCollectMs = 0.0f, lastTrainMs = 0.0f;
     float commTimeout = 0.0f;  // seconds; > 0: train() waits through the watchdog (watchdog.h)
     struct ArRanges {
         uint64_t r[2][2];  // [begin, end) element ranges of the gradient arena

@@ -221,6 +221,12 @@ class PPOModel:
     def set_step_counter(self, v: float):
         check(lib().mg_ppo_set_step_counter(self._h, v))
 
+    def phase_ms(self) -> tuple[float, float]:
+        """Device time (ms) of the last collect() and train() (mg_ppo_phase_ms)."""
+        v = (C.c_float * 2)()
+        check(lib().mg_ppo_phase_ms(self._h, v))
+        return float(v[0]), float(v[1])
+
     def graph_kernels(self) -> tuple[int, int]:
         """Kernel launches per replay of the collect and train graphs."""
         v = (C.c_uint64 * 2)()

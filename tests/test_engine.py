@@ -444,3 +444,15 @@ def test_two_host_threads_train_independently(mg):
         for b in ("weights", "master", "obs", "done"):
             assert np.array_equal(together[i][b], alone[i][b]), (cases[i][0], b)
         assert together[i]["stats"] == alone[i]["stats"]
+
+
+def test_phase_times_are_device_times(mg):
+    """mg_ppo_phase_ms: the device time of the last collect() and train()."""
+    _, model = make("rollout_cartpole", 512, 128, 4, 2, 4)
+    assert model.phase_ms() == (0.0, 0.0)
+    model.collect()
+    c0, t0 = model.phase_ms()
+    assert 0.0 < c0 < 5000.0 and t0 == 0.0
+    model.train(1)
+    c1, t1 = model.phase_ms()
+    assert c1 == c0 and 0.0 < t1 < 5000.0
