@@ -282,6 +282,8 @@ def run_mine(args, rank, world, local_rank, dist):
     # ---- the full loop at the other two configurations (weak scaling per GPU)
     if not args.no_extra_legs:
         for name, cfg in EXTRA_LOOPS.items():
+            if args.c4_action == "tanh" and cfg["env"] == "rollout_cartpole_continuous":
+                cfg = dict(cfg, env="rollout_cartpole_continuous_tanh")
             legs[name] = extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist,
                                         fused_collect=args.collect == "fused")
 
@@ -380,7 +382,8 @@ def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist, fused_col
     fwd, bwd = flops_per_row(model.obs_dim, model.act_dim, cfg["embed"], cfg["embed"] * cfg["scale"], cfg["blocks"])
     steps_per_iter = n * HORIZON
     flop = steps_per_iter * ((HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd))
-    out = {"value": steps_per_iter * world / (ms / 1e3), "unit": "env steps/s", "ms_per_iteration": ms,
+    out = {"value": steps_per_iter * world / (ms / 1e3), "unit": "env steps/s", "env": cfg["env"],
+           "ms_per_iteration": ms,
            "collect_ms": cms, "collect": "fused kernel" if model.collect_fused else "per-step graph",
            "envs_per_gpu": n, "horizon": HORIZON, "embed": cfg["embed"],
            "hidden": cfg["embed"] * cfg["scale"], "blocks": cfg["blocks"], "epochs": EPOCHS,
@@ -657,6 +660,9 @@ def main():
     ap.add_argument("--allreduce-overlap", action="store_true",
                     help="N > 1 with NCCL: all-reduce all but the last backward layer's gradients on a side "
                          "stream while that layer's backward runs (default: one all-reduce after the backward)")
+    ap.add_argument("--c4-action", choices=["clamp", "tanh"], default="clamp",
+                    help="configs[3] leg: the reference code's clamped force (default) or the BASELINE text's "
+                         "tanh-squashed one (rollout_cartpole_continuous_tanh)")
     ap.add_argument("--collect", choices=["graph", "fused"], default="graph",
                     help="collect() of the headline loop: the captured per-step graph (default) or the one "
                          "persistent kernel of collect_fused.cu")

@@ -1,4 +1,4 @@
-// Project-owned single-precision transcendentals: sin, cos, exp, log.
+// Project-owned single-precision transcendentals: sin, cos, exp, tanh, log.
 //
 // Why they exist: environment dynamics (cos/sin in the cart-pole step, the
 // ray directions of the voxel camera), the categorical sampler (exp/log) and
@@ -154,6 +154,40 @@ MG_HD inline float mg_expf(float xf) {
     p = fma(p, r, 1.0);
     p = fma(p, r, 1.0);
     return (float)ldexp(p, (int)k);
+}
+
+// tanh x = sign(x) E / (E + 2) with E = e^(2|x|) - 1, which has no
+// cancellation for small |x|: 2|x| = k ln2 + r, |r| <= ln2/2, e^r - 1 = r (1 +
+// r/2! + ... + r^12/14!) by Taylor, E = 2^k (e^r - 1) + (2^k - 1). Beyond
+// |x| = 20, tanh x rounds to +-1 in float.
+MG_HD inline float mg_tanhf(float xf) {
+    using namespace mg_math;
+    if (xf != xf || xf == 0.0f) return xf;  // NaN, and +-0 keeps its sign
+    const double ax = xf < 0.0f ? -(double)xf : (double)xf;
+    if (ax > 20.0) return xf < 0.0f ? -1.0f : 1.0f;
+    const double y = 2.0 * ax;
+    const double k = rint(y * INV_LN2);
+    double r = fma(-k, LN2_HI, y);
+    r = fma(-k, LN2_LO, r);
+    double p = F14;
+    p = fma(p, r, F13);
+    p = fma(p, r, F12);
+    p = fma(p, r, F11);
+    p = fma(p, r, F10);
+    p = fma(p, r, F9);
+    p = fma(p, r, F8);
+    p = fma(p, r, F7);
+    p = fma(p, r, F6);
+    p = fma(p, r, F5);
+    p = fma(p, r, F4);
+    p = fma(p, r, F3);
+    p = fma(p, r, F2);
+    p = fma(p, r, 1.0);
+    const double em1 = p * r;  // e^r - 1
+    const double sk = ldexp(1.0, (int)k);
+    const double e = fma(sk, em1, sk - 1.0);
+    const double t = e / (e + 2.0);
+    return (float)(xf < 0.0f ? -t : t);
 }
 
 // ln x: x = 2^e m with m in [sqrt(1/2), sqrt(2)), s = (m-1)/(m+1),

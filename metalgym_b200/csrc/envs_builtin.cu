@@ -1,6 +1,7 @@
 // The three example environments of the reference (CartPole,
 // CartPoleContinuous, VoxelNav), registered under their reference kernel
-// names. Compiled with --fmad=false (see metalgym_b200/build.py).
+// names, and the tanh-squashed CartPoleContinuous of the BASELINE text
+// (rollout_cartpole_continuous_tanh). Compiled with --fmad=false (see metalgym_b200/build.py).
 #include "metalgym/envs/cartpole.h"
 #include "metalgym/envs/cartpole_continuous.h"
 #include "metalgym/envs/voxelnav.h"
@@ -8,4 +9,5 @@
 
 MG_REGISTER_ENV(CartPole)
 MG_REGISTER_ENV(CartPoleContinuous)
+MG_REGISTER_ENV(CartPoleContinuousTanh)
 MG_REGISTER_ENV(VoxelNav)

@@ -35,6 +35,7 @@ extern "C" __attribute__((visibility("default"))) void hostenv_rollout(int which
         case 0: run<CartPole>(states, actions, obs, reward, done, rng, n, threads); break;
         case 1: run<CartPoleContinuous>(states, actions, obs, reward, done, rng, n, threads); break;
         case 2: run<VoxelNav>(states, actions, obs, reward, done, rng, n, threads); break;
+        case 3: run<CartPoleContinuousTanh>(states, actions, obs, reward, done, rng, n, threads); break;
     }
 }
 
@@ -42,3 +43,4 @@ extern "C" __attribute__((visibility("default"))) float hostenv_sinf(float x) { 
 extern "C" __attribute__((visibility("default"))) float hostenv_cosf(float x) { return mg_cosf(x); }
 extern "C" __attribute__((visibility("default"))) float hostenv_expf(float x) { return mg_expf(x); }
 extern "C" __attribute__((visibility("default"))) float hostenv_logf(float x) { return mg_logf(x); }
+extern "C" __attribute__((visibility("default"))) float hostenv_tanhf(float x) { return mg_tanhf(x); }

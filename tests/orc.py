@@ -121,7 +121,7 @@ def load_hostenv():
                         "-I", str(ROOT / "include"), str(src), "-o", str(HOSTENV_LIB)], check=True)
     lib = C.CDLL(str(HOSTENV_LIB))
     _sig(lib, "hostenv_rollout", None, [I, P, P, P, P, P, P, U, I])
-    for n in ("hostenv_sinf", "hostenv_cosf", "hostenv_expf", "hostenv_logf"):
+    for n in ("hostenv_sinf", "hostenv_cosf", "hostenv_expf", "hostenv_logf", "hostenv_tanhf"):
         _sig(lib, n, F, [F])
     return lib
 
