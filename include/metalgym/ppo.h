@@ -230,6 +230,17 @@ struct PPOModel {
     void setComm(void* comm, int rank, int world) {
         metalgym::check_or_exit(mg_ppo_set_comm(handle, comm, rank, world), "setComm");
     }
+    // Extensions of data-parallel training (mg_ppo_set_allreduce_overlap,
+    // mg_ppo_set_comm_timeout): the gradient all-reduce overlapped with the
+    // last backward layer; a timeout after which a failed or missing peer
+    // makes train() fail with MG_ERR_COMM (printed, then exit) instead of
+    // blocking for good.
+    void setAllreduceOverlap(bool on) {
+        metalgym::check_or_exit(mg_ppo_set_allreduce_overlap(handle, on ? 1 : 0), "setAllreduceOverlap");
+    }
+    void setCommTimeout(float seconds) {
+        metalgym::check_or_exit(mg_ppo_set_comm_timeout(handle, seconds), "setCommTimeout");
+    }
     // Extension: collect() as one persistent kernel (mg_ppo_set_collect_fused;
     // environments with a State of at most 64 bytes and at most 32
     // observations, embed 128, hidden 512).
