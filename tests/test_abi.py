@@ -129,3 +129,16 @@ def test_null_pointers_are_argument_errors():
         if rc != 1 or not msg:
             wrong[name] = (rc, msg.decode(errors="replace"))
     assert not wrong, wrong
+
+
+def test_header_is_plain_c(tmp_path):
+    """include/metalgym_b200.h is a C header (hosts bind it through C FFIs):
+    it compiles as C99 with every warning an error."""
+    import subprocess
+
+    src = tmp_path / "use.c"
+    src.write_text('#include "metalgym_b200.h"\nint main(void) {\n    mg_collect_fused_args a = {0};\n'
+                   '    mg_env_ops o = {0};\n    (void)a; (void)o;\n    return mg_version() == MG_VERSION ? 0 : 1;\n}\n')
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", str(ROOT / "include"),
+                        "-fsyntax-only", str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
