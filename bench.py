@@ -219,7 +219,15 @@ def run_mine(args, rank, world, local_rank, dist):
             ce[k].record(stream)
     torch.cuda.synchronize()
     cms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(cs, ce)) / args.steps, dist)
-    legs["collect"] = {"value": steps_per_iter * world / (cms / 1e3), "ms_per_call": cms}
+    # its roofline: the T + 1 policy forwards' algorithmic FLOPs per collect() over its device time
+    # (latency bound at 4096 envs: the fraction says how far from the tensor roof, not the bound)
+    c_fwd, _ = flops_per_row(4, 2, EMBED, EMBED * SCALE, LAYERS)
+    c_flop = ENVS_PER_GPU * (HORIZON + 1) * c_fwd
+    _, c_peak, c_kind = measured_peaks()
+    legs["collect"] = {"value": steps_per_iter * world / (cms / 1e3), "ms_per_call": cms,
+                       "path": "one persistent kernel (fused)" if model.collect_fused else "captured per-step graph",
+                       "flop_per_call": c_flop, "achieved_tflops": c_flop / (cms / 1e3) / 1e12,
+                       "tensor_frac": c_flop / (cms / 1e3) / 1e12 / c_peak, "peak_kind": c_kind}
     legs["full_loop"] = {"value": value, "ms_per_iteration": ms}
 
     # ---- raw env step (config 1): fused multi-step kernel and the gym.run loop
