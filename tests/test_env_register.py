@@ -191,3 +191,14 @@ def test_collect_fused_entry_point_checks_before_the_gpu():
     assert lib.mg_env_collect_fused(b"rollout_cartpole", ctypes.byref(deep), None) == 1
     assert lib.mg_env_collect_fused(b"rollout_cartpole", ctypes.byref(a), None) == 1  # no buffers
     assert b"null" in lib.mg_last_error()
+    # every buffer given, but the head rows (stored as 16-byte vectors) misaligned
+    for f in ("w_in", "b_in", "w_head", "states", "done", "rng", "obs_slots", "action_slots", "logp_slots",
+              "value_slots", "reward_slots", "done_slots", "adv_slots", "ret_slots"):
+        setattr(a, f, 0x10000)
+    for i in range(3):
+        a.ln_gamma[i] = a.ln_beta[i] = 0x10000
+    for i in range(2):
+        a.w_up[i] = a.w_down[i] = 0x10000
+    a.boot_head = 0x10008
+    assert lib.mg_env_collect_fused(b"rollout_cartpole", ctypes.byref(a), None) == 1
+    assert b"16-byte aligned" in lib.mg_last_error()
