@@ -5,6 +5,7 @@
 //       -L metalgym_b200 -lmetalgym_b200 -Wl,-rpath,<repo>/metalgym_b200 -o cartpole
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 
 #include "gym.h"
 #include "model/ppo.h"
@@ -23,11 +24,13 @@ struct CartPoleHost {
     static constexpr const char* KERNEL = "rollout_cartpole";
 };
 
+// usage: cartpole [iterations] [fused]   ("fused": collect() as one persistent kernel)
 int main(int argc, char** argv) {
     const uint32_t envs = 4096, horizon = 32;
     const int iterations = argc > 1 ? std::atoi(argv[1]) : 40;
     Gym<CartPoleHost> gym(envs);
     PPOModel<CartPoleHost> model(gym, 128, 4, 2, 3e-4f, horizon);
+    if (argc > 2 && std::strcmp(argv[2], "fused") == 0) model.setFusedCollect(true);
     for (int it = 0; it < iterations; it++) {
         model.collect();
         uint64_t ended = 0;
