@@ -1011,8 +1011,10 @@ int PpoEngine::captureTrain(int minibatches, bool rowMode) {
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "train capture");
-    // this library's kernels: the NCCL all-reduce adds one NCCL kernel per minibatch
-    trainKernels = count_kernel_nodes(graph) - (world > 1 && !p2pOn ? (size_t)minibatches : 0);
+    // this library's kernels: the NCCL all-reduce adds one NCCL kernel per
+    // minibatch (two, one per grouped half, when overlapped)
+    const size_t ncclPerMinibatch = world > 1 && !p2pOn ? (overlapAllreduce ? 2 : 1) : 0;
+    trainKernels = count_kernel_nodes(graph) - ncclPerMinibatch * (size_t)minibatches;
     cudaGraphExec_t exec = nullptr;
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
