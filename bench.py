@@ -128,8 +128,8 @@ def run_mine(args, rank, world, local_rank, dist):
     lib = metalgym_b200.lib()
     gym = Gym(ENV, ENVS_PER_GPU, seed=0, first_env_id=env_shard(rank, ENVS_PER_GPU), device=local_rank)
     model = PPOModel(gym, EMBED, SCALE, LAYERS, LR, HORIZON, seed=0)
-    if args.collect == "fused":
-        model.collect_fused = True
+    if args.collect != "auto":
+        model.collect_fused = args.collect == "fused"
     comm = None
 
     def connect(m):
@@ -292,32 +292,27 @@ def run_mine(args, rank, world, local_rank, dist):
         for name, cfg in EXTRA_LOOPS.items():
             if args.c4_action == "tanh" and cfg["env"] == "rollout_cartpole_continuous":
                 cfg = dict(cfg, env="rollout_cartpole_continuous_tanh")
-            legs[name] = extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist,
-                                        fused_collect=args.collect == "fused")
+            legs[name] = extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist, collect=args.collect)
 
     # ---- dominant kernel, timed live: see profiles/ for the launch-share list
     roof = dominant_kernel_roofline(lib, torch, local_rank, stream)
 
     result = None
     if rank == 0:
-        fwd, bwd = flops_per_row(4, 2, EMBED, EMBED * SCALE, LAYERS)
         result = {
             "metric": METRIC, "value": value, "unit": "env steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": value / REFERENCE_M4_FULL_LOOP, "dtype": "bf16", "data": "synthetic (simulated CartPole)",
-            "config": {"workload": "CartPole full PPO loop (BASELINE configs[2]): collect() + train(4) per step",
-                       "envs_per_gpu": ENVS_PER_GPU, "horizon": HORIZON, "embed": EMBED,
-                       "hidden": EMBED * SCALE, "blocks": LAYERS, "epochs": EPOCHS,
-                       "minibatch": "one slot (4096 rows)", "parallelism": f"dp{world}",
-                       "collect": ("one persistent kernel (fused)" if args.collect == "fused" else
-                                   "captured per-step graph"),
-                       "allreduce": ("none" if world == 1 else
-                                     "NVLink peer memory (library kernels)" if args.allreduce == "p2p" else
-                                     "NCCL, overlapped with the last backward layer" if args.allreduce_overlap else
-                                     "NCCL"),
-                       "l2": "flushed between timed steps (256 MiB write, outside the events)",
-                       "env_steps_per_step": steps_per_iter * world,
-                       "flop_per_env_step": (HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd)},
+            "config": workload_config(world),
+            "setup": {"collect": ("one persistent kernel (fused)" if model.collect_fused else
+                                  "captured per-step graph"),
+                      "allreduce": ("none" if world == 1 else
+                                    "NVLink peer memory (library kernels)" if args.allreduce == "p2p" else
+                                    "NCCL, overlapped with the last backward layer" if args.allreduce_overlap else
+                                    "NCCL"),
+                      "timing": "CUDA events on the engine stream, max over ranks"},
+            "raw_env_steps_per_s": legs["raw_env"]["value"],
+            "collect_env_steps_per_s": legs["collect"]["value"],
             "legs": legs, "e2e": e2e, "roofline": roof,
             "gpu_launches": args.steps * (collect_k + EPOCHS * train_k),
             "gpu_launches_per_step": {"collect_graph": collect_k, "train_graph_per_epoch": train_k,
@@ -332,6 +327,17 @@ def run_mine(args, rank, world, local_rank, dist):
     return result
 
 
+def workload_config(world):
+    """The headline workload, identical in both arms' JSON lines."""
+    fwd, bwd = flops_per_row(4, 2, EMBED, EMBED * SCALE, LAYERS)
+    return {"workload": "CartPole full PPO loop (BASELINE configs[2]): collect() + train(4) per step",
+            "envs_per_gpu": ENVS_PER_GPU, "horizon": HORIZON, "embed": EMBED, "hidden": EMBED * SCALE,
+            "blocks": LAYERS, "epochs": EPOCHS, "minibatch": "one slot (4096 rows)", "parallelism": f"dp{world}",
+            "l2": "GPU arm: flushed between timed steps (256 MiB write, outside the events)",
+            "env_steps_per_step": ENVS_PER_GPU * HORIZON * world,
+            "flop_per_env_step": (HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd)}
+
+
 # BASELINE configs[3] and configs[4]: (env, envs per GPU, embed, scale, blocks,
 # minibatch rows, timed iterations, warm-up iterations)
 EXTRA_LOOPS = {
@@ -342,11 +348,12 @@ EXTRA_LOOPS = {
 }
 
 
-def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist, fused_collect=False):
+def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist, collect="auto"):
     """collect() + train(4) at another configuration, device-timed like the
     headline (CUDA events on the engine stream, L2 flushed between steps).
-    fused_collect: collect() as the persistent kernel where the configuration
-    has one (embed 128 / hidden 512 with a small env state; not VoxelNav)."""
+    collect: "fused" runs collect() as the persistent kernel where the
+    configuration has one (embed 128 / hidden 512 with a small env state; not
+    VoxelNav), "graph" as the per-step graph, "auto" as the library chooses."""
     import torch
 
     from metalgym_b200 import MgError
@@ -357,9 +364,9 @@ def extra_loop_leg(cfg, rank, world, local_rank, connect, flush, dist, fused_col
     gym = Gym(cfg["env"], n, seed=0, first_env_id=env_shard(rank, n), device=local_rank)
     model = PPOModel(gym, cfg["embed"], cfg["scale"], cfg["blocks"], LR, HORIZON, seed=0)
     model.minibatch_rows = cfg["minibatch"]
-    if fused_collect:
+    if collect != "auto":
         try:
-            model.collect_fused = True
+            model.collect_fused = collect == "fused"
         except MgError:
             pass  # no fused kernel for this configuration: the per-step graph
     connect(model)
@@ -518,7 +525,8 @@ def cpu_full_loop(seconds_budget=20.0, threads=None):
     from source (oracle/_ref) and the C++ restatement of its PPO arithmetic,
     OpenMP over rows on all host cores. Bounded sample: one collect() (the
     whole T-step rollout of 4096 envs) and as many of the 128 minibatches as
-    fit in the budget; the iteration time is extrapolated to 128 minibatches."""
+    fit in the budget; the iteration time is extrapolated to 128 minibatches
+    (wall_s: the sample's own wall time)."""
     sys.path.insert(0, str(ROOT / "tests"))
     from orc import load_hostenv, load_oracle, load_ref, ptr, seed_words  # noqa: F401
 
@@ -555,7 +563,8 @@ def cpu_full_loop(seconds_budget=20.0, threads=None):
         n_mb += 1
     orc.orc_model_destroy(m)
     per_iter = t_collect + (t_mb / n_mb) * EPOCHS * T
-    return {"value": R * T / per_iter, "unit": "env steps/s", "cores": threads,
+    return {"value": R * T / per_iter, "unit": "env steps/s", "cores": threads, "wall_s": t_collect + t_mb,
+            "iteration_s_extrapolated": per_iter,
             "kind": "reference" if ref is not None else "port",
             "sample": f"1 collect (4096 envs x 32 steps, {t_collect:.2f} s) + {n_mb} of 128 minibatches "
                       f"({t_mb / n_mb:.3f} s each), iteration time extrapolated",
@@ -564,24 +573,32 @@ def cpu_full_loop(seconds_budget=20.0, threads=None):
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU path on this box's host cores."""
+    """--impl reference: the reference's CPU path on this box's host cores.
+
+    A whole iteration of that path takes about 20 s on 16 cores, so each step
+    here is a bounded sample of one iteration (one collect() and as many
+    minibatches as fit in ~8 s; cpu_full_loop), and the line says so: `steps`
+    and `warmup` are the samples actually run, `ms_per_step` is a sample's
+    measured wall time, and `value` is the env-step rate of the whole
+    iteration extrapolated from each sample (median over the samples)."""
     if rank != 0:
         return None
-    vals = []
-    for _ in range(max(1, min(args.steps, 3))):
-        vals.append(cpu_full_loop(seconds_budget=15.0)["value"])
-    base = cpu_full_loop(seconds_budget=5.0)
-    v = statistics.median(vals)
-    fwd, bwd = flops_per_row(4, 2, EMBED, EMBED * SCALE, LAYERS)
+    n_warm, n_timed = 1, max(1, min(args.steps, 3))
+    for _ in range(n_warm):
+        cpu_full_loop(seconds_budget=3.0)
+    runs = [cpu_full_loop(seconds_budget=8.0) for _ in range(n_timed)]
+    v = statistics.median(r["value"] for r in runs)
+    wall_ms = 1e3 * statistics.mean(r["wall_s"] for r in runs)
+    base = runs[len(runs) // 2]
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": "env steps/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ENVS_PER_GPU * HORIZON / v * 1e3,
+            "steps": n_timed, "warmup": n_warm, "ms_per_step": wall_ms,
+            "ms_per_step_kind": "wall time of one bounded sample (a collect() plus some of the 128 minibatches)",
+            "ms_per_iteration_extrapolated": ENVS_PER_GPU * HORIZON / v * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": v / REFERENCE_M4_FULL_LOOP, "dtype": "bf16",
             "data": "synthetic (simulated CartPole)",
-            "config": {"workload": "CartPole full PPO loop (BASELINE configs[2]): collect() + train(4) per step",
-                       "envs_per_gpu": ENVS_PER_GPU, "horizon": HORIZON, "embed": EMBED, "hidden": EMBED * SCALE,
-                       "blocks": LAYERS, "epochs": EPOCHS, "minibatch": "one slot (4096 rows)",
-                       "parallelism": "host cores (OpenMP)",
-                       "flop_per_env_step": (HORIZON + 1) / HORIZON * fwd + EPOCHS * (fwd + bwd)},
+            "config": workload_config(world),
+            "setup": {"arm": "the reference's CPU path on the host cores (OpenMP), rank 0 only",
+                      "requested_steps": args.steps, "requested_warmup": args.warmup},
             "cpu_baseline": {"value": v, "unit": "env steps/s", "cores": base["cores"], "kind": base["kind"],
                              "sample": base["sample"]},
             "e2e": {"value": v, "unit": "env steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -661,19 +678,18 @@ def main():
     ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-legs", action="store_true", help="skip the configs[3] / configs[4] loops")
-    ap.add_argument("--allreduce", choices=["auto", "nccl", "p2p"], default="auto",
-                    help="N > 1: gradient all-reduce with NCCL or the library's own kernel over NVLink peer "
-                         "memory; auto (default): peer memory at 2 GPUs (12.9 against 13.4 ms per CartPole "
-                         "iteration), NCCL above (faster at 8 GPUs: 19.8 against 22.6 ms)")
+    ap.add_argument("--allreduce", choices=["nccl", "p2p"], default="nccl",
+                    help="N > 1: gradient all-reduce with NCCL (default, at every N) or the library's own "
+                         "kernel over NVLink peer memory")
     ap.add_argument("--allreduce-overlap", action="store_true",
                     help="N > 1 with NCCL: all-reduce all but the last backward layer's gradients on a side "
                          "stream while that layer's backward runs (default: one all-reduce after the backward)")
     ap.add_argument("--c4-action", choices=["clamp", "tanh"], default="clamp",
                     help="configs[3] leg: the reference code's clamped force (default) or the BASELINE text's "
                          "tanh-squashed one (rollout_cartpole_continuous_tanh)")
-    ap.add_argument("--collect", choices=["graph", "fused"], default="graph",
-                    help="collect() of the headline loop: the captured per-step graph (default) or the one "
-                         "persistent kernel of collect_fused.cu")
+    ap.add_argument("--collect", choices=["auto", "graph", "fused"], default="auto",
+                    help="collect(): the library's choice (default: the persistent kernel of collect_fused.cu "
+                         "where it applies, up to 4096 envs), the captured per-step graph, or the kernel")
     ap.add_argument("--profile-minibatch", choices=["c3", "c4", "c5"],
                     help="profiling driver: one training minibatch and one forward of that configuration, "
                          "bracketed by cudaProfilerStart / Stop (for ncu --profile-from-start off); no JSON line")
@@ -683,8 +699,6 @@ def main():
         return
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.allreduce == "auto":
-        args.allreduce = "p2p" if world == 2 else "nccl"
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     dist = None

@@ -489,16 +489,33 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_collect_fused(const __grid_
         float lastAdv = 0.0f;
         float nextValue = bootValue;
         const float gl = __fmul_rn(p.gamma, p.lambda);
-        for (int t = T - 1; t >= 0; t--) {
-            const size_t k = (size_t)t * R + envRow;
-            const float nonTerminal = p.doneSlots[k] ? 0.0f : 1.0f;
-            const float val = p.valueSlots[k];
-            const float delta =
-                __fsub_rn(__fadd_rn(p.rewardSlots[k], __fmul_rn(__fmul_rn(p.gamma, nextValue), nonTerminal)), val);
-            lastAdv = __fadd_rn(delta, __fmul_rn(__fmul_rn(gl, nonTerminal), lastAdv));
-            p.advSlots[k] = lastAdv;
-            p.retSlots[k] = __fadd_rn(lastAdv, val);
-            nextValue = val;
+        // slots in chunks of 8, newest first, each chunk's loads issued
+        // together before its part of the (unchanged) serial recurrence
+        constexpr int kChunk = 8;
+        for (int t = T - 1; t >= 0; t -= kChunk) {
+            float rw[kChunk], vl[kChunk];
+            uint8_t dn[kChunk];
+#pragma unroll
+            for (int j = 0; j < kChunk; j++) {
+                if (t - j < 0) break;
+                const size_t k = (size_t)(t - j) * R + envRow;
+                rw[j] = p.rewardSlots[k];
+                vl[j] = p.valueSlots[k];
+                dn[j] = p.doneSlots[k];
+            }
+#pragma unroll
+            for (int j = 0; j < kChunk; j++) {
+                if (t - j < 0) break;
+                const size_t k = (size_t)(t - j) * R + envRow;
+                const float nonTerminal = dn[j] ? 0.0f : 1.0f;
+                const float val = vl[j];
+                const float delta =
+                    __fsub_rn(__fadd_rn(rw[j], __fmul_rn(__fmul_rn(p.gamma, nextValue), nonTerminal)), val);
+                lastAdv = __fadd_rn(delta, __fmul_rn(__fmul_rn(gl, nonTerminal), lastAdv));
+                p.advSlots[k] = lastAdv;
+                p.retSlots[k] = __fadd_rn(lastAdv, val);
+                nextValue = val;
+            }
         }
         static_cast<State*>(p.states)[envRow] = s;
         p.rng[envRow] = w;

@@ -158,7 +158,7 @@ MG_HD inline float mg_expf(float xf) {
 
 // tanh x = sign(x) E / (E + 2) with E = e^(2|x|) - 1, which has no
 // cancellation for small |x|: 2|x| = k ln2 + r, |r| <= ln2/2, e^r - 1 = r (1 +
-// r/2! + ... + r^12/14!) by Taylor, E = 2^k (e^r - 1) + (2^k - 1). Beyond
+// r/2! + ... + r^13/14!) by Taylor, E = 2^k (e^r - 1) + (2^k - 1). Beyond
 // |x| = 20, tanh x rounds to +-1 in float.
 MG_HD inline float mg_tanhf(float xf) {
     using namespace mg_math;

@@ -11,10 +11,10 @@
 // is done, as in the reference.
 //
 // The policy, sampler, GAE and PPO update run on the GPU (one CUDA graph per
-// collect() and per train()); act() and actGreedy() stay host code with the
-// caller's RNG, exactly as model/ppo.h:636-702. Slot accessors and
-// headValue() read pinned host mirrors refreshed after device work (see
-// gym.h). Extensions: no compile-time N_EMBED_CFG (embed 64/128/256/512),
+// collect() and per train()); act() stays host code with the caller's RNG,
+// exactly as model/ppo.h:636-686, and actGreedy() runs on the device. Slot
+// accessors and headValue() read pinned host mirrors refreshed after device
+// work (see gym.h). Extensions: no compile-time N_EMBED_CFG (embed 64/128/256/512),
 // setComm() for data parallelism over NCCL, save() / load() checkpoints of the
 // training state, and the field minibatchRows
 // (0, the default, keeps the reference's one-slot minibatches; B > 0 trains
@@ -22,6 +22,7 @@
 // order).
 #pragma once
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -30,6 +31,76 @@
 #include <vector>
 
 #include "gym.h"
+
+namespace metalgym {
+
+inline float bf16_bits_to_float(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// act(rng) of model/ppo.h:636-686 over head rows [parallels][64] (bf16
+// bits): per row a categorical draw from the logits with the caller's host
+// generator (std::uniform_real_distribution, inverse CDF over the softmax
+// weights) or ACT_DIM Gaussian draws around the means with log-std logStd
+// (std::normal_distribution), the log-probability of the drawn action and
+// the value column. The same calls of the same distributions in the same
+// order as the reference, so the same generator state gives the same
+// actions.
+template <typename Env, typename Rng>
+void sample_actions_host(const uint16_t* head, uint32_t parallels, const float* logStd, Rng& rng,
+                         typename Env::Action* action, float* value, float* logProb) {
+    constexpr uint32_t kHead = 64;
+    if constexpr (!std::is_integral_v<typename Env::Action>) {
+        std::normal_distribution<float> normal(0.0f, 1.0f);
+        float* actionF = reinterpret_cast<float*>(action);
+        for (uint32_t row = 0; row < parallels; ++row) {
+            const uint16_t* h = head + (size_t)row * kHead;
+            float lp = 0.0f;
+            for (uint32_t k = 0; k < Env::ACT_DIM; ++k) {
+                const float ls = logStd[k];
+                const float mu = bf16_bits_to_float(h[k]);
+                const float a = mu + std::exp(ls) * normal(rng);
+                const float d = (a - mu) * std::exp(-ls);
+                actionF[(size_t)row * Env::ACT_DIM + k] = a;
+                lp += -0.5f * d * d - ls - 0.9189385332046727f;
+            }
+            logProb[row] = lp;
+            value[row] = bf16_bits_to_float(h[Env::ACT_DIM]);
+        }
+    } else {
+        std::uniform_real_distribution<float> uniform(0.0f, 1.0f);
+        float logits[Env::ACT_DIM];
+        for (uint32_t row = 0; row < parallels; ++row) {
+            const uint16_t* h = head + (size_t)row * kHead;
+            float rowMax = -INFINITY;
+            for (uint32_t a = 0; a < Env::ACT_DIM; ++a) {
+                logits[a] = bf16_bits_to_float(h[a]);
+                rowMax = std::max(rowMax, logits[a]);
+            }
+            float sum = 0.0f;
+            for (uint32_t a = 0; a < Env::ACT_DIM; ++a) sum += std::exp(logits[a] - rowMax);
+            const float lse = rowMax + std::log(sum);
+            const float u = uniform(rng) * sum;
+            uint32_t chosen = Env::ACT_DIM - 1;
+            float acc = 0.0f;
+            for (uint32_t a = 0; a < Env::ACT_DIM; ++a) {
+                acc += std::exp(logits[a] - rowMax);
+                if (u < acc) {
+                    chosen = a;
+                    break;
+                }
+            }
+            action[row] = (typename Env::Action)chosen;
+            logProb[row] = logits[chosen] - lse;
+            value[row] = bf16_bits_to_float(h[Env::ACT_DIM]);
+        }
+    }
+}
+
+}  // namespace metalgym
 
 // model/ppo.h:97-104
 struct LossStats {
@@ -116,72 +187,21 @@ struct PPOModel {
         afterDeviceWork(MG_PPO_HEAD);
     }
 
-    // ---- manual stepping on the host (model/ppo.h:636-702)
+    // ---- manual stepping (model/ppo.h:636-702). act() draws on the host from
+    // the caller's generator (metalgym::sample_actions_host over the head rows
+    // of the last forward); actGreedy() runs on the device (mg_ppo_act_greedy)
+    // and leaves the actions in gym.actions() as the host version does.
     template <typename Rng>
     void act(Rng& rng) {
-        typename Env::Action* action = gym.actions();
-        float* value = values();
-        float* logProb = logProbs();
-        if constexpr (CONTINUOUS) {
-            std::normal_distribution<float> normal(0.0f, 1.0f);
-            float* actionF = reinterpret_cast<float*>(action);
-            float ls[Env::ACT_DIM];
+        syncHead();
+        float ls[Env::ACT_DIM] = {};
+        if constexpr (CONTINUOUS)
             for (uint32_t k = 0; k < Env::ACT_DIM; ++k) ls[k] = logStdValue(k);
-            for (uint32_t row = 0; row < parallels; ++row) {
-                float lp = 0.0f;
-                for (uint32_t k = 0; k < Env::ACT_DIM; ++k) {
-                    const float mu = headValue(row, k);
-                    const float a = mu + std::exp(ls[k]) * normal(rng);
-                    const float d = (a - mu) * std::exp(-ls[k]);
-                    actionF[(size_t)row * Env::ACT_DIM + k] = a;
-                    lp += -0.5f * d * d - ls[k] - 0.9189385332046727f;
-                }
-                logProb[row] = lp;
-                value[row] = headValue(row, Env::ACT_DIM);
-            }
-        } else {
-            std::uniform_real_distribution<float> uniform(0.0f, 1.0f);
-            float logits[Env::ACT_DIM];
-            for (uint32_t row = 0; row < parallels; ++row) {
-                float rowMax = -INFINITY;
-                for (uint32_t a = 0; a < Env::ACT_DIM; ++a) {
-                    logits[a] = headValue(row, a);
-                    rowMax = std::max(rowMax, logits[a]);
-                }
-                float sum = 0.0f;
-                for (uint32_t a = 0; a < Env::ACT_DIM; ++a) sum += std::exp(logits[a] - rowMax);
-                const float lse = rowMax + std::log(sum);
-                const float u = uniform(rng) * sum;
-                uint32_t chosen = Env::ACT_DIM - 1;
-                float acc = 0.0f;
-                for (uint32_t a = 0; a < Env::ACT_DIM; ++a) {
-                    acc += std::exp(logits[a] - rowMax);
-                    if (u < acc) {
-                        chosen = a;
-                        break;
-                    }
-                }
-                action[row] = (typename Env::Action)chosen;
-                logProb[row] = logits[chosen] - lse;
-                value[row] = headValue(row, Env::ACT_DIM);
-            }
-        }
+        metalgym::sample_actions_host<Env>(head_, parallels, ls, rng, gym.actions(), values(), logProbs());
     }
     // discrete: argmax; continuous: the mean
     void actGreedy() {
-        typename Env::Action* action = gym.actions();
-        if constexpr (CONTINUOUS) {
-            float* actionF = reinterpret_cast<float*>(action);
-            for (uint32_t row = 0; row < parallels; ++row)
-                for (uint32_t k = 0; k < Env::ACT_DIM; ++k) actionF[(size_t)row * Env::ACT_DIM + k] = headValue(row, k);
-        } else {
-            for (uint32_t row = 0; row < parallels; ++row) {
-                uint32_t best = 0;
-                for (uint32_t a = 1; a < Env::ACT_DIM; ++a)
-                    if (headValue(row, a) > headValue(row, best)) best = a;
-                action[row] = (typename Env::Action)best;
-            }
-        }
+        metalgym::check_or_exit(mg_ppo_act_greedy(handle, headSource_, gym.actions()), "actGreedy");
     }
 
     // ---- observability (model/ppo.h:448-476, 925-943)
@@ -243,7 +263,9 @@ struct PPOModel {
     }
     // Extension: collect() as one persistent kernel (mg_ppo_set_collect_fused;
     // environments with a State of at most 64 bytes and at most 32
-    // observations, embed 128, hidden 512).
+    // observations, embed 128, hidden 512): true = the kernel, false = the
+    // per-step graph. Without a call the library chooses (the kernel where it
+    // applies, up to 4096 parallels).
     void setFusedCollect(bool on) {
         metalgym::check_or_exit(mg_ppo_set_collect_fused(handle, on ? 1 : 0), "setFusedCollect");
     }

@@ -460,11 +460,26 @@ int mg_ppo_minibatch_rows(mg_ppo_t model, int* out);
  * environment whose State has at most 64 bytes and whose observation at most
  * 32 floats (mg_env_ops.collect_fused; CartPole and CartPoleContinuous among
  * the built-ins, not VoxelNav); the policy must be embed 128, hidden 512, 1
- * to 4 blocks. Other configurations return MG_ERR_UNSUPPORTED. 0 (the
- * default) keeps the captured per-step graph. Up to 4096 parallels the two
- * produce identical rollouts. */
+ * to 4 blocks. Other configurations return MG_ERR_UNSUPPORTED. on = 0 runs
+ * the captured per-step graph. on = -1 (the default) chooses: the kernel
+ * where it applies and parallels <= 4096 (one wave of clusters), else the
+ * graph. Up to 4096 parallels the two produce identical rollouts.
+ * mg_ppo_collect_fused reports the path the next collect() takes. */
 int mg_ppo_set_collect_fused(mg_ppo_t model, int on);
 int mg_ppo_collect_fused(mg_ppo_t model, int* out);
+/* One training minibatch's per-tile work as one kernel (no counterpart in the
+ * reference, which encodes every layer of a minibatch as its own dispatches,
+ * model/ppo.h:753-865): on = 1 runs the block forwards, the
+ * head with the PPO loss and the block backwards of a minibatch in one launch
+ * of 4-CTA clusters, one per 128-row tile, where each of them would run as a
+ * cluster kernel of its own (embed 128, hidden 512, 1 or 2 blocks, categorical
+ * head, minibatches of at most 4096 rows, no overlapped all-reduce); the
+ * results are bit-identical to the separate kernels (on = 0, the default:
+ * chained by programmatic dependent launch in the train graph they measured
+ * 2 % faster at 4096 rows). The gradient sums and Adam stay kernels of their
+ * own. mg_ppo_fused_minibatch reads the setting. */
+int mg_ppo_set_fused_minibatch(mg_ppo_t model, int on);
+int mg_ppo_fused_minibatch(mg_ppo_t model, int* out);
 /* One row-mode minibatch over rollout rows perm(base .. base + B - 1) of the
  * permutation keyed by key[4], with an Adam step; blocks (the manual path
  * of row mode, as mg_ppo_train_slot is of slot mode). */
@@ -474,6 +489,14 @@ int mg_ppo_train_rows(mg_ppo_t model, const uint32_t key[4], uint32_t base);
 int mg_minibatch_rows(const uint32_t key[4], uint32_t base, uint32_t rows, uint64_t total, uint64_t* out);
 /* forward() on the gym's live obs (model/ppo.h:628-634); blocks. */
 int mg_ppo_forward(mg_ppo_t model);
+/* actGreedy() (model/ppo.h:688-702) on the device: from the head rows of the
+ * last forward (head_source MG_PPO_HEAD: forward() or collect();
+ * MG_PPO_TRAIN_HEAD: the last training minibatch, which must hold a row per
+ * environment), per environment the index of the largest logit (the first of
+ * equal ones) or, for a Gaussian head, the means, written to the gym's
+ * action buffer and, when actions_host is not NULL, to actions_host
+ * (parallels Actions); blocks. */
+int mg_ppo_act_greedy(mg_ppo_t model, int head_source, void* actions_host);
 /* lastStats() (model/ppo.h:925-943): policy, value, entropy, approxKl,
  * clipFrac, gradNorm (pre-clip). */
 int mg_ppo_last_stats(mg_ppo_t model, float out6[6]);
@@ -519,7 +542,10 @@ int mg_ppo_set_allreduce_overlap(mg_ppo_t model, int on);
  * the work has not finished after `seconds`, the communicator is aborted
  * (ncclCommAbort: the all-reduce kernels in flight return) and the call
  * returns MG_ERR_COMM; every later call with that communicator returns
- * MG_ERR_COMM too. 0 (the default): block until done. */
+ * MG_ERR_COMM too. 0 (the default): block until done. If the stream has
+ * still not drained 30 s after the abort, mg_ppo_destroy and mg_gym_destroy
+ * leave the device buffers allocated (freeing them could block without limit
+ * or free memory a running kernel uses) and return MG_ERR_COMM. */
 int mg_ppo_set_comm_timeout(mg_ppo_t model, float seconds);
 
 /* ---------------------------------------------------------------- NCCL / host memory */

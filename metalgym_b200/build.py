@@ -35,6 +35,7 @@ SOURCES: dict[str, list[str]] = {
     "block_cluster.cu": [],
     "collect_fused.cu": [],
     "head_tail.cu": [],
+    "minibatch_tiles.cu": [],
     "envs.cu": [],
     "envs_builtin.cu": ["--fmad=false"],
     "p2p.cu": [],

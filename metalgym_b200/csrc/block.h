@@ -72,4 +72,35 @@ int block_cluster_backward(const void* dS, const void* wDown, const void* v, con
                            const float* stdev, const void* resid, void* residOut, float* partial, int M,
                            cudaStream_t st, const BlockClusterInput* in = nullptr);
 
+// The per-tile part of one training minibatch in one kernel
+// (minibatch_tiles.cu): the passes of block_cluster_forward (block 0 with the
+// input layer, then blocks 1 .. L-1), head_tail and block_cluster_backward
+// (blocks L-1 .. 0), recorded with the same arguments as those calls, then
+// launched as one kernel of 4-CTA clusters; bit-identical to the separate
+// kernels. Embed 128, hidden 512, categorical head, 1..kMaxBlocks blocks.
+struct PolicyLossRows;
+class MinibatchTiles {
+   public:
+    static constexpr int kMaxBlocks = 2;
+    MinibatchTiles();
+    ~MinibatchTiles();
+    MinibatchTiles(const MinibatchTiles&) = delete;
+    MinibatchTiles& operator=(const MinibatchTiles&) = delete;
+    void reset();
+    int forward(const void* lnOut, const void* wUp, const void* wDown, void* h, void* v, const LnOutputs& next, int M,
+                const BlockClusterForwardInput* in);
+    int headTail(const void* fOut, const void* wHead, void* head, const PolicyLossRows& loss, float* headPart,
+                 const void* gammaF, const void* xNormF, const float* stdevF, void* dS, float* lnPart, int M);
+    int backward(const void* dS, const void* wDown, const void* v, const void* wUp, void* dV, const void* lnOut,
+                 float* upPart, float* downPart, const void* xNorm, const void* gamma, const float* stdev,
+                 const void* resid, void* residOut, float* partial, int M, const BlockClusterInput* in);
+    // one launch of the recorded passes (checks that they form a minibatch)
+    int launch(cudaStream_t st);
+
+   private:
+    struct Plan;
+    Plan* plan;
+    int record(int rc);
+};
+
 }  // namespace mg

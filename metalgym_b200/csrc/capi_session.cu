@@ -88,7 +88,11 @@ int mg_gym_create(const char* kernel_name, int parallels, uint32_t seed, uint32_
 }
 
 int mg_gym_destroy(mg_gym_t gym) {
+    const bool busy = G(gym) && G(gym)->stillBusy();
     delete G(gym);
+    if (busy)
+        return mg::fail(MG_ERR_COMM, "mg_gym_destroy: the stream of an aborted all-reduce is still running; "
+                                     "its device buffers were left allocated");
     return MG_OK;
 }
 
@@ -204,7 +208,11 @@ int mg_ppo_create(mg_gym_t gym, int embed, int scale, int layers, float lr, int 
 }
 
 int mg_ppo_destroy(mg_ppo_t model) {
+    const bool busy = P(model) && P(model)->gym && P(model)->gym->stillBusy();
     delete P(model);
+    if (busy)
+        return mg::fail(MG_ERR_COMM, "mg_ppo_destroy: the stream of an aborted all-reduce is still running; "
+                                     "the model's device buffers were left allocated");
     return MG_OK;
 }
 
@@ -270,12 +278,25 @@ int mg_ppo_set_allreduce_overlap(mg_ppo_t model, int on) {
     return P(model)->setAllreduceOverlap(on != 0);
 }
 int mg_ppo_set_collect_fused(mg_ppo_t model, int on) {
-    MG_CHECK_ARG(model && (on == 0 || on == 1), "mg_ppo_set_collect_fused: null model or on not 0 / 1");
-    return P(model)->setCollectFused(on != 0);
+    MG_CHECK_ARG(model && on >= -1 && on <= 1, "mg_ppo_set_collect_fused: null model or on not -1 / 0 / 1");
+    return P(model)->setCollectMode(on);
 }
 int mg_ppo_collect_fused(mg_ppo_t model, int* out) {
     MG_CHECK_ARG(model && out, "mg_ppo_collect_fused: null argument");
-    *out = P(model)->fusedCollect ? 1 : 0;
+    *out = P(model)->useFusedCollect() ? 1 : 0;
+    return MG_OK;
+}
+int mg_ppo_act_greedy(mg_ppo_t model, int head_source, void* actions_host) {
+    MG_CHECK_ARG(model, "mg_ppo_act_greedy: null model");
+    return P(model)->actGreedy(head_source, actions_host);
+}
+int mg_ppo_set_fused_minibatch(mg_ppo_t model, int on) {
+    MG_CHECK_ARG(model && (on == 0 || on == 1), "mg_ppo_set_fused_minibatch: null model or on not 0 / 1");
+    return P(model)->setFusedMinibatch(on != 0);
+}
+int mg_ppo_fused_minibatch(mg_ppo_t model, int* out) {
+    MG_CHECK_ARG(model && out, "mg_ppo_fused_minibatch: null argument");
+    *out = P(model)->fusedMinibatch ? 1 : 0;
     return MG_OK;
 }
 int mg_ppo_train_rows(mg_ppo_t model, const uint32_t key[4], uint32_t base) {

@@ -50,12 +50,6 @@ int dalloc(T** p, size_t bytes) {
     return MG_OK;
 }
 
-#define MG_TRY(expr)              \
-    do {                          \
-        int mg_rc_ = (expr);      \
-        if (mg_rc_) return mg_rc_; \
-    } while (0)
-
 // ---- NCCL, loaded on first use (the process may already hold torch's copy)
 struct Nccl {
     decltype(&ncclGetUniqueId) getUniqueId = nullptr;
@@ -187,7 +181,10 @@ int splits_for(int M, int N, int K, int bn) {
 
 // ------------------------------------------------------------------ gym
 
+bool GymCore::stillBusy() const { return busy && stream && cudaStreamQuery(stream) == cudaErrorNotReady; }
+
 GymCore::~GymCore() {
+    if (stillBusy()) return;  // leaked on purpose: work that may never finish still uses the buffers
     int cur = 0;
     cudaGetDevice(&cur);
     cudaSetDevice(device);
@@ -260,6 +257,7 @@ PpoEngine::PpoEngine(GymCore* g, int embed, int scale, int layers, float learnin
 // Touches nothing of the gym, which may already be gone (a garbage collector
 // can finalise a borrowed gym before the model that borrowed it).
 PpoEngine::~PpoEngine() {
+    if (gym && gym->stillBusy()) return;  // leaked on purpose, as GymCore's buffers
     int cur = 0;
     cudaGetDevice(&cur);
     cudaSetDevice(device);
@@ -610,12 +608,15 @@ int PpoEngine::waitStream(const char* what) {
     o.now = [](void*) -> double {
         return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
     };
-    o.pause = [](void*) { std::this_thread::yield(); };
+    // a short sleep, not a spin: the wait lasts the whole step and must leave
+    // the host cores to the NCCL proxy and gloo threads
+    o.pause = [](void*) { std::this_thread::sleep_for(std::chrono::microseconds(100)); };
     bool drained = false;
     const int r = watch_wait(o, (double)commTimeout, 30.0, &drained);
     if (r == kWatchDone) return MG_OK;
     if (r == kWatchCudaError) return cuda_fail(c.err, what);
     comm_mark_aborted(comm);
+    if (!drained) gym->busy = true;
     if (trainExec) {  // it holds the aborted communicator (freed when it completes, if still in flight)
         cudaGraphExecDestroy(trainExec);
         trainExec = nullptr;
@@ -661,7 +662,8 @@ BlockFwdArgs PpoEngine::blockArgs(ActSet& a, int n, int rows) {
 // with the LayerNorm epilogue the down GEMM of block n also computes the
 // LayerNorm that follows it (block n + 1's, or the final one), which then has
 // no kernel of its own.
-int PpoEngine::blocksForward(const float* obs, const RowMap& rm, ActSet& a, int rows, cudaStream_t st) {
+int PpoEngine::blocksForward(const float* obs, const RowMap& rm, ActSet& a, int rows, cudaStream_t st,
+                             MinibatchTiles* mt) {
     auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
     auto bw = [&](uint32_t p) { return reinterpret_cast<const __nv_bfloat16*>(weights + params[p].offset); };
     const bool cluster = useBlockClusterForward(rows);
@@ -688,8 +690,12 @@ int PpoEngine::blocksForward(const float* obs, const RowMap& rm, ActSet& a, int 
                                       static_cast<__nv_bfloat16*>(a.fOut), a.fSd};
             const BlockClusterForwardInput in{obs, rm.mb, rm.envRows, rm.total, O, w(pInW), w(pInB), w(pLnG[0]),
                                               w(pLnB[0]), a.lnXn[0], a.lnSd[0]};
-            MG_TRY(block_cluster_forward(a.lnOut[n], w(pUp[n]), w(pDown[n]), a.h, a.v[n], next, rows, st,
-                                         n == 0 && inputInBlock ? &in : nullptr));
+            if (mt)
+                MG_TRY(mt->forward(a.lnOut[n], w(pUp[n]), w(pDown[n]), a.h, a.v[n], next, rows,
+                                   n == 0 && inputInBlock ? &in : nullptr));
+            else
+                MG_TRY(block_cluster_forward(a.lnOut[n], w(pUp[n]), w(pDown[n]), a.h, a.v[n], next, rows, st,
+                                             n == 0 && inputInBlock ? &in : nullptr));
             continue;
         }
         GemmCall up;
@@ -749,8 +755,17 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     const RowMap rm{sched + j, (uint64_t)R, (uint64_t)T * R};
     ActSet& a = trainActs;
     auto w = [&](uint32_t p) { return static_cast<const void*>(weights + params[p].offset); };
+    const bool overlapAr = world > 1 && !p2pOn && overlapAllreduce;
+    // every per-tile pass as a cluster kernel: record them, then one launch
+    MinibatchTiles* mt = nullptr;
+    if (fusedMinibatch && !cont && !overlapAr && L >= 1 && L <= MinibatchTiles::kMaxBlocks &&
+        useBlockClusterForward(rows) && O <= kBlockClusterMaxInputDim && useHeadTail(rows) &&
+        useBlockClusterBackward(rows)) {
+        mt = &tilesPlan;
+        mt->reset();
+    }
     // forward with activations saved (the input gathers the minibatch's obs rows)
-    MG_TRY(blocksForward(obsSlots, rm, a, rows, st));
+    MG_TRY(blocksForward(obsSlots, rm, a, rows, st, mt));
     // loss (model/ppo.h:753-781): per-slot advantage statistics from
     // collect(), or in row mode the statistics of this minibatch's rows
     const LossHyper lh{hp.clip, hp.valueCoef, hp.entropyCoef};
@@ -765,7 +780,11 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     if (headTail) {
         const PolicyLossRows pl = policy_loss_rows(static_cast<const int32_t*>(actionSlots), advSlots, as, retSlots,
                                                    logpSlots, dLogits, stats, rows, A, lh, rm);
-        MG_TRY(head_tail(a.fOut, w(pHead), a.head, pl, headPart, w(pLnFg), a.fXn, a.fSd, dS[L], lnFPart, rows, st));
+        if (mt)
+            MG_TRY(mt->headTail(a.fOut, w(pHead), a.head, pl, headPart, w(pLnFg), a.fXn, a.fSd, dS[L], lnFPart, rows));
+        else
+            MG_TRY(head_tail(a.fOut, w(pHead), a.head, pl, headPart, w(pLnFg), a.fXn, a.fSd, dS[L], lnFPart, rows,
+                             st));
     } else {
         GemmCall hd;
         hd.A = a.fOut; hd.lda = E;
@@ -819,7 +838,6 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
     // the first block's kernel also sums the input layer's gradient partials
     // (the same 16-row partials input_backward writes at these row counts)
     const bool inputFused = clusterBwd && inputGradFusable(rows);
-    const bool overlapAr = world > 1 && !p2pOn && overlapAllreduce;
     for (int n = L - 1; n >= 0; n--) {
         if (overlapAr && n == 0) {
             // every gradient but block 0's and the input layer's is complete:
@@ -835,9 +853,14 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
             // dV, dBranch, the LayerNorm backward with the skip add and both
             // weight-gradient partials in one kernel
             const BlockClusterInput in{obsSlots, rm.mb, rm.envRows, rm.total, O, inPart};
-            MG_TRY(block_cluster_backward(dS[n + 1], w(pDown[n]), a.v[n], w(pUp[n]), dVs[n], a.lnOut[n], upPart[n],
-                                          downPart[n], a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1], dS[n], lnPart[n],
-                                          rows, st, n == 0 && inputFused ? &in : nullptr));
+            if (mt)
+                MG_TRY(mt->backward(dS[n + 1], w(pDown[n]), a.v[n], w(pUp[n]), dVs[n], a.lnOut[n], upPart[n],
+                                    downPart[n], a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1], dS[n], lnPart[n], rows,
+                                    n == 0 && inputFused ? &in : nullptr));
+            else
+                MG_TRY(block_cluster_backward(dS[n + 1], w(pDown[n]), a.v[n], w(pUp[n]), dVs[n], a.lnOut[n],
+                                              upPart[n], downPart[n], a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1],
+                                              dS[n], lnPart[n], rows, st, n == 0 && inputFused ? &in : nullptr));
             continue;
         } else {
             GemmCall g1;  // dV = bf16(dS Dp^T) * (V > 0) (model/mlp.metal:88-127)
@@ -879,6 +902,7 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         MG_TRY(layernorm_backward(dBranch, a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1], lnPart[n], rows, E, st,
                                   dS[n]));
     }
+    if (mt) MG_TRY(mt->launch(st));
     if (!inputFused) MG_TRY(input_backward(obsSlots, dS[0], inPart, rows, O, E, st, rm));
     if (forked) {
         MG_CUDA_TRY(cudaEventRecord(joinEv, side));
@@ -933,6 +957,7 @@ int PpoEngine::captureCollect() {
     int rc = MG_OK;
     const void* logStd = cont ? static_cast<const void*>(weights + params[pLogStd].offset) : nullptr;
     const mg_env_ops* ops = gym->ops;
+    const bool fusedCollect = useFusedCollect();
     if (fusedCollect) {
         // every step, the bootstrap forward and GAE in one kernel; the
         // advantage statistics need every environment's column
@@ -996,6 +1021,7 @@ int PpoEngine::captureCollect() {
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) return cuda_fail(e, "collect graph instantiate");
     collectHp = hp;
+    collectExecFused = fusedCollect;
     return MG_OK;
 }
 
@@ -1076,17 +1102,32 @@ static MgMinibatch row_minibatch(const uint32_t key[4], uint32_t base) {
 
 bool PpoEngine::collectFusedApplies() const { return collect_fused_supported(gym->ops, E, H, L, O); }
 
-int PpoEngine::setCollectFused(bool on) {
-    if (on && !collectFusedApplies())
+int PpoEngine::setFusedMinibatch(bool on) {
+    if (on != fusedMinibatch && trainExec) {
+        cudaGraphExecDestroy(trainExec);  // recaptured by the next train()
+        trainExec = nullptr;
+    }
+    fusedMinibatch = on;
+    return MG_OK;
+}
+
+bool PpoEngine::useFusedCollect() const {
+    if (collectMode >= 0) return collectMode == 1;
+    return collectFusedApplies() && R <= kFusedCollectAutoRows;
+}
+
+int PpoEngine::setCollectMode(int mode) {
+    MG_CHECK_ARG(mode >= -1 && mode <= 1, "setCollectMode: mode must be -1 (automatic), 0 (graph) or 1 (fused)");
+    if (mode == 1 && !collectFusedApplies())
         return fail(MG_ERR_UNSUPPORTED,
-                    "setCollectFused: no fused collect kernel for this environment and policy shape (an "
+                    "setCollectMode: no fused collect kernel for this environment and policy shape (an "
                     "environment with a State of at most 64 bytes and at most 32 observations; embed 128, hidden "
                     "512, 1-4 blocks)");
-    if (on != fusedCollect && collectExec) {
+    collectMode = mode;
+    if (collectExec && collectExecFused != useFusedCollect()) {
         cudaGraphExecDestroy(collectExec);  // recaptured by the next collect()
         collectExec = nullptr;
     }
-    fusedCollect = on;
     return MG_OK;
 }
 
@@ -1185,6 +1226,21 @@ int PpoEngine::forward() {
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     MG_TRY(forwardOn(static_cast<const float*>(gym->obs), R, collectActs, gym->stream));
     return checkStatus("forward");
+}
+
+// model/ppo.h:688-702
+int PpoEngine::actGreedy(int source, void* hostOut) {
+    MG_CHECK_ARG(source == MG_PPO_HEAD || source == MG_PPO_TRAIN_HEAD,
+                 "actGreedy: the head is MG_PPO_HEAD or MG_PPO_TRAIN_HEAD");
+    const void* head = source == MG_PPO_HEAD ? collectActs.head : trainActs.head;
+    const int rows = source == MG_PPO_HEAD ? R : trainBufRows;
+    MG_CHECK_ARG(head && rows >= R, "actGreedy: that head does not hold a row per environment");
+    MG_CUDA_TRY(cudaSetDevice(gym->device));
+    cudaStream_t st = gym->stream;
+    MG_TRY(act_greedy(head, R, A, cont, gym->actions, st));
+    if (hostOut) MG_CUDA_TRY(cudaMemcpyAsync(hostOut, gym->actions, (size_t)R * actBytes, cudaMemcpyDeviceToHost, st));
+    MG_CUDA_TRY(cudaStreamSynchronize(st));
+    return MG_OK;
 }
 
 // model/ppo.h:925-943 (means on the device; gradNorm is the pre-clip norm)

@@ -41,6 +41,12 @@ struct GymCore {
     uint8_t* doneRing = nullptr;
     int ringSlots = 0;
     int steps_rng_reserved = 0;
+    // Set when a data-parallel train() aborted its communicator and the
+    // stream had not drained within the watchdog's limit: its kernels may
+    // still run, so teardown leaves every device and pinned buffer allocated
+    // (freeing them would block without limit or free memory in use).
+    bool busy = false;
+    bool stillBusy() const;
 
     ~GymCore();
 };
@@ -86,11 +92,16 @@ class PpoEngine {
     // Minibatch rows of train(): 0 = one time slot per minibatch (the
     // reference); B > 0 = B rollout rows drawn without replacement per epoch.
     int setMinibatchRows(int rows);
-    // collect() as one persistent kernel (collect_fused.cu) instead of the
-    // captured per-step graph; MG_ERR_UNSUPPORTED where the environment or
-    // the policy shape has no fused kernel. Off by default.
-    int setCollectFused(bool on);
+    // collect() as one persistent kernel (collect_fused.cu) or as the
+    // captured per-step graph: mode 1 = the kernel (MG_ERR_UNSUPPORTED where
+    // the environment or the policy shape has none), 0 = the graph, -1 =
+    // automatic, the default: the kernel where it applies and the rollout has
+    // at most kFusedCollectAutoRows parallels (one wave of clusters; there the
+    // two paths give identical rollouts).
+    int setCollectMode(int mode);
     bool collectFusedApplies() const;
+    bool useFusedCollect() const;
+    static constexpr int kFusedCollectAutoRows = 4096;
     // With an NCCL communicator (world > 1): all-reduce the gradients of
     // everything but the last backward layer (block 0 and the input layer) on
     // the side stream while that layer's backward runs, then the rest. Off by
@@ -101,6 +112,10 @@ class PpoEngine {
     int trainRows(const uint32_t key[4], uint32_t base);
     int forward();  // on the gym's live obs; head in the collect activations
     int lastStats(float out6[6]);
+    // actGreedy on the device from the collect head (source MG_PPO_HEAD) or
+    // the last training forward's (MG_PPO_TRAIN_HEAD) into the gym's actions,
+    // copied to hostOut too when it is given; blocks.
+    int actGreedy(int source, void* hostOut);
     int setLogStd(float v);
     int logStd(int k, float* out);
     int setComm(void* comm, int rank, int world);
@@ -120,7 +135,8 @@ class PpoEngine {
     uint32_t seed;
     PpoHyper hp;
     bool rolloutStarted = false;
-    bool fusedCollect = false;  // setCollectFused
+    int collectMode = -1;          // setCollectMode
+    bool collectExecFused = false;  // the path collectExec was captured with
     float stepCounter = 0.0f;  // model/ppo.h:265 (float, as the reference)
     std::mt19937 hostRng;      // slot shuffle (model/ppo.h:349, 920), row-mode keys
     int mbRows = 0;            // 0: slot mode; > 0: rows per row-mode minibatch
@@ -229,6 +245,15 @@ class PpoEngine {
     }
     static constexpr int kClusterForwardMaxRows = 4096;
     static constexpr int kClusterBackwardMaxRows = 4096;
+    // the block forwards, the head and the block backwards of a minibatch in
+    // one kernel (minibatch_tiles.cu) where each of them would run as a
+    // cluster kernel of its own (block_cluster.cu, head_tail.cu). Off by
+    // default: in the train graph the separate kernels, chained by
+    // programmatic dependent launch, measured 2 % faster (9.84 against 10.05
+    // ms per train(4) at 4096 rows); setFusedMinibatch
+    bool fusedMinibatch = false;
+    MinibatchTiles tilesPlan;
+    int setFusedMinibatch(bool on);
 
     // multi-GPU: NCCL all-reduce (setComm) or the all-reduce over NVLink peer
     // memory (p2p.cu: p2pHandle on every rank, exchange, p2pOpen)
@@ -260,7 +285,9 @@ class PpoEngine {
 
    private:
     int forwardOn(const float* obs, int rows, ActSet& a, cudaStream_t st);
-    int blocksForward(const float* obs, const RowMap& rm, ActSet& a, int rows, cudaStream_t st);
+    // mt: record the cluster block passes there instead of launching them
+    int blocksForward(const float* obs, const RowMap& rm, ActSet& a, int rows, cudaStream_t st,
+                      MinibatchTiles* mt = nullptr);
     BlockFwdArgs blockArgs(ActSet& a, int n, int rows);
     int minibatch(int j, bool rowMode, cudaStream_t st);  // reads sched[j], schedBetaPow[2j..]
     int captureCollect();

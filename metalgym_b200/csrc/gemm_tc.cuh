@@ -21,7 +21,7 @@
 #include "row_epilogues.cuh"
 #include "metalgym/detail/tile.cuh"
 #include "metalgym/pdl.cuh"
-#include "ptx.cuh"
+#include "metalgym/detail/ptx.cuh"
 
 namespace mg {
 

@@ -28,20 +28,25 @@ static __device__ __align__(256) float g_noalloc_scratch[kScratchBytes / sizeof(
 
 constexpr int kMaxDevices = 64;
 float* g_scratch_addr[kMaxDevices] = {};
+uint64_t g_scratch_ctx[kMaxDevices] = {};  // the context each address belongs to
 std::mutex g_scratch_mu;
 
 // Device address of the scratch on the current device, looked up on the
-// first call made on that device (host code cannot use the symbol itself).
+// first call made on that device (host code cannot use the symbol itself),
+// and again when the device's context changed (after cudaDeviceReset the
+// array lives at a new address in the new context).
 int scratch_address(float** out) {
     int dev = 0;
     MG_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return mg::fail(MG_ERR_UNSUPPORTED, "device index out of range");
+    const uint64_t ctx = mg::current_context_id();
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    if (!g_scratch_addr[dev] || ctx == 0 || g_scratch_ctx[dev] != ctx) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return mg::cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
         g_scratch_addr[dev] = static_cast<float*>(p);
+        g_scratch_ctx[dev] = mg::current_context_id();
     }
     *out = g_scratch_addr[dev];
     return MG_OK;

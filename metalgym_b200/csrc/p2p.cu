@@ -24,7 +24,7 @@
 
 #include "metalgym/pdl.cuh"
 #include "policy_kernels.cuh"
-#include "ptx.cuh"
+#include "metalgym/detail/ptx.cuh"
 #include "runtime.h"
 
 namespace mg {

@@ -559,6 +559,8 @@ __global__ void __launch_bounds__(kGaussRowsPerCta) k_gaussian_loss(
 // model/gae.metal:14-36: one thread per env, reverse scan over the T slots of
 // the slot-major buffers [t * rows + i]; the bootstrap value is column actDim
 // of the last forward's head. Operation order as the reference (no FMA).
+constexpr int kGaeChunk = 8;
+
 __global__ void k_gae(const float* __restrict__ reward, const uint8_t* __restrict__ done,
                       const float* __restrict__ value, const __nv_bfloat16* __restrict__ bootHead,
                       float* __restrict__ advantage, float* __restrict__ ret, int rows, int horizon, int actDim,
@@ -570,15 +572,32 @@ __global__ void k_gae(const float* __restrict__ reward, const uint8_t* __restric
     float lastAdv = 0.0f;
     float nextValue = bf(bootHead[(size_t)i * kHeadDim + actDim]);
     const float gl = __fmul_rn(gamma, lambda);
-    for (int t = horizon - 1; t >= 0; t--) {
-        const size_t k = (size_t)t * rows + i;
-        const float nonTerminal = done[k] ? 0.0f : 1.0f;
-        const float v = value[k];
-        const float delta = __fsub_rn(__fadd_rn(reward[k], __fmul_rn(__fmul_rn(gamma, nextValue), nonTerminal)), v);
-        lastAdv = __fadd_rn(delta, __fmul_rn(__fmul_rn(gl, nonTerminal), lastAdv));
-        advantage[k] = lastAdv;
-        ret[k] = __fadd_rn(lastAdv, v);
-        nextValue = v;
+    // slots in chunks of kGaeChunk, newest first: a chunk's loads do not depend
+    // on the recurrence, so they are issued together before it runs (the
+    // arithmetic, and so every bit, is that of the one-slot-at-a-time scan)
+    for (int t = horizon - 1; t >= 0; t -= kGaeChunk) {
+        float rw[kGaeChunk], vl[kGaeChunk];
+        uint8_t dn[kGaeChunk];
+#pragma unroll
+        for (int j = 0; j < kGaeChunk; j++) {
+            if (t - j < 0) break;
+            const size_t k = (size_t)(t - j) * rows + i;
+            rw[j] = reward[k];
+            vl[j] = value[k];
+            dn[j] = done[k];
+        }
+#pragma unroll
+        for (int j = 0; j < kGaeChunk; j++) {
+            if (t - j < 0) break;
+            const size_t k = (size_t)(t - j) * rows + i;
+            const float nonTerminal = dn[j] ? 0.0f : 1.0f;
+            const float v = vl[j];
+            const float delta = __fsub_rn(__fadd_rn(rw[j], __fmul_rn(__fmul_rn(gamma, nextValue), nonTerminal)), v);
+            lastAdv = __fadd_rn(delta, __fmul_rn(__fmul_rn(gl, nonTerminal), lastAdv));
+            advantage[k] = lastAdv;
+            ret[k] = __fadd_rn(lastAdv, v);
+            nextValue = v;
+        }
     }
 }
 
@@ -1232,6 +1251,33 @@ int adam(float* param, const float* grad, float* mom, float* var, void* weights,
 int stats_mean(const float* stats, int rows, float* out, cudaStream_t st) {
     MG_LAUNCH(k_stats_mean, 1, 256, 0, st, stats, rows, out);
     return check_launch("k_stats_mean");
+}
+
+// actGreedy (model/ppo.h:688-702) on the device, one thread per row of the
+// head [rows][64] (bf16): a categorical head's action is the index of the
+// largest logit (the first of equal ones: the reference's strict >), a
+// Gaussian head's the ACT_DIM means as floats.
+__global__ void k_act_greedy(const __nv_bfloat16* __restrict__ head, int rows, int actDim, int continuous,
+                             void* __restrict__ actions) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows) return;
+    const __nv_bfloat16* h = head + (size_t)i * kHeadDim;
+    if (continuous) {
+        float* a = static_cast<float*>(actions) + (size_t)i * actDim;
+        for (int k = 0; k < actDim; k++) a[k] = bf(h[k]);
+    } else {
+        int best = 0;
+        for (int a = 1; a < actDim; a++)
+            if (bf(h[a]) > bf(h[best])) best = a;
+        static_cast<int32_t*>(actions)[i] = best;
+    }
+}
+
+int act_greedy(const void* head, int rows, int actDim, bool continuous, void* actions, cudaStream_t st) {
+    MG_CHECK_ARG(head && actions && rows > 0 && actDim >= 1 && actDim < kHeadDim, "act_greedy: bad arguments");
+    MG_LAUNCH(k_act_greedy, grid_rows(rows, 256), 256, 0, st, static_cast<const __nv_bfloat16*>(head), rows, actDim,
+              continuous ? 1 : 0, actions);
+    return check_launch("k_act_greedy");
 }
 
 }  // namespace mg

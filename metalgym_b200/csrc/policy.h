@@ -118,5 +118,8 @@ int adam(float* param, const float* grad, float* mom, float* var, void* weights,
          int64_t count, AdamHyper hp, const float* betaPow, float* normSqOut, cudaStream_t st,
          const float* normSqIn = nullptr);
 int stats_mean(const float* stats, int rows, float* out, cudaStream_t st);
+// actGreedy (model/ppo.h:688-702): per row of head [rows][64] bf16 the argmax
+// action (int32) or, continuous, the actDim means (float) into actions.
+int act_greedy(const void* head, int rows, int actDim, bool continuous, void* actions, cudaStream_t st);
 
 }  // namespace mg

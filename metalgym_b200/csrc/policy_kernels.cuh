@@ -15,7 +15,7 @@
 
 #include "metalgym/pdl.cuh"
 #include "metalgym/sampling.cuh"
-#include "ptx.cuh"
+#include "metalgym/detail/ptx.cuh"
 
 namespace mg {
 

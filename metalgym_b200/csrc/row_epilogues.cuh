@@ -9,7 +9,7 @@
 
 #include "metalgym/mathf.h"
 #include "metalgym/rowmap.h"
-#include "ptx.cuh"
+#include "metalgym/detail/ptx.cuh"
 
 namespace mg {
 

@@ -74,17 +74,46 @@ int num_sms() {
     return n;
 }
 
+uint64_t current_context_id() {
+    typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+    typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+    static CtxGetCurrentFn getCurrent = nullptr;
+    static CtxGetIdFn getId = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            getCurrent = reinterpret_cast<CtxGetCurrentFn>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            getId = reinterpret_cast<CtxGetIdFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!getCurrent || !getId || getCurrent(&ctx) != CUDA_SUCCESS || !ctx || getId(ctx, &id) != CUDA_SUCCESS) return 0;
+    return (uint64_t)id;
+}
+
 int* status_ptr() {
     constexpr int kMaxDevices = 64;
+    // per device: the address and the id of the context it was looked up in
+    // (a device reset makes a new context, with the word at a new address)
     static int* cache[kMaxDevices] = {};
+    static uint64_t cacheCtx[kMaxDevices] = {};
     static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    // 0 before the runtime made a context current: the lookup below does,
+    // and the next call sees the real id and looks the address up once more
+    const uint64_t ctx = current_context_id();
     std::lock_guard<std::mutex> lock(mu);
-    if (!cache[dev]) {
+    if (!cache[dev] || cacheCtx[dev] != ctx) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
         cache[dev] = static_cast<int*>(p);
+        cacheCtx[dev] = ctx;
     }
     return cache[dev];
 }

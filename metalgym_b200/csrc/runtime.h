@@ -29,9 +29,21 @@ int cuda_fail(cudaError_t e, const char* what);
         if (!(cond)) return ::mg::fail(MG_ERR_ARGUMENT, msg);    \
     } while (0)
 
+// Returns the status of expr from the calling function when it is not MG_OK.
+#define MG_TRY(expr)               \
+    do {                           \
+        int mg_rc_ = (expr);       \
+        if (mg_rc_) return mg_rc_; \
+    } while (0)
+
 // Device address of the status word of the current device (a __device__ int
 // in runtime.cu, looked up once per device with cudaGetSymbolAddress).
 int* status_ptr();
+// A unique id of the calling thread's current CUDA context (cuCtxGetId; 0
+// when none is current or the driver lacks the call). Caches of per-context
+// device addresses compare it so that they are looked up again after a
+// device reset.
+uint64_t current_context_id();
 // NCCL communicators aborted by the train() watchdog (ncclCommAbort freed
 // them): their handles must not be used or destroyed again. A new
 // communicator at the same address is not aborted (comm_forget_aborted).

@@ -182,14 +182,30 @@ class PPOModel:
 
     @property
     def collect_fused(self) -> bool:
-        """collect() as one persistent kernel (mg_ppo_set_collect_fused)."""
+        """Whether the next collect() runs as one persistent kernel
+        (mg_ppo_collect_fused). Set True / False to choose the kernel / the
+        per-step graph, None for the library's choice (the default: the kernel
+        where it applies, up to 4096 parallels)."""
         v = C.c_int()
         check(lib().mg_ppo_collect_fused(self._h, C.byref(v)))
         return bool(v.value)
 
     @collect_fused.setter
-    def collect_fused(self, on: bool):
-        check(lib().mg_ppo_set_collect_fused(self._h, 1 if on else 0), "collect_fused")
+    def collect_fused(self, on):
+        mode = -1 if on is None else (1 if on else 0)
+        check(lib().mg_ppo_set_collect_fused(self._h, mode), "collect_fused")
+
+    @property
+    def fused_minibatch(self) -> bool:
+        """A minibatch's block forwards, head and block backwards as one kernel
+        where they apply (mg_ppo_set_fused_minibatch; off by default)."""
+        v = C.c_int()
+        check(lib().mg_ppo_fused_minibatch(self._h, C.byref(v)))
+        return bool(v.value)
+
+    @fused_minibatch.setter
+    def fused_minibatch(self, on: bool):
+        check(lib().mg_ppo_set_fused_minibatch(self._h, 1 if on else 0), "fused_minibatch")
 
     def train_rows(self, key, base: int):
         """One row-mode minibatch over rows perm(base .. base + B - 1) of the

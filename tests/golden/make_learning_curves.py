@@ -1,5 +1,6 @@
-"""Generates tests/golden/learning_curves.npz: mean episode length per
-iteration of the CartPole PPO loop on the CPU reference path, for five seeds.
+"""Generates tests/golden/learning_curves.npz (and, with `c3`,
+tests/golden/learning_curves_c3.npz): mean episode length per iteration of
+the CartPole PPO loop on the CPU reference path, for five seeds.
 
 The environment is the reference's own code (oracle/_ref, built from the
 reference sources) when available, else the host build of the environment
@@ -11,7 +12,12 @@ restatement in oracle/. Configuration: 1024 envs, T = 32, embed 64, hidden
 envs x T / (number of done flags in the rollout) (examples/CartPoleContinuous/
 main.cpp:33-39).
 
+`c3` is BASELINE configs[2]'s shape instead: 4096 envs, T = 32, embed 128,
+hidden 512, 2 blocks, train(4), 20 iterations (the reference's own CartPole
+driver trains 40 iterations of that shape, examples/CartPole/main.cpp:20-34).
+
     python tests/golden/make_learning_curves.py      (about a minute per seed)
+    python tests/golden/make_learning_curves.py c3   (about 15 minutes per seed on 8 cores)
 """
 import ctypes
 import os
@@ -24,8 +30,13 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent))
 from orc import load_hostenv, load_oracle, load_ref, ptr, seed_words  # noqa: E402
 
-CFG = dict(envs=1024, horizon=32, embed=64, scale=4, layers=2, lr=3e-4, epochs=4, iterations=15,
-           seeds=(0, 1, 2, 3, 4))
+CONFIGS = {
+    "small": (dict(envs=1024, horizon=32, embed=64, scale=4, layers=2, lr=3e-4, epochs=4, iterations=15,
+                   seeds=(0, 1, 2, 3, 4)), "learning_curves.npz"),
+    "c3": (dict(envs=4096, horizon=32, embed=128, scale=4, layers=2, lr=3e-4, epochs=4, iterations=20,
+                seeds=(0, 1, 2, 3, 4)), "learning_curves_c3.npz"),
+}
+CFG = CONFIGS["small"][0]
 
 
 def curve(orc, env_fn, seed, threads):
@@ -53,6 +64,9 @@ def curve(orc, env_fn, seed, threads):
 
 
 def main():
+    global CFG
+    which = sys.argv[1] if len(sys.argv) > 1 else "small"
+    CFG, out_name = CONFIGS[which]
     threads = os.cpu_count()
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     orc = load_oracle()
@@ -65,7 +79,7 @@ def main():
         print(f"seed {s}: " + " ".join(f"{x:.1f}" for x in c), flush=True)
         curves.append(c)
         stats.append(st)
-    np.savez(HERE / "learning_curves.npz", lengths=np.array(curves), stats=np.array(stats),
+    np.savez(HERE / out_name, lengths=np.array(curves), stats=np.array(stats),
              config=np.array([repr(CFG)]), env_code=np.array(["reference" if ref is not None else "port"]))
 
 

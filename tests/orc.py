@@ -19,7 +19,20 @@ ROOT = Path(__file__).resolve().parent.parent
 ORACLE_LIB = ROOT / "oracle" / "_build" / "libmg_oracle.so"
 REF_LIB = ROOT / "oracle" / "_ref" / "libmg_ref.so"
 HOSTENV_LIB = ROOT / "tests" / "_build" / "libmg_hostenv.so"
-REFERENCE_TREE = Path(os.environ.get("METALGYM_REFERENCE", "/root/reference"))
+
+
+def reference_tree() -> Path | None:
+    """The reference's source tree: $METALGYM_REFERENCE, else the tree that
+    `make -C oracle ref REF=<dir>` recorded in oracle/_ref/tree, else None
+    (a GPU box has the built oracle/_ref library but not the tree)."""
+    env = os.environ.get("METALGYM_REFERENCE")
+    if env:
+        return Path(env) if Path(env).is_dir() else None
+    rec = ROOT / "oracle" / "_ref" / "tree"
+    if rec.exists():
+        t = Path(rec.read_text().strip())
+        return t if t.is_dir() else None
+    return None
 
 I, U, F, D = C.c_int, C.c_uint32, C.c_float, C.c_double
 U16 = C.c_uint16
@@ -86,11 +99,38 @@ def load_oracle():
     return lib
 
 
+REF_HOST_LIB = ROOT / "oracle" / "_ref" / "libmg_ref_host.so"
+
+
+def load_ref_host():
+    """The reference's own host code (oracle/ref_host.cpp), or None when it was
+    not built and the reference tree is absent."""
+    if not REF_HOST_LIB.exists():
+        tree = reference_tree()
+        if tree is None:
+            return None
+        _make("ref-host", [f"REF={tree}"])
+    lib = C.CDLL(str(REF_HOST_LIB))
+    _sig(lib, "ref_host_create", C.c_void_p, [I, I, I, I, I, F, I, U])
+    _sig(lib, "ref_host_destroy", None, [C.c_void_p])
+    _sig(lib, "ref_host_sizes", None, [C.c_void_p, P])
+    _sig(lib, "ref_host_params", None, [C.c_void_p, P, P])
+    _sig(lib, "ref_host_param_info", None, [C.c_void_p, U, P, P])
+    _sig(lib, "ref_host_set_head", None, [C.c_void_p, P])
+    _sig(lib, "ref_host_act", None, [C.c_void_p, U, I, P, P, P])
+    _sig(lib, "ref_host_act_greedy", None, [C.c_void_p, P])
+    _sig(lib, "ref_host_set_log_std", None, [C.c_void_p, F])
+    _sig(lib, "ref_host_log_std", F, [C.c_void_p, I])
+    _sig(lib, "ref_host_last_stats", None, [C.c_void_p, P, F, P])
+    return lib
+
+
 def load_ref():
     if not REF_LIB.exists():
-        if not REFERENCE_TREE.exists():
+        tree = reference_tree()
+        if tree is None:
             return None
-        _make("ref", [f"REF={REFERENCE_TREE}"])
+        _make("ref", [f"REF={tree}"])
     lib = C.CDLL(str(REF_LIB))
     _sig(lib, "ref_env_sizes", I, [I, P])
     _sig(lib, "ref_rollout", None, [I, P, P, P, P, P, P, U, I])
@@ -123,6 +163,25 @@ def load_hostenv():
     _sig(lib, "hostenv_rollout", None, [I, P, P, P, P, P, P, U, I])
     for n in ("hostenv_sinf", "hostenv_cosf", "hostenv_expf", "hostenv_logf", "hostenv_tanhf"):
         _sig(lib, n, F, [F])
+    return lib
+
+
+HOST_SAMPLER_LIB = ROOT / "tests" / "_build" / "libmg_host_sampler.so"
+
+
+def load_host_sampler():
+    """metalgym::sample_actions_host (the drop-in act(), include/metalgym/ppo.h)
+    built for the host (tests/helpers/host_sampler.cpp)."""
+    src = ROOT / "tests" / "helpers" / "host_sampler.cpp"
+    hdrs = list((ROOT / "include").rglob("*.h"))
+    lib_ = HOST_SAMPLER_LIB
+    stale = not lib_.exists() or any(p.stat().st_mtime > lib_.stat().st_mtime for p in [src, *hdrs])
+    if stale:
+        lib_.parent.mkdir(parents=True, exist_ok=True)
+        subprocess.run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-ffp-contract=off", "-I",
+                        str(ROOT / "include"), str(src), "-o", str(lib_)], check=True)
+    lib = C.CDLL(str(lib_))
+    _sig(lib, "host_act", None, [I, P, U, P, U, I, P, P, P])
     return lib
 
 

@@ -32,3 +32,10 @@ def test_reference_arm_prints_its_json_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["sample"] and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # the record describes what ran: one timed sample (--steps 1) after one
+    # warm-up sample, each sample's wall time, and the GPU arm's config
+    assert d["steps"] == 1 and d["warmup"] == 1 and 1e3 <= d["ms_per_step"] <= 60e3
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    assert d["config"] == bench.workload_config(1)

@@ -10,20 +10,11 @@ gym's env states / RNG words / done flags after collect(). Several collect()
 calls in a row with a train() between them check the carried state and the
 updated weights. A teacher-forced replay of the fused rollout against the
 CPU oracle checks it against the reference independently of the graph path.
-
-The kernel tests run when METALGYM_TEST_FUSED_COLLECT=1 is set: the kernel
-is new and has not been run on a B200 yet, so the default GPU suite does not
-launch it. The configuration checks launch nothing and always run.
 """
-import os
-
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
-
-run_kernel = pytest.mark.skipif(os.environ.get("METALGYM_TEST_FUSED_COLLECT") != "1",
-                                reason="fused collect kernel not yet run on a B200 (METALGYM_TEST_FUSED_COLLECT=1)")
 
 SLOTS = ("obs", "actions", "logp", "value", "reward", "done", "adv", "ret")
 
@@ -33,8 +24,8 @@ def make(name, R, L, T, seed=0, fused=False, embed=128, scale=4):
 
     gym = Gym(name, R, seed=0)
     model = PPOModel(gym, embed, scale, L, 3e-4, T, seed)
-    if fused:
-        model.collect_fused = True
+    if embed == 128 and scale == 4 and name != "rollout_voxelnav":
+        model.collect_fused = fused
     return gym, model
 
 
@@ -66,9 +57,22 @@ def test_unsupported_configurations_are_rejected(mg):
     assert model.collect_fused is True
     model.collect_fused = False
     assert model.collect_fused is False
+    model.collect_fused = None  # the library's choice: the kernel, at 256 parallels
+    assert model.collect_fused is True
 
 
-@run_kernel
+def test_automatic_choice(mg):
+    """Without a choice, collect() runs the kernel where it applies up to 4096
+    parallels (one wave of clusters) and the per-step graph above."""
+    from metalgym_b200.session import Gym, PPOModel
+
+    for R, want in [(4096, True), (4097, False)]:
+        model = PPOModel(Gym("rollout_cartpole", R), 128, 4, 2, 3e-4, 2, 0)
+        assert model.collect_fused is want, R
+    model = PPOModel(Gym("rollout_cartpole", 512), 64, 4, 2, 3e-4, 2, 0)
+    assert model.collect_fused is False
+
+
 @pytest.mark.parametrize("name,R,L,T", [("rollout_cartpole", 4096, 2, 32), ("rollout_cartpole", 1000, 1, 8),
                                         ("rollout_cartpole_continuous", 2048, 2, 16),
                                         ("rollout_cartpole", 300, 4, 3)])
@@ -85,7 +89,6 @@ def test_fused_collect_is_bit_identical_to_the_step_graph(mg, name, R, L, T):
         assert np.array_equal(ref[1].download("master"), fused[1].download("master")), f"train after collect {it}"
 
 
-@run_kernel
 @pytest.mark.parametrize("name,R,T", [("rollout_cartpole", 1024, 8), ("rollout_cartpole_continuous", 512, 6)])
 def test_fused_collect_teacher_forced(mg, oracle, hostenv, name, R, T):
     from test_engine import replay_collect
@@ -95,7 +98,6 @@ def test_fused_collect_teacher_forced(mg, oracle, hostenv, name, R, T):
     replay_collect(oracle, hostenv, model, name, 1)
 
 
-@run_kernel
 def test_fused_collect_can_be_switched_between_calls(mg):
     """Switching paths between collect() calls recaptures the collect graph and
     continues the same rollout."""
@@ -108,7 +110,6 @@ def test_fused_collect_can_be_switched_between_calls(mg):
         assert_same_rollout(ref, mixed, it)
 
 
-@run_kernel
 @pytest.mark.parametrize("name", ["rollout_test_walk", "rollout_test_glide"])
 def test_fused_collect_of_a_user_environment(mg, tmp_path, name):
     """A user environment built against the public headers alone (the walk and
@@ -136,7 +137,6 @@ def test_fused_collect_of_a_user_environment(mg, tmp_path, name):
         assert_same_rollout(ref, fused, it)
 
 
-@run_kernel
 @pytest.mark.parametrize("name,L", [("rollout_cartpole", 2), ("rollout_cartpole_continuous", 3)])
 def test_c_entry_point_on_session_buffers(mg, name, L):
     """mg_env_collect_fused on the buffers of a PPO session (weights located

@@ -25,11 +25,11 @@ def free_port():
         return s.getsockname()[1]
 
 
-def launch(mode, nproc=2, limit=600, extra=()):
+def launch(mode, nproc=2, limit=600, extra=(), env=None):
     cmd = ["timeout", "-k", "30", str(limit), sys.executable, "-m", "torch.distributed.run", "--nnodes", "1",
            "--nproc-per-node", str(nproc), "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
            str(ROOT / "tests" / "dp_worker.py"), "--mode", mode, *extra]
-    p = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT)
+    p = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, env={**os.environ, **(env or {})})
     lines = [l for l in p.stdout.splitlines() if l.startswith("{")]
     assert p.returncode == 0 and lines, f"rc={p.returncode}\n{p.stdout[-3000:]}\n{p.stderr[-3000:]}"
     return json.loads(lines[-1])
@@ -41,16 +41,8 @@ def test_data_parallel_host_logic_gloo(oracle):
     assert res["ranks"][0]["equals_single_process"] and res["ranks"][0]["ranks_identical"]
 
 
-# The overlapped all-reduce (all but the last backward layer's gradients
-# reduced on a side stream while that layer's backward runs) has not run on
-# B200s yet: its case runs with METALGYM_TEST_ALLREDUCE_OVERLAP=1.
-_OVERLAP = pytest.param("nccl-overlap", marks=pytest.mark.skipif(
-    os.environ.get("METALGYM_TEST_ALLREDUCE_OVERLAP") != "1",
-    reason="overlapped all-reduce not yet run on B200s (METALGYM_TEST_ALLREDUCE_OVERLAP=1)"))
-
-
 @pytest.mark.gpu
-@pytest.mark.parametrize("allreduce", ["nccl", "p2p", _OVERLAP])
+@pytest.mark.parametrize("allreduce", ["nccl", "p2p", "nccl-overlap"])
 def test_data_parallel_two_gpus(mg, allreduce):
     import torch
 
@@ -64,16 +56,16 @@ def test_data_parallel_two_gpus(mg, allreduce):
 
 
 @pytest.mark.gpu
-@pytest.mark.skipif(os.environ.get("METALGYM_TEST_COMM_WATCHDOG") != "1",
-                    reason="train() watchdog not yet run on B200s (METALGYM_TEST_COMM_WATCHDOG=1)")
 def test_rank_that_leaves_turns_into_an_error_two_gpus(mg):
     """A rank that stays out of the gradient all-reduce: the other rank's
-    train() returns MG_ERR_COMM within its communication timeout."""
+    train() returns MG_ERR_COMM within its communication timeout. NVLink
+    multicast (NVLS) is off in NCCL for this test: no rank leaves while its
+    memory is bound to a multicast object."""
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    res = launch("gpu-rank-leaves", limit=180)
+    res = launch("gpu-rank-leaves", limit=180, env={"NCCL_NVLS_ENABLE": "0"})
     assert res["ok"], res
     r0 = res["ranks"][0]
     assert r0["comm_error"] and r0["within_deadline"] and r0["second_comm_error"], r0

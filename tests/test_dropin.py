@@ -10,11 +10,12 @@ import subprocess
 from pathlib import Path
 
 import pytest
+from orc import reference_tree
 
 ROOT = Path(__file__).resolve().parent.parent
 BUILD = ROOT / "tests" / "_build"
 LIB_DIR = ROOT / "metalgym_b200"
-REFERENCE_TREE = Path(os.environ.get("METALGYM_REFERENCE", "/root/reference"))
+REFERENCE_TREE = reference_tree()
 REF_PROGRAMS = ["examples/CartPole/main.cpp", "examples/CartPoleContinuous/main.cpp", "examples/VoxelNav/main.cpp",
                 "bench/metalrl_bench.cpp", "bench/metalrl_bench_voxelnav.cpp"]
 OWN_EXAMPLES = ["cartpole", "cartpole_continuous", "voxelnav"]
@@ -34,8 +35,8 @@ def ref_binary(rel: str) -> Path:
 
 @pytest.mark.parametrize("rel", REF_PROGRAMS)
 def test_reference_programs_compile_unchanged(rel):
-    if not REFERENCE_TREE.exists():
-        pytest.skip("reference source tree not present")
+    if REFERENCE_TREE is None:
+        pytest.skip("reference source tree not present (set METALGYM_REFERENCE or build oracle/_ref)")
     compile_program(REFERENCE_TREE / rel, ref_binary(rel))
 
 

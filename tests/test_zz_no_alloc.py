@@ -2,7 +2,10 @@
 allocate device memory, checked through the C ABI against the existing
 entry points (mg_gemm_bf16 split-K partials + mg_reduce_partials, whose
 workspace the caller allocates) on two calls in a row, with the tolerance the
-other weight-gradient tests use (rtol 1e-5). Collected last on purpose."""
+other weight-gradient tests use (rtol 1e-5), and against an independent
+fp64 product x^T dz of the same bf16 inputs with the GEMM tests' tolerances
+(bf16-rounded output: rtol 1e-2, atol 1e-2 x scale; fp32 output: rtol 2e-3,
+atol 1e-3 x scale). Collected last on purpose."""
 import ctypes
 
 import numpy as np
@@ -41,6 +44,12 @@ def test_noalloc_matches_existing_entry_points_twice(mg, rows, M, N, splits, rou
         st = ctypes.c_int(0)
         assert mg.mg_device_status(1, ctypes.byref(st)) == 0 and st.value == 0
         torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-6, msg=f"call {call}")
+        exact = (x.double().t() @ dz.double()).float()
+        scale = exact.abs().max().item()
+        if round_bf16:
+            torch.testing.assert_close(out, exact, rtol=1e-2, atol=1e-2 * scale, msg=f"call {call} vs fp64")
+        else:
+            torch.testing.assert_close(out, exact, rtol=2e-3, atol=1e-3 * scale, msg=f"call {call} vs fp64")
 
 
 def test_noalloc_rejects_sizes_beyond_the_scratch(mg):
