@@ -54,6 +54,14 @@ int mg_version(void);
  * if `clear` is non-zero. Synchronous. Replaces the command-buffer error check
  * of model/ppo.h:507-515. */
 int mg_device_status(int clear, int* status);
+/* Phase trace of the 4-CTA cluster tile kernels (block, head and minibatch
+ * tile kernels; no counterpart in the reference): with a device buffer of
+ * uint64 [CTAs of the launch][64], thread 0 of every CTA writes %globaltimer
+ * (ns) at each phase boundary of its passes into its row, in order, for the
+ * kernels launched or captured afterwards; NULL (the default) turns it off.
+ * For profiling only: one buffer serves every launch, so the last kernel's
+ * stamps remain. */
+int mg_set_tile_trace(uint64_t* buffer);
 
 /* ---------------------------------------------------------------- GEMM */
 

@@ -90,6 +90,7 @@ SIGNATURES = {
     "mg_ppo_phase_ms": (I, [P, PF]),
     "mg_ppo_collect_fused": (I, [P, PI]),
     "mg_ppo_set_fused_minibatch": (I, [P, I]),
+    "mg_set_tile_trace": (I, [P]),
     "mg_ppo_act_greedy": (I, [P, I, P]),
     "mg_ppo_fused_minibatch": (I, [P, PI]),
     "mg_ppo_train_rows": (I, [P, P, U]),

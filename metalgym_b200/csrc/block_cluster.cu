@@ -77,6 +77,7 @@ int block_cluster_forward_args(const void* lnOut, const void* wUp, const void* w
     p.e.out = static_cast<__nv_bfloat16*>(h);
     p.e.ln = next;
     p.status = status_ptr();
+    p.trace = tile_trace();
     if (in) {
         p.in = BcInput{in->obs, in->mb, in->envRows, in->total, in->inDim,
                        static_cast<const __nv_bfloat16*>(in->w), static_cast<const __nv_bfloat16*>(in->b),
@@ -137,6 +138,7 @@ int block_cluster_backward_args(const void* dS, const void* wDown, const void* v
         p.e.inPartial = in->partial;
     }
     p.status = status_ptr();
+    p.trace = tile_trace();
     return MG_OK;
 }
 

@@ -81,6 +81,7 @@ struct BcParams {
     float* downPart;      // backward: [tile][512][128] partial sums of dW_down
     RowsEpi e;
     int* status;
+    uint64_t* trace;  // phase trace (tile_pass.cuh); null: off
 };
 
 // Maps (all SW128, 64-wide boxes):
@@ -261,6 +262,8 @@ __device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const B
     const int m0 = (int)(blockIdx.x / kRowsCluster) * kRowsBM;
     const int h0 = (int)q * kRowsBN;  // this CTA's hidden columns
     const uint32_t tmem = t.tmem;
+    t.trace = p.trace;
+    tp_mark(t);  // pass start
 
     if (threadIdx.x == 0 && t.ok()) {
         t.issuing(kTbFull1);
@@ -317,11 +320,13 @@ __device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const B
     // the mask tile arrived with full1: observe that phase before reading it
     if (BWD && ok) ok = tp_wait_warp(t, kTbFull1, p.status, kDevTimeoutFull);
     tc_fence_after();
+    tp_mark(t);  // first product done (warp 0)
     bc_hidden_tile<BWD>(smem, A2, kBcBwdM, tmem, ok);
     fence_async_smem();  // generic writes of A2 -> visible to the tensor core and TMA
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    tp_mark(t);  // hidden tile in shared memory
     if (threadIdx.x == 0) {
         // V_q / dV_q to global memory (the backward reads V, the weight gradient reads dV)
         for (int kb = 0; kb < 2; kb++)
@@ -341,6 +346,7 @@ __device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const B
     __syncwarp();
     const bool ok2 = tp_wait_warp(t, kTbMma2, p.status, kDevTimeoutDone);
     tc_fence_after();
+    tp_mark(t);  // second product done (warp 0)
     rows_tmem_to_tile(smem, tmem + 128, ok && ok2);
     if (BWD) {
         // this tile's weight-gradient partial sums: dW_up[:, h0..], dW_down[h0.., :]
@@ -371,13 +377,16 @@ __device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const B
             }
         }
     }
+    tp_mark(t);  // partial tile (and weight-gradient partials) written
     cluster_sync();  // every partial tile of the cluster is complete
+    tp_mark(t);  // cluster barrier passed
 
     RowsEpi e = p.e;
     if (BWD) e.inStage = reinterpret_cast<float*>(smem + kBcBwdLn);  // the lnOut tile is no longer needed
     rows_cluster_epilogue<BWD ? kRowsLNBackward : kRowsResidLN, RPC>(smem, reinterpret_cast<float*>(smem + kBcBwdM),
                                                                     q, m0, e);
 
+    tp_mark(t);  // row epilogue done
     if (threadIdx.x == 0) bulk_wait<0>();  // the V / dV store is complete
     t.flip(kTbFull1);
     t.flip(kTbFull2);

@@ -67,6 +67,7 @@ int head_tail_args(const void* fOut, const void* wHead, void* head, const Policy
     p.e.stdev = stdevF;
     p.e.partial = lnPart;
     p.status = status_ptr();
+    p.trace = tile_trace();
     return MG_OK;
 }
 

@@ -44,6 +44,7 @@ struct HeadTailParams {
     float* headPart;      // [tile][128][64] fp32
     RowsEpi e;            // the final LayerNorm's backward: out = dS, no resid
     int* status;
+    uint64_t* trace;      // phase trace (tile_pass.cuh); null: off
 };
 
 
@@ -66,6 +67,8 @@ __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, c
     const int tile = (int)(blockIdx.x >> 2);
     const int m0 = tile * kRowsBM;
     const uint32_t tmem = t.tmem;
+    t.trace = p.trace;
+    tp_mark(t);  // pass start
 
     if (threadIdx.x == 0) {
         if (t.ok()) {
@@ -92,6 +95,7 @@ __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, c
     __syncwarp();
     const bool ok1 = tp_wait_warp(t, kTbMma1, p.status, kDevTimeoutDone);
     tc_fence_after();
+    tp_mark(t);  // head product done (warp 0)
     if (warp < 4) {
         const int r = warp * 32 + lane;
         const int row = m0 + r;
@@ -144,6 +148,7 @@ __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, c
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    tp_mark(t);  // loss and dZ tile done
     if (warp == 1 && lane == 0) {
         if (ok1) {
             // dS = dZ W_head^T: A = dZ (K = 64, K-major), B = W_head as [N = 128][K = 64], K-major
@@ -169,6 +174,7 @@ __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, c
     __syncwarp();
     const bool ok2 = tp_wait_warp(t, kTbMma2, p.status, kDevTimeoutDone) && ok1;
     tc_fence_after();
+    tp_mark(t);  // head dX and dW_head products done (warp 0)
     {
         const int qd = warp & 3, cc = warp >> 2;
         if (qd == q) {
@@ -213,8 +219,10 @@ __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, c
         if (!ok1 && threadIdx.x == 0) mbar_wait(t.bar(kTbFull1), 0, p.status, kDevTimeoutFull);  // let the loads land
     }
 
+    tp_mark(t);  // dS tile written
     rows_cluster_epilogue<kRowsLNBackward, RPC, 1>(smem, reinterpret_cast<float*>(smem + kHtRed), (uint32_t)q, m0,
                                                    p.e);
+    tp_mark(t);  // row epilogue done
     t.flip(kTbFull1);
     t.flip(kTbMma1);
     t.flip(kTbMma2);

@@ -1,6 +1,7 @@
 // Host runtime: error strings, the device status word, TMA descriptors.
 #include "runtime.h"
 
+#include <atomic>
 #include <mutex>
 #include <set>
 #include <string>
@@ -118,6 +119,12 @@ int* status_ptr() {
     return cache[dev];
 }
 
+namespace {
+std::atomic<uint64_t*> g_tile_trace{nullptr};
+}
+
+uint64_t* tile_trace() { return g_tile_trace.load(std::memory_order_relaxed); }
+
 int make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride,
                    uint32_t box_outer) {
     EncodeTiledFn fn = encode_fn();
@@ -148,6 +155,11 @@ extern "C" {
 const char* mg_last_error(void) { return mg::g_last_error.c_str(); }
 
 int mg_version(void) { return MG_VERSION; }
+
+int mg_set_tile_trace(uint64_t* buffer) {
+    mg::g_tile_trace.store(buffer, std::memory_order_relaxed);
+    return MG_OK;
+}
 
 int mg_device_status(int clear, int* status) {
     int* p = mg::status_ptr();

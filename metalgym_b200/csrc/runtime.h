@@ -39,6 +39,9 @@ int cuda_fail(cudaError_t e, const char* what);
 // Device address of the status word of the current device (a __device__ int
 // in runtime.cu, looked up once per device with cudaGetSymbolAddress).
 int* status_ptr();
+// The device buffer of the tile kernels' phase trace (mg_set_tile_trace), or
+// null when tracing is off (the default).
+uint64_t* tile_trace();
 // A unique id of the calling thread's current CUDA context (cuCtxGetId; 0
 // when none is current or the driver lacks the call). Caches of per-context
 // device addresses compare it so that they are looked up again after a

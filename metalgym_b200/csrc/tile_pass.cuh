@@ -32,6 +32,10 @@ struct TilePass {
     // thread 0, merged kernels: the parity of the last load issued on each
     // full barrier (bit b), and which barriers have a load issued at all
     uint32_t lastLoad, loaded;
+    // phase trace (mg_set_tile_trace; null: off): thread 0 of each CTA
+    // writes %globaltimer at every tp_mark into trace[blockIdx.x][mark]
+    uint64_t* trace;
+    int mark;
 
     __device__ __forceinline__ uint64_t* bar(int b) const { return bars + b; }
     __device__ __forceinline__ uint32_t parity(int b) const { return (ph >> b) & 1u; }
@@ -43,6 +47,15 @@ struct TilePass {
         loaded |= 1u << b;
     }
 };
+
+constexpr int kTileTraceSlots = 64;
+
+// A phase boundary of the trace: every thread counts it, thread 0 stamps it.
+__device__ __forceinline__ void tp_mark(TilePass& t) {
+    if (t.trace && threadIdx.x == 0 && t.mark < kTileTraceSlots)
+        t.trace[(size_t)blockIdx.x * kTileTraceSlots + t.mark] = globaltimer();
+    t.mark++;
+}
 
 // Bounded wait of one thread for barrier b's current phase; false once the
 // CTA gave up (then without waiting).
@@ -98,6 +111,8 @@ __device__ __forceinline__ TilePass tp_setup(uint8_t* barMem, uint32_t tmemCols,
     t.merged = merged;
     t.lastLoad = 0;
     t.loaded = 0;
+    t.trace = nullptr;
+    t.mark = 0;
     return t;
 }
 
