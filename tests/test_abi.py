@@ -89,6 +89,7 @@ _NO_ARGUMENT_CHECK = {
     "mg_gemm_rows_splits", "mg_input_backward_num_partials", "mg_layernorm_backward_num_partials",
     "mg_gaussian_loss_num_partials", "mg_reduce_partials_num_norm_partials", "mg_gym_destroy", "mg_ppo_destroy",
     "mg_comm_destroy", "mg_host_free",
+    "mg_set_tile_trace",  # NULL turns the trace off
 }
 
 
