@@ -130,6 +130,7 @@ def run_mine(args, rank, world, local_rank, dist):
     model = PPOModel(gym, EMBED, SCALE, LAYERS, LR, HORIZON, seed=0)
     if args.collect != "auto":
         model.collect_fused = args.collect == "fused"
+    model.fused_minibatch = args.fused_minibatch
     comm = None
 
     def connect(m):
@@ -306,6 +307,8 @@ def run_mine(args, rank, world, local_rank, dist):
             "config": workload_config(world),
             "setup": {"collect": ("one persistent kernel (fused)" if model.collect_fused else
                                   "captured per-step graph"),
+                      "minibatch": ("tile passes as one kernel" if model.fused_minibatch else
+                                    "separate cluster kernels chained by PDL"),
                       "allreduce": ("none" if world == 1 else
                                     "NVLink peer memory (library kernels)" if args.allreduce == "p2p" else
                                     "NCCL, overlapped with the last backward layer" if args.allreduce_overlap else
@@ -655,10 +658,11 @@ def cpu_raw_env(seconds_budget=10.0):
 
 # ------------------------------------------------------------------ main
 
-def profile_minibatch(which):
+def profile_minibatch(which, fused_minibatch=False):
     """Builds the configuration's model, collects once, runs one minibatch and
     one forward as warm-up, then one minibatch and one forward inside the
-    profiler range."""
+    profiler range (fused_minibatch: the minibatch's tile passes as one
+    kernel, mg_ppo_set_fused_minibatch)."""
     import torch
 
     from metalgym_b200.session import Gym, PPOModel
@@ -670,6 +674,7 @@ def profile_minibatch(which):
     gym = Gym(env, n, seed=0)
     model = PPOModel(gym, embed, SCALE, blocks, LR, HORIZON, seed=0)
     model.minibatch_rows = rows
+    model.fused_minibatch = fused_minibatch
     model.collect()
 
     def minibatch(k):
@@ -684,6 +689,24 @@ def profile_minibatch(which):
     torch.cuda.profiler.start()
     minibatch(1)
     model.forward()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+
+
+def profile_collect():
+    """The configs[1] model (4096 CartPole envs, T = 32): one collect() as
+    warm-up, then one collect() inside the profiler range (the library's
+    default path: the fused collect kernel)."""
+    import torch
+
+    from metalgym_b200.session import Gym, PPOModel
+
+    gym = Gym(ENV, ENVS_PER_GPU, seed=0)
+    model = PPOModel(gym, EMBED, SCALE, LAYERS, LR, HORIZON, seed=0)
+    model.collect()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    model.collect()
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
 
@@ -708,12 +731,20 @@ def main():
     ap.add_argument("--collect", choices=["auto", "graph", "fused"], default="auto",
                     help="collect(): the library's choice (default: the persistent kernel of collect_fused.cu "
                          "where it applies, up to 4096 envs), the captured per-step graph, or the kernel")
+    ap.add_argument("--fused-minibatch", action="store_true",
+                    help="a minibatch's block forwards, head and block backwards as one kernel "
+                         "(mg_ppo_set_fused_minibatch; default: the separate kernels)")
     ap.add_argument("--profile-minibatch", choices=["c3", "c4", "c5"],
                     help="profiling driver: one training minibatch and one forward of that configuration, "
                          "bracketed by cudaProfilerStart / Stop (for ncu --profile-from-start off); no JSON line")
+    ap.add_argument("--profile-collect", action="store_true",
+                    help="profiling driver: one collect() of the configs[1] model inside the profiler range")
     args = ap.parse_args()
     if args.profile_minibatch:
-        profile_minibatch(args.profile_minibatch)
+        profile_minibatch(args.profile_minibatch, args.fused_minibatch)
+        return
+    if args.profile_collect:
+        profile_collect()
         return
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

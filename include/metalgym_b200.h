@@ -558,7 +558,12 @@ int mg_ppo_set_comm_timeout(mg_ppo_t model, float seconds);
 
 /* ---------------------------------------------------------------- NCCL / host memory */
 
-/* NCCL communicator helpers (libnccl.so.2 is loaded on first use). */
+/* NCCL communicator helpers (libnccl.so.2 is loaded on first use).
+ * mg_comm_init connects every channel when the communicator is created
+ * (it sets NCCL_RUNTIME_CONNECT=0 unless the caller set it): with NCCL's lazy
+ * connection the first collective would handshake with every peer on the
+ * host, and a peer that never joins would block the caller there, where the
+ * train() watchdog (mg_ppo_set_comm_timeout) cannot see it. */
 int mg_comm_unique_id(void* out128);
 int mg_comm_init(int world, int rank, const void* id128, int device, void** comm);
 int mg_comm_destroy(void* comm);

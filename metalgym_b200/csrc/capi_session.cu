@@ -2,6 +2,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -424,6 +425,11 @@ int mg_comm_init(int world, int rank, const void* id128, int device, void** comm
     void* h = nccl_handle();
     if (!h) return mg::fail(MG_ERR_COMM, "libnccl.so.2 not found");
     if (device >= 0) MG_CUDA_TRY(cudaSetDevice(device));
+    // connect every channel now, while all ranks take part: with NCCL's lazy
+    // connection the first collective would handshake with every peer on the
+    // host, and a peer that never joins would block the caller there, out of
+    // reach of the train() watchdog (a caller's own setting is kept)
+    setenv("NCCL_RUNTIME_CONNECT", "0", 0);
     auto fn = reinterpret_cast<decltype(&ncclCommInitRank)>(dlsym(h, "ncclCommInitRank"));
     ncclUniqueId id;
     std::memcpy(&id, id128, sizeof(id));

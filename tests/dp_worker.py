@@ -174,12 +174,20 @@ def run_gpu(rank, world, local, dist, allreduce):
     return out
 
 
+def log(rank, msg):
+    """Progress on stderr, so a failing run shows where each rank was."""
+    import time
+
+    print(f"[rank {rank} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def run_gpu_rank_leaves(rank, world, local, dist):
-    """Rank 0 trains with a 5 s communication timeout while rank 1 stays out
-    of the all-reduce (it leaves between steps, with nothing in flight): rank
-    0's train() must fail with MG_ERR_COMM (6) well within the deadline
-    instead of blocking, and keep failing; then rank 1 aborts its own
-    communicator. The failure is made on the host; no kernel is broken."""
+    """Both ranks train one step together; then rank 1 leaves between steps
+    (with nothing in flight) and stays out of the next all-reduce. Rank 0
+    trains with a 5 s communication timeout: its train() must fail with
+    MG_ERR_COMM (6) well within the deadline instead of blocking, and keep
+    failing; then rank 1 aborts its own communicator. The failure is made on
+    the host; no kernel is broken."""
     import time
 
     import torch
@@ -196,8 +204,12 @@ def run_gpu_rank_leaves(rank, world, local, dist):
     comm = nccl_comm(dist, rank, world, local)
     model.set_comm(comm, rank, world)
     model.set_comm_timeout(5.0)
+    log(rank, "communicator ready; one step with both ranks")
+    model.collect()
+    model.train(1)
     model.collect()
     dist.barrier()
+    log(rank, "rank 1 leaves")
     out = {}
     if rank == 0:
         t0 = time.time()
@@ -206,19 +218,23 @@ def run_gpu_rank_leaves(rank, world, local, dist):
             out["comm_error"] = False
         except MgError as e:
             out["comm_error"] = "code 6" in str(e)
+        log(rank, f"train() returned after {time.time() - t0:.1f} s: comm_error={out['comm_error']}")
         out["within_deadline"] = time.time() - t0 < 60.0
         try:
             model.train(1)
             out["second_comm_error"] = False
         except MgError as e:
             out["second_comm_error"] = "code 6" in str(e)
+        log(rank, f"second train(): comm_error={out['second_comm_error']}")
     dist.barrier()  # rank 1 stayed out until rank 0 gave up
+    log(rank, "past the barrier")
     if rank != 0:
         metalgym_b200.check(metalgym_b200.lib().mg_comm_abort(comm), "mg_comm_abort")
         out["aborted"] = True
     model.close()
     gym.close()
     destroy_comm(comm)  # nothing to do for an aborted communicator
+    log(rank, "closed")
     return out
 
 

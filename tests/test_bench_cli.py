@@ -15,7 +15,7 @@ def test_bench_options_parse():
                        timeout=120, cwd=ROOT)
     assert r.returncode == 0, r.stderr
     for opt in ("--gpus", "--steps", "--warmup", "--impl", "--allreduce", "--allreduce-overlap", "--collect",
-                "--c4-action", "--profile-minibatch"):
+                "--c4-action", "--profile-minibatch", "--profile-collect", "--fused-minibatch"):
         assert opt in r.stdout, opt
 
 
