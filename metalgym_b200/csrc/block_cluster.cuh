@@ -296,16 +296,11 @@ __device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const B
             for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcB2 + kb * 16384, &tm.b2, h0 + 64 * kb, 0, t.bar(kTbFull2));
         }
     }
-    constexpr int EPI = BWD ? kRowsLNBackward : kRowsResidLN;
-    RowsPrefetch<EPI, RPC> pf;
-    if (!INPUT) pf = rows_prefetch<EPI, RPC>(q, m0, p.e);  // the epilogue's inputs, while the products run
     if (INPUT) {
         // the A tile is computed here: the input layer and the first LayerNorm
         bc_input_prologue(smem, reinterpret_cast<float*>(smem + A2), q, m0, p.M, p.in);
         cluster_sync();  // every CTA's rows are in every CTA's A tile
         tc_fence_after();
-        // h is the prologue's output: each thread reads back what it wrote
-        pf = rows_prefetch<EPI, RPC>(q, m0, p.e);
     }
     if (warp == 1 && lane == 0) {
         if (tp_wait(t, kTbFull1, p.status, kDevTimeoutFull)) {
@@ -388,7 +383,8 @@ __device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const B
 
     RowsEpi e = p.e;
     if (BWD) e.inStage = reinterpret_cast<float*>(smem + kBcBwdLn);  // the lnOut tile is no longer needed
-    rows_cluster_epilogue<EPI, RPC>(smem, reinterpret_cast<float*>(smem + kBcBwdM), q, m0, e, &pf);
+    rows_cluster_epilogue<BWD ? kRowsLNBackward : kRowsResidLN, RPC>(smem, reinterpret_cast<float*>(smem + kBcBwdM),
+                                                                    q, m0, e);
 
     tp_mark(t);  // row epilogue done
     if (threadIdx.x == 0) bulk_wait<0>();  // the V / dV store is complete

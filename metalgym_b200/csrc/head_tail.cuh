@@ -69,8 +69,6 @@ __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, c
     const uint32_t tmem = t.tmem;
     t.trace = p.trace;
     tp_mark(t);  // pass start
-    // the LayerNorm backward's inputs, while the copies and products run
-    const RowsPrefetch<kRowsLNBackward, RPC> pf = rows_prefetch<kRowsLNBackward, RPC>((uint32_t)q, m0, p.e);
 
     if (threadIdx.x == 0) {
         if (t.ok()) {
@@ -223,7 +221,7 @@ __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, c
 
     tp_mark(t);  // dS tile written
     rows_cluster_epilogue<kRowsLNBackward, RPC, 1>(smem, reinterpret_cast<float*>(smem + kHtRed), (uint32_t)q, m0,
-                                                   p.e, &pf);
+                                                   p.e);
     tp_mark(t);  // row epilogue done
     t.flip(kTbFull1);
     t.flip(kTbMma1);

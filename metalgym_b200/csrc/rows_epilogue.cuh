@@ -46,78 +46,14 @@ struct RowsEpi {
 };
 constexpr int kRowsInputMaxDim = 32;
 
-// Rows per thread of the epilogue, and the tile row (within this CTA's 32)
-// of thread row t: kRowsResidLN: row warp + 16 t; kRowsLNBackward: the
-// virtual-warp order of k_layernorm_backward (see below).
-template <int EPI, int RPC>
-struct RowsMap {
-    static constexpr int J = RPC / 8;
-    static constexpr int NR = EPI == kRowsResidLN ? 2 : (RPC == 32 ? 4 : 2);
-    __device__ __forceinline__ static bool active(int warp) { return EPI == kRowsResidLN || RPC != 32 || warp < 8; }
-    __device__ __forceinline__ static int tile_row(int warp, int t) {
-        if (EPI == kRowsResidLN) return warp + 16 * t;
-        const int pr = warp + 16 * (t / J), j = t % J;
-        return (pr / 8) * RPC + (pr % 8) + 8 * j;
-    }
-};
-
-// The global-memory inputs of rows_cluster_epilogue for this thread's rows,
-// loaded ahead of it (they do not depend on the kernel's products, so a
-// kernel can load them while its copies and products run): kRowsResidLN: h
-// before the residual add, gamma and beta of the LayerNorm; kRowsLNBackward:
-// x-hat, sigma, the skip gradient (when e.resid) and gamma.
-template <int EPI, int RPC>
-struct RowsPrefetch {
-    static constexpr int NR = RowsMap<EPI, RPC>::NR;
-    float4 in[NR];    // h (kRowsResidLN) / x-hat (kRowsLNBackward)
-    float4 skip[NR];  // the skip gradient (kRowsLNBackward with e.resid)
-    float sd[NR];     // sigma (kRowsLNBackward)
-    float4 g, b;      // gamma (and beta for kRowsResidLN)
-};
-
-template <int EPI, int RPC>
-__device__ __forceinline__ RowsPrefetch<EPI, RPC> rows_prefetch(uint32_t q, int m0, const RowsEpi& e) {
-    using Map = RowsMap<EPI, RPC>;
-    constexpr int E = kRowsBN;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int c0 = lane * 4;
-    RowsPrefetch<EPI, RPC> pf;
-    if (EPI == kRowsResidLN) {
-        pf.g = bf4_load(e.ln.gamma + c0);
-        pf.b = bf4_load(e.ln.beta + c0);
-    } else {
-        pf.g = bf4_load(e.gamma + c0);
-        pf.b = make_float4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int t = 0; t < Map::NR; t++) {
-        const int row = m0 + 32 * (int)q + Map::tile_row(warp, t);
-        const bool live = Map::active(warp) && row < e.M;
-        pf.in[t] = make_float4(0, 0, 0, 0);
-        pf.skip[t] = make_float4(0, 0, 0, 0);
-        pf.sd[t] = 1.0f;
-        if (!live) continue;
-        if (EPI == kRowsResidLN) {
-            pf.in[t] = bf4_load(e.resid + (size_t)row * E + c0);
-        } else {
-            pf.in[t] = bf4_load(e.xNorm + (size_t)row * E + c0);
-            pf.sd[t] = e.stdev[row];
-            if (e.resid) pf.skip[t] = bf4_load(e.resid + (size_t)row * E + c0);
-        }
-    }
-    return pf;
-}
-
 // After the cluster barrier that completes every CTA's tile: this CTA's 32
 // rows of the tile (tile rows of the cluster at the same offset `smem` in
 // every CTA), the sum of the 4 tiles in CTA order, then the epilogue. `red`:
 // kRowsRedBytes of this CTA's shared memory, unused by the tiles.
 // NSUM = 1: the tile is this CTA's own and complete (no cluster).
-// pf: the global inputs, loaded ahead by rows_prefetch (null: loaded here).
 template <int EPI, int RPC, int NSUM = (int)kRowsCluster>
 __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red, uint32_t q, int m0,
-                                                      const RowsEpi& e,
-                                                      const RowsPrefetch<EPI, RPC>* pf = nullptr) {
+                                                      const RowsEpi& e) {
     constexpr int E = kRowsBN;
     // x / E as x * (1 / E): exact for a power of two; 1 / x as the correctly
     // rounded reciprocal: the same values as the LayerNorm kernels' divisions
@@ -131,16 +67,22 @@ __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red,
     // dbeta over them in that order; virtual warp (g, v) is warp 8 g + v (mod
     // 16) here.
     constexpr int G = 32 / RPC;
-    constexpr int J = RowsMap<EPI, RPC>::J;
-    constexpr int NR = RowsMap<EPI, RPC>::NR;
-    const bool active = RowsMap<EPI, RPC>::active(warp);
+    constexpr int J = RPC / 8;
+    constexpr int NR = EPI == kRowsResidLN ? 2 : (RPC == 32 ? 4 : 2);
+    const bool active = EPI == kRowsResidLN || RPC != 32 || warp < 8;
     const int c0 = lane * 4;
     int rows[NR];
     bool live[NR];
     float4 acc[NR];
 #pragma unroll
     for (int t = 0; t < NR; t++) {
-        const int tl = RowsMap<EPI, RPC>::tile_row(warp, t);  // row within this CTA's 32
+        int tl;  // row within this CTA's 32
+        if (EPI == kRowsResidLN) {
+            tl = warp + 16 * t;
+        } else {
+            const int pr = warp + 16 * (t / J), j = t % J;
+            tl = (pr / 8) * RPC + (pr % 8) + 8 * j;
+        }
         const int tr = 32 * (int)q + tl;
         rows[t] = m0 + tr;
         live[t] = active && rows[t] < e.M;
@@ -160,13 +102,12 @@ __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red,
     }
 
     if (EPI == kRowsResidLN) {
-        const float4 gm = pf ? pf->g : bf4_load(e.ln.gamma + c0), bt = pf ? pf->b : bf4_load(e.ln.beta + c0);
+        const float4 gm = bf4_load(e.ln.gamma + c0), bt = bf4_load(e.ln.beta + c0);
         const float g[4] = {gm.x, gm.y, gm.z, gm.w}, b[4] = {bt.x, bt.y, bt.z, bt.w};
         float v[NR][4], ms[2 * NR];  // ms: row sums (0..NR-1), sums of squares (NR..)
 #pragma unroll
         for (int t = 0; t < NR; t++) {
-            const float4 hin = pf ? pf->in[t]
-                                  : live[t] ? bf4_load(e.resid + (size_t)rows[t] * E + c0) : make_float4(0, 0, 0, 0);
+            const float4 hin = live[t] ? bf4_load(e.resid + (size_t)rows[t] * E + c0) : make_float4(0, 0, 0, 0);
             // the residual add of the down projection (kEpiBf16Resid), then h as bf16
             v[t][0] = round_bf16(hin.x + round_bf16(acc[t].x));
             v[t][1] = round_bf16(hin.y + round_bf16(acc[t].y));
@@ -208,15 +149,14 @@ __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red,
         }
     } else {
         // red: [G][8 virtual warps][dgamma | dbeta]
-        const float4 gm = pf ? pf->g : bf4_load(e.gamma + c0);
+        const float4 gm = bf4_load(e.gamma + c0);
         const float g[4] = {gm.x, gm.y, gm.z, gm.w};
         float xn[NR][4], dxn[NR][4], s12[2 * NR], rdev[NR];  // s12: sums of dxn (0..NR-1), of dxn x-hat (NR..)
         float dg[4], db[4];
 #pragma unroll
         for (int t = 0; t < NR; t++) {
-            const float4 x4 = pf ? pf->in[t]
-                                 : live[t] ? bf4_load(e.xNorm + (size_t)rows[t] * E + c0) : make_float4(0, 0, 0, 0);
-            rdev[t] = __frcp_rn(pf ? pf->sd[t] : live[t] ? e.stdev[rows[t]] : 1.0f);
+            const float4 x4 = live[t] ? bf4_load(e.xNorm + (size_t)rows[t] * E + c0) : make_float4(0, 0, 0, 0);
+            rdev[t] = __frcp_rn(live[t] ? e.stdev[rows[t]] : 1.0f);
             xn[t][0] = x4.x;
             xn[t][1] = x4.y;
             xn[t][2] = x4.z;
@@ -257,7 +197,7 @@ __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red,
             for (int i = 0; i < 4; i++)
                 o[i] = __fmul_rn(rdev[t], __fsub_rn(__fsub_rn(dxn[t][i], s12[t]), __fmul_rn(xn[t][i], s12[NR + t])));
             if (e.resid) {  // the skip add: bf16(bf16(dx) + resid)
-                const float4 rs = pf ? pf->skip[t] : bf4_load(e.resid + (size_t)rows[t] * E + c0);
+                const float4 rs = bf4_load(e.resid + (size_t)rows[t] * E + c0);
                 o[0] = __fadd_rn(rbf(o[0]), rs.x);
                 o[1] = __fadd_rn(rbf(o[1]), rs.y);
                 o[2] = __fadd_rn(rbf(o[2]), rs.z);
