@@ -21,6 +21,11 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_
     // 128-column accumulators: 2 (forward), 4 (backward)
     TilePass t = tp_setup(smem + (BWD ? kBcBwdBar : kBcFwdBar), BWD ? 512 : 256, false);
     if (INPUT) cluster_arrive_relaxed();  // this CTA has started (waited on before the peers' A tiles are written)
+    // a training minibatch's observation rows do not depend on the preceding
+    // kernel: stage them while it finishes
+    if (INPUT && p.in.earlyObs)
+        bc_input_stage_obs(reinterpret_cast<float*>(smem + kBcFwdA2), cluster_ctarank(),
+                           (int)(blockIdx.x / kRowsCluster) * kRowsBM, p.M, p.in);
     mg_pdl_wait();  // activations and weights come from earlier kernels
     bc_pass<BWD, RPC, INPUT>(smem, tm, p, t);
 }
@@ -85,7 +90,8 @@ int block_cluster_forward_args(const void* lnOut, const void* wUp, const void* w
                        LnOutputs{static_cast<const __nv_bfloat16*>(in->gamma),
                                  static_cast<const __nv_bfloat16*>(in->beta),
                                  static_cast<__nv_bfloat16*>(in->xNorm),
-                                 static_cast<__nv_bfloat16*>(const_cast<void*>(lnOut)), in->stdev}};
+                                 static_cast<__nv_bfloat16*>(const_cast<void*>(lnOut)), in->stdev},
+                       in->mb != nullptr};
     }
     return MG_OK;
 }

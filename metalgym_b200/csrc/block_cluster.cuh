@@ -71,6 +71,11 @@ struct BcInput {
     const __nv_bfloat16* b;  // [128]
     __nv_bfloat16* h;        // [M][128]
     LnOutputs ln;
+    // the observation rows may be staged before the kernel's PDL wait: they
+    // come through a training minibatch's schedule from rollout slots that
+    // collect() filled before the train work began (never the output of the
+    // preceding kernel, as the env step's is for a collect-step forward)
+    bool earlyObs;
 };
 
 struct BcParams {
@@ -129,15 +134,10 @@ __device__ __forceinline__ void bc_tmem_to_global(uint8_t* stage, float* dst, in
 // warp, lane l: columns 4l..4l+3), their LayerNorm output written into the A
 // tile of every CTA of the cluster. `stage`: free shared memory for the input
 // weights (fp32) and the rows' observations.
-__device__ __forceinline__ void bc_input_prologue(uint8_t* smem, float* stage, uint32_t q, int m0, int M,
-                                                  const BcInput& in) {
-    constexpr int E = kRowsBN;
-    constexpr float kInvE = 1.0f / E;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int c0 = lane * 4;
-    float* sW = stage;                    // [inDim][128]
-    float* sObs = stage + in.inDim * E;   // [32][inDim]
-    for (int i = threadIdx.x; i < in.inDim * E; i += blockDim.x) sW[i] = __bfloat162float(in.w[i]);
+// The observation rows of this CTA's 32 rows into the staging area after the
+// input weights (stage + inDim x 128 floats), read through the row map.
+__device__ __forceinline__ void bc_input_stage_obs(float* stage, uint32_t q, int m0, int M, const BcInput& in) {
+    float* sObs = stage + in.inDim * kRowsBN;  // [32][inDim]
     for (int i = threadIdx.x; i < 32 * in.inDim; i += blockDim.x) {
         const int row = m0 + 32 * (int)q + i / in.inDim;
         float o = 0.0f;
@@ -147,6 +147,18 @@ __device__ __forceinline__ void bc_input_prologue(uint8_t* smem, float* stage, u
         }
         sObs[i] = o;
     }
+}
+
+__device__ __forceinline__ void bc_input_prologue(uint8_t* smem, float* stage, uint32_t q, int m0, int M,
+                                                  const BcInput& in) {
+    constexpr int E = kRowsBN;
+    constexpr float kInvE = 1.0f / E;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = lane * 4;
+    float* sW = stage;                    // [inDim][128]
+    float* sObs = stage + in.inDim * E;   // [32][inDim]
+    for (int i = threadIdx.x; i < in.inDim * E; i += blockDim.x) sW[i] = __bfloat162float(in.w[i]);
+    if (!in.earlyObs) bc_input_stage_obs(stage, q, m0, M, in);  // else staged before the PDL wait
     __syncthreads();
     const float4 bias = bf4_load(in.b + c0);
     const float4 gm = bf4_load(in.ln.gamma + c0), bt = bf4_load(in.ln.beta + c0);

@@ -11,7 +11,7 @@ namespace mg {
 
 namespace {
 
-template <int RPC>
+template <int RPC, int AD>
 __global__ void __launch_bounds__(kRowsThreads, 1)
     k_head_tail(const __grid_constant__ CUtensorMap tmF, const __grid_constant__ CUtensorMap tmW,
                 const HeadTailParams p) {
@@ -24,14 +24,15 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     }
     TilePass t = tp_setup(smem + kHtBar, 256, false);
     mg_pdl_wait();
-    ht_pass<RPC>(smem, tmF, tmW, p, t);
+    ht_pass<RPC, AD>(smem, tmF, tmW, p, t);
 }
 
 template <int RPC>
 int launch_ht(const CUtensorMap& tf, const CUtensorMap& tw, const HeadTailParams& p, cudaStream_t st) {
-    auto kern = k_head_tail<RPC>;
-    static std::atomic<uint64_t> attr_done{0};
-    if (int rc = smem_limit_once(kern, kHtSmem, attr_done)) return rc;
+    // two actions (CartPole): the loss with its loops unrolled
+    auto kern = p.loss.actDim == 2 ? k_head_tail<RPC, 2> : k_head_tail<RPC, 0>;
+    static std::atomic<uint64_t> attr_done[2] = {};  // per kernel variant
+    if (int rc = smem_limit_once(kern, kHtSmem, attr_done[p.loss.actDim == 2 ? 1 : 0])) return rc;
     const int grid = ((p.M + kRowsBM - 1) / kRowsBM) * 4;
     MG_CUDA_TRY(mg_launch(kern, dim3(grid), dim3(kRowsThreads), (size_t)kHtSmem, st, tf, tw, p));
     return check_launch("k_head_tail");

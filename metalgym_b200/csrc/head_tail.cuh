@@ -54,10 +54,11 @@ int head_tail_args(const void* fOut, const void* wHead, void* head, const Policy
                    const void* gammaF, const void* xNormF, const float* stdevF, void* dS, float* lnPart, int M,
                    CUtensorMap& tf, CUtensorMap& tw, HeadTailParams& p);
 
-// The pass over tile blockIdx.x / 4 as CTA q = blockIdx.x % 4 of the tile.
+// The pass over tile blockIdx.x / 4 as CTA q = blockIdx.x % 4 of the tile;
+// AD > 0: the head has AD actions (the loss with its loops unrolled).
 // Standalone (!t.merged): frees its 256 TMEM columns (logits 0..63, dW_head
 // 64..127, dS 128..255) before the epilogue. Merged: ends at a pass boundary.
-template <int RPC>
+template <int RPC, int AD = 0>
 __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, const CUtensorMap& tmW,
                                         const HeadTailParams& p, TilePass& t) {
     __nv_bfloat16* hs = reinterpret_cast<__nv_bfloat16*>(smem + kHtH);
@@ -123,8 +124,8 @@ __device__ __forceinline__ void ht_pass(uint8_t* smem, const CUtensorMap& tmF, c
         uint32_t packed[kLossHeadDim / 2];
         float st[5];
         bool lossOk = false;
-        if (row < p.M) lossOk = policy_loss_compute(p.loss, row, hs + r * kHtHStride, own ? p.status : nullptr,
-                                                    packed, st);
+        if (row < p.M)
+            lossOk = policy_loss_compute<AD>(p.loss, row, hs + r * kHtHStride, own ? p.status : nullptr, packed, st);
         if (!lossOk) {
 #pragma unroll
             for (int i = 0; i < kLossHeadDim / 2; i++) packed[i] = 0;

@@ -40,7 +40,7 @@ struct MtParams {
     HeadTailParams head;
 };
 
-template <int RPC>
+template <int RPC, int AD>
 __global__ void __launch_bounds__(kRowsThreads, 1) k_minibatch_tiles(const __grid_constant__ MtParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -55,19 +55,23 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_minibatch_tiles(const __gri
     }
     TilePass t = tp_setup(smem + kMtBar, 512, true);
     cluster_arrive_relaxed();  // this CTA has started (waited on before the peers' A tiles are written)
-    mg_pdl_wait();             // the observations, weights and schedule come from earlier kernels
+    if (p.fwd[0].in.earlyObs)  // the minibatch's observation rows, while the preceding kernel finishes
+        bc_input_stage_obs(reinterpret_cast<float*>(smem + kBcFwdA2), cluster_ctarank(),
+                           (int)(blockIdx.x / kRowsCluster) * kRowsBM, p.fwd[0].M, p.fwd[0].in);
+    mg_pdl_wait();             // the weights come from earlier kernels
     bc_pass<false, 32, true>(smem, p.fwdMaps[0], p.fwd[0], t);
     for (int n = 1; n < p.L; n++) bc_pass<false, 32, false>(smem, p.fwdMaps[n], p.fwd[n], t);
-    ht_pass<RPC>(smem, p.headF, p.headW, p.head, t);
+    ht_pass<RPC, AD>(smem, p.headF, p.headW, p.head, t);
     for (int n = p.L - 1; n >= 0; n--) bc_pass<true, RPC, false>(smem, p.bwdMaps[n], p.bwd[n], t);
     tp_teardown(t, p.head.status);
 }
 
 template <int RPC>
 int launch_mt(const MtParams& p, int M, cudaStream_t st) {
-    auto kern = k_minibatch_tiles<RPC>;
-    static std::atomic<uint64_t> attr_done{0};
-    if (int rc = smem_limit_once(kern, kMtSmem, attr_done)) return rc;
+    // two actions (CartPole): the loss with its loops unrolled
+    auto kern = p.head.loss.actDim == 2 ? k_minibatch_tiles<RPC, 2> : k_minibatch_tiles<RPC, 0>;
+    static std::atomic<uint64_t> attr_done[2] = {};  // per kernel variant
+    if (int rc = smem_limit_once(kern, kMtSmem, attr_done[p.head.loss.actDim == 2 ? 1 : 0])) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((M + kRowsBM - 1) / kRowsBM) * kRowsCluster));
     cfg.blockDim = dim3(kRowsThreads);

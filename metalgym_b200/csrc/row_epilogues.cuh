@@ -47,13 +47,19 @@ __device__ __forceinline__ __nv_bfloat16 loss_tobf(float x) { return __float2bfl
 
 // Row r of the minibatch, its head row h (64 bf16): the row's dZ (64 bf16,
 // packed in pairs) and its 5 statistics. Returns false (and records
-// kDevBadAction) for an action outside [0, actDim).
+// kDevBadAction) for an action outside [0, actDim). AD > 0: the caller
+// guarantees L.actDim == AD, and every loop over the actions has a known trip
+// count (the same operations in the same order, so the same bits, in far
+// less code: the loss runs once per kernel launch, from a cold instruction
+// cache).
+template <int AD = 0>
 __device__ inline bool policy_loss_compute(const PolicyLossRows& L, int r, const __nv_bfloat16* h, int* status,
                                            uint32_t* packed, float* st) {
+    static_assert(AD >= 0 && AD <= 8, "AD: 0 (the actions known at run time) or 1..8");
     const int64_t g = L.mb ? (int64_t)mg_minibatch_row(*L.mb, r, L.envRows, L.total) : r;
     const float* advStats = L.advStats;
     if (L.mb && L.mb->slot >= 0 && advStats) advStats += 2 * L.mb->slot;  // per-slot statistics
-    const int actDim = L.actDim;
+    const int actDim = AD > 0 ? AD : L.actDim;
     const float scale = __fdiv_rn(1.0f, (float)L.rows);
     // exp(logp_j) is needed twice (entropy, gradient): keep up to kCache of them
     constexpr int kCache = 8;

@@ -1,10 +1,12 @@
 """Learning curves of the CartPole PPO loop against the CPU reference path.
 
-tests/golden/learning_curves.npz holds the mean episode length per iteration
-(envs x T / number of done flags of the rollout) for five seeds of the
-reference's environment code with the C++ restatement of its PPO arithmetic
-(tests/golden/make_learning_curves.py: 1024 envs, T = 32, embed 64, hidden
-256, 2 blocks, train(4), 15 iterations). The GPU runs the same five seeds
+tests/golden/learning_curves.npz and learning_curves_c3.npz hold the mean
+episode length per iteration (envs x T / number of done flags of the
+rollout) for five seeds of the reference's environment code with the C++
+restatement of its PPO arithmetic (tests/golden/make_learning_curves.py):
+1024 envs, T = 32, embed 64, hidden 256, 2 blocks, train(4), 15 iterations;
+and BASELINE configs[2]'s shape, 4096 envs, T = 32, embed 128, hidden 512,
+2 blocks, train(4), 20 iterations. The GPU runs the same five seeds
 (same initial weights, env seeds and slot shuffles). Training trajectories
 diverge once a sampled action differs, so the comparison is statistical.
 The band:
@@ -23,13 +25,16 @@ import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
-GOLD = Path(__file__).resolve().parent / "golden" / "learning_curves.npz"
+GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
-def test_learning_curves_within_reference_band(mg):
+@pytest.mark.parametrize("fixture", ["learning_curves.npz", "learning_curves_c3.npz"])
+def test_learning_curves_within_reference_band(mg, fixture):
     from metalgym_b200.session import Gym, PPOModel
 
-    g = np.load(GOLD)
+    if not (GOLDEN / fixture).exists():
+        pytest.skip(f"{fixture} not generated (tests/golden/make_learning_curves.py)")
+    g = np.load(GOLDEN / fixture)
     ref = g["lengths"]
     cfg = ast.literal_eval(str(g["config"][0]))
     gpu = []
