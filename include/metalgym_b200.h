@@ -566,6 +566,10 @@ int mg_ppo_set_comm_timeout(mg_ppo_t model, float seconds);
  * train() watchdog (mg_ppo_set_comm_timeout) cannot see it. */
 int mg_comm_unique_id(void* out128);
 int mg_comm_init(int world, int rank, const void* id128, int device, void** comm);
+/* Destroy and abort first release the train graphs of every model bound to
+ * the communicator (mg_ppo_set_comm): NCCL waits until each graph that
+ * captured its collectives is gone, so a graph kept alive would block the
+ * call for good. Those models recapture at their next train(). */
 int mg_comm_destroy(void* comm);
 /* Aborts the communicator and its operations in flight (ncclCommAbort), for
  * a rank that leaves a data-parallel job. The handle is freed: later

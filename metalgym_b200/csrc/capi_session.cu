@@ -449,6 +449,7 @@ int mg_comm_abort(void* comm) {
     auto fn = reinterpret_cast<decltype(&ncclCommAbort)>(dlsym(h, "ncclCommAbort"));
     if (!fn) return mg::fail(MG_ERR_COMM, "ncclCommAbort not found");
     mg::comm_mark_aborted(comm);
+    mg::comm_release_graphs(comm);  // NCCL's abort waits for the graphs that captured its collectives
     return fn(static_cast<ncclComm_t>(comm)) == ncclSuccess ? MG_OK : mg::fail(MG_ERR_COMM, "ncclCommAbort failed");
 }
 
@@ -458,6 +459,7 @@ int mg_comm_destroy(void* comm) {
     void* h = nccl_handle();
     if (!h) return mg::fail(MG_ERR_COMM, "libnccl.so.2 not found");
     auto fn = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));
+    mg::comm_release_graphs(comm);  // as for the abort: the destroy waits for them
     return fn(static_cast<ncclComm_t>(comm)) == ncclSuccess ? MG_OK : mg::fail(MG_ERR_COMM, "ncclCommDestroy failed");
 }
 

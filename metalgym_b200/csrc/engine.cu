@@ -257,6 +257,7 @@ PpoEngine::PpoEngine(GymCore* g, int embed, int scale, int layers, float learnin
 // Touches nothing of the gym, which may already be gone (a garbage collector
 // can finalise a borrowed gym before the model that borrowed it).
 PpoEngine::~PpoEngine() {
+    comm_unbind_graph(comm, &trainExec);
     if (gym && gym->stillBusy()) return;  // leaked on purpose, as GymCore's buffers
     int cur = 0;
     cudaGetDevice(&cur);
@@ -601,6 +602,7 @@ int PpoEngine::waitStream(const char* what) {
         if (x->nc->getAsyncError(x->comm, &a) != ncclSuccess) return 1;
         return a != ncclSuccess && a != ncclInProgress;
     };
+    o.release = [](void* p) { comm_release_graphs(static_cast<Ctx*>(p)->comm); };
     o.abort = [](void* p) {
         Ctx* x = static_cast<Ctx*>(p);
         x->nc->commAbort(x->comm);
@@ -617,10 +619,6 @@ int PpoEngine::waitStream(const char* what) {
     if (r == kWatchCudaError) return cuda_fail(c.err, what);
     comm_mark_aborted(comm);
     if (!drained) gym->busy = true;
-    if (trainExec) {  // it holds the aborted communicator (freed when it completes, if still in flight)
-        cudaGraphExecDestroy(trainExec);
-        trainExec = nullptr;
-    }
     std::ostringstream m;
     m << what << ": the gradient all-reduce "
       << (r == kWatchPeerError ? "failed on a peer" : "did not finish within the communication timeout (")
@@ -1518,13 +1516,15 @@ int PpoEngine::setComm(void* c, int r, int w) {
     MG_CHECK_ARG(w == 1 || c, "setComm: a communicator is needed for world size > 1");
     if (c && comm_aborted(c)) return fail(MG_ERR_COMM, "setComm: the communicator was aborted");
     if (w > 1 && !nccl().ok) return fail(MG_ERR_COMM, "NCCL (libnccl.so.2) could not be loaded");
-    comm = c;
-    rank = r;
-    world = w;
     if (trainExec) {
         cudaGraphExecDestroy(trainExec);
         trainExec = nullptr;
     }
+    comm_unbind_graph(comm, &trainExec);
+    comm = c;
+    rank = r;
+    world = w;
+    if (w > 1) comm_bind_graph(comm, &trainExec);
     return MG_OK;
 }
 

@@ -720,6 +720,20 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
         if (i < sg.count) {
             const bool v4 = sg.vec4 && i + 3 < sg.count;
             int p = warp;
+            // sixteen loads in flight per thread while they last, then four
+            for (; p + 120 < sg.nparts && v4; p += 128) {
+                float4 v[16];
+#pragma unroll
+                for (int q = 0; q < 16; q++)
+                    v[q] = *reinterpret_cast<const float4*>(sg.src + (int64_t)(p + 8 * q) * st + i);
+#pragma unroll
+                for (int q = 0; q < 16; q++) {
+                    acc.x = __fadd_rn(acc.x, v[q].x);
+                    acc.y = __fadd_rn(acc.y, v[q].y);
+                    acc.z = __fadd_rn(acc.z, v[q].z);
+                    acc.w = __fadd_rn(acc.w, v[q].w);
+                }
+            }
             for (; p + 24 < sg.nparts && v4; p += 32) {
                 float4 v[4];
 #pragma unroll

@@ -2,6 +2,7 @@
 #include "runtime.h"
 
 #include <atomic>
+#include <map>
 #include <mutex>
 #include <set>
 #include <string>
@@ -61,6 +62,39 @@ bool comm_aborted(const void* comm) {
 bool comm_forget_aborted(const void* comm) {
     std::lock_guard<std::mutex> g(g_comm_mu);
     return aborted_comms().erase(comm) != 0;
+}
+
+namespace {
+std::map<const void*, std::set<cudaGraphExec_t*>>& comm_graphs() {
+    static std::map<const void*, std::set<cudaGraphExec_t*>> m;
+    return m;
+}
+}  // namespace
+
+void comm_bind_graph(const void* comm, cudaGraphExec_t* slot) {
+    if (!comm || !slot) return;
+    std::lock_guard<std::mutex> g(g_comm_mu);
+    comm_graphs()[comm].insert(slot);
+}
+
+void comm_unbind_graph(const void* comm, cudaGraphExec_t* slot) {
+    if (!comm || !slot) return;
+    std::lock_guard<std::mutex> g(g_comm_mu);
+    auto it = comm_graphs().find(comm);
+    if (it == comm_graphs().end()) return;
+    it->second.erase(slot);
+    if (it->second.empty()) comm_graphs().erase(it);
+}
+
+void comm_release_graphs(const void* comm) {
+    std::lock_guard<std::mutex> g(g_comm_mu);
+    auto it = comm_graphs().find(comm);
+    if (it == comm_graphs().end()) return;
+    for (cudaGraphExec_t* slot : it->second)
+        if (*slot) {
+            cudaGraphExecDestroy(*slot);
+            *slot = nullptr;
+        }
 }
 
 int num_sms() {

@@ -53,6 +53,15 @@ uint64_t current_context_id();
 void comm_mark_aborted(const void* comm);
 bool comm_aborted(const void* comm);
 bool comm_forget_aborted(const void* comm);  // true if it was aborted
+// Executable graphs that captured a communicator's collectives, by the
+// address of the field that holds each (a model's train graph). NCCL's
+// ncclCommAbort and ncclCommDestroy keep polling until every graph that
+// references the communicator is gone, so comm_release_graphs destroys them
+// first (a graph still in flight is freed when its launch completes, which
+// the abort's flag brings about). Binding the same field again is a no-op.
+void comm_bind_graph(const void* comm, cudaGraphExec_t* slot);
+void comm_unbind_graph(const void* comm, cudaGraphExec_t* slot);
+void comm_release_graphs(const void* comm);
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms();
 

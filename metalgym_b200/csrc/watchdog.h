@@ -4,10 +4,12 @@
 // A rank whose peer died, or never joined the collective, would otherwise
 // wait forever in cudaStreamSynchronize while the NCCL kernel spins. Instead
 // the host polls: the stream's completion, the communicator's asynchronous
-// error, and a deadline. On a peer error or at the deadline it aborts the
-// communicator's operations in flight (ncclCommAbort makes the spinning
-// kernels return) and then waits, again at most a bounded time, for the
-// stream to drain. Plain C++ with the operations passed as function
+// error, and a deadline. On a peer error or at the deadline it releases the
+// CUDA graphs that captured the communicator's collectives (NCCL's abort waits
+// until every such graph is gone; one still in flight is freed when its launch
+// completes), aborts the communicator's operations in flight (ncclCommAbort
+// makes the spinning kernels return) and then waits, again at most a bounded
+// time, for the stream to drain. Plain C++ with the operations passed as function
 // pointers, so the logic is tested on the CPU with fakes.
 #pragma once
 
@@ -17,6 +19,7 @@ struct WatchOps {
     void* ctx;
     int (*done)(void* ctx);       // 1: the stream has finished; 0: not yet; < 0: a CUDA error
     int (*peerError)(void* ctx);  // non-zero: the communicator reported an asynchronous error
+    void (*release)(void* ctx);   // releases the graphs that the abort would wait for
     void (*abort)(void* ctx);     // aborts the communicator and its operations in flight
     double (*now)(void* ctx);     // monotonic seconds
     void (*pause)(void* ctx);     // a short sleep between polls
@@ -52,6 +55,7 @@ inline int watch_wait(const WatchOps& o, double limit, double drain, bool* drain
         }
         o.pause(o.ctx);
     }
+    o.release(o.ctx);
     o.abort(o.ctx);
     const double t1 = o.now(o.ctx);
     for (;;) {

@@ -197,6 +197,9 @@ def run_gpu_rank_leaves(rank, world, local, dist):
     from metalgym_b200.dist import destroy_comm, env_shard, nccl_comm
     from metalgym_b200.session import Gym, PPOModel
 
+    import faulthandler
+
+    faulthandler.dump_traceback_later(90, exit=False)  # where a rank still waits after 90 s
     torch.cuda.set_device(local)
     R, T = 512, 4
     gym = Gym("rollout_cartpole", R, seed=0, first_env_id=env_shard(rank, R), device=local)
@@ -235,6 +238,7 @@ def run_gpu_rank_leaves(rank, world, local, dist):
     gym.close()
     destroy_comm(comm)  # nothing to do for an aborted communicator
     log(rank, "closed")
+    faulthandler.cancel_dump_traceback_later()
     return out
 
 

@@ -1,6 +1,6 @@
 // Drives mg::watch_wait (metalgym_b200/csrc/watchdog.h) with fake streams,
 // communicators and clocks; prints one line per scenario:
-//   <name> <result> <drained> <aborts> <polls>
+//   <name> <result> <drained> <aborts> <polls> <released first>
 #include <cstdio>
 
 #include "watchdog.h"
@@ -12,7 +12,8 @@ struct Fake {
     int peerErrorAtPoll = -1;   // peerError() returns 1 from this poll on
     int cudaErrorAtPoll = -1;   // done() returns -1 at this poll
     bool drainsAfterAbort = true;
-    int polls = 0, aborts = 0;
+    int polls = 0, aborts = 0, releases = 0;
+    bool abortBeforeRelease = false;  // NCCL's abort would wait for good on a live graph
     double clock = 0.0;         // advances 0.001 s per pause
 };
 
@@ -27,15 +28,21 @@ int peer(void* p) {
     Fake* f = static_cast<Fake*>(p);
     return f->peerErrorAtPoll >= 0 && f->polls > f->peerErrorAtPoll ? 1 : 0;
 }
-void abort_(void* p) { static_cast<Fake*>(p)->aborts++; }
+void release(void* p) { static_cast<Fake*>(p)->releases++; }
+void abort_(void* p) {
+    Fake* f = static_cast<Fake*>(p);
+    if (f->releases == 0) f->abortBeforeRelease = true;
+    f->aborts++;
+}
 double now(void* p) { return static_cast<Fake*>(p)->clock; }
 void pause_(void* p) { static_cast<Fake*>(p)->clock += 0.001; }
 
 void run(const char* name, Fake f, double limit, double drain) {
-    mg::WatchOps o{&f, done, peer, abort_, now, pause_};
+    mg::WatchOps o{&f, done, peer, release, abort_, now, pause_};
     bool drained = false;
     const int r = mg::watch_wait(o, limit, drain, &drained);
-    std::printf("%s %d %d %d %d\n", name, r, drained ? 1 : 0, f.aborts, f.polls);
+    std::printf("%s %d %d %d %d %d\n", name, r, drained ? 1 : 0, f.aborts, f.polls,
+                f.aborts > 0 && !f.abortBeforeRelease ? 1 : 0);
 }
 
 }  // namespace

@@ -31,7 +31,8 @@ def launch(mode, nproc=2, limit=600, extra=(), env=None):
            str(ROOT / "tests" / "dp_worker.py"), "--mode", mode, *extra]
     p = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, env={**os.environ, **(env or {})})
     lines = [l for l in p.stdout.splitlines() if l.startswith("{")]
-    assert p.returncode == 0 and lines, f"rc={p.returncode}\n{p.stdout[-3000:]}\n{p.stderr[-3000:]}"
+    progress = "\n".join(l for l in p.stderr.splitlines() if l.startswith(("[rank", "Timeout (")) or "dp_worker.py" in l or "metalgym_b200" in l)
+    assert p.returncode == 0 and lines, f"rc={p.returncode}\n{progress}\n{p.stdout[-3000:]}\n{p.stderr[-3000:]}"
     return json.loads(lines[-1])
 
 

@@ -8,8 +8,8 @@ activations and the head rows; over whole train() calls (the captured graph)
 as well as single trainSlot / trainRows minibatches, for 1 and 2 blocks,
 ragged tile counts and row-mode minibatches. The separate kernels are pinned
 to the oracle and to torch by their own tests (test_engine.py,
-test_block_cluster.py, test_head_tail.py); test_engine.py's oracle tests run
-the merged kernel too, since it is the default."""
+test_block_cluster.py, test_head_tail.py); test_parity_full_shapes.py checks
+a 4096-row minibatch of the merged kernel against the oracle as well."""
 import numpy as np
 import pytest
 

@@ -1,8 +1,9 @@
 """The train() watchdog's wait loop (metalgym_b200/csrc/watchdog.h) on the
 CPU, driven by fake streams, communicators and clocks: a finished stream
 returns at once and aborts nothing; a peer's asynchronous error or the
-deadline aborts the communicator exactly once and then waits, bounded, for
-the stream to drain; a CUDA error returns without an abort. No GPU, no NCCL:
+deadline releases the graphs that captured the collectives (NCCL's abort
+waits for them) and then aborts the communicator exactly once and waits,
+bounded, for the stream to drain; a CUDA error returns without an abort. No GPU, no NCCL:
 the failure is made on the host, as the real test on two GPUs does by
 keeping one rank out of the all-reduce."""
 import subprocess
@@ -22,8 +23,9 @@ def test_watch_wait_scenarios(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
     res = {}
     for line in out.splitlines():
-        name, result, drained, aborts, polls = line.split()
+        name, result, drained, aborts, polls, released_first = line.split()
         res[name] = (int(result), int(drained), int(aborts), int(polls))
+        assert int(released_first) == (int(aborts) > 0), name
     assert res["finishes"] == (DONE, 1, 0, 51)
     result, drained, aborts, _ = res["peer_error"]
     assert (result, drained, aborts) == (PEER_ERROR, 1, 1)
