@@ -52,9 +52,13 @@ struct BlockClusterForwardInput {
     void* xNorm;
     float* stdev;
 };
+// prefetch: the preceding kernel on st is one of these block kernels or the
+// head kernel (head_tail), which signal their dependents only after their
+// own dependency wait; the weights (and the backward's other operands but the
+// A tile) are then loaded before this kernel's wait (BcParams::prefetch).
 int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown, void* h, void* v,
                           const LnOutputs& next, int M, cudaStream_t st,
-                          const BlockClusterForwardInput* in = nullptr);
+                          const BlockClusterForwardInput* in = nullptr, bool prefetch = false);
 // It also writes the weight-gradient partial sums of each 128-row tile t:
 // upPart[t] = lnOut_t^T dV_t ([128][512]), downPart[t] = V_t^T dS_t ([512][128]).
 // With `in` (the first block), the rows written are the input layer's dZ,
@@ -70,7 +74,7 @@ struct BlockClusterInput {
 int block_cluster_backward(const void* dS, const void* wDown, const void* v, const void* wUp, void* dV,
                            const void* lnOut, float* upPart, float* downPart, const void* xNorm, const void* gamma,
                            const float* stdev, const void* resid, void* residOut, float* partial, int M,
-                           cudaStream_t st, const BlockClusterInput* in = nullptr);
+                           cudaStream_t st, const BlockClusterInput* in = nullptr, bool prefetch = false);
 
 // The per-tile part of one training minibatch in one kernel
 // (minibatch_tiles.cu): the passes of block_cluster_forward (block 0 with the

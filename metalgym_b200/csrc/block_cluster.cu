@@ -16,7 +16,6 @@ template <bool BWD, int RPC, bool INPUT = false>
 __global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_constant__ BcMaps tm, const BcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    mg_pdl_trigger();
     if (threadIdx.x == 0) bc_prefetch_maps(tm, BWD);
     // 128-column accumulators: 2 (forward), 4 (backward)
     TilePass t = tp_setup(smem + (BWD ? kBcBwdBar : kBcFwdBar), BWD ? 512 : 256, false);
@@ -26,8 +25,15 @@ __global__ void __launch_bounds__(kRowsThreads, 1) k_block_cluster(const __grid_
     if (INPUT && p.in.earlyObs)
         bc_input_stage_obs(reinterpret_cast<float*>(smem + kBcFwdA2), cluster_ctarank(),
                            (int)(blockIdx.x / kRowsCluster) * kRowsBM, p.M, p.in);
+    // the weights (and the backward's mask and LayerNorm output), where they
+    // come from kernels before the preceding one (BcParams::prefetch)
+    const bool early = !INPUT && p.prefetch;
+    if (early && threadIdx.x == 0) bc_issue_static<BWD, INPUT>(smem, tm, t);
     mg_pdl_wait();  // activations and weights come from earlier kernels
-    bc_pass<BWD, RPC, INPUT>(smem, tm, p, t);
+    // dependents start only now, after this kernel's predecessor completed:
+    // their pre-wait loads may read what came before this kernel
+    mg_pdl_trigger();
+    bc_pass<BWD, RPC, INPUT>(smem, tm, p, t, early);
 }
 
 template <bool BWD, int RPC, bool INPUT = false>
@@ -97,10 +103,11 @@ int block_cluster_forward_args(const void* lnOut, const void* wUp, const void* w
 }
 
 int block_cluster_forward(const void* lnOut, const void* wUp, const void* wDown, void* h, void* v, const LnOutputs& next,
-                          int M, cudaStream_t st, const BlockClusterForwardInput* in) {
+                          int M, cudaStream_t st, const BlockClusterForwardInput* in, bool prefetch) {
     BcMaps tm;
     BcParams p;
     MG_TRY(block_cluster_forward_args(lnOut, wUp, wDown, h, v, next, M, in, tm, p));
+    p.prefetch = prefetch && !in;
     return in ? launch_bc<false, 32, true>(tm, p, st) : launch_bc<false, 32>(tm, p, st);
 }
 
@@ -151,11 +158,12 @@ int block_cluster_backward_args(const void* dS, const void* wDown, const void* v
 int block_cluster_backward(const void* dS, const void* wDown, const void* v, const void* wUp, void* dV,
                            const void* lnOut, float* upPart, float* downPart, const void* xNorm, const void* gamma,
                            const float* stdev, const void* resid, void* residOut, float* partial, int M,
-                           cudaStream_t st, const BlockClusterInput* in) {
+                           cudaStream_t st, const BlockClusterInput* in, bool prefetch) {
     BcMaps tm;
     BcParams p;
     MG_TRY(block_cluster_backward_args(dS, wDown, v, wUp, dV, lnOut, upPart, downPart, xNorm, gamma, stdev, resid,
                                        residOut, partial, M, in, tm, p));
+    p.prefetch = prefetch;
     switch (layernorm_rows_per_part(M)) {
         case 8: return launch_bc<true, 8>(tm, p, st);
         case 16: return launch_bc<true, 16>(tm, p, st);

@@ -87,6 +87,13 @@ struct BcParams {
     RowsEpi e;
     int* status;
     uint64_t* trace;  // phase trace (tile_pass.cuh); null: off
+    // standalone kernel: issue the loads of everything but the A operand
+    // before the programmatic-dependency wait. Only where the preceding
+    // kernel is a tile kernel that signals its dependents after its own wait
+    // (block_cluster.cu, head_tail.cu): this kernel's pre-wait code then runs
+    // after every kernel before that one completed, and the weights, the
+    // ReLU mask and the LayerNorm output all come from those.
+    bool prefetch;
 };
 
 // Maps (all SW128, 64-wide boxes):
@@ -257,6 +264,41 @@ __device__ __forceinline__ void bc_prefetch_maps(const BcMaps& tm, bool bwd) {
     }
 }
 
+// Thread 0: the pass's loads other than the A operand (the weight slices;
+// backward: the ReLU mask and the LayerNorm output), with the byte counts of
+// both full barriers, the A operand's included (its loads follow, before or
+// after the programmatic-dependency wait).
+template <bool BWD, bool INPUT>
+__device__ __forceinline__ void bc_issue_static(uint8_t* smem, const BcMaps& tm, TilePass& t) {
+    const int m0 = (int)(blockIdx.x / kRowsCluster) * kRowsBM;
+    const int h0 = (int)cluster_ctarank() * kRowsBN;
+    t.issuing(kTbFull1);
+    mbar_arrive_expect_tx(t.bar(kTbFull1), (INPUT ? 1 : 2) * kBcTile + (BWD ? kBcTile : 0));
+    if (!BWD) {
+        // W_up[k][h0 + n]: K rows 64 kb.., N boxes h0 + 64 j
+        for (int kb = 0; kb < 2; kb++)
+            for (int j = 0; j < 2; j++)
+                tma_load_2d(smem + kBcB1 + kb * 16384 + j * 8192, &tm.b1, h0 + 64 * j, 64 * kb, t.bar(kTbFull1));
+    } else {
+        // W_down rows h0 .. h0 + 127 as [N][K = 128]; the mask V[m0.., h0..]
+        for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcB1 + kb * 16384, &tm.b1, 64 * kb, h0, t.bar(kTbFull1));
+        for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcBwdM + kb * 16384, &tm.v, h0 + 64 * kb, m0, t.bar(kTbFull1));
+    }
+    t.issuing(kTbFull2);
+    mbar_arrive_expect_tx(t.bar(kTbFull2), kBcTile * (BWD ? 2 : 1));
+    if (BWD)  // the block's LayerNorm output, for dW_up
+        for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcBwdLn + kb * 16384, &tm.ln, 64 * kb, m0, t.bar(kTbFull2));
+    if (!BWD) {
+        // W_down[h0 + k][n]: K rows h0 + 64 kb.., N boxes 64 j
+        for (int kb = 0; kb < 2; kb++)
+            for (int j = 0; j < 2; j++)
+                tma_load_2d(smem + kBcB2 + kb * 16384 + j * 8192, &tm.b2, 64 * j, h0 + 64 * kb, t.bar(kTbFull2));
+    } else {
+        // W_up as [N = 128][K = 512], K columns h0 + 64 kb ..
+        for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcB2 + kb * 16384, &tm.b2, h0 + 64 * kb, 0, t.bar(kTbFull2));
+    }
+}
+
 // One block pass over the tile m0 = 128 (blockIdx.x / 4) of this CTA's
 // cluster. On entry: the barriers and TMEM of `t` are set up, every CTA of
 // the cluster is running (or, with INPUT, has arrived on the cluster barrier
@@ -264,8 +306,10 @@ __device__ __forceinline__ void bc_prefetch_maps(const BcMaps& tm, bool bwd) {
 // frees the pass's TMEM (BWD ? 512 : 256 columns) before the epilogue, as
 // the kernel's last use of it. Merged: leaves TMEM allocated and ends at a
 // pass boundary.
+// staticIssued: bc_issue_static already ran (before the kernel's wait).
 template <bool BWD, int RPC, bool INPUT>
-__device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const BcParams& p, TilePass& t) {
+__device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const BcParams& p, TilePass& t,
+                                        bool staticIssued = false) {
     constexpr int A2 = BWD ? kBcBwdA2 : kBcFwdA2;
     constexpr uint32_t kTmemCols = BWD ? 512 : 256;
     const int warp = threadIdx.x >> 5;
@@ -278,35 +322,9 @@ __device__ __forceinline__ void bc_pass(uint8_t* smem, const BcMaps& tm, const B
     tp_mark(t);  // pass start
 
     if (threadIdx.x == 0 && t.ok()) {
-        t.issuing(kTbFull1);
-        mbar_arrive_expect_tx(t.bar(kTbFull1), (INPUT ? 1 : 2) * kBcTile + (BWD ? kBcTile : 0));
+        if (!staticIssued) bc_issue_static<BWD, INPUT>(smem, tm, t);
         if (!INPUT)
             for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcA1 + kb * 16384, &tm.a, 64 * kb, m0, t.bar(kTbFull1));
-        if (!BWD) {
-            // W_up[k][h0 + n]: K rows 64 kb.., N boxes h0 + 64 j
-            for (int kb = 0; kb < 2; kb++)
-                for (int j = 0; j < 2; j++)
-                    tma_load_2d(smem + kBcB1 + kb * 16384 + j * 8192, &tm.b1, h0 + 64 * j, 64 * kb, t.bar(kTbFull1));
-        } else {
-            // W_down rows h0 .. h0 + 127 as [N][K = 128]; the mask V[m0.., h0..]
-            for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcB1 + kb * 16384, &tm.b1, 64 * kb, h0, t.bar(kTbFull1));
-            for (int kb = 0; kb < 2; kb++)
-                tma_load_2d(smem + kBcBwdM + kb * 16384, &tm.v, h0 + 64 * kb, m0, t.bar(kTbFull1));
-        }
-        t.issuing(kTbFull2);
-        mbar_arrive_expect_tx(t.bar(kTbFull2), kBcTile * (BWD ? 2 : 1));
-        if (BWD)  // the block's LayerNorm output, for dW_up
-            for (int kb = 0; kb < 2; kb++)
-                tma_load_2d(smem + kBcBwdLn + kb * 16384, &tm.ln, 64 * kb, m0, t.bar(kTbFull2));
-        if (!BWD) {
-            // W_down[h0 + k][n]: K rows h0 + 64 kb.., N boxes 64 j
-            for (int kb = 0; kb < 2; kb++)
-                for (int j = 0; j < 2; j++)
-                    tma_load_2d(smem + kBcB2 + kb * 16384 + j * 8192, &tm.b2, 64 * j, h0 + 64 * kb, t.bar(kTbFull2));
-        } else {
-            // W_up as [N = 128][K = 512], K columns h0 + 64 kb ..
-            for (int kb = 0; kb < 2; kb++) tma_load_2d(smem + kBcB2 + kb * 16384, &tm.b2, h0 + 64 * kb, 0, t.bar(kTbFull2));
-        }
     }
     if (INPUT) {
         // the A tile is computed here: the input layer and the first LayerNorm

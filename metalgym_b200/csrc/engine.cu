@@ -692,8 +692,9 @@ int PpoEngine::blocksForward(const float* obs, const RowMap& rm, ActSet& a, int 
                 MG_TRY(mt->forward(a.lnOut[n], w(pUp[n]), w(pDown[n]), a.h, a.v[n], next, rows,
                                    n == 0 && inputInBlock ? &in : nullptr));
             else
+                // blocks after the first follow the previous block's kernel
                 MG_TRY(block_cluster_forward(a.lnOut[n], w(pUp[n]), w(pDown[n]), a.h, a.v[n], next, rows, st,
-                                             n == 0 && inputInBlock ? &in : nullptr));
+                                             n == 0 && inputInBlock ? &in : nullptr, n > 0));
             continue;
         }
         GemmCall up;
@@ -856,9 +857,12 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
                                     downPart[n], a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1], dS[n], lnPart[n], rows,
                                     n == 0 && inputFused ? &in : nullptr));
             else
+                // the kernel before is the next block's backward kernel, or the
+                // head kernel for the last block
                 MG_TRY(block_cluster_backward(dS[n + 1], w(pDown[n]), a.v[n], w(pUp[n]), dVs[n], a.lnOut[n],
                                               upPart[n], downPart[n], a.lnXn[n], w(pLnG[n]), a.lnSd[n], dS[n + 1],
-                                              dS[n], lnPart[n], rows, st, n == 0 && inputFused ? &in : nullptr));
+                                              dS[n], lnPart[n], rows, st, n == 0 && inputFused ? &in : nullptr,
+                                              n < L - 1 || headTail));
             continue;
         } else {
             GemmCall g1;  // dV = bf16(dS Dp^T) * (V > 0) (model/mlp.metal:88-127)

@@ -17,13 +17,15 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                 const HeadTailParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    mg_pdl_trigger();
     if (threadIdx.x == 0) {
         prefetch_tensormap(&tmF);
         prefetch_tensormap(&tmW);
     }
     TilePass t = tp_setup(smem + kHtBar, 256, false);
     mg_pdl_wait();
+    // dependents start only now, after this kernel's predecessor completed
+    // (the block backward kernels load their weights before their own wait)
+    mg_pdl_trigger();
     ht_pass<RPC, AD>(smem, tmF, tmW, p, t);
 }
 
