@@ -164,11 +164,12 @@ __device__ __forceinline__ void bc_input_prologue(uint8_t* smem, float* stage, u
     const int c0 = lane * 4;
     float* sW = stage;                    // [inDim][128]
     float* sObs = stage + in.inDim * E;   // [32][inDim]
+    // the bias and LayerNorm parameters in flight with the weights' loads
+    const float4 bias = bf4_load(in.b + c0);
+    const float4 gm = bf4_load(in.ln.gamma + c0), bt = bf4_load(in.ln.beta + c0);
     for (int i = threadIdx.x; i < in.inDim * E; i += blockDim.x) sW[i] = __bfloat162float(in.w[i]);
     if (!in.earlyObs) bc_input_stage_obs(stage, q, m0, M, in);  // else staged before the PDL wait
     __syncthreads();
-    const float4 bias = bf4_load(in.b + c0);
-    const float4 gm = bf4_load(in.ln.gamma + c0), bt = bf4_load(in.ln.beta + c0);
     const float g[4] = {gm.x, gm.y, gm.z, gm.w}, bb[4] = {bt.x, bt.y, bt.z, bt.w};
     float v[2][4], ms[4];
 #pragma unroll

@@ -57,11 +57,22 @@ __global__ void __launch_bounds__(256) k_input_forward(const float* __restrict__
 #pragma unroll
     for (int j = 0; j < NP; j++) b[j] = make_float2(bf(bias[2 * lane + 64 * j]), bf(bias[2 * lane + 64 * j + 1]));
     for (int r0 = (blockIdx.x * nwarps + warp) * RPW; r0 < rows; r0 += gridDim.x * nwarps * RPW) {
+        // each row's rollout index once (lane q for row r0 + q), then its observations
+        uint64_t gq = 0;
+        if (lane < RPW && r0 + lane < rows)
+            gq = rm.mb ? mg_minibatch_row(*rm.mb, r0 + lane, rm.envRows, rm.total) : (uint64_t)(r0 + lane);
+        uint64_t gr[RPW];
+#pragma unroll
+        for (int q = 0; q < RPW; q++) gr[q] = __shfl_sync(0xffffffffu, gq, q);
         for (int i = lane; i < RPW * inDim; i += 32) {
-            const int r = r0 + i / inDim;
+            const int qi = i / inDim;
+            const int r = r0 + qi;
             float v = 0.0f;
             if (r < rows) {
-                const uint64_t g = rm.mb ? mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : (uint64_t)r;
+                uint64_t g = gr[0];
+#pragma unroll
+                for (int q = 1; q < RPW; q++)
+                    if (qi == q) g = gr[q];
                 v = obs[g * inDim + i % inDim];
             }
             s_obs[i] = v;
@@ -150,15 +161,16 @@ __global__ void __launch_bounds__(256) k_input_backward(const float* __restrict_
                                                         int rowsPerCta, RowMap rm) {
     mg_pdl_trigger();
     mg_pdl_wait();
-    extern __shared__ float s_obs[];  // rowsPerCta x inDim fp32, then rowsPerCta x outDim bf16
+    extern __shared__ float s_obs[];  // rowsPerCta x inDim fp32, rowsPerCta x outDim bf16, rowsPerCta x u64
     const int r0 = blockIdx.x * rowsPerCta;
     const int nr = min(rowsPerCta, rows - r0);
     __nv_bfloat16* s_dz = reinterpret_cast<__nv_bfloat16*>(s_obs + rowsPerCta * inDim);
-    for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) {
-        const int r = r0 + i / inDim;
-        const uint64_t g = rm.mb ? mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : (uint64_t)r;
-        s_obs[i] = obs[g * inDim + i % inDim];
-    }
+    // each row's rollout index once, then its observations
+    uint64_t* s_g = reinterpret_cast<uint64_t*>(s_dz + rowsPerCta * outDim);
+    for (int i = threadIdx.x; i < nr; i += blockDim.x)
+        s_g[i] = rm.mb ? mg_minibatch_row(*rm.mb, r0 + i, rm.envRows, rm.total) : (uint64_t)(r0 + i);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) s_obs[i] = obs[s_g[i / inDim] * inDim + i % inDim];
     {
         // dZ rows r0 .. r0 + nr are contiguous: 16-byte copies
         const uint4* src = reinterpret_cast<const uint4*>(dZ + (size_t)r0 * outDim);
@@ -216,15 +228,16 @@ __global__ void __launch_bounds__(256) k_input_backward_regs(const float* __rest
                                                              int outDim, int rowsPerCta, RowMap rm) {
     mg_pdl_trigger();
     mg_pdl_wait();
-    extern __shared__ float s_obs[];  // rowsPerCta x inDim fp32, then rowsPerCta x outDim bf16
+    extern __shared__ float s_obs[];  // rowsPerCta x inDim fp32, rowsPerCta x outDim bf16, rowsPerCta x u64
     const int r0 = blockIdx.x * rowsPerCta;
     const int nr = min(rowsPerCta, rows - r0);
     __nv_bfloat16* s_dz = reinterpret_cast<__nv_bfloat16*>(s_obs + rowsPerCta * inDim);
-    for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) {
-        const int r = r0 + i / inDim;
-        const uint64_t g = rm.mb ? mg_minibatch_row(*rm.mb, r, rm.envRows, rm.total) : (uint64_t)r;
-        s_obs[i] = obs[g * inDim + i % inDim];
-    }
+    // each row's rollout index once, then its observations
+    uint64_t* s_g = reinterpret_cast<uint64_t*>(s_dz + rowsPerCta * outDim);
+    for (int i = threadIdx.x; i < nr; i += blockDim.x)
+        s_g[i] = rm.mb ? mg_minibatch_row(*rm.mb, r0 + i, rm.envRows, rm.total) : (uint64_t)(r0 + i);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr * inDim; i += blockDim.x) s_obs[i] = obs[s_g[i / inDim] * inDim + i % inDim];
     {
         const uint4* src = reinterpret_cast<const uint4*>(dZ + (size_t)r0 * outDim);
         uint4* dst = reinterpret_cast<uint4*>(s_dz);
@@ -1045,7 +1058,7 @@ int input_forward(const float* obs, const void* w, const void* b, void* out, int
 static int input_rows_per_cta(int rows, int inDim, int outDim) {
     const int64_t perPart = (int64_t)(inDim + 1) * outDim * 4;
     const int64_t maxParts = std::max<int64_t>(1, std::min<int64_t>(kMaxRowParts, kInputPartialBudget / perPart));
-    const int perRowSmem = inDim * 4 + outDim * 2;
+    const int perRowSmem = inDim * 4 + outDim * 2 + 8;
     const int maxRpc = std::max(8, (int)(kInputSmemBudget / perRowSmem) / 8 * 8);
     int rpc = std::max<int64_t>(16, (rows + maxParts - 1) / maxParts);
     rpc = (rpc + 7) / 8 * 8;
@@ -1062,7 +1075,9 @@ int input_backward(const float* obs, const void* dZ, float* partial, int rows, i
                  "input_backward: bad shape");
     MG_CHECK_ARG((reinterpret_cast<uintptr_t>(dZ) & 15) == 0, "input_backward: dZ must be 16-byte aligned");
     const int rpc = input_rows_per_cta(rows, inDim, outDim);
-    const size_t sm = (size_t)rpc * inDim * 4 + (size_t)rpc * outDim * 2;
+    // observations, dZ rows, the rows' rollout indices (8-byte aligned: rows per
+    // CTA a multiple of 8, outDim % 8 == 0)
+    const size_t sm = (size_t)rpc * inDim * 4 + (size_t)rpc * outDim * 2 + (size_t)rpc * 8;
     MG_CHECK_ARG(sm <= 200 * 1024, "input_backward: rows per CTA x widths too large for shared memory");
     const auto* DZ = static_cast<const __nv_bfloat16*>(dZ);
     const int blocks = grid_rows(rows, rpc), threads = std::min(outDim, 256);

@@ -60,6 +60,10 @@ __device__ inline bool policy_loss_compute(const PolicyLossRows& L, int r, const
     const float* advStats = L.advStats;
     if (L.mb && L.mb->slot >= 0 && advStats) advStats += 2 * L.mb->slot;  // per-slot statistics
     const int actDim = AD > 0 ? AD : L.actDim;
+    // the row's inputs first, so that their loads overlap the exponentials
+    const int a = L.action[g];
+    const float advG = L.adv[g], oldLogProb = L.oldLogProb[g], retG = L.ret[g];
+    const float adv0 = advStats ? advStats[0] : 0.0f, adv1 = advStats ? advStats[1] : 0.0f;
     const float scale = __fdiv_rn(1.0f, (float)L.rows);
     // exp(logp_j) is needed twice (entropy, gradient): keep up to kCache of them
     constexpr int kCache = 8;
@@ -69,6 +73,10 @@ __device__ inline bool policy_loss_compute(const PolicyLossRows& L, int r, const
     float sum = 0.0f;
     for (int j = 0; j < actDim; j++) sum = __fadd_rn(sum, mg_expf(__fsub_rn(loss_bf(h[j]), rowMax)));
     const float lse = __fadd_rn(rowMax, mg_logf(sum));
+    // the ratio's exponential beside the probabilities' (the action is
+    // checked below; index 0 stands in for an invalid one until then)
+    const float logpA = __fsub_rn(loss_bf(h[(a >= 0 && a < actDim) ? a : 0]), lse);
+    const float ratio = mg_expf(__fsub_rn(logpA, oldLogProb));
     float entropy = 0.0f;
 #pragma unroll
     for (int j = 0; j < kCache; j++) {
@@ -82,15 +90,12 @@ __device__ inline bool policy_loss_compute(const PolicyLossRows& L, int r, const
         const float logp = __fsub_rn(loss_bf(h[j]), lse);
         entropy = __fsub_rn(entropy, __fmul_rn(mg_expf(logp), logp));
     }
-    const int a = L.action[g];
     if (a < 0 || a >= actDim) {  // never index the head with an invalid action
         record_error(status, kDevBadAction);
         return false;
     }
     // model/gae.metal:76: (a - mean) * inv, inv = 1 / (sigma + 1e-8)
-    const float A = advStats ? __fmul_rn(__fsub_rn(L.adv[g], advStats[0]), advStats[1]) : L.adv[g];
-    const float logpA = __fsub_rn(loss_bf(h[a]), lse);
-    const float ratio = mg_expf(__fsub_rn(logpA, L.oldLogProb[g]));
+    const float A = advStats ? __fmul_rn(__fsub_rn(advG, adv0), adv1) : advG;
     const float surr1 = __fmul_rn(ratio, A);
     const float surr2 = __fmul_rn(fminf(fmaxf(ratio, __fsub_rn(1.0f, L.clip)), __fadd_rn(1.0f, L.clip)), A);
     const float policyLoss = -fminf(surr1, surr2);
@@ -112,12 +117,12 @@ __device__ inline bool policy_loss_compute(const PolicyLossRows& L, int r, const
                                    __fmul_rn(__fmul_rn(L.entropyCoef, prob), __fadd_rn(logp, entropy)));
         pz[j] = loss_tobf(__fmul_rn(gr, scale));
     }
-    const float vErr = __fsub_rn(loss_bf(h[actDim]), L.ret[g]);
+    const float vErr = __fsub_rn(loss_bf(h[actDim]), retG);
     pz[actDim] = loss_tobf(__fmul_rn(__fmul_rn(L.valueCoef, vErr), scale));
     st[0] = policyLoss;
     st[1] = __fmul_rn(__fmul_rn(__fmul_rn(0.5f, L.valueCoef), vErr), vErr);
     st[2] = entropy;
-    st[3] = __fsub_rn(L.oldLogProb[g], logpA);
+    st[3] = __fsub_rn(oldLogProb, logpA);
     st[4] = (fabsf(__fsub_rn(ratio, 1.0f)) > L.clip) ? 1.0f : 0.0f;
     return true;
 }
