@@ -950,6 +950,16 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
 }
 
 int PpoEngine::captureCollect() {
+    std::lock_guard<std::mutex> lock(capture_mutex());
+    for (int attempt = 0;; attempt++) {
+        bool invalidated = false;
+        const int rc = captureCollectOnce(&invalidated);
+        if (rc == MG_OK || !invalidated || attempt == 2) return rc;
+        cudaGetLastError();  // another thread's module load ended the capture: capture again
+    }
+}
+
+int PpoEngine::captureCollectOnce(bool* invalidated) {
     cudaStream_t st = gym->stream;
     if (collectExec) {
         cudaGraphExecDestroy(collectExec);
@@ -1013,6 +1023,7 @@ int PpoEngine::captureCollect() {
     if (!rc) rc = advantage_stats(advSlots, advStats, R, T, st);
     cudaGraph_t graph = nullptr;
     cudaError_t e = cudaStreamEndCapture(st, &graph);
+    *invalidated = e == cudaErrorStreamCaptureInvalidated;
     if (rc) {
         if (graph) cudaGraphDestroy(graph);
         return rc;
@@ -1028,12 +1039,23 @@ int PpoEngine::captureCollect() {
 }
 
 int PpoEngine::captureTrain(int minibatches, bool rowMode) {
+    std::lock_guard<std::mutex> lock(capture_mutex());
+    for (int attempt = 0;; attempt++) {
+        bool invalidated = false;
+        const int rc = captureTrainOnce(minibatches, rowMode, &invalidated);
+        if (rc == MG_OK || !invalidated || attempt == 2) return rc;
+        cudaGetLastError();  // another thread's module load ended the capture: capture again
+    }
+}
+
+int PpoEngine::captureTrainOnce(int minibatches, bool rowMode, bool* invalidated) {
     cudaStream_t st = gym->stream;
     MG_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
     int rc = MG_OK;
     for (int j = 0; j < minibatches && !rc; j++) rc = minibatch(j, rowMode, st);
     cudaGraph_t graph = nullptr;
     cudaError_t e = cudaStreamEndCapture(st, &graph);
+    *invalidated = e == cudaErrorStreamCaptureInvalidated;
     if (rc) {
         if (graph) cudaGraphDestroy(graph);
         return rc;

@@ -292,6 +292,9 @@ class PpoEngine {
     int minibatch(int j, bool rowMode, cudaStream_t st);  // reads sched[j], schedBetaPow[2j..]
     int captureCollect();
     int captureTrain(int minibatches, bool rowMode);
+    // one capture attempt; *invalidated: the capture ended invalidated (capture_mutex)
+    int captureCollectOnce(bool* invalidated);
+    int captureTrainOnce(int minibatches, bool rowMode, bool* invalidated);
     int ensureSchedule(int device, int host);
     int allocTrain(int rows);
     void freeTrain();

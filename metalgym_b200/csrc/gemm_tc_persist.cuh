@@ -11,9 +11,11 @@
 //   warps 2-5  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, i.e.
 //              output rows 32 (w % 4) + lane of the tile, applies the
 //              epilogue and arrives on tempty[a]. bf16 outputs go through a
-//              per-warp shared-memory slab (32 rows x BN, 128-byte swizzled)
-//              that one lane stores with TMA; the aux operand of the residual
-//              and mask epilogues is loaded into the same slab by TMA first.
+//              per-warp shared-memory slab (32 rows x the warp's columns,
+//              128-byte swizzled; half of them per round for the epilogues
+//              without aux at 256-wide tiles) that one lane stores with TMA;
+//              the aux operand of the residual and mask epilogues is loaded
+//              into the same slab by TMA first.
 //              fp32 split-K partials are stored directly.
 //
 // Units are numbered with the N tile fastest, so the CTAs working at the same
@@ -37,8 +39,14 @@ struct PersistShape {
     static constexpr int EW = (STAGED && EPI != kEpiResidLN) ? 8 : 4;
     static constexpr int EPI_COLS = BN * 4 / EW;             // columns per epilogue warp
     static constexpr int THREADS = 64 + 32 * EW;
-    static constexpr int SLAB = 32 * EPI_COLS * 2;           // per epilogue warp: 32 rows x EPI_COLS bf16
-    static constexpr int STAGES = STAGED ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6);
+    // the elementwise epilogues without an aux operand at 256-wide tiles
+    // store each warp's columns in two rounds through a half-size slab, which
+    // leaves room for a fourth TMA stage (more operand bytes in flight)
+    static constexpr bool HALF_SLAB = STAGED && EW == 8 && BN == 256 && (EPI == kEpiBf16 || EPI == kEpiBf16Relu);
+    static constexpr int SLAB_COLS = HALF_SLAB ? EPI_COLS / 2 : EPI_COLS;  // columns the slab holds
+    static constexpr int ROUNDS = EPI_COLS / SLAB_COLS;
+    static constexpr int SLAB = 32 * SLAB_COLS * 2;          // per epilogue warp: 32 rows x SLAB_COLS bf16
+    static constexpr int STAGES = STAGED ? (BN == 256 ? (HALF_SLAB ? 4 : 3) : 4) : (BN == 256 ? 4 : 6);
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -268,8 +276,27 @@ __global__ void __launch_bounds__(PersistShape<BN, EPI>::THREADS, 1)
             tc_fence_after();
             const int row = row0 + lane;
             const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN + hc);
+            // TMA store of slab round r (columns hc + r SLAB_COLS ..) of the tile
+            auto storeRound = [&](int r) {
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int j = 0; j < S::SLAB_COLS / 64; j++)
+                        if (n0 + hc + r * S::SLAB_COLS + 64 * j < p.N && row0 < p.M)
+                            tma_store_2d(&em.out, n0 + hc + r * S::SLAB_COLS + 64 * j, row0, slab + j * 4096);
+                    bulk_commit();
+                }
+            };
+            constexpr int kChunksPerRound = S::SLAB_COLS / 32;
 #pragma unroll 1
             for (int c = 0; c < S::EPI_COLS / 32; c++) {
+                if (S::STAGED && S::ROUNDS > 1 && c > 0 && c % kChunksPerRound == 0) {
+                    // the finished round out, and the slab free for the next one
+                    storeRound(c / kChunksPerRound - 1);
+                    if (lane == 0) bulk_wait_read<0>();
+                    __syncwarp();
+                }
                 const int col = n0 + hc + c * 32;
                 float v[32];
                 tmem_ld32(acc + (uint32_t)(c * 32), v);
@@ -285,7 +312,7 @@ __global__ void __launch_bounds__(PersistShape<BN, EPI>::THREADS, 1)
                 }
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
-                    uint4* cell = reinterpret_cast<uint4*>(slab + slab_offset(lane, c * 4 + k));
+                    uint4* cell = reinterpret_cast<uint4*>(slab + slab_offset(lane, (c % kChunksPerRound) * 4 + k));
                     float x[8];
 #pragma unroll
                     for (int i = 0; i < 8; i++) x[i] = v[8 * k + i];
@@ -318,17 +345,7 @@ __global__ void __launch_bounds__(PersistShape<BN, EPI>::THREADS, 1)
                     *cell = make_uint4(o[0], o[1], o[2], o[3]);
                 }
             }
-            if (S::STAGED) {
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-#pragma unroll
-                    for (int j = 0; j < S::EPI_COLS / 64; j++)
-                        if (n0 + hc + 64 * j < p.N && row0 < p.M)
-                            tma_store_2d(&em.out, n0 + hc + 64 * j, row0, slab + j * 4096);
-                    bulk_commit();
-                }
-            }
+            if (S::STAGED) storeRound(S::ROUNDS - 1);
             if constexpr (EPI == kEpiResidLN) {
                 // the LayerNorm of the warp's 32 rows now in the slab: one row
                 // across the lanes at a time (lane l: columns l VPT ..), eight

@@ -97,6 +97,11 @@ void comm_release_graphs(const void* comm) {
         }
 }
 
+std::mutex& capture_mutex() {
+    static std::mutex m;
+    return m;
+}
+
 int num_sms() {
     static std::atomic<int> cache[64] = {};
     int dev = 0;

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <mutex>
 #include <string>
 
 #include "../../include/metalgym_b200.h"
@@ -62,6 +63,12 @@ bool comm_forget_aborted(const void* comm);  // true if it was aborted
 void comm_bind_graph(const void* comm, cudaGraphExec_t* slot);
 void comm_unbind_graph(const void* comm, cudaGraphExec_t* slot);
 void comm_release_graphs(const void* comm);
+// Serialises the engines' CUDA-graph captures across host threads. A capture
+// open in one thread can still be invalidated by what another thread does
+// meanwhile (the driver loading a kernel module on a kernel's first use under
+// lazy loading, for one): the engine then captures again (at most three
+// attempts), with the modules the first attempt loaded already in place.
+std::mutex& capture_mutex();
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms();
 
