@@ -92,13 +92,21 @@ __global__ void __launch_bounds__(256) k_p2p_allreduce(const __grid_constant__ P
     float4* gd = reinterpret_cast<float4*>(grad);
     float sq = 0.0f;
     for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < count / 4; g += (int64_t)gridDim.x * blockDim.x) {
-        float4 acc = reinterpret_cast<const float4*>(t.base[0] + xOff)[g];
-        for (int p = 1; p < t.world; p++) {
-            const float4 v = reinterpret_cast<const float4*>(t.base[p] + xOff)[g];
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+        // every rank's values in flight at once (one NVLink round trip), then
+        // the sum in rank order
+        float4 v[kP2PMaxRanks];
+#pragma unroll
+        for (int p = 0; p < kP2PMaxRanks; p++)
+            if (p < t.world) v[p] = __ldcg(reinterpret_cast<const float4*>(t.base[p] + xOff) + g);
+        float4 acc = v[0];
+#pragma unroll
+        for (int p = 1; p < kP2PMaxRanks; p++) {
+            if (p < t.world) {
+                acc.x = __fadd_rn(acc.x, v[p].x);
+                acc.y = __fadd_rn(acc.y, v[p].y);
+                acc.z = __fadd_rn(acc.z, v[p].z);
+                acc.w = __fadd_rn(acc.w, v[p].w);
+            }
         }
         acc = make_float4(__fmul_rn(acc.x, scale), __fmul_rn(acc.y, scale), __fmul_rn(acc.z, scale),
                           __fmul_rn(acc.w, scale));

@@ -21,8 +21,8 @@ struct P2PTable {
 };
 
 // CTAs of the exchange kernel: few enough to be resident together (CTA 0
-// announces for all of them), enough to keep NVLink busy.
-inline int p2p_blocks() { return 64; }
+// announces for all of them), enough to keep NVLink busy: one per SM.
+inline int p2p_blocks() { return 148; }
 
 // Bytes of one rank's region for a gradient of `count` floats, and the
 // buffer offsets within it.
