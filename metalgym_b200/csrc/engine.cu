@@ -916,7 +916,7 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         // peer memory leaves the averaged gradient in grad and its norm in normSq
         float* x0 = reinterpret_cast<float*>(static_cast<unsigned char*>(p2pRegion) + p2pTable.xOff[0]);
         float* x1 = reinterpret_cast<float*>(static_cast<unsigned char*>(p2pRegion) + p2pTable.xOff[1]);
-        MG_TRY(grad_finalize(gradTable, x0, normPartial, st, nullptr, nullptr, x1, p2pSeq));
+        MG_TRY(grad_finalize(gradTable, x0, normPartial, st, nullptr, nullptr, x1, p2pSeq, (int64_t)optFloatCount));
         MG_TRY(p2p_allreduce(p2pTable, (int64_t)optCount, grad, p2pSeq, p2pCounter, normPartial, normSq, st));
         const AdamHyper ah{lr, hp.maxGradNorm, 0.0f, 0.0f};
         return adam(master, grad, mom, var, weights, normPartial, 0, (int64_t)optCount, ah, schedBetaPow + 2 * j,
@@ -1446,7 +1446,7 @@ int PpoEngine::p2pHandle(void* out64) {
     MG_CHECK_ARG(out64, "p2pHandle: null output");
     MG_CUDA_TRY(cudaSetDevice(gym->device));
     if (!p2pRegion) {
-        const size_t bytes = p2p_region_bytes((int64_t)optCount);
+        const size_t bytes = p2p_region_bytes((int64_t)optCount, (int64_t)optFloatCount);
         MG_CUDA_TRY(cudaMalloc(&p2pRegion, bytes));
         MG_CUDA_TRY(cudaMemset(p2pRegion, 0, bytes));
         MG_TRY(dalloc(&p2pSeq, 4));
@@ -1488,7 +1488,7 @@ int PpoEngine::p2pOpen(const void* handles, int r, int w) {
         p2pOpened.push_back(ptr);
         t.base[p] = static_cast<unsigned char*>(ptr);
     }
-    p2p_layout(t, (int64_t)optCount);
+    p2p_layout(t, (int64_t)optCount, (int64_t)optFloatCount);
     t.rank = r;
     t.world = w;
     p2pTable = t;

@@ -2,7 +2,8 @@
 // per GPU). Replaces the NCCL all-reduce of each minibatch's flat gradient:
 //
 //   finalize    each rank sums its split-K partials into its exchange buffer
-//               xbuf[b] (k_grad_finalize, buffer chosen on the device)
+//               xbuf[b] (k_grad_finalize, buffer chosen on the device; the
+//               bf16-rounded GEMM-weight sums packed as bf16, exact)
 //   all-reduce  k_p2p_allreduce: every rank announces xbuf[b] complete (a
 //               flag written into every rank's memory), waits for all
 //               announcements, then reads every rank's xbuf[b] over NVLink,
@@ -61,8 +62,9 @@ __device__ void wait_flags(const unsigned int* flags, int world, unsigned int se
 
 // Thread 0 of CTA 0 writes seq into slot `rank` of the flag array at byte
 // `flagOff` of every rank's region (its own included). The data the flag
-// announces was written by an earlier kernel, complete before this one
-// started; the release makes it visible to the ranks that acquire the flag.
+// announces was written by an earlier kernel, complete once this kernel's
+// dependency wait returned; the release makes it visible to the ranks that
+// acquire the flag.
 __device__ void announce(const P2PTable& t, size_t flagOff, unsigned int seq) {
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         __threadfence_system();
@@ -84,6 +86,10 @@ __global__ void __launch_bounds__(256) k_p2p_allreduce(const __grid_constant__ P
                                                        int* status) {
     __shared__ float s_red[8];
     __shared__ bool s_last;
+    // launched as a programmatic dependent of the finalisation: its buffer
+    // (and the counter) are complete once the wait returns
+    mg_pdl_wait();
+    mg_pdl_trigger();
     const unsigned int seq = *seqPtr + 1;
     const int b = seq & 1;
     announce(t, kP2PFlagsA, seq);
@@ -91,28 +97,49 @@ __global__ void __launch_bounds__(256) k_p2p_allreduce(const __grid_constant__ P
     const size_t xOff = t.xOff[b];
     float4* gd = reinterpret_cast<float4*>(grad);
     float sq = 0.0f;
-    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < count / 4; g += (int64_t)gridDim.x * blockDim.x) {
-        // every rank's values in flight at once (one NVLink round trip), then
-        // the sum in rank order
-        float4 v[kP2PMaxRanks];
+    // work items: the fp32 part in groups of 4 elements, then the bf16 part
+    // in groups of 8 (16 bytes per rank either way)
+    const int64_t nf = t.floatCount / 4, nh = (count - t.floatCount) / 8;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < nf + nh; g += (int64_t)gridDim.x * blockDim.x) {
+        // every rank's 16 bytes in flight at once (one NVLink round trip),
+        // then the sum in rank order
+        uint4 raw[kP2PMaxRanks];
+        const int64_t byteOff = g < nf ? g * 16 : t.floatCount * 4 + (g - nf) * 16;
 #pragma unroll
         for (int p = 0; p < kP2PMaxRanks; p++)
-            if (p < t.world) v[p] = __ldcg(reinterpret_cast<const float4*>(t.base[p] + xOff) + g);
-        float4 acc = v[0];
+            if (p < t.world) raw[p] = __ldcg(reinterpret_cast<const uint4*>(t.base[p] + xOff + byteOff));
+        const int ne = g < nf ? 4 : 8;
+        float acc[8];
 #pragma unroll
-        for (int p = 1; p < kP2PMaxRanks; p++) {
+        for (int p = 0; p < kP2PMaxRanks; p++) {
             if (p < t.world) {
-                acc.x = __fadd_rn(acc.x, v[p].x);
-                acc.y = __fadd_rn(acc.y, v[p].y);
-                acc.z = __fadd_rn(acc.z, v[p].z);
-                acc.w = __fadd_rn(acc.w, v[p].w);
+                float v[8];
+                const uint32_t w[4] = {raw[p].x, raw[p].y, raw[p].z, raw[p].w};
+                if (ne == 4) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) v[e] = __uint_as_float(w[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        v[2 * e] = __uint_as_float(w[e] << 16);
+                        v[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    if (e < ne) acc[e] = p == 0 ? v[e] : __fadd_rn(acc[e], v[e]);
             }
         }
-        acc = make_float4(__fmul_rn(acc.x, scale), __fmul_rn(acc.y, scale), __fmul_rn(acc.z, scale),
-                          __fmul_rn(acc.w, scale));
-        gd[g] = acc;
-        sq = __fadd_rn(sq, __fadd_rn(__fadd_rn(__fmul_rn(acc.x, acc.x), __fmul_rn(acc.y, acc.y)),
-                                     __fadd_rn(__fmul_rn(acc.z, acc.z), __fmul_rn(acc.w, acc.w))));
+        float* dst = g < nf ? grad + g * 4 : grad + t.floatCount + (g - nf) * 8;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            if (e < ne) {
+                acc[e] = __fmul_rn(acc[e], scale);
+                sq = __fadd_rn(sq, __fmul_rn(acc[e], acc[e]));
+            }
+        }
+        reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (ne == 8) reinterpret_cast<float4*>(dst)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
     sq = warp_sum(sq);
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = sq;
@@ -144,25 +171,28 @@ __global__ void __launch_bounds__(256) k_p2p_allreduce(const __grid_constant__ P
 
 }  // namespace
 
-size_t p2p_region_bytes(int64_t count) {
-    const size_t xb = ((size_t)count * 4 + 255) / 256 * 256;
-    return kP2PData + 2 * xb;
+// One exchange buffer: floatCount fp32 elements, then the rest as bf16.
+static size_t xbuf_bytes(int64_t count, int64_t floatCount) {
+    return ((size_t)floatCount * 4 + (size_t)(count - floatCount) * 2 + 255) / 256 * 256;
 }
 
-void p2p_layout(P2PTable& t, int64_t count) {
-    const size_t xb = ((size_t)count * 4 + 255) / 256 * 256;
+size_t p2p_region_bytes(int64_t count, int64_t floatCount) { return kP2PData + 2 * xbuf_bytes(count, floatCount); }
+
+void p2p_layout(P2PTable& t, int64_t count, int64_t floatCount) {
+    const size_t xb = xbuf_bytes(count, floatCount);
     t.xOff[0] = kP2PData;
     t.xOff[1] = kP2PData + xb;
+    t.floatCount = floatCount;
 }
 
 int p2p_allreduce(const P2PTable& t, int64_t count, float* grad, unsigned int* seq, unsigned int* counter,
                   float* normPartial, float* normSqOut, cudaStream_t st) {
     MG_CHECK_ARG(t.world >= 2 && t.world <= kP2PMaxRanks && t.rank >= 0 && t.rank < t.world,
                  "p2p all-reduce: bad rank / world size");
-    MG_CHECK_ARG(count % 4 == 0, "p2p all-reduce: count must be a multiple of 4");
-    // a plain launch: this kernel waits on other GPUs, not on earlier kernels of this stream
-    k_p2p_allreduce<<<p2p_blocks(), 256, 0, st>>>(t, count, 1.0f / (float)t.world, grad, seq, counter, normPartial,
-                                                  normSqOut, status_ptr());
+    MG_CHECK_ARG(count % 8 == 0 && t.floatCount % 8 == 0 && t.floatCount <= count,
+                 "p2p all-reduce: the element counts must be multiples of 8");
+    MG_LAUNCH(k_p2p_allreduce, p2p_blocks(), 256, 0, st, t, count, 1.0f / (float)t.world, grad, seq, counter,
+              normPartial, normSqOut, status_ptr());
     return check_launch("k_p2p_allreduce");
 }
 

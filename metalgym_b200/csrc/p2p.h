@@ -14,9 +14,13 @@ constexpr size_t kP2PData = (size_t)kP2PMaxRanks * kP2PFlagStride * 4;  // buffe
 
 // Every rank's region (own and peers', opened through CUDA IPC) and the
 // buffer offsets inside a region.
+// An exchange buffer holds the gradient arena's first floatCount elements as
+// fp32 and the rest (the GEMM weights' gradients, rounded to bf16 by the
+// finalisation) packed as bf16: exact, and half the bytes over NVLink.
 struct P2PTable {
     unsigned char* base[kP2PMaxRanks];
     size_t xOff[2];
+    int64_t floatCount;
     int rank, world;
 };
 
@@ -24,14 +28,16 @@ struct P2PTable {
 // announces for all of them), enough to keep NVLink busy: one per SM.
 inline int p2p_blocks() { return 148; }
 
-// Bytes of one rank's region for a gradient of `count` floats, and the
+// Bytes of one rank's region for a gradient of `count` elements whose first
+// floatCount are fp32 in the exchange buffers (both multiples of 8), and the
 // buffer offsets within it.
-size_t p2p_region_bytes(int64_t count);
-void p2p_layout(P2PTable& t, int64_t count);
+size_t p2p_region_bytes(int64_t count, int64_t floatCount);
+void p2p_layout(P2PTable& t, int64_t count, int64_t floatCount);
 
 // The exchange kernel: grad = (sum over ranks of xbuf[b], in rank order) /
 // world, normSqOut = |grad|^2; seq is the device minibatch counter that
-// selects b (the gradient finalisation writes xbuf[b] with the same rule).
+// selects b (the gradient finalisation writes xbuf[b] with the same rule,
+// its elements from t.floatCount on packed as bf16).
 int p2p_allreduce(const P2PTable& t, int64_t count, float* grad, unsigned int* seq, unsigned int* counter,
                   float* normPartial, float* normSqOut, cudaStream_t st);
 

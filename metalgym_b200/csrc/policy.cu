@@ -711,11 +711,23 @@ __global__ void __launch_bounds__(256) k_adv_stats_rows(const float* __restrict_
 
 // ------------------------------------------------------ gradients and Adam
 
+// Element i of the destination: fp32 at grad[i], or, from element bf16From
+// on, packed bf16 after the fp32 elements (the exchange buffer of the
+// peer-memory all-reduce, where the bf16-rounded sums travel as bf16).
+__device__ __forceinline__ void grad_store(float* grad, int64_t bf16From, int64_t i, float v) {
+    if (i < bf16From)
+        grad[i] = v;
+    else
+        reinterpret_cast<__nv_bfloat16*>(grad + bf16From)[i - bf16From] = __float2bfloat16_rn(v);
+}
+
 // Virtual block b of the finalisation (k_grad_finalize's CTA b): its
 // gradient elements summed over their partials into grad, the block's sum of
-// squares into normPartial[b]. Every thread of the CTA calls it.
+// squares into normPartial[b]. Every thread of the CTA calls it. Elements
+// from bf16From on are stored packed as bf16 (grad_store); they belong to
+// bf16-rounded segments, so the values are exact.
 __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab, int b, float* __restrict__ grad,
-                                                    float* __restrict__ normPartial) {
+                                                    float* __restrict__ normPartial, int64_t bf16From) {
     __shared__ float s_red[8];
     int si = 0;
     while (si < tab.n - 1 && b >= tab.seg[si].blockEnd) si++;
@@ -781,7 +793,7 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
             if (sg.roundBf16) t = make_float4(rbf(t.x), rbf(t.y), rbf(t.z), rbf(t.w));
             const float tv[4] = {t.x, t.y, t.z, t.w};
             for (int e = 0; e < 4 && i + e < sg.count; e++) {
-                grad[sg.dstOffset + i + e] = tv[e];
+                grad_store(grad, bf16From, sg.dstOffset + i + e, tv[e]);
                 sq = __fadd_rn(sq, __fmul_rn(tv[e], tv[e]));
             }
         }
@@ -824,7 +836,13 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
             acc.w = __fadd_rn(acc.w, v.w);
         }
         if (sg.roundBf16) acc = make_float4(rbf(acc.x), rbf(acc.y), rbf(acc.z), rbf(acc.w));
-        *reinterpret_cast<float4*>(grad + sg.dstOffset + i) = acc;
+        if (sg.dstOffset + i < bf16From) {
+            *reinterpret_cast<float4*>(grad + sg.dstOffset + i) = acc;
+        } else {  // four packed bf16 (8 bytes: bf16From and the offset are multiples of 4)
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(grad + bf16From) + (sg.dstOffset + i - bf16From)) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+        }
         sq = __fadd_rn(__fadd_rn(__fmul_rn(acc.x, acc.x), __fmul_rn(acc.y, acc.y)),
                        __fadd_rn(__fmul_rn(acc.z, acc.z), __fmul_rn(acc.w, acc.w)));
     } else {
@@ -835,7 +853,7 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
             float acc = 0.0f;
             for (int p = 0; p < sg.nparts; p++) acc = __fadd_rn(acc, src[(int64_t)p * st]);
             if (sg.roundBf16) acc = rbf(acc);
-            grad[sg.dstOffset + i + e] = acc;
+            grad_store(grad, bf16From, sg.dstOffset + i + e, acc);
             sq = __fadd_rn(sq, __fmul_rn(acc, acc));
         }
     }
@@ -858,7 +876,7 @@ __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ G
                                                        float* gradA, float* gradB, const unsigned int* sel,
                                                        float* __restrict__ normPartial,
                                                        unsigned int* __restrict__ counter,
-                                                       float* __restrict__ normSqOut) {
+                                                       float* __restrict__ normSqOut, int64_t bf16From) {
     mg_pdl_trigger();
     mg_pdl_wait();
     // with sel (the peer all-reduce's minibatch counter): gradB when the next
@@ -866,7 +884,7 @@ __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ G
     float* __restrict__ grad = (sel && ((*sel + 1u) & 1u)) ? gradB : gradA;
     __shared__ float s_red[8];
     __shared__ bool s_last;
-    grad_finalize_block(tab, blockIdx.x, grad, normPartial);
+    grad_finalize_block(tab, blockIdx.x, grad, normPartial, bf16From);
     if (threadIdx.x == 0) {
         s_last = false;
         if (counter) {
@@ -1244,7 +1262,7 @@ int grad_table_layout(GradSegmentTable& tab, bool allowDeep) {
 }
 
 int grad_finalize(const GradSegmentTable& table, float* grad, float* normPartial, cudaStream_t st,
-                  unsigned int* counter, float* normSqOut, float* grad2, const unsigned int* sel) {
+                  unsigned int* counter, float* normSqOut, float* grad2, const unsigned int* sel, int64_t bf16From) {
     MG_CHECK_ARG(table.n > 0 && table.n <= kMaxGradSegments, "grad_finalize: bad segment count");
     const int nblocks = table.seg[table.n - 1].blockEnd;
     MG_CHECK_ARG(nblocks > 0, "grad_finalize: empty");
@@ -1255,7 +1273,14 @@ int grad_finalize(const GradSegmentTable& table, float* grad, float* normPartial
         g.vec4 = (reinterpret_cast<uintptr_t>(g.src) % 16 == 0) && g.partStride % 4 == 0 && g.dstOffset % 4 == 0 &&
                  (reinterpret_cast<uintptr_t>(grad) % 16 == 0);
     }
-    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, grad2, sel, normPartial, counter, normSqOut);
+    if (bf16From != INT64_MAX) {
+        MG_CHECK_ARG(bf16From % 4 == 0, "grad_finalize: the bf16 part must start at a multiple of 4 elements");
+        for (int k = 0; k < tab.n; k++)
+            MG_CHECK_ARG(tab.seg[k].dstOffset + tab.seg[k].count <= bf16From ||
+                             (tab.seg[k].roundBf16 && tab.seg[k].dstOffset >= bf16From),
+                         "grad_finalize: only bf16-rounded segments may lie in the bf16 part");
+    }
+    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, grad2, sel, normPartial, counter, normSqOut, bf16From);
     return check_launch("k_grad_finalize");
 }
 

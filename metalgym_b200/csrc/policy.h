@@ -107,9 +107,12 @@ int grad_table_layout(GradSegmentTable& tab, bool allowDeep = true);
 // the per-CTA partials into *normSqOut and re-zeroes the counter.
 // With sel (a device counter): the sums go to grad2 when *sel + 1 is odd, else
 // to grad (the two exchange buffers of the peer all-reduce).
+// bf16From: elements from this index on are stored packed as bf16 after the
+// fp32 ones (only bf16-rounded segments may lie there; the exchange buffer of
+// the peer-memory all-reduce); INT64_MAX: every element fp32.
 int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st,
                   unsigned int* counter = nullptr, float* normSqOut = nullptr, float* grad2 = nullptr,
-                  const unsigned int* sel = nullptr);
+                  const unsigned int* sel = nullptr, int64_t bf16From = INT64_MAX);
 int grad_scale_norm_blocks(int64_t count);
 int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st,
                     unsigned int* counter = nullptr, float* normSqOut = nullptr);
