@@ -960,6 +960,20 @@ __global__ void __launch_bounds__(256) k_grad_scale_norm(float* __restrict__ gra
     }
 }
 
+// model/optimizer.metal:36-60 for one element: gRaw the unclipped gradient,
+// `scale` the clip factor, c1 = 1 - beta1^t, c2 = 1 - beta2^t; m, v, x the
+// moments and the master weight, updated in place.
+__device__ __forceinline__ void adam_math(float gRaw, float scale, float lr, float c1, float c2, float& m, float& v,
+                                          float& x) {
+    const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
+    const float g = __fmul_rn(gRaw, scale);
+    m = __fadd_rn(__fmul_rn(b1, m), __fmul_rn(__fsub_rn(1.0f, b1), g));
+    v = __fadd_rn(__fmul_rn(b2, v), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
+    const float mHat = __fdiv_rn(m, c1);
+    const float vHat = __fdiv_rn(v, c2);
+    x = __fsub_rn(x, __fdiv_rn(__fmul_rn(lr, mHat), __fadd_rn(__fsqrt_rn(vHat), eps)));
+}
+
 // model/optimizer.metal:36-60 with the host bias-correction powers of
 // model/ppo.h:879-880 (from betaPow[0..1] if given, else the scalars).
 // Every CTA first sums the norm partials in the same order, so all agree.
@@ -969,19 +983,14 @@ __device__ __forceinline__ void adam_range(float* __restrict__ param, const floa
                                            float* __restrict__ mom, float* __restrict__ var,
                                            __nv_bfloat16* __restrict__ weights, int64_t count, const AdamHyper& hp,
                                            const float* __restrict__ betaPow, float scale, int64_t i0, int64_t stride) {
-    const float b1 = 0.9f, b2 = 0.999f, eps = 1e-8f;
     const float b1p = betaPow ? betaPow[0] : hp.beta1Pow;
     const float b2p = betaPow ? betaPow[1] : hp.beta2Pow;
     const float c1 = __fsub_rn(1.0f, b1p), c2 = __fsub_rn(1.0f, b2p);
     for (int64_t i = i0; i < count; i += stride) {
-        const float g = __fmul_rn(grad[i], scale);
-        const float m = __fadd_rn(__fmul_rn(b1, mom[i]), __fmul_rn(__fsub_rn(1.0f, b1), g));
-        const float v = __fadd_rn(__fmul_rn(b2, var[i]), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
+        float m = mom[i], v = var[i], x = param[i];
+        adam_math(grad[i], scale, hp.lr, c1, c2, m, v, x);
         mom[i] = m;
         var[i] = v;
-        const float mHat = __fdiv_rn(m, c1);
-        const float vHat = __fdiv_rn(v, c2);
-        const float x = __fsub_rn(param[i], __fdiv_rn(__fmul_rn(hp.lr, mHat), __fadd_rn(__fsqrt_rn(vHat), eps)));
         param[i] = x;
         weights[i] = tobf(x);
     }
@@ -996,6 +1005,18 @@ __global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const f
     mg_pdl_trigger();
     mg_pdl_wait();
     __shared__ float s_scale;
+    // the first element's operands and the bias corrections in flight while
+    // the clip factor is formed (one memory round trip instead of two)
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+    float g0 = 0.0f, m0 = 0.0f, v0 = 0.0f, x0 = 0.0f;
+    if (i0 < count) {
+        g0 = grad[i0];
+        m0 = mom[i0];
+        v0 = var[i0];
+        x0 = param[i0];
+    }
+    const float c1 = __fsub_rn(1.0f, betaPow ? betaPow[0] : hp.beta1Pow);
+    const float c2 = __fsub_rn(1.0f, betaPow ? betaPow[1] : hp.beta2Pow);
     if (threadIdx.x < 32) {
         float s = 0.0f;
         if (normSqIn) {
@@ -1013,8 +1034,14 @@ __global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const f
         }
     }
     __syncthreads();
-    adam_range(param, grad, mom, var, weights, count, hp, betaPow, s_scale, (int64_t)blockIdx.x * blockDim.x + threadIdx.x,
-               (int64_t)gridDim.x * blockDim.x);
+    if (i0 < count) {
+        adam_math(g0, s_scale, hp.lr, c1, c2, m0, v0, x0);
+        mom[i0] = m0;
+        var[i0] = v0;
+        param[i0] = x0;
+        weights[i0] = tobf(x0);
+    }
+    adam_range(param, grad, mom, var, weights, count, hp, betaPow, s_scale, i0 + stride, stride);
 }
 
 // LossStats (model/ppo.h:925-943): column means of the rows x 5 stats.
