@@ -721,6 +721,15 @@ __device__ __forceinline__ void grad_store(float* grad, int64_t bf16From, int64_
         reinterpret_cast<__nv_bfloat16*>(grad + bf16From)[i - bf16From] = __float2bfloat16_rn(v);
 }
 
+// A 16-byte global load issued where it stands: the loads of a batch all go
+// out before the first add consumes one (the compiler would otherwise
+// interleave them with the adds and keep only a few in flight).
+__device__ __forceinline__ float4 ld_f4_now(const float* p) {
+    float4 v;
+    asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+
 // Virtual block b of the finalisation (k_grad_finalize's CTA b): its
 // gradient elements summed over their partials into grad, the block's sum of
 // squares into normPartial[b]. Every thread of the CTA calls it. Elements
@@ -745,12 +754,25 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
         if (i < sg.count) {
             const bool v4 = sg.vec4 && i + 3 < sg.count;
             int p = warp;
-            // sixteen loads in flight per thread while they last, then four
+            // thirty-two loads in flight per thread while they last (the 256
+            // partials of a 4096-row minibatch in one round trip), then
+            // sixteen, then four
+            for (; p + 248 < sg.nparts && v4; p += 256) {
+                float4 v[32];
+#pragma unroll
+                for (int q = 0; q < 32; q++) v[q] = ld_f4_now(sg.src + (int64_t)(p + 8 * q) * st + i);
+#pragma unroll
+                for (int q = 0; q < 32; q++) {
+                    acc.x = __fadd_rn(acc.x, v[q].x);
+                    acc.y = __fadd_rn(acc.y, v[q].y);
+                    acc.z = __fadd_rn(acc.z, v[q].z);
+                    acc.w = __fadd_rn(acc.w, v[q].w);
+                }
+            }
             for (; p + 120 < sg.nparts && v4; p += 128) {
                 float4 v[16];
 #pragma unroll
-                for (int q = 0; q < 16; q++)
-                    v[q] = *reinterpret_cast<const float4*>(sg.src + (int64_t)(p + 8 * q) * st + i);
+                for (int q = 0; q < 16; q++) v[q] = ld_f4_now(sg.src + (int64_t)(p + 8 * q) * st + i);
 #pragma unroll
                 for (int q = 0; q < 16; q++) {
                     acc.x = __fadd_rn(acc.x, v[q].x);
@@ -762,7 +784,7 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
             for (; p + 24 < sg.nparts && v4; p += 32) {
                 float4 v[4];
 #pragma unroll
-                for (int q = 0; q < 4; q++) v[q] = *reinterpret_cast<const float4*>(sg.src + (int64_t)(p + 8 * q) * st + i);
+                for (int q = 0; q < 4; q++) v[q] = ld_f4_now(sg.src + (int64_t)(p + 8 * q) * st + i);
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     acc.x = __fadd_rn(acc.x, v[q].x);
@@ -803,11 +825,24 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
         const float* src = sg.src + i;
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         int p = 0;
-        // sixteen loads in flight per thread (fewer round trips to L2), then eight
+        // thirty-two loads in flight per thread (one round trip to L2 for the
+        // 32 tile partials of a 4096-row minibatch), then sixteen, then eight
+        for (; p + 32 <= sg.nparts; p += 32) {
+            float4 v[32];
+#pragma unroll
+            for (int q = 0; q < 32; q++) v[q] = ld_f4_now(src + (int64_t)(p + q) * st);
+#pragma unroll
+            for (int q = 0; q < 32; q++) {
+                acc.x = __fadd_rn(acc.x, v[q].x);
+                acc.y = __fadd_rn(acc.y, v[q].y);
+                acc.z = __fadd_rn(acc.z, v[q].z);
+                acc.w = __fadd_rn(acc.w, v[q].w);
+            }
+        }
         for (; p + 16 <= sg.nparts; p += 16) {
             float4 v[16];
 #pragma unroll
-            for (int q = 0; q < 16; q++) v[q] = *reinterpret_cast<const float4*>(src + (int64_t)(p + q) * st);
+            for (int q = 0; q < 16; q++) v[q] = ld_f4_now(src + (int64_t)(p + q) * st);
 #pragma unroll
             for (int q = 0; q < 16; q++) {
                 acc.x = __fadd_rn(acc.x, v[q].x);
@@ -819,7 +854,7 @@ __device__ __forceinline__ void grad_finalize_block(const GradSegmentTable& tab,
         for (; p + 8 <= sg.nparts; p += 8) {
             float4 v[8];
 #pragma unroll
-            for (int q = 0; q < 8; q++) v[q] = *reinterpret_cast<const float4*>(src + (int64_t)(p + q) * st);
+            for (int q = 0; q < 8; q++) v[q] = ld_f4_now(src + (int64_t)(p + q) * st);
 #pragma unroll
             for (int q = 0; q < 8; q++) {
                 acc.x = __fadd_rn(acc.x, v[q].x);
