@@ -145,6 +145,23 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// ---------------------------------------------------------------- batched loads
+// 16-byte loads issued where they stand (volatile): a batch of them all goes
+// out before the first add consumes one. Without it the compiler interleaves
+// the loads of a batch with the adds that consume them and keeps only a few
+// in flight. ld_f4_now: global memory; ld_f4_generic_now: any address space
+// (distributed shared memory through a cluster-mapped generic address).
+__device__ __forceinline__ float4 ld_f4_now(const float* p) {
+    float4 v;
+    asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float4 ld_f4_generic_now(const void* p) {
+    float4 v;
+    asm volatile("ld.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+
 // ---------------------------------------------------------------- paired fp32
 // Two independent IEEE round-to-nearest operations in one instruction (the
 // f32x2 forms of sm_100), at half the issue cost. A paired multiply feeding a

@@ -32,6 +32,15 @@ namespace mg {
 
 namespace {
 
+// A 16-byte load of peer memory, cached in L2 only, issued where it stands:
+// every rank's load of a work item goes out before the first add (one NVLink
+// round trip per item, not one per rank).
+__device__ __forceinline__ uint4 ld_u4_cg_now(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ void store_release_sys(unsigned int* p, unsigned int v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -107,7 +116,7 @@ __global__ void __launch_bounds__(256) k_p2p_allreduce(const __grid_constant__ P
         const int64_t byteOff = g < nf ? g * 16 : t.floatCount * 4 + (g - nf) * 16;
 #pragma unroll
         for (int p = 0; p < kP2PMaxRanks; p++)
-            if (p < t.world) raw[p] = __ldcg(reinterpret_cast<const uint4*>(t.base[p] + xOff + byteOff));
+            if (p < t.world) raw[p] = ld_u4_cg_now(t.base[p] + xOff + byteOff);
         const int ne = g < nf ? 4 : 8;
         float acc[8];
 #pragma unroll

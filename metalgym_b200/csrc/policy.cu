@@ -721,15 +721,6 @@ __device__ __forceinline__ void grad_store(float* grad, int64_t bf16From, int64_
         reinterpret_cast<__nv_bfloat16*>(grad + bf16From)[i - bf16From] = __float2bfloat16_rn(v);
 }
 
-// A 16-byte global load issued where it stands: the loads of a batch all go
-// out before the first add consumes one (the compiler would otherwise
-// interleave them with the adds and keep only a few in flight).
-__device__ __forceinline__ float4 ld_f4_now(const float* p) {
-    float4 v;
-    asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
-    return v;
-}
-
 // Virtual block b of the finalisation (k_grad_finalize's CTA b): its
 // gradient elements summed over their partials into grad, the block's sum of
 // squares into normPartial[b]. Every thread of the CTA calls it. Elements

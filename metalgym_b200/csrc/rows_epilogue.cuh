@@ -74,6 +74,9 @@ __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red,
     int rows[NR];
     bool live[NR];
     float4 acc[NR];
+    // the cluster's partial tiles: every row's four loads (distributed shared
+    // memory) issued before the first add, then the sums in rank order
+    float4 part[NR][NSUM];
 #pragma unroll
     for (int t = 0; t < NR; t++) {
         int tl;  // row within this CTA's 32
@@ -87,17 +90,21 @@ __device__ __forceinline__ void rows_cluster_epilogue(uint8_t* smem, float* red,
         rows[t] = m0 + tr;
         live[t] = active && rows[t] < e.M;
         const uint8_t* cell = smem + tile_offset(tr & 127, lane);
-        float4 a = make_float4(0, 0, 0, 0);
-        if (active && NSUM == 1) {
-            a = *reinterpret_cast<const float4*>(cell);
-        } else if (active) {
-            a = *reinterpret_cast<const float4*>(__cluster_map_shared_rank(cell, 0));
 #pragma unroll
-            for (uint32_t r = 1; r < kRowsCluster; r++) {
-                const float4 b = *reinterpret_cast<const float4*>(__cluster_map_shared_rank(cell, r));
-                a = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
-            }
+        for (int r = 0; r < NSUM; r++) {
+            part[t][r] = make_float4(0, 0, 0, 0);
+            if (active)
+                part[t][r] = NSUM == 1 ? *reinterpret_cast<const float4*>(cell)
+                                       : ld_f4_generic_now(__cluster_map_shared_rank(cell, (uint32_t)r));
         }
+    }
+#pragma unroll
+    for (int t = 0; t < NR; t++) {
+        float4 a = part[t][0];
+#pragma unroll
+        for (int r = 1; r < NSUM; r++)
+            a = make_float4(__fadd_rn(a.x, part[t][r].x), __fadd_rn(a.y, part[t][r].y), __fadd_rn(a.z, part[t][r].z),
+                            __fadd_rn(a.w, part[t][r].w));
         acc[t] = a;
     }
 
