@@ -484,6 +484,11 @@ int PpoEngine::allocTrain(int rows) {
         s.count = count;
         s.dstOffset = (int64_t)params[p].offset;
         s.roundBf16 = round;
+        // written before the last backward kernel (block 0's): the other
+        // blocks', the final LayerNorm's and the head's partials
+        bool block0 = p == pInW || p == pInB;
+        for (uint32_t q : {pLnG[0], pLnB[0], pUp[0], pDown[0]}) block0 = block0 || p == q;
+        s.early = L > 0 && !block0 && p != pLogStd ? 1 : 0;
         tb.seg[tb.n++] = s;
         // the overlapped all-reduce: block 0 and the input layer (the last
         // backward layer), and everything before them in backward order
@@ -936,8 +941,13 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         return adam(master, grad, mom, var, weights, normPartial, 0, (int64_t)optCount, ah, schedBetaPow + 2 * j,
                     nullptr, st, normSq);
     }
-    // the finalisation's last CTA leaves the squared norm in normSq
-    MG_TRY(grad_finalize(gradTable, grad, normPartial, st, normCounter, normSq));
+    // the finalisation's last CTA leaves the squared norm in normSq. When the
+    // kernel before it is block 0's cluster backward (which signals its
+    // dependents after its own wait, with the input layer's gradient inside
+    // it and no join in between), the other blocks' and the head's sums start
+    // beside it.
+    const bool earlyOk = world == 1 && clusterBwd && !mt && inputFused && !forked;
+    MG_TRY(grad_finalize(gradTable, grad, normPartial, st, normCounter, normSq, nullptr, nullptr, INT64_MAX, earlyOk));
     if (world > 1) {
         Nccl& nc = nccl();
         ncclResult_t r = nc.allReduce(grad, grad, (size_t)optCount, ncclFloat, ncclSum, static_cast<ncclComm_t>(comm), st);

@@ -902,9 +902,19 @@ __global__ void __launch_bounds__(256) k_grad_finalize(const __grid_constant__ G
                                                        float* gradA, float* gradB, const unsigned int* sel,
                                                        float* __restrict__ normPartial,
                                                        unsigned int* __restrict__ counter,
-                                                       float* __restrict__ normSqOut, int64_t bf16From) {
+                                                       float* __restrict__ normSqOut, int64_t bf16From,
+                                                       bool earlyOk) {
     mg_pdl_trigger();
-    mg_pdl_wait();
+    // a CTA of a segment whose partials were written before the preceding
+    // kernel runs beside that kernel (earlyOk: it signalled this launch only
+    // after every kernel before it had completed); the others wait for it
+    bool wait = true;
+    if (earlyOk) {
+        int si = 0;
+        while (si < tab.n - 1 && (int)blockIdx.x >= tab.seg[si].blockEnd) si++;
+        wait = !tab.seg[si].early;
+    }
+    if (wait) mg_pdl_wait();
     // with sel (the peer all-reduce's minibatch counter): gradB when the next
     // count is odd, else gradA; without it: gradA
     float* __restrict__ grad = (sel && ((*sel + 1u) & 1u)) ? gradB : gradA;
@@ -1315,7 +1325,8 @@ int grad_table_layout(GradSegmentTable& tab, bool allowDeep) {
 }
 
 int grad_finalize(const GradSegmentTable& table, float* grad, float* normPartial, cudaStream_t st,
-                  unsigned int* counter, float* normSqOut, float* grad2, const unsigned int* sel, int64_t bf16From) {
+                  unsigned int* counter, float* normSqOut, float* grad2, const unsigned int* sel, int64_t bf16From,
+                  bool earlyOk) {
     MG_CHECK_ARG(table.n > 0 && table.n <= kMaxGradSegments, "grad_finalize: bad segment count");
     const int nblocks = table.seg[table.n - 1].blockEnd;
     MG_CHECK_ARG(nblocks > 0, "grad_finalize: empty");
@@ -1333,7 +1344,8 @@ int grad_finalize(const GradSegmentTable& table, float* grad, float* normPartial
                              (tab.seg[k].roundBf16 && tab.seg[k].dstOffset >= bf16From),
                          "grad_finalize: only bf16-rounded segments may lie in the bf16 part");
     }
-    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, grad2, sel, normPartial, counter, normSqOut, bf16From);
+    MG_LAUNCH(k_grad_finalize, nblocks, 256, 0, st, tab, grad, grad2, sel, normPartial, counter, normSqOut, bf16From,
+              earlyOk);
     return check_launch("k_grad_finalize");
 }
 

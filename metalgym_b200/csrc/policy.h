@@ -37,7 +37,9 @@ struct GradSegment {
     int blockEnd;   // filled by grad_table_layout
     int deep;       // filled by grad_table_layout: nparts > kGradDeepParts
     int vec4;       // set by grad_finalize: 16-byte aligned addresses and strides
-    int pad;
+    // the partials come from kernels before the one that precedes the
+    // finalisation (grad_finalize's earlyOk: those CTAs skip the dependency wait)
+    int early;
 };
 
 // Gradient elements per CTA of the finalisation (one norm partial each):
@@ -110,9 +112,12 @@ int grad_table_layout(GradSegmentTable& tab, bool allowDeep = true);
 // bf16From: elements from this index on are stored packed as bf16 after the
 // fp32 ones (only bf16-rounded segments may lie there; the exchange buffer of
 // the peer-memory all-reduce); INT64_MAX: every element fp32.
+// earlyOk: the kernel preceding the finalisation on st signals its dependents
+// only after its own dependency wait, so the CTAs of segments marked early
+// (their partials written before that kernel) start without waiting.
 int grad_finalize(const GradSegmentTable& tab, float* grad, float* normPartial, cudaStream_t st,
                   unsigned int* counter = nullptr, float* normSqOut = nullptr, float* grad2 = nullptr,
-                  const unsigned int* sel = nullptr, int64_t bf16From = INT64_MAX);
+                  const unsigned int* sel = nullptr, int64_t bf16From = INT64_MAX, bool earlyOk = false);
 int grad_scale_norm_blocks(int64_t count);
 int grad_scale_norm(float* grad, int64_t count, float scale, float* normPartial, cudaStream_t st,
                     unsigned int* counter = nullptr, float* normSqOut = nullptr);
