@@ -156,11 +156,6 @@ __device__ __forceinline__ float4 ld_f4_now(const float* p) {
     asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
     return v;
 }
-__device__ __forceinline__ float ld_f_cg_now(const float* p) {  // one float, L2 only
-    float v;
-    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
-    return v;
-}
 __device__ __forceinline__ float4 ld_f4_generic_now(const void* p) {
     float4 v;
     asm volatile("ld.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));

@@ -941,29 +941,20 @@ int PpoEngine::minibatch(int j, bool rowMode, cudaStream_t st) {
         return adam(master, grad, mom, var, weights, normPartial, 0, (int64_t)optCount, ah, schedBetaPow + 2 * j,
                     nullptr, st, normSq);
     }
-    // (with several ranks the finalisation's last CTA leaves the squared norm
-    // in normSq, before the all-reduce recomputes it.) When the kernel before
-    // the finalisation is block 0's cluster backward (which signals its
+    // the finalisation's last CTA leaves the squared norm in normSq. When the
+    // kernel before it is block 0's cluster backward (which signals its
     // dependents after its own wait, with the input layer's gradient inside
     // it and no join in between), the other blocks' and the head's sums start
     // beside it.
     const bool earlyOk = world == 1 && clusterBwd && !mt && inputFused && !forked;
-    const AdamHyper ah{lr, hp.maxGradNorm, 0.0f, 0.0f};
-    if (world == 1) {
-        // Adam's CTAs add the sums' per-CTA squared norms themselves (loads
-        // beside their element loads), instead of waiting for a last CTA of
-        // the sums to add them; Adam's first CTA leaves the result in normSq
-        MG_TRY(grad_finalize(gradTable, grad, normPartial, st, nullptr, nullptr, nullptr, nullptr, INT64_MAX, earlyOk));
-        return adam(master, grad, mom, var, weights, normPartial, nNorm, (int64_t)optCount, ah, schedBetaPow + 2 * j,
-                    normSq, st);
-    }
     MG_TRY(grad_finalize(gradTable, grad, normPartial, st, normCounter, normSq, nullptr, nullptr, INT64_MAX, earlyOk));
-    {
+    if (world > 1) {
         Nccl& nc = nccl();
         ncclResult_t r = nc.allReduce(grad, grad, (size_t)optCount, ncclFloat, ncclSum, static_cast<ncclComm_t>(comm), st);
         if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
         MG_TRY(grad_scale_norm(grad, (int64_t)optCount, 1.0f / (float)world, normPartial, st, normCounter, normSq));
     }
+    const AdamHyper ah{lr, hp.maxGradNorm, 0.0f, 0.0f};
     return adam(master, grad, mom, var, weights, normPartial, 0, (int64_t)optCount, ah, schedBetaPow + 2 * j, nullptr,
                 st, normSq);
 }

@@ -1058,19 +1058,7 @@ __global__ void __launch_bounds__(256) k_adam(float* __restrict__ param, const f
         if (normSqIn) {
             s = *normSqIn;
         } else {
-            // lane l adds partials l, l + 32, .. in order; up to sixteen of
-            // its loads in flight at a time
-            for (int base = 0; base < nNorm; base += 16 * 32) {
-                float v[16];
-#pragma unroll
-                for (int u = 0; u < 16; u++) {
-                    const int i = base + (int)threadIdx.x + 32 * u;
-                    v[u] = i < nNorm ? ld_f_cg_now(normPartial + i) : 0.0f;
-                }
-#pragma unroll
-                for (int u = 0; u < 16; u++)
-                    if (base + (int)threadIdx.x + 32 * u < nNorm) s = __fadd_rn(s, v[u]);
-            }
+            for (int i = threadIdx.x; i < nNorm; i += 32) s = __fadd_rn(s, normPartial[i]);
             s = warp_sum(s);
         }
         if (threadIdx.x == 0) {
